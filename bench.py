@@ -1,0 +1,506 @@
+#!/usr/bin/env python
+"""Benchmark of the KaniTTS fused decode-path kernels on B200.
+
+Headline workload (one "step" = one launch of the fused kernel):
+  rope_kv_write, bf16: T = 4096 tokens of Q [T, 16, 64], K/V [T, 8, 64]
+  ~ N(0, 1); rotary theta = 1e6 with the learnable alpha at its init
+  (w = 0 -> alpha = 1.05 in bf16); positions 0..4095; frame table
+  [1024, 64] ~ N(0, 0.02) indexed by position // 4; K/V written into a
+  static cache [1, 8, 4096, 64] at slot = position.  This is the prefill
+  end of the decode-step RoPE + KV-write configuration (its sweep maximum).
+  Eight independent input sets (272 MB > 126 MB L2) rotate between steps, so
+  every step reads cold inputs from HBM.
+
+  metric: fused-op HBM GB/s = algorithmic bytes / time, 8320 B per token
+  (read Q 2048 + K 1024 + V 1024 + frame row 128, write Q 2048 + K slot
+  1024 + V slot 1024).
+
+Timing: W warm-up launches, then exactly K launches replayed from CUDA
+graphs, bracketed by a barrier + synchronize and CUDA events on the
+launching stream; the max over ranks is taken.  N > 1 runs N independent
+replicas (the work shards by independent streams; there is no collective on
+the data path), so scaling is weak.
+
+Also reported:
+  e2e         — the same metric through the public Python API with pinned host
+                buffers: per step H2D of Q/K/V/positions/slots, the kernel, and
+                D2H of the rotated Q and the written K/V slots;
+  roofline    — achieved vs the measured HBM copy peak (MEASURED_PEAKS.json);
+  cpu_baseline— the CPU oracle (PyTorch eager restatement of the reference
+                path) on the host cores, rank 0 at N = 1;
+  sweep       — every fused op at its configuration sizes (µs per call and GB/s);
+  clocks      — nvidia-smi samples taken during the timed region.
+
+``--impl reference`` times the reference's CPU path (the oracle port; the
+reference's Triton source cannot be shipped to the GPU host) on the same
+workload and prints the same line with "impl": "reference".
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "kani-tts-2-openai-server_b200"))
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+METRIC = "fused-op HBM GB/s vs peak; decode step µs & tokens/s (LFM2-style, bs=1/64)"
+UNIT = "GB/s"
+T_TOK, HQ, HK, D = 4096, 16, 8, 64
+TABLE_ROWS, TPF = 1024, 4
+BYTES_PER_TOKEN = 8320
+STEP_BYTES = BYTES_PER_TOKEN * T_TOK
+N_SETS = 8
+WORKLOAD = (f"rope_kv_write bf16 T={T_TOK} Q[{T_TOK},{HQ},{D}] K/V[{T_TOK},{HK},{D}] theta=1e6 alpha=1.05 "
+            f"frame_table[{TABLE_ROWS},{D}] cache[1,{HK},{T_TOK},{D}] slot=pos")
+
+
+def _peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return 6650.0, "fallback"
+
+
+def _traffic_per_launch() -> float | None:
+    """DRAM bytes per headline launch from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / "rope_kv_write_t4096.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+# ------------------------------------------------------------ distributed
+
+def _dist_init():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def _barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def _max_over_ranks(x: float, world: int, dev) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """nvidia-smi sampling of one GPU while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, dev: torch.device):
+        self.proc = None
+        self.lines: list[str] = []
+        try:
+            uuid = str(torch.cuda.get_device_properties(dev).uuid)
+            self.target = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+        except Exception:
+            self.target = None
+
+    def __enter__(self):
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50"]
+        if self.target:
+            cmd += ["-i", self.target]
+        try:
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.reader = threading.Thread(target=self._read, daemon=True)
+            self.reader.start()
+            time.sleep(0.2)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.1)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.reader.join(timeout=5)
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------- workload
+
+def make_inputs(seed: int, t: int = T_TOK, device="cpu"):
+    """One seeded input set of the headline workload (generated on the CPU)."""
+    from kani_tts_b200 import positions as P
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(t, HQ, D, generator=g).to(torch.bfloat16)
+    k = torch.randn(t, HK, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(t, HK, D, generator=g).to(torch.bfloat16)
+    table = (0.02 * torch.randn(TABLE_ROWS, D, generator=g)).to(torch.bfloat16)
+    inv = P.learnable_inv_freq(D, 1e6, 0.0)
+    pos = torch.arange(t, dtype=torch.long)
+    s_len = max(2048, t)
+    kc = torch.zeros(1, HK, s_len, D, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    d = dict(q=q, k=k, v=v, table=table, inv=inv, pos=pos, slots=pos.clone(), kc=kc, vc=vc)
+    return {n: x.to(device) for n, x in d.items()}
+
+
+def launch(K, s: dict, q_out=None):
+    t = s["q"].shape[0]
+    return K.fused_rope_kv_write(
+        s["q"].view(1, t, HQ, D), s["k"].view(1, t, HK, D), s["v"].view(1, t, HK, D), s["inv"], s["pos"],
+        s["kc"], s["vc"], s["slots"], frame_table=s["table"], tokens_per_frame=TPF, q_out=q_out)
+
+
+def graph_of(fn_list):
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for fn in fn_list:
+            fn()
+    return g
+
+
+def time_graph_steps(step_fns, steps: int, dev, world: int, chunk: int = 1000):
+    """Replay exactly `steps` launches (cycling step_fns) from CUDA graphs;
+    return (elapsed seconds on this rank, launches captured per full graph)."""
+    chunk = max(1, min(chunk, steps))
+    full = steps // chunk
+    rest = steps - full * chunk
+    g_full = graph_of([step_fns[i % len(step_fns)] for i in range(chunk)])
+    g_rest = graph_of([step_fns[i % len(step_fns)] for i in range(rest)]) if rest else None
+    # one untimed replay of each graph (first replay uploads the graph)
+    g_full.replay()
+    if g_rest is not None:
+        g_rest.replay()
+    torch.cuda.synchronize(dev)
+    _barrier(world)
+    torch.cuda.synchronize(dev)
+    st = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(full):
+        g_full.replay()
+    if g_rest is not None:
+        g_rest.replay()
+    e1.record(st)
+    torch.cuda.synchronize(dev)
+    _barrier(world)
+    return e0.elapsed_time(e1) / 1e3
+
+
+# ------------------------------------------------------------ CPU arm
+
+def cpu_oracle_rate(seconds: float = 10.0, t: int = T_TOK, max_iters: int | None = None) -> dict:
+    """Time the oracle (CPU restatement of the reference path) on host cores."""
+    from oracle import kani_oracle as O
+    torch.set_num_threads(os.cpu_count() or 1)
+    s = make_inputs(0, t)
+    def one():
+        kc, vc = s["kc"], s["vc"]
+        O.rope_kv_write_ref(s["q"], s["k"], s["v"], s["inv"], s["pos"], kc, vc, s["slots"],
+                            frame_table=s["table"], tokens_per_frame=TPF)
+    one()
+    n, t0 = 0, time.perf_counter()
+    while True:
+        one()
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or (max_iters is not None and n >= max_iters):
+            break
+    return {"value": n * BYTES_PER_TOKEN * t / el / 1e9, "unit": UNIT, "cores": torch.get_num_threads(),
+            "kind": "port", "seconds": el, "iters": n,
+            "sample": f"{n} oracle calls of the full workload (T={t}) in {el:.1f} s"}
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    from oracle import kani_oracle as O
+    torch.set_num_threads(os.cpu_count() or 1)
+    s = make_inputs(0)
+    def one():
+        O.rope_kv_write_ref(s["q"], s["k"], s["v"], s["inv"], s["pos"], s["kc"], s["vc"], s["slots"],
+                            frame_table=s["table"], tokens_per_frame=TPF)
+    for _ in range(args.warmup):
+        one()
+    steps = min(args.steps, 50)          # bounded sample: each step is the full T=4096 workload
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        one()
+    el = time.perf_counter() - t0
+    value = steps * STEP_BYTES / el / 1e9
+    line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
+            "steps": steps, "warmup": args.warmup, "ms_per_step": round(el / steps * 1e3, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) inputs)", "impl": "reference",
+            "config": {"workload": WORKLOAD, "implementation": "CPU oracle (PyTorch eager restatement of "
+                       "kani_tts triton_kernels / optimized_decode / static_cache)", "l2": "n/a (CPU)"},
+            "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": torch.get_num_threads(),
+                             "kind": "port", "sample": f"{steps} full-workload steps"},
+            "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------- GPU arm
+
+def run_e2e(K, dev, steps: int) -> dict:
+    """Public API with pinned host buffers: H2D inputs, kernel, D2H results."""
+    host = make_inputs(1)
+    pin = {n: host[n].pin_memory() for n in ("q", "k", "v", "pos", "slots")}
+    devs = make_inputs(1, device=dev)
+    q_host = torch.empty(T_TOK, HQ, D, dtype=torch.bfloat16).pin_memory()
+    kv_host = torch.empty(2, HK, T_TOK, D, dtype=torch.bfloat16).pin_memory()
+    q_out = torch.empty(1, T_TOK, HQ, D, dtype=torch.bfloat16, device=dev)
+    h2d = sum(pin[n].numel() * pin[n].element_size() for n in pin)
+    d2h = q_host.numel() * 2 + kv_host.numel() * 2
+    st = torch.cuda.current_stream(dev)
+
+    def step():
+        for n in pin:
+            devs[n].copy_(pin[n], non_blocking=True)
+        launch(K, devs, q_out)
+        q_host.copy_(q_out.view(T_TOK, HQ, D), non_blocking=True)
+        kv_host[0].copy_(devs["kc"][0, :, :T_TOK], non_blocking=True)
+        kv_host[1].copy_(devs["vc"][0, :, :T_TOK], non_blocking=True)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(steps):
+        step()
+    e1.record(st)
+    torch.cuda.synchronize(dev)
+    el = e0.elapsed_time(e1) / 1e3
+    return {"seconds": el, "steps": steps, "h2d": h2d, "d2h": d2h}
+
+
+def run_sweep(K, dev, peak: float) -> dict:
+    """Every fused op at its configuration sizes, graph-replayed, inputs rotated."""
+    from kani_tts_b200 import positions as P
+    out = {}
+    g = torch.Generator().manual_seed(5)
+
+    def rot_sets(make, nbytes):
+        n = int(min(64, max(1, -(-256e6 // max(nbytes, 1)))))
+        return [make(i) for i in range(n)]
+
+    def measure(name, fns, nbytes, launches=400):
+        torch.cuda.synchronize(dev)
+        g_ = graph_of([fns[i % len(fns)] for i in range(launches)])
+        g_.replay()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        g_.replay()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        us = e0.elapsed_time(e1) * 1e3 / launches
+        gbs = nbytes / (us * 1e-6) / 1e9
+        out[name] = {"us": round(us, 3), "GB_s": round(gbs, 1), "frac": round(gbs / peak, 4),
+                     "bytes": int(nbytes), "rotated_sets": len(fns)}
+        del g_
+
+    # add + RMSNorm (config 1 and row sweep)
+    for dtype, rows in [(torch.float32, 8), (torch.bfloat16, 1), (torch.bfloat16, 16384),
+                        (torch.bfloat16, 65536), (torch.float32, 16384)]:
+        es = torch.tensor([], dtype=dtype).element_size()
+        nbytes = rows * 1024 * es * 4 + 1024 * es
+        def mk(i, rows=rows, dtype=dtype):
+            x = torch.randn(rows, 1024, generator=g).to(dtype).to(dev)
+            r = torch.randn(rows, 1024, generator=g).to(dtype).to(dev)
+            w = (1 + 0.02 * torch.randn(1024, generator=g)).to(dtype).to(dev)
+            y, h = torch.empty_like(x), torch.empty_like(x)
+            return lambda: K.fused_add_rms_norm(x, r, w, 1e-5, out=y, residual_out=h)
+        measure(f"add_rms_norm_{str(dtype)[6:]}_{rows}x1024", rot_sets(mk, nbytes), nbytes)
+    # SiLU*mul (config 3)
+    for t in (1, 64, 512, 4096, 32768):
+        nbytes = t * 27648
+        def mk(i, t=t):
+            x = torch.randn(t, 9216, generator=g).to(torch.bfloat16).to(dev)
+            y = torch.empty(t, 4608, dtype=torch.bfloat16, device=dev)
+            return lambda: K.fused_silu_mul(x, out=y)
+        measure(f"silu_mul_bf16_T{t}", rot_sets(mk, nbytes), nbytes, launches=100 if t >= 32768 else 400)
+    # RoPE + frame table + KV write (config 2 sweep), and the decode step with q/k norm
+    for t in (1, 64, 512, 4096):
+        nbytes = t * BYTES_PER_TOKEN
+        def mk(i, t=t):
+            s = make_inputs(100 + i, t, dev)
+            qo = torch.empty(1, t, HQ, D, dtype=torch.bfloat16, device=dev)
+            if t == 1:
+                p = int(torch.randint(0, 2048, (1,), generator=g))
+                s["pos"].fill_(p)
+                s["slots"].fill_(p)
+            return lambda: launch(K, s, qo)
+        measure(f"rope_kv_write_bf16_T{t}", rot_sets(mk, nbytes), nbytes)
+    nbytes = BYTES_PER_TOKEN - 128 + 256
+    def mk_norm(i):
+        s = make_inputs(200 + i, 1, dev)
+        qw = (1 + 0.02 * torch.randn(D, generator=g)).to(torch.bfloat16).to(dev)
+        kw = (1 + 0.02 * torch.randn(D, generator=g)).to(torch.bfloat16).to(dev)
+        qo = torch.empty(1, 1, HQ, D, dtype=torch.bfloat16, device=dev)
+        return lambda: K.fused_rope_kv_write(s["q"].view(1, 1, HQ, D), s["k"].view(1, 1, HK, D),
+                                             s["v"].view(1, 1, HK, D), s["inv"], s["pos"], s["kc"], s["vc"],
+                                             s["slots"], q_norm_w=qw, k_norm_w=kw, q_out=qo)
+    measure("rope_kv_write_qknorm_decode_bf16", rot_sets(mk_norm, nbytes), nbytes)
+    del P
+    return out
+
+
+def run_gpu(args, world, rank, local):
+    from kani_tts_b200 import _lib
+    from kani_tts_b200 import fused_kernels as K
+    _lib.load_library()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    peak, peak_kind = _peaks()
+    _lib.error_flag(dev)
+
+    sets = [make_inputs(1000 * rank + i, device=dev) for i in range(N_SETS)]
+    outs = [torch.empty(1, T_TOK, HQ, D, dtype=torch.bfloat16, device=dev) for _ in range(N_SETS)]
+    fns = [lambda s=s, o=o: launch(K, s, o) for s, o in zip(sets, outs)]
+    for i in range(max(3, args.warmup)):
+        fns[i % N_SETS]()
+    torch.cuda.synchronize(dev)
+
+    c0 = _lib.launch_count()
+    with ClockSampler(dev) as clocks:
+        elapsed = time_graph_steps(fns, args.steps, dev, world)
+    captured = _lib.launch_count() - c0        # launches recorded into the graphs
+    elapsed_max = _max_over_ranks(elapsed, world, dev)
+    flags = _lib.read_and_clear_errors(dev)
+    if flags:
+        raise RuntimeError(f"kernel error flags set during the bench: {flags}")
+
+    value = world * args.steps * STEP_BYTES / elapsed_max / 1e9
+    per_launch_s = elapsed / args.steps
+    achieved = STEP_BYTES / per_launch_s / 1e9
+
+    extras = {}
+    cpu = None
+    _barrier(world)
+    e = run_e2e(K, dev, min(args.steps, 200))
+    e_max = _max_over_ranks(e["seconds"], world, dev)
+    e2e_line = {"value": round(world * e["steps"] * STEP_BYTES / e_max / 1e9, 3), "unit": UNIT,
+                "h2d_bytes_per_step": e["h2d"], "d2h_bytes_per_step": e["d2h"], "steps": e["steps"],
+                "ms_per_step": round(e_max / e["steps"] * 1e3, 4),
+                "path": "kani_tts_b200.fused_rope_kv_write (ctypes -> kani_rope_kv_write), pinned host buffers"}
+    if rank == 0:
+        if not args.no_sweep:
+            extras["sweep"] = run_sweep(K, dev, peak)
+        if world == 1 and not args.no_cpu:
+            cpu = cpu_oracle_rate(args.cpu_seconds)
+    if rank != 0:
+        return
+    traffic = _traffic_per_launch()
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": round(elapsed_max / args.steps * 1e3, 6),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) inputs, N(0,0.02) frame table)",
+        "config": {"workload": WORKLOAD, "bytes_per_step": STEP_BYTES,
+                   "l2": f"inputs rotated over {N_SETS} sets ({N_SETS * STEP_BYTES / 1e6:.0f} MB > 126 MB L2)",
+                   "launch": "CUDA-graph replay of the kernel, one launch per step",
+                   "parallelism": f"replicas x{world} (independent streams, no collectives)"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": traffic,
+                     "algorithmic_bytes": STEP_BYTES,
+                     "kernel": "rope_vec_kernel<bf16, norm=0, table=1, cs_given=0>"},
+        "e2e": e2e_line,
+        "gpu_launches": args.steps,
+        "graph_launches_captured": captured,
+        "clocks": clocks.summary(),
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = {k: (round(v, 4) if isinstance(v, float) else v) for k, v in cpu.items()
+                                if k in ("value", "unit", "cores", "kind", "sample")}
+    line.update(extras)
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100000)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["kani_b200", "reference"], default="kani_b200")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the per-op sweep")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        # CPU arm: rank 0 alone measures; other ranks exit without work or a process group
+        run_reference(args, int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")))
+        return
+    world, rank, local = _dist_init()
+    try:
+        run_gpu(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

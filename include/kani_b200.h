@@ -1,0 +1,179 @@
+/*
+ * kani_b200.h — C ABI of the B200 (sm_100a) decode-path kernels for KaniTTS.
+ *
+ * These entry points replace the device work of the reference's per-token
+ * decode loop: the three Triton kernels in kani_tts/triton_kernels.py, the
+ * eager residual adds in kani_tts/optimized_decode.py and the scatter_ KV
+ * write in kani_tts/static_cache.py.  Each entry point cites the reference
+ * interface it replaces.
+ *
+ * Conventions (all entry points):
+ *   - Every pointer is a DEVICE pointer owned by the caller; the library never
+ *     allocates, frees or synchronises.  Launches go on `stream`
+ *     (a cudaStream_t passed as void*; NULL = legacy default stream), so every
+ *     call is capturable in a CUDA graph.
+ *   - `dtype` codes: KANI_DTYPE_F32 / _BF16 / _F16.  Arithmetic is fp32 with a
+ *     single round-to-nearest-even to the storage type per output element.
+ *   - Strides are in ELEMENTS.  Rows / tokens / heads are described by the
+ *     stride arguments; the innermost dimension is always contiguous.
+ *   - Return value: KANI_OK (0), a negative KANI_ERR_* for an argument the
+ *     library rejects before launching, or a positive cudaError_t from the
+ *     launch.  A zero-sized problem returns KANI_OK without launching.
+ *   - Data-dependent errors found on the device (a KV slot or a frame index out
+ *     of range) do not trap: the offending access is skipped and a KANI_FLAG_*
+ *     bit is OR-ed into the caller's device int32 `err_flag` (may be NULL).
+ */
+#ifndef KANI_B200_H
+#define KANI_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define KANI_API __attribute__((visibility("default")))
+#else
+#define KANI_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KANI_DTYPE_F32 0
+#define KANI_DTYPE_BF16 1
+#define KANI_DTYPE_F16 2
+
+#define KANI_OK 0
+#define KANI_ERR_INVALID_ARG (-1) /* null pointer, negative size, bad stride */
+#define KANI_ERR_DTYPE (-2)       /* unknown or unsupported dtype code */
+#define KANI_ERR_UNSUPPORTED (-3) /* shape the kernels do not implement */
+
+#define KANI_FLAG_SLOT_OOB 1  /* a KV write slot was outside [0, cache_len) */
+#define KANI_FLAG_FRAME_OOB 2 /* a frame-table row was outside [0, frame_rows) */
+
+/* Library ABI version (major*100 + minor). */
+KANI_API int kani_version(void);
+
+/* Human-readable text for a return code of this library. */
+KANI_API const char* kani_status_string(int status);
+
+/* Number of kernel launches this library has issued in this process. */
+KANI_API uint64_t kani_launch_count(void);
+
+/*
+ * RMSNorm over the last dimension:  y = round(x * rsqrt(mean(x^2) + eps) * w).
+ * Replaces `_rms_norm_kernel` and its launch in `fused_rms_norm`
+ * (kani_tts/triton_kernels.py:17-35, :38-60).  Unlike the reference, an fp32
+ * input yields a true fp32 output (the reference stores bf16-rounded values).
+ *   x, y:   [rows, n] with row strides x_row_stride / y_row_stride (y may alias x)
+ *   weight: [n], dtype w_dtype
+ */
+KANI_API int kani_rms_norm(int32_t dtype, int32_t w_dtype,
+                  const void* x, int64_t x_row_stride,
+                  const void* weight,
+                  void* y, int64_t y_row_stride,
+                  int64_t rows, int64_t n, float eps, void* stream);
+
+/*
+ * Residual add fused into RMSNorm:  h = round(x + residual);
+ * y = round(h * rsqrt(mean(h^2) + eps) * w); residual_out = h.
+ * Replaces the eager `hidden = hidden + F.linear(...)` at
+ * kani_tts/optimized_decode.py:252, :277, :283 together with the following
+ * `fused_rms_norm` call (optimized_decode.py:206, :280, :286).
+ * y may alias x; residual_out may alias x or residual (element-wise in place).
+ */
+KANI_API int kani_add_rms_norm(int32_t dtype, int32_t w_dtype,
+                      const void* x, int64_t x_row_stride,
+                      const void* residual, int64_t r_row_stride,
+                      const void* weight,
+                      void* y, int64_t y_row_stride,
+                      void* residual_out, int64_t h_row_stride,
+                      int64_t rows, int64_t n, float eps, void* stream);
+
+/*
+ * SiLU-gated activation: y[r, i] = round(silu(g[r, i]) * u[r, i]) where each
+ * input row is [g (n) | u (n)].
+ * Replaces `_silu_mul_kernel` and `fused_silu_mul`
+ * (kani_tts/triton_kernels.py:67-82, :85-105).
+ *   gate_up: [rows, 2n] with row stride in_row_stride; y: [rows, n].
+ */
+KANI_API int kani_silu_mul(int32_t dtype,
+                  const void* gate_up, int64_t in_row_stride,
+                  void* y, int64_t out_row_stride,
+                  int64_t rows, int64_t n, void* stream);
+
+/*
+ * Rotate-half RoPE of one token's Q and K heads with one shared cos/sin row,
+ * in ONE launch (the reference issues two).
+ * Replaces `_rope_kernel` and `fused_rope` (kani_tts/triton_kernels.py:112-165).
+ *   q, q_out: [num_q_heads, head_dim]; k, k_out: [num_k_heads, head_dim]
+ *   cos, sin: [head_dim] (same dtype as q)
+ *   y[i] = x[i]*cos[i] + sign(i)*x[(i+D/2) % D]*sin[i], sign = -1 for i < D/2.
+ */
+KANI_API int kani_rope_qk(int32_t dtype,
+                 const void* q, const void* k,
+                 const void* cos, const void* sin,
+                 void* q_out, void* k_out,
+                 int32_t num_q_heads, int32_t num_k_heads, int32_t head_dim,
+                 void* stream);
+
+/*
+ * Static KV-cache write of one token per stream:
+ *   k_cache[b, h, slot_b, :] = k[b, h, :];  v_cache[b, h, slot_b, :] = v[b, h, :]
+ * with slot_b = write_pos[b] if per_stream_pos else write_pos[0].
+ * Replaces the scatter_ in `StaticLfm2HybridConvCache.update`
+ * (kani_tts/static_cache.py:110-142; write position :81, :144-146).
+ *   k, v: [batch, num_kv_heads, head_dim] contiguous;
+ *   k_cache, v_cache: [batch, num_kv_heads, cache_len, head_dim] contiguous;
+ *   write_pos: device int64.  An out-of-range slot skips the write and sets
+ *   KANI_FLAG_SLOT_OOB.
+ */
+KANI_API int kani_kv_cache_write(int32_t dtype,
+                        const void* k, const void* v,
+                        int64_t batch, int32_t num_kv_heads, int32_t head_dim,
+                        void* k_cache, void* v_cache, int64_t cache_len,
+                        const int64_t* write_pos, int32_t per_stream_pos,
+                        int32_t* err_flag, void* stream);
+
+/*
+ * Fused attention-input step of one decode (or prefill) call, per token t of
+ * n_tokens = batch * seq_tokens:
+ *   1. optional per-head RMSNorm of Q and K (weights q_norm_w / k_norm_w [head_dim]),
+ *      rounded to dtype (kani_tts/optimized_decode.py:220-221);
+ *   2. cos/sin built in-kernel: angle_i = inv_freq[i] * float(positions[t]),
+ *      rounded to dtype (optimized_decode.py:229-234, learnable-alpha inv_freq
+ *      from kani_tts/model.py:180-196 and optimized_decode.py:104-111);
+ *   3. rotate-half RoPE of Q and K in fp32 (triton_kernels.py:121-130);
+ *   4. optional BemaTTS frame-position term: + frame_table[frame_pos[t] / tokens_per_frame]
+ *      broadcast over heads (frame_pos NULL -> positions), added in fp32 before the
+ *      single rounding;
+ *   5. Q -> q_out[t*q_out_tok_stride + h*q_out_head_stride + i];
+ *      K (rotated) and V (raw) -> k_cache / v_cache at
+ *      b*cache_batch_stride + h*cache_head_stride + slot*cache_slot_stride + i,
+ *      slot = write_slots[t] (static_cache.py:131-140).
+ * Replaces optimized_decode.py:220-240 (q/k norm, cos/sin glue, fused_rope,
+ * past_key_values.update).  Inputs are read at
+ * q + t*q_tok_stride + h*head_dim (likewise k, v), so the packed QKV
+ * projection output can be passed without a copy.
+ */
+KANI_API int kani_rope_kv_write(int32_t dtype,
+                       int64_t batch, int64_t seq_tokens,
+                       int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                       const void* q, int64_t q_tok_stride,
+                       const void* k, int64_t k_tok_stride,
+                       const void* v, int64_t v_tok_stride,
+                       const float* inv_freq, const int64_t* positions,
+                       const void* q_norm_w, const void* k_norm_w, float eps,
+                       const void* frame_table, int64_t frame_rows,
+                       const int64_t* frame_pos, int32_t tokens_per_frame,
+                       void* q_out, int64_t q_out_tok_stride, int64_t q_out_head_stride,
+                       void* k_cache, void* v_cache,
+                       int64_t cache_batch_stride, int64_t cache_head_stride,
+                       int64_t cache_slot_stride, int64_t cache_len,
+                       const int64_t* write_slots,
+                       int32_t* err_flag, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KANI_B200_H */

@@ -1,0 +1,189 @@
+// Shared device helpers for the KaniTTS decode-path kernels (sm_100a).
+//
+// Every kernel in this library streams rows of bf16 / fp16 / fp32 data through
+// 128-bit global loads and stores, does its arithmetic in fp32 and rounds once
+// (round-to-nearest-even) to the storage type.  These helpers hold the 16-byte
+// vector <-> fp32 conversions and the cache-hinted memory operations.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "kani_b200.h"
+
+namespace kani {
+
+// ---------------------------------------------------------------- elements
+
+template <typename T> struct Elem;
+
+template <> struct Elem<float> {
+  static __device__ __forceinline__ float to_f(float v) { return v; }
+  static __device__ __forceinline__ float from_f(float v) { return v; }
+};
+
+template <> struct Elem<__nv_bfloat16> {
+  static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+  static __device__ __forceinline__ __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+};
+
+template <> struct Elem<__half> {
+  static __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+  static __device__ __forceinline__ __half from_f(float v) { return __float2half_rn(v); }
+};
+
+// Round an fp32 value to T and back (models the store/reload of an
+// intermediate tensor of type T).
+template <typename T>
+__device__ __forceinline__ float round_to(float v) {
+  return Elem<T>::to_f(Elem<T>::from_f(v));
+}
+
+// ------------------------------------------------------- 16-byte vectors
+
+// Number of T elements in one 16-byte vector.
+template <typename T> struct VecN { static constexpr int value = 16 / (int)sizeof(T); };
+
+// Unpack 16 bytes holding VecN<T> elements into fp32.
+template <typename T>
+__device__ __forceinline__ void unpack16(const uint4& raw, float* f);
+
+template <>
+__device__ __forceinline__ void unpack16<float>(const uint4& raw, float* f) {
+  f[0] = __uint_as_float(raw.x); f[1] = __uint_as_float(raw.y);
+  f[2] = __uint_as_float(raw.z); f[3] = __uint_as_float(raw.w);
+}
+
+template <>
+__device__ __forceinline__ void unpack16<__nv_bfloat16>(const uint4& raw, float* f) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    // bf16 -> fp32 is exact: the bf16 bits are the high half of the fp32.
+    f[2 * i + 0] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+
+template <>
+__device__ __forceinline__ void unpack16<__half>(const uint4& raw, float* f) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __half2 h2 = *reinterpret_cast<const __half2*>(&w[i]);
+    float2 p = __half22float2(h2);
+    f[2 * i + 0] = p.x;
+    f[2 * i + 1] = p.y;
+  }
+}
+
+// Pack VecN<T> fp32 values into 16 bytes of T (one RNE rounding each).
+template <typename T>
+__device__ __forceinline__ uint4 pack16(const float* f);
+
+template <>
+__device__ __forceinline__ uint4 pack16<float>(const float* f) {
+  return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]),
+                    __float_as_uint(f[2]), __float_as_uint(f[3]));
+}
+
+template <>
+__device__ __forceinline__ uint4 pack16<__nv_bfloat16>(const float* f) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __nv_bfloat162 b = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+    w[i] = *reinterpret_cast<uint32_t*>(&b);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+template <>
+__device__ __forceinline__ uint4 pack16<__half>(const float* f) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __half2 h = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+    w[i] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// ------------------------------------------------------ memory operations
+
+// Plain coherent 128-bit load (safe when the same kernel later overwrites
+// the location in place).
+__device__ __forceinline__ uint4 ld16(const void* p) {
+  return *reinterpret_cast<const uint4*>(p);
+}
+
+// Streaming 128-bit load for data read exactly once (evict-first in L1/L2).
+__device__ __forceinline__ uint4 ld16_stream(const void* p) {
+  return __ldcs(reinterpret_cast<const uint4*>(p));
+}
+
+// Read-only 128-bit load through the non-coherent path, for small tables
+// (norm weights, frame table) that many threads re-read.
+__device__ __forceinline__ uint4 ld16_ro(const void* p) {
+  return __ldg(reinterpret_cast<const uint4*>(p));
+}
+
+__device__ __forceinline__ void st16(void* p, const uint4& v) {
+  *reinterpret_cast<uint4*>(p) = v;
+}
+
+// Load E weights of type W starting at element `off` and convert to fp32.
+// E is the element count of one 16-byte vector of the row type, so the load
+// is 8, 16 or 32 bytes wide; the caller guarantees matching alignment.
+template <typename W, int E>
+__device__ __forceinline__ void load_weights(const W* w, int64_t off, float* out) {
+  constexpr int BYTES = E * (int)sizeof(W);
+  static_assert(BYTES == 8 || BYTES == 16 || BYTES == 32, "weight vector width");
+  const char* p = reinterpret_cast<const char*>(w + off);
+  if constexpr (BYTES == 16) {
+    uint4 raw = ld16_ro(p);
+    unpack16<W>(raw, out);
+  } else if constexpr (BYTES == 32) {
+    uint4 a = ld16_ro(p), b = ld16_ro(p + 16);
+    unpack16<W>(a, out);
+    unpack16<W>(b, out + VecN<W>::value);
+  } else {  // 8 bytes: E = 4 elements of a 2-byte type
+    uint2 raw = __ldg(reinterpret_cast<const uint2*>(p));
+    uint4 wide = make_uint4(raw.x, raw.y, 0u, 0u);
+    float tmp[8];
+    unpack16<W>(wide, tmp);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) out[i] = tmp[i];
+  }
+}
+
+// ---------------------------------------------------------------- misc
+
+__host__ __device__ __forceinline__ bool aligned16(const void* p) {
+  return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+// Host-side launch accounting (number of kernels this library launched).
+void note_launch();
+
+// Dispatch a runtime dtype code to a C++ type and invoke f.template
+// operator()<T>().  Returns KANI_ERR_DTYPE for unknown codes.
+template <typename F>
+int dispatch_dtype(int32_t code, F&& f) {
+  switch (code) {
+    case KANI_DTYPE_F32: return f.template operator()<float>();
+    case KANI_DTYPE_BF16: return f.template operator()<__nv_bfloat16>();
+    case KANI_DTYPE_F16: return f.template operator()<__half>();
+    default: return KANI_ERR_DTYPE;
+  }
+}
+
+inline int launch_status() {
+  cudaError_t e = cudaGetLastError();
+  note_launch();
+  return e == cudaSuccess ? KANI_OK : (int)e;
+}
+
+}  // namespace kani

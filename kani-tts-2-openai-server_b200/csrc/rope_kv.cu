@@ -1,0 +1,562 @@
+// Rotary embedding of Q/K fused with the static KV-cache write (sm_100a).
+//
+// Reference algorithm, per token and head (all fp32, one rounding per store):
+//   optional q/k RMSNorm of the head, rounded to the storage type
+//       (kani_tts/optimized_decode.py:220-221 via triton_kernels.py:17-35)
+//   angle_i = inv_freq[i] * float(pos)   for i < D/2, shared by both halves
+//       (optimized_decode.py:229-232; inv_freq = bf16(theta^(-2i/D)) * alpha,
+//        kani_tts/model.py:180-196, optimized_decode.py:104-111)
+//   cos_i, sin_i rounded to the storage type (optimized_decode.py:233-234)
+//   y_i = x_i*cos_i + sign_i * x_{(i+D/2)%D} * sin_i,  sign = -1 for i < D/2
+//       (triton_kernels.py:121-130; the products and the sum are separately
+//        rounded fp32 operations, no fused multiply-add)
+//   optional frame term: y_i += table[frame, i] (fp32, before the one rounding)
+//   K_rot and raw V are stored at cache[b, h, slot, :]
+//       (static_cache.py:131-140).
+//
+// Vector kernel: a rope item is one lane holding the 16-byte vector of
+// elements [jE, jE+E) of the first half of a head AND the matching vector of
+// the second half, so the rotate-half partner is already in registers and no
+// shuffle is needed.  A head is L = (D/2)/E lanes (bf16, D=64: 4 lanes); its
+// sum of squares for the fused norm is an L-wide xor-shuffle tree.  Per token
+// the items are [Q heads | K heads | V heads], padded to whole warps, so a
+// head never straddles a warp and a token's K and V land in one CTA; a CTA
+// carries `tpb` tokens.  With cos/sin built in-kernel, the first D/2*tpb
+// threads compute one (cos, sin) pair each into shared memory (one sinf/cosf
+// per frequency per token instead of one per element per head).
+//
+// Generic kernel: any even D and any alignment — one warp per
+// (token, head) with scalar accesses.
+#include "common.cuh"
+
+namespace kani {
+namespace {
+
+struct RopeParams {
+  int64_t n_tokens;
+  int64_t seq_tokens;
+  int hq, hk, d;
+  const void* q;
+  int64_t qts;
+  const void* k;
+  int64_t kts;
+  const void* v;
+  int64_t vts;
+  const float* inv_freq;
+  const int64_t* positions;
+  const void* cos;
+  const void* sin;
+  const void* qw;
+  const void* kw;
+  float eps;
+  const void* table;
+  int64_t table_rows;
+  const int64_t* frame_pos;
+  int tpf;
+  void* q_out;
+  int64_t qots, qohs;
+  void* k_cache;
+  void* v_cache;
+  int64_t cbs, chs, css, clen;
+  const int64_t* slots;
+  int32_t* err;
+};
+
+struct TokenMeta {
+  int64_t b;
+  int64_t slot;
+  int64_t frame;
+  bool slot_ok;
+  bool frame_ok;
+};
+
+template <bool TABLE>
+__device__ __forceinline__ TokenMeta token_meta(const RopeParams& p, int64_t t) {
+  TokenMeta m;
+  m.b = t / p.seq_tokens;
+  m.slot = p.slots ? p.slots[t] : (t - m.b * p.seq_tokens);
+  m.slot_ok = m.slot >= 0 && m.slot < p.clen;
+  m.frame = 0;
+  m.frame_ok = true;
+  if constexpr (TABLE) {
+    const int64_t fp = p.frame_pos ? p.frame_pos[t] : p.positions[t];
+    m.frame = fp >= 0 ? fp / p.tpf : -1;
+    m.frame_ok = m.frame >= 0 && m.frame < p.table_rows;
+  }
+  return m;
+}
+
+template <bool TABLE>
+__device__ __forceinline__ void flag_token(const RopeParams& p, const TokenMeta& m) {
+  if (p.err == nullptr) return;
+  int bits = 0;
+  if (!m.slot_ok) bits |= KANI_FLAG_SLOT_OOB;
+  if (TABLE && !m.frame_ok) bits |= KANI_FLAG_FRAME_OOB;
+  if (bits) atomicOr(p.err, bits);
+}
+
+__device__ __forceinline__ float rrms_of(float ss, int n, float eps) {
+  return 1.0f / sqrtf(ss / (float)n + eps);
+}
+
+// ------------------------------------------------------------ vector kernel
+template <typename T, bool NORM, bool TABLE, bool CS_GIVEN>
+__global__ void __launch_bounds__(512)
+rope_vec_kernel(RopeParams p, int log2l, int ipt, int iptr, int tpb) {
+  constexpr int E = VecN<T>::value;
+  extern __shared__ float2 cs[];  // [tpb][D/2] (cos, sin), in-kernel angles only
+  const int L = 1 << log2l;
+  const int half = p.d >> 1;
+  const int tl = threadIdx.x / iptr;
+  const int item = threadIdx.x - tl * iptr;
+  const int64_t t = (int64_t)blockIdx.x * tpb + tl;
+
+  if constexpr (!CS_GIVEN) {
+    for (int idx = threadIdx.x; idx < tpb * half; idx += blockDim.x) {
+      const int ttl = idx / half;
+      const int i = idx - ttl * half;
+      const int64_t tt = (int64_t)blockIdx.x * tpb + ttl;
+      float c = 0.f, s = 0.f;
+      if (tt < p.n_tokens) {
+        const float ang = __fmul_rn(p.inv_freq[i], (float)p.positions[tt]);
+        c = round_to<T>(cosf(ang));
+        s = round_to<T>(sinf(ang));
+      }
+      cs[idx] = make_float2(c, s);
+    }
+    __syncthreads();
+  }
+
+  const bool tok_ok = t < p.n_tokens;
+  const int head_item = item >> log2l;
+  const int j = item & (L - 1);
+  // kind: 0 = Q rope, 1 = K rope, 2 = V copy, 3 = idle lane
+  int kind = 3, h = 0;
+  if (tok_ok && item < ipt) {
+    if (head_item < p.hq) {
+      kind = 0;
+      h = head_item;
+    } else if (head_item < p.hq + p.hk) {
+      kind = 1;
+      h = head_item - p.hq;
+    } else {
+      kind = 2;
+      h = head_item - p.hq - p.hk;
+    }
+  }
+  const int lo = j * E, hi = half + j * E;
+
+  TokenMeta m{};
+  if (tok_ok) {
+    m = token_meta<TABLE>(p, t);
+    if (item == 0) flag_token<TABLE>(p, m);
+  }
+
+  uint4 xlo = make_uint4(0, 0, 0, 0), xhi = xlo, plo = xlo, phi = xlo;
+  if (kind == 0) {
+    const T* src = static_cast<const T*>(p.q) + t * p.qts + (int64_t)h * p.d;
+    xlo = ld16(src + lo);
+    xhi = ld16(src + hi);
+  } else if (kind == 1) {
+    const T* src = static_cast<const T*>(p.k) + t * p.kts + (int64_t)h * p.d;
+    xlo = ld16(src + lo);
+    xhi = ld16(src + hi);
+  } else if (kind == 2) {
+    const T* src = static_cast<const T*>(p.v) + t * p.vts + (int64_t)h * p.d;
+    xlo = ld16(src + lo);
+    xhi = ld16(src + hi);
+  }
+  if constexpr (TABLE) {
+    if (kind < 2 && m.frame_ok) {
+      const T* pr = static_cast<const T*>(p.table) + m.frame * p.d;
+      plo = ld16_ro(pr + lo);
+      phi = ld16_ro(pr + hi);
+    }
+  }
+
+  float a[E], b[E];
+  unpack16<T>(xlo, a);
+  unpack16<T>(xhi, b);
+
+  if constexpr (NORM) {
+    float ss = 0.f;
+    if (kind < 2) {
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        ss = fmaf(a[e], a[e], ss);
+        ss = fmaf(b[e], b[e], ss);
+      }
+    }
+    // all lanes take part; a head's L lanes are an aligned group of the warp
+    for (int off = L >> 1; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    if (kind < 2) {
+      const T* w = static_cast<const T*>(kind == 0 ? p.qw : p.kw);
+      float wl[E], wh[E];
+      unpack16<T>(ld16_ro(w + lo), wl);
+      unpack16<T>(ld16_ro(w + hi), wh);
+      const float r = rrms_of(ss, p.d, p.eps);
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        a[e] = round_to<T>(__fmul_rn(__fmul_rn(a[e], r), wl[e]));
+        b[e] = round_to<T>(__fmul_rn(__fmul_rn(b[e], r), wh[e]));
+      }
+    }
+  }
+
+  if (kind < 2) {
+    float clo[E], slo[E], chi[E], shi[E];
+    if constexpr (CS_GIVEN) {
+      unpack16<T>(ld16_ro(static_cast<const T*>(p.cos) + lo), clo);
+      unpack16<T>(ld16_ro(static_cast<const T*>(p.cos) + hi), chi);
+      unpack16<T>(ld16_ro(static_cast<const T*>(p.sin) + lo), slo);
+      unpack16<T>(ld16_ro(static_cast<const T*>(p.sin) + hi), shi);
+    } else {
+      const float2* row = cs + tl * half + lo;
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        const float2 v = row[e];
+        clo[e] = chi[e] = v.x;
+        slo[e] = shi[e] = v.y;
+      }
+    }
+    float ylo[E], yhi[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      ylo[e] = __fadd_rn(__fmul_rn(a[e], clo[e]), __fmul_rn(-b[e], slo[e]));
+      yhi[e] = __fadd_rn(__fmul_rn(b[e], chi[e]), __fmul_rn(a[e], shi[e]));
+    }
+    if constexpr (TABLE) {
+      if (m.frame_ok) {
+        float pl[E], ph[E];
+        unpack16<T>(plo, pl);
+        unpack16<T>(phi, ph);
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          ylo[e] = __fadd_rn(ylo[e], pl[e]);
+          yhi[e] = __fadd_rn(yhi[e], ph[e]);
+        }
+      }
+    }
+    if (kind == 0) {
+      T* dst = static_cast<T*>(p.q_out) + t * p.qots + (int64_t)h * p.qohs;
+      st16(dst + lo, pack16<T>(ylo));
+      st16(dst + hi, pack16<T>(yhi));
+    } else if (m.slot_ok) {
+      T* dst = static_cast<T*>(p.k_cache) + m.b * p.cbs + (int64_t)h * p.chs + m.slot * p.css;
+      st16(dst + lo, pack16<T>(ylo));
+      st16(dst + hi, pack16<T>(yhi));
+    }
+  } else if (kind == 2 && m.slot_ok) {
+    T* dst = static_cast<T*>(p.v_cache) + m.b * p.cbs + (int64_t)h * p.chs + m.slot * p.css;
+    st16(dst + lo, xlo);
+    st16(dst + hi, xhi);
+  }
+}
+
+// ----------------------------------------------------------- generic kernel
+template <typename T, bool NORM, bool TABLE, bool CS_GIVEN>
+__global__ void __launch_bounds__(256)
+rope_generic_kernel(RopeParams p, int heads_per_tok) {
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= p.n_tokens * heads_per_tok) return;  // warp-uniform exit
+  const int64_t t = gw / heads_per_tok;
+  const int hitem = (int)(gw - t * heads_per_tok);
+  const int half = p.d >> 1;
+  const TokenMeta m = token_meta<TABLE>(p, t);
+  if (hitem == 0 && lane == 0) flag_token<TABLE>(p, m);
+
+  if (hitem >= p.hq + p.hk) {  // V copy
+    if (!m.slot_ok) return;
+    const int h = hitem - p.hq - p.hk;
+    const T* src = static_cast<const T*>(p.v) + t * p.vts + (int64_t)h * p.d;
+    T* dst = static_cast<T*>(p.v_cache) + m.b * p.cbs + (int64_t)h * p.chs + m.slot * p.css;
+    for (int i = lane; i < p.d; i += 32) dst[i] = src[i];
+    return;
+  }
+  const bool is_q = hitem < p.hq;
+  const int h = is_q ? hitem : hitem - p.hq;
+  const T* src = is_q ? static_cast<const T*>(p.q) + t * p.qts + (int64_t)h * p.d
+                      : static_cast<const T*>(p.k) + t * p.kts + (int64_t)h * p.d;
+  float r = 1.f;
+  if constexpr (NORM) {
+    float ss = 0.f;
+    for (int i = lane; i < p.d; i += 32) {
+      const float x = Elem<T>::to_f(src[i]);
+      ss = fmaf(x, x, ss);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    r = rrms_of(ss, p.d, p.eps);
+  }
+  const T* w = static_cast<const T*>(is_q ? p.qw : p.kw);
+  const float pos = CS_GIVEN ? 0.f : (float)p.positions[t];
+  const T* prow = (TABLE && m.frame_ok) ? static_cast<const T*>(p.table) + m.frame * p.d : nullptr;
+  T* dst = nullptr;
+  if (is_q) {
+    dst = static_cast<T*>(p.q_out) + t * p.qots + (int64_t)h * p.qohs;
+  } else if (m.slot_ok) {
+    dst = static_cast<T*>(p.k_cache) + m.b * p.cbs + (int64_t)h * p.chs + m.slot * p.css;
+  }
+  if (dst == nullptr) return;
+  for (int i = lane; i < half; i += 32) {
+    float a = Elem<T>::to_f(src[i]);
+    float b = Elem<T>::to_f(src[i + half]);
+    if constexpr (NORM) {
+      a = round_to<T>(__fmul_rn(__fmul_rn(a, r), Elem<T>::to_f(w[i])));
+      b = round_to<T>(__fmul_rn(__fmul_rn(b, r), Elem<T>::to_f(w[i + half])));
+    }
+    float clo, slo, chi, shi;
+    if constexpr (CS_GIVEN) {
+      const T* cp = static_cast<const T*>(p.cos);
+      const T* sp = static_cast<const T*>(p.sin);
+      clo = Elem<T>::to_f(cp[i]);
+      chi = Elem<T>::to_f(cp[i + half]);
+      slo = Elem<T>::to_f(sp[i]);
+      shi = Elem<T>::to_f(sp[i + half]);
+    } else {
+      const float ang = __fmul_rn(p.inv_freq[i], pos);
+      clo = chi = round_to<T>(cosf(ang));
+      slo = shi = round_to<T>(sinf(ang));
+    }
+    float ylo = __fadd_rn(__fmul_rn(a, clo), __fmul_rn(-b, slo));
+    float yhi = __fadd_rn(__fmul_rn(b, chi), __fmul_rn(a, shi));
+    if (prow != nullptr) {
+      ylo = __fadd_rn(ylo, Elem<T>::to_f(prow[i]));
+      yhi = __fadd_rn(yhi, Elem<T>::to_f(prow[i + half]));
+    }
+    dst[i] = Elem<T>::from_f(ylo);
+    dst[i + half] = Elem<T>::from_f(yhi);
+  }
+}
+
+// -------------------------------------------------------------- KV write
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(256)
+kv_write_kernel(const T* __restrict__ k, const T* __restrict__ v, int64_t batch, int hk, int d,
+                T* kc, T* vc, int64_t clen, const int64_t* __restrict__ wp, int per_stream,
+                int32_t* err) {
+  constexpr int E = VEC ? VecN<T>::value : 1;
+  const int vpr = d / E;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= batch * hk * vpr) return;
+  const int64_t bh = idx / vpr;
+  const int c = (int)(idx - bh * vpr);
+  const int64_t b = bh / hk;
+  const int64_t slot = per_stream ? wp[b] : wp[0];
+  const bool ok = slot >= 0 && slot < clen;
+  if (!ok) {
+    if (c == 0 && (bh - b * hk) == 0 && err != nullptr) atomicOr(err, KANI_FLAG_SLOT_OOB);
+    return;
+  }
+  const int64_t src = bh * d + (int64_t)c * E;
+  const int64_t dst = (bh * clen + slot) * d + (int64_t)c * E;
+  if constexpr (VEC) {
+    st16(kc + dst, ld16(k + src));
+    st16(vc + dst, ld16(v + src));
+  } else {
+    kc[dst] = k[src];
+    vc[dst] = v[src];
+  }
+}
+
+// ------------------------------------------------------------------ launch
+template <typename T, bool NORM, bool TABLE, bool CS_GIVEN>
+int launch_rope_t(const RopeParams& p, cudaStream_t s) {
+  constexpr int E = VecN<T>::value;
+  const int half = p.d / 2;
+  const bool has_v = p.v != nullptr;
+  int log2l = -1;
+  if (half % E == 0) {
+    const int L = half / E;
+    if (L >= 1 && L <= 32 && (L & (L - 1)) == 0) {
+      log2l = 0;
+      while ((1 << log2l) < L) ++log2l;
+    }
+  }
+  bool vec = log2l >= 0 && aligned16(p.q) && aligned16(p.k) && aligned16(p.q_out) &&
+             aligned16(p.k_cache) && p.qts % E == 0 && p.kts % E == 0 && p.qots % E == 0 &&
+             p.qohs % E == 0 && p.cbs % E == 0 && p.chs % E == 0 && p.css % E == 0;
+  if (has_v) vec = vec && aligned16(p.v) && aligned16(p.v_cache) && p.vts % E == 0;
+  if (NORM) vec = vec && aligned16(p.qw) && aligned16(p.kw);
+  if (TABLE) vec = vec && aligned16(p.table);
+  if (CS_GIVEN) vec = vec && aligned16(p.cos) && aligned16(p.sin);
+
+  if (vec) {
+    const int heads = p.hq + p.hk + (has_v ? p.hk : 0);
+    const int ipt = heads << log2l;
+    const int iptr = ((ipt + 31) / 32) * 32;
+    if (iptr <= 512) {
+      int tpb = 512 / iptr;
+      if (tpb > 4) tpb = 4;
+      if (tpb > p.n_tokens) tpb = (int)p.n_tokens;
+      const int64_t grid = (p.n_tokens + tpb - 1) / tpb;
+      if (grid <= 0x7fffffff) {
+        const size_t smem = CS_GIVEN ? 0 : (size_t)tpb * half * sizeof(float2);
+        rope_vec_kernel<T, NORM, TABLE, CS_GIVEN>
+            <<<(unsigned)grid, tpb * iptr, smem, s>>>(p, log2l, ipt, iptr, tpb);
+        return launch_status();
+      }
+    }
+  }
+  const int heads = p.hq + p.hk + (has_v ? p.hk : 0);
+  const int64_t warps = p.n_tokens * heads;
+  const int64_t grid = (warps + 7) / 8;
+  if (grid > 0x7fffffff) return KANI_ERR_UNSUPPORTED;
+  rope_generic_kernel<T, NORM, TABLE, CS_GIVEN><<<(unsigned)grid, 256, 0, s>>>(p, heads);
+  return launch_status();
+}
+
+template <typename T>
+int launch_rope(const RopeParams& p, cudaStream_t s) {
+  const bool norm = p.qw != nullptr;
+  const bool table = p.table != nullptr;
+  const bool given = p.cos != nullptr;
+  if (given) {
+    // the reference-signature path: no norm, no table
+    if (norm || table) return KANI_ERR_UNSUPPORTED;
+    return launch_rope_t<T, false, false, true>(p, s);
+  }
+  if (norm && table) return launch_rope_t<T, true, true, false>(p, s);
+  if (norm) return launch_rope_t<T, true, false, false>(p, s);
+  if (table) return launch_rope_t<T, false, true, false>(p, s);
+  return launch_rope_t<T, false, false, false>(p, s);
+}
+
+}  // namespace
+}  // namespace kani
+
+using kani::RopeParams;
+
+extern "C" int kani_rope_qk(int32_t dtype, const void* q, const void* k, const void* cos,
+                            const void* sin, void* q_out, void* k_out, int32_t num_q_heads,
+                            int32_t num_k_heads, int32_t head_dim, void* stream) {
+  if (num_q_heads < 0 || num_k_heads < 0 || head_dim < 0) return KANI_ERR_INVALID_ARG;
+  if (head_dim % 2 != 0) return KANI_ERR_UNSUPPORTED;
+  if (num_q_heads == 0 && num_k_heads == 0) return KANI_OK;
+  if (head_dim == 0) return KANI_OK;
+  if (cos == nullptr || sin == nullptr) return KANI_ERR_INVALID_ARG;
+  if (num_q_heads > 0 && (q == nullptr || q_out == nullptr)) return KANI_ERR_INVALID_ARG;
+  if (num_k_heads > 0 && (k == nullptr || k_out == nullptr)) return KANI_ERR_INVALID_ARG;
+  // An empty head group still needs 16-byte aligned dummies for the vector test.
+  if (num_q_heads == 0) { q = k; q_out = k_out; }
+  if (num_k_heads == 0) { k = q; k_out = q_out; }
+  RopeParams p{};
+  p.n_tokens = 1;
+  p.seq_tokens = 1;
+  p.hq = num_q_heads;
+  p.hk = num_k_heads;
+  p.d = head_dim;
+  p.q = q;
+  p.qts = (int64_t)num_q_heads * head_dim;
+  p.k = k;
+  p.kts = (int64_t)num_k_heads * head_dim;
+  p.cos = cos;
+  p.sin = sin;
+  p.q_out = q_out;
+  p.qots = (int64_t)num_q_heads * head_dim;
+  p.qohs = head_dim;
+  // K output viewed as a one-slot cache [1, Hk, 1, D]
+  p.k_cache = k_out;
+  p.cbs = 0;
+  p.chs = head_dim;
+  p.css = 0;
+  p.clen = 1;
+  p.tpf = 1;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return kani::dispatch_dtype(dtype, [&]<typename T>() { return kani::launch_rope<T>(p, s); });
+}
+
+extern "C" int kani_kv_cache_write(int32_t dtype, const void* k, const void* v, int64_t batch,
+                                   int32_t num_kv_heads, int32_t head_dim, void* k_cache,
+                                   void* v_cache, int64_t cache_len, const int64_t* write_pos,
+                                   int32_t per_stream_pos, int32_t* err_flag, void* stream) {
+  if (batch < 0 || num_kv_heads < 0 || head_dim < 0 || cache_len < 0) return KANI_ERR_INVALID_ARG;
+  if (batch == 0 || num_kv_heads == 0 || head_dim == 0) return KANI_OK;
+  if (!k || !v || !k_cache || !v_cache || !write_pos) return KANI_ERR_INVALID_ARG;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return kani::dispatch_dtype(dtype, [&]<typename T>() {
+    constexpr int E = kani::VecN<T>::value;
+    const bool vec = head_dim % E == 0 && kani::aligned16(k) && kani::aligned16(v) &&
+                     kani::aligned16(k_cache) && kani::aligned16(v_cache);
+    const int per = vec ? head_dim / E : head_dim;
+    const int64_t total = batch * num_kv_heads * per;
+    const int64_t grid = (total + 255) / 256;
+    if (grid > 0x7fffffff) return (int)KANI_ERR_UNSUPPORTED;
+    if (vec)
+      kani::kv_write_kernel<T, true><<<(unsigned)grid, 256, 0, s>>>(
+          static_cast<const T*>(k), static_cast<const T*>(v), batch, num_kv_heads, head_dim,
+          static_cast<T*>(k_cache), static_cast<T*>(v_cache), cache_len, write_pos,
+          per_stream_pos, err_flag);
+    else
+      kani::kv_write_kernel<T, false><<<(unsigned)grid, 256, 0, s>>>(
+          static_cast<const T*>(k), static_cast<const T*>(v), batch, num_kv_heads, head_dim,
+          static_cast<T*>(k_cache), static_cast<T*>(v_cache), cache_len, write_pos,
+          per_stream_pos, err_flag);
+    return kani::launch_status();
+  });
+}
+
+extern "C" int kani_rope_kv_write(
+    int32_t dtype, int64_t batch, int64_t seq_tokens, int32_t num_q_heads, int32_t num_kv_heads,
+    int32_t head_dim, const void* q, int64_t q_tok_stride, const void* k, int64_t k_tok_stride,
+    const void* v, int64_t v_tok_stride, const float* inv_freq, const int64_t* positions,
+    const void* q_norm_w, const void* k_norm_w, float eps, const void* frame_table,
+    int64_t frame_rows, const int64_t* frame_pos, int32_t tokens_per_frame, void* q_out,
+    int64_t q_out_tok_stride, int64_t q_out_head_stride, void* k_cache, void* v_cache,
+    int64_t cache_batch_stride, int64_t cache_head_stride, int64_t cache_slot_stride,
+    int64_t cache_len, const int64_t* write_slots, int32_t* err_flag, void* stream) {
+  if (batch < 0 || seq_tokens < 0 || num_q_heads < 0 || num_kv_heads < 0 || head_dim < 0 ||
+      cache_len < 0)
+    return KANI_ERR_INVALID_ARG;
+  if (head_dim % 2 != 0) return KANI_ERR_UNSUPPORTED;
+  const int64_t n_tokens = batch * seq_tokens;
+  if (n_tokens == 0 || head_dim == 0 || (num_q_heads == 0 && num_kv_heads == 0)) return KANI_OK;
+  if (!inv_freq || !positions) return KANI_ERR_INVALID_ARG;
+  if (num_q_heads > 0 && (!q || !q_out)) return KANI_ERR_INVALID_ARG;
+  if (num_kv_heads > 0 && (!k || !v || !k_cache || !v_cache)) return KANI_ERR_INVALID_ARG;
+  if ((q_norm_w == nullptr) != (k_norm_w == nullptr)) return KANI_ERR_INVALID_ARG;
+  if (frame_table != nullptr && (frame_rows < 0 || tokens_per_frame <= 0))
+    return KANI_ERR_INVALID_ARG;
+  // Empty head groups: point the unused side at the used one so the
+  // alignment test sees real pointers; no item of that kind is generated.
+  if (num_q_heads == 0) { q = k; q_out = k_cache; q_tok_stride = k_tok_stride; }
+  if (num_kv_heads == 0) {
+    k = q; v = nullptr; k_cache = q_out; v_cache = nullptr; k_tok_stride = q_tok_stride;
+  }
+  RopeParams p{};
+  p.n_tokens = n_tokens;
+  p.seq_tokens = seq_tokens;
+  p.hq = num_q_heads;
+  p.hk = num_kv_heads;
+  p.d = head_dim;
+  p.q = q;
+  p.qts = q_tok_stride;
+  p.k = k;
+  p.kts = k_tok_stride;
+  p.v = v;
+  p.vts = v_tok_stride;
+  p.inv_freq = inv_freq;
+  p.positions = positions;
+  p.qw = q_norm_w;
+  p.kw = k_norm_w;
+  p.eps = eps;
+  p.table = frame_table;
+  p.table_rows = frame_rows;
+  p.frame_pos = frame_pos;
+  p.tpf = tokens_per_frame > 0 ? tokens_per_frame : 1;
+  p.q_out = q_out;
+  p.qots = q_out_tok_stride;
+  p.qohs = q_out_head_stride;
+  p.k_cache = k_cache;
+  p.v_cache = v_cache;
+  p.cbs = cache_batch_stride;
+  p.chs = cache_head_stride;
+  p.css = cache_slot_stride;
+  // without KV heads there is no cache write, so no slot can be out of range
+  p.clen = num_kv_heads == 0 ? INT64_MAX : cache_len;
+  p.slots = num_kv_heads == 0 ? nullptr : write_slots;
+  p.err = err_flag;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return kani::dispatch_dtype(dtype, [&]<typename T>() { return kani::launch_rope<T>(p, s); });
+}

@@ -1,0 +1,359 @@
+"""Drop-in replacements for ``kani_tts/triton_kernels.py`` plus the fused entry points.
+
+Same names, argument meaning and return values as the reference module
+(``fused_rms_norm``, ``fused_silu_mul``, ``fused_rope``), so
+``kani_tts/optimized_decode.py:14`` can bind them unchanged, plus:
+
+* ``fused_add_rms_norm`` — the residual add of optimized_decode.py:252/277/283
+  folded into the following RMSNorm;
+* ``kv_cache_write`` — the scatter_ of static_cache.py:131-140;
+* ``fused_rope_kv_write`` — q/k norm + cos/sin + RoPE (+ BemaTTS frame term)
+  + KV write of optimized_decode.py:220-240 in one launch.
+
+Each call validates its tensors on the host (device, dtype, shape) before a
+single launch through the C ABI on the current CUDA stream; nothing
+synchronises, so every op is capturable in a CUDA graph.  Differences from
+the reference, all deliberate:
+
+* an fp32 input to ``fused_rms_norm`` gives a true fp32 result (the Triton
+  kernel stores bf16-rounded values into an fp32 tensor,
+  triton_kernels.py:35/53);
+* ``fused_rope`` is one launch for Q and K (the reference launches twice,
+  triton_kernels.py:160-163);
+* invalid input raises ``TypeError`` / ``ValueError`` before any launch (the
+  reference wrappers do not validate).
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+from ._lib import check, dtype_code, error_flag, load_library, ptr, require_cuda, stream_ptr
+
+__all__ = [
+    "fused_rms_norm",
+    "fused_add_rms_norm",
+    "fused_silu_mul",
+    "fused_rope",
+    "kv_cache_write",
+    "fused_rope_kv_write",
+]
+
+
+def _rows_view(t: torch.Tensor, n: int) -> tuple[torch.Tensor, int, int]:
+    """View ``t`` as [rows, n] rows with a uniform row stride (copying if needed)."""
+    if t.dim() == 0 or t.shape[-1] != n:
+        raise ValueError(f"expected last dimension {n}, got shape {tuple(t.shape)}")
+    if t.stride(-1) != 1:
+        t = t.contiguous()
+    rows = t.numel() // n if n else 0
+    if rows <= 1:
+        return t, rows, n
+    # leading dims must collapse to one stride
+    lead = [(s, st) for s, st in zip(t.shape[:-1], t.stride()[:-1]) if s != 1]
+    stride = lead[-1][1] if lead else n
+    if stride < n:  # overlapping rows (e.g. an expanded view)
+        t = t.contiguous()
+        return t, rows, n
+    expect = stride
+    for s, st in reversed(lead):
+        if st != expect:
+            t = t.contiguous()
+            return t, rows, n
+        expect = st * s
+    return t, rows, stride
+
+
+def fused_rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """RMSNorm over the last dim (reference ``fused_rms_norm``, triton_kernels.py:38-60).
+
+    Args:
+        x: [..., N] bf16 / fp16 / fp32 CUDA tensor.
+        weight: [N] norm weight (bf16 / fp16 / fp32).
+        eps: epsilon added to mean(x^2).
+    Returns:
+        [..., N] tensor of x's dtype.
+    """
+    require_cuda(x, "x")
+    require_cuda(weight, "weight")
+    lib = load_library()
+    n = x.shape[-1] if x.dim() else 0
+    if weight.dim() != 1 or weight.shape[0] != n:
+        raise ValueError(f"weight must have shape [{n}], got {tuple(weight.shape)}")
+    if weight.device != x.device:
+        raise ValueError("x and weight must be on the same device")
+    code, wcode = dtype_code(x, "x"), dtype_code(weight, "weight")
+    weight = weight.contiguous()
+    xv, rows, xs = _rows_view(x, n)
+    y = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    check(lib.kani_rms_norm(code, wcode, ptr(xv), xs, ptr(weight), ptr(y), n, rows, n, float(eps),
+                            stream_ptr(x.device)), "kani_rms_norm")
+    return y
+
+
+def fused_add_rms_norm(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor,
+                       eps: float = 1e-6, out: torch.Tensor | None = None,
+                       residual_out: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """``h = x + residual`` (rounded to the dtype, like the eager add) then RMSNorm of h.
+
+    Replaces ``hidden = hidden + F.linear(...)`` (optimized_decode.py:252, 277, 283)
+    plus the next ``fused_rms_norm``.  Returns ``(normed, h)``.  ``out`` /
+    ``residual_out`` may be given for in-place use (``residual_out=residual``
+    updates the residual stream in place); they must be contiguous.
+    """
+    for t, w in ((x, "x"), (residual, "residual"), (weight, "weight")):
+        require_cuda(t, w)
+    lib = load_library()
+    if x.shape != residual.shape:
+        raise ValueError(f"x {tuple(x.shape)} and residual {tuple(residual.shape)} differ in shape")
+    if x.dtype != residual.dtype:
+        raise TypeError(f"x ({x.dtype}) and residual ({residual.dtype}) differ in dtype")
+    n = x.shape[-1] if x.dim() else 0
+    if weight.dim() != 1 or weight.shape[0] != n:
+        raise ValueError(f"weight must have shape [{n}], got {tuple(weight.shape)}")
+    if not (x.device == residual.device == weight.device):
+        raise ValueError("x, residual and weight must be on the same device")
+    code, wcode = dtype_code(x, "x"), dtype_code(weight, "weight")
+    weight = weight.contiguous()
+    xv, rows, xs = _rows_view(x, n)
+    rv, _, rs = _rows_view(residual, n)
+    for t, w in ((out, "out"), (residual_out, "residual_out")):
+        if t is not None:
+            require_cuda(t, w)
+            if t.shape != x.shape or t.dtype != x.dtype or not t.is_contiguous() or t.device != x.device:
+                raise ValueError(f"{w} must be a contiguous tensor like x")
+    y = out if out is not None else torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    h = residual_out if residual_out is not None else torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    if y.data_ptr() == h.data_ptr() and y.numel() > 0:
+        raise ValueError("out and residual_out must be different tensors")
+    check(lib.kani_add_rms_norm(code, wcode, ptr(xv), xs, ptr(rv), rs, ptr(weight), ptr(y), n, ptr(h), n,
+                                rows, n, float(eps), stream_ptr(x.device)), "kani_add_rms_norm")
+    return y, h
+
+
+def fused_silu_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """SiLU(gate) * up from a concatenated [gate | up] tensor (triton_kernels.py:85-105).
+
+    Args:
+        gate_up: [..., 2 * intermediate_size].
+    Returns:
+        [..., intermediate_size] of gate_up's dtype.
+    """
+    require_cuda(gate_up, "gate_up")
+    lib = load_library()
+    code = dtype_code(gate_up, "gate_up")
+    if gate_up.dim() == 0 or gate_up.shape[-1] % 2 != 0:
+        raise ValueError(f"gate_up last dimension must be even, got shape {tuple(gate_up.shape)}")
+    two_n = gate_up.shape[-1]
+    n = two_n // 2
+    gv, rows, gs = _rows_view(gate_up, two_n)
+    shape = (*gate_up.shape[:-1], n)
+    if out is None:
+        out = torch.empty(shape, dtype=gate_up.dtype, device=gate_up.device)
+    else:
+        require_cuda(out, "out")
+        if tuple(out.shape) != shape or out.dtype != gate_up.dtype or not out.is_contiguous():
+            raise ValueError(f"out must be a contiguous {gate_up.dtype} tensor of shape {shape}")
+    check(lib.kani_silu_mul(code, ptr(gv), gs, ptr(out), n, rows, n, stream_ptr(gate_up.device)),
+          "kani_silu_mul")
+    return out
+
+
+def fused_rope(q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor):
+    """Rotate-half RoPE on Q and K with one cos/sin row (triton_kernels.py:134-165).
+
+    Args:
+        q: [1, num_q_heads, 1, head_dim]; k: [1, num_k_heads, 1, head_dim].
+        cos, sin: head_dim elements (any shape), same dtype as q.
+    Returns:
+        (q_rotated, k_rotated), same shapes as q and k.
+    """
+    for t, w in ((q, "q"), (k, "k"), (cos, "cos"), (sin, "sin")):
+        require_cuda(t, w)
+    lib = load_library()
+    code = dtype_code(q, "q")
+    if not (k.dtype == cos.dtype == sin.dtype == q.dtype):
+        raise TypeError("q, k, cos and sin must share one dtype")
+    if q.dim() < 2 or k.dim() < 2:
+        raise ValueError("q and k must be [1, heads, 1, head_dim]")
+    num_q, num_k, hd = q.shape[1], k.shape[1], q.shape[-1]
+    if k.shape[-1] != hd or q.numel() != num_q * hd or k.numel() != num_k * hd:
+        raise ValueError(f"q {tuple(q.shape)} / k {tuple(k.shape)} are not [1, heads, 1, head_dim]")
+    if cos.numel() != hd or sin.numel() != hd:
+        raise ValueError(f"cos and sin must hold head_dim={hd} elements")
+    if hd % 2:
+        raise ValueError(f"head_dim must be even, got {hd}")
+    qf, kf = q.contiguous(), k.contiguous()
+    cf, sf = cos.contiguous(), sin.contiguous()
+    q_out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    k_out = torch.empty(k.shape, dtype=k.dtype, device=k.device)
+    check(lib.kani_rope_qk(code, ptr(qf), ptr(kf), ptr(cf), ptr(sf), ptr(q_out), ptr(k_out),
+                           num_q, num_k, hd, stream_ptr(q.device)), "kani_rope_qk")
+    return q_out, k_out
+
+
+def kv_cache_write(key_states: torch.Tensor, value_states: torch.Tensor, k_cache: torch.Tensor,
+                   v_cache: torch.Tensor, write_pos: torch.Tensor,
+                   err_flag: torch.Tensor | None = None) -> None:
+    """``cache[b, h, slot, :] = states[b, h, 0, :]`` for K and V (static_cache.py:131-140).
+
+    ``write_pos`` is a device int64 tensor: one element (shared by the batch,
+    as in the reference) or one per stream.  A slot outside the cache is
+    skipped and flagged in ``err_flag`` (default: the per-device flag).
+    """
+    for t, w in ((key_states, "key_states"), (value_states, "value_states"), (k_cache, "k_cache"),
+                 (v_cache, "v_cache"), (write_pos, "write_pos")):
+        require_cuda(t, w)
+    lib = load_library()
+    code = dtype_code(k_cache, "k_cache")
+    if k_cache.dim() != 4 or v_cache.shape != k_cache.shape:
+        raise ValueError("k_cache / v_cache must both be [batch, kv_heads, max_len, head_dim]")
+    b, hk, s, d = k_cache.shape
+    exp = (b, hk, 1, d)
+    if tuple(key_states.shape) != exp or tuple(value_states.shape) != exp:
+        raise ValueError(f"key/value states must be {exp}, got {tuple(key_states.shape)} / "
+                         f"{tuple(value_states.shape)}")
+    if not (key_states.dtype == value_states.dtype == v_cache.dtype == k_cache.dtype):
+        raise TypeError("states and caches must share one dtype")
+    if not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise ValueError("k_cache and v_cache must be contiguous")
+    if write_pos.dtype != torch.int64 or write_pos.numel() not in (1, b):
+        raise ValueError(f"write_pos must be int64 with 1 or {b} elements")
+    wp = write_pos.contiguous()
+    ks, vs = key_states.contiguous(), value_states.contiguous()
+    flag = err_flag if err_flag is not None else error_flag(k_cache.device)
+    per_stream = 1 if (wp.numel() == b and b > 1) else 0
+    check(lib.kani_kv_cache_write(code, ptr(ks), ptr(vs), b, hk, d, ptr(k_cache), ptr(v_cache), s,
+                                  ptr(wp), per_stream, ptr(flag), stream_ptr(k_cache.device)),
+          "kani_kv_cache_write")
+
+
+def _token_view(t: torch.Tensor, heads: int, d: int, what: str) -> tuple[int, int]:
+    """Check t is [*lead, heads, d] with heads at stride d; return (tokens, token stride)."""
+    if t.dim() < 2 or t.shape[-1] != d or t.shape[-2] != heads:
+        raise ValueError(f"{what} must end in [{heads}, {d}], got {tuple(t.shape)}")
+    if t.stride(-1) != 1 or (heads > 1 and t.stride(-2) != d):
+        raise ValueError(f"{what} must have contiguous heads (strides [..., {d}, 1]), got {t.stride()}")
+    lead = [(s, st) for s, st in zip(t.shape[:-2], t.stride()[:-2]) if s != 1]
+    tokens = math.prod(t.shape[:-2])
+    if not lead:
+        return tokens, heads * d
+    stride = lead[-1][1]
+    expect = stride
+    for s, st in reversed(lead):
+        if st != expect:
+            raise ValueError(f"{what}: leading dims of shape {tuple(t.shape[:-2])} / strides "
+                             f"{t.stride()[:-2]} do not collapse to one token stride")
+        expect = st * s
+    return tokens, stride
+
+
+def fused_rope_kv_write(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, inv_freq: torch.Tensor,
+                        position: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                        write_pos: torch.Tensor, frame_table: torch.Tensor | None = None,
+                        tokens_per_frame: int = 4, q_norm_w: torch.Tensor | None = None,
+                        k_norm_w: torch.Tensor | None = None, eps: float = 1e-5,
+                        frame_pos: torch.Tensor | None = None, q_out: torch.Tensor | None = None,
+                        err_flag: torch.Tensor | None = None) -> torch.Tensor:
+    """Fused q/k-norm + RoPE (+ frame term) + static KV write for a batch of tokens.
+
+    Replaces optimized_decode.py:220-240.  Shapes (B streams x T tokens):
+        q: [B, T, Hq, D], k / v: [B, T, Hk, D]  (views into a packed QKV output are fine:
+           heads must be contiguous, leading dims must collapse to one token stride)
+        inv_freq: [D/2] fp32 (learnable-alpha frequencies of the layer)
+        position: [B, T] int64 angle positions (BemaTTS frame-level position ids)
+        k_cache / v_cache: [B, Hk, S, D] (last dim contiguous)
+        write_pos: [B, T] int64 KV slots
+        frame_table: optional [F, D]; row = frame_pos // tokens_per_frame
+           (frame_pos defaults to position), added to rotated Q and K
+        q_norm_w / k_norm_w: optional [D] per-head RMSNorm weights (both or neither)
+        q_out: optional output, indexed like q ([B, T, Hq, D] view; may be the
+           transpose of a [B, Hq, T, D] tensor when B == 1 or T == 1)
+    Returns q_out (rotated Q).  K and V land in the caches.  Slots or frame
+    rows out of range are skipped and flagged in ``err_flag``.
+    """
+    for t, w in ((q, "q"), (k, "k"), (v, "v"), (inv_freq, "inv_freq"), (position, "position"),
+                 (k_cache, "k_cache"), (v_cache, "v_cache"), (write_pos, "write_pos")):
+        require_cuda(t, w)
+    lib = load_library()
+    code = dtype_code(q, "q")
+    if not (k.dtype == v.dtype == k_cache.dtype == v_cache.dtype == q.dtype):
+        raise TypeError("q, k, v and the caches must share one dtype")
+    if q.dim() < 3:
+        raise ValueError("q must be [..., heads, head_dim] with a token dimension")
+    hq, d = q.shape[-2], q.shape[-1]
+    if k_cache.dim() != 4 or v_cache.shape != k_cache.shape or k_cache.shape[-1] != d:
+        raise ValueError("k_cache / v_cache must both be [batch, kv_heads, max_len, head_dim]")
+    bsz, hk, s_len, _ = k_cache.shape
+    nq, qts = _token_view(q, hq, d, "q")
+    nk, kts = _token_view(k, hk, d, "k")
+    nv, vts = _token_view(v, hk, d, "v")
+    if not (nq == nk == nv):
+        raise ValueError(f"q, k and v hold different token counts ({nq}, {nk}, {nv})")
+    if nq % bsz:
+        raise ValueError(f"{nq} tokens do not split over a cache batch of {bsz}")
+    seq_tokens = nq // bsz
+    if inv_freq.dtype != torch.float32 or inv_freq.numel() != d // 2:
+        raise ValueError(f"inv_freq must be fp32 with head_dim/2 = {d // 2} elements")
+    for t, w in ((position, "position"), (write_pos, "write_pos")) + (
+            ((frame_pos, "frame_pos"),) if frame_pos is not None else ()):
+        if t.dtype != torch.int64 or t.numel() != nq:
+            raise ValueError(f"{w} must be int64 with one element per token ({nq})")
+    if (q_norm_w is None) != (k_norm_w is None):
+        raise ValueError("q_norm_w and k_norm_w must be given together")
+    if q_norm_w is not None:
+        for t, w in ((q_norm_w, "q_norm_w"), (k_norm_w, "k_norm_w")):
+            require_cuda(t, w)
+            if t.dtype != q.dtype or t.numel() != d:
+                raise ValueError(f"{w} must be a {q.dtype} tensor of head_dim={d} elements")
+    frame_rows = 0
+    if frame_table is not None:
+        require_cuda(frame_table, "frame_table")
+        if frame_table.dtype != q.dtype or frame_table.dim() != 2 or frame_table.shape[1] != d:
+            raise ValueError(f"frame_table must be a {q.dtype} [rows, {d}] tensor")
+        if tokens_per_frame <= 0:
+            raise ValueError("tokens_per_frame must be positive")
+        frame_table = frame_table.contiguous()
+        frame_rows = frame_table.shape[0]
+    if k_cache.stride(-1) != 1 or k_cache.stride() != v_cache.stride():
+        raise ValueError("k_cache and v_cache need the same strides with a contiguous last dim")
+    if q_out is None:
+        q_out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+        qots, qohs = hq * d, d
+    else:
+        require_cuda(q_out, "q_out")
+        if q_out.shape != q.shape or q_out.dtype != q.dtype or q_out.stride(-1) != 1:
+            raise ValueError("q_out must be indexed like q with a contiguous last dim")
+        lead = [(s, st) for s, st in zip(q_out.shape[:-2], q_out.stride()[:-2]) if s != 1]
+        qots = lead[-1][1] if lead else hq * d
+        expect = qots
+        for s, st in reversed(lead):
+            if st != expect:
+                raise ValueError("q_out leading dims do not collapse to one token stride")
+            expect = st * s
+        qohs = q_out.stride(-2)
+    dev = q.device
+    flag = err_flag if err_flag is not None else error_flag(dev)
+    cs = k_cache.stride()
+    pos_c, wp_c = position.contiguous(), write_pos.contiguous()
+    fp_c = frame_pos.contiguous() if frame_pos is not None else None
+    inv_c = inv_freq.contiguous()
+    qw = q_norm_w.contiguous() if q_norm_w is not None else None
+    kw = k_norm_w.contiguous() if k_norm_w is not None else None
+    check(lib.kani_rope_kv_write(
+        code, bsz, seq_tokens, hq, hk, d,
+        ptr(q), qts, ptr(k), kts, ptr(v), vts,
+        ptr(inv_c), ptr(pos_c),
+        ptr(qw), ptr(kw), float(eps),
+        ptr(frame_table), frame_rows, ptr(fp_c), int(tokens_per_frame),
+        ptr(q_out), qots, qohs,
+        ptr(k_cache), ptr(v_cache), cs[0], cs[1], cs[2], s_len,
+        ptr(wp_c), ptr(flag), stream_ptr(dev)), "kani_rope_kv_write")
+    return q_out
+
+
+def launch_count() -> int:
+    """Kernel launches issued by the library so far in this process."""
+    return _lib.launch_count()

@@ -1,0 +1,206 @@
+"""Generate the golden vectors in tests/golden/*.npz from the reference itself.
+
+Run in a container that has the reference checkout (default
+/root/reference, override with KANI_REFERENCE_DIR):
+
+    python tests/golden/make_golden.py
+
+What runs, all on the CPU:
+  * the reference's three Triton kernels (kani_tts/triton_kernels.py) under
+    the Triton interpreter (TRITON_INTERPRET=1);
+  * StaticLfm2HybridConvCache.update (kani_tts/static_cache.py);
+  * LearnableRotaryEmbedding and compute_frame_level_positions
+    (kani_tts/model.py);
+  * HF Lfm2RMSNorm (the eager norm the reference's model uses) for the
+    fp32 residual-add + norm case.
+The reference package __init__ imports NeMo, which is absent, so a bare
+``kani_tts`` package object pointing at the checkout is registered instead;
+the static cache and model modules import ``Lfm2HybridConvCache``, which the
+installed transformers no longer has, so a placeholder class is added.  The
+reference files are read, never modified.
+
+Inputs are seeded (torch.Generator per tensor, seeds 0, 1, 2, ... in argument
+order) and saved next to the outputs; bf16 tensors are stored as their uint16
+bit patterns (key suffix ``__bf16``).
+"""
+from __future__ import annotations
+
+import importlib
+import os
+import sys
+import types
+from pathlib import Path
+
+import numpy as np
+
+os.environ["TRITON_INTERPRET"] = "1"
+import torch  # noqa: E402
+
+REF = Path(os.environ.get("KANI_REFERENCE_DIR", "/root/reference"))
+OUT = Path(__file__).resolve().parent
+
+
+def _import_reference():
+    import transformers.models.lfm2.modeling_lfm2 as hf
+    if not hasattr(hf, "Lfm2HybridConvCache"):
+        class Lfm2HybridConvCache:  # placeholder for the removed HF class (type use only)
+            pass
+        hf.Lfm2HybridConvCache = Lfm2HybridConvCache
+    pkg = types.ModuleType("kani_tts")
+    pkg.__path__ = [str(REF / "kani_tts")]
+    sys.modules["kani_tts"] = pkg
+    tk = importlib.import_module("kani_tts.triton_kernels")
+    sc = importlib.import_module("kani_tts.static_cache")
+    md = importlib.import_module("kani_tts.model")
+    return tk, sc, md, hf
+
+
+def _gen(seed: int) -> torch.Generator:
+    return torch.Generator().manual_seed(seed)
+
+
+def randn(shape, seed, dtype=torch.bfloat16, mean=0.0, std=1.0):
+    return (mean + std * torch.randn(shape, generator=_gen(seed))).to(dtype)
+
+
+def pack(d: dict) -> dict:
+    out = {}
+    for k, v in d.items():
+        if isinstance(v, torch.Tensor):
+            if v.dtype == torch.bfloat16:
+                out[k + "__bf16"] = v.contiguous().view(torch.int16).numpy().view(np.uint16)
+            else:
+                out[k] = v.contiguous().numpy()
+        else:
+            out[k] = np.asarray(v)
+    return out
+
+
+def save(name: str, cases: dict[str, dict]) -> None:
+    flat = {}
+    for case, d in cases.items():
+        for k, v in pack(d).items():
+            flat[f"{case}/{k}"] = v
+    np.savez_compressed(OUT / f"{name}.npz", **flat)
+    print(f"wrote {name}.npz: {len(cases)} cases")
+
+
+def make_config(hf, hidden=1024, heads=16, kv_heads=8, layers=2, layer_types=None, theta=1e6):
+    from transformers import Lfm2Config
+    cfg = Lfm2Config(hidden_size=hidden, num_attention_heads=heads, num_key_value_heads=kv_heads,
+                     num_hidden_layers=layers, layer_types=layer_types or ["conv", "full_attention"])
+    cfg.rope_theta = theta
+    return cfg
+
+
+def main() -> None:
+    tk, sc, md, hf = _import_reference()
+
+    # ---------------------------------------------------- Triton RMSNorm
+    cases = {}
+    for name, shape, n, dtype in [("hidden_bf16", (4, 1024), 1024, torch.bfloat16),
+                                  ("decode_bf16", (1, 1, 1024), 1024, torch.bfloat16),
+                                  ("qnorm_bf16", (1, 1, 16, 64), 64, torch.bfloat16),
+                                  ("knorm_bf16", (1, 1, 8, 64), 64, torch.bfloat16),
+                                  ("odd_bf16", (3, 100), 100, torch.bfloat16),
+                                  ("fp32_storage", (8, 1024), 1024, torch.float32)]:
+        x = randn(shape, 0, dtype)
+        w = randn((n,), 1, dtype, mean=1.0, std=0.02)
+        eps = 1e-5
+        y = tk.fused_rms_norm(x, w, eps)
+        cases[name] = dict(x=x, w=w, eps=np.float32(eps), y=y)
+    save("triton_rms_norm", cases)
+
+    # ------------------------------------- residual add + norm (eager paths)
+    cases = {}
+    x = randn((8, 1024), 0, torch.float32)
+    r = randn((8, 1024), 1, torch.float32)
+    g = randn((1024,), 2, torch.float32, mean=1.0, std=0.02)
+    norm = hf.Lfm2RMSNorm(1024, eps=1e-5)
+    with torch.no_grad():
+        norm.weight.copy_(g)
+        h = x + r
+        y = norm(h)
+    cases["config1_fp32_hf"] = dict(x=x, r=r, w=g, eps=np.float32(1e-5), h=h, y=y)
+    xb = randn((4, 1024), 3, torch.bfloat16)
+    rb = randn((4, 1024), 4, torch.bfloat16)
+    wb = randn((1024,), 5, torch.bfloat16, mean=1.0, std=0.02)
+    hb = xb + rb                                   # optimized_decode.py:252 (bf16 eager add)
+    yb = tk.fused_rms_norm(hb, wb, 1e-5)           # next norm (optimized_decode.py:280)
+    cases["decode_bf16_triton"] = dict(x=xb, r=rb, w=wb, eps=np.float32(1e-5), h=hb, y=yb)
+    save("add_rms_norm", cases)
+
+    # ------------------------------------------------------ Triton SiLU*mul
+    cases = {}
+    for name, shape in [("rows4_bf16", (4, 9216)), ("decode_bf16", (1, 1, 9216)),
+                        ("odd_bf16", (3, 200))]:
+        gu = randn(shape, 0)
+        cases[name] = dict(gate_up=gu, y=tk.fused_silu_mul(gu))
+    save("triton_silu_mul", cases)
+
+    # ------------------------------- learnable-alpha inv_freq (model.py:141-196)
+    cases = {}
+    cfg = make_config(hf)
+    for i, wa in enumerate([0.0, 0.3, -1.2]):
+        rope = md.LearnableRotaryEmbedding(cfg, layer_idx=1, total_attention_layers=1)
+        with torch.no_grad():
+            rope.alpha_weight.fill_(wa)
+            inv = (rope.inv_freq_base * rope.alpha).float()   # optimized_decode.py:108
+        cases[f"alpha{i}"] = dict(head_dim=np.int64(64), theta=np.float64(1e6),
+                                  alpha_weight=np.float32(wa), inv_freq=inv)
+    save("inv_freq", cases)
+
+    # ------------------------------------- Triton RoPE with decode cos/sin rows
+    cases = {}
+    rope = md.LearnableRotaryEmbedding(cfg, layer_idx=1, total_attention_layers=1)
+    with torch.no_grad():
+        inv = (rope.inv_freq_base * rope.alpha).float()
+    for i, pos in enumerate([0, 1, 777, 2047]):
+        q = randn((1, 16, 1, 64), 2 * i)
+        k = randn((1, 8, 1, 64), 2 * i + 1)
+        # optimized_decode.py:229-234
+        p = torch.tensor([[pos]], dtype=torch.long)[0, 0].float()
+        freqs = inv * p
+        emb = torch.cat([freqs, freqs])
+        cos, sin = emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16)
+        qo, ko = tk.fused_rope(q, k, cos, sin)
+        cases[f"pos{pos}"] = dict(q=q, k=k, cos=cos, sin=sin, inv_freq=inv, pos=np.int64(pos),
+                                  q_out=qo, k_out=ko)
+    save("triton_rope", cases)
+
+    # ------------------------------------------- static cache update (scatter_)
+    cases = {}
+    for name, bsz, slot in [("b1_slot5", 1, 5), ("b2_slot0", 2, 0), ("b1_last", 1, 15)]:
+        cache = sc.StaticLfm2HybridConvCache(cfg, max_total_len=16, batch_size=bsz,
+                                             dtype=torch.bfloat16, device="cpu")
+        k_prev = randn((bsz, 8, 16, 64), 10)
+        v_prev = randn((bsz, 8, 16, 64), 11)
+        cache.key_cache[1].copy_(k_prev)
+        cache.value_cache[1].copy_(v_prev)
+        k = randn((bsz, 8, 1, 64), 12)
+        v = randn((bsz, 8, 1, 64), 13)
+        cache.set_write_position(slot)
+        kf, vf = cache.update(k, v, 1)
+        cases[name] = dict(k_prev=k_prev, v_prev=v_prev, k=k, v=v, slot=np.int64(slot),
+                           k_cache=kf.clone(), v_cache=vf.clone())
+    save("static_cache_update", cases)
+
+    # ------------------------------------------------ frame-level positions
+    cases = {}
+    ids_doc = torch.tensor([[100, 200, 64410, 68442, 72474, 76506, 300]])
+    for i, step in enumerate([1.0, 0.5]):
+        cases[f"docstring_step{i}"] = dict(
+            input_ids=ids_doc, audio_tokens_start=np.int64(64410), tokens_per_frame=np.int64(4),
+            audio_step=np.float64(step),
+            positions=md.compute_frame_level_positions(ids_doc, 64410, 4, step).float())
+    ids_mix = torch.randint(0, 80000, (2, 40), generator=_gen(7))
+    cases["mixed_step1"] = dict(
+        input_ids=ids_mix, audio_tokens_start=np.int64(64410), tokens_per_frame=np.int64(4),
+        audio_step=np.float64(1.0),
+        positions=md.compute_frame_level_positions(ids_mix, 64410, 4, 1.0).float())
+    save("frame_positions", cases)
+    print("golden vectors written to", OUT)
+
+
+if __name__ == "__main__":
+    main()

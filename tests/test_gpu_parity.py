@@ -1,0 +1,484 @@
+"""GPU parity of every kernel against the CPU oracle and the reference goldens.
+
+Tolerances (written per test):
+  * fp32 outputs: relative error <= 1e-5 against the oracle / HF eager;
+  * bf16 / fp16 outputs: <= 1 ULP against the oracle's reference algorithm
+    (nearest-even store; the only differences come from the sum-of-squares
+    order, exp and sin/cos), with >= 99.9 % of elements bit-identical;
+    <= 1 ULP against the Triton-interpreter goldens (which truncate);
+    <= 2 ULP against the eager PyTorch/HF compositions;
+  * KV-cache slots and V copies: bit-exact, and no other slot changes.
+"""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from golden_io import load
+from oracle import kani_oracle as O
+
+from kani_tts_b200 import StaticKVCache, fused_kernels as K, positions as P
+from kani_tts_b200 import _lib
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+
+
+def rnd(shape, seed, dtype=torch.bfloat16, mean=0.0, std=1.0):
+    g = torch.Generator().manual_seed(seed)
+    return (mean + std * torch.randn(shape, generator=g)).to(dtype)
+
+
+def gpu(t):
+    return t.to(DEV)
+
+
+def ulp(a, b):
+    return O.ulp_distance(a.cpu(), b.cpu())
+
+
+def assert_close_ulp(got, ref, max_ulp=1, min_exact=0.999):
+    d = ulp(got, ref)
+    assert int(d.max()) <= max_ulp, f"max ULP {int(d.max())}"
+    if d.numel():
+        assert float((d == 0).float().mean()) >= min_exact, f"exact fraction {float((d == 0).float().mean())}"
+
+
+def assert_rel(got, ref, tol=1e-5):
+    got, ref = got.cpu().float(), ref.cpu().float()
+    rel = ((got - ref).abs() / ref.abs().clamp_min(1e-30))
+    assert float(rel.max()) <= tol, float(rel.max())
+
+
+@pytest.fixture(autouse=True)
+def _clear_flags():
+    _lib.read_and_clear_errors(DEV)
+    yield
+
+
+# ---------------------------------------------------------------- RMSNorm
+
+
+@pytest.mark.parametrize("case", ["hidden_bf16", "decode_bf16", "qnorm_bf16", "knorm_bf16", "odd_bf16"])
+def test_rms_norm_vs_reference_golden(case):
+    c = load("triton_rms_norm")[case]
+    y = K.fused_rms_norm(gpu(c["x"]), gpu(c["w"]), float(c["eps"]))
+    assert y.shape == c["x"].shape and y.dtype == c["x"].dtype
+    assert int(ulp(y, c["y"]).max()) <= 1                       # interpreter truncates
+    assert_close_ulp(y, O.rms_norm_ref(c["x"], c["w"], float(c["eps"])))
+    assert int(ulp(y, O.eager_rms_norm_hf(c["x"], c["w"], float(c["eps"]))).max()) <= 2
+
+
+def test_rms_norm_fp32_is_true_fp32():
+    c = load("triton_rms_norm")["fp32_storage"]
+    y = K.fused_rms_norm(gpu(c["x"]), gpu(c["w"]), float(c["eps"]))
+    assert y.dtype == torch.float32
+    assert_rel(y, O.rms_norm_ref(c["x"], c["w"], float(c["eps"])), 1e-5)
+    assert_rel(y, O.eager_rms_norm_hf(c["x"], c["w"], float(c["eps"])), 1e-5)
+    assert not torch.equal(y.cpu(), y.cpu().to(torch.bfloat16).float())
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("n", [64, 100, 1024, 2048, 4096, 8192, 12000])
+@pytest.mark.parametrize("rows", [1, 3, 257])
+def test_rms_norm_shapes(dtype, n, rows):
+    x = rnd((rows, n), 0, dtype)
+    w = rnd((n,), 1, dtype, 1.0, 0.02)
+    y = K.fused_rms_norm(gpu(x), gpu(w), 1e-5)
+    ref = O.rms_norm_ref(x, w, 1e-5)
+    if dtype == torch.float32:
+        assert_rel(y, ref, 1e-5)
+    else:
+        assert_close_ulp(y, ref, 1, 0.995)
+
+
+def test_rms_norm_mixed_weight_dtype_and_strided_rows():
+    base = rnd((33, 1536), 2, torch.float32)
+    x = gpu(base)[:, :1024]                       # row stride 1536: vector path with a stride
+    w = rnd((1024,), 3, torch.bfloat16, 1.0, 0.02)
+    y = K.fused_rms_norm(x, gpu(w), 1e-5)
+    assert_rel(y, O.rms_norm_ref(base[:, :1024], w, 1e-5), 1e-5)
+
+
+def test_rms_norm_misaligned_uses_generic_path():
+    buf = gpu(rnd((5 * 1024 + 1,), 4))
+    x = buf[1:].view(5, 1024)                    # 2-byte offset: not 16-byte aligned
+    w = rnd((1024,), 5, torch.bfloat16, 1.0, 0.02)
+    y = K.fused_rms_norm(x, gpu(w), 1e-5)
+    assert_close_ulp(y, O.rms_norm_ref(x.cpu(), w, 1e-5))
+
+
+# ------------------------------------------------------ residual + RMSNorm
+
+
+def test_add_rms_norm_config1_fp32_vs_hf_golden():
+    c = load("add_rms_norm")["config1_fp32_hf"]
+    y, h = K.fused_add_rms_norm(gpu(c["x"]), gpu(c["r"]), gpu(c["w"]), float(c["eps"]))
+    assert torch.equal(h.cpu(), c["h"])
+    assert_rel(y, c["y"], 1e-5)
+
+
+def test_add_rms_norm_bf16_vs_golden_and_in_place():
+    c = load("add_rms_norm")["decode_bf16_triton"]
+    x, r = gpu(c["x"]), gpu(c["r"])
+    y, h = K.fused_add_rms_norm(x, r, gpu(c["w"]), float(c["eps"]))
+    assert torch.equal(h.cpu(), c["h"])
+    assert int(ulp(y, c["y"]).max()) <= 1
+    yo, ho = O.add_rms_norm_ref(c["x"], c["r"], c["w"], float(c["eps"]))
+    assert_close_ulp(y, yo)
+    # in place: residual stream updated, normed output written over x
+    K.fused_add_rms_norm(x, r, gpu(c["w"]), float(c["eps"]), out=x, residual_out=r)
+    assert torch.equal(r.cpu(), ho) and torch.equal(x.cpu(), y.cpu())
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("rows", [1, 8, 1000, 16384])
+def test_add_rms_norm_rows(dtype, rows):
+    x, r = rnd((rows, 1024), 6, dtype), rnd((rows, 1024), 7, dtype)
+    w = rnd((1024,), 8, dtype, 1.0, 0.02)
+    y, h = K.fused_add_rms_norm(gpu(x), gpu(r), gpu(w), 1e-5)
+    yo, ho = O.add_rms_norm_ref(x, r, w, 1e-5)
+    assert torch.equal(h.cpu(), ho)
+    if dtype == torch.float32:
+        assert_rel(y, yo, 1e-5)
+    else:
+        assert_close_ulp(y, yo)
+
+
+# ---------------------------------------------------------------- SiLU*mul
+
+
+@pytest.mark.parametrize("case", ["rows4_bf16", "decode_bf16", "odd_bf16"])
+def test_silu_mul_vs_reference_golden(case):
+    c = load("triton_silu_mul")[case]
+    y = K.fused_silu_mul(gpu(c["gate_up"]))
+    assert y.shape == c["y"].shape
+    assert int(ulp(y, c["y"]).max()) <= 1
+    assert_close_ulp(y, O.silu_mul_ref(c["gate_up"]))
+    assert int(ulp(y, O.eager_silu_mul(c["gate_up"])).max()) <= 2
+
+
+@pytest.mark.parametrize("t", [1, 64, 512, 4096, 32768])
+def test_silu_mul_sweep(t):
+    gu = rnd((t, 9216), 9)
+    y = K.fused_silu_mul(gpu(gu))
+    assert_close_ulp(y, O.silu_mul_ref(gu))
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_silu_mul_other_dtypes(dtype):
+    gu = rnd((17, 2 * 4608), 10, dtype)
+    y = K.fused_silu_mul(gpu(gu))
+    ref = O.silu_mul_ref(gu)
+    if dtype == torch.float32:
+        assert torch.allclose(y.cpu(), ref, rtol=1e-5, atol=1e-6)
+    else:
+        assert_close_ulp(y, ref)
+
+
+def test_silu_mul_strided_and_odd():
+    big = rnd((9, 2 * 4608 + 64), 11)
+    y = K.fused_silu_mul(gpu(big)[:, : 2 * 4608])          # row stride 9280, vector path
+    assert_close_ulp(y, O.silu_mul_ref(big[:, : 2 * 4608]))
+    odd = rnd((5, 2 * 77), 12)                               # n = 77: generic path
+    assert_close_ulp(K.fused_silu_mul(gpu(odd)), O.silu_mul_ref(odd))
+
+
+def test_silu_mul_extreme_values():
+    g = torch.tensor([-100.0, -20.0, -1e-3, 0.0, 1e-3, 20.0, 88.0, -88.0])
+    u = torch.ones_like(g) * 1.5
+    gu = torch.cat([g, u]).reshape(1, 16).to(torch.bfloat16)
+    y = K.fused_silu_mul(gpu(gu))
+    assert_close_ulp(y, O.silu_mul_ref(gu), 1, 0.0)
+
+
+# --------------------------------------------------------------- RoPE (ref)
+
+
+@pytest.mark.parametrize("case", ["pos0", "pos1", "pos777", "pos2047"])
+def test_rope_vs_reference_golden(case):
+    c = load("triton_rope")[case]
+    qo, ko = K.fused_rope(gpu(c["q"]), gpu(c["k"]), gpu(c["cos"]), gpu(c["sin"]))
+    assert qo.shape == c["q"].shape and ko.shape == c["k"].shape
+    assert int(ulp(qo, c["q_out"]).max()) <= 1 and int(ulp(ko, c["k_out"]).max()) <= 1
+    # same fp32 operations, nearest-even store: bit-identical to the oracle
+    assert torch.equal(qo.cpu(), O.rope_ref(c["q"], c["cos"], c["sin"]))
+    assert torch.equal(ko.cpu(), O.rope_ref(c["k"], c["cos"], c["sin"]))
+
+
+@pytest.mark.parametrize("d,dtype", [(32, torch.bfloat16), (128, torch.bfloat16), (64, torch.float32),
+                                     (48, torch.bfloat16), (64, torch.float16)])
+def test_rope_head_dims(d, dtype):
+    q, k = rnd((1, 12, 1, d), 13, dtype), rnd((1, 4, 1, d), 14, dtype)
+    cos, sin = rnd((d,), 15, dtype), rnd((d,), 16, dtype)    # arbitrary rows: halves differ
+    qo, ko = K.fused_rope(gpu(q), gpu(k), gpu(cos), gpu(sin))
+    assert torch.equal(qo.cpu(), O.rope_ref(q, cos, sin))
+    assert torch.equal(ko.cpu(), O.rope_ref(k, cos, sin))
+
+
+# ------------------------------------------------------------ KV write
+
+
+@pytest.mark.parametrize("case", ["b1_slot5", "b2_slot0", "b1_last"])
+def test_kv_cache_write_vs_static_cache_golden(case):
+    c = load("static_cache_update")[case]
+    kc, vc = gpu(c["k_prev"]), gpu(c["v_prev"])
+    K.kv_cache_write(gpu(c["k"]), gpu(c["v"]), kc, vc, torch.tensor([int(c["slot"])], device=DEV))
+    assert torch.equal(kc.cpu(), c["k_cache"]) and torch.equal(vc.cpu(), c["v_cache"])
+    assert _lib.read_and_clear_errors(DEV) == 0
+
+
+def test_kv_cache_write_per_stream_and_out_of_range():
+    b = 4
+    kc0, vc0 = rnd((b, 8, 16, 64), 17), rnd((b, 8, 16, 64), 18)
+    k, v = rnd((b, 8, 1, 64), 19), rnd((b, 8, 1, 64), 20)
+    slots = torch.tensor([3, 0, 15, 16])                      # last one out of range
+    kc, vc = gpu(kc0), gpu(vc0)
+    K.kv_cache_write(gpu(k), gpu(v), kc, vc, gpu(slots))
+    ek, ev = kc0.clone(), vc0.clone()
+    O.kv_write_ref(ek, ev, k, v, slots.tolist())
+    assert torch.equal(kc.cpu(), ek) and torch.equal(vc.cpu(), ev)
+    assert _lib.read_and_clear_errors(DEV) == _lib.KANI_FLAG_SLOT_OOB
+
+
+def test_static_cache_update_matches_reference_semantics():
+    class Cfg:
+        num_key_value_heads, num_attention_heads, hidden_size = 8, 16, 1024
+        num_hidden_layers, layer_types, conv_L_cache = 2, ["conv", "full_attention"], 3
+    cache = StaticKVCache(Cfg, max_total_len=16, batch_size=2, device=DEV)
+    k, v = rnd((2, 8, 1, 64), 21), rnd((2, 8, 1, 64), 22)
+    cache.set_write_position(7)
+    kf, vf = cache.update(gpu(k), gpu(v), 1)
+    ek = torch.zeros(2, 8, 16, 64, dtype=torch.bfloat16)
+    ev = ek.clone()
+    O.kv_write_ref(ek, ev, k, v, 7)
+    assert torch.equal(kf.cpu(), ek) and torch.equal(vf.cpu(), ev)
+    assert cache.update(None, None, 0)[0].numel() == 0
+    assert cache.read_errors() == 0
+
+
+# ------------------------------------------------- fused RoPE + KV write
+
+
+def _config2_case(seed, t=1, b=1, s_len=2048, p0=None, norm=False, table=True, dtype=torch.bfloat16,
+                  hq=16, hk=8, d=64):
+    g = torch.Generator().manual_seed(seed)
+    n = b * t
+    q = rnd((n, hq, d), seed + 1, dtype)
+    k = rnd((n, hk, d), seed + 2, dtype)
+    v = rnd((n, hk, d), seed + 3, dtype)
+    inv = P.learnable_inv_freq(d, 1e6, 0.0)
+    if p0 is None:
+        pos = torch.randint(0, 2048, (n,), generator=g)
+    else:
+        pos = (p0 + torch.arange(t)).repeat(b)
+    slots = pos.clone()
+    tab = rnd((1024, d), seed + 4, dtype, 0.0, 0.02) if table else None
+    qw = rnd((d,), seed + 5, dtype, 1.0, 0.02) if norm else None
+    kw = rnd((d,), seed + 6, dtype, 1.0, 0.02) if norm else None
+    kc = rnd((b, hk, s_len, d), seed + 7, dtype)
+    vc = rnd((b, hk, s_len, d), seed + 8, dtype)
+    return dict(q=q, k=k, v=v, inv=inv, pos=pos, slots=slots, tab=tab, qw=qw, kw=kw, kc=kc, vc=vc)
+
+
+def _run_both(c, t, b, frame_pos=None, tpf=4):
+    hq, d = c["q"].shape[1:]
+    hk = c["k"].shape[1]
+    kc, vc = gpu(c["kc"]), gpu(c["vc"])
+    q_rot = K.fused_rope_kv_write(
+        gpu(c["q"]).view(b, t, hq, d), gpu(c["k"]).view(b, t, hk, d), gpu(c["v"]).view(b, t, hk, d),
+        gpu(c["inv"]), gpu(c["pos"]), kc, vc, gpu(c["slots"]),
+        frame_table=None if c["tab"] is None else gpu(c["tab"]), tokens_per_frame=tpf,
+        q_norm_w=None if c["qw"] is None else gpu(c["qw"]),
+        k_norm_w=None if c["kw"] is None else gpu(c["kw"]), eps=1e-5,
+        frame_pos=None if frame_pos is None else gpu(frame_pos))
+    ekc, evc = c["kc"].clone(), c["vc"].clone()
+    eq, flags = O.rope_kv_write_ref(c["q"], c["k"], c["v"], c["inv"], c["pos"], ekc, evc, c["slots"],
+                                    frame_table=c["tab"], tokens_per_frame=tpf, q_norm_w=c["qw"],
+                                    k_norm_w=c["kw"], eps=1e-5, frame_pos=frame_pos)
+    return q_rot.reshape(eq.shape), kc, vc, eq, ekc, evc, flags
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2, 3])
+@pytest.mark.parametrize("norm", [False, True])
+def test_rope_kv_write_config2_decode(seed, norm):
+    c = _config2_case(100 + seed, norm=norm)
+    q, kc, vc, eq, ekc, evc, flags = _run_both(c, 1, 1)
+    assert flags == 0 and _lib.read_and_clear_errors(DEV) == 0
+    assert_close_ulp(q, eq, 1, 0.99)
+    assert_close_ulp(kc, ekc, 1, 0.999)
+    assert torch.equal(vc.cpu(), evc)                       # V copy and untouched slots exact
+    slot = int(c["slots"][0])
+    mask = torch.ones(2048, dtype=torch.bool)
+    mask[slot] = False
+    assert torch.equal(kc.cpu()[:, :, mask], c["kc"][:, :, mask])
+
+
+@pytest.mark.parametrize("t", [1, 64, 512, 4096])
+def test_rope_kv_write_prefill_sweep(t):
+    p0 = 0 if t == 4096 else 1000
+    s_len = max(2048, p0 + t)
+    c = _config2_case(200 + t, t=t, s_len=s_len, p0=p0, norm=True)
+    q, kc, vc, eq, ekc, evc, flags = _run_both(c, t, 1)
+    assert flags == 0 and _lib.read_and_clear_errors(DEV) == 0
+    assert_close_ulp(q, eq, 1, 0.99)
+    assert_close_ulp(kc, ekc, 1, 0.999)
+    assert torch.equal(vc.cpu(), evc)
+
+
+def test_rope_kv_write_batched_streams():
+    b = 64
+    c = _config2_case(300, t=1, b=b, norm=True)
+    q, kc, vc, eq, ekc, evc, flags = _run_both(c, 1, b)
+    assert flags == 0
+    assert_close_ulp(q, eq, 1, 0.99)
+    assert_close_ulp(kc, ekc, 1, 0.999)
+    assert torch.equal(vc.cpu(), evc)
+
+
+def test_rope_kv_write_packed_qkv_and_heads_major_output():
+    b, t, hq, hk, d = 1, 37, 16, 8, 64
+    c = _config2_case(400, t=t, b=b, p0=50, norm=True)
+    qkv = torch.cat([c["q"].reshape(t, -1), c["k"].reshape(t, -1), c["v"].reshape(t, -1)], dim=1)
+    qkv = gpu(qkv).view(b, t, (hq + 2 * hk) * d)
+    q, k, v = qkv.split([hq * d, hk * d, hk * d], dim=-1)
+    q_attn = torch.empty(b, hq, t, d, dtype=torch.bfloat16, device=DEV)   # SDPA layout
+    kc, vc = gpu(c["kc"]), gpu(c["vc"])
+    K.fused_rope_kv_write(q.view(b, t, hq, d), k.view(b, t, hk, d), v.view(b, t, hk, d), gpu(c["inv"]),
+                          gpu(c["pos"]), kc, vc, gpu(c["slots"]), frame_table=gpu(c["tab"]),
+                          q_norm_w=gpu(c["qw"]), k_norm_w=gpu(c["kw"]), q_out=q_attn.transpose(1, 2))
+    ekc, evc = c["kc"].clone(), c["vc"].clone()
+    eq, _ = O.rope_kv_write_ref(c["q"], c["k"], c["v"], c["inv"], c["pos"], ekc, evc, c["slots"],
+                                frame_table=c["tab"], q_norm_w=c["qw"], k_norm_w=c["kw"])
+    assert_close_ulp(q_attn.transpose(1, 2).reshape(t, hq, d), eq, 1, 0.99)
+    assert_close_ulp(kc, ekc, 1, 0.999)
+    assert torch.equal(vc.cpu(), evc)
+
+
+def test_rope_kv_write_out_of_range_slot_and_frame():
+    c = _config2_case(500, t=4, p0=0)
+    c["slots"] = torch.tensor([0, 2048, -1, 5])             # two bad slots
+    fp = torch.tensor([0, 4096, 8, -4])                      # frames 0, 1024 (bad), 2, -1 (bad)
+    q, kc, vc, eq, ekc, evc, flags = _run_both(c, 4, 1, frame_pos=fp)
+    assert flags == 3
+    assert _lib.read_and_clear_errors(DEV) == 3
+    assert_close_ulp(q, eq, 1, 0.99)
+    assert_close_ulp(kc, ekc, 1, 0.999)
+    assert torch.equal(vc.cpu(), evc)
+
+
+@pytest.mark.parametrize("dtype,d,hq,hk", [(torch.float32, 64, 16, 8), (torch.float16, 64, 16, 8),
+                                           (torch.bfloat16, 128, 8, 2), (torch.bfloat16, 48, 4, 2)])
+def test_rope_kv_write_dtypes_and_generic_path(dtype, d, hq, hk):
+    c = _config2_case(600, t=9, p0=100, norm=True, dtype=dtype, hq=hq, hk=hk, d=d)
+    q, kc, vc, eq, ekc, evc, flags = _run_both(c, 9, 1)
+    assert flags == 0
+    if dtype == torch.float32:
+        assert torch.allclose(q.cpu(), eq, rtol=1e-5, atol=1e-5)
+        assert torch.allclose(kc.cpu(), ekc, rtol=1e-5, atol=1e-5)
+    else:
+        assert_close_ulp(q, eq, 1, 0.99)
+        assert_close_ulp(kc, ekc, 1, 0.999)
+    assert torch.equal(vc.cpu(), evc)
+
+
+def test_rope_kv_write_matches_reference_decode_composition():
+    """Against the reference's decode sequence on the same inputs: per-head
+    RMSNorm, cos/sin rows, RoPE and scatter_ (optimized_decode.py:220-240),
+    each step through the oracle restatement of that step."""
+    c = _config2_case(700, norm=True, table=False)
+    pos = int(c["pos"][0])
+    qn = O.rms_norm_ref(c["q"], c["qw"], 1e-5)
+    kn = O.rms_norm_ref(c["k"], c["kw"], 1e-5)
+    cos, sin = O.rope_cos_sin_ref(c["inv"], pos)
+    q_ref, k_ref = O.rope_ref(qn, cos, sin), O.rope_ref(kn, cos, sin)
+    q, kc, vc, *_ = _run_both(c, 1, 1)
+    assert_close_ulp(q, q_ref, 1, 0.99)
+    assert_close_ulp(kc.cpu()[0, :, pos], k_ref[0], 1, 0.99)
+    assert torch.equal(vc.cpu()[0, :, pos], c["v"][0])
+
+
+def test_update_fused_through_static_cache():
+    class Cfg:
+        num_key_value_heads, num_attention_heads, hidden_size = 8, 16, 1024
+        num_hidden_layers, layer_types, conv_L_cache = 1, ["full_attention"], 3
+    b = 3
+    cache = StaticKVCache(Cfg, max_total_len=64, batch_size=b, device=DEV, per_stream_positions=True)
+    c = _config2_case(800, t=1, b=b, s_len=64, norm=True, table=False)
+    c["pos"] = torch.tensor([5, 9, 63])
+    c["slots"] = c["pos"].clone()
+    c["kc"] = torch.zeros(b, 8, 64, 64, dtype=torch.bfloat16)
+    c["vc"] = torch.zeros_like(c["kc"])
+    cache.set_write_position(gpu(c["slots"]))
+    q_rot, kf, vf = cache.update_fused(gpu(c["q"]).view(b, 1, 16, 64), gpu(c["k"]).view(b, 1, 8, 64),
+                                       gpu(c["v"]).view(b, 1, 8, 64), 0, gpu(c["inv"]),
+                                       gpu(c["pos"]).view(b, 1), gpu(c["qw"]), gpu(c["kw"]))
+    ekc, evc = c["kc"].clone(), c["vc"].clone()
+    eq, _ = O.rope_kv_write_ref(c["q"], c["k"], c["v"], c["inv"], c["pos"], ekc, evc, c["slots"],
+                                q_norm_w=c["qw"], k_norm_w=c["kw"])
+    assert_close_ulp(q_rot.reshape(eq.shape), eq, 1, 0.99)
+    assert_close_ulp(kf, ekc, 1, 0.999)
+    assert torch.equal(vf.cpu(), evc)
+
+
+# ---------------------------------------------------------- graph capture
+
+
+def test_ops_capture_in_cuda_graph():
+    """Every op launches on the current stream without syncing: capture once,
+    replay with new positions/slots written into the static inputs."""
+    hq, hk, d, s_len = 16, 8, 64, 128
+    c = _config2_case(900, t=1, s_len=s_len, norm=True)
+    x, r = gpu(rnd((1, 1024), 901)), gpu(rnd((1, 1024), 902))
+    w = gpu(rnd((1024,), 903, mean=1.0, std=0.02))
+    gu = gpu(rnd((1, 9216), 904))
+    q, k, v = gpu(c["q"]).view(1, 1, hq, d), gpu(c["k"]).view(1, 1, hk, d), gpu(c["v"]).view(1, 1, hk, d)
+    kc, vc = gpu(c["kc"][:, :, :s_len]).contiguous(), gpu(c["vc"][:, :, :s_len]).contiguous()
+    pos = torch.zeros(1, dtype=torch.long, device=DEV)
+    slot = torch.zeros(1, dtype=torch.long, device=DEV)
+    inv, tab, qw, kw = gpu(c["inv"]), gpu(c["tab"]), gpu(c["qw"]), gpu(c["kw"])
+    _lib.error_flag(DEV)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):                               # warm-up outside capture
+        K.fused_add_rms_norm(x, r, w, 1e-5)
+        K.fused_silu_mul(gu)
+        K.fused_rope_kv_write(q, k, v, inv, pos, kc, vc, slot, frame_table=tab, q_norm_w=qw, k_norm_w=kw)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        y, h = K.fused_add_rms_norm(x, r, w, 1e-5)
+        a = K.fused_silu_mul(gu)
+        qo = K.fused_rope_kv_write(q, k, v, inv, pos, kc, vc, slot, frame_table=tab, q_norm_w=qw, k_norm_w=kw)
+    for p in (5, 77, 127):
+        pos.fill_(p)
+        slot.fill_(p)
+        g.replay()
+        torch.cuda.synchronize()
+        ekc, evc = c["kc"][:, :, :s_len].clone(), c["vc"][:, :, :s_len].clone()
+        eq, _ = O.rope_kv_write_ref(c["q"], c["k"], c["v"], c["inv"], torch.tensor([p]), ekc, evc,
+                                    torch.tensor([p]), frame_table=c["tab"], q_norm_w=c["qw"],
+                                    k_norm_w=c["kw"])
+        assert_close_ulp(qo.reshape(eq.shape), eq, 1, 0.99)
+        assert_close_ulp(kc.cpu()[:, :, p], ekc[:, :, p], 1, 0.99)
+    yo, ho = O.add_rms_norm_ref(x.cpu(), r.cpu(), w.cpu(), 1e-5)
+    assert torch.equal(h.cpu(), ho)
+    assert_close_ulp(y, yo)
+    assert_close_ulp(a, O.silu_mul_ref(gu.cpu()))
+    del g
+
+
+def test_errors_raise_before_launch_on_gpu_tensors():
+    x = gpu(rnd((2, 64), 1))
+    with pytest.raises(TypeError):
+        K.fused_rms_norm(x.to(torch.int32), gpu(rnd((64,), 2)))
+    with pytest.raises(ValueError):
+        K.fused_rms_norm(x, gpu(rnd((32,), 2)))
+    with pytest.raises(ValueError):
+        K.fused_silu_mul(gpu(rnd((2, 9), 3)))
+    with pytest.raises(ValueError):
+        K.fused_add_rms_norm(x, gpu(rnd((2, 32), 4)), gpu(rnd((64,), 2)))
+    kc = torch.zeros(1, 8, 16, 64, dtype=torch.bfloat16, device=DEV)
+    with pytest.raises(ValueError):
+        K.kv_cache_write(gpu(rnd((1, 8, 2, 64), 5)), gpu(rnd((1, 8, 1, 64), 5)), kc, kc.clone(),
+                         torch.zeros(1, dtype=torch.long, device=DEV))

@@ -1,0 +1,112 @@
+"""Host-side checks that need no GPU: the C-ABI library loads and exports every
+symbol the header declares, argument validation rejects bad calls before any
+launch, and the Python layer refuses CPU tensors (there is no CPU fallback)."""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+from kani_tts_b200 import _lib
+from kani_tts_b200 import fused_kernels as K
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "kani_b200.h"
+
+
+def header_symbols() -> list[str]:
+    text = HEADER.read_text()
+    return re.findall(r"KANI_API\s+[\w\s\*]+?\b(kani_\w+)\s*\(", text)
+
+
+def test_header_declares_the_abi():
+    syms = header_symbols()
+    assert set(syms) == set(_lib.EXPORTED_SYMBOLS)
+    assert len(syms) == len(set(syms))
+
+
+def test_library_loads_and_exports_every_symbol():
+    lib = _lib.load_library()
+    raw = ctypes.CDLL(str(_lib.LIB_PATH))
+    for name in header_symbols():
+        assert hasattr(raw, name), name
+    assert lib.kani_version() == 100
+
+
+def test_status_strings():
+    assert _lib.status_string(0) == "ok"
+    assert "invalid" in _lib.status_string(-1)
+    assert "dtype" in _lib.status_string(-2)
+    assert "not supported" in _lib.status_string(-3)
+
+
+def _null():
+    return ctypes.c_void_p(0)
+
+
+def test_abi_rejects_bad_arguments_without_launching():
+    lib = _lib.load_library()
+    before = lib.kani_launch_count()
+    fake = ctypes.c_void_p(0x1000)       # never dereferenced: every call below returns early
+    # negative sizes
+    assert lib.kani_rms_norm(1, 1, fake, 8, fake, fake, 8, -1, 8, 1e-5, _null()) == -1
+    assert lib.kani_silu_mul(1, fake, 16, fake, 8, 4, -8, _null()) == -1
+    # null pointers
+    assert lib.kani_rms_norm(1, 1, _null(), 8, fake, fake, 8, 4, 8, 1e-5, _null()) == -1
+    assert lib.kani_add_rms_norm(1, 1, fake, 8, _null(), 8, fake, fake, 8, fake, 8, 4, 8, 1e-5,
+                                 _null()) == -1
+    # out and residual_out may not be the same buffer
+    assert lib.kani_add_rms_norm(1, 1, fake, 8, fake, 8, fake, fake, 8, fake, 8, 4, 8, 1e-5,
+                                 _null()) == -1
+    # overlapping rows (stride < n)
+    assert lib.kani_silu_mul(1, fake, 8, fake, 8, 4, 8, _null()) == -1
+    # unknown dtype code
+    assert lib.kani_rms_norm(7, 1, fake, 8, fake, fake, 8, 4, 8, 1e-5, _null()) == -2
+    assert lib.kani_rms_norm(1, 9, fake, 8, fake, fake, 8, 4, 8, 1e-5, _null()) == -2
+    # odd head_dim is unsupported (rotate-half needs pairs)
+    assert lib.kani_rope_qk(1, fake, fake, fake, fake, fake, fake, 16, 8, 63, _null()) == -3
+    # q/k norm weights must come together
+    args = [1, 1, 1, 16, 8, 64, fake, 2048, fake, 2048, fake, 2048, fake, fake,
+            fake, _null(), 1e-5, _null(), 0, _null(), 4, fake, 1024, 64,
+            fake, fake, 8 * 2048 * 64, 2048 * 64, 64, 2048, fake, _null(), _null()]
+    assert lib.kani_rope_kv_write(*args) == -1
+    # missing KV write slots pointer is allowed (slot = token index); missing positions is not
+    args[13] = _null()
+    args[15] = fake
+    assert lib.kani_rope_kv_write(*args) == -1
+    assert lib.kani_kv_cache_write(1, fake, fake, 1, 8, 64, fake, fake, 16, _null(), 0, _null(),
+                                   _null()) == -1
+    assert lib.kani_launch_count() == before
+
+
+def test_abi_zero_sized_calls_are_noops():
+    lib = _lib.load_library()
+    before = lib.kani_launch_count()
+    n = _null()
+    assert lib.kani_rms_norm(1, 1, n, 0, n, n, 0, 0, 1024, 1e-5, n) == 0
+    assert lib.kani_add_rms_norm(1, 1, n, 0, n, 0, n, n, 0, n, 0, 0, 1024, 1e-5, n) == 0
+    assert lib.kani_silu_mul(1, n, 0, n, 0, 0, 4608, n) == 0
+    assert lib.kani_rope_qk(1, n, n, n, n, n, n, 0, 0, 64, n) == 0
+    assert lib.kani_kv_cache_write(1, n, n, 0, 8, 64, n, n, 16, n, 0, n, n) == 0
+    assert lib.kani_rope_kv_write(1, 0, 1, 16, 8, 64, n, 0, n, 0, n, 0, n, n, n, n, 1e-5, n, 0, n, 4,
+                                  n, 0, 0, n, n, 0, 0, 0, 16, n, n, n) == 0
+    assert lib.kani_launch_count() == before
+
+
+@pytest.mark.parametrize("call", [
+    lambda: K.fused_rms_norm(torch.zeros(2, 8), torch.ones(8)),
+    lambda: K.fused_add_rms_norm(torch.zeros(2, 8), torch.zeros(2, 8), torch.ones(8)),
+    lambda: K.fused_silu_mul(torch.zeros(2, 16)),
+    lambda: K.fused_rope(torch.zeros(1, 2, 1, 8), torch.zeros(1, 1, 1, 8), torch.zeros(8), torch.zeros(8)),
+])
+def test_cpu_tensors_are_refused(call):
+    with pytest.raises(ValueError, match="CUDA"):
+        call()
+
+
+def test_missing_library_fails_loudly(tmp_path, monkeypatch):
+    monkeypatch.setattr(_lib, "_lib", None)
+    with pytest.raises(ImportError, match="no fallback"):
+        _lib.load_library(tmp_path / "absent.so")

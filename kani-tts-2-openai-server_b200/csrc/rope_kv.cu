@@ -21,9 +21,9 @@
 // sum of squares for the fused norm is an L-wide xor-shuffle tree.  Per token
 // the items are [Q heads | K heads | V heads], padded to whole warps, so a
 // head never straddles a warp and a token's K and V land in one CTA; a CTA
-// carries `tpb` tokens.  With cos/sin built in-kernel, the first D/2*tpb
-// threads compute one (cos, sin) pair each into shared memory (one sinf/cosf
-// per frequency per token instead of one per element per head).
+// of up to 256 threads carries `tpb` tokens.  With cos/sin built in-kernel,
+// the lanes of a warp split the frequencies among themselves and exchange
+// them by shuffles (see the kernel).
 //
 // Generic kernel: any even D and any alignment — one warp per
 // (token, head) with scalar accesses.
@@ -100,34 +100,24 @@ __device__ __forceinline__ float rrms_of(float ss, int n, float eps) {
 }
 
 // ------------------------------------------------------------ vector kernel
+// Lane layout inside a warp: lane = hh * L + jj, hh in [0, 32/L) the head slot,
+// jj in [0, L) the chunk.  A rope lane needs cos/sin of frequencies
+// jj*E .. jj*E+E-1; the 32/L lanes sharing a chunk jj compute those E
+// frequencies between them (one sinf/cosf pair each when 32/L >= E) and
+// exchange them with shuffles, so there is no shared memory and no block
+// barrier: every warp runs on its own, its global loads are issued first and
+// their latency overlaps the trig.
 template <typename T, bool NORM, bool TABLE, bool CS_GIVEN>
-__global__ void __launch_bounds__(512)
+__global__ void __launch_bounds__(256, NORM ? 3 : 4)
 rope_vec_kernel(RopeParams p, int log2l, int ipt, int iptr, int tpb) {
   constexpr int E = VecN<T>::value;
-  extern __shared__ float2 cs[];  // [tpb][D/2] (cos, sin), in-kernel angles only
   const int L = 1 << log2l;
   const int half = p.d >> 1;
   const int tl = threadIdx.x / iptr;
   const int item = threadIdx.x - tl * iptr;
   const int64_t t = (int64_t)blockIdx.x * tpb + tl;
-
-  if constexpr (!CS_GIVEN) {
-    for (int idx = threadIdx.x; idx < tpb * half; idx += blockDim.x) {
-      const int ttl = idx / half;
-      const int i = idx - ttl * half;
-      const int64_t tt = (int64_t)blockIdx.x * tpb + ttl;
-      float c = 0.f, s = 0.f;
-      if (tt < p.n_tokens) {
-        const float ang = __fmul_rn(p.inv_freq[i], (float)p.positions[tt]);
-        c = round_to<T>(cosf(ang));
-        s = round_to<T>(sinf(ang));
-      }
-      cs[idx] = make_float2(c, s);
-    }
-    __syncthreads();
-  }
-
   const bool tok_ok = t < p.n_tokens;
+  const int lane = threadIdx.x & 31;
   const int head_item = item >> log2l;
   const int j = item & (L - 1);
   // kind: 0 = Q rope, 1 = K rope, 2 = V copy, 3 = idle lane
@@ -146,25 +136,21 @@ rope_vec_kernel(RopeParams p, int log2l, int ipt, int iptr, int tpb) {
   }
   const int lo = j * E, hi = half + j * E;
 
+  // 1. the head's data: independent of everything else, issued first
+  uint4 xlo = make_uint4(0, 0, 0, 0), xhi = xlo, plo = xlo, phi = xlo;
+  if (kind < 3) {
+    const T* base = kind == 0 ? static_cast<const T*>(p.q) + t * p.qts
+                  : kind == 1 ? static_cast<const T*>(p.k) + t * p.kts
+                              : static_cast<const T*>(p.v) + t * p.vts;
+    const T* src = base + (int64_t)h * p.d;
+    xlo = ld16_stream(src + lo);
+    xhi = ld16_stream(src + hi);
+  }
+  // 2. token metadata (slot, frame) and the frame-table row
   TokenMeta m{};
   if (tok_ok) {
     m = token_meta<TABLE>(p, t);
     if (item == 0) flag_token<TABLE>(p, m);
-  }
-
-  uint4 xlo = make_uint4(0, 0, 0, 0), xhi = xlo, plo = xlo, phi = xlo;
-  if (kind == 0) {
-    const T* src = static_cast<const T*>(p.q) + t * p.qts + (int64_t)h * p.d;
-    xlo = ld16(src + lo);
-    xhi = ld16(src + hi);
-  } else if (kind == 1) {
-    const T* src = static_cast<const T*>(p.k) + t * p.kts + (int64_t)h * p.d;
-    xlo = ld16(src + lo);
-    xhi = ld16(src + hi);
-  } else if (kind == 2) {
-    const T* src = static_cast<const T*>(p.v) + t * p.vts + (int64_t)h * p.d;
-    xlo = ld16(src + lo);
-    xhi = ld16(src + hi);
   }
   if constexpr (TABLE) {
     if (kind < 2 && m.frame_ok) {
@@ -173,11 +159,52 @@ rope_vec_kernel(RopeParams p, int log2l, int ipt, int iptr, int tpb) {
       phi = ld16_ro(pr + hi);
     }
   }
+  // 3. cos/sin of this lane's E frequencies (both halves share them unless
+  //    explicit cos/sin rows are given)
+  float clo[E], slo[E];
+  float chi_[CS_GIVEN ? E : 1], shi_[CS_GIVEN ? E : 1];
+  float* chi = CS_GIVEN ? chi_ : clo;
+  float* shi = CS_GIVEN ? shi_ : slo;
+  if constexpr (CS_GIVEN) {
+    if (kind < 2) {
+      unpack16<T>(ld16_ro(static_cast<const T*>(p.cos) + lo), clo);
+      unpack16<T>(ld16_ro(static_cast<const T*>(p.cos) + hi), chi);
+      unpack16<T>(ld16_ro(static_cast<const T*>(p.sin) + lo), slo);
+      unpack16<T>(ld16_ro(static_cast<const T*>(p.sin) + hi), shi);
+    }
+  } else {
+    // warp-uniform: skip when no lane of the warp rotates (a V-only warp)
+    if (__any_sync(0xffffffffu, kind < 2)) {
+      const int log2g = 5 - log2l;            // 32/L lanes share one chunk
+      const int G = 1 << log2g;
+      const int hh = lane >> log2l;
+      const int jj = lane & (L - 1);
+      const float posf = tok_ok ? (float)p.positions[t] : 0.f;
+      const int rounds = (E + G - 1) >> log2g;
+      for (int r = 0; r < rounds; ++r) {
+        const int e_own = r * G + hh;
+        float cv = 0.f, sv = 0.f;
+        if (e_own < E) {
+          const float ang = __fmul_rn(__ldg(p.inv_freq + jj * E + e_own), posf);
+          cv = round_to<T>(cosf(ang));
+          sv = round_to<T>(sinf(ang));
+        }
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          if ((e >> log2g) == r) {  // uniform across the warp
+            const int src = ((e & (G - 1)) << log2l) | jj;
+            clo[e] = __shfl_sync(0xffffffffu, cv, src);
+            slo[e] = __shfl_sync(0xffffffffu, sv, src);
+          }
+        }
+      }
+    }
+  }
 
+  // 4. optional per-head RMSNorm (an L-lane shuffle tree per head)
   float a[E], b[E];
   unpack16<T>(xlo, a);
   unpack16<T>(xhi, b);
-
   if constexpr (NORM) {
     float ss = 0.f;
     if (kind < 2) {
@@ -187,7 +214,6 @@ rope_vec_kernel(RopeParams p, int log2l, int ipt, int iptr, int tpb) {
         ss = fmaf(b[e], b[e], ss);
       }
     }
-    // all lanes take part; a head's L lanes are an aligned group of the warp
     for (int off = L >> 1; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
     if (kind < 2) {
       const T* w = static_cast<const T*>(kind == 0 ? p.qw : p.kw);
@@ -203,22 +229,8 @@ rope_vec_kernel(RopeParams p, int log2l, int ipt, int iptr, int tpb) {
     }
   }
 
+  // 5. rotate, add the frame term, store
   if (kind < 2) {
-    float clo[E], slo[E], chi[E], shi[E];
-    if constexpr (CS_GIVEN) {
-      unpack16<T>(ld16_ro(static_cast<const T*>(p.cos) + lo), clo);
-      unpack16<T>(ld16_ro(static_cast<const T*>(p.cos) + hi), chi);
-      unpack16<T>(ld16_ro(static_cast<const T*>(p.sin) + lo), slo);
-      unpack16<T>(ld16_ro(static_cast<const T*>(p.sin) + hi), shi);
-    } else {
-      const float2* row = cs + tl * half + lo;
-#pragma unroll
-      for (int e = 0; e < E; ++e) {
-        const float2 v = row[e];
-        clo[e] = chi[e] = v.x;
-        slo[e] = shi[e] = v.y;
-      }
-    }
     float ylo[E], yhi[E];
 #pragma unroll
     for (int e = 0; e < E; ++e) {
@@ -386,15 +398,13 @@ int launch_rope_t(const RopeParams& p, cudaStream_t s) {
     const int heads = p.hq + p.hk + (has_v ? p.hk : 0);
     const int ipt = heads << log2l;
     const int iptr = ((ipt + 31) / 32) * 32;
-    if (iptr <= 512) {
-      int tpb = 512 / iptr;
-      if (tpb > 4) tpb = 4;
+    if (iptr <= 256) {
+      int tpb = 256 / iptr;
       if (tpb > p.n_tokens) tpb = (int)p.n_tokens;
       const int64_t grid = (p.n_tokens + tpb - 1) / tpb;
       if (grid <= 0x7fffffff) {
-        const size_t smem = CS_GIVEN ? 0 : (size_t)tpb * half * sizeof(float2);
         rope_vec_kernel<T, NORM, TABLE, CS_GIVEN>
-            <<<(unsigned)grid, tpb * iptr, smem, s>>>(p, log2l, ipt, iptr, tpb);
+            <<<(unsigned)grid, tpb * iptr, 0, s>>>(p, log2l, ipt, iptr, tpb);
         return launch_status();
       }
     }

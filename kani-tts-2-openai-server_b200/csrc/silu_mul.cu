@@ -18,8 +18,11 @@ namespace kani {
 namespace {
 
 __device__ __forceinline__ float silu_mul_f(float g, float u) {
-  // silu(g) = g / (1 + e^-g); __expf / __fdividef keep the op memory-bound.
-  return __fmul_rn(__fdividef(g, 1.0f + __expf(-g)), u);
+  // (g * sigmoid(g)) * u with sigmoid(g) = 1 / (1 + e^-g).  The reciprocal is
+  // the IEEE one: an approximate divide returns 0 once 1 + e^-g exceeds 2^126
+  // (g < -87.3), where the true result is still a normal number.
+  const float sig = __frcp_rn(1.0f + __expf(-g));
+  return __fmul_rn(__fmul_rn(g, sig), u);
 }
 
 template <typename T, int RY>

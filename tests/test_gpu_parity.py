@@ -7,6 +7,12 @@ Tolerances (written per test):
     order, exp and sin/cos), with >= 99.9 % of elements bit-identical;
     <= 1 ULP against the Triton-interpreter goldens (which truncate);
     <= 2 ULP against the eager PyTorch/HF compositions;
+  * RoPE outputs: rotate-half is a difference of two products, so a 1-ULP
+    difference in a normalised input or in a bf16 cos/sin value (sin/cos and
+    the sum-of-squares order differ between CPU and GPU) can become several
+    ULPs of a small, cancelled output.  An element passes when it is within
+    1 ULP or within 2^-8 x the largest magnitude of its head vector (the size
+    of such a one-ULP input change); >= 99 % of elements are bit-identical;
   * KV-cache slots and V copies: bit-exact, and no other slot changes.
 """
 from __future__ import annotations
@@ -40,6 +46,16 @@ def ulp(a, b):
 def assert_close_ulp(got, ref, max_ulp=1, min_exact=0.999):
     d = ulp(got, ref)
     assert int(d.max()) <= max_ulp, f"max ULP {int(d.max())}"
+    if d.numel():
+        assert float((d == 0).float().mean()) >= min_exact, f"exact fraction {float((d == 0).float().mean())}"
+
+
+def assert_rope_close(got, ref, min_exact=0.99):
+    got, ref = got.cpu(), ref.cpu()
+    d = ulp(got, ref)
+    scale = ref.float().abs().amax(dim=-1, keepdim=True) * 2.0 ** -8
+    ok = (d <= 1) | ((got.float() - ref.float()).abs() <= scale)
+    assert bool(ok.all()), f"{int((~ok).sum())} elements outside tolerance, max ULP {int(d.max())}"
     if d.numel():
         assert float((d == 0).float().mean()) >= min_exact, f"exact fraction {float((d == 0).float().mean())}"
 
@@ -305,8 +321,8 @@ def test_rope_kv_write_config2_decode(seed, norm):
     c = _config2_case(100 + seed, norm=norm)
     q, kc, vc, eq, ekc, evc, flags = _run_both(c, 1, 1)
     assert flags == 0 and _lib.read_and_clear_errors(DEV) == 0
-    assert_close_ulp(q, eq, 1, 0.99)
-    assert_close_ulp(kc, ekc, 1, 0.999)
+    assert_rope_close(q, eq)
+    assert_rope_close(kc, ekc, 0.999)
     assert torch.equal(vc.cpu(), evc)                       # V copy and untouched slots exact
     slot = int(c["slots"][0])
     mask = torch.ones(2048, dtype=torch.bool)
@@ -321,8 +337,8 @@ def test_rope_kv_write_prefill_sweep(t):
     c = _config2_case(200 + t, t=t, s_len=s_len, p0=p0, norm=True)
     q, kc, vc, eq, ekc, evc, flags = _run_both(c, t, 1)
     assert flags == 0 and _lib.read_and_clear_errors(DEV) == 0
-    assert_close_ulp(q, eq, 1, 0.99)
-    assert_close_ulp(kc, ekc, 1, 0.999)
+    assert_rope_close(q, eq)
+    assert_rope_close(kc, ekc, 0.999)
     assert torch.equal(vc.cpu(), evc)
 
 
@@ -331,8 +347,8 @@ def test_rope_kv_write_batched_streams():
     c = _config2_case(300, t=1, b=b, norm=True)
     q, kc, vc, eq, ekc, evc, flags = _run_both(c, 1, b)
     assert flags == 0
-    assert_close_ulp(q, eq, 1, 0.99)
-    assert_close_ulp(kc, ekc, 1, 0.999)
+    assert_rope_close(q, eq)
+    assert_rope_close(kc, ekc, 0.999)
     assert torch.equal(vc.cpu(), evc)
 
 
@@ -350,8 +366,8 @@ def test_rope_kv_write_packed_qkv_and_heads_major_output():
     ekc, evc = c["kc"].clone(), c["vc"].clone()
     eq, _ = O.rope_kv_write_ref(c["q"], c["k"], c["v"], c["inv"], c["pos"], ekc, evc, c["slots"],
                                 frame_table=c["tab"], q_norm_w=c["qw"], k_norm_w=c["kw"])
-    assert_close_ulp(q_attn.transpose(1, 2).reshape(t, hq, d), eq, 1, 0.99)
-    assert_close_ulp(kc, ekc, 1, 0.999)
+    assert_rope_close(q_attn.transpose(1, 2).reshape(t, hq, d), eq)
+    assert_rope_close(kc, ekc, 0.999)
     assert torch.equal(vc.cpu(), evc)
 
 
@@ -362,8 +378,8 @@ def test_rope_kv_write_out_of_range_slot_and_frame():
     q, kc, vc, eq, ekc, evc, flags = _run_both(c, 4, 1, frame_pos=fp)
     assert flags == 3
     assert _lib.read_and_clear_errors(DEV) == 3
-    assert_close_ulp(q, eq, 1, 0.99)
-    assert_close_ulp(kc, ekc, 1, 0.999)
+    assert_rope_close(q, eq)
+    assert_rope_close(kc, ekc, 0.999)
     assert torch.equal(vc.cpu(), evc)
 
 
@@ -377,8 +393,8 @@ def test_rope_kv_write_dtypes_and_generic_path(dtype, d, hq, hk):
         assert torch.allclose(q.cpu(), eq, rtol=1e-5, atol=1e-5)
         assert torch.allclose(kc.cpu(), ekc, rtol=1e-5, atol=1e-5)
     else:
-        assert_close_ulp(q, eq, 1, 0.99)
-        assert_close_ulp(kc, ekc, 1, 0.999)
+        assert_rope_close(q, eq)
+        assert_rope_close(kc, ekc, 0.999)
     assert torch.equal(vc.cpu(), evc)
 
 
@@ -393,8 +409,8 @@ def test_rope_kv_write_matches_reference_decode_composition():
     cos, sin = O.rope_cos_sin_ref(c["inv"], pos)
     q_ref, k_ref = O.rope_ref(qn, cos, sin), O.rope_ref(kn, cos, sin)
     q, kc, vc, *_ = _run_both(c, 1, 1)
-    assert_close_ulp(q, q_ref, 1, 0.99)
-    assert_close_ulp(kc.cpu()[0, :, pos], k_ref[0], 1, 0.99)
+    assert_rope_close(q, q_ref)
+    assert_rope_close(kc.cpu()[0, :, pos], k_ref[0])
     assert torch.equal(vc.cpu()[0, :, pos], c["v"][0])
 
 
@@ -416,8 +432,8 @@ def test_update_fused_through_static_cache():
     ekc, evc = c["kc"].clone(), c["vc"].clone()
     eq, _ = O.rope_kv_write_ref(c["q"], c["k"], c["v"], c["inv"], c["pos"], ekc, evc, c["slots"],
                                 q_norm_w=c["qw"], k_norm_w=c["kw"])
-    assert_close_ulp(q_rot.reshape(eq.shape), eq, 1, 0.99)
-    assert_close_ulp(kf, ekc, 1, 0.999)
+    assert_rope_close(q_rot.reshape(eq.shape), eq)
+    assert_rope_close(kf, ekc, 0.999)
     assert torch.equal(vf.cpu(), evc)
 
 
@@ -459,8 +475,8 @@ def test_ops_capture_in_cuda_graph():
         eq, _ = O.rope_kv_write_ref(c["q"], c["k"], c["v"], c["inv"], torch.tensor([p]), ekc, evc,
                                     torch.tensor([p]), frame_table=c["tab"], q_norm_w=c["qw"],
                                     k_norm_w=c["kw"])
-        assert_close_ulp(qo.reshape(eq.shape), eq, 1, 0.99)
-        assert_close_ulp(kc.cpu()[:, :, p], ekc[:, :, p], 1, 0.99)
+        assert_rope_close(qo.reshape(eq.shape), eq)
+        assert_rope_close(kc.cpu()[:, :, p], ekc[:, :, p])
     yo, ho = O.add_rms_norm_ref(x.cpu(), r.cpu(), w.cpu(), 1e-5)
     assert torch.equal(h.cpu(), ho)
     assert_close_ulp(y, yo)

@@ -53,6 +53,7 @@ struct RopeParams {
   int64_t table_rows;
   const int64_t* frame_pos;
   int tpf;
+  int tpf_shift;  // log2(tpf) when tpf is a power of two, else -1
   void* q_out;
   int64_t qots, qohs;
   void* k_cache;
@@ -70,17 +71,22 @@ struct TokenMeta {
   bool frame_ok;
 };
 
+// Stream index and frame row of token t.  The divisions are avoided in the
+// usual cases (one stream, one token per stream, power-of-two tokens per
+// frame): a 64-bit division is a long software sequence on the GPU.
 template <bool TABLE>
 __device__ __forceinline__ TokenMeta token_meta(const RopeParams& p, int64_t t) {
   TokenMeta m;
-  m.b = t / p.seq_tokens;
+  if (p.seq_tokens == 1) m.b = t;
+  else if (p.n_tokens == p.seq_tokens) m.b = 0;
+  else m.b = t / p.seq_tokens;
   m.slot = p.slots ? p.slots[t] : (t - m.b * p.seq_tokens);
   m.slot_ok = m.slot >= 0 && m.slot < p.clen;
   m.frame = 0;
   m.frame_ok = true;
   if constexpr (TABLE) {
     const int64_t fp = p.frame_pos ? p.frame_pos[t] : p.positions[t];
-    m.frame = fp >= 0 ? fp / p.tpf : -1;
+    m.frame = fp < 0 ? -1 : (p.tpf_shift >= 0 ? (fp >> p.tpf_shift) : fp / p.tpf);
     m.frame_ok = m.frame >= 0 && m.frame < p.table_rows;
   }
   return m;
@@ -265,6 +271,174 @@ rope_vec_kernel(RopeParams p, int log2l, int ipt, int iptr, int tpb) {
   }
 }
 
+// ------------------------------------------------------------- token kernel
+// Two warps per token: warp 0 rotates all Q heads, warp 1 rotates the K heads
+// and copies the V heads.  Lane = hh * L + jj as above; a lane carries QI Q
+// heads (hh, hh + G, ...) or KI K and V heads that all use the SAME E
+// frequencies, so per warp the sin/cos, their shuffles and the token metadata
+// are computed once for QI (or 2*KI) head vectors.  All of the warp's global
+// loads are issued before the trig.  Used when num_q_heads <= QI*G and
+// num_kv_heads <= KI*G (bf16, D=64: G=8, 16 Q / 8 KV heads -> QI=2, KI=1).
+template <typename T, bool NORM, bool TABLE, int QI, int KI>
+__global__ void __launch_bounds__(256)
+rope_token_kernel(RopeParams p, int log2l) {
+  constexpr int E = VecN<T>::value;
+  constexpr int NI = QI > KI ? QI : KI;
+  const int L = 1 << log2l;
+  const int log2g = 5 - log2l;
+  const int G = 1 << log2g;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 6) + (warp >> 1);
+  if (t >= p.n_tokens) return;  // warp-uniform exit
+  const bool qrole = (warp & 1) == 0;
+  const int hh = lane >> log2l;
+  const int jj = lane & (L - 1);
+  const int half = p.d >> 1;
+  const int lo = jj * E, hi = half + jj * E;
+
+  // 1. head data
+  uint4 xlo[NI], xhi[NI], vlo[KI], vhi[KI];
+  if (qrole) {
+    const T* base = static_cast<const T*>(p.q) + t * p.qts;
+#pragma unroll
+    for (int i = 0; i < QI; ++i) {
+      const int h = hh + i * G;
+      if (h < p.hq) {
+        xlo[i] = ld16_stream(base + (int64_t)h * p.d + lo);
+        xhi[i] = ld16_stream(base + (int64_t)h * p.d + hi);
+      }
+    }
+  } else {
+    const T* kb = static_cast<const T*>(p.k) + t * p.kts;
+    const T* vb = static_cast<const T*>(p.v) + t * p.vts;
+#pragma unroll
+    for (int i = 0; i < KI; ++i) {
+      const int h = hh + i * G;
+      if (h < p.hk) {
+        xlo[i] = ld16_stream(kb + (int64_t)h * p.d + lo);
+        xhi[i] = ld16_stream(kb + (int64_t)h * p.d + hi);
+        vlo[i] = ld16_stream(vb + (int64_t)h * p.d + lo);
+        vhi[i] = ld16_stream(vb + (int64_t)h * p.d + hi);
+      }
+    }
+  }
+  // 2. token metadata and the frame-table row
+  const TokenMeta m = token_meta<TABLE>(p, t);
+  if (qrole && lane == 0) flag_token<TABLE>(p, m);
+  uint4 plo = make_uint4(0, 0, 0, 0), phi = plo;
+  if constexpr (TABLE) {
+    if (m.frame_ok) {
+      const T* pr = static_cast<const T*>(p.table) + m.frame * p.d;
+      plo = ld16_ro(pr + lo);
+      phi = ld16_ro(pr + hi);
+    }
+  }
+
+  // 3. cos/sin of frequencies jj*E .. jj*E+E-1, shared through shuffles
+  float cs[E], sn[E];
+  {
+    const float posf = (float)p.positions[t];
+    const int rounds = (E + G - 1) >> log2g;
+    for (int r = 0; r < rounds; ++r) {
+      const int e_own = r * G + hh;
+      float cv = 0.f, sv = 0.f;
+      if (e_own < E) {
+        const float ang = __fmul_rn(__ldg(p.inv_freq + jj * E + e_own), posf);
+        cv = round_to<T>(cosf(ang));
+        sv = round_to<T>(sinf(ang));
+      }
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        if ((e >> log2g) == r) {  // uniform across the warp
+          const int src = ((e & (G - 1)) << log2l) | jj;
+          cs[e] = __shfl_sync(0xffffffffu, cv, src);
+          sn[e] = __shfl_sync(0xffffffffu, sv, src);
+        }
+      }
+    }
+  }
+  float pl[E], ph[E];
+  if constexpr (TABLE) {
+    unpack16<T>(plo, pl);
+    unpack16<T>(phi, ph);
+  }
+
+  // 4. per head: optional norm, rotate, frame term, store
+  const int nh = qrole ? p.hq : p.hk;
+  const int ni = qrole ? QI : KI;
+  const T* nw = static_cast<const T*>(qrole ? p.qw : p.kw);
+  T* qdst = static_cast<T*>(p.q_out) + t * p.qots;
+  T* kdst = static_cast<T*>(p.k_cache) + m.b * p.cbs + m.slot * p.css;
+#pragma unroll
+  for (int i = 0; i < NI; ++i) {
+    if (i >= ni) break;  // warp-uniform
+    const int h = hh + i * G;
+    const bool live = h < nh;
+    float a[E], b[E];
+    unpack16<T>(xlo[i], a);
+    unpack16<T>(xhi[i], b);
+    if constexpr (NORM) {
+      float ss = 0.f;
+      if (live) {
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          ss = fmaf(a[e], a[e], ss);
+          ss = fmaf(b[e], b[e], ss);
+        }
+      }
+      for (int off = L >> 1; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+      if (live) {
+        float wl[E], wh[E];
+        unpack16<T>(ld16_ro(nw + lo), wl);
+        unpack16<T>(ld16_ro(nw + hi), wh);
+        const float r = rrms_of(ss, p.d, p.eps);
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          a[e] = round_to<T>(__fmul_rn(__fmul_rn(a[e], r), wl[e]));
+          b[e] = round_to<T>(__fmul_rn(__fmul_rn(b[e], r), wh[e]));
+        }
+      }
+    }
+    if (!live) continue;
+    float ylo[E], yhi[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      ylo[e] = __fadd_rn(__fmul_rn(a[e], cs[e]), __fmul_rn(-b[e], sn[e]));
+      yhi[e] = __fadd_rn(__fmul_rn(b[e], cs[e]), __fmul_rn(a[e], sn[e]));
+    }
+    if constexpr (TABLE) {
+      if (m.frame_ok) {
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          ylo[e] = __fadd_rn(ylo[e], pl[e]);
+          yhi[e] = __fadd_rn(yhi[e], ph[e]);
+        }
+      }
+    }
+    if (qrole) {
+      T* dst = qdst + (int64_t)h * p.qohs;
+      st16(dst + lo, pack16<T>(ylo));
+      st16(dst + hi, pack16<T>(yhi));
+    } else if (m.slot_ok) {
+      T* dst = kdst + (int64_t)h * p.chs;
+      st16(dst + lo, pack16<T>(ylo));
+      st16(dst + hi, pack16<T>(yhi));
+    }
+  }
+  if (!qrole && m.slot_ok) {
+    T* vdst = static_cast<T*>(p.v_cache) + m.b * p.cbs + m.slot * p.css;
+#pragma unroll
+    for (int i = 0; i < KI; ++i) {
+      const int h = hh + i * G;
+      if (h < p.hk) {
+        st16(vdst + (int64_t)h * p.chs + lo, vlo[i]);
+        st16(vdst + (int64_t)h * p.chs + hi, vhi[i]);
+      }
+    }
+  }
+}
+
 // ----------------------------------------------------------- generic kernel
 template <typename T, bool NORM, bool TABLE, bool CS_GIVEN>
 __global__ void __launch_bounds__(256)
@@ -394,6 +568,25 @@ int launch_rope_t(const RopeParams& p, cudaStream_t s) {
   if (TABLE) vec = vec && aligned16(p.table);
   if (CS_GIVEN) vec = vec && aligned16(p.cos) && aligned16(p.sin);
 
+  if constexpr (!CS_GIVEN) {
+    // two-warps-per-token kernel: needs V, Q/K/V present and the heads to fit
+    if (vec && has_v && p.hq > 0 && p.hk > 0) {
+      const int G = 32 >> log2l;
+      const int64_t tpb = p.n_tokens < 4 ? p.n_tokens : 4;
+      const int64_t grid = (p.n_tokens + tpb - 1) / tpb;
+      if (grid <= 0x7fffffff) {
+        const dim3 blk((unsigned)(64 * tpb));
+        if (p.hq <= 2 * G && p.hk <= G) {
+          rope_token_kernel<T, NORM, TABLE, 2, 1><<<(unsigned)grid, blk, 0, s>>>(p, log2l);
+          return launch_status();
+        }
+        if (p.hq <= 4 * G && p.hk <= 2 * G) {
+          rope_token_kernel<T, NORM, TABLE, 4, 2><<<(unsigned)grid, blk, 0, s>>>(p, log2l);
+          return launch_status();
+        }
+      }
+    }
+  }
   if (vec) {
     const int heads = p.hq + p.hk + (has_v ? p.hk : 0);
     const int ipt = heads << log2l;
@@ -473,6 +666,7 @@ extern "C" int kani_rope_qk(int32_t dtype, const void* q, const void* k, const v
   p.css = 0;
   p.clen = 1;
   p.tpf = 1;
+  p.tpf_shift = 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return kani::dispatch_dtype(dtype, [&]<typename T>() { return kani::launch_rope<T>(p, s); });
 }
@@ -555,6 +749,9 @@ extern "C" int kani_rope_kv_write(
   p.table_rows = frame_rows;
   p.frame_pos = frame_pos;
   p.tpf = tokens_per_frame > 0 ? tokens_per_frame : 1;
+  p.tpf_shift = -1;
+  for (int sh = 0; sh < 31; ++sh)
+    if ((1 << sh) == p.tpf) p.tpf_shift = sh;
   p.q_out = q_out;
   p.qots = q_out_tok_stride;
   p.qohs = q_out_head_stride;

@@ -384,7 +384,8 @@ def test_rope_kv_write_out_of_range_slot_and_frame():
 
 
 @pytest.mark.parametrize("dtype,d,hq,hk", [(torch.float32, 64, 16, 8), (torch.float16, 64, 16, 8),
-                                           (torch.bfloat16, 128, 8, 2), (torch.bfloat16, 48, 4, 2)])
+                                           (torch.bfloat16, 128, 8, 2), (torch.bfloat16, 48, 4, 2),
+                                           (torch.bfloat16, 64, 48, 4), (torch.bfloat16, 32, 12, 12)])
 def test_rope_kv_write_dtypes_and_generic_path(dtype, d, hq, hk):
     c = _config2_case(600, t=9, p0=100, norm=True, dtype=dtype, hq=hq, hk=hk, d=d)
     q, kc, vc, eq, ekc, evc, flags = _run_both(c, 9, 1)

@@ -49,6 +49,7 @@ extern "C" {
 
 #define KANI_FLAG_SLOT_OOB 1  /* a KV write slot was outside [0, cache_len) */
 #define KANI_FLAG_FRAME_OOB 2 /* a frame-table row was outside [0, frame_rows) */
+#define KANI_FLAG_TIMEOUT 4   /* a bounded on-chip wait gave up (the call's outputs are incomplete) */
 
 /* Library ABI version (major*100 + minor). */
 KANI_API int kani_version(void);

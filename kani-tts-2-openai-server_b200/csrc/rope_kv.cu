@@ -271,22 +271,110 @@ rope_vec_kernel(RopeParams p, int log2l, int ipt, int iptr, int tpb) {
   }
 }
 
+// ------------------------------------------------------ shared warp helpers
+
+// cos/sin (rounded to T) of frequencies jj*E .. jj*E+E-1 at angle position
+// posf.  Lane = hh * L + jj: the 32/L lanes that share chunk jj compute the E
+// values between them (one cosf/sinf pair each when 32/L >= E) and exchange
+// them with shuffles.  Every lane of the warp must call this.
+template <typename T>
+__device__ __forceinline__ void warp_cos_sin(const float* __restrict__ inv_freq, float posf,
+                                             int log2l, int lane, float* cs, float* sn) {
+  constexpr int E = VecN<T>::value;
+  const int log2g = 5 - log2l;
+  const int G = 1 << log2g;
+  const int hh = lane >> log2l;
+  const int jj = lane & ((1 << log2l) - 1);
+  const int rounds = (E + G - 1) >> log2g;
+  for (int r = 0; r < rounds; ++r) {
+    const int e_own = r * G + hh;
+    float cv = 0.f, sv = 0.f;
+    if (e_own < E) {
+      const float ang = __fmul_rn(__ldg(inv_freq + jj * E + e_own), posf);
+      cv = round_to<T>(cosf(ang));
+      sv = round_to<T>(sinf(ang));
+    }
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      if ((e >> log2g) == r) {  // uniform across the warp
+        const int src = ((e & (G - 1)) << log2l) | jj;
+        cs[e] = __shfl_sync(0xffffffffu, cv, src);
+        sn[e] = __shfl_sync(0xffffffffu, sv, src);
+      }
+    }
+  }
+}
+
+// One lane's two chunks (elements [lo, lo+E) and [hi, hi+E)) of one head:
+// optional RMSNorm (an L-lane shuffle tree over the head, so every lane of
+// the warp must call this, live or not), rotate-half, optional frame term,
+// one rounding, store at dst + lo / dst + hi.
+template <typename T, bool NORM, bool TABLE>
+__device__ __forceinline__ void rope_chunk_store(uint4 xlo, uint4 xhi, bool live, const float* cs,
+                                                 const float* sn, const float* pl, const float* ph,
+                                                 bool frame_ok, const T* nw, int lo, int hi, int log2l,
+                                                 int d, float eps, T* dst) {
+  constexpr int E = VecN<T>::value;
+  float a[E], b[E];
+  unpack16<T>(xlo, a);
+  unpack16<T>(xhi, b);
+  if constexpr (NORM) {
+    float ss = 0.f;
+    if (live) {
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        ss = fmaf(a[e], a[e], ss);
+        ss = fmaf(b[e], b[e], ss);
+      }
+    }
+    for (int off = (1 << log2l) >> 1; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    if (live) {
+      float wl[E], wh[E];
+      unpack16<T>(ld16_ro(nw + lo), wl);
+      unpack16<T>(ld16_ro(nw + hi), wh);
+      const float r = rrms_of(ss, d, eps);
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        a[e] = round_to<T>(__fmul_rn(__fmul_rn(a[e], r), wl[e]));
+        b[e] = round_to<T>(__fmul_rn(__fmul_rn(b[e], r), wh[e]));
+      }
+    }
+  }
+  if (!live) return;
+  float ylo[E], yhi[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    ylo[e] = __fadd_rn(__fmul_rn(a[e], cs[e]), __fmul_rn(-b[e], sn[e]));
+    yhi[e] = __fadd_rn(__fmul_rn(b[e], cs[e]), __fmul_rn(a[e], sn[e]));
+  }
+  if constexpr (TABLE) {
+    if (frame_ok) {
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        ylo[e] = __fadd_rn(ylo[e], pl[e]);
+        yhi[e] = __fadd_rn(yhi[e], ph[e]);
+      }
+    }
+  }
+  st16(dst + lo, pack16<T>(ylo));
+  st16(dst + hi, pack16<T>(yhi));
+}
+
 // ------------------------------------------------------------- token kernel
 // Two warps per token: warp 0 rotates all Q heads, warp 1 rotates the K heads
-// and copies the V heads.  Lane = hh * L + jj as above; a lane carries QI Q
-// heads (hh, hh + G, ...) or KI K and V heads that all use the SAME E
-// frequencies, so per warp the sin/cos, their shuffles and the token metadata
-// are computed once for QI (or 2*KI) head vectors.  All of the warp's global
-// loads are issued before the trig.  Used when num_q_heads <= QI*G and
-// num_kv_heads <= KI*G (bf16, D=64: G=8, 16 Q / 8 KV heads -> QI=2, KI=1).
+// and copies the V heads.  A lane carries QI Q heads (hh, hh + G, ...) or KI
+// K and V heads that all use the SAME E frequencies, so per warp the
+// sin/cos, their shuffles and the token metadata are computed once for QI
+// (or 2*KI) head vectors.  All of the warp's global loads are issued before
+// the trig.  Used for short calls (decode steps) when num_q_heads <= QI*G
+// and num_kv_heads <= KI*G (bf16, D=64: G=8, 16 Q / 8 KV heads -> QI=2, KI=1).
 template <typename T, bool NORM, bool TABLE, int QI, int KI>
 __global__ void __launch_bounds__(256)
 rope_token_kernel(RopeParams p, int log2l) {
   constexpr int E = VecN<T>::value;
   constexpr int NI = QI > KI ? QI : KI;
   const int L = 1 << log2l;
-  const int log2g = 5 - log2l;
-  const int G = 1 << log2g;
+  const int G = 32 >> log2l;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 6) + (warp >> 1);
@@ -294,8 +382,7 @@ rope_token_kernel(RopeParams p, int log2l) {
   const bool qrole = (warp & 1) == 0;
   const int hh = lane >> log2l;
   const int jj = lane & (L - 1);
-  const int half = p.d >> 1;
-  const int lo = jj * E, hi = half + jj * E;
+  const int lo = jj * E, hi = (p.d >> 1) + jj * E;
 
   // 1. head data
   uint4 xlo[NI], xhi[NI], vlo[KI], vhi[KI];
@@ -334,97 +421,27 @@ rope_token_kernel(RopeParams p, int log2l) {
       phi = ld16_ro(pr + hi);
     }
   }
-
-  // 3. cos/sin of frequencies jj*E .. jj*E+E-1, shared through shuffles
+  // 3. cos/sin
   float cs[E], sn[E];
-  {
-    const float posf = (float)p.positions[t];
-    const int rounds = (E + G - 1) >> log2g;
-    for (int r = 0; r < rounds; ++r) {
-      const int e_own = r * G + hh;
-      float cv = 0.f, sv = 0.f;
-      if (e_own < E) {
-        const float ang = __fmul_rn(__ldg(p.inv_freq + jj * E + e_own), posf);
-        cv = round_to<T>(cosf(ang));
-        sv = round_to<T>(sinf(ang));
-      }
-#pragma unroll
-      for (int e = 0; e < E; ++e) {
-        if ((e >> log2g) == r) {  // uniform across the warp
-          const int src = ((e & (G - 1)) << log2l) | jj;
-          cs[e] = __shfl_sync(0xffffffffu, cv, src);
-          sn[e] = __shfl_sync(0xffffffffu, sv, src);
-        }
-      }
-    }
-  }
+  warp_cos_sin<T>(p.inv_freq, (float)p.positions[t], log2l, lane, cs, sn);
   float pl[E], ph[E];
   if constexpr (TABLE) {
     unpack16<T>(plo, pl);
     unpack16<T>(phi, ph);
   }
-
-  // 4. per head: optional norm, rotate, frame term, store
+  // 4. per head: norm, rotate, frame term, store
   const int nh = qrole ? p.hq : p.hk;
-  const int ni = qrole ? QI : KI;
   const T* nw = static_cast<const T*>(qrole ? p.qw : p.kw);
   T* qdst = static_cast<T*>(p.q_out) + t * p.qots;
   T* kdst = static_cast<T*>(p.k_cache) + m.b * p.cbs + m.slot * p.css;
 #pragma unroll
   for (int i = 0; i < NI; ++i) {
-    if (i >= ni) break;  // warp-uniform
+    if (i >= (qrole ? QI : KI)) break;  // warp-uniform
     const int h = hh + i * G;
-    const bool live = h < nh;
-    float a[E], b[E];
-    unpack16<T>(xlo[i], a);
-    unpack16<T>(xhi[i], b);
-    if constexpr (NORM) {
-      float ss = 0.f;
-      if (live) {
-#pragma unroll
-        for (int e = 0; e < E; ++e) {
-          ss = fmaf(a[e], a[e], ss);
-          ss = fmaf(b[e], b[e], ss);
-        }
-      }
-      for (int off = L >> 1; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-      if (live) {
-        float wl[E], wh[E];
-        unpack16<T>(ld16_ro(nw + lo), wl);
-        unpack16<T>(ld16_ro(nw + hi), wh);
-        const float r = rrms_of(ss, p.d, p.eps);
-#pragma unroll
-        for (int e = 0; e < E; ++e) {
-          a[e] = round_to<T>(__fmul_rn(__fmul_rn(a[e], r), wl[e]));
-          b[e] = round_to<T>(__fmul_rn(__fmul_rn(b[e], r), wh[e]));
-        }
-      }
-    }
-    if (!live) continue;
-    float ylo[E], yhi[E];
-#pragma unroll
-    for (int e = 0; e < E; ++e) {
-      ylo[e] = __fadd_rn(__fmul_rn(a[e], cs[e]), __fmul_rn(-b[e], sn[e]));
-      yhi[e] = __fadd_rn(__fmul_rn(b[e], cs[e]), __fmul_rn(a[e], sn[e]));
-    }
-    if constexpr (TABLE) {
-      if (m.frame_ok) {
-#pragma unroll
-        for (int e = 0; e < E; ++e) {
-          ylo[e] = __fadd_rn(ylo[e], pl[e]);
-          yhi[e] = __fadd_rn(yhi[e], ph[e]);
-        }
-      }
-    }
-    if (qrole) {
-      T* dst = qdst + (int64_t)h * p.qohs;
-      st16(dst + lo, pack16<T>(ylo));
-      st16(dst + hi, pack16<T>(yhi));
-    } else if (m.slot_ok) {
-      T* dst = kdst + (int64_t)h * p.chs;
-      st16(dst + lo, pack16<T>(ylo));
-      st16(dst + hi, pack16<T>(yhi));
-    }
+    const bool live = h < nh && (qrole || m.slot_ok);
+    T* dst = qrole ? qdst + (int64_t)h * p.qohs : kdst + (int64_t)h * p.chs;
+    rope_chunk_store<T, NORM, TABLE>(xlo[i], xhi[i], live, cs, sn, pl, ph, m.frame_ok, nw, lo, hi,
+                                     log2l, p.d, p.eps, dst);
   }
   if (!qrole && m.slot_ok) {
     T* vdst = static_cast<T*>(p.v_cache) + m.b * p.cbs + m.slot * p.css;
@@ -437,6 +454,265 @@ rope_token_kernel(RopeParams p, int log2l) {
       }
     }
   }
+}
+
+// -------------------------------------------------------------- bulk kernel
+// Long calls (prefill-sized token counts).  A persistent CTA walks groups of
+// kBulkTPS tokens; thread 0 streams each group's Q, K and V rows into a
+// kBulkStages-deep shared-memory ring with TMA bulk copies
+// (cp.async.bulk, completion on an mbarrier, no multicast), so the bytes in
+// flight are bounded by shared memory rather than by registers.  The eight
+// warps of the CTA are the two roles of the token kernel for four tokens and
+// read their head chunks from shared memory.  Every mbarrier wait is bounded:
+// on a timeout the CTA raises KANI_FLAG_TIMEOUT, waits (bounded) for the
+// copies it issued and returns.
+constexpr int kBulkTPS = 4;
+constexpr int kBulkStages = 4;
+constexpr long long kWaitCycles = 2000000000LL;  // ~1 s at the B200 clock
+
+__device__ __forceinline__ uint32_t smem_u32(const void* ptr) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(ptr));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long start = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - start > kWaitCycles) return false;
+  }
+  return true;
+}
+
+// global -> shared bulk copy; addresses 16-byte aligned, bytes a multiple of 16
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+// Copy `cnt` token rows of `row` bytes (source rows `stride` bytes apart) to
+// consecutive shared memory: one copy when the rows are contiguous.
+__device__ __forceinline__ void bulk_rows(uint32_t dst, const char* src, uint32_t row, int64_t stride,
+                                          int cnt, uint32_t bar) {
+  if (stride == (int64_t)row) {
+    bulk_g2s(dst, src, row * cnt, bar);
+  } else {
+    for (int i = 0; i < cnt; ++i) bulk_g2s(dst + i * row, src + i * stride, row, bar);
+  }
+}
+
+template <typename T, bool NORM, bool TABLE, int QI, int KI>
+__global__ void __launch_bounds__(256)
+rope_bulk_kernel(RopeParams p, int log2l, int64_t n_groups, uint32_t stage_bytes) {
+  constexpr int E = VecN<T>::value;
+  constexpr int ES = (int)sizeof(T);
+  extern __shared__ __align__(128) unsigned char ring[];
+  __shared__ __align__(8) uint64_t bars[kBulkStages];
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const uint32_t qrow = (uint32_t)(p.hq * p.d * ES);
+  const uint32_t krow = (uint32_t)(p.hk * p.d * ES);
+
+  if (tid == 0) {
+    for (int s = 0; s < kBulkStages; ++s) mbar_init(smem_u32(&bars[s]), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  // thread 0: fill stage s with token group g
+  auto issue = [&](int s, int64_t g) {
+    const int64_t t0 = g * kBulkTPS;
+    const int cnt = (int)(p.n_tokens - t0 < kBulkTPS ? p.n_tokens - t0 : kBulkTPS);
+    const uint32_t bar = smem_u32(&bars[s]);
+    const uint32_t base = smem_u32(ring + (size_t)s * stage_bytes);
+    mbar_expect_tx(bar, (uint32_t)cnt * (qrow + 2 * krow));
+    bulk_rows(base, reinterpret_cast<const char*>(static_cast<const T*>(p.q) + t0 * p.qts), qrow,
+              p.qts * ES, cnt, bar);
+    bulk_rows(base + kBulkTPS * qrow, reinterpret_cast<const char*>(static_cast<const T*>(p.k) + t0 * p.kts),
+              krow, p.kts * ES, cnt, bar);
+    bulk_rows(base + kBulkTPS * (qrow + krow),
+              reinterpret_cast<const char*>(static_cast<const T*>(p.v) + t0 * p.vts), krow, p.vts * ES, cnt,
+              bar);
+  };
+  if (tid == 0) {
+    for (int s = 0; s < kBulkStages; ++s) {
+      const int64_t g = blockIdx.x + (int64_t)s * gridDim.x;
+      if (g < n_groups) issue(s, g);
+    }
+  }
+
+  const int L = 1 << log2l;
+  const int G = 32 >> log2l;
+  const int tl = warp >> 1;
+  const bool qrole = (warp & 1) == 0;
+  const int hh = lane >> log2l;
+  const int jj = lane & (L - 1);
+  const int lo = jj * E, hi = (p.d >> 1) + jj * E;
+  const int nh = qrole ? p.hq : p.hk;
+  const T* nw = static_cast<const T*>(qrole ? p.qw : p.kw);
+
+  int64_t it = 0;
+  bool failed = false;
+  for (;; ++it) {
+    const int64_t g = blockIdx.x + it * gridDim.x;
+    if (g >= n_groups) break;  // uniform across the CTA
+    const int s = (int)(it % kBulkStages);
+    const uint32_t parity = (uint32_t)((it / kBulkStages) & 1);
+    const int64_t t = g * kBulkTPS + tl;
+    const bool tok_ok = t < p.n_tokens;  // warp-uniform
+    // token metadata and frame row: plain loads whose latency overlaps the wait
+    TokenMeta m{};
+    float posf = 0.f;
+    uint4 plo = make_uint4(0, 0, 0, 0), phi = plo;
+    if (tok_ok) {
+      m = token_meta<TABLE>(p, t);
+      posf = (float)p.positions[t];
+      if (qrole && lane == 0) flag_token<TABLE>(p, m);
+      if constexpr (TABLE) {
+        if (m.frame_ok) {
+          const T* pr = static_cast<const T*>(p.table) + m.frame * p.d;
+          plo = ld16_ro(pr + lo);
+          phi = ld16_ro(pr + hi);
+        }
+      }
+    }
+    const bool ready = mbar_wait_bounded(smem_u32(&bars[s]), parity);
+    if (ready && tok_ok) {
+      float cs[E], sn[E], pl[E], ph[E];
+      warp_cos_sin<T>(p.inv_freq, posf, log2l, lane, cs, sn);
+      if constexpr (TABLE) {
+        unpack16<T>(plo, pl);
+        unpack16<T>(phi, ph);
+      }
+      const unsigned char* st = ring + (size_t)s * stage_bytes;
+      if (qrole) {
+        const unsigned char* src = st + tl * qrow;
+        T* qdst = static_cast<T*>(p.q_out) + t * p.qots;
+#pragma unroll
+        for (int i = 0; i < QI; ++i) {
+          const int h = hh + i * G;
+          const bool live = h < nh;
+          uint4 xlo = make_uint4(0, 0, 0, 0), xhi = xlo;
+          if (live) {
+            const T* hs = reinterpret_cast<const T*>(src) + h * p.d;
+            xlo = *reinterpret_cast<const uint4*>(hs + lo);
+            xhi = *reinterpret_cast<const uint4*>(hs + hi);
+          }
+          rope_chunk_store<T, NORM, TABLE>(xlo, xhi, live, cs, sn, pl, ph, m.frame_ok, nw, lo, hi, log2l,
+                                           p.d, p.eps, qdst + (int64_t)h * p.qohs);
+        }
+      } else {
+        const unsigned char* ksrc = st + kBulkTPS * qrow + tl * krow;
+        const unsigned char* vsrc = st + kBulkTPS * (qrow + krow) + tl * krow;
+        T* kdst = static_cast<T*>(p.k_cache) + m.b * p.cbs + m.slot * p.css;
+        T* vdst = static_cast<T*>(p.v_cache) + m.b * p.cbs + m.slot * p.css;
+#pragma unroll
+        for (int i = 0; i < KI; ++i) {
+          const int h = hh + i * G;
+          const bool has = h < nh;
+          uint4 xlo = make_uint4(0, 0, 0, 0), xhi = xlo;
+          if (has) {
+            const T* hs = reinterpret_cast<const T*>(ksrc) + h * p.d;
+            xlo = *reinterpret_cast<const uint4*>(hs + lo);
+            xhi = *reinterpret_cast<const uint4*>(hs + hi);
+          }
+          rope_chunk_store<T, NORM, TABLE>(xlo, xhi, has && m.slot_ok, cs, sn, pl, ph, m.frame_ok, nw, lo,
+                                           hi, log2l, p.d, p.eps, kdst + (int64_t)h * p.chs);
+          if (has && m.slot_ok) {
+            const T* vs = reinterpret_cast<const T*>(vsrc) + h * p.d;
+            st16(vdst + (int64_t)h * p.chs + lo, *reinterpret_cast<const uint4*>(vs + lo));
+            st16(vdst + (int64_t)h * p.chs + hi, *reinterpret_cast<const uint4*>(vs + hi));
+          }
+        }
+      }
+    }
+    failed = failed || !ready;
+    // every thread arrives: the stage is free again, and a timeout anywhere
+    // stops the whole CTA at the same iteration
+    if (__syncthreads_or(failed)) break;
+    if (tid == 0) {
+      const int64_t gn = g + (int64_t)kBulkStages * gridDim.x;
+      if (gn < n_groups) {
+        // order this CTA's shared-memory reads before the async-proxy refill
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        issue(s, gn);
+      }
+    }
+  }
+  if (failed && tid == 0) {
+    if (p.err != nullptr) atomicOr(p.err, KANI_FLAG_TIMEOUT);
+    // copies issued for iterations it .. it+kBulkStages-1 were never consumed
+    for (int64_t j = it; j < it + kBulkStages; ++j) {
+      if (blockIdx.x + j * gridDim.x >= n_groups) break;
+      mbar_wait_bounded(smem_u32(&bars[j % kBulkStages]), (uint32_t)((j / kBulkStages) & 1));
+    }
+  }
+}
+
+// Per-device cached SM count (the one piece of state the library keeps).
+int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+template <typename T, bool NORM, bool TABLE, int QI, int KI>
+int launch_bulk(const RopeParams& p, int log2l, cudaStream_t s) {
+  constexpr int ES = (int)sizeof(T);
+  const uint32_t row_bytes = (uint32_t)((p.hq + 2 * p.hk) * p.d * ES);
+  const uint32_t stage_bytes = ((kBulkTPS * row_bytes + 127u) / 128u) * 128u;
+  const size_t smem = (size_t)kBulkStages * stage_bytes;
+  auto kern = rope_bulk_kernel<T, NORM, TABLE, QI, KI>;
+  static int smem_set[64] = {0};
+  static int per_sm[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return KANI_ERR_UNSUPPORTED;
+  if (smem_set[dev] < (int)smem) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return launch_status();
+    smem_set[dev] = (int)smem;
+    per_sm[dev] = 0;
+  }
+  if (per_sm[dev] == 0) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, 256, smem) != cudaSuccess || n <= 0) n = 1;
+    per_sm[dev] = n;
+  }
+  const int64_t n_groups = (p.n_tokens + kBulkTPS - 1) / kBulkTPS;
+  int64_t grid = (int64_t)sm_count() * per_sm[dev];
+  if (grid > n_groups) grid = n_groups;
+  kern<<<(unsigned)grid, 256, smem, s>>>(p, log2l, n_groups, stage_bytes);
+  return launch_status();
 }
 
 // ----------------------------------------------------------- generic kernel
@@ -547,6 +823,8 @@ kv_write_kernel(const T* __restrict__ k, const T* __restrict__ v, int64_t batch,
 }
 
 // ------------------------------------------------------------------ launch
+constexpr int64_t kBulkMinTokens = 256;  // shorter calls use the token kernel
+
 template <typename T, bool NORM, bool TABLE, bool CS_GIVEN>
 int launch_rope_t(const RopeParams& p, cudaStream_t s) {
   constexpr int E = VecN<T>::value;
@@ -569,6 +847,17 @@ int launch_rope_t(const RopeParams& p, cudaStream_t s) {
   if (CS_GIVEN) vec = vec && aligned16(p.cos) && aligned16(p.sin);
 
   if constexpr (!CS_GIVEN) {
+    // long calls: bulk-copy ring; needs 16-byte token rows and strides
+    if (vec && has_v && p.hq > 0 && p.hk > 0 && p.n_tokens >= kBulkMinTokens) {
+      const int G = 32 >> log2l;
+      const bool rows16 = ((int64_t)p.hq * p.d * (int64_t)sizeof(T)) % 16 == 0 &&
+                          ((int64_t)p.hk * p.d * (int64_t)sizeof(T)) % 16 == 0;
+      const int64_t stage = (int64_t)kBulkTPS * (p.hq + 2 * p.hk) * p.d * (int64_t)sizeof(T);
+      if (rows16 && stage * kBulkStages <= 160 * 1024) {
+        if (p.hq <= 2 * G && p.hk <= G) return launch_bulk<T, NORM, TABLE, 2, 1>(p, log2l, s);
+        if (p.hq <= 4 * G && p.hk <= 2 * G) return launch_bulk<T, NORM, TABLE, 4, 2>(p, log2l, s);
+      }
+    }
     // two-warps-per-token kernel: needs V, Q/K/V present and the heads to fit
     if (vec && has_v && p.hq > 0 && p.hk > 0) {
       const int G = 32 >> log2l;

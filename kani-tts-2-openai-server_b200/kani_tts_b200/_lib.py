@@ -21,6 +21,7 @@ KANI_DTYPE_F16 = 2
 
 KANI_FLAG_SLOT_OOB = 1
 KANI_FLAG_FRAME_OOB = 2
+KANI_FLAG_TIMEOUT = 4
 
 _DTYPE_CODES = {
     torch.float32: KANI_DTYPE_F32,

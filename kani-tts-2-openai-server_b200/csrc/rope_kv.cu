@@ -92,6 +92,25 @@ __device__ __forceinline__ TokenMeta token_meta(const RopeParams& p, int64_t t) 
   return m;
 }
 
+// Same as token_meta, from already-loaded position / slot / frame values.
+template <bool TABLE>
+__device__ __forceinline__ TokenMeta token_meta_vals(const RopeParams& p, int64_t t, int64_t slot,
+                                                     int64_t fp) {
+  TokenMeta m;
+  if (p.seq_tokens == 1) m.b = t;
+  else if (p.n_tokens == p.seq_tokens) m.b = 0;
+  else m.b = t / p.seq_tokens;
+  m.slot = slot;
+  m.slot_ok = m.slot >= 0 && m.slot < p.clen;
+  m.frame = 0;
+  m.frame_ok = true;
+  if constexpr (TABLE) {
+    m.frame = fp < 0 ? -1 : (p.tpf_shift >= 0 ? (fp >> p.tpf_shift) : fp / p.tpf);
+    m.frame_ok = m.frame >= 0 && m.frame < p.table_rows;
+  }
+  return m;
+}
+
 template <bool TABLE>
 __device__ __forceinline__ void flag_token(const RopeParams& p, const TokenMeta& m) {
   if (p.err == nullptr) return;
@@ -512,6 +531,11 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
       : "memory");
 }
 
+// Hint: pull [src, src + bytes) into L2 (bytes a multiple of 16).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // Copy `cnt` token rows of `row` bytes (source rows `stride` bytes apart) to
 // consecutive shared memory: one copy when the rows are contiguous.
 __device__ __forceinline__ void bulk_rows(uint32_t dst, const char* src, uint32_t row, int64_t stride,
@@ -525,7 +549,7 @@ __device__ __forceinline__ void bulk_rows(uint32_t dst, const char* src, uint32_
 
 template <typename T, bool NORM, bool TABLE, int QI, int KI>
 __global__ void __launch_bounds__(256)
-rope_bulk_kernel(RopeParams p, int log2l, int64_t n_groups, uint32_t stage_bytes) {
+rope_bulk_kernel(RopeParams p, int log2l, int64_t n_groups, uint32_t stage_bytes, bool meta_bulk) {
   constexpr int E = VecN<T>::value;
   constexpr int ES = (int)sizeof(T);
   extern __shared__ __align__(128) unsigned char ring[];
@@ -542,13 +566,25 @@ rope_bulk_kernel(RopeParams p, int log2l, int64_t n_groups, uint32_t stage_bytes
   }
   __syncthreads();
 
+  // Stage layout: [Q rows][K rows][V rows][positions][slots][frame positions]
+  // (the last three: kBulkTPS int64 each, copied only for full groups when
+  // the arrays are 16-byte aligned; otherwise each warp loads its own).
+  const uint32_t meta_off = kBulkTPS * (qrow + 2 * krow);
   // thread 0: fill stage s with token group g
   auto issue = [&](int s, int64_t g) {
     const int64_t t0 = g * kBulkTPS;
     const int cnt = (int)(p.n_tokens - t0 < kBulkTPS ? p.n_tokens - t0 : kBulkTPS);
+    const bool meta = meta_bulk && cnt == kBulkTPS;
     const uint32_t bar = smem_u32(&bars[s]);
     const uint32_t base = smem_u32(ring + (size_t)s * stage_bytes);
-    mbar_expect_tx(bar, (uint32_t)cnt * (qrow + 2 * krow));
+    const uint32_t mb = kBulkTPS * 8;
+    const uint32_t meta_bytes = meta ? mb * (1u + (p.slots ? 1u : 0u) + (p.frame_pos ? 1u : 0u)) : 0u;
+    mbar_expect_tx(bar, (uint32_t)cnt * (qrow + 2 * krow) + meta_bytes);
+    if (meta) {
+      bulk_g2s(base + meta_off, p.positions + t0, mb, bar);
+      if (p.slots) bulk_g2s(base + meta_off + mb, p.slots + t0, mb, bar);
+      if (p.frame_pos) bulk_g2s(base + meta_off + 2 * mb, p.frame_pos + t0, mb, bar);
+    }
     bulk_rows(base, reinterpret_cast<const char*>(static_cast<const T*>(p.q) + t0 * p.qts), qrow,
               p.qts * ES, cnt, bar);
     bulk_rows(base + kBulkTPS * qrow, reinterpret_cast<const char*>(static_cast<const T*>(p.k) + t0 * p.kts),
@@ -561,6 +597,15 @@ rope_bulk_kernel(RopeParams p, int log2l, int64_t n_groups, uint32_t stage_bytes
     for (int s = 0; s < kBulkStages; ++s) {
       const int64_t g = blockIdx.x + (int64_t)s * gridDim.x;
       if (g < n_groups) issue(s, g);
+    }
+    if constexpr (TABLE) {
+      // each CTA pulls its share of the frame table into L2 (rows are 16-byte multiples)
+      const int64_t rows = p.table_rows;
+      const int64_t per = (rows + gridDim.x - 1) / gridDim.x;
+      const int64_t r0 = (int64_t)blockIdx.x * per;
+      const int64_t r1 = r0 + per < rows ? r0 + per : rows;
+      if (r1 > r0)
+        bulk_prefetch_l2(static_cast<const T*>(p.table) + r0 * p.d, (uint32_t)((r1 - r0) * p.d * ES));
     }
   }
 
@@ -583,14 +628,25 @@ rope_bulk_kernel(RopeParams p, int log2l, int64_t n_groups, uint32_t stage_bytes
     const uint32_t parity = (uint32_t)((it / kBulkStages) & 1);
     const int64_t t = g * kBulkTPS + tl;
     const bool tok_ok = t < p.n_tokens;  // warp-uniform
-    // token metadata and frame row: plain loads whose latency overlaps the wait
-    TokenMeta m{};
-    float posf = 0.f;
-    uint4 plo = make_uint4(0, 0, 0, 0), phi = plo;
-    if (tok_ok) {
-      m = token_meta<TABLE>(p, t);
-      posf = (float)p.positions[t];
+    const bool meta_here = meta_bulk && (g + 1) * kBulkTPS <= p.n_tokens;
+    const bool ready = mbar_wait_bounded(smem_u32(&bars[s]), parity);
+    if (ready && tok_ok) {
+      const unsigned char* st = ring + (size_t)s * stage_bytes;
+      int64_t pos, slot, fp;
+      if (meta_here) {
+        const int64_t* mp = reinterpret_cast<const int64_t*>(st + meta_off);
+        pos = mp[tl];
+        slot = p.slots ? mp[kBulkTPS + tl] : (t - (t / p.seq_tokens) * p.seq_tokens);
+        fp = p.frame_pos ? mp[2 * kBulkTPS + tl] : pos;
+      } else {
+        pos = p.positions[t];
+        slot = p.slots ? p.slots[t] : (t - (t / p.seq_tokens) * p.seq_tokens);
+        fp = p.frame_pos ? p.frame_pos[t] : pos;
+      }
+      const TokenMeta m = token_meta_vals<TABLE>(p, t, slot, fp);
       if (qrole && lane == 0) flag_token<TABLE>(p, m);
+      // the frame row (an L2 hit after the prefetch) overlaps the trig
+      uint4 plo = make_uint4(0, 0, 0, 0), phi = plo;
       if constexpr (TABLE) {
         if (m.frame_ok) {
           const T* pr = static_cast<const T*>(p.table) + m.frame * p.d;
@@ -598,16 +654,12 @@ rope_bulk_kernel(RopeParams p, int log2l, int64_t n_groups, uint32_t stage_bytes
           phi = ld16_ro(pr + hi);
         }
       }
-    }
-    const bool ready = mbar_wait_bounded(smem_u32(&bars[s]), parity);
-    if (ready && tok_ok) {
       float cs[E], sn[E], pl[E], ph[E];
-      warp_cos_sin<T>(p.inv_freq, posf, log2l, lane, cs, sn);
+      warp_cos_sin<T>(p.inv_freq, (float)pos, log2l, lane, cs, sn);
       if constexpr (TABLE) {
         unpack16<T>(plo, pl);
         unpack16<T>(phi, ph);
       }
-      const unsigned char* st = ring + (size_t)s * stage_bytes;
       if (qrole) {
         const unsigned char* src = st + tl * qrow;
         T* qdst = static_cast<T*>(p.q_out) + t * p.qots;
@@ -689,7 +741,9 @@ template <typename T, bool NORM, bool TABLE, int QI, int KI>
 int launch_bulk(const RopeParams& p, int log2l, cudaStream_t s) {
   constexpr int ES = (int)sizeof(T);
   const uint32_t row_bytes = (uint32_t)((p.hq + 2 * p.hk) * p.d * ES);
-  const uint32_t stage_bytes = ((kBulkTPS * row_bytes + 127u) / 128u) * 128u;
+  const uint32_t stage_bytes = ((kBulkTPS * row_bytes + 3 * kBulkTPS * 8 + 127u) / 128u) * 128u;
+  const bool meta_bulk = aligned16(p.positions) && (p.slots == nullptr || aligned16(p.slots)) &&
+                         (p.frame_pos == nullptr || aligned16(p.frame_pos));
   const size_t smem = (size_t)kBulkStages * stage_bytes;
   auto kern = rope_bulk_kernel<T, NORM, TABLE, QI, KI>;
   static int smem_set[64] = {0};
@@ -711,7 +765,7 @@ int launch_bulk(const RopeParams& p, int log2l, cudaStream_t s) {
   const int64_t n_groups = (p.n_tokens + kBulkTPS - 1) / kBulkTPS;
   int64_t grid = (int64_t)sm_count() * per_sm[dev];
   if (grid > n_groups) grid = n_groups;
-  kern<<<(unsigned)grid, 256, smem, s>>>(p, log2l, n_groups, stage_bytes);
+  kern<<<(unsigned)grid, 256, smem, s>>>(p, log2l, n_groups, stage_bytes, meta_bulk);
   return launch_status();
 }
 
@@ -852,7 +906,7 @@ int launch_rope_t(const RopeParams& p, cudaStream_t s) {
       const int G = 32 >> log2l;
       const bool rows16 = ((int64_t)p.hq * p.d * (int64_t)sizeof(T)) % 16 == 0 &&
                           ((int64_t)p.hk * p.d * (int64_t)sizeof(T)) % 16 == 0;
-      const int64_t stage = (int64_t)kBulkTPS * (p.hq + 2 * p.hk) * p.d * (int64_t)sizeof(T);
+      const int64_t stage = (int64_t)kBulkTPS * (p.hq + 2 * p.hk) * p.d * (int64_t)sizeof(T) + 3 * kBulkTPS * 8;
       if (rows16 && stage * kBulkStages <= 160 * 1024) {
         if (p.hq <= 2 * G && p.hk <= G) return launch_bulk<T, NORM, TABLE, 2, 1>(p, log2l, s);
         if (p.hq <= 4 * G && p.hk <= 2 * G) return launch_bulk<T, NORM, TABLE, 4, 2>(p, log2l, s);

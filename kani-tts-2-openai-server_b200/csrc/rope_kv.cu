@@ -476,17 +476,19 @@ rope_token_kernel(RopeParams p, int log2l) {
 }
 
 // -------------------------------------------------------------- bulk kernel
-// Long calls (prefill-sized token counts).  A persistent CTA walks groups of
-// kBulkTPS tokens; thread 0 streams each group's Q, K and V rows into a
-// kBulkStages-deep shared-memory ring with TMA bulk copies
-// (cp.async.bulk, completion on an mbarrier, no multicast), so the bytes in
-// flight are bounded by shared memory rather than by registers.  The eight
-// warps of the CTA are the two roles of the token kernel for four tokens and
-// read their head chunks from shared memory.  Every mbarrier wait is bounded:
-// on a timeout the CTA raises KANI_FLAG_TIMEOUT, waits (bounded) for the
-// copies it issued and returns.
+// Long calls (prefill-sized token counts).  One CTA of kBulkTPS warps per
+// group of kBulkTPS tokens; the hardware block scheduler balances the groups
+// over the SMs.  Thread 0 brings the group's Q, K and V rows (and, for a full
+// group with 16-byte aligned arrays, its positions / slots / frame positions)
+// into shared memory with TMA bulk copies (cp.async.bulk, completion on one
+// mbarrier, no multicast) and pulls the CTA's share of the frame table into
+// L2; shared memory, not registers, holds the bytes in flight.  Each warp
+// then owns one whole token: its lanes carry QI Q heads, KI K heads and KI V
+// heads that all use the same E frequencies, so the sin/cos, their shuffles
+// and the token metadata are computed once per token.  The mbarrier wait is
+// bounded: on a timeout the warp raises KANI_FLAG_TIMEOUT, waits once more
+// (bounded) for the copies and returns.
 constexpr int kBulkTPS = 4;
-constexpr int kBulkStages = 4;
 constexpr long long kWaitCycles = 2000000000LL;  // ~1 s at the B200 clock
 
 __device__ __forceinline__ uint32_t smem_u32(const void* ptr) {
@@ -502,14 +504,16 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
                : "memory");
 }
 
+// One wait attempt; the thread may be suspended (up to the hint, in ns) until
+// the phase completes, so a waiting warp does not occupy issue slots.
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(bar), "r"(parity)
+      : "r"(bar), "r"(parity), "r"(1000000u)
       : "memory");
   return ok != 0;
 }
@@ -548,36 +552,29 @@ __device__ __forceinline__ void bulk_rows(uint32_t dst, const char* src, uint32_
 }
 
 template <typename T, bool NORM, bool TABLE, int QI, int KI>
-__global__ void __launch_bounds__(256)
-rope_bulk_kernel(RopeParams p, int log2l, int64_t n_groups, uint32_t stage_bytes, bool meta_bulk) {
+__global__ void __launch_bounds__(kBulkTPS * 32)
+rope_bulk_kernel(RopeParams p, int log2l, bool meta_bulk) {
   constexpr int E = VecN<T>::value;
   constexpr int ES = (int)sizeof(T);
-  extern __shared__ __align__(128) unsigned char ring[];
-  __shared__ __align__(8) uint64_t bars[kBulkStages];
+  extern __shared__ __align__(128) unsigned char stage[];
+  __shared__ __align__(8) uint64_t bar_storage;
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
   const uint32_t qrow = (uint32_t)(p.hq * p.d * ES);
   const uint32_t krow = (uint32_t)(p.hk * p.d * ES);
+  // stage layout: [Q rows][K rows][V rows][positions][slots][frame positions]
+  const uint32_t meta_off = kBulkTPS * (qrow + 2 * krow);
+  const uint32_t mb = kBulkTPS * 8;
+  const int64_t t0 = (int64_t)blockIdx.x * kBulkTPS;
+  const int cnt = (int)(p.n_tokens - t0 < kBulkTPS ? p.n_tokens - t0 : kBulkTPS);
+  const bool meta = meta_bulk && cnt == kBulkTPS;
+  const uint32_t bar = smem_u32(&bar_storage);
 
   if (tid == 0) {
-    for (int s = 0; s < kBulkStages; ++s) mbar_init(smem_u32(&bars[s]), 1);
+    mbar_init(bar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  __syncthreads();
-
-  // Stage layout: [Q rows][K rows][V rows][positions][slots][frame positions]
-  // (the last three: kBulkTPS int64 each, copied only for full groups when
-  // the arrays are 16-byte aligned; otherwise each warp loads its own).
-  const uint32_t meta_off = kBulkTPS * (qrow + 2 * krow);
-  // thread 0: fill stage s with token group g
-  auto issue = [&](int s, int64_t g) {
-    const int64_t t0 = g * kBulkTPS;
-    const int cnt = (int)(p.n_tokens - t0 < kBulkTPS ? p.n_tokens - t0 : kBulkTPS);
-    const bool meta = meta_bulk && cnt == kBulkTPS;
-    const uint32_t bar = smem_u32(&bars[s]);
-    const uint32_t base = smem_u32(ring + (size_t)s * stage_bytes);
-    const uint32_t mb = kBulkTPS * 8;
+    const uint32_t base = smem_u32(stage);
     const uint32_t meta_bytes = meta ? mb * (1u + (p.slots ? 1u : 0u) + (p.frame_pos ? 1u : 0u)) : 0u;
     mbar_expect_tx(bar, (uint32_t)cnt * (qrow + 2 * krow) + meta_bytes);
     if (meta) {
@@ -592,180 +589,120 @@ rope_bulk_kernel(RopeParams p, int log2l, int64_t n_groups, uint32_t stage_bytes
     bulk_rows(base + kBulkTPS * (qrow + krow),
               reinterpret_cast<const char*>(static_cast<const T*>(p.v) + t0 * p.vts), krow, p.vts * ES, cnt,
               bar);
-  };
-  if (tid == 0) {
-    for (int s = 0; s < kBulkStages; ++s) {
-      const int64_t g = blockIdx.x + (int64_t)s * gridDim.x;
-      if (g < n_groups) issue(s, g);
-    }
     if constexpr (TABLE) {
-      // each CTA pulls its share of the frame table into L2 (rows are 16-byte multiples)
-      const int64_t rows = p.table_rows;
-      const int64_t per = (rows + gridDim.x - 1) / gridDim.x;
+      // this CTA's share of the frame table goes to L2 while the rows stream in
+      const int64_t per = (p.table_rows + gridDim.x - 1) / gridDim.x;
       const int64_t r0 = (int64_t)blockIdx.x * per;
-      const int64_t r1 = r0 + per < rows ? r0 + per : rows;
+      const int64_t r1 = r0 + per < p.table_rows ? r0 + per : p.table_rows;
       if (r1 > r0)
         bulk_prefetch_l2(static_cast<const T*>(p.table) + r0 * p.d, (uint32_t)((r1 - r0) * p.d * ES));
     }
   }
+  __syncthreads();  // the barrier is initialised before anyone waits on it
+  if (warp >= cnt) return;  // warp 0 always stays, so the CTA outlives its copies
 
+  const int64_t t = t0 + warp;
   const int L = 1 << log2l;
   const int G = 32 >> log2l;
-  const int tl = warp >> 1;
-  const bool qrole = (warp & 1) == 0;
   const int hh = lane >> log2l;
   const int jj = lane & (L - 1);
   const int lo = jj * E, hi = (p.d >> 1) + jj * E;
-  const int nh = qrole ? p.hq : p.hk;
-  const T* nw = static_cast<const T*>(qrole ? p.qw : p.kw);
 
-  int64_t it = 0;
-  bool failed = false;
-  for (;; ++it) {
-    const int64_t g = blockIdx.x + it * gridDim.x;
-    if (g >= n_groups) break;  // uniform across the CTA
-    const int s = (int)(it % kBulkStages);
-    const uint32_t parity = (uint32_t)((it / kBulkStages) & 1);
-    const int64_t t = g * kBulkTPS + tl;
-    const bool tok_ok = t < p.n_tokens;  // warp-uniform
-    const bool meta_here = meta_bulk && (g + 1) * kBulkTPS <= p.n_tokens;
-    const bool ready = mbar_wait_bounded(smem_u32(&bars[s]), parity);
-    if (ready && tok_ok) {
-      const unsigned char* st = ring + (size_t)s * stage_bytes;
-      int64_t pos, slot, fp;
-      if (meta_here) {
-        const int64_t* mp = reinterpret_cast<const int64_t*>(st + meta_off);
-        pos = mp[tl];
-        slot = p.slots ? mp[kBulkTPS + tl] : (t - (t / p.seq_tokens) * p.seq_tokens);
-        fp = p.frame_pos ? mp[2 * kBulkTPS + tl] : pos;
-      } else {
-        pos = p.positions[t];
-        slot = p.slots ? p.slots[t] : (t - (t / p.seq_tokens) * p.seq_tokens);
-        fp = p.frame_pos ? p.frame_pos[t] : pos;
-      }
-      const TokenMeta m = token_meta_vals<TABLE>(p, t, slot, fp);
-      if (qrole && lane == 0) flag_token<TABLE>(p, m);
-      // the frame row (an L2 hit after the prefetch) overlaps the trig
-      uint4 plo = make_uint4(0, 0, 0, 0), phi = plo;
-      if constexpr (TABLE) {
-        if (m.frame_ok) {
-          const T* pr = static_cast<const T*>(p.table) + m.frame * p.d;
-          plo = ld16_ro(pr + lo);
-          phi = ld16_ro(pr + hi);
-        }
-      }
-      float cs[E], sn[E], pl[E], ph[E];
-      warp_cos_sin<T>(p.inv_freq, (float)pos, log2l, lane, cs, sn);
-      if constexpr (TABLE) {
-        unpack16<T>(plo, pl);
-        unpack16<T>(phi, ph);
-      }
-      if (qrole) {
-        const unsigned char* src = st + tl * qrow;
-        T* qdst = static_cast<T*>(p.q_out) + t * p.qots;
+  if (!mbar_wait_bounded(bar, 0)) {
+    if (lane == 0 && p.err != nullptr) atomicOr(p.err, KANI_FLAG_TIMEOUT);
+    mbar_wait_bounded(bar, 0);  // the copies target this CTA's shared memory
+    return;
+  }
+  int64_t pos, slot, fp;
+  if (meta) {
+    const int64_t* mp = reinterpret_cast<const int64_t*>(stage + meta_off);
+    pos = mp[warp];
+    slot = p.slots ? mp[kBulkTPS + warp] : (t - (t / p.seq_tokens) * p.seq_tokens);
+    fp = p.frame_pos ? mp[2 * kBulkTPS + warp] : pos;
+  } else {
+    pos = p.positions[t];
+    slot = p.slots ? p.slots[t] : (t - (t / p.seq_tokens) * p.seq_tokens);
+    fp = p.frame_pos ? p.frame_pos[t] : pos;
+  }
+  const TokenMeta m = token_meta_vals<TABLE>(p, t, slot, fp);
+  if (lane == 0) flag_token<TABLE>(p, m);
+  uint4 plo = make_uint4(0, 0, 0, 0), phi = plo;
+  if constexpr (TABLE) {
+    if (m.frame_ok) {
+      const T* pr = static_cast<const T*>(p.table) + m.frame * p.d;
+      plo = ld16_ro(pr + lo);
+      phi = ld16_ro(pr + hi);
+    }
+  }
+  float cs[E], sn[E], pl[E], ph[E];
+  warp_cos_sin<T>(p.inv_freq, (float)pos, log2l, lane, cs, sn);
+  if constexpr (TABLE) {
+    unpack16<T>(plo, pl);
+    unpack16<T>(phi, ph);
+  }
+  // Q heads
+  {
+    const T* src = reinterpret_cast<const T*>(stage + warp * qrow);
+    T* qdst = static_cast<T*>(p.q_out) + t * p.qots;
+    const T* nw = static_cast<const T*>(p.qw);
 #pragma unroll
-        for (int i = 0; i < QI; ++i) {
-          const int h = hh + i * G;
-          const bool live = h < nh;
-          uint4 xlo = make_uint4(0, 0, 0, 0), xhi = xlo;
-          if (live) {
-            const T* hs = reinterpret_cast<const T*>(src) + h * p.d;
-            xlo = *reinterpret_cast<const uint4*>(hs + lo);
-            xhi = *reinterpret_cast<const uint4*>(hs + hi);
-          }
-          rope_chunk_store<T, NORM, TABLE>(xlo, xhi, live, cs, sn, pl, ph, m.frame_ok, nw, lo, hi, log2l,
-                                           p.d, p.eps, qdst + (int64_t)h * p.qohs);
-        }
-      } else {
-        const unsigned char* ksrc = st + kBulkTPS * qrow + tl * krow;
-        const unsigned char* vsrc = st + kBulkTPS * (qrow + krow) + tl * krow;
-        T* kdst = static_cast<T*>(p.k_cache) + m.b * p.cbs + m.slot * p.css;
-        T* vdst = static_cast<T*>(p.v_cache) + m.b * p.cbs + m.slot * p.css;
+    for (int i = 0; i < QI; ++i) {
+      const int h = hh + i * G;
+      const bool live = h < p.hq;
+      uint4 xlo = make_uint4(0, 0, 0, 0), xhi = xlo;
+      if (live) {
+        xlo = *reinterpret_cast<const uint4*>(src + h * p.d + lo);
+        xhi = *reinterpret_cast<const uint4*>(src + h * p.d + hi);
+      }
+      rope_chunk_store<T, NORM, TABLE>(xlo, xhi, live, cs, sn, pl, ph, m.frame_ok, nw, lo, hi, log2l, p.d,
+                                       p.eps, qdst + (int64_t)h * p.qohs);
+    }
+  }
+  // K heads (rotated) and V heads (copied) into the cache slot
+  {
+    const T* ksrc = reinterpret_cast<const T*>(stage + kBulkTPS * qrow + warp * krow);
+    const T* vsrc = reinterpret_cast<const T*>(stage + kBulkTPS * (qrow + krow) + warp * krow);
+    T* kdst = static_cast<T*>(p.k_cache) + m.b * p.cbs + m.slot * p.css;
+    T* vdst = static_cast<T*>(p.v_cache) + m.b * p.cbs + m.slot * p.css;
+    const T* nw = static_cast<const T*>(p.kw);
 #pragma unroll
-        for (int i = 0; i < KI; ++i) {
-          const int h = hh + i * G;
-          const bool has = h < nh;
-          uint4 xlo = make_uint4(0, 0, 0, 0), xhi = xlo;
-          if (has) {
-            const T* hs = reinterpret_cast<const T*>(ksrc) + h * p.d;
-            xlo = *reinterpret_cast<const uint4*>(hs + lo);
-            xhi = *reinterpret_cast<const uint4*>(hs + hi);
-          }
-          rope_chunk_store<T, NORM, TABLE>(xlo, xhi, has && m.slot_ok, cs, sn, pl, ph, m.frame_ok, nw, lo,
-                                           hi, log2l, p.d, p.eps, kdst + (int64_t)h * p.chs);
-          if (has && m.slot_ok) {
-            const T* vs = reinterpret_cast<const T*>(vsrc) + h * p.d;
-            st16(vdst + (int64_t)h * p.chs + lo, *reinterpret_cast<const uint4*>(vs + lo));
-            st16(vdst + (int64_t)h * p.chs + hi, *reinterpret_cast<const uint4*>(vs + hi));
-          }
-        }
+    for (int i = 0; i < KI; ++i) {
+      const int h = hh + i * G;
+      const bool has = h < p.hk;
+      uint4 xlo = make_uint4(0, 0, 0, 0), xhi = xlo;
+      if (has) {
+        xlo = *reinterpret_cast<const uint4*>(ksrc + h * p.d + lo);
+        xhi = *reinterpret_cast<const uint4*>(ksrc + h * p.d + hi);
       }
-    }
-    failed = failed || !ready;
-    // every thread arrives: the stage is free again, and a timeout anywhere
-    // stops the whole CTA at the same iteration
-    if (__syncthreads_or(failed)) break;
-    if (tid == 0) {
-      const int64_t gn = g + (int64_t)kBulkStages * gridDim.x;
-      if (gn < n_groups) {
-        // order this CTA's shared-memory reads before the async-proxy refill
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        issue(s, gn);
+      rope_chunk_store<T, NORM, TABLE>(xlo, xhi, has && m.slot_ok, cs, sn, pl, ph, m.frame_ok, nw, lo, hi,
+                                       log2l, p.d, p.eps, kdst + (int64_t)h * p.chs);
+      if (has && m.slot_ok) {
+        st16(vdst + (int64_t)h * p.chs + lo, *reinterpret_cast<const uint4*>(vsrc + h * p.d + lo));
+        st16(vdst + (int64_t)h * p.chs + hi, *reinterpret_cast<const uint4*>(vsrc + h * p.d + hi));
       }
     }
   }
-  if (failed && tid == 0) {
-    if (p.err != nullptr) atomicOr(p.err, KANI_FLAG_TIMEOUT);
-    // copies issued for iterations it .. it+kBulkStages-1 were never consumed
-    for (int64_t j = it; j < it + kBulkStages; ++j) {
-      if (blockIdx.x + j * gridDim.x >= n_groups) break;
-      mbar_wait_bounded(smem_u32(&bars[j % kBulkStages]), (uint32_t)((j / kBulkStages) & 1));
-    }
-  }
-}
-
-// Per-device cached SM count (the one piece of state the library keeps).
-int sm_count() {
-  static int cached[64] = {0};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (cached[dev] == 0) {
-    int n = 0;
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-    cached[dev] = n;
-  }
-  return cached[dev];
 }
 
 template <typename T, bool NORM, bool TABLE, int QI, int KI>
 int launch_bulk(const RopeParams& p, int log2l, cudaStream_t s) {
   constexpr int ES = (int)sizeof(T);
-  const uint32_t row_bytes = (uint32_t)((p.hq + 2 * p.hk) * p.d * ES);
-  const uint32_t stage_bytes = ((kBulkTPS * row_bytes + 3 * kBulkTPS * 8 + 127u) / 128u) * 128u;
+  const size_t row_bytes = (size_t)(p.hq + 2 * p.hk) * p.d * ES;
+  const size_t smem = kBulkTPS * row_bytes + 3 * kBulkTPS * 8;
   const bool meta_bulk = aligned16(p.positions) && (p.slots == nullptr || aligned16(p.slots)) &&
                          (p.frame_pos == nullptr || aligned16(p.frame_pos));
-  const size_t smem = (size_t)kBulkStages * stage_bytes;
   auto kern = rope_bulk_kernel<T, NORM, TABLE, QI, KI>;
   static int smem_set[64] = {0};
-  static int per_sm[64] = {0};
   int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return KANI_ERR_UNSUPPORTED;
-  if (smem_set[dev] < (int)smem) {
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return KANI_ERR_UNSUPPORTED;
+  if (smem > 48 * 1024 && smem_set[dev] < (int)smem) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return launch_status();
     smem_set[dev] = (int)smem;
-    per_sm[dev] = 0;
   }
-  if (per_sm[dev] == 0) {
-    int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, 256, smem) != cudaSuccess || n <= 0) n = 1;
-    per_sm[dev] = n;
-  }
-  const int64_t n_groups = (p.n_tokens + kBulkTPS - 1) / kBulkTPS;
-  int64_t grid = (int64_t)sm_count() * per_sm[dev];
-  if (grid > n_groups) grid = n_groups;
-  kern<<<(unsigned)grid, 256, smem, s>>>(p, log2l, n_groups, stage_bytes, meta_bulk);
+  const int64_t grid = (p.n_tokens + kBulkTPS - 1) / kBulkTPS;
+  if (grid > 0x7fffffff) return KANI_ERR_UNSUPPORTED;
+  kern<<<(unsigned)grid, kBulkTPS * 32, smem, s>>>(p, log2l, meta_bulk);
   return launch_status();
 }
 
@@ -907,7 +844,7 @@ int launch_rope_t(const RopeParams& p, cudaStream_t s) {
       const bool rows16 = ((int64_t)p.hq * p.d * (int64_t)sizeof(T)) % 16 == 0 &&
                           ((int64_t)p.hk * p.d * (int64_t)sizeof(T)) % 16 == 0;
       const int64_t stage = (int64_t)kBulkTPS * (p.hq + 2 * p.hk) * p.d * (int64_t)sizeof(T) + 3 * kBulkTPS * 8;
-      if (rows16 && stage * kBulkStages <= 160 * 1024) {
+      if (rows16 && stage <= 200 * 1024) {
         if (p.hq <= 2 * G && p.hk <= G) return launch_bulk<T, NORM, TABLE, 2, 1>(p, log2l, s);
         if (p.hq <= 4 * G && p.hk <= 2 * G) return launch_bulk<T, NORM, TABLE, 4, 2>(p, log2l, s);
       }

@@ -499,3 +499,28 @@ def test_errors_raise_before_launch_on_gpu_tensors():
     with pytest.raises(ValueError):
         K.kv_cache_write(gpu(rnd((1, 8, 2, 64), 5)), gpu(rnd((1, 8, 1, 64), 5)), kc, kc.clone(),
                          torch.zeros(1, dtype=torch.long, device=DEV))
+
+
+def test_rope_kv_write_bulk_partial_group_and_unaligned_metadata():
+    """Long calls take the bulk-copy kernel: a token count that is not a
+    multiple of its 4-token groups, and position/slot arrays that are not
+    16-byte aligned (so they are loaded per warp instead of bulk-copied)."""
+    t = 1030
+    c = _config2_case(1000, t=t, s_len=2048, p0=17, norm=True)
+    q, kc, vc, eq, ekc, evc, flags = _run_both(c, t, 1)
+    assert flags == 0 and _lib.read_and_clear_errors(DEV) == 0
+    assert_rope_close(q, eq)
+    assert_rope_close(kc, ekc, 0.999)
+    assert torch.equal(vc.cpu(), evc)
+    # same call with the metadata arrays at an 8-byte offset
+    pos_buf = torch.zeros(t + 1, dtype=torch.long, device=DEV)
+    slot_buf = torch.zeros(t + 1, dtype=torch.long, device=DEV)
+    pos_buf[1:] = gpu(c["pos"])
+    slot_buf[1:] = gpu(c["slots"])
+    kc2, vc2 = gpu(c["kc"]), gpu(c["vc"])
+    q2 = K.fused_rope_kv_write(gpu(c["q"]).view(1, t, 16, 64), gpu(c["k"]).view(1, t, 8, 64),
+                               gpu(c["v"]).view(1, t, 8, 64), gpu(c["inv"]), pos_buf[1:], kc2, vc2,
+                               slot_buf[1:], frame_table=gpu(c["tab"]), q_norm_w=gpu(c["qw"]),
+                               k_norm_w=gpu(c["kw"]))
+    assert torch.equal(q2.cpu().reshape(q.shape), q.cpu())
+    assert torch.equal(kc2.cpu(), kc.cpu()) and torch.equal(vc2.cpu(), vc.cpu())

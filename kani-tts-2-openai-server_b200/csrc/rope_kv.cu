@@ -292,30 +292,76 @@ rope_vec_kernel(RopeParams p, int log2l, int ipt, int iptr, int tpb) {
 
 // ------------------------------------------------------ shared warp helpers
 
+// sin and cos of one fp32 angle with a shared argument reduction.
+// Method: Cody-Waite reduction by pi/2 (W. J. Cody and W. Waite, "Software
+// Manual for the Elementary Functions", 1980) in its fused-multiply-add form:
+// pi/2 = C1 + C2 + C3 with C1 = fp32(pi/2), C2 = fp32(pi/2 - C1),
+// C3 = fp32(pi/2 - C1 - C2); then the Taylor series of sin and cos on
+// [-pi/4, pi/4] (through x^11 and x^12; truncation below 2^-30), then the
+// quadrant swap and signs.  Measured against float64 sin/cos over
+// |x| <= 65536: <= 1.5 fp32 ulp.  Larger angles (not produced by the decode
+// positions of this model family) use sinf / cosf.
+__device__ __forceinline__ void sincos_reduced(float x, float* s_out, float* c_out) {
+  if (!(fabsf(x) <= 65536.0f)) {  // also catches NaN / inf
+    *s_out = sinf(x);
+    *c_out = cosf(x);
+    return;
+  }
+  const float n = rintf(x * 0.636619746685028076f);  // x * fp32(2/pi)
+  float r = fmaf(-n, 1.57079637050628662f, x);
+  r = fmaf(-n, -4.37113882867379300e-08f, r);
+  r = fmaf(-n, -1.71512451000588189e-15f, r);
+  const float r2 = r * r;
+  // sin r = r (1 - r2/3! + r2^2/5! - r2^3/7! + r2^4/9! - r2^5/11!)
+  float ps = fmaf(r2, -2.5052108385441720e-8f, 2.7557319223985891e-6f);
+  ps = fmaf(r2, ps, -1.9841269841269841e-4f);
+  ps = fmaf(r2, ps, 8.3333333333333333e-3f);
+  ps = fmaf(r2, ps, -1.6666666666666667e-1f);
+  const float sr = fmaf(r * r2, ps, r);
+  // cos r = 1 - r2/2! + r2^2/4! - r2^3/6! + r2^4/8! - r2^5/10! + r2^6/12!
+  float pc = fmaf(r2, 2.0876756987868099e-9f, -2.7557319223985891e-7f);
+  pc = fmaf(r2, pc, 2.4801587301587302e-5f);
+  pc = fmaf(r2, pc, -1.3888888888888889e-3f);
+  pc = fmaf(r2, pc, 4.1666666666666667e-2f);
+  pc = fmaf(r2, pc, -0.5f);
+  const float cr = fmaf(r2, pc, 1.0f);
+  const int q = static_cast<int>(n) & 3;
+  const float sv = (q & 1) ? cr : sr;
+  const float cv = (q & 1) ? sr : cr;
+  *s_out = (q & 2) ? -sv : sv;
+  *c_out = ((q + 1) & 2) ? -cv : cv;
+}
+
 // cos/sin (rounded to T) of frequencies jj*E .. jj*E+E-1 at angle position
 // posf.  Lane = hh * L + jj: the 32/L lanes that share chunk jj compute the E
-// values between them (one cosf/sinf pair each when 32/L >= E) and exchange
-// them with shuffles.  Every lane of the warp must call this.
-template <typename T>
+// values between them (one sincos each when 32/L >= E) and exchange them
+// with shuffles.  Every lane of the warp must call this.  LOG2L_CT >= 0 fixes
+// the lane geometry at compile time (constant shuffle sources); -1 reads it
+// from log2l.
+template <typename T, int LOG2L_CT>
 __device__ __forceinline__ void warp_cos_sin(const float* __restrict__ inv_freq, float posf,
-                                             int log2l, int lane, float* cs, float* sn) {
+                                             int log2l_rt, int lane, float* cs, float* sn) {
   constexpr int E = VecN<T>::value;
+  const int log2l = LOG2L_CT >= 0 ? LOG2L_CT : log2l_rt;
   const int log2g = 5 - log2l;
   const int G = 1 << log2g;
   const int hh = lane >> log2l;
   const int jj = lane & ((1 << log2l) - 1);
   const int rounds = (E + G - 1) >> log2g;
-  for (int r = 0; r < rounds; ++r) {
+#pragma unroll
+  for (int r = 0; r < (LOG2L_CT >= 0 ? ((E + (32 >> LOG2L_CT) - 1) / (32 >> LOG2L_CT)) : E); ++r) {
+    if (LOG2L_CT < 0 && r >= rounds) break;
     const int e_own = r * G + hh;
     float cv = 0.f, sv = 0.f;
     if (e_own < E) {
-      const float ang = __fmul_rn(__ldg(inv_freq + jj * E + e_own), posf);
-      cv = round_to<T>(cosf(ang));
-      sv = round_to<T>(sinf(ang));
+      float sr, cr;
+      sincos_reduced(__fmul_rn(__ldg(inv_freq + jj * E + e_own), posf), &sr, &cr);
+      cv = round_to<T>(cr);
+      sv = round_to<T>(sr);
     }
 #pragma unroll
     for (int e = 0; e < E; ++e) {
-      if ((e >> log2g) == r) {  // uniform across the warp
+      if ((e >> log2g) == r) {  // uniform across the warp (constant with LOG2L_CT)
         const int src = ((e & (G - 1)) << log2l) | jj;
         cs[e] = __shfl_sync(0xffffffffu, cv, src);
         sn[e] = __shfl_sync(0xffffffffu, sv, src);
@@ -442,7 +488,7 @@ rope_token_kernel(RopeParams p, int log2l) {
   }
   // 3. cos/sin
   float cs[E], sn[E];
-  warp_cos_sin<T>(p.inv_freq, (float)p.positions[t], log2l, lane, cs, sn);
+  warp_cos_sin<T, -1>(p.inv_freq, (float)p.positions[t], log2l, lane, cs, sn);
   float pl[E], ph[E];
   if constexpr (TABLE) {
     unpack16<T>(plo, pl);
@@ -551,9 +597,10 @@ __device__ __forceinline__ void bulk_rows(uint32_t dst, const char* src, uint32_
   }
 }
 
-template <typename T, bool NORM, bool TABLE, int QI, int KI>
+template <typename T, bool NORM, bool TABLE, int QI, int KI, int LOG2L_CT>
 __global__ void __launch_bounds__(kBulkTPS * 32)
-rope_bulk_kernel(RopeParams p, int log2l, bool meta_bulk) {
+rope_bulk_kernel(RopeParams p, int log2l_rt, bool meta_bulk) {
+  const int log2l = LOG2L_CT >= 0 ? LOG2L_CT : log2l_rt;
   constexpr int E = VecN<T>::value;
   constexpr int ES = (int)sizeof(T);
   extern __shared__ __align__(128) unsigned char stage[];
@@ -635,63 +682,66 @@ rope_bulk_kernel(RopeParams p, int log2l, bool meta_bulk) {
     }
   }
   float cs[E], sn[E], pl[E], ph[E];
-  warp_cos_sin<T>(p.inv_freq, (float)pos, log2l, lane, cs, sn);
+  warp_cos_sin<T, LOG2L_CT>(p.inv_freq, (float)pos, log2l, lane, cs, sn);
   if constexpr (TABLE) {
     unpack16<T>(plo, pl);
     unpack16<T>(phi, ph);
   }
+  // per-lane bases (head hh); head hh + i*G is a constant stride further
+  const int hstride = G * p.d;  // elements between a lane's heads in shared memory
   // Q heads
   {
-    const T* src = reinterpret_cast<const T*>(stage + warp * qrow);
-    T* qdst = static_cast<T*>(p.q_out) + t * p.qots;
+    const T* src = reinterpret_cast<const T*>(stage + warp * qrow) + hh * p.d;
+    T* qdst = static_cast<T*>(p.q_out) + t * p.qots + (int64_t)hh * p.qohs;
+    const int64_t qstep = (int64_t)G * p.qohs;
     const T* nw = static_cast<const T*>(p.qw);
 #pragma unroll
     for (int i = 0; i < QI; ++i) {
-      const int h = hh + i * G;
-      const bool live = h < p.hq;
+      const bool live = hh + i * G < p.hq;
       uint4 xlo = make_uint4(0, 0, 0, 0), xhi = xlo;
       if (live) {
-        xlo = *reinterpret_cast<const uint4*>(src + h * p.d + lo);
-        xhi = *reinterpret_cast<const uint4*>(src + h * p.d + hi);
+        xlo = *reinterpret_cast<const uint4*>(src + i * hstride + lo);
+        xhi = *reinterpret_cast<const uint4*>(src + i * hstride + hi);
       }
       rope_chunk_store<T, NORM, TABLE>(xlo, xhi, live, cs, sn, pl, ph, m.frame_ok, nw, lo, hi, log2l, p.d,
-                                       p.eps, qdst + (int64_t)h * p.qohs);
+                                       p.eps, qdst + i * qstep);
     }
   }
   // K heads (rotated) and V heads (copied) into the cache slot
   {
-    const T* ksrc = reinterpret_cast<const T*>(stage + kBulkTPS * qrow + warp * krow);
-    const T* vsrc = reinterpret_cast<const T*>(stage + kBulkTPS * (qrow + krow) + warp * krow);
-    T* kdst = static_cast<T*>(p.k_cache) + m.b * p.cbs + m.slot * p.css;
-    T* vdst = static_cast<T*>(p.v_cache) + m.b * p.cbs + m.slot * p.css;
+    const T* ksrc = reinterpret_cast<const T*>(stage + kBulkTPS * qrow + warp * krow) + hh * p.d;
+    const T* vsrc = reinterpret_cast<const T*>(stage + kBulkTPS * (qrow + krow) + warp * krow) + hh * p.d;
+    const int64_t off = m.b * p.cbs + m.slot * p.css + (int64_t)hh * p.chs;
+    T* kdst = static_cast<T*>(p.k_cache) + off;
+    T* vdst = static_cast<T*>(p.v_cache) + off;
+    const int64_t cstep = (int64_t)G * p.chs;
     const T* nw = static_cast<const T*>(p.kw);
 #pragma unroll
     for (int i = 0; i < KI; ++i) {
-      const int h = hh + i * G;
-      const bool has = h < p.hk;
+      const bool has = hh + i * G < p.hk;
       uint4 xlo = make_uint4(0, 0, 0, 0), xhi = xlo;
       if (has) {
-        xlo = *reinterpret_cast<const uint4*>(ksrc + h * p.d + lo);
-        xhi = *reinterpret_cast<const uint4*>(ksrc + h * p.d + hi);
+        xlo = *reinterpret_cast<const uint4*>(ksrc + i * hstride + lo);
+        xhi = *reinterpret_cast<const uint4*>(ksrc + i * hstride + hi);
       }
       rope_chunk_store<T, NORM, TABLE>(xlo, xhi, has && m.slot_ok, cs, sn, pl, ph, m.frame_ok, nw, lo, hi,
-                                       log2l, p.d, p.eps, kdst + (int64_t)h * p.chs);
+                                       log2l, p.d, p.eps, kdst + i * cstep);
       if (has && m.slot_ok) {
-        st16(vdst + (int64_t)h * p.chs + lo, *reinterpret_cast<const uint4*>(vsrc + h * p.d + lo));
-        st16(vdst + (int64_t)h * p.chs + hi, *reinterpret_cast<const uint4*>(vsrc + h * p.d + hi));
+        st16(vdst + i * cstep + lo, *reinterpret_cast<const uint4*>(vsrc + i * hstride + lo));
+        st16(vdst + i * cstep + hi, *reinterpret_cast<const uint4*>(vsrc + i * hstride + hi));
       }
     }
   }
 }
 
-template <typename T, bool NORM, bool TABLE, int QI, int KI>
+template <typename T, bool NORM, bool TABLE, int QI, int KI, int LOG2L_CT>
 int launch_bulk(const RopeParams& p, int log2l, cudaStream_t s) {
   constexpr int ES = (int)sizeof(T);
   const size_t row_bytes = (size_t)(p.hq + 2 * p.hk) * p.d * ES;
   const size_t smem = kBulkTPS * row_bytes + 3 * kBulkTPS * 8;
   const bool meta_bulk = aligned16(p.positions) && (p.slots == nullptr || aligned16(p.slots)) &&
                          (p.frame_pos == nullptr || aligned16(p.frame_pos));
-  auto kern = rope_bulk_kernel<T, NORM, TABLE, QI, KI>;
+  auto kern = rope_bulk_kernel<T, NORM, TABLE, QI, KI, LOG2L_CT>;
   static int smem_set[64] = {0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return KANI_ERR_UNSUPPORTED;
@@ -845,8 +895,13 @@ int launch_rope_t(const RopeParams& p, cudaStream_t s) {
                           ((int64_t)p.hk * p.d * (int64_t)sizeof(T)) % 16 == 0;
       const int64_t stage = (int64_t)kBulkTPS * (p.hq + 2 * p.hk) * p.d * (int64_t)sizeof(T) + 3 * kBulkTPS * 8;
       if (rows16 && stage <= 200 * 1024) {
-        if (p.hq <= 2 * G && p.hk <= G) return launch_bulk<T, NORM, TABLE, 2, 1>(p, log2l, s);
-        if (p.hq <= 4 * G && p.hk <= 2 * G) return launch_bulk<T, NORM, TABLE, 4, 2>(p, log2l, s);
+        // the common geometry (16-bit types, D = 64 -> 4 lanes per head) is
+        // compiled with constant shuffle sources
+        if (p.hq <= 2 * G && p.hk <= G) {
+          if (sizeof(T) == 2 && log2l == 2) return launch_bulk<T, NORM, TABLE, 2, 1, 2>(p, log2l, s);
+          return launch_bulk<T, NORM, TABLE, 2, 1, -1>(p, log2l, s);
+        }
+        if (p.hq <= 4 * G && p.hk <= 2 * G) return launch_bulk<T, NORM, TABLE, 4, 2, -1>(p, log2l, s);
       }
     }
     // two-warps-per-token kernel: needs V, Q/K/V present and the heads to fit

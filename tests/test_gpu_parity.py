@@ -524,3 +524,26 @@ def test_rope_kv_write_bulk_partial_group_and_unaligned_metadata():
                                k_norm_w=gpu(c["kw"]))
     assert torch.equal(q2.cpu().reshape(q.shape), q.cpu())
     assert torch.equal(kc2.cpu(), kc.cpu()) and torch.equal(vc2.cpu(), vc.cpu())
+
+
+@pytest.mark.parametrize("t", [64, 65536])
+def test_in_kernel_cos_sin_match_cuda_math(t):
+    """The kernel's shared-reduction sin/cos, read back through RoPE of a unit
+    vector (x = [1 ... 1 | 0 ... 0] gives y = [cos | sin]), against CUDA's own
+    cosf/sinf (torch on the GPU) of the same fp32 angles, both rounded to
+    bf16: at most 1 ULP apart and almost always identical."""
+    d = 64
+    inv = gpu(P.learnable_inv_freq(d, 1e6, 0.0))
+    pos = torch.arange(t, dtype=torch.long, device=DEV)
+    q = torch.zeros(1, t, 1, d, dtype=torch.bfloat16, device=DEV)
+    q[..., : d // 2] = 1.0
+    k, v = q.clone(), q.clone()
+    kc = torch.zeros(1, 1, t, d, dtype=torch.bfloat16, device=DEV)
+    vc = torch.zeros_like(kc)
+    y = K.fused_rope_kv_write(q, k, v, inv, pos, kc, vc, pos).reshape(t, d)
+    ang = inv[None, :] * pos.float()[:, None]            # fp32 angles, as the reference forms them
+    ref_c, ref_s = ang.cos().to(torch.bfloat16), ang.sin().to(torch.bfloat16)
+    for got, ref in ((y[:, : d // 2], ref_c), (y[:, d // 2:], ref_s)):
+        dist = ulp(got, ref)
+        assert int(dist.max()) <= 1
+        assert float((dist != 0).float().mean()) < 1e-4

@@ -373,12 +373,15 @@ __device__ __forceinline__ void warp_cos_sin(const float* __restrict__ inv_freq,
 // One lane's two chunks (elements [lo, lo+E) and [hi, hi+E)) of one head:
 // optional RMSNorm (an L-lane shuffle tree over the head, so every lane of
 // the warp must call this, live or not), rotate-half, optional frame term,
-// one rounding, store at dst + lo / dst + hi.
+// one rounding, store at dst + lo / dst + hi.  The arithmetic runs on
+// sm_100's paired fp32 units (__fmul2_rn / __fadd2_rn: two independent
+// round-to-nearest operations per instruction, bit-identical to the scalar
+// form).  nsn holds -sin.
 template <typename T, bool NORM, bool TABLE>
 __device__ __forceinline__ void rope_chunk_store(uint4 xlo, uint4 xhi, bool live, const float* cs,
-                                                 const float* sn, const float* pl, const float* ph,
-                                                 bool frame_ok, const T* nw, int lo, int hi, int log2l,
-                                                 int d, float eps, T* dst) {
+                                                 const float* nsn, const float* sn, const float* pl,
+                                                 const float* ph, bool frame_ok, const T* nw, int lo,
+                                                 int hi, int log2l, int d, float eps, T* dst) {
   constexpr int E = VecN<T>::value;
   float a[E], b[E];
   unpack16<T>(xlo, a);
@@ -398,28 +401,39 @@ __device__ __forceinline__ void rope_chunk_store(uint4 xlo, uint4 xhi, bool live
       unpack16<T>(ld16_ro(nw + lo), wl);
       unpack16<T>(ld16_ro(nw + hi), wh);
       const float r = rrms_of(ss, d, eps);
+      const float2 r2 = make_float2(r, r);
 #pragma unroll
-      for (int e = 0; e < E; ++e) {
-        a[e] = round_to<T>(__fmul_rn(__fmul_rn(a[e], r), wl[e]));
-        b[e] = round_to<T>(__fmul_rn(__fmul_rn(b[e], r), wh[e]));
+      for (int e = 0; e < E; e += 2) {
+        const float2 na = __fmul2_rn(__fmul2_rn(make_float2(a[e], a[e + 1]), r2), make_float2(wl[e], wl[e + 1]));
+        const float2 nb = __fmul2_rn(__fmul2_rn(make_float2(b[e], b[e + 1]), r2), make_float2(wh[e], wh[e + 1]));
+        a[e] = round_to<T>(na.x);
+        a[e + 1] = round_to<T>(na.y);
+        b[e] = round_to<T>(nb.x);
+        b[e + 1] = round_to<T>(nb.y);
       }
     }
   }
   if (!live) return;
   float ylo[E], yhi[E];
 #pragma unroll
-  for (int e = 0; e < E; ++e) {
-    ylo[e] = __fadd_rn(__fmul_rn(a[e], cs[e]), __fmul_rn(-b[e], sn[e]));
-    yhi[e] = __fadd_rn(__fmul_rn(b[e], cs[e]), __fmul_rn(a[e], sn[e]));
-  }
-  if constexpr (TABLE) {
-    if (frame_ok) {
-#pragma unroll
-      for (int e = 0; e < E; ++e) {
-        ylo[e] = __fadd_rn(ylo[e], pl[e]);
-        yhi[e] = __fadd_rn(yhi[e], ph[e]);
+  for (int e = 0; e < E; e += 2) {
+    const float2 a2 = make_float2(a[e], a[e + 1]);
+    const float2 b2 = make_float2(b[e], b[e + 1]);
+    const float2 c2 = make_float2(cs[e], cs[e + 1]);
+    const float2 s2 = make_float2(sn[e], sn[e + 1]);
+    const float2 n2 = make_float2(nsn[e], nsn[e + 1]);
+    float2 l2 = __fadd2_rn(__fmul2_rn(a2, c2), __fmul2_rn(b2, n2));  // a cos - b sin
+    float2 h2 = __fadd2_rn(__fmul2_rn(b2, c2), __fmul2_rn(a2, s2));  // b cos + a sin
+    if constexpr (TABLE) {
+      if (frame_ok) {
+        l2 = __fadd2_rn(l2, make_float2(pl[e], pl[e + 1]));
+        h2 = __fadd2_rn(h2, make_float2(ph[e], ph[e + 1]));
       }
     }
+    ylo[e] = l2.x;
+    ylo[e + 1] = l2.y;
+    yhi[e] = h2.x;
+    yhi[e + 1] = h2.y;
   }
   st16(dst + lo, pack16<T>(ylo));
   st16(dst + hi, pack16<T>(yhi));
@@ -489,6 +503,9 @@ rope_token_kernel(RopeParams p, int log2l) {
   // 3. cos/sin
   float cs[E], sn[E];
   warp_cos_sin<T, -1>(p.inv_freq, (float)p.positions[t], log2l, lane, cs, sn);
+  float nsn[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) nsn[e] = -sn[e];
   float pl[E], ph[E];
   if constexpr (TABLE) {
     unpack16<T>(plo, pl);
@@ -505,7 +522,7 @@ rope_token_kernel(RopeParams p, int log2l) {
     const int h = hh + i * G;
     const bool live = h < nh && (qrole || m.slot_ok);
     T* dst = qrole ? qdst + (int64_t)h * p.qohs : kdst + (int64_t)h * p.chs;
-    rope_chunk_store<T, NORM, TABLE>(xlo[i], xhi[i], live, cs, sn, pl, ph, m.frame_ok, nw, lo, hi,
+    rope_chunk_store<T, NORM, TABLE>(xlo[i], xhi[i], live, cs, nsn, sn, pl, ph, m.frame_ok, nw, lo, hi,
                                      log2l, p.d, p.eps, dst);
   }
   if (!qrole && m.slot_ok) {
@@ -683,6 +700,9 @@ rope_bulk_kernel(RopeParams p, int log2l_rt, bool meta_bulk) {
   }
   float cs[E], sn[E], pl[E], ph[E];
   warp_cos_sin<T, LOG2L_CT>(p.inv_freq, (float)pos, log2l, lane, cs, sn);
+  float nsn[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) nsn[e] = -sn[e];
   if constexpr (TABLE) {
     unpack16<T>(plo, pl);
     unpack16<T>(phi, ph);
@@ -703,7 +723,7 @@ rope_bulk_kernel(RopeParams p, int log2l_rt, bool meta_bulk) {
         xlo = *reinterpret_cast<const uint4*>(src + i * hstride + lo);
         xhi = *reinterpret_cast<const uint4*>(src + i * hstride + hi);
       }
-      rope_chunk_store<T, NORM, TABLE>(xlo, xhi, live, cs, sn, pl, ph, m.frame_ok, nw, lo, hi, log2l, p.d,
+      rope_chunk_store<T, NORM, TABLE>(xlo, xhi, live, cs, nsn, sn, pl, ph, m.frame_ok, nw, lo, hi, log2l, p.d,
                                        p.eps, qdst + i * qstep);
     }
   }
@@ -724,7 +744,7 @@ rope_bulk_kernel(RopeParams p, int log2l_rt, bool meta_bulk) {
         xlo = *reinterpret_cast<const uint4*>(ksrc + i * hstride + lo);
         xhi = *reinterpret_cast<const uint4*>(ksrc + i * hstride + hi);
       }
-      rope_chunk_store<T, NORM, TABLE>(xlo, xhi, has && m.slot_ok, cs, sn, pl, ph, m.frame_ok, nw, lo, hi,
+      rope_chunk_store<T, NORM, TABLE>(xlo, xhi, has && m.slot_ok, cs, nsn, sn, pl, ph, m.frame_ok, nw, lo, hi,
                                        log2l, p.d, p.eps, kdst + i * cstep);
       if (has && m.slot_ok) {
         st16(vdst + i * cstep + lo, *reinterpret_cast<const uint4*>(vsrc + i * hstride + lo));

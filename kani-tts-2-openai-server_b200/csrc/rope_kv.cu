@@ -337,10 +337,37 @@ __device__ __forceinline__ void sincos_reduced(float x, float* s_out, float* c_o
 // values between them (one sincos each when 32/L >= E) and exchange them
 // with shuffles.  Every lane of the warp must call this.  LOG2L_CT >= 0 fixes
 // the lane geometry at compile time (constant shuffle sources); -1 reads it
-// from log2l.
+// from log2l.  `own_freq` holds the lane's frequencies for each round
+// (lane_freqs below), loaded ahead of time so no global load sits on the
+// critical path.
 template <typename T, int LOG2L_CT>
-__device__ __forceinline__ void warp_cos_sin(const float* __restrict__ inv_freq, float posf,
-                                             int log2l_rt, int lane, float* cs, float* sn) {
+struct LaneFreqs {
+  static constexpr int E = VecN<T>::value;
+  static constexpr int R = LOG2L_CT >= 0 ? (E + (32 >> LOG2L_CT) - 1) / (32 >> LOG2L_CT) : E;
+  float f[R];
+};
+
+template <typename T, int LOG2L_CT>
+__device__ __forceinline__ LaneFreqs<T, LOG2L_CT> lane_freqs(const float* __restrict__ inv_freq, int log2l_rt,
+                                                             int lane) {
+  constexpr int E = VecN<T>::value;
+  LaneFreqs<T, LOG2L_CT> lf;
+  const int log2l = LOG2L_CT >= 0 ? LOG2L_CT : log2l_rt;
+  const int log2g = 5 - log2l;
+  const int G = 1 << log2g;
+  const int hh = lane >> log2l;
+  const int jj = lane & ((1 << log2l) - 1);
+#pragma unroll
+  for (int r = 0; r < LaneFreqs<T, LOG2L_CT>::R; ++r) {
+    const int e_own = r * G + hh;
+    lf.f[r] = e_own < E ? __ldg(inv_freq + jj * E + e_own) : 0.f;
+  }
+  return lf;
+}
+
+template <typename T, int LOG2L_CT>
+__device__ __forceinline__ void warp_cos_sin(const LaneFreqs<T, LOG2L_CT>& lf, float posf, int log2l_rt,
+                                             int lane, float* cs, float* sn) {
   constexpr int E = VecN<T>::value;
   const int log2l = LOG2L_CT >= 0 ? LOG2L_CT : log2l_rt;
   const int log2g = 5 - log2l;
@@ -349,13 +376,12 @@ __device__ __forceinline__ void warp_cos_sin(const float* __restrict__ inv_freq,
   const int jj = lane & ((1 << log2l) - 1);
   const int rounds = (E + G - 1) >> log2g;
 #pragma unroll
-  for (int r = 0; r < (LOG2L_CT >= 0 ? ((E + (32 >> LOG2L_CT) - 1) / (32 >> LOG2L_CT)) : E); ++r) {
+  for (int r = 0; r < LaneFreqs<T, LOG2L_CT>::R; ++r) {
     if (LOG2L_CT < 0 && r >= rounds) break;
-    const int e_own = r * G + hh;
     float cv = 0.f, sv = 0.f;
-    if (e_own < E) {
+    if (r * G + hh < E) {
       float sr, cr;
-      sincos_reduced(__fmul_rn(__ldg(inv_freq + jj * E + e_own), posf), &sr, &cr);
+      sincos_reduced(__fmul_rn(lf.f[r], posf), &sr, &cr);
       cv = round_to<T>(cr);
       sv = round_to<T>(sr);
     }
@@ -502,7 +528,8 @@ rope_token_kernel(RopeParams p, int log2l) {
   }
   // 3. cos/sin
   float cs[E], sn[E];
-  warp_cos_sin<T, -1>(p.inv_freq, (float)p.positions[t], log2l, lane, cs, sn);
+  warp_cos_sin<T, -1>(lane_freqs<T, -1>(p.inv_freq, log2l, lane), (float)p.positions[t], log2l, lane, cs,
+                      sn);
   float nsn[E];
 #pragma unroll
   for (int e = 0; e < E; ++e) nsn[e] = -sn[e];
@@ -541,11 +568,11 @@ rope_token_kernel(RopeParams p, int log2l) {
 // -------------------------------------------------------------- bulk kernel
 // Long calls (prefill-sized token counts).  One CTA of kBulkTPS warps per
 // group of kBulkTPS tokens; the hardware block scheduler balances the groups
-// over the SMs.  Thread 0 brings the group's Q, K and V rows (and, for a full
-// group with 16-byte aligned arrays, its positions / slots / frame positions)
-// into shared memory with TMA bulk copies (cp.async.bulk, completion on one
-// mbarrier, no multicast) and pulls the CTA's share of the frame table into
-// L2; shared memory, not registers, holds the bytes in flight.  Each warp
+// over the SMs.  Thread 0 brings the group's Q, K and V rows into shared
+// memory with TMA bulk copies (cp.async.bulk, completion on one mbarrier, no
+// multicast) and pulls the CTA's share of the frame table into L2; shared
+// memory, not registers, holds the bytes in flight, and each warp fetches
+// its token's position, slot and frame row while the rows stream in.  Each warp
 // then owns one whole token: its lanes carry QI Q heads, KI K heads and KI V
 // heads that all use the same E frequencies, so the sin/cos, their shuffles
 // and the token metadata are computed once per token.  The mbarrier wait is
@@ -616,7 +643,7 @@ __device__ __forceinline__ void bulk_rows(uint32_t dst, const char* src, uint32_
 
 template <typename T, bool NORM, bool TABLE, int QI, int KI, int LOG2L_CT>
 __global__ void __launch_bounds__(kBulkTPS * 32)
-rope_bulk_kernel(RopeParams p, int log2l_rt, bool meta_bulk) {
+rope_bulk_kernel(RopeParams p, int log2l_rt) {
   const int log2l = LOG2L_CT >= 0 ? LOG2L_CT : log2l_rt;
   constexpr int E = VecN<T>::value;
   constexpr int ES = (int)sizeof(T);
@@ -627,25 +654,16 @@ rope_bulk_kernel(RopeParams p, int log2l_rt, bool meta_bulk) {
   const int lane = tid & 31;
   const uint32_t qrow = (uint32_t)(p.hq * p.d * ES);
   const uint32_t krow = (uint32_t)(p.hk * p.d * ES);
-  // stage layout: [Q rows][K rows][V rows][positions][slots][frame positions]
-  const uint32_t meta_off = kBulkTPS * (qrow + 2 * krow);
-  const uint32_t mb = kBulkTPS * 8;
+  // stage layout: [Q rows][K rows][V rows]
   const int64_t t0 = (int64_t)blockIdx.x * kBulkTPS;
   const int cnt = (int)(p.n_tokens - t0 < kBulkTPS ? p.n_tokens - t0 : kBulkTPS);
-  const bool meta = meta_bulk && cnt == kBulkTPS;
   const uint32_t bar = smem_u32(&bar_storage);
 
   if (tid == 0) {
     mbar_init(bar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     const uint32_t base = smem_u32(stage);
-    const uint32_t meta_bytes = meta ? mb * (1u + (p.slots ? 1u : 0u) + (p.frame_pos ? 1u : 0u)) : 0u;
-    mbar_expect_tx(bar, (uint32_t)cnt * (qrow + 2 * krow) + meta_bytes);
-    if (meta) {
-      bulk_g2s(base + meta_off, p.positions + t0, mb, bar);
-      if (p.slots) bulk_g2s(base + meta_off + mb, p.slots + t0, mb, bar);
-      if (p.frame_pos) bulk_g2s(base + meta_off + 2 * mb, p.frame_pos + t0, mb, bar);
-    }
+    mbar_expect_tx(bar, (uint32_t)cnt * (qrow + 2 * krow));
     bulk_rows(base, reinterpret_cast<const char*>(static_cast<const T*>(p.q) + t0 * p.qts), qrow,
               p.qts * ES, cnt, bar);
     bulk_rows(base + kBulkTPS * qrow, reinterpret_cast<const char*>(static_cast<const T*>(p.k) + t0 * p.kts),
@@ -672,24 +690,15 @@ rope_bulk_kernel(RopeParams p, int log2l_rt, bool meta_bulk) {
   const int jj = lane & (L - 1);
   const int lo = jj * E, hi = (p.d >> 1) + jj * E;
 
-  if (!mbar_wait_bounded(bar, 0)) {
-    if (lane == 0 && p.err != nullptr) atomicOr(p.err, KANI_FLAG_TIMEOUT);
-    mbar_wait_bounded(bar, 0);  // the copies target this CTA's shared memory
-    return;
-  }
-  int64_t pos, slot, fp;
-  if (meta) {
-    const int64_t* mp = reinterpret_cast<const int64_t*>(stage + meta_off);
-    pos = mp[warp];
-    slot = p.slots ? mp[kBulkTPS + warp] : (t - (t / p.seq_tokens) * p.seq_tokens);
-    fp = p.frame_pos ? mp[2 * kBulkTPS + warp] : pos;
-  } else {
-    pos = p.positions[t];
-    slot = p.slots ? p.slots[t] : (t - (t / p.seq_tokens) * p.seq_tokens);
-    fp = p.frame_pos ? p.frame_pos[t] : pos;
-  }
+  // Everything that does not need the staged rows is fetched while they
+  // stream in: the lane's frequencies, the token's position / slot / frame
+  // and the frame-table row.
+  const LaneFreqs<T, LOG2L_CT> lf = lane_freqs<T, LOG2L_CT>(p.inv_freq, log2l, lane);
+  const int64_t pos = p.positions[t];
+  const int64_t slot = p.slots ? p.slots[t]
+                               : (p.seq_tokens == 1 ? 0 : t - (t / p.seq_tokens) * p.seq_tokens);
+  const int64_t fp = p.frame_pos ? p.frame_pos[t] : pos;
   const TokenMeta m = token_meta_vals<TABLE>(p, t, slot, fp);
-  if (lane == 0) flag_token<TABLE>(p, m);
   uint4 plo = make_uint4(0, 0, 0, 0), phi = plo;
   if constexpr (TABLE) {
     if (m.frame_ok) {
@@ -698,8 +707,15 @@ rope_bulk_kernel(RopeParams p, int log2l_rt, bool meta_bulk) {
       phi = ld16_ro(pr + hi);
     }
   }
+
+  if (!mbar_wait_bounded(bar, 0)) {
+    if (lane == 0 && p.err != nullptr) atomicOr(p.err, KANI_FLAG_TIMEOUT);
+    mbar_wait_bounded(bar, 0);  // the copies target this CTA's shared memory
+    return;
+  }
+  if (lane == 0) flag_token<TABLE>(p, m);
   float cs[E], sn[E], pl[E], ph[E];
-  warp_cos_sin<T, LOG2L_CT>(p.inv_freq, (float)pos, log2l, lane, cs, sn);
+  warp_cos_sin<T, LOG2L_CT>(lf, (float)pos, log2l, lane, cs, sn);
   float nsn[E];
 #pragma unroll
   for (int e = 0; e < E; ++e) nsn[e] = -sn[e];
@@ -758,9 +774,7 @@ template <typename T, bool NORM, bool TABLE, int QI, int KI, int LOG2L_CT>
 int launch_bulk(const RopeParams& p, int log2l, cudaStream_t s) {
   constexpr int ES = (int)sizeof(T);
   const size_t row_bytes = (size_t)(p.hq + 2 * p.hk) * p.d * ES;
-  const size_t smem = kBulkTPS * row_bytes + 3 * kBulkTPS * 8;
-  const bool meta_bulk = aligned16(p.positions) && (p.slots == nullptr || aligned16(p.slots)) &&
-                         (p.frame_pos == nullptr || aligned16(p.frame_pos));
+  const size_t smem = kBulkTPS * row_bytes;
   auto kern = rope_bulk_kernel<T, NORM, TABLE, QI, KI, LOG2L_CT>;
   static int smem_set[64] = {0};
   int dev = 0;
@@ -772,7 +786,7 @@ int launch_bulk(const RopeParams& p, int log2l, cudaStream_t s) {
   }
   const int64_t grid = (p.n_tokens + kBulkTPS - 1) / kBulkTPS;
   if (grid > 0x7fffffff) return KANI_ERR_UNSUPPORTED;
-  kern<<<(unsigned)grid, kBulkTPS * 32, smem, s>>>(p, log2l, meta_bulk);
+  kern<<<(unsigned)grid, kBulkTPS * 32, smem, s>>>(p, log2l);
   return launch_status();
 }
 
@@ -913,7 +927,7 @@ int launch_rope_t(const RopeParams& p, cudaStream_t s) {
       const int G = 32 >> log2l;
       const bool rows16 = ((int64_t)p.hq * p.d * (int64_t)sizeof(T)) % 16 == 0 &&
                           ((int64_t)p.hk * p.d * (int64_t)sizeof(T)) % 16 == 0;
-      const int64_t stage = (int64_t)kBulkTPS * (p.hq + 2 * p.hk) * p.d * (int64_t)sizeof(T) + 3 * kBulkTPS * 8;
+      const int64_t stage = (int64_t)kBulkTPS * (p.hq + 2 * p.hk) * p.d * (int64_t)sizeof(T);
       if (rows16 && stage <= 200 * 1024) {
         // the common geometry (16-bit types, D = 64 -> 4 lanes per head) is
         // compiled with constant shuffle sources

@@ -29,6 +29,9 @@ Also reported:
   cpu_baseline— the CPU oracle (PyTorch eager restatement of the reference
                 path) on the host cores, rank 0 at N = 1;
   sweep       — every fused op at its configuration sizes (µs per call and GB/s);
+  decode      — the synthetic LFM2 decode step on the fused kernels: bs=1 latency next
+                to the reference's decode structure with eager ops, and 64 streams
+                per GPU (tokens/s aggregated over the N GPUs);
   clocks      — nvidia-smi samples taken during the timed region.
 
 ``--impl reference`` times the reference's CPU path (the oracle port; the
@@ -406,6 +409,108 @@ def run_sweep(K, dev, peak: float) -> dict:
     return out
 
 
+# ------------------------------------------------------------ decode step
+
+def _eager_rms(x, w, eps):
+    """The reference RMSNorm math (triton_kernels.py:28-35) as eager ops."""
+    xf = x.float()
+    return ((xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)) * w.float()).to(x.dtype)
+
+
+def _make_eager_decoder_cls():
+    """The reference decode step (optimized_decode.py:175-289) with eager PyTorch
+    ops in place of its three Triton kernels and scatter_ for the KV write: the
+    comparison arm for the decode-step latency (the reference's Triton source
+    cannot be shipped to the GPU host).  Attention uses the same folded-GQA
+    SDPA call as the fused decoder, so the two arms differ only in the ops this
+    library replaces."""
+    import torch.nn.functional as F
+    from kani_tts_b200.decode import FusedDecoder
+
+    class EagerReferenceDecoder(FusedDecoder):
+        def step(self, input_ids, positions, slots, mask):
+            b, hq, hk, d = self.batch, self.hq, self.hk, self.d
+            hidden = F.embedding(input_ids, self.embed)
+            for i, L in enumerate(self.layers):
+                normed = _eager_rms(hidden, L["op_norm"], self.eps)
+                if L["attn"]:
+                    qkv = F.linear(normed, L["qkv"])
+                    q, k, v = qkv.split([self.q_dim, self.kv_dim, self.kv_dim], dim=-1)
+                    q = _eager_rms(q.reshape(b, 1, hq, d), L["q_norm"], self.eps).reshape(b, hq, 1, d)
+                    k = _eager_rms(k.reshape(b, 1, hk, d), L["k_norm"], self.eps).reshape(b, hk, 1, d)
+                    v = v.reshape(b, hk, 1, d)
+                    freqs = L["inv_freq"] * positions.float().view(b, 1)           # :229-231
+                    emb = torch.cat([freqs, freqs], dim=-1)
+                    cos = emb.cos().to(self.dtype).view(b, 1, 1, d)
+                    sin = emb.sin().to(self.dtype).view(b, 1, 1, d)
+
+                    def rope(x):                                                  # Triton RoPE math
+                        xf = x.float()
+                        rot = torch.cat([-xf[..., d // 2:], xf[..., : d // 2]], dim=-1)
+                        return (xf * cos.float() + rot * sin.float()).to(self.dtype)
+                    q, k = rope(q), rope(k)
+                    idx = slots.view(b, 1, 1, 1).expand(b, hk, 1, d)               # static_cache.py:135-140
+                    self.k_cache[i].scatter_(2, idx, k)
+                    self.v_cache[i].scatter_(2, idx, v)
+                    attn = F.scaled_dot_product_attention(q.view(b, hk, hq // hk, d), self.k_cache[i],
+                                                          self.v_cache[i], attn_mask=mask, scale=self.scale)
+                    hidden = hidden + F.linear(attn.reshape(b, 1, self.q_dim), L["o"])
+                else:
+                    hidden = hidden + self._conv_step(i, L, normed)
+                normed = _eager_rms(hidden, L["ffn_norm"], self.eps)
+                gu = F.linear(normed, L["gate_up"])
+                n = gu.shape[-1] // 2
+                mlp = (gu[..., :n].float() * torch.sigmoid(gu[..., :n].float()) * gu[..., n:].float()).to(self.dtype)
+                hidden = hidden + F.linear(mlp, L["down"])
+            return F.linear(_eager_rms(hidden, self.final_norm, self.eps), self.head)
+
+    return EagerReferenceDecoder
+
+
+def run_decode(dev, world, rank, batch: int, steps: int, prompt: int = 128, eager: bool = False) -> dict:
+    """Synthetic LFM2 (16 layers: 10 short-conv + 6 GQA 16/8/64, H 1024, FF 4608,
+    vocab 80000, random bf16 weights std 0.02): `prompt`-token prefill (plus a
+    128-d speaker embedding inserted at position 1), then `steps` greedy decode
+    tokens per stream from a captured CUDA graph, static cache 2048 slots."""
+    from kani_tts_b200 import _lib
+    from kani_tts_b200.decode import DecodeEngine, FusedDecoder
+    from kani_tts_b200.model import LFM2Config, synthetic_state_dict
+    cfg = LFM2Config()
+    sd = synthetic_state_dict(cfg, seed=0, device=dev)
+    g = torch.Generator(device="cpu").manual_seed(1 + rank)
+    ids = torch.randint(0, cfg.audio_tokens_start, (batch, prompt), generator=g).to(dev)
+    spk = torch.randn(batch, cfg.speaker_emb_dim, generator=g).to(dev)
+    out = {}
+    arms = [("fused", FusedDecoder)] + ([("eager_reference", _make_eager_decoder_cls())] if eager else [])
+    for name, cls in arms:
+        eng = DecodeEngine(cls(cfg, sd, dev, batch=batch, max_len=2048))
+        eng.start(ids, spk, steps + 8)
+        eng.capture()
+        eng.run(3)                                     # warm-up replays
+        torch.cuda.synchronize(dev)
+        launches0 = _lib.launch_count()
+        _barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        eng.run(steps)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        _barrier(world)
+        sec = _max_over_ranks(e0.elapsed_time(e1) / 1e3, world, dev)
+        flags = int(eng.dec.err_flag.item())
+        out[name] = {"us_per_step": round(sec / steps * 1e6, 2),
+                     "tokens_per_s": round(world * batch * steps / sec, 1),
+                     "kernel_flags": flags}
+        del eng
+        torch.cuda.empty_cache()
+    if eager:
+        out["speedup_vs_eager_reference"] = round(out["eager_reference"]["us_per_step"] /
+                                                  out["fused"]["us_per_step"], 3)
+    out["config"] = (f"bs={batch} x {world} GPU(s), prompt {prompt}+speaker, {steps} decode steps, "
+                     "S=2048, CUDA graph, greedy")
+    return out
+
+
 def run_gpu(args, world, rank, local):
     from kani_tts_b200 import _lib
     from kani_tts_b200 import fused_kernels as K
@@ -444,6 +549,10 @@ def run_gpu(args, world, rank, local):
                 "h2d_bytes_per_step": e["h2d"], "d2h_bytes_per_step": e["d2h"], "steps": e["steps"],
                 "ms_per_step": round(e_max / e["steps"] * 1e3, 4),
                 "path": "kani_tts_b200.fused_rope_kv_write (ctypes -> kani_rope_kv_write), pinned host buffers"}
+    if not args.no_decode:
+        # decode steps: bs=1 (with the eager reference-structure arm) and 64 streams per GPU
+        extras["decode"] = {"bs1": run_decode(dev, world, rank, 1, args.decode_steps, eager=True),
+                            "bs64": run_decode(dev, world, rank, 64, args.decode_steps)}
     if rank == 0:
         if not args.no_sweep:
             extras["sweep"] = run_sweep(K, dev, peak)
@@ -485,6 +594,8 @@ def main():
     ap.add_argument("--impl", choices=["kani_b200", "reference"], default="kani_b200")
     ap.add_argument("--no-sweep", action="store_true", help="skip the per-op sweep")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-decode", action="store_true", help="skip the decode-step measurements")
+    ap.add_argument("--decode-steps", type=int, default=1500)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
     if args.warmup < 3:

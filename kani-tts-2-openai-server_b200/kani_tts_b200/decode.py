@@ -1,0 +1,273 @@
+"""Fused LFM2 decode step and generation engine on the B200 kernels.
+
+``FusedDecoder`` is ``OptimizedDecoder.__call__`` (kani_tts/optimized_decode.py:
+175-289) rebuilt on this library, for one or many independent speech streams:
+
+* every residual add is folded into the RMSNorm that follows it
+  (``fused_add_rms_norm``: optimized_decode.py:252/277/283 + :206/:280/:286);
+* q/k per-head norm, cos/sin, RoPE (with the optional BemaTTS frame term) and
+  the static KV write are one ``fused_rope_kv_write`` launch per attention
+  layer (optimized_decode.py:220-240), reading the packed QKV output in place
+  and writing Q straight into the attention layout;
+* ``fused_silu_mul`` between the fused gate/up and down projections;
+* QKV and gate/up weights are concatenated and the LM head is reduced to
+  [EOS] + audio rows, as the reference does (optimized_decode.py:85-99, 134-156);
+* GQA decode attention runs as plain SDPA with the query heads of one KV head
+  folded into the query-length axis (no K/V expansion), over the
+  [B, Hk, S, D] cache with an additive mask;
+* the short-conv layers use the reference's eager composition
+  (optimized_decode.py:256-277).
+
+GEMVs and attention are library calls (cuBLAS / PyTorch SDPA).
+
+``DecodeEngine`` adds batched prefill (the same kernels at T tokens per
+stream, causal SDPA, causal depthwise conv) and a CUDA-graph decode loop
+whose per-step bookkeeping (position schedule of inference_engine.py:615-619,
+KV slot, mask slot, next token) also runs inside the graph, so generation
+needs no host synchronisation per token.  Sampling is greedy.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from . import _lib
+from .fused_kernels import fused_add_rms_norm, fused_rms_norm, fused_rope_kv_write, fused_silu_mul
+from .model import LFM2Config
+from .positions import learnable_inv_freq
+
+
+class FusedDecoder:
+    """Flat, fused decode forward over a static cache for `batch` streams."""
+
+    def __init__(self, cfg: LFM2Config, state_dict: dict[str, torch.Tensor], device, batch: int,
+                 max_len: int, frame_table: torch.Tensor | None = None):
+        self.cfg = cfg
+        self.device = dev = torch.device(device)
+        self.batch = batch
+        self.max_len = max_len
+        self.dtype = torch.bfloat16
+        h, d = cfg.hidden_size, cfg.head_dim
+        self.hq, self.hk, self.d = cfg.num_attention_heads, cfg.num_key_value_heads, d
+        self.q_dim, self.kv_dim = self.hq * d, self.hk * d
+        self.eps = cfg.norm_eps
+        self.scale = d ** -0.5
+        self.frame_table = frame_table
+
+        def t(name):
+            return state_dict[name].to(dev, self.dtype).contiguous()
+
+        self.embed = t("model.embed_tokens.weight")
+        self.layers = []
+        for i, kind in enumerate(cfg.layer_types):
+            p = f"model.layers.{i}."
+            L = {"attn": kind == "full_attention",
+                 "op_norm": t(p + "operator_norm.weight"), "ffn_norm": t(p + "ffn_norm.weight"),
+                 "gate_up": torch.cat([t(p + "feed_forward.w1.weight"), t(p + "feed_forward.w3.weight")], 0),
+                 "down": t(p + "feed_forward.w2.weight")}
+            if L["attn"]:
+                L["qkv"] = torch.cat([t(p + "self_attn.q_proj.weight"), t(p + "self_attn.k_proj.weight"),
+                                      t(p + "self_attn.v_proj.weight")], 0)
+                L["q_norm"] = t(p + "self_attn.q_layernorm.weight")
+                L["k_norm"] = t(p + "self_attn.k_layernorm.weight")
+                L["o"] = t(p + "self_attn.out_proj.weight")
+                aw = state_dict.get(f"model.learnable_rope_layers.{i}.alpha_weight", torch.tensor(0.0))
+                L["inv_freq"] = learnable_inv_freq(d, cfg.rope_theta, aw, cfg.alpha_min, cfg.alpha_max).to(dev)
+            else:
+                L["in_proj"] = t(p + "conv.in_proj.weight")
+                L["conv_w"] = t(p + "conv.conv.weight")[:, 0, :].contiguous()
+                L["out_proj"] = t(p + "conv.out_proj.weight")
+            self.layers.append(L)
+        self.final_norm = t("model.embedding_norm.weight")
+        head = t("lm_head.weight")
+        self.head = torch.cat([head[cfg.eos_token_id:cfg.eos_token_id + 1], head[cfg.audio_tokens_start:]], 0)
+        self.reduced_to_full = torch.cat([
+            torch.tensor([cfg.eos_token_id], device=dev, dtype=torch.long),
+            torch.arange(cfg.audio_tokens_start, cfg.vocab_size, device=dev, dtype=torch.long)])
+        sp = state_dict.get("model.speaker_emb_projection.weight")
+        self.speaker_proj = sp.to(dev, self.dtype) if sp is not None else None
+
+        # static state: caches, conv states, error flag
+        self.k_cache = {i: torch.zeros(batch, self.hk, max_len, d, dtype=self.dtype, device=dev)
+                        for i, L in enumerate(self.layers) if L["attn"]}
+        self.v_cache = {i: torch.zeros_like(self.k_cache[i]) for i in self.k_cache}
+        self.conv_state = {i: torch.zeros(batch, h, cfg.conv_L_cache, dtype=self.dtype, device=dev)
+                           for i, L in enumerate(self.layers) if not L["attn"]}
+        self.err_flag = _lib.error_flag(dev)
+
+    # ------------------------------------------------------------ decode
+    def step(self, input_ids: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor,
+             mask: torch.Tensor) -> torch.Tensor:
+        """One decode token per stream.
+
+        input_ids [B, 1] int64; positions / slots [B] int64 (angle position and
+        KV slot); mask [B, 1, 1, S] additive (0 = attend).  Returns reduced-head
+        logits [B, 1, num_reduced].
+        """
+        b, hq, hk, d = self.batch, self.hq, self.hk, self.d
+        hidden = F.embedding(input_ids, self.embed)              # [B, 1, H] residual stream
+        delta = None
+        for i, L in enumerate(self.layers):
+            if delta is None:
+                normed = fused_rms_norm(hidden, L["op_norm"], self.eps)
+            else:
+                normed, hidden = fused_add_rms_norm(delta, hidden, L["op_norm"], self.eps)
+            if L["attn"]:
+                qkv = F.linear(normed, L["qkv"])                  # [B, 1, (Hq+2Hk)D]
+                q, k, v = qkv.split([self.q_dim, self.kv_dim, self.kv_dim], dim=-1)
+                q_rot = fused_rope_kv_write(
+                    q.view(b, 1, hq, d), k.view(b, 1, hk, d), v.view(b, 1, hk, d), L["inv_freq"], positions,
+                    self.k_cache[i], self.v_cache[i], slots, frame_table=self.frame_table,
+                    tokens_per_frame=self.cfg.tokens_per_frame, q_norm_w=L["q_norm"], k_norm_w=L["k_norm"],
+                    eps=self.eps, err_flag=self.err_flag)
+                # GQA without expansion: the query heads of one KV head become its query rows
+                attn = F.scaled_dot_product_attention(
+                    q_rot.view(b, hk, hq // hk, d), self.k_cache[i], self.v_cache[i], attn_mask=mask,
+                    scale=self.scale)                             # [B, Hk, Hq/Hk, D]
+                delta = F.linear(attn.reshape(b, 1, self.q_dim), L["o"])
+            else:
+                delta = self._conv_step(i, L, normed)
+            normed, hidden = fused_add_rms_norm(delta, hidden, L["ffn_norm"], self.eps)
+            delta = F.linear(fused_silu_mul(F.linear(normed, L["gate_up"])), L["down"])
+        normed, _ = fused_add_rms_norm(delta, hidden, self.final_norm, self.eps)
+        return F.linear(normed, self.head)
+
+    def _conv_step(self, i, L, normed):
+        """Short-conv decode step as the reference composes it (optimized_decode.py:256-277)."""
+        bcx = F.linear(normed, L["in_proj"]).transpose(-1, -2)   # [B, 3H, 1]
+        bg, c, xc = bcx.chunk(3, dim=-2)
+        bx = bg * xc
+        state = self.conv_state[i].roll(shifts=-1, dims=-1)
+        state[:, :, -1:] = bx                                     # cache_position >= L-1 in decode
+        self.conv_state[i].copy_(state)
+        conv_out = torch.sum(state * L["conv_w"], dim=-1).unsqueeze(-1)
+        y = (c * conv_out).transpose(-1, -2)
+        return F.linear(y, L["out_proj"])
+
+    # ----------------------------------------------------------- prefill
+    def prefill(self, input_ids: torch.Tensor, positions: torch.Tensor,
+                speaker_emb: torch.Tensor | None = None) -> torch.Tensor:
+        """Prompt pass for all streams (equal lengths).  input_ids [B, T];
+        positions [B, T'] (T' = T + 1 with a speaker embedding, inserted at
+        position 1 as inference_engine.py:475-491 does).  Fills KV slots
+        0..T'-1 and the conv states; returns reduced-head logits of the last
+        token [B, 1, num_reduced]."""
+        b = self.batch
+        x = F.embedding(input_ids, self.embed)
+        if speaker_emb is not None:
+            spk = F.linear(speaker_emb.to(self.dtype), self.speaker_proj).unsqueeze(1)
+            x = torch.cat([x[:, :1], spk, x[:, 1:]], dim=1)
+        t = x.shape[1]
+        hq, hk, d = self.hq, self.hk, self.d
+        slots = torch.arange(t, device=self.device, dtype=torch.long).repeat(b)
+        pos = positions.reshape(-1).to(torch.long)
+        hidden, delta = x, None
+        for i, L in enumerate(self.layers):
+            if delta is None:
+                normed = fused_rms_norm(hidden, L["op_norm"], self.eps)
+            else:
+                normed, hidden = fused_add_rms_norm(delta, hidden, L["op_norm"], self.eps)
+            if L["attn"]:
+                qkv = F.linear(normed, L["qkv"])
+                q, k, v = qkv.split([self.q_dim, self.kv_dim, self.kv_dim], dim=-1)
+                q_rot = fused_rope_kv_write(
+                    q.view(b, t, hq, d), k.view(b, t, hk, d), v.view(b, t, hk, d), L["inv_freq"], pos,
+                    self.k_cache[i], self.v_cache[i], slots, frame_table=self.frame_table,
+                    tokens_per_frame=self.cfg.tokens_per_frame, q_norm_w=L["q_norm"], k_norm_w=L["k_norm"],
+                    eps=self.eps, err_flag=self.err_flag)
+                rep = hq // hk                                    # prefill: expand K/V heads for GQA
+                attn = F.scaled_dot_product_attention(
+                    q_rot.transpose(1, 2), self.k_cache[i][:, :, :t].repeat_interleave(rep, dim=1),
+                    self.v_cache[i][:, :, :t].repeat_interleave(rep, dim=1),
+                    is_causal=True, scale=self.scale)                  # [B, Hq, T, D]
+                delta = F.linear(attn.transpose(1, 2).reshape(b, t, self.q_dim), L["o"])
+            else:
+                bcx = F.linear(normed, L["in_proj"]).transpose(-1, -2)   # [B, 3H, T]
+                bg, c, xc = bcx.chunk(3, dim=-2)
+                bx = bg * xc
+                lc = self.cfg.conv_L_cache
+                self.conv_state[i].copy_(F.pad(bx, (lc - t, 0)) if t < lc else bx[..., t - lc:])
+                conv_out = F.conv1d(bx, L["conv_w"].unsqueeze(1), padding=lc - 1, groups=bx.shape[1])[..., :t]
+                delta = F.linear((c * conv_out).transpose(-1, -2), L["out_proj"])
+            normed, hidden = fused_add_rms_norm(delta, hidden, L["ffn_norm"], self.eps)
+            delta = F.linear(fused_silu_mul(F.linear(normed, L["gate_up"])), L["down"])
+        normed, _ = fused_add_rms_norm(delta[:, -1:], hidden[:, -1:], self.final_norm, self.eps)
+        return F.linear(normed, self.head)
+
+
+class DecodeEngine:
+    """Prefill + CUDA-graph greedy decode for `batch` independent streams."""
+
+    def __init__(self, decoder: FusedDecoder):
+        self.dec = decoder
+        dev, b, s = decoder.device, decoder.batch, decoder.max_len
+        self.input_ids = torch.zeros(b, 1, dtype=torch.long, device=dev)
+        self.positions = torch.zeros(b, dtype=torch.long, device=dev)
+        self.slots = torch.zeros(b, dtype=torch.long, device=dev)
+        self.mask = torch.full((b, 1, 1, s), float("-inf"), dtype=torch.bfloat16, device=dev)
+        self.step_idx = torch.zeros(1, dtype=torch.long, device=dev)
+        self.base_pos = torch.zeros(b, dtype=torch.long, device=dev)
+        self.base_slot = torch.zeros(b, dtype=torch.long, device=dev)
+        self.generated = None
+        self.graph = None
+        self.logits = None
+
+    def start(self, input_ids: torch.Tensor, speaker_emb: torch.Tensor | None, max_new_tokens: int) -> None:
+        """Prefill all streams and arm the decode loop."""
+        dec, cfg = self.dec, self.dec.cfg
+        b, t = input_ids.shape
+        t_eff = t + (1 if speaker_emb is not None else 0)
+        if t_eff + max_new_tokens > dec.max_len:
+            raise ValueError(f"cache of {dec.max_len} slots cannot hold {t_eff} + {max_new_tokens} tokens")
+        if speaker_emb is not None:   # speaker-conditioned prompts are sequential (inference_engine.py:497-499)
+            pos = torch.arange(t_eff, device=dec.device).repeat(b, 1)
+        else:
+            from .positions import frame_level_positions
+            pos = frame_level_positions(input_ids, cfg.audio_tokens_start, cfg.tokens_per_frame,
+                                        cfg.audio_step).long()
+        logits = dec.prefill(input_ids, pos, speaker_emb)
+        first = dec.reduced_to_full[logits[:, -1].argmax(-1)]
+        self.input_ids.copy_(first.view(b, 1))
+        self.mask.fill_(float("-inf"))
+        self.mask[..., :t_eff] = 0.0
+        self.base_pos.fill_(t_eff)        # decode step k: t_eff + (k // tpf) * audio_step
+        self.base_slot.fill_(t_eff)       # decode step k writes slot t_eff + k
+        self.step_idx.zero_()
+        self.generated = torch.zeros(b, max_new_tokens, dtype=torch.long, device=dec.device)
+
+    def _step_body(self):
+        cfg = self.dec.cfg
+        k = self.step_idx
+        self.positions.copy_(self.base_pos + (torch.div(k, cfg.tokens_per_frame, rounding_mode="floor")
+                                              * cfg.audio_step).long())
+        self.slots.copy_(self.base_slot + k)
+        self.mask.scatter_(3, self.slots.view(-1, 1, 1, 1), 0.0)
+        self.logits = self.dec.step(self.input_ids, self.positions, self.slots, self.mask)
+        nxt = self.dec.reduced_to_full[self.logits[:, 0].argmax(-1)]
+        self.generated.index_copy_(1, k, nxt.view(-1, 1))
+        self.input_ids.copy_(nxt.view(-1, 1))
+        self.step_idx.add_(1)
+
+    def capture(self) -> None:
+        """Warm up once outside capture, then capture one decode step."""
+        dec = self.dec
+        saved = ({i: c.clone() for i, c in dec.conv_state.items()}, self.input_ids.clone(), self.mask.clone(),
+                 self.step_idx.clone())
+        s = torch.cuda.Stream(device=dec.device)
+        s.wait_stream(torch.cuda.current_stream(dec.device))
+        with torch.cuda.stream(s):
+            self._step_body()
+        torch.cuda.current_stream(dec.device).wait_stream(s)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._step_body()
+        # undo the warm-up and capture steps (they ran the step twice)
+        for i, c in saved[0].items():
+            dec.conv_state[i].copy_(c)
+        self.input_ids.copy_(saved[1])
+        self.mask.copy_(saved[2])
+        self.step_idx.copy_(saved[3])
+
+    def run(self, n_steps: int) -> None:
+        for _ in range(n_steps):
+            self.graph.replay()

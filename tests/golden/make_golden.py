@@ -199,7 +199,103 @@ def main() -> None:
         audio_step=np.float64(1.0),
         positions=md.compute_frame_level_positions(ids_mix, 64410, 4, 1.0).float())
     save("frame_positions", cases)
+
+    save("decode_step", decode_step_cases(sc, md, hf))
     print("golden vectors written to", OUT)
+
+
+def decode_step_cases(sc, md, hf):
+    """Three decode steps of the reference OptimizedDecoder (kani_tts/optimized_decode.py)
+    on a tiny synthetic LFM2 held by a stand-in model object that exposes exactly the
+    attributes OptimizedDecoder reads.  Weights come from the package's seeded
+    generator (only the seed and a checksum are stored)."""
+    import types as _t
+    sys.path.insert(0, str(Path(__file__).resolve().parents[2] / "kani-tts-2-openai-server_b200"))
+    from kani_tts_b200.model import synthetic_state_dict, tiny_config
+    od = importlib.import_module("kani_tts.optimized_decode")
+    cfg = tiny_config()
+    seed = 1234
+    sd = synthetic_state_dict(cfg, seed=seed)
+    hcfg = make_config(hf, hidden=cfg.hidden_size, heads=cfg.num_attention_heads,
+                       kv_heads=cfg.num_key_value_heads, layers=cfg.num_hidden_layers,
+                       layer_types=list(cfg.layer_types), theta=cfg.rope_theta)
+    hcfg.head_dim = cfg.head_dim
+    hcfg.vocab_size = cfg.vocab_size
+    hcfg.norm_eps = cfg.norm_eps
+    hcfg.conv_L_cache = cfg.conv_L_cache
+    ns = _t.SimpleNamespace
+    W = lambda name: ns(weight=sd[name])  # noqa: E731
+    layers, ropes = [], []
+    for i, kind in enumerate(cfg.layer_types):
+        p = f"model.layers.{i}."
+        L = ns(operator_norm=W(p + "operator_norm.weight"), ffn_norm=W(p + "ffn_norm.weight"),
+               feed_forward=ns(w1=W(p + "feed_forward.w1.weight"), w2=W(p + "feed_forward.w2.weight"),
+                               w3=W(p + "feed_forward.w3.weight")))
+        if kind == "full_attention":
+            L.self_attn = ns(q_proj=W(p + "self_attn.q_proj.weight"), k_proj=W(p + "self_attn.k_proj.weight"),
+                             v_proj=W(p + "self_attn.v_proj.weight"),
+                             q_layernorm=W(p + "self_attn.q_layernorm.weight"),
+                             k_layernorm=W(p + "self_attn.k_layernorm.weight"),
+                             out_proj=W(p + "self_attn.out_proj.weight"))
+            rope = md.LearnableRotaryEmbedding(hcfg, layer_idx=i, total_attention_layers=2)
+            with torch.no_grad():
+                rope.alpha_weight.copy_(sd[f"model.learnable_rope_layers.{i}.alpha_weight"])
+            ropes.append(rope)
+        else:
+            L.conv = ns(in_proj=W(p + "conv.in_proj.weight"), conv=W(p + "conv.conv.weight"),
+                        out_proj=W(p + "conv.out_proj.weight"))
+            ropes.append(None)
+        layers.append(L)
+    emb = torch.nn.Embedding(cfg.vocab_size, cfg.hidden_size)
+    with torch.no_grad():
+        emb.weight.copy_(sd["model.embed_tokens.weight"].float())
+    emb = emb.to(torch.bfloat16)
+    stand_in = ns(config=hcfg, parameters=lambda: iter([sd["lm_head.weight"]]),
+                  model=ns(embed_tokens=emb, layers=layers, learnable_rope_layers=ropes,
+                           embedding_norm=W("model.embedding_norm.weight"), pos_emb=None),
+                  lm_head=W("lm_head.weight"))
+    dec = od.OptimizedDecoder(stand_in, cfg.audio_tokens_start, cfg.eos_token_id)
+
+    max_len, prefix = 16, 5
+    cache = sc.StaticLfm2HybridConvCache(hcfg, max_total_len=max_len, batch_size=1, dtype=torch.bfloat16,
+                                         device="cpu")
+    init = {}
+    for i in cfg.attn_layers:
+        kp = randn((1, cfg.num_key_value_heads, max_len, cfg.head_dim), 100 + i)
+        vp = randn((1, cfg.num_key_value_heads, max_len, cfg.head_dim), 200 + i)
+        kp[:, :, prefix:] = 0
+        vp[:, :, prefix:] = 0
+        cache.key_cache[i].copy_(kp)
+        cache.value_cache[i].copy_(vp)
+        init[f"k_init_{i}"], init[f"v_init_{i}"] = kp, vp
+    for i, kind in enumerate(cfg.layer_types):
+        if kind != "full_attention":
+            cs = randn((1, cfg.hidden_size, cfg.conv_L_cache), 300 + i)
+            cache.conv_cache[i].copy_(cs)
+            init[f"conv_init_{i}"] = cs
+    mask = torch.full((1, 1, 1, max_len), float("-inf"), dtype=torch.bfloat16)
+    mask[..., :prefix] = 0
+    tokens = [650, 7, 612]
+    positions = [prefix, prefix, prefix + 1]
+    out = {"seed": np.int64(seed), "max_len": np.int64(max_len), "prefix": np.int64(prefix),
+           "tokens": torch.tensor(tokens), "positions": torch.tensor(positions),
+           "weight_checksum": np.float64(sum(float(v.float().abs().sum()) for v in sd.values())), **init}
+    with torch.no_grad():
+        for step, (tok, pos) in enumerate(zip(tokens, positions)):
+            slot = prefix + step
+            cache.set_write_position(slot)
+            mask[..., slot] = 0
+            logits = dec(input_ids=torch.tensor([[tok]]), position_ids=torch.tensor([[pos]]),
+                         past_key_values=cache, causal_mask=mask,
+                         cache_position=torch.tensor([slot]))
+            out[f"logits_{step}"] = logits.clone()
+    for i in cfg.attn_layers:
+        out[f"k_final_{i}"] = cache.key_cache[i].clone()
+        out[f"v_final_{i}"] = cache.value_cache[i].clone()
+    for i, kind in enumerate(cfg.layer_types):
+        if kind != "full_attention":
+            out[f"conv_final_{i}"] = cache.conv_cache[i].clone()
+    return {"tiny": out}
 
 
 if __name__ == "__main__":

@@ -596,10 +596,21 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode-step measurements")
     ap.add_argument("--decode-steps", type=int, default=1500)
+    ap.add_argument("--decode-only", action="store_true", help="profiling aid: run only the decode arms")
+    ap.add_argument("--decode-batch", type=int, default=1, help="streams for --decode-only")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.decode_only:
+        # profiling aid: only the bs=1 decode arms, one JSON line with the decode results
+        world, rank, local = _dist_init()
+        dev = torch.device("cuda", local)
+        torch.cuda.set_device(dev)
+        res = run_decode(dev, world, rank, args.decode_batch, args.decode_steps, eager=args.decode_batch == 1)
+        if rank == 0:
+            print(json.dumps({"decode": res}), flush=True)
+        return
     if args.impl == "reference":
         # CPU arm: rank 0 alone measures; other ranks exit without work or a process group
         run_reference(args, int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")))

@@ -87,7 +87,10 @@ def test_batched_fused_step_matches_oracle(full):
         mask[s, ..., : int(slots[s]) + 1] = 0
     got = dec.step(ids.to(DEV), pos.to(DEV), slots.to(DEV), mask.to(DEV))
     ref = ora.step(ids, pos, slots, mask)
-    close(got, ref)
+    # at full size 16 layers of bf16 GEMVs accumulate in a different order than on the CPU
+    close(got, ref, 0.05 if full else 0.02)
+    cos = torch.nn.functional.cosine_similarity(got.float().cpu().flatten(1), ref.float().flatten(1))
+    assert float(cos.min()) > 0.999
     same_argmax(got, ref)
     for i in cfg.attn_layers:
         for s in range(b):

@@ -421,14 +421,14 @@ def _make_eager_decoder_cls():
     """The reference decode step (optimized_decode.py:175-289) with eager PyTorch
     ops in place of its three Triton kernels and scatter_ for the KV write: the
     comparison arm for the decode-step latency (the reference's Triton source
-    cannot be shipped to the GPU host).  Attention uses the same folded-GQA
-    SDPA call as the fused decoder, so the two arms differ only in the ops this
-    library replaces."""
+    cannot be shipped to the GPU host).  Attention is the reference's SDPA call
+    over the whole masked static buffer and the short-conv step its eager
+    composition."""
     import torch.nn.functional as F
     from kani_tts_b200.decode import FusedDecoder
 
     class EagerReferenceDecoder(FusedDecoder):
-        def step(self, input_ids, positions, slots, mask):
+        def step(self, input_ids, positions, slots, kv_len, mask):
             b, hq, hk, d = self.batch, self.hq, self.hk, self.d
             hidden = F.embedding(input_ids, self.embed)
             for i, L in enumerate(self.layers):
@@ -452,11 +452,12 @@ def _make_eager_decoder_cls():
                     idx = slots.view(b, 1, 1, 1).expand(b, hk, 1, d)               # static_cache.py:135-140
                     self.k_cache[i].scatter_(2, idx, k)
                     self.v_cache[i].scatter_(2, idx, v)
-                    attn = F.scaled_dot_product_attention(q.view(b, hk, hq // hk, d), self.k_cache[i],
-                                                          self.v_cache[i], attn_mask=mask, scale=self.scale)
+                    # the reference's SDPA over the whole masked buffer (GQA as the reference calls it)
+                    attn = F.scaled_dot_product_attention(q, self.k_cache[i], self.v_cache[i], attn_mask=mask,
+                                                          scale=self.scale, enable_gqa=True)
                     hidden = hidden + F.linear(attn.reshape(b, 1, self.q_dim), L["o"])
                 else:
-                    hidden = hidden + self._conv_step(i, L, normed)
+                    hidden = hidden + self._conv_step_eager(i, L, normed)
                 normed = _eager_rms(hidden, L["ffn_norm"], self.eps)
                 gu = F.linear(normed, L["gate_up"])
                 n = gu.shape[-1] // 2
@@ -483,7 +484,7 @@ def run_decode(dev, world, rank, batch: int, steps: int, prompt: int = 128, eage
     out = {}
     arms = [("fused", FusedDecoder)] + ([("eager_reference", _make_eager_decoder_cls())] if eager else [])
     for name, cls in arms:
-        eng = DecodeEngine(cls(cfg, sd, dev, batch=batch, max_len=2048))
+        eng = DecodeEngine(cls(cfg, sd, dev, batch=batch, max_len=2048), keep_mask=(name != "fused"))
         eng.start(ids, spk, steps + 8)
         eng.capture()
         eng.run(3)                                     # warm-up replays

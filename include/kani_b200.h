@@ -173,6 +173,45 @@ KANI_API int kani_rope_kv_write(int32_t dtype,
                        const int64_t* write_slots,
                        int32_t* err_flag, void* stream);
 
+/*
+ * GQA decode attention over the valid cache prefix, one query token per stream:
+ *   out[b, hq, :] = softmax_j(scale * q[b, hq, :] . K[b, hq/G, j, :]) V[b, hq/G, j, :]
+ * for slots j in [0, kv_len[b]) (kv_len: device int64 [batch]; values above
+ * cache_len are clamped and flag KANI_FLAG_SLOT_OOB), G = num_q_heads / num_kv_heads.
+ * Replaces the SDPA over the whole -inf-masked static buffer of
+ * kani_tts/optimized_decode.py:243-248 (mask: kani_tts/inference_engine.py:259-265,
+ * opened slot by slot at :643, always a prefix).  fp32 online softmax, one
+ * rounding of the output.  head_dim 64 (G = 1, 2, 4) or 128 (G = 1, 2);
+ * 16-byte aligned rows.
+ *   q, out: [batch, num_q_heads, head_dim] with batch / head strides
+ *   k_cache, v_cache: [batch, num_kv_heads, cache_len, head_dim] with strides
+ */
+KANI_API int kani_decode_attention(int32_t dtype, int64_t batch, int32_t num_q_heads,
+                          int32_t num_kv_heads, int32_t head_dim,
+                          const void* q, int64_t q_batch_stride, int64_t q_head_stride,
+                          const void* k_cache, const void* v_cache,
+                          int64_t cache_batch_stride, int64_t cache_head_stride,
+                          int64_t cache_slot_stride, int64_t cache_len,
+                          const int64_t* kv_len, float scale,
+                          void* out, int64_t out_batch_stride, int64_t out_head_stride,
+                          int32_t* err_flag, void* stream);
+
+/*
+ * LFM2 gated short-convolution decode step for `batch` streams:
+ *   [Bg | C | x] = bcx[b] (3*hidden, the in_proj output);  Bx = Bg * x;
+ *   state[b] = roll(state[b], -1 along the kernel axis) with Bx in the last column;
+ *   y[b] = C * sum_i(state[b, :, i] * conv_w[:, i])
+ * with the rounding of the eager bf16 ops (bit-identical to them).
+ * Replaces kani_tts/optimized_decode.py:256-277 (between in_proj and out_proj).
+ *   bcx: [batch, 3*hidden] (row stride); state: [batch, hidden, kernel_len]
+ *   (batch stride, contiguous per stream); conv_w: [hidden, kernel_len];
+ *   y: [batch, hidden] (row stride).  kernel_len in 2..4.
+ */
+KANI_API int kani_short_conv_step(int32_t dtype, const void* bcx, int64_t bcx_row_stride,
+                         void* state, int64_t state_batch_stride, const void* conv_w,
+                         void* y, int64_t y_row_stride, int64_t batch, int32_t hidden,
+                         int32_t kernel_len, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

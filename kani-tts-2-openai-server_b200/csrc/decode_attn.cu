@@ -1,0 +1,262 @@
+// GQA decode attention over the valid cache prefix (sm_100a).
+//
+// Computes, per stream b and query head hq (KV head h = hq / G),
+//     out[b, hq, :] = softmax_j(scale * q[b, hq, :] . K[b, h, j, :]) V[b, h, j, :],
+// over cache slots j in [0, kv_len[b]).  This is the attention the reference
+// decode step runs as SDPA over the whole static buffer with an additive
+// -inf mask (kani_tts/optimized_decode.py:243-248; mask built at
+// kani_tts/inference_engine.py:259-265 and opened slot by slot at :643,
+// always a prefix); here only the valid prefix is read.
+//
+// Structure: one thread-block cluster of kClusterCTAs CTAs per (b, h).  The
+// valid prefix is split evenly over the cluster's CTAs; inside a CTA, lane
+// = (key group kg in 0..7, dim slice ds in 0..3): four lanes share one key,
+// each holding D/4 dims of it and of all G query heads, so a score is a
+// 2-step shuffle sum and K/V rows are read with 16-byte loads.  Each lane
+// keeps an online softmax (running max, sum, weighted V) per query head in
+// fp32 (base-2 exponentials, the query pre-scaled by scale * log2 e).  The
+// partials are merged across key groups by shuffles, across the CTA's warps
+// through shared memory, and across the cluster through distributed shared
+// memory by CTA rank 0, which writes the normalised output with one
+// rounding.  No global scratch is used; the two cluster barriers are
+// hardware barriers that every CTA of the cluster reaches.
+#include <cooperative_groups.h>
+
+#include "common.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace kani {
+namespace {
+
+constexpr int kClusterCTAs = 8;
+constexpr int kAttnThreads = 128;
+
+struct AttnParams {
+  const void* q;
+  int64_t qb, qh;  // strides of q [B, Hq, D]
+  const void* k;
+  const void* v;
+  int64_t cb, ch, cs;  // cache strides [B, Hk, S, D]
+  int64_t cache_len;
+  const int64_t* kv_len;
+  void* out;
+  int64_t ob, oh;  // strides of out [B, Hq, D]
+  float qscale;    // scale * log2(e)
+  int32_t* err;
+};
+
+__device__ __forceinline__ float merge_weight(float m, float mnew) {
+  return m == -INFINITY ? 0.f : exp2f(m - mnew);
+}
+
+template <typename T, int G, int D>
+__global__ void __cluster_dims__(kClusterCTAs, 1, 1) __launch_bounds__(kAttnThreads)
+decode_attn_kernel(AttnParams p) {
+  constexpr int DL = D / 4;           // dims per lane
+  constexpr int VE = VecN<T>::value;  // elements per 16-byte vector
+  constexpr int NV = DL / VE;         // 16-byte vectors per lane per row
+  constexpr int NW = kAttnThreads / 32;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int crank = (int)cluster.block_rank();
+  const int h = blockIdx.y;
+  const int b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kg = lane >> 2, ds = lane & 3;
+
+  __shared__ float w_m[NW][G], w_l[NW][G];
+  __shared__ float w_acc[NW][G][D];
+  __shared__ float c_m[G], c_l[G];
+  __shared__ float c_acc[G][D];
+
+  int64_t len = p.kv_len[b];
+  if (len > p.cache_len) {
+    if (crank == 0 && threadIdx.x == 0 && h == 0 && p.err != nullptr) atomicOr(p.err, KANI_FLAG_SLOT_OOB);
+    len = p.cache_len;
+  }
+  if (len < 0) len = 0;
+  const int64_t chunk = (len + kClusterCTAs - 1) / kClusterCTAs;
+  const int64_t k0 = crank * chunk;
+  const int64_t k1 = k0 + chunk < len ? k0 + chunk : len;
+
+  // the G query heads of this KV head, this lane's dims, pre-scaled
+  float q[G][DL];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const T* qp = static_cast<const T*>(p.q) + b * p.qb + (int64_t)(h * G + g) * p.qh + ds * DL;
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      float f[VE];
+      unpack16<T>(ld16(qp + v * VE), f);
+#pragma unroll
+      for (int e = 0; e < VE; ++e) q[g][v * VE + e] = f[e] * p.qscale;
+    }
+  }
+
+  float m[G], l[G], acc[G][DL];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+#pragma unroll
+    for (int d = 0; d < DL; ++d) acc[g][d] = 0.f;
+  }
+
+  const T* kbase = static_cast<const T*>(p.k) + b * p.cb + (int64_t)h * p.ch + ds * DL;
+  const T* vbase = static_cast<const T*>(p.v) + b * p.cb + (int64_t)h * p.ch + ds * DL;
+  // warp-uniform loop: every lane reaches the shuffles
+  for (int64_t base = k0 + warp * 8; base < k1; base += 8 * NW) {
+    const int64_t j = base + kg;
+    const bool valid = j < k1;
+    uint4 kv[NV], vv[NV];
+    if (valid) {
+#pragma unroll
+      for (int v = 0; v < NV; ++v) {
+        kv[v] = ld16_stream(kbase + j * p.cs + v * VE);
+        vv[v] = ld16_stream(vbase + j * p.cs + v * VE);
+      }
+    }
+    float kf[DL], vf[DL];
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      unpack16<T>(valid ? kv[v] : make_uint4(0, 0, 0, 0), kf + v * VE);
+      unpack16<T>(valid ? vv[v] : make_uint4(0, 0, 0, 0), vf + v * VE);
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float s = 0.f;
+#pragma unroll
+      for (int d = 0; d < DL; ++d) s = fmaf(q[g][d], kf[d], s);
+      s += __shfl_xor_sync(0xffffffffu, s, 1);
+      s += __shfl_xor_sync(0xffffffffu, s, 2);
+      if (valid) {
+        const float mn = fmaxf(m[g], s);
+        const float corr = merge_weight(m[g], mn);
+        const float pr = exp2f(s - mn);
+        l[g] = fmaf(l[g], corr, pr);
+#pragma unroll
+        for (int d = 0; d < DL; ++d) acc[g][d] = fmaf(acc[g][d], corr, pr * vf[d]);
+        m[g] = mn;
+      }
+    }
+  }
+
+  // merge the 8 key groups of the warp (lanes with the same dim slice)
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float mo = __shfl_xor_sync(0xffffffffu, m[g], off);
+      const float lo = __shfl_xor_sync(0xffffffffu, l[g], off);
+      const float mn = fmaxf(m[g], mo);
+      const float wa = merge_weight(m[g], mn), wb = merge_weight(mo, mn);
+      l[g] = l[g] * wa + lo * wb;
+#pragma unroll
+      for (int d = 0; d < DL; ++d) {
+        const float ao = __shfl_xor_sync(0xffffffffu, acc[g][d], off);
+        acc[g][d] = acc[g][d] * wa + ao * wb;
+      }
+      m[g] = mn;
+    }
+  }
+  if (kg == 0) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      if (ds == 0) {
+        w_m[warp][g] = m[g];
+        w_l[warp][g] = l[g];
+      }
+#pragma unroll
+      for (int d = 0; d < DL; ++d) w_acc[warp][g][ds * DL + d] = acc[g][d];
+    }
+  }
+  __syncthreads();
+  // merge the warps: one (head, dim) per thread
+  for (int t = threadIdx.x; t < G * D; t += kAttnThreads) {
+    const int g = t / D, d = t - (t / D) * D;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) mx = fmaxf(mx, w_m[w][g]);
+    float ls = 0.f, as = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      const float wt = merge_weight(w_m[w][g], mx);
+      ls += w_l[w][g] * wt;
+      as += w_acc[w][g][d] * wt;
+    }
+    c_acc[g][d] = as;
+    if (d == 0) {
+      c_m[g] = mx;
+      c_l[g] = ls;
+    }
+  }
+  cluster.sync();  // every CTA's partial is in its shared memory
+  if (crank == 0) {
+    for (int t = threadIdx.x; t < G * D; t += kAttnThreads) {
+      const int g = t / D, d = t - (t / D) * D;
+      float mr[kClusterCTAs];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int r = 0; r < kClusterCTAs; ++r) {
+        mr[r] = *cluster.map_shared_rank(&c_m[g], r);
+        mx = fmaxf(mx, mr[r]);
+      }
+      float ls = 0.f, as = 0.f;
+#pragma unroll
+      for (int r = 0; r < kClusterCTAs; ++r) {
+        const float wt = merge_weight(mr[r], mx);
+        ls += *cluster.map_shared_rank(&c_l[g], r) * wt;
+        as += *cluster.map_shared_rank(&c_acc[g][d], r) * wt;
+      }
+      T* o = static_cast<T*>(p.out) + b * p.ob + (int64_t)(h * G + g) * p.oh + d;
+      *o = Elem<T>::from_f(ls > 0.f ? as / ls : 0.f);
+    }
+  }
+  cluster.sync();  // rank 0 has read the other CTAs' shared memory
+}
+
+template <typename T, int G, int D>
+int launch_attn(const AttnParams& p, int64_t batch, int hk, cudaStream_t s) {
+  const dim3 grid(kClusterCTAs, (unsigned)hk, (unsigned)batch);
+  decode_attn_kernel<T, G, D><<<grid, kAttnThreads, 0, s>>>(p);
+  return launch_status();
+}
+
+}  // namespace
+}  // namespace kani
+
+extern "C" int kani_decode_attention(int32_t dtype, int64_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                                     int32_t head_dim, const void* q, int64_t q_batch_stride,
+                                     int64_t q_head_stride, const void* k_cache, const void* v_cache,
+                                     int64_t cache_batch_stride, int64_t cache_head_stride,
+                                     int64_t cache_slot_stride, int64_t cache_len, const int64_t* kv_len,
+                                     float scale, void* out, int64_t out_batch_stride,
+                                     int64_t out_head_stride, int32_t* err_flag, void* stream) {
+  if (batch < 0 || num_q_heads < 0 || num_kv_heads < 0 || head_dim < 0 || cache_len < 0)
+    return KANI_ERR_INVALID_ARG;
+  if (batch == 0 || num_q_heads == 0) return KANI_OK;
+  if (!q || !k_cache || !v_cache || !kv_len || !out || num_kv_heads == 0) return KANI_ERR_INVALID_ARG;
+  if (num_q_heads % num_kv_heads != 0) return KANI_ERR_INVALID_ARG;
+  if (batch > 65535 || num_kv_heads > 65535) return KANI_ERR_UNSUPPORTED;
+  const int g = num_q_heads / num_kv_heads;
+  kani::AttnParams p{q, q_batch_stride, q_head_stride, k_cache, v_cache, cache_batch_stride,
+                     cache_head_stride, cache_slot_stride, cache_len, kv_len, out, out_batch_stride,
+                     out_head_stride, scale * 1.4426950408889634f, err_flag};
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return kani::dispatch_dtype(dtype, [&]<typename T>() -> int {
+    constexpr int E = kani::VecN<T>::value;
+    const bool vec = kani::aligned16(q) && kani::aligned16(k_cache) && kani::aligned16(v_cache) &&
+                     q_batch_stride % E == 0 && q_head_stride % E == 0 && cache_batch_stride % E == 0 &&
+                     cache_head_stride % E == 0 && cache_slot_stride % E == 0;
+    if (!vec) return KANI_ERR_UNSUPPORTED;
+    if (head_dim == 64) {
+      if (g == 1) return kani::launch_attn<T, 1, 64>(p, batch, num_kv_heads, s);
+      if (g == 2) return kani::launch_attn<T, 2, 64>(p, batch, num_kv_heads, s);
+      if (g == 4) return kani::launch_attn<T, 4, 64>(p, batch, num_kv_heads, s);
+    } else if (head_dim == 128) {
+      if (g == 1) return kani::launch_attn<T, 1, 128>(p, batch, num_kv_heads, s);
+      if (g == 2) return kani::launch_attn<T, 2, 128>(p, batch, num_kv_heads, s);
+    }
+    return KANI_ERR_UNSUPPORTED;
+  });
+}

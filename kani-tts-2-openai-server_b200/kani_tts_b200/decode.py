@@ -12,13 +12,14 @@
 * ``fused_silu_mul`` between the fused gate/up and down projections;
 * QKV and gate/up weights are concatenated and the LM head is reduced to
   [EOS] + audio rows, as the reference does (optimized_decode.py:85-99, 134-156);
-* GQA decode attention runs as plain SDPA with the query heads of one KV head
-  folded into the query-length axis (no K/V expansion), over the
-  [B, Hk, S, D] cache with an additive mask;
-* the short-conv layers use the reference's eager composition
-  (optimized_decode.py:256-277).
+* GQA decode attention reads only each stream's valid cache prefix
+  (``decode_attention``: split over an 8-CTA cluster, partials merged in
+  distributed shared memory) instead of SDPA over the whole -inf-masked
+  buffer (optimized_decode.py:243-248);
+* the gated short-conv step between in_proj and out_proj is one
+  ``short_conv_step`` launch (optimized_decode.py:256-277).
 
-GEMVs and attention are library calls (cuBLAS / PyTorch SDPA).
+The GEMVs are cuBLAS calls; prefill attention is PyTorch SDPA.
 
 ``DecodeEngine`` adds batched prefill (the same kernels at T tokens per
 stream, causal SDPA, causal depthwise conv) and a CUDA-graph decode loop
@@ -32,7 +33,8 @@ import torch
 import torch.nn.functional as F
 
 from . import _lib
-from .fused_kernels import fused_add_rms_norm, fused_rms_norm, fused_rope_kv_write, fused_silu_mul
+from .fused_kernels import (decode_attention, fused_add_rms_norm, fused_rms_norm, fused_rope_kv_write,
+                            fused_silu_mul, short_conv_step)
 from .model import LFM2Config
 from .positions import learnable_inv_freq
 
@@ -97,12 +99,14 @@ class FusedDecoder:
 
     # ------------------------------------------------------------ decode
     def step(self, input_ids: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor,
-             mask: torch.Tensor) -> torch.Tensor:
+             kv_len: torch.Tensor, mask: torch.Tensor | None = None) -> torch.Tensor:
         """One decode token per stream.
 
-        input_ids [B, 1] int64; positions / slots [B] int64 (angle position and
-        KV slot); mask [B, 1, 1, S] additive (0 = attend).  Returns reduced-head
-        logits [B, 1, num_reduced].
+        input_ids [B, 1] int64; positions / slots / kv_len [B] int64 (angle
+        position, KV slot, number of valid cache slots including this one).
+        ``mask`` is accepted for interface parity with the reference step and
+        ignored: the valid region is the prefix [0, kv_len).  Returns
+        reduced-head logits [B, 1, num_reduced].
         """
         b, hq, hk, d = self.batch, self.hq, self.hk, self.d
         hidden = F.embedding(input_ids, self.embed)              # [B, 1, H] residual stream
@@ -120,11 +124,9 @@ class FusedDecoder:
                     self.k_cache[i], self.v_cache[i], slots, frame_table=self.frame_table,
                     tokens_per_frame=self.cfg.tokens_per_frame, q_norm_w=L["q_norm"], k_norm_w=L["k_norm"],
                     eps=self.eps, err_flag=self.err_flag)
-                # GQA without expansion: the query heads of one KV head become its query rows
-                attn = F.scaled_dot_product_attention(
-                    q_rot.view(b, hk, hq // hk, d), self.k_cache[i], self.v_cache[i], attn_mask=mask,
-                    scale=self.scale)                             # [B, Hk, Hq/Hk, D]
-                delta = F.linear(attn.reshape(b, 1, self.q_dim), L["o"])
+                attn = decode_attention(q_rot, self.k_cache[i], self.v_cache[i], kv_len, self.scale,
+                                        err_flag=self.err_flag)   # [B, Hq, D]
+                delta = F.linear(attn.view(b, 1, self.q_dim), L["o"])
             else:
                 delta = self._conv_step(i, L, normed)
             normed, hidden = fused_add_rms_norm(delta, hidden, L["ffn_norm"], self.eps)
@@ -133,7 +135,12 @@ class FusedDecoder:
         return F.linear(normed, self.head)
 
     def _conv_step(self, i, L, normed):
-        """Short-conv decode step as the reference composes it (optimized_decode.py:256-277)."""
+        """Gated short-conv decode step: in_proj, one fused kernel, out_proj."""
+        y = short_conv_step(F.linear(normed, L["in_proj"]), self.conv_state[i], L["conv_w"])
+        return F.linear(y, L["out_proj"])
+
+    def _conv_step_eager(self, i, L, normed):
+        """The reference's eager composition of the same step (optimized_decode.py:256-277)."""
         bcx = F.linear(normed, L["in_proj"]).transpose(-1, -2)   # [B, 3H, 1]
         bg, c, xc = bcx.chunk(3, dim=-2)
         bx = bg * xc
@@ -198,12 +205,14 @@ class FusedDecoder:
 class DecodeEngine:
     """Prefill + CUDA-graph greedy decode for `batch` independent streams."""
 
-    def __init__(self, decoder: FusedDecoder):
+    def __init__(self, decoder: FusedDecoder, keep_mask: bool = False):
         self.dec = decoder
+        self.keep_mask = keep_mask   # maintain the additive mask (for steps that use one)
         dev, b, s = decoder.device, decoder.batch, decoder.max_len
         self.input_ids = torch.zeros(b, 1, dtype=torch.long, device=dev)
         self.positions = torch.zeros(b, dtype=torch.long, device=dev)
         self.slots = torch.zeros(b, dtype=torch.long, device=dev)
+        self.kv_len = torch.zeros(b, dtype=torch.long, device=dev)
         self.mask = torch.full((b, 1, 1, s), float("-inf"), dtype=torch.bfloat16, device=dev)
         self.step_idx = torch.zeros(1, dtype=torch.long, device=dev)
         self.base_pos = torch.zeros(b, dtype=torch.long, device=dev)
@@ -241,8 +250,10 @@ class DecodeEngine:
         self.positions.copy_(self.base_pos + (torch.div(k, cfg.tokens_per_frame, rounding_mode="floor")
                                               * cfg.audio_step).long())
         self.slots.copy_(self.base_slot + k)
-        self.mask.scatter_(3, self.slots.view(-1, 1, 1, 1), 0.0)
-        self.logits = self.dec.step(self.input_ids, self.positions, self.slots, self.mask)
+        self.kv_len.copy_(self.slots + 1)
+        if self.keep_mask:
+            self.mask.scatter_(3, self.slots.view(-1, 1, 1, 1), 0.0)
+        self.logits = self.dec.step(self.input_ids, self.positions, self.slots, self.kv_len, self.mask)
         nxt = self.dec.reduced_to_full[self.logits[:, 0].argmax(-1)]
         self.generated.index_copy_(1, k, nxt.view(-1, 1))
         self.input_ids.copy_(nxt.view(-1, 1))

@@ -39,6 +39,8 @@ __all__ = [
     "fused_rope",
     "kv_cache_write",
     "fused_rope_kv_write",
+    "decode_attention",
+    "short_conv_step",
 ]
 
 
@@ -352,6 +354,74 @@ def fused_rope_kv_write(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, inv_f
         ptr(k_cache), ptr(v_cache), cs[0], cs[1], cs[2], s_len,
         ptr(wp_c), ptr(flag), stream_ptr(dev)), "kani_rope_kv_write")
     return q_out
+
+
+def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, kv_len: torch.Tensor,
+                     scale: float | None = None, out: torch.Tensor | None = None,
+                     err_flag: torch.Tensor | None = None) -> torch.Tensor:
+    """GQA decode attention of one query token per stream over cache slots [0, kv_len[b]).
+
+    Replaces SDPA over the whole -inf-masked static buffer (optimized_decode.py:243-248).
+        q: [B, Hq, D] or [B, 1, Hq, D] (heads at stride D); k_cache / v_cache: [B, Hk, S, D];
+        kv_len: device int64 [B].  Returns out [B, Hq, D] (or writes ``out``).
+    """
+    for t, w in ((q, "q"), (k_cache, "k_cache"), (v_cache, "v_cache"), (kv_len, "kv_len")):
+        require_cuda(t, w)
+    lib = load_library()
+    code = dtype_code(q, "q")
+    if k_cache.dim() != 4 or v_cache.shape != k_cache.shape or k_cache.stride() != v_cache.stride():
+        raise ValueError("k_cache / v_cache must both be [batch, kv_heads, max_len, head_dim] with equal strides")
+    b, hk, s_len, d = k_cache.shape
+    qv = q.reshape(b, -1, d) if q.is_contiguous() else q
+    if qv.dim() != 3 or qv.shape[0] != b or qv.shape[2] != d or qv.stride(-1) != 1:
+        raise ValueError(f"q must be [{b}, heads, {d}] with a contiguous last dim")
+    hq = qv.shape[1]
+    if hq % hk:
+        raise ValueError(f"{hq} query heads do not group over {hk} KV heads")
+    if not (k_cache.dtype == v_cache.dtype == q.dtype):
+        raise TypeError("q and the caches must share one dtype")
+    if kv_len.dtype != torch.int64 or kv_len.numel() != b:
+        raise ValueError(f"kv_len must be int64 with {b} elements")
+    if out is None:
+        out = torch.empty(b, hq, d, dtype=q.dtype, device=q.device)
+    elif out.numel() != b * hq * d or out.dtype != q.dtype or not out.is_contiguous():
+        raise ValueError(f"out must be a contiguous {q.dtype} tensor of {b * hq * d} elements")
+    ov = out.view(b, hq, d)
+    flag = err_flag if err_flag is not None else error_flag(q.device)
+    cs = k_cache.stride()
+    check(lib.kani_decode_attention(
+        code, b, hq, hk, d, ptr(qv), qv.stride(0), qv.stride(1), ptr(k_cache), ptr(v_cache),
+        cs[0], cs[1], cs[2], s_len, ptr(kv_len.contiguous()),
+        float(d ** -0.5 if scale is None else scale), ptr(ov), ov.stride(0), ov.stride(1), ptr(flag),
+        stream_ptr(q.device)), "kani_decode_attention")
+    return out
+
+
+def short_conv_step(bcx: torch.Tensor, state: torch.Tensor, conv_w: torch.Tensor,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    """LFM2 gated short-conv decode step (optimized_decode.py:256-277, between in_proj
+    and out_proj).  bcx: [B, 1, 3H] or [B, 3H] in_proj output; state: [B, H, L]
+    (updated in place); conv_w: [H, L].  Returns y [B, 1, H] (or [B, H])."""
+    for t, w in ((bcx, "bcx"), (state, "state"), (conv_w, "conv_w")):
+        require_cuda(t, w)
+    lib = load_library()
+    code = dtype_code(bcx, "bcx")
+    if state.dim() != 3 or conv_w.dim() != 2:
+        raise ValueError("state must be [batch, hidden, L] and conv_w [hidden, L]")
+    b, h, lc = state.shape
+    if tuple(conv_w.shape) != (h, lc) or bcx.shape[-1] != 3 * h or bcx.numel() != b * 3 * h:
+        raise ValueError(f"bcx [..., {3 * h}] / conv_w [{h}, {lc}] do not match state {tuple(state.shape)}")
+    if not (state.dtype == conv_w.dtype == bcx.dtype):
+        raise TypeError("bcx, state and conv_w must share one dtype")
+    if state.stride(2) != 1 or state.stride(1) != lc:
+        raise ValueError("state must be contiguous per stream")
+    bv, _, bs = _rows_view(bcx, 3 * h)
+    shape = (*bcx.shape[:-1], h)
+    if out is None:
+        out = torch.empty(shape, dtype=bcx.dtype, device=bcx.device)
+    check(lib.kani_short_conv_step(code, ptr(bv), bs, ptr(state), state.stride(0), ptr(conv_w.contiguous()),
+                                   ptr(out), h, b, h, lc, stream_ptr(bcx.device)), "kani_short_conv_step")
+    return out
 
 
 def launch_count() -> int:

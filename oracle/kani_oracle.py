@@ -209,6 +209,44 @@ def rope_kv_write_ref(q, k, v, inv_freq, positions, k_cache, v_cache, slots, fra
     return q_rot, flags
 
 
+def decode_attention_ref(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, kv_len,
+                         scale: float) -> torch.Tensor:
+    """Decode attention of the reference step (optimized_decode.py:243-248): SDPA of
+    one query per stream over the static buffer with the -inf mask opened on the
+    prefix [0, kv_len[b]) (inference_engine.py:259-265, :643), GQA by head groups.
+    Computed in float64; returned in q's dtype.  q [B, Hq, D]; caches [B, Hk, S, D]."""
+    b, hq, d = q.shape
+    hk = k_cache.shape[1]
+    g = hq // hk
+    out = torch.zeros(b, hq, d, dtype=torch.float64)
+    for s in range(b):
+        n = int(kv_len[s])
+        if n <= 0:
+            continue
+        k = k_cache[s, :, :n].double().repeat_interleave(g, dim=0)    # [Hq, n, D]
+        v = v_cache[s, :, :n].double().repeat_interleave(g, dim=0)
+        sc = torch.einsum("hd,hnd->hn", q[s].double(), k) * scale
+        out[s] = torch.einsum("hn,hnd->hd", torch.softmax(sc, dim=-1), v)
+    return out.to(q.dtype)
+
+
+def short_conv_step_ref(bcx: torch.Tensor, state: torch.Tensor, conv_w: torch.Tensor) -> torch.Tensor:
+    """Gated short-conv decode step, the eager ops of optimized_decode.py:258-276 on
+    bcx [B, 3H] (in_proj output).  Updates `state` [B, H, L] in place; returns
+    y [B, H] (every product rounded to the storage dtype, fp32 sum)."""
+    h = state.shape[1]
+    bg, c, x = bcx[:, :h], bcx[:, h:2 * h], bcx[:, 2 * h:3 * h]
+    bx = bg * x                                         # :261
+    st = state.roll(shifts=-1, dims=-1)                 # :265
+    st[:, :, -1] = bx                                   # :267
+    state.copy_(st)                                     # :268
+    prod = (st * conv_w).float()                        # :270-271, products rounded
+    conv = prod[..., 0]
+    for i in range(1, prod.shape[-1]):
+        conv = conv + prod[..., i]
+    return c * conv.to(bcx.dtype)                       # :275
+
+
 # ------------------------------------------------------ eager compositions
 
 

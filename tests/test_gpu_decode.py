@@ -43,13 +43,10 @@ def test_fused_decoder_matches_reference_decoder_golden():
         dec.v_cache[i].copy_(c[f"v_init_{i}"])
     for i in dec.conv_state:
         dec.conv_state[i].copy_(c[f"conv_init_{i}"])
-    mask = torch.full((1, 1, 1, max_len), float("-inf"), dtype=torch.bfloat16, device=DEV)
-    mask[..., :prefix] = 0
     for step in range(3):
         slot = prefix + step
-        mask[..., slot] = 0
         logits = dec.step(c["tokens"][step].view(1, 1).to(DEV), c["positions"][step:step + 1].to(DEV),
-                          torch.tensor([slot], device=DEV), mask)
+                          torch.tensor([slot], device=DEV), torch.tensor([slot + 1], device=DEV))
         close(logits, c[f"logits_{step}"])
         same_argmax(logits, c[f"logits_{step}"])
     for i in cfg.attn_layers:
@@ -85,7 +82,7 @@ def test_batched_fused_step_matches_oracle(full):
     mask = torch.full((b, 1, 1, max_len), float("-inf"), dtype=torch.bfloat16)
     for s in range(b):
         mask[s, ..., : int(slots[s]) + 1] = 0
-    got = dec.step(ids.to(DEV), pos.to(DEV), slots.to(DEV), mask.to(DEV))
+    got = dec.step(ids.to(DEV), pos.to(DEV), slots.to(DEV), (slots + 1).to(DEV))
     ref = ora.step(ids, pos, slots, mask)
     # at full size 16 layers of bf16 GEMVs accumulate in a different order than on the CPU
     close(got, ref, 0.05 if full else 0.02)
@@ -111,10 +108,8 @@ def test_prefill_matches_token_by_token_decode():
     a = FusedDecoder(cfg, sd, DEV, batch=b, max_len=max_len)
     la = a.prefill(ids, pos)
     s = FusedDecoder(cfg, sd, DEV, batch=b, max_len=max_len)
-    mask = torch.full((b, 1, 1, max_len), float("-inf"), dtype=torch.bfloat16, device=DEV)
     for k in range(t):
-        mask[..., k] = 0
-        ls = s.step(ids[:, k:k + 1], pos[:, k], torch.full((b,), k, device=DEV), mask)
+        ls = s.step(ids[:, k:k + 1], pos[:, k], torch.full((b,), k, device=DEV), torch.full((b,), k + 1, device=DEV))
     close(la, ls, 0.03)
     same_argmax(la, ls)
     for i in cfg.attn_layers:

@@ -547,3 +547,48 @@ def test_in_kernel_cos_sin_match_cuda_math(t):
         dist = ulp(got, ref)
         assert int(dist.max()) <= 1
         assert float((dist != 0).float().mean()) < 1e-4
+
+
+# ------------------------------------------------ decode attention / short conv
+
+
+@pytest.mark.parametrize("b,hq,hk,s_len,lens", [(1, 16, 8, 2048, [1629]), (3, 16, 8, 512, [1, 7, 512]),
+                                                (2, 8, 8, 64, [33, 64]), (2, 16, 4, 300, [250, 9])])
+def test_decode_attention_vs_oracle(b, hq, hk, s_len, lens):
+    d = 64
+    q = rnd((b, hq, d), 1100)
+    kc, vc = rnd((b, hk, s_len, d), 1101), rnd((b, hk, s_len, d), 1102)
+    kv_len = torch.tensor(lens, dtype=torch.long)
+    got = K.decode_attention(gpu(q), gpu(kc), gpu(vc), gpu(kv_len))
+    ref = O.decode_attention_ref(q, kc, vc, kv_len, d ** -0.5)
+    assert_close_ulp(got, ref, 2, 0.95)            # fp32 online softmax vs float64, one rounding each
+    assert _lib.read_and_clear_errors(DEV) == 0
+
+
+def test_decode_attention_ignores_slots_past_the_prefix_and_flags_overflow():
+    b, hq, hk, s_len, d = 2, 16, 8, 128, 64
+    q = rnd((b, hq, d), 1110)
+    kc, vc = rnd((b, hk, s_len, d), 1111), rnd((b, hk, s_len, d), 1112)
+    kv_len = torch.tensor([40, 128])
+    got = K.decode_attention(gpu(q), gpu(kc), gpu(vc), gpu(kv_len))
+    kc2, vc2 = kc.clone(), vc.clone()
+    kc2[0, :, 40:] = 1e4                           # garbage beyond the prefix must not matter
+    vc2[0, :, 40:] = -1e4
+    got2 = K.decode_attention(gpu(q), gpu(kc2), gpu(vc2), gpu(kv_len))
+    assert torch.equal(got.cpu(), got2.cpu())
+    K.decode_attention(gpu(q), gpu(kc), gpu(vc), gpu(torch.tensor([40, 129])))
+    assert _lib.read_and_clear_errors(DEV) == _lib.KANI_FLAG_SLOT_OOB
+
+
+@pytest.mark.parametrize("b,h", [(1, 1024), (64, 1024), (3, 256)])
+def test_short_conv_step_bit_exact_vs_eager(b, h):
+    bcx = rnd((b, 3 * h), 1200)
+    state = rnd((b, h, 3), 1201)
+    w = rnd((h, 3), 1202, std=0.3)
+    st_gpu = gpu(state)
+    y = K.short_conv_step(gpu(bcx), st_gpu, gpu(w))
+    st_ref = state.clone()
+    y_ref = O.short_conv_step_ref(bcx, st_ref, w)
+    assert torch.equal(st_gpu.cpu(), st_ref)
+    assert int(ulp(y, y_ref).max()) <= 1            # three-term fp32 sum order
+    assert float((ulp(y, y_ref) == 0).float().mean()) > 0.999

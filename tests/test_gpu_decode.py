@@ -89,11 +89,12 @@ def test_batched_fused_step_matches_oracle(full):
     cos = torch.nn.functional.cosine_similarity(got.float().cpu().flatten(1), ref.float().flatten(1))
     assert float(cos.min()) > 0.999
     same_argmax(got, ref)
+    tol = 0.05 if full else 0.02
     for i in cfg.attn_layers:
         for s in range(b):
             sl = int(slots[s])
-            close(dec.k_cache[i][s, :, sl], ora.k_cache[i][s, :, sl])
-            close(dec.v_cache[i][s, :, sl], ora.v_cache[i][s, :, sl])
+            close(dec.k_cache[i][s, :, sl], ora.k_cache[i][s, :, sl], tol)
+            close(dec.v_cache[i][s, :, sl], ora.v_cache[i][s, :, sl], tol)
 
 
 def test_prefill_matches_token_by_token_decode():

@@ -108,17 +108,15 @@ def _dist_init():
 
 def _barrier(world):
     if world > 1:
-        import torch.distributed as dist
-        dist.barrier()
+        from kani_tts_b200.replicas import barrier
+        barrier()
 
 
 def _max_over_ranks(x: float, world: int, dev) -> float:
     if world == 1:
         return x
-    import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device=dev)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    from kani_tts_b200.replicas import max_over_ranks
+    return max_over_ranks(x, dev)
 
 
 # ------------------------------------------------------------------ clocks

@@ -569,10 +569,11 @@ rope_token_kernel(RopeParams p, int log2l) {
 // Long calls (prefill-sized token counts).  One CTA of kBulkTPS warps per
 // group of kBulkTPS tokens; the hardware block scheduler balances the groups
 // over the SMs.  Thread 0 brings the group's Q, K and V rows into shared
-// memory with TMA bulk copies (cp.async.bulk, completion on one mbarrier, no
-// multicast) and pulls the CTA's share of the frame table into L2; shared
-// memory, not registers, holds the bytes in flight, and each warp fetches
-// its token's position, slot and frame row while the rows stream in.  Each warp
+// memory with plain TMA bulk copies (cp.async.bulk completing on one
+// mbarrier; every copy targets this CTA only) and pulls the CTA's share of
+// the frame table into L2; shared memory, not registers, holds the bytes in
+// flight, and each warp fetches its token's position, slot and frame row
+// while the rows stream in.  Each warp
 // then owns one whole token: its lanes carry QI Q heads, KI K heads and KI V
 // heads that all use the same E frequencies, so the sin/cos, their shuffles
 // and the token metadata are computed once per token.  The mbarrier wait is

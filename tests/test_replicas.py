@@ -1,0 +1,68 @@
+"""The multi-GPU path is independent replicas; its host-side pieces (stream
+sharding, max / sum aggregation of timings and work) run here as two gloo
+ranks on the CPU."""
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch.multiprocessing as mp
+
+from kani_tts_b200.replicas import aggregate_throughput, max_over_ranks, stream_shard
+
+
+def test_stream_shard_partitions_all_streams():
+    for total in (0, 1, 63, 64, 128, 512, 513):
+        for world in (1, 2, 3, 4, 8):
+            shards = [stream_shard(total, world, r) for r in range(world)]
+            ids = [i for s in shards for i in s]
+            assert ids == list(range(total))
+            sizes = [len(s) for s in shards]
+            assert max(sizes) - min(sizes) <= 1
+    with pytest.raises(ValueError):
+        stream_shard(8, 2, 2)
+
+
+def test_single_process_aggregation_is_identity():
+    assert max_over_ranks(3.5) == 3.5
+    assert aggregate_throughput(64 * 1500, 2.0) == (96000.0, 2.0, 48000.0)
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        shard = stream_shard(64 * world, world, rank)
+        # rank r "processes" its shard in (r + 1) seconds
+        total, slowest, rate = aggregate_throughput(len(shard) * 1500, float(rank + 1))
+        q.put((rank, list(shard)[:1], len(shard), total, slowest, rate))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gloo_ranks_aggregate_like_the_bench():
+    world, port = 2, _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    res = sorted(q.get(timeout=10) for _ in range(world))
+    assert [r[1] for r in res] == [[0], [64]]           # disjoint shards of 64 streams
+    for _, _, n, total, slowest, rate in res:
+        assert n == 64
+        assert total == 2 * 64 * 1500
+        assert slowest == 2.0                            # max over ranks
+        assert rate == total / 2.0

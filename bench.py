@@ -303,33 +303,61 @@ def run_reference(args, world, rank):
 # ------------------------------------------------------------- GPU arm
 
 def run_e2e(K, dev, steps: int) -> dict:
-    """Public API with pinned host buffers: H2D inputs, kernel, D2H results."""
+    """Public API with pinned host buffers, every step: H2D of the step's inputs
+    (Q, K, V, positions, slots), the kernel, D2H of its results (rotated Q and
+    the written K/V cache slots).  Steps are pipelined over two buffer sets and
+    three streams (copy-in, compute, copy-out) so that one step's H2D overlaps
+    the previous step's D2H (PCIe is full duplex); events order every buffer
+    reuse."""
     host = make_inputs(1)
     pin = {n: host[n].pin_memory() for n in ("q", "k", "v", "pos", "slots")}
-    devs = make_inputs(1, device=dev)
-    q_host = torch.empty(T_TOK, HQ, D, dtype=torch.bfloat16).pin_memory()
-    kv_host = torch.empty(2, HK, T_TOK, D, dtype=torch.bfloat16).pin_memory()
-    q_out = torch.empty(1, T_TOK, HQ, D, dtype=torch.bfloat16, device=dev)
+    nbuf = 2
+    devs = [make_inputs(1, device=dev) for _ in range(nbuf)]
+    q_out = [torch.empty(1, T_TOK, HQ, D, dtype=torch.bfloat16, device=dev) for _ in range(nbuf)]
+    q_host = [torch.empty(T_TOK, HQ, D, dtype=torch.bfloat16).pin_memory() for _ in range(nbuf)]
+    kv_host = [torch.empty(2, HK, T_TOK, D, dtype=torch.bfloat16).pin_memory() for _ in range(nbuf)]
     h2d = sum(pin[n].numel() * pin[n].element_size() for n in pin)
-    d2h = q_host.numel() * 2 + kv_host.numel() * 2
-    st = torch.cuda.current_stream(dev)
+    d2h = q_host[0].numel() * 2 + kv_host[0].numel() * 2
+    s_in, s_comp, s_out = (torch.cuda.Stream(device=dev) for _ in range(3))
+    ev = lambda: torch.cuda.Event()  # noqa: E731
+    in_done = [ev() for _ in range(nbuf)]
+    comp_done = [ev() for _ in range(nbuf)]
+    out_done = [ev() for _ in range(nbuf)]
+    used = [False] * nbuf
 
-    def step():
-        for n in pin:
-            devs[n].copy_(pin[n], non_blocking=True)
-        launch(K, devs, q_out)
-        q_host.copy_(q_out.view(T_TOK, HQ, D), non_blocking=True)
-        kv_host[0].copy_(devs["kc"][0, :, :T_TOK], non_blocking=True)
-        kv_host[1].copy_(devs["vc"][0, :, :T_TOK], non_blocking=True)
+    def step(i):
+        j = i % nbuf
+        d = devs[j]
+        with torch.cuda.stream(s_in):
+            if used[j]:
+                s_in.wait_event(comp_done[j])      # inputs of buffer j no longer read
+            for n in pin:
+                d[n].copy_(pin[n], non_blocking=True)
+            in_done[j].record(s_in)
+        with torch.cuda.stream(s_comp):
+            s_comp.wait_event(in_done[j])
+            if used[j]:
+                s_comp.wait_event(out_done[j])     # results of buffer j already read back
+            launch(K, d, q_out[j])
+            comp_done[j].record(s_comp)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(comp_done[j])
+            q_host[j].copy_(q_out[j].view(T_TOK, HQ, D), non_blocking=True)
+            kv_host[j][0].copy_(d["kc"][0, :, :T_TOK], non_blocking=True)
+            kv_host[j][1].copy_(d["vc"][0, :, :T_TOK], non_blocking=True)
+            out_done[j].record(s_out)
+        used[j] = True
 
-    for _ in range(3):
-        step()
+    for i in range(4):
+        step(i)
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(st)
-    for _ in range(steps):
-        step()
-    e1.record(st)
+    e0.record(s_in)
+    for i in range(steps):
+        step(i)
+    s_out.wait_stream(s_in)
+    s_out.wait_stream(s_comp)
+    e1.record(s_out)
     torch.cuda.synchronize(dev)
     el = e0.elapsed_time(e1) / 1e3
     return {"seconds": el, "steps": steps, "h2d": h2d, "d2h": d2h}
@@ -547,7 +575,8 @@ def run_gpu(args, world, rank, local):
     e2e_line = {"value": round(world * e["steps"] * STEP_BYTES / e_max / 1e9, 3), "unit": UNIT,
                 "h2d_bytes_per_step": e["h2d"], "d2h_bytes_per_step": e["d2h"], "steps": e["steps"],
                 "ms_per_step": round(e_max / e["steps"] * 1e3, 4),
-                "path": "kani_tts_b200.fused_rope_kv_write (ctypes -> kani_rope_kv_write), pinned host buffers"}
+                "path": ("kani_tts_b200.fused_rope_kv_write (ctypes -> kani_rope_kv_write), pinned host "
+                         "buffers, copy-in / compute / copy-out streams over two buffer sets")}
     if not args.no_decode:
         # decode steps: bs=1 (with the eager reference-structure arm) and 64 streams per GPU
         extras["decode"] = {"bs1": run_decode(dev, world, rank, 1, args.decode_steps, eager=True),
@@ -572,7 +601,7 @@ def run_gpu(args, world, rank, local):
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": traffic,
                      "algorithmic_bytes": STEP_BYTES,
-                     "kernel": "rope_vec_kernel<bf16, norm=0, table=1, cs_given=0>"},
+                     "kernel": "rope_bulk_kernel<bf16, NORM=0, TABLE=1, QI=2, KI=1, LOG2L=2>"},
         "e2e": e2e_line,
         "gpu_launches": args.steps,
         "graph_launches_captured": captured,

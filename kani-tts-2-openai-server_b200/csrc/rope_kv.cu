@@ -135,8 +135,6 @@ __device__ __forceinline__ float rrms_of(float ss, int n, float eps) {
 template <typename T, bool NORM, bool TABLE, bool CS_GIVEN>
 __global__ void __launch_bounds__(256, NORM ? 3 : 4)
 rope_vec_kernel(RopeParams p, int log2l, int ipt, int iptr, int tpb) {
-  griddep_launch_dependents();
-  griddep_wait();
   constexpr int E = VecN<T>::value;
   const int L = 1 << log2l;
   const int half = p.d >> 1;
@@ -478,8 +476,6 @@ __device__ __forceinline__ void rope_chunk_store(uint4 xlo, uint4 xhi, bool live
 template <typename T, bool NORM, bool TABLE, int QI, int KI>
 __global__ void __launch_bounds__(256)
 rope_token_kernel(RopeParams p, int log2l) {
-  griddep_launch_dependents();
-  griddep_wait();
   constexpr int E = VecN<T>::value;
   constexpr int NI = QI > KI ? QI : KI;
   const int L = 1 << log2l;
@@ -664,10 +660,6 @@ rope_bulk_kernel(RopeParams p, int log2l_rt) {
   const int cnt = (int)(p.n_tokens - t0 < kBulkTPS ? p.n_tokens - t0 : kBulkTPS);
   const uint32_t bar = smem_u32(&bar_storage);
 
-  // launched as a programmatic dependent: let the next launch schedule early,
-  // and read nothing global before the previous grid has completed
-  griddep_launch_dependents();
-  griddep_wait();
   if (tid == 0) {
     mbar_init(bar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -795,7 +787,7 @@ int launch_bulk(const RopeParams& p, int log2l, cudaStream_t s) {
   }
   const int64_t grid = (p.n_tokens + kBulkTPS - 1) / kBulkTPS;
   if (grid > 0x7fffffff) return KANI_ERR_UNSUPPORTED;
-  launch_pdl(kern, dim3((unsigned)grid), dim3(kBulkTPS * 32), smem, s, p, log2l);
+  kern<<<(unsigned)grid, kBulkTPS * 32, smem, s>>>(p, log2l);
   return launch_status();
 }
 
@@ -803,8 +795,6 @@ int launch_bulk(const RopeParams& p, int log2l, cudaStream_t s) {
 template <typename T, bool NORM, bool TABLE, bool CS_GIVEN>
 __global__ void __launch_bounds__(256)
 rope_generic_kernel(RopeParams p, int heads_per_tok) {
-  griddep_launch_dependents();
-  griddep_wait();
   const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (gw >= p.n_tokens * heads_per_tok) return;  // warp-uniform exit
@@ -884,8 +874,6 @@ __global__ void __launch_bounds__(256)
 kv_write_kernel(const T* __restrict__ k, const T* __restrict__ v, int64_t batch, int hk, int d,
                 T* kc, T* vc, int64_t clen, const int64_t* __restrict__ wp, int per_stream,
                 int32_t* err) {
-  griddep_launch_dependents();
-  griddep_wait();
   constexpr int E = VEC ? VecN<T>::value : 1;
   const int vpr = d / E;
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -959,11 +947,11 @@ int launch_rope_t(const RopeParams& p, cudaStream_t s) {
       if (grid <= 0x7fffffff) {
         const dim3 blk((unsigned)(64 * tpb));
         if (p.hq <= 2 * G && p.hk <= G) {
-          launch_pdl(rope_token_kernel<T, NORM, TABLE, 2, 1>, dim3((unsigned)grid), dim3(blk), 0, s, p, log2l);
+          rope_token_kernel<T, NORM, TABLE, 2, 1><<<(unsigned)grid, blk, 0, s>>>(p, log2l);
           return launch_status();
         }
         if (p.hq <= 4 * G && p.hk <= 2 * G) {
-          launch_pdl(rope_token_kernel<T, NORM, TABLE, 4, 2>, dim3((unsigned)grid), dim3(blk), 0, s, p, log2l);
+          rope_token_kernel<T, NORM, TABLE, 4, 2><<<(unsigned)grid, blk, 0, s>>>(p, log2l);
           return launch_status();
         }
       }
@@ -978,7 +966,8 @@ int launch_rope_t(const RopeParams& p, cudaStream_t s) {
       if (tpb > p.n_tokens) tpb = (int)p.n_tokens;
       const int64_t grid = (p.n_tokens + tpb - 1) / tpb;
       if (grid <= 0x7fffffff) {
-        launch_pdl(rope_vec_kernel<T, NORM, TABLE, CS_GIVEN>, dim3((unsigned)grid), dim3(tpb * iptr), 0, s, p, log2l, ipt, iptr, tpb);
+        rope_vec_kernel<T, NORM, TABLE, CS_GIVEN>
+            <<<(unsigned)grid, tpb * iptr, 0, s>>>(p, log2l, ipt, iptr, tpb);
         return launch_status();
       }
     }
@@ -987,7 +976,7 @@ int launch_rope_t(const RopeParams& p, cudaStream_t s) {
   const int64_t warps = p.n_tokens * heads;
   const int64_t grid = (warps + 7) / 8;
   if (grid > 0x7fffffff) return KANI_ERR_UNSUPPORTED;
-  launch_pdl(rope_generic_kernel<T, NORM, TABLE, CS_GIVEN>, dim3((unsigned)grid), dim3(256), 0, s, p, heads);
+  rope_generic_kernel<T, NORM, TABLE, CS_GIVEN><<<(unsigned)grid, 256, 0, s>>>(p, heads);
   return launch_status();
 }
 
@@ -1069,11 +1058,13 @@ extern "C" int kani_kv_cache_write(int32_t dtype, const void* k, const void* v, 
     const int64_t grid = (total + 255) / 256;
     if (grid > 0x7fffffff) return (int)KANI_ERR_UNSUPPORTED;
     if (vec)
-      kani::launch_pdl(kani::kv_write_kernel<T, true>, dim3((unsigned)grid), dim3(256), 0, s, static_cast<const T*>(k), static_cast<const T*>(v), batch, num_kv_heads, head_dim,
+      kani::kv_write_kernel<T, true><<<(unsigned)grid, 256, 0, s>>>(
+          static_cast<const T*>(k), static_cast<const T*>(v), batch, num_kv_heads, head_dim,
           static_cast<T*>(k_cache), static_cast<T*>(v_cache), cache_len, write_pos,
           per_stream_pos, err_flag);
     else
-      kani::launch_pdl(kani::kv_write_kernel<T, false>, dim3((unsigned)grid), dim3(256), 0, s, static_cast<const T*>(k), static_cast<const T*>(v), batch, num_kv_heads, head_dim,
+      kani::kv_write_kernel<T, false><<<(unsigned)grid, 256, 0, s>>>(
+          static_cast<const T*>(k), static_cast<const T*>(v), batch, num_kv_heads, head_dim,
           static_cast<T*>(k_cache), static_cast<T*>(v_cache), cache_len, write_pos,
           per_stream_pos, err_flag);
     return kani::launch_status();

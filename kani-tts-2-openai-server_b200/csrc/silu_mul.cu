@@ -29,8 +29,6 @@ template <typename T, int RY>
 __global__ void __launch_bounds__(256)
 silu_mul_vec_kernel(const T* __restrict__ gu, int64_t in_stride, T* __restrict__ y,
                     int64_t out_stride, int64_t rows, int vpr, int64_t n) {
-  griddep_launch_dependents();
-  griddep_wait();
   constexpr int E = VecN<T>::value;
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= vpr) return;
@@ -64,8 +62,6 @@ template <typename T>
 __global__ void __launch_bounds__(256)
 silu_mul_generic_kernel(const T* __restrict__ gu, int64_t in_stride, T* __restrict__ y,
                         int64_t out_stride, int64_t rows, int64_t n) {
-  griddep_launch_dependents();
-  griddep_wait();
   const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= n) return;
   for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {
@@ -98,17 +94,20 @@ int launch_silu(const void* gu, int64_t in_stride, void* y, int64_t out_stride, 
     const int64_t groups = (rows + RY - 1) / RY;
     const unsigned gy = (unsigned)(groups < 65535 ? groups : 65535);
     if (rows >= RY) {
-      launch_pdl(silu_mul_vec_kernel<T, RY>, dim3(gx, gy), dim3(bx), 0, s, static_cast<const T*>(gu), in_stride, static_cast<T*>(y), out_stride, rows, vpr, n);
+      silu_mul_vec_kernel<T, RY><<<dim3(gx, gy), bx, 0, s>>>(
+          static_cast<const T*>(gu), in_stride, static_cast<T*>(y), out_stride, rows, vpr, n);
     } else {
       const unsigned gy1 = (unsigned)rows;
-      launch_pdl(silu_mul_vec_kernel<T, 1>, dim3(gx, gy1), dim3(bx), 0, s, static_cast<const T*>(gu), in_stride, static_cast<T*>(y), out_stride, rows, vpr, n);
+      silu_mul_vec_kernel<T, 1><<<dim3(gx, gy1), bx, 0, s>>>(
+          static_cast<const T*>(gu), in_stride, static_cast<T*>(y), out_stride, rows, vpr, n);
     }
     return launch_status();
   }
   const int64_t gx64 = (n + 255) / 256;
   if (gx64 > 0x7fffffff) return KANI_ERR_UNSUPPORTED;
   const unsigned gy = (unsigned)(rows < 65535 ? rows : 65535);
-  launch_pdl(silu_mul_generic_kernel<T>, dim3((unsigned)gx64, gy), dim3(256), 0, s, static_cast<const T*>(gu), in_stride, static_cast<T*>(y), out_stride, rows, n);
+  silu_mul_generic_kernel<T><<<dim3((unsigned)gx64, gy), 256, 0, s>>>(
+      static_cast<const T*>(gu), in_stride, static_cast<T*>(y), out_stride, rows, n);
   return launch_status();
 }
 

@@ -11,6 +11,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "kani_b200.h"
 
 namespace kani {
@@ -178,6 +180,34 @@ int dispatch_dtype(int32_t code, F&& f) {
     case KANI_DTYPE_F16: return f.template operator()<__half>();
     default: return KANI_ERR_DTYPE;
   }
+}
+
+// Programmatic dependent launch.  A kernel launched with launch_pdl may start
+// while the kernel before it in the stream is still finishing; it must call
+// griddep_wait() before it touches global memory that kernel may have
+// written (the wait returns once the earlier grid has completed and its
+// writes are visible).  griddep_launch_dependents() lets the next launch's
+// blocks be scheduled before this grid ends.  Both are no-ops when there is
+// no programmatic dependency.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 inline int launch_status() {

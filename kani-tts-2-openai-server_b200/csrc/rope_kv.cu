@@ -660,6 +660,10 @@ rope_bulk_kernel(RopeParams p, int log2l_rt) {
   const int cnt = (int)(p.n_tokens - t0 < kBulkTPS ? p.n_tokens - t0 : kBulkTPS);
   const uint32_t bar = smem_u32(&bar_storage);
 
+  // launched as a programmatic dependent: let the next launch schedule early,
+  // and read nothing global before the previous grid has completed
+  griddep_launch_dependents();
+  griddep_wait();
   if (tid == 0) {
     mbar_init(bar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -787,7 +791,7 @@ int launch_bulk(const RopeParams& p, int log2l, cudaStream_t s) {
   }
   const int64_t grid = (p.n_tokens + kBulkTPS - 1) / kBulkTPS;
   if (grid > 0x7fffffff) return KANI_ERR_UNSUPPORTED;
-  kern<<<(unsigned)grid, kBulkTPS * 32, smem, s>>>(p, log2l);
+  launch_pdl(kern, dim3((unsigned)grid), dim3(kBulkTPS * 32), smem, s, p, log2l);
   return launch_status();
 }
 

@@ -614,6 +614,51 @@ def run_gpu(args, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
+def run_op(name: str, size: int, steps: int, warmup: int) -> dict:
+    """Profiling aid: one fused op alone at one size, eager launches, seeded inputs."""
+    from kani_tts_b200 import fused_kernels as K
+    dev = torch.device("cuda", 0)
+    g = torch.Generator().manual_seed(0)
+    bf = torch.bfloat16
+
+    def rn(*shape):
+        return torch.randn(*shape, generator=g).to(bf).to(dev)
+    if name == "silu_mul":
+        x, y = rn(size, 9216), torch.empty(size, 4608, dtype=bf, device=dev)
+        fn, nbytes = (lambda: K.fused_silu_mul(x, out=y)), size * 27648
+    elif name == "add_rms_norm":
+        x, r, w = rn(size, 1024), rn(size, 1024), rn(1024)
+        o, h = torch.empty_like(x), torch.empty_like(x)
+        fn, nbytes = (lambda: K.fused_add_rms_norm(x, r, w, 1e-5, out=o, residual_out=h)), size * 1024 * 8 + 2048
+    elif name == "rope_kv_write":
+        st = make_inputs(0, size, dev)
+        qo = torch.empty(1, size, HQ, D, dtype=bf, device=dev)
+        fn, nbytes = (lambda: launch(K, st, qo)), size * BYTES_PER_TOKEN
+    elif name == "decode_attention":          # size = streams, 1629 valid slots of 2048
+        q, kc, vc = rn(size, HQ, D), rn(size, HK, 2048, D), rn(size, HK, 2048, D)
+        kv_len = torch.full((size,), 1629, dtype=torch.long, device=dev)
+        out = torch.empty(size, HQ, D, dtype=bf, device=dev)
+        fn, nbytes = (lambda: K.decode_attention(q, kc, vc, kv_len, out=out)), size * (2 * HK * 1629 * D * 2 + 2 * HQ * D * 2)
+    elif name == "short_conv":               # size = streams, hidden 1024, L = 3
+        bcx, stt, w = rn(size, 3 * 1024), rn(size, 1024, 3), rn(1024, 3)
+        y = torch.empty(size, 1024, dtype=bf, device=dev)
+        fn, nbytes = (lambda: K.short_conv_step(bcx, stt, w, out=y)), size * 1024 * 2 * (3 + 3 + 3 + 1) + 1024 * 6
+    else:
+        raise SystemExit(f"unknown op {name}")
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    us = e0.elapsed_time(e1) * 1e3 / steps
+    return {"op": name, "size": size, "us_per_call_eager": round(us, 3), "bytes": nbytes,
+            "GB_s": round(nbytes / us / 1e3, 1)}
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -626,10 +671,16 @@ def main():
     ap.add_argument("--decode-steps", type=int, default=1500)
     ap.add_argument("--decode-only", action="store_true", help="profiling aid: run only the decode arms")
     ap.add_argument("--decode-batch", type=int, default=1, help="streams for --decode-only")
+    ap.add_argument("--op", default=None, help="profiling aid: run one fused op alone "
+                    "(silu_mul, add_rms_norm, rope_kv_write, decode_attention, short_conv)")
+    ap.add_argument("--size", type=int, default=4096, help="rows / tokens / streams for --op")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.op:
+        print(json.dumps(run_op(args.op, args.size, args.steps, args.warmup)), flush=True)
+        return
     if args.decode_only:
         # profiling aid: only the bs=1 decode arms, one JSON line with the decode results
         world, rank, local = _dist_init()

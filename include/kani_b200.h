@@ -205,7 +205,8 @@ KANI_API int kani_decode_attention(int32_t dtype, int64_t batch, int32_t num_q_h
  * Replaces kani_tts/optimized_decode.py:256-277 (between in_proj and out_proj).
  *   bcx: [batch, 3*hidden] (row stride); state: [batch, hidden, kernel_len]
  *   (batch stride, contiguous per stream); conv_w: [hidden, kernel_len];
- *   y: [batch, hidden] (row stride).  kernel_len in 2..4.
+ *   y: [batch, hidden] (row stride).  kernel_len in 2..4; all four buffers and
+ *   the row / batch strides 16-byte aligned (KANI_ERR_UNSUPPORTED otherwise).
  */
 KANI_API int kani_short_conv_step(int32_t dtype, const void* bcx, int64_t bcx_row_stride,
                          void* state, int64_t state_batch_stride, const void* conv_w,

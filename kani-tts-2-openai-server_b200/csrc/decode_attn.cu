@@ -19,7 +19,9 @@
 // through shared memory, and across the cluster through distributed shared
 // memory by CTA rank 0, which writes the normalised output with one
 // rounding.  No global scratch is used; the two cluster barriers are
-// hardware barriers that every CTA of the cluster reaches.
+// hardware barriers that every CTA of the cluster reaches.  With contiguous
+// cache rows the K/V range is staged by TMA (decode_attn_kernel below);
+// otherwise the register variant reads it directly.
 #include <cooperative_groups.h>
 
 #include "common.cuh"
@@ -52,7 +54,7 @@ __device__ __forceinline__ float merge_weight(float m, float mnew) {
 
 template <typename T, int G, int D>
 __global__ void __cluster_dims__(kClusterCTAs, 1, 1) __launch_bounds__(kAttnThreads)
-decode_attn_kernel(AttnParams p) {
+decode_attn_reg_kernel(AttnParams p) {
   constexpr int DL = D / 4;           // dims per lane
   constexpr int VE = VecN<T>::value;  // elements per 16-byte vector
   constexpr int NV = DL / VE;         // 16-byte vectors per lane per row
@@ -215,10 +217,289 @@ decode_attn_kernel(AttnParams p) {
   cluster.sync();  // rank 0 has read the other CTAs' shared memory
 }
 
+// ------------------------------------------------------- TMA-staged variant
+// Same math and lane layout; the CTA's key range is brought into a ring of
+// kAttnStages shared-memory stages of kAttnTile keys (K tile + V tile) by TMA
+// bulk copies completing on one mbarrier per stage (plain bulk copies, each
+// targeting this CTA only), so the bytes in flight are bounded by shared
+// memory instead of registers.  Needs contiguous cache rows (slot stride ==
+// head_dim).  Each lane takes two keys per tile pass and rescales its running
+// sums once per pair.  Waits are bounded (KANI_FLAG_TIMEOUT); a CTA that
+// times out contributes an empty partial and still reaches both cluster
+// barriers.
+constexpr int kAttnTile = 64;
+constexpr int kAttnStages = 4;
+constexpr long long kAttnWaitCycles = 2000000000LL;  // ~1 s
+
+__device__ __forceinline__ uint32_t attn_smem_u32(const void* ptr) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(ptr));
+}
+
+__device__ __forceinline__ bool attn_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(1000000u)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool attn_wait_bounded(uint32_t bar, uint32_t parity) {
+  if (attn_try_wait(bar, parity)) return true;
+  const long long start = clock64();
+  while (!attn_try_wait(bar, parity)) {
+    if (clock64() - start > kAttnWaitCycles) return false;
+  }
+  return true;
+}
+
+template <typename T, int G, int D>
+__global__ void __cluster_dims__(kClusterCTAs, 1, 1) __launch_bounds__(kAttnThreads)
+decode_attn_kernel(AttnParams p) {
+  constexpr int DL = D / 4;
+  constexpr int VE = VecN<T>::value;
+  constexpr int NV = DL / VE;
+  constexpr int NW = kAttnThreads / 32;
+  constexpr uint32_t ROW = D * sizeof(T);
+  constexpr uint32_t TILE_BYTES = kAttnTile * ROW;
+  extern __shared__ __align__(128) unsigned char ring[];  // [stage][K tile | V tile]
+  __shared__ __align__(8) uint64_t bars[kAttnStages];
+  __shared__ float w_m[NW][G], w_l[NW][G];
+  __shared__ float w_acc[NW][G][D];
+  __shared__ float c_m[G], c_l[G];
+  __shared__ float c_acc[G][D];
+
+  cg::cluster_group cluster = cg::this_cluster();
+  const int crank = (int)cluster.block_rank();
+  const int h = blockIdx.y;
+  const int b = blockIdx.z;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int kg = lane >> 2, ds = lane & 3;
+
+  int64_t len = p.kv_len[b];
+  if (len > p.cache_len) {
+    if (crank == 0 && tid == 0 && h == 0 && p.err != nullptr) atomicOr(p.err, KANI_FLAG_SLOT_OOB);
+    len = p.cache_len;
+  }
+  if (len < 0) len = 0;
+  const int64_t chunk = (len + kClusterCTAs - 1) / kClusterCTAs;
+  const int64_t k0 = crank * chunk;
+  const int64_t k1 = k0 + chunk < len ? k0 + chunk : len;
+  const int n = k1 > k0 ? (int)(k1 - k0) : 0;
+  const int ntiles = (n + kAttnTile - 1) / kAttnTile;
+  const char* kb = reinterpret_cast<const char*>(static_cast<const T*>(p.k) + b * p.cb + (int64_t)h * p.ch + k0 * p.cs);
+  const char* vb = reinterpret_cast<const char*>(static_cast<const T*>(p.v) + b * p.cb + (int64_t)h * p.ch + k0 * p.cs);
+
+  auto issue = [&](int t) {  // thread 0: tile t into stage t % kAttnStages
+    const int st = t % kAttnStages;
+    const int rows = n - t * kAttnTile < kAttnTile ? n - t * kAttnTile : kAttnTile;
+    const uint32_t bytes = (uint32_t)rows * ROW;
+    const uint32_t bar = attn_smem_u32(&bars[st]);
+    const uint32_t dst = attn_smem_u32(ring + (size_t)st * 2 * TILE_BYTES);
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(2 * bytes) : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(kb + (int64_t)t * TILE_BYTES), "r"(bytes), "r"(bar) : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     dst + TILE_BYTES),
+                 "l"(vb + (int64_t)t * TILE_BYTES), "r"(bytes), "r"(bar) : "memory");
+  };
+  if (tid == 0) {
+    for (int st = 0; st < kAttnStages; ++st)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(attn_smem_u32(&bars[st])), "r"(1) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    for (int t = 0; t < ntiles && t < kAttnStages; ++t) issue(t);
+  }
+
+  // query heads (global) while the first tiles stream in
+  float q[G][DL];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const T* qp = static_cast<const T*>(p.q) + b * p.qb + (int64_t)(h * G + g) * p.qh + ds * DL;
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      float f[VE];
+      unpack16<T>(ld16(qp + v * VE), f);
+#pragma unroll
+      for (int e = 0; e < VE; ++e) q[g][v * VE + e] = f[e] * p.qscale;
+    }
+  }
+  float m[G], l[G], acc[G][DL];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+#pragma unroll
+    for (int d = 0; d < DL; ++d) acc[g][d] = 0.f;
+  }
+  __syncthreads();  // barriers initialised
+
+  bool failed = false;
+  int t_fail = ntiles;
+  for (int t = 0; t < ntiles; ++t) {
+    const int st = t % kAttnStages;
+    if (!failed && !attn_wait_bounded(attn_smem_u32(&bars[st]), (uint32_t)((t / kAttnStages) & 1))) {
+      failed = true;
+      t_fail = t;
+      if (lane == 0 && p.err != nullptr) atomicOr(p.err, KANI_FLAG_TIMEOUT);
+    }
+    const int rows = n - t * kAttnTile < kAttnTile ? n - t * kAttnTile : kAttnTile;
+    const T* ktile = reinterpret_cast<const T*>(ring + (size_t)st * 2 * TILE_BYTES);
+    const T* vtile = reinterpret_cast<const T*>(ring + (size_t)st * 2 * TILE_BYTES + TILE_BYTES);
+    // two keys per lane group per pass: r0 and r0 + 8*NW
+#pragma unroll 1
+    for (int base = warp * 8; base < kAttnTile; base += 16 * NW) {
+      const int r0 = base + kg, r1 = base + kg + 8 * NW;
+      const bool v0 = !failed && r0 < rows, v1 = !failed && r1 < rows;
+      float k0f[DL], k1f[DL];
+#pragma unroll
+      for (int v = 0; v < NV; ++v) {
+        unpack16<T>(v0 ? ld16(ktile + r0 * D + ds * DL + v * VE) : make_uint4(0, 0, 0, 0), k0f + v * VE);
+        unpack16<T>(v1 ? ld16(ktile + r1 * D + ds * DL + v * VE) : make_uint4(0, 0, 0, 0), k1f + v * VE);
+      }
+      float s0[G], s1[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+        for (int d = 0; d < DL; ++d) {
+          a0 = fmaf(q[g][d], k0f[d], a0);
+          a1 = fmaf(q[g][d], k1f[d], a1);
+        }
+        a0 += __shfl_xor_sync(0xffffffffu, a0, 1);
+        a1 += __shfl_xor_sync(0xffffffffu, a1, 1);
+        a0 += __shfl_xor_sync(0xffffffffu, a0, 2);
+        a1 += __shfl_xor_sync(0xffffffffu, a1, 2);
+        s0[g] = v0 ? a0 : -INFINITY;
+        s1[g] = v1 ? a1 : -INFINITY;
+      }
+      if (v0 || v1) {
+        float vf0[DL], vf1[DL];
+#pragma unroll
+        for (int v = 0; v < NV; ++v) {
+          unpack16<T>(v0 ? ld16(vtile + r0 * D + ds * DL + v * VE) : make_uint4(0, 0, 0, 0), vf0 + v * VE);
+          unpack16<T>(v1 ? ld16(vtile + r1 * D + ds * DL + v * VE) : make_uint4(0, 0, 0, 0), vf1 + v * VE);
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float mn = fmaxf(m[g], fmaxf(s0[g], s1[g]));
+          const float corr = merge_weight(m[g], mn);
+          const float p0 = v0 ? exp2f(s0[g] - mn) : 0.f;
+          const float p1 = v1 ? exp2f(s1[g] - mn) : 0.f;
+          l[g] = fmaf(l[g], corr, p0 + p1);
+#pragma unroll
+          for (int d = 0; d < DL; ++d) acc[g][d] = fmaf(acc[g][d], corr, fmaf(p0, vf0[d], p1 * vf1[d]));
+          m[g] = mn;
+        }
+      }
+    }
+    __syncthreads();  // stage st is free again
+    if (tid == 0 && !failed && t + kAttnStages < ntiles) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(t + kAttnStages);
+    }
+  }
+  if (failed && tid == 0) {
+    // tiles t_fail .. t_fail + kAttnStages - 1 were issued and never consumed:
+    // let those copies into this CTA's shared memory land before it exits
+    for (int t = t_fail; t < ntiles && t < t_fail + kAttnStages; ++t)
+      attn_wait_bounded(attn_smem_u32(&bars[t % kAttnStages]), (uint32_t)((t / kAttnStages) & 1));
+  }
+
+  // merge key groups (shuffles), warps (shared memory), CTAs (DSMEM)
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float mo = __shfl_xor_sync(0xffffffffu, m[g], off);
+      const float lo = __shfl_xor_sync(0xffffffffu, l[g], off);
+      const float mn = fmaxf(m[g], mo);
+      const float wa = merge_weight(m[g], mn), wb = merge_weight(mo, mn);
+      l[g] = l[g] * wa + lo * wb;
+#pragma unroll
+      for (int d = 0; d < DL; ++d) {
+        const float ao = __shfl_xor_sync(0xffffffffu, acc[g][d], off);
+        acc[g][d] = acc[g][d] * wa + ao * wb;
+      }
+      m[g] = mn;
+    }
+  }
+  if (kg == 0) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      if (ds == 0) {
+        w_m[warp][g] = m[g];
+        w_l[warp][g] = l[g];
+      }
+#pragma unroll
+      for (int d = 0; d < DL; ++d) w_acc[warp][g][ds * DL + d] = acc[g][d];
+    }
+  }
+  __syncthreads();
+  for (int t = tid; t < G * D; t += kAttnThreads) {
+    const int g = t / D, d = t - (t / D) * D;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) mx = fmaxf(mx, w_m[w][g]);
+    float ls = 0.f, as = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      const float wt = merge_weight(w_m[w][g], mx);
+      ls += w_l[w][g] * wt;
+      as += w_acc[w][g][d] * wt;
+    }
+    c_acc[g][d] = as;
+    if (d == 0) {
+      c_m[g] = mx;
+      c_l[g] = ls;
+    }
+  }
+  cluster.sync();
+  if (crank == 0) {
+    for (int t = tid; t < G * D; t += kAttnThreads) {
+      const int g = t / D, d = t - (t / D) * D;
+      float mr[kClusterCTAs];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int r = 0; r < kClusterCTAs; ++r) {
+        mr[r] = *cluster.map_shared_rank(&c_m[g], r);
+        mx = fmaxf(mx, mr[r]);
+      }
+      float ls = 0.f, as = 0.f;
+#pragma unroll
+      for (int r = 0; r < kClusterCTAs; ++r) {
+        const float wt = merge_weight(mr[r], mx);
+        ls += *cluster.map_shared_rank(&c_l[g], r) * wt;
+        as += *cluster.map_shared_rank(&c_acc[g][d], r) * wt;
+      }
+      T* o = static_cast<T*>(p.out) + b * p.ob + (int64_t)(h * G + g) * p.oh + d;
+      *o = Elem<T>::from_f(ls > 0.f ? as / ls : 0.f);
+    }
+  }
+  cluster.sync();
+}
+
 template <typename T, int G, int D>
 int launch_attn(const AttnParams& p, int64_t batch, int hk, cudaStream_t s) {
   const dim3 grid(kClusterCTAs, (unsigned)hk, (unsigned)batch);
-  decode_attn_kernel<T, G, D><<<grid, kAttnThreads, 0, s>>>(p);
+  if (p.cs == D) {  // contiguous cache rows: TMA-staged kernel
+    constexpr size_t smem = (size_t)kAttnStages * 2 * kAttnTile * D * sizeof(T);
+    static int smem_set[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return KANI_ERR_UNSUPPORTED;
+    if (smem > 48 * 1024 && !smem_set[dev]) {
+      if (cudaFuncSetAttribute(decode_attn_kernel<T, G, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)smem) != cudaSuccess)
+        return launch_status();
+      smem_set[dev] = 1;
+    }
+    decode_attn_kernel<T, G, D><<<grid, kAttnThreads, smem, s>>>(p);
+  } else {
+    decode_attn_reg_kernel<T, G, D><<<grid, kAttnThreads, 0, s>>>(p);
+  }
   return launch_status();
 }
 

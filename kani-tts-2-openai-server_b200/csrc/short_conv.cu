@@ -37,34 +37,52 @@ short_conv_kernel(const T* __restrict__ bcx, int64_t bcx_stride, T* __restrict__
   unpack16<T>(ld16(row + c0), bg);
   unpack16<T>(ld16(row + hidden + c0), cg);
   unpack16<T>(ld16(row + 2 * hidden + c0), xg);
-  // state and weights of these E channels: E*L contiguous elements each
-  constexpr int NV = (E * L * (int)sizeof(T) + 15) / 16;
+  // state and weights of these E channels: E*L contiguous elements each,
+  // moved as 16-byte vectors when E*L*sizeof(T) is a multiple of 16
+  constexpr int BYTES = E * L * (int)sizeof(T);
+  constexpr bool VEC = BYTES % 16 == 0;
   T* st = state + b * state_stride + (int64_t)c0 * L;
-  T sv[E * L], wv[E * L];
+  const T* wr = w + (int64_t)c0 * L;
+  union Row {
+    T e[E * L];
+    uint4 v[VEC ? BYTES / 16 : 1];
+  } sv, wv;
+  if constexpr (VEC) {
 #pragma unroll
-  for (int i = 0; i < E * L; ++i) {
-    sv[i] = st[i];
-    wv[i] = w[(int64_t)c0 * L + i];
+    for (int i = 0; i < BYTES / 16; ++i) {
+      sv.v[i] = ld16(st + i * (16 / (int)sizeof(T)));
+      wv.v[i] = ld16_ro(wr + i * (16 / (int)sizeof(T)));
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < E * L; ++i) {
+      sv.e[i] = st[i];
+      wv.e[i] = wr[i];
+    }
   }
-  (void)NV;
   float out[E];
 #pragma unroll
   for (int e = 0; e < E; ++e) {
     const float bx = round_to<T>(__fmul_rn(bg[e], xg[e]));
     float s[L];
 #pragma unroll
-    for (int i = 0; i + 1 < L; ++i) s[i] = Elem<T>::to_f(sv[e * L + i + 1]);
+    for (int i = 0; i + 1 < L; ++i) s[i] = Elem<T>::to_f(sv.e[e * L + i + 1]);
     s[L - 1] = bx;
     float acc = 0.f;
 #pragma unroll
     for (int i = 0; i < L; ++i) {
-      sv[e * L + i] = Elem<T>::from_f(s[i]);
-      acc = __fadd_rn(acc, round_to<T>(__fmul_rn(s[i], Elem<T>::to_f(wv[e * L + i]))));
+      sv.e[e * L + i] = Elem<T>::from_f(s[i]);
+      acc = __fadd_rn(acc, round_to<T>(__fmul_rn(s[i], Elem<T>::to_f(wv.e[e * L + i]))));
     }
     out[e] = __fmul_rn(cg[e], round_to<T>(acc));
   }
+  if constexpr (VEC) {
 #pragma unroll
-  for (int i = 0; i < E * L; ++i) st[i] = sv[i];
+    for (int i = 0; i < BYTES / 16; ++i) st16(st + i * (16 / (int)sizeof(T)), sv.v[i]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < E * L; ++i) st[i] = sv.e[i];
+  }
   st16(y + b * y_stride + c0, pack16<T>(out));
 }
 
@@ -72,7 +90,8 @@ template <typename T>
 int launch_conv(const void* bcx, int64_t bcx_stride, void* state, int64_t state_stride, const void* w,
                 void* y, int64_t y_stride, int64_t batch, int hidden, int L, cudaStream_t s) {
   constexpr int E = VecN<T>::value;
-  if (hidden % E != 0 || !aligned16(bcx) || !aligned16(y) || bcx_stride % E != 0 || y_stride % E != 0)
+  if (hidden % E != 0 || !aligned16(bcx) || !aligned16(y) || bcx_stride % E != 0 || y_stride % E != 0 ||
+      !aligned16(state) || !aligned16(w) || (state_stride * (int64_t)sizeof(T)) % 16 != 0)
     return KANI_ERR_UNSUPPORTED;
   const int64_t threads = batch * (hidden / E);
   const int64_t grid = (threads + 127) / 128;

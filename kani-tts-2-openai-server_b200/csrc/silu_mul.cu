@@ -18,10 +18,14 @@ namespace kani {
 namespace {
 
 __device__ __forceinline__ float silu_mul_f(float g, float u) {
-  // (g * sigmoid(g)) * u with sigmoid(g) = 1 / (1 + e^-g).  The reciprocal is
-  // the IEEE one: an approximate divide returns 0 once 1 + e^-g exceeds 2^126
-  // (g < -87.3), where the true result is still a normal number.
-  const float sig = __frcp_rn(1.0f + __expf(-g));
+  // (g * sigmoid(g)) * u.  sigmoid from t = e^-|g| in (0, 1]: g / (1 + e^-g)
+  // is 1/(1+t) for g >= 0 and t/(1+t) for g < 0, so the divisor stays in
+  // [1, 2], where the fast divide is accurate.  Below |g| ~ 87 the fast
+  // exponential flushes to zero while e^g is still representable, so that
+  // (rare) case takes the full-range expf.
+  const float t = __expf(-fabsf(g));
+  float sig = __fdividef(g >= 0.f ? 1.0f : t, 1.0f + t);
+  if (t == 0.f && g < 0.f) sig = expf(g);
   return __fmul_rn(__fmul_rn(g, sig), u);
 }
 

@@ -592,3 +592,16 @@ def test_short_conv_step_bit_exact_vs_eager(b, h):
     assert torch.equal(st_gpu.cpu(), st_ref)
     assert int(ulp(y, y_ref).max()) <= 1            # three-term fp32 sum order
     assert float((ulp(y, y_ref) == 0).float().mean()) > 0.999
+
+
+def test_decode_attention_strided_cache_uses_register_path():
+    """A [B, S, Hk, D] cache viewed as [B, Hk, S, D] (slot stride != head_dim)
+    takes the register kernel; same results as the oracle."""
+    b, hq, hk, s_len, d = 2, 16, 8, 300, 64
+    q = rnd((b, hq, d), 1120)
+    kc_bshd, vc_bshd = rnd((b, s_len, hk, d), 1121), rnd((b, s_len, hk, d), 1122)
+    kc, vc = gpu(kc_bshd).permute(0, 2, 1, 3), gpu(vc_bshd).permute(0, 2, 1, 3)
+    kv_len = torch.tensor([300, 77])
+    got = K.decode_attention(gpu(q), kc, vc, gpu(kv_len))
+    ref = O.decode_attention_ref(q, kc_bshd.permute(0, 2, 1, 3), vc_bshd.permute(0, 2, 1, 3), kv_len, d ** -0.5)
+    assert_close_ulp(got, ref, 2, 0.95)

@@ -48,8 +48,16 @@ struct AttnParams {
   int32_t* err;
 };
 
+// 2^x with the hardware approximation (ex2.approx: relative error ~2^-22,
+// ample for softmax weights that end in a bf16 output).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ float merge_weight(float m, float mnew) {
-  return m == -INFINITY ? 0.f : exp2f(m - mnew);
+  return m == -INFINITY ? 0.f : ex2(m - mnew);
 }
 
 template <typename T, int G, int D>
@@ -134,7 +142,7 @@ decode_attn_reg_kernel(AttnParams p) {
       if (valid) {
         const float mn = fmaxf(m[g], s);
         const float corr = merge_weight(m[g], mn);
-        const float pr = exp2f(s - mn);
+        const float pr = ex2(s - mn);
         l[g] = fmaf(l[g], corr, pr);
 #pragma unroll
         for (int d = 0; d < DL; ++d) acc[g][d] = fmaf(acc[g][d], corr, pr * vf[d]);
@@ -228,7 +236,7 @@ decode_attn_reg_kernel(AttnParams p) {
 // times out contributes an empty partial and still reaches both cluster
 // barriers.
 constexpr int kAttnTile = 64;
-constexpr int kAttnStages = 4;
+constexpr int kAttnStages = 3;
 constexpr long long kAttnWaitCycles = 2000000000LL;  // ~1 s
 
 __device__ __forceinline__ uint32_t attn_smem_u32(const void* ptr) {
@@ -363,18 +371,21 @@ decode_attn_kernel(AttnParams p) {
       float s0[G], s1[G];
 #pragma unroll
       for (int g = 0; g < G; ++g) {
-        float a0 = 0.f, a1 = 0.f;
+        // paired fp32 FMAs: two dims per instruction, two chains per key
+        float2 a0 = make_float2(0.f, 0.f), a1 = a0;
 #pragma unroll
-        for (int d = 0; d < DL; ++d) {
-          a0 = fmaf(q[g][d], k0f[d], a0);
-          a1 = fmaf(q[g][d], k1f[d], a1);
+        for (int d = 0; d < DL; d += 2) {
+          const float2 qq = make_float2(q[g][d], q[g][d + 1]);
+          a0 = __ffma2_rn(qq, make_float2(k0f[d], k0f[d + 1]), a0);
+          a1 = __ffma2_rn(qq, make_float2(k1f[d], k1f[d + 1]), a1);
         }
-        a0 += __shfl_xor_sync(0xffffffffu, a0, 1);
-        a1 += __shfl_xor_sync(0xffffffffu, a1, 1);
-        a0 += __shfl_xor_sync(0xffffffffu, a0, 2);
-        a1 += __shfl_xor_sync(0xffffffffu, a1, 2);
-        s0[g] = v0 ? a0 : -INFINITY;
-        s1[g] = v1 ? a1 : -INFINITY;
+        float x0 = a0.x + a0.y, x1 = a1.x + a1.y;
+        x0 += __shfl_xor_sync(0xffffffffu, x0, 1);
+        x1 += __shfl_xor_sync(0xffffffffu, x1, 1);
+        x0 += __shfl_xor_sync(0xffffffffu, x0, 2);
+        x1 += __shfl_xor_sync(0xffffffffu, x1, 2);
+        s0[g] = v0 ? x0 : -INFINITY;
+        s1[g] = v1 ? x1 : -INFINITY;
       }
       if (v0 || v1) {
         float vf0[DL], vf1[DL];
@@ -387,11 +398,18 @@ decode_attn_kernel(AttnParams p) {
         for (int g = 0; g < G; ++g) {
           const float mn = fmaxf(m[g], fmaxf(s0[g], s1[g]));
           const float corr = merge_weight(m[g], mn);
-          const float p0 = v0 ? exp2f(s0[g] - mn) : 0.f;
-          const float p1 = v1 ? exp2f(s1[g] - mn) : 0.f;
+          const float p0 = v0 ? ex2(s0[g] - mn) : 0.f;
+          const float p1 = v1 ? ex2(s1[g] - mn) : 0.f;
           l[g] = fmaf(l[g], corr, p0 + p1);
+          const float2 c2 = make_float2(corr, corr), p02 = make_float2(p0, p0), p12 = make_float2(p1, p1);
 #pragma unroll
-          for (int d = 0; d < DL; ++d) acc[g][d] = fmaf(acc[g][d], corr, fmaf(p0, vf0[d], p1 * vf1[d]));
+          for (int d = 0; d < DL; d += 2) {
+            const float2 w = __ffma2_rn(p02, make_float2(vf0[d], vf0[d + 1]),
+                                        __fmul2_rn(p12, make_float2(vf1[d], vf1[d + 1])));
+            const float2 r = __ffma2_rn(make_float2(acc[g][d], acc[g][d + 1]), c2, w);
+            acc[g][d] = r.x;
+            acc[g][d + 1] = r.y;
+          }
           m[g] = mn;
         }
       }

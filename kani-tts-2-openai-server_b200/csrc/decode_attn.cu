@@ -508,7 +508,7 @@ int launch_attn(const AttnParams& p, int64_t batch, int hk, cudaStream_t s) {
     static int smem_set[64] = {0};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return KANI_ERR_UNSUPPORTED;
-    if (smem > 48 * 1024 && !smem_set[dev]) {
+    if (!smem_set[dev]) {  // dynamic + static shared memory may pass the 48 KB default
       if (cudaFuncSetAttribute(decode_attn_kernel<T, G, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)smem) != cudaSuccess)
         return launch_status();

@@ -8,8 +8,10 @@
 // kani_tts/inference_engine.py:259-265 and opened slot by slot at :643,
 // always a prefix); here only the valid prefix is read.
 //
-// Structure: one thread-block cluster of kClusterCTAs CTAs per (b, h).  The
-// valid prefix is split evenly over the cluster's CTAs; inside a CTA, lane
+// Structure: one thread-block cluster of CTAs per (b, h) (8 in the register
+// variant; 1, 2, 4 or 8 in the TMA variant, as many as it takes to give the
+// GPU about four CTAs per SM).  The valid prefix is split evenly over the
+// cluster's CTAs; inside a CTA, lane
 // = (key group kg in 0..7, dim slice ds in 0..3): four lanes share one key,
 // each holding D/4 dims of it and of all G query heads, so a score is a
 // 2-step shuffle sum and K/V rows are read with 16-byte loads.  Each lane
@@ -265,7 +267,7 @@ __device__ __forceinline__ bool attn_wait_bounded(uint32_t bar, uint32_t parity)
 }
 
 template <typename T, int G, int D>
-__global__ void __cluster_dims__(kClusterCTAs, 1, 1) __launch_bounds__(kAttnThreads)
+__global__ void __launch_bounds__(kAttnThreads)
 decode_attn_kernel(AttnParams p) {
   constexpr int DL = D / 4;
   constexpr int VE = VecN<T>::value;
@@ -282,6 +284,7 @@ decode_attn_kernel(AttnParams p) {
 
   cg::cluster_group cluster = cg::this_cluster();
   const int crank = (int)cluster.block_rank();
+  const int ncl = (int)cluster.num_blocks();  // CTAs splitting this (b, h): 1, 2, 4 or 8
   const int h = blockIdx.y;
   const int b = blockIdx.z;
   const int tid = threadIdx.x;
@@ -294,7 +297,7 @@ decode_attn_kernel(AttnParams p) {
     len = p.cache_len;
   }
   if (len < 0) len = 0;
-  const int64_t chunk = (len + kClusterCTAs - 1) / kClusterCTAs;
+  const int64_t chunk = (len + ncl - 1) / ncl;
   const int64_t k0 = crank * chunk;
   const int64_t k1 = k0 + chunk < len ? k0 + chunk : len;
   const int n = k1 > k0 ? (int)(k1 - k0) : 0;
@@ -483,12 +486,13 @@ decode_attn_kernel(AttnParams p) {
       float mx = -INFINITY;
 #pragma unroll
       for (int r = 0; r < kClusterCTAs; ++r) {
-        mr[r] = *cluster.map_shared_rank(&c_m[g], r);
+        mr[r] = r < ncl ? *cluster.map_shared_rank(&c_m[g], r) : -INFINITY;
         mx = fmaxf(mx, mr[r]);
       }
       float ls = 0.f, as = 0.f;
 #pragma unroll
       for (int r = 0; r < kClusterCTAs; ++r) {
+        if (r >= ncl) break;
         const float wt = merge_weight(mr[r], mx);
         ls += *cluster.map_shared_rank(&c_l[g], r) * wt;
         as += *cluster.map_shared_rank(&c_acc[g][d], r) * wt;
@@ -502,20 +506,41 @@ decode_attn_kernel(AttnParams p) {
 
 template <typename T, int G, int D>
 int launch_attn(const AttnParams& p, int64_t batch, int hk, cudaStream_t s) {
-  const dim3 grid(kClusterCTAs, (unsigned)hk, (unsigned)batch);
-  if (p.cs == D) {  // contiguous cache rows: TMA-staged kernel
-    constexpr size_t smem = (size_t)kAttnStages * 2 * kAttnTile * D * sizeof(T);
+  if (p.cs == D) {  // contiguous cache rows: TMA-staged kernel, cluster size sized to fill the GPU
+    static int sms[64] = {0};
     static int smem_set[64] = {0};
+    constexpr size_t smem = (size_t)kAttnStages * 2 * kAttnTile * D * sizeof(T);
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return KANI_ERR_UNSUPPORTED;
+    if (!sms[dev]) {
+      int n = 0;
+      if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+      sms[dev] = n;
+    }
     if (!smem_set[dev]) {  // dynamic + static shared memory may pass the 48 KB default
       if (cudaFuncSetAttribute(decode_attn_kernel<T, G, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)smem) != cudaSuccess)
         return launch_status();
       smem_set[dev] = 1;
     }
-    decode_attn_kernel<T, G, D><<<grid, kAttnThreads, smem, s>>>(p);
+    // split each (stream, KV head) over 1..8 CTAs until about 4 CTAs per SM are busy
+    int cl = 1;
+    while (cl < kClusterCTAs && batch * hk * cl < 4LL * sms[dev]) cl *= 2;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)cl, (unsigned)hk, (unsigned)batch);
+    cfg.blockDim = dim3(kAttnThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)cl;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, decode_attn_kernel<T, G, D>, p);
   } else {
+    const dim3 grid(kClusterCTAs, (unsigned)hk, (unsigned)batch);
     decode_attn_reg_kernel<T, G, D><<<grid, kAttnThreads, 0, s>>>(p);
   }
   return launch_status();

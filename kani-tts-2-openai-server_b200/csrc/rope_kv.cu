@@ -784,7 +784,7 @@ int launch_bulk(const RopeParams& p, int log2l, cudaStream_t s) {
   static int smem_set[64] = {0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return KANI_ERR_UNSUPPORTED;
-  if (smem > 48 * 1024 && smem_set[dev] < (int)smem) {
+  if (smem + 1024 > 48 * 1024 && smem_set[dev] < (int)smem) {  // static shared memory counts too
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return launch_status();
     smem_set[dev] = (int)smem;

@@ -60,6 +60,18 @@ def assert_rope_close(got, ref, min_exact=0.99):
         assert float((d == 0).float().mean()) >= min_exact, f"exact fraction {float((d == 0).float().mean())}"
 
 
+def assert_attention_close(got, ref):
+    """Attention output vs the float64 oracle: within 2 bf16 ULP, or within 2e-5
+    absolute (outputs are weighted means of N(0, 1) values; where they cancel to
+    ~1e-5, fp32 accumulation and the 2^-22 relative error of the hardware
+    base-2 exponential are a few ULP of the tiny result); >= 95 % bit-identical."""
+    got, ref = got.cpu(), ref.cpu()
+    d = ulp(got, ref)
+    ok = (d <= 2) | ((got.float() - ref.float()).abs() <= 2e-5)
+    assert bool(ok.all()), f"{int((~ok).sum())} elements outside tolerance, max ULP {int(d.max())}"
+    assert float((d == 0).float().mean()) >= 0.95
+
+
 def assert_rel(got, ref, tol=1e-5):
     got, ref = got.cpu().float(), ref.cpu().float()
     rel = ((got - ref).abs() / ref.abs().clamp_min(1e-30))
@@ -564,7 +576,7 @@ def test_decode_attention_vs_oracle(b, hq, hk, s_len, lens):
     kv_len = torch.tensor(lens, dtype=torch.long)
     got = K.decode_attention(gpu(q), gpu(kc), gpu(vc), gpu(kv_len))
     ref = O.decode_attention_ref(q, kc, vc, kv_len, d ** -0.5)
-    assert_close_ulp(got, ref, 2, 0.95)            # fp32 online softmax vs float64, one rounding each
+    assert_attention_close(got, ref)
     assert _lib.read_and_clear_errors(DEV) == 0
 
 
@@ -607,4 +619,4 @@ def test_decode_attention_strided_cache_uses_register_path():
     kv_len = torch.tensor([300, 77])
     got = K.decode_attention(gpu(q), kc, vc, gpu(kv_len))
     ref = O.decode_attention_ref(q, kc_bshd.permute(0, 2, 1, 3), vc_bshd.permute(0, 2, 1, 3), kv_len, d ** -0.5)
-    assert_close_ulp(got, ref, 2, 0.95)
+    assert_attention_close(got, ref)

@@ -643,6 +643,16 @@ def run_op(name: str, size: int, steps: int, warmup: int) -> dict:
         bcx, stt, w = rn(size, 3 * 1024), rn(size, 1024, 3), rn(1024, 3)
         y = torch.empty(size, 1024, dtype=bf, device=dev)
         fn, nbytes = (lambda: K.short_conv_step(bcx, stt, w, out=y)), size * 1024 * 2 * (3 + 3 + 3 + 1) + 1024 * 6
+    elif name == "sample":                   # size = streams, reduced vocab 15591, config sampling settings
+        from kani_tts_b200 import sampling as KS
+        v = 15591
+        lg = rn(size, v)
+        seen = KS.seen_bitmap(torch.randint(0, v, (size, 200), generator=g), v, device=dev)
+        step = torch.zeros(1, dtype=torch.long, device=dev)
+        tok = torch.empty(size, dtype=torch.long, device=dev)
+        fn = (lambda: K.sample_tokens(lg, seen, temperature=0.5, top_p=0.85, repetition_penalty=1.2, seed=1,
+                                      step=step, out=tok))
+        nbytes = size * (v * 2 + seen.shape[1] * 4 + 8)
     else:
         raise SystemExit(f"unknown op {name}")
     for _ in range(warmup):
@@ -672,7 +682,7 @@ def main():
     ap.add_argument("--decode-only", action="store_true", help="profiling aid: run only the decode arms")
     ap.add_argument("--decode-batch", type=int, default=1, help="streams for --decode-only")
     ap.add_argument("--op", default=None, help="profiling aid: run one fused op alone "
-                    "(silu_mul, add_rms_norm, rope_kv_write, decode_attention, short_conv)")
+                    "(silu_mul, add_rms_norm, rope_kv_write, decode_attention, short_conv, sample)")
     ap.add_argument("--size", type=int, default=4096, help="rows / tokens / streams for --op")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()

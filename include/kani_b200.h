@@ -213,6 +213,40 @@ KANI_API int kani_short_conv_step(int32_t dtype, const void* bcx, int64_t bcx_ro
                          void* y, int64_t y_row_stride, int64_t batch, int32_t hidden,
                          int32_t kernel_len, void* stream);
 
+/*
+ * Next-token sampling for `batch` streams, one launch, no host sync.
+ * Replaces KaniInferenceEngine._sample_next_token
+ * (kani_tts/inference_engine.py:349-430) and its per-token `.item()`:
+ *   1. repetition penalty on the tokens set in `seen_bitmap`
+ *      (l > 0 ? l / rp : l * rp, rounded to the logits dtype; skipped when
+ *      rp == 1 or the bitmap is NULL);
+ *   2. optional additive `logit_bias` [vocab] (the full-vocab audio mask);
+ *   3. top-k (k = top_k <= 256), ordered by value, ties by lower index;
+ *   4. temperature (l / T when T != 1), softmax, in-order cumulative sum, and
+ *      top-p (candidate j >= 1 dropped when cumsum[j-1] >= top_p, compared in
+ *      the logits dtype; skipped when top_p >= 1);
+ *   5. softmax of the kept candidates and torch.multinomial's exponential
+ *      race: token = argmax_j round(p_j / round(E_j)), E_j ~ Exp(1).
+ *   logits: [batch, vocab] with a row stride; seen_bitmap: [batch, seen_row_words]
+ *   uint32 (bit i of the row = index i seen), updated with the sampled index
+ *   when update_seen != 0; index_map: [vocab] int64 (index -> token id, e.g.
+ *   the reduced-to-full map), NULL = identity.
+ *   E_j: from exp_draws [batch, top_k] fp32 when non-NULL, else Philox4x32-10
+ *   keyed by `seed`, counter (j / 4, stream, *step_counter) (step 0 when
+ *   step_counter is NULL).  Optional outputs, each [batch, top_k]: draws_out
+ *   (the E_j used), probs_out (the kept distribution, logits dtype),
+ *   cand_out (the candidates' indices, sorted).  tokens_out[b * stride] gets
+ *   the token id.  vocab * dtype size is limited to about 200 KB per row.
+ */
+KANI_API int kani_sample_tokens(int32_t dtype, const void* logits, int64_t logits_row_stride,
+                       int64_t batch, int32_t vocab, const void* logit_bias,
+                       uint32_t* seen_bitmap, int64_t seen_row_words, int32_t update_seen,
+                       float repetition_penalty, float temperature, float top_p, int32_t top_k,
+                       const int64_t* index_map, uint64_t seed, const int64_t* step_counter,
+                       const float* exp_draws, float* draws_out, void* probs_out,
+                       int32_t* cand_out, int64_t* tokens_out, int64_t tokens_out_stride,
+                       void* stream);
+
 #ifdef __cplusplus
 }
 #endif

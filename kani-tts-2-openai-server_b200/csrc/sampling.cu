@@ -1,0 +1,456 @@
+// Next-token sampling on the device (sm_100a): repetition penalty, optional
+// additive logit bias, top-k, temperature, top-p and a categorical draw, for
+// a batch of independent streams, in one launch.
+//
+// Reference: KaniInferenceEngine._sample_next_token,
+// kani_tts/inference_engine.py:349-430, which runs on the host once per token
+// (a dozen small launches plus `unique()` and an `.item()` sync):
+//   * penalty (375-395): every distinct token of the history gets
+//       l = l > 0 ? l / rp : l * rp                 (one rounding to the dtype)
+//   * audio mask (398-399, full-vocab mode): l = l + mask
+//   * top-k (402-403): torch.topk(l, min(256, V)), sorted descending
+//   * temperature (406-407): l = l / T                (one rounding)
+//   * top-p (410-415): p = softmax(l); c = cumsum(p);
+//       candidate j >= 1 is dropped when c[j-1] >= top_p
+//   * draw (418-419): p' = softmax(l with dropped = -inf); torch.multinomial(p', 1)
+//   * map back (422-428): topk index -> reduced index -> full token id.
+// The arithmetic follows torch's CPU kernels for a bf16/f16/f32 tensor:
+//   * scalar multiply/divide in fp32 with the original scalar, then one rounding;
+//   * softmax in fp32: exp(x - max) scaled by 1/sum, rounded once;
+//   * cumsum accumulated in order in fp32 (double for f32 tensors), each prefix rounded;
+//   * the top_p comparison in the tensor's dtype (the scalar is rounded to it).
+// torch.multinomial with one sample is the exponential race of
+// aten/src/ATen/native/Distributions.cpp (torch 2.x): q ~ Exp(1) stored in
+// the dtype, s = p' / q rounded to the dtype, token = argmax(s), first index
+// on ties.  The Exp(1) draws come either from the caller (`exp_draws`) or from
+// Philox4x32-10 (Salmon, Moraes, Dror & Shaw, SC 2011) keyed by the seed and
+// counted by (candidate group, stream, step): u = (2m + 1) 2^-24 with m the
+// top 23 bits of a Philox word, E = -log(u).
+//
+// Ties: torch.topk does not specify the order of equal logits; this kernel
+// orders candidates by value, then by lower index (a stable descending sort).
+//
+// Layout: one 1024-thread CTA per stream.  The penalised row is staged in
+// shared memory (coalesced loads); the k-th largest value is found by an
+// 8-bit-digit radix select over order-preserving keys (2 passes for 16-bit
+// types, 4 for f32), with equal values at the boundary taken in index order
+// through one block-wide scan; the k candidates are sorted by counting ranks;
+// one warp then runs temperature, both softmaxes, the cumulative sum and the
+// race.  No global scratch; no waits.
+#include "common.cuh"
+
+#include <math.h>
+
+namespace kani {
+namespace {
+
+constexpr int kSampleThreads = 1024;
+constexpr int kMaxTopK = 256;
+constexpr int kSampleMaxDynSmem = 200 * 1024;
+
+struct SampleParams {
+  const void* logits;
+  int64_t row_stride;
+  const void* bias;
+  uint32_t* seen;
+  int64_t seen_words;
+  int update_seen;
+  float penalty, temperature, top_p;
+  int vocab, top_k, ipt;
+  const int64_t* index_map;
+  uint64_t seed;
+  const int64_t* step;
+  const float* draws;
+  float* draws_out;
+  void* probs_out;
+  int32_t* cand_out;
+  int64_t* tokens;
+  int64_t tokens_stride;
+};
+
+// Order-preserving unsigned key of a stored value (larger value -> larger
+// key; -0 and +0 share a key).  NaN inputs are not ordered like torch.topk.
+template <typename T> struct KeyOf;
+template <> struct KeyOf<__nv_bfloat16> {
+  using Raw = uint16_t;
+  static constexpr int kBits = 16;
+  static __device__ __forceinline__ uint32_t key(uint16_t b) {
+    if ((b & 0x7fffu) == 0) b = 0;
+    return (uint32_t)(b ^ ((b & 0x8000u) ? 0xffffu : 0x8000u));
+  }
+};
+template <> struct KeyOf<__half> : KeyOf<__nv_bfloat16> {};
+template <> struct KeyOf<float> {
+  using Raw = uint32_t;
+  static constexpr int kBits = 32;
+  static __device__ __forceinline__ uint32_t key(uint32_t b) {
+    if ((b & 0x7fffffffu) == 0) b = 0;
+    return b ^ ((b & 0x80000000u) ? 0xffffffffu : 0x80000000u);
+  }
+};
+
+// Cumulative-sum accumulator type of torch's CPU kernel for the dtype.
+template <typename T> struct CumAcc { using type = float; };
+template <> struct CumAcc<float> { using type = double; };
+
+// Philox4x32-10 block (counter c, key k); constants from the Random123 paper.
+__device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint2 k) {
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint32_t lo0 = 0xD2511F53u * c.x, hi0 = __umulhi(0xD2511F53u, c.x);
+    const uint32_t lo1 = 0xCD9E8D57u * c.z, hi1 = __umulhi(0xCD9E8D57u, c.z);
+    c = make_uint4(hi1 ^ c.y ^ k.x, lo1, hi0 ^ c.w ^ k.y, lo0);
+    k.x += 0x9E3779B9u;
+    k.y += 0xBB67AE85u;
+  }
+  return c;
+}
+
+// Exp(1) draw from one 32-bit word: u = (2m + 1) * 2^-24 in (0, 1), exact in fp32.
+__device__ __forceinline__ float exp_draw(uint32_t w) {
+  const float u = (float)(((w >> 9) << 1) | 1u) * 5.9604644775390625e-08f;
+  return -logf(u);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams p) {
+  using K = KeyOf<T>;
+  using Raw = typename K::Raw;
+  constexpr int E = VecN<T>::value;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ uint32_t hist[256];
+  __shared__ int warp_tot[32];
+  __shared__ unsigned long long cand_key[kMaxTopK];
+  __shared__ float cand_val[kMaxTopK];
+  __shared__ int cand_idx[kMaxTopK];
+  __shared__ float s_val[kMaxTopK];
+  __shared__ int s_idx[kMaxTopK];
+  __shared__ uint32_t sh_digit, sh_need, sh_eq;
+  __shared__ int sh_ncand;
+
+  T* row = reinterpret_cast<T*>(smem_raw);
+  const int b = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int V = p.vocab, KK = p.top_k, ipt = p.ipt;
+  const T* src = static_cast<const T*>(p.logits) + (int64_t)b * p.row_stride;
+  const T* bias = static_cast<const T*>(p.bias);
+  const uint32_t* seen = p.seen ? p.seen + (int64_t)b * p.seen_words : nullptr;
+  const bool pen = seen != nullptr && p.penalty != 1.0f;
+
+  // 1. stage the (penalised, biased) row in shared memory, coalesced
+  for (int i = tid; i < V; i += kSampleThreads) {
+    float v = Elem<T>::to_f(src[i]);
+    if (pen && ((__ldg(seen + (i >> 5)) >> (i & 31)) & 1u))
+      v = round_to<T>(v > 0.f ? __fdiv_rn(v, p.penalty) : __fmul_rn(v, p.penalty));
+    if (bias) v = round_to<T>(__fadd_rn(v, Elem<T>::to_f(bias[i])));
+    row[i] = Elem<T>::from_f(v);
+  }
+  if (tid == 0) sh_ncand = 0;
+  __syncthreads();
+
+  // this thread's block of the row: [base, base + ipt), ipt a multiple of E,
+  // read from shared memory as 16-byte vectors
+  const int base = tid * ipt;
+  auto keys_at = [&](int i, uint32_t* key) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(row + i);
+    Raw v[E];
+    memcpy(v, &raw, 16);
+#pragma unroll
+    for (int e = 0; e < E; ++e) key[e] = K::key(v[e]);
+  };
+
+  // 2. radix select of the k-th largest key
+  uint32_t pre = 0, mask_hi = 0, need = (uint32_t)KK, eq = 0;
+  for (int shift = K::kBits - 8; shift >= 0; shift -= 8) {
+    if (tid < 256) hist[tid] = 0;
+    __syncthreads();
+    for (int r = 0; r < ipt; r += E) {
+      uint32_t key[E];
+      keys_at(base + r, key);
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        const bool m = base + r + e < V && (key[e] & mask_hi) == pre;
+        const uint32_t d = m ? (key[e] >> shift) & 255u : 256u + (uint32_t)lane;
+        const uint32_t peers = __match_any_sync(0xffffffffu, d);
+        if (m && lane == __ffs(peers) - 1) atomicAdd(&hist[d], (uint32_t)__popc(peers));
+      }
+    }
+    __syncthreads();
+    if (warp == 0) {
+      uint32_t c[8], tot = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        c[j] = hist[lane * 8 + j];
+        tot += c[j];
+      }
+      uint32_t suf = tot;  // inclusive suffix over lanes lane..31
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t v = __shfl_down_sync(0xffffffffu, suf, o);
+        if (lane + o < 32) suf += v;
+      }
+      const uint32_t above = suf - tot;
+      if (above < need && need <= suf) {
+        uint32_t acc = above;
+        for (int j = 7; j >= 0; --j) {
+          if (acc + c[j] >= need) {
+            sh_digit = (uint32_t)(lane * 8 + j);
+            sh_need = need - acc;
+            sh_eq = c[j];
+            break;
+          }
+          acc += c[j];
+        }
+      }
+    }
+    __syncthreads();
+    pre |= sh_digit << shift;
+    mask_hi |= 255u << shift;
+    need = sh_need;
+    eq = sh_eq;
+    if (eq == need) break;  // the whole group is taken: no lower digits needed
+  }
+
+  // 3. equal keys at the boundary are taken in index order
+  int eq_rank = 0;
+  if (eq > need) {
+    int c = 0;
+    for (int r = 0; r < ipt && base + r < V; r += E) {
+      uint32_t key[E];
+      keys_at(base + r, key);
+#pragma unroll
+      for (int e = 0; e < E; ++e) c += (base + r + e < V && (key[e] & mask_hi) == pre) ? 1 : 0;
+    }
+    int inc = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += v;
+    }
+    if (lane == 31) warp_tot[warp] = inc;
+    __syncthreads();
+    if (warp == 0) {
+      const int t = warp_tot[lane];
+      int ti = t;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, ti, o);
+        if (lane >= o) ti += v;
+      }
+      warp_tot[lane] = ti - t;
+    }
+    __syncthreads();
+    eq_rank = warp_tot[warp] + inc - c;
+  }
+
+  // 4. gather the k candidates (unordered)
+  for (int r = 0; r < ipt && base + r < V; r += E) {
+    uint32_t key[E];
+    keys_at(base + r, key);
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      const int i = base + r + e;
+      const uint32_t hk = key[e] & mask_hi;
+      bool take = i < V && hk > pre;
+      if (i < V && hk == pre) take = (uint32_t)(eq_rank++) < need;
+      if (take) {
+        const int slot = atomicAdd(&sh_ncand, 1);
+        if (slot < kMaxTopK) {  // exactly top_k items qualify; the guard only bounds the store
+          cand_key[slot] = ((unsigned long long)key[e] << 32) | (unsigned long long)(0xffffffffu - (uint32_t)i);
+          cand_val[slot] = Elem<T>::to_f(row[i]);
+          cand_idx[slot] = i;
+        }
+      }
+    }
+  }
+  __syncthreads();
+
+  // 5. sort descending by (value, -index): rank = number of larger keys
+  {
+    const int j = tid >> 2, q = tid & 3;
+    const bool act = j < KK;
+    const unsigned long long kj = act ? cand_key[j] : 0ull;
+    int rank = 0;
+    if (act)
+      for (int i = q; i < KK; i += 4) rank += cand_key[i] > kj ? 1 : 0;
+    rank += __shfl_xor_sync(0xffffffffu, rank, 1);
+    rank += __shfl_xor_sync(0xffffffffu, rank, 2);
+    if (act && q == 0) {
+      s_val[rank] = cand_val[j];
+      s_idx[rank] = cand_idx[j];
+    }
+  }
+  __syncthreads();
+  if (warp != 0) return;
+
+  // 6. one warp: lane owns sorted positions lane*8 .. lane*8+7
+  constexpr int P = kMaxTopK / 32;
+  float x[P];
+#pragma unroll
+  for (int e = 0; e < P; ++e) {
+    const int j = lane * P + e;
+    float v = j < KK ? s_val[j] : -INFINITY;
+    if (j < KK && p.temperature != 1.0f) v = round_to<T>(__fdiv_rn(v, p.temperature));
+    x[e] = v;
+  }
+  const float mx = __shfl_sync(0xffffffffu, x[0], 0);
+
+  auto softmax = [&](int keep, float* out) {
+    float s = 0.f;
+#pragma unroll
+    for (int e = 0; e < P; ++e) {
+      const int j = lane * P + e;
+      out[e] = j < keep ? expf(__fsub_rn(x[e], mx)) : 0.f;
+      s = __fadd_rn(s, out[e]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+    const float inv = __frcp_rn(s);
+#pragma unroll
+    for (int e = 0; e < P; ++e) out[e] = round_to<T>(__fmul_rn(out[e], inv));
+  };
+
+  float pr[P];
+  int keep = KK;
+  if (p.top_p < 1.0f) {
+    softmax(KK, pr);
+    // first dropped position: smallest j >= 1 with round(c[j-1]) >= round(top_p),
+    // c accumulated in order; each lane scans its 8 with the carry of the lanes before
+    using Acc = typename CumAcc<T>::type;
+    const float thr = round_to<T>(p.top_p);
+    int cut = KK;
+    Acc carry = 0;
+    for (int l = 0; l < 32 && cut == KK && l * P < KK; ++l) {
+      int lcut = KK;
+      Acc c = carry;
+      if (lane == l) {
+#pragma unroll
+        for (int e = 0; e < P; ++e) {
+          const int j = l * P + e;
+          if (j + 1 >= KK) break;
+          c += (Acc)pr[e];
+          if (round_to<T>((float)c) >= thr) {
+            lcut = j + 1;
+            break;
+          }
+        }
+      }
+      lcut = __shfl_sync(0xffffffffu, lcut, l);
+      if (lcut < KK) cut = lcut;
+      carry = __shfl_sync(0xffffffffu, c, l);
+    }
+    keep = cut;
+  }
+  softmax(keep, pr);
+
+  // 7. exponential race over the kept candidates
+  float draw[P];
+  if (p.draws) {
+#pragma unroll
+    for (int e = 0; e < P; ++e) {
+      const int j = lane * P + e;
+      draw[e] = j < KK ? p.draws[(int64_t)b * KK + j] : 1.f;
+    }
+  } else {
+    const uint64_t step = p.step ? (uint64_t)*p.step : 0ull;
+    const uint2 key = make_uint2((uint32_t)p.seed, (uint32_t)(p.seed >> 32));
+#pragma unroll
+    for (int h = 0; h < P / 4; ++h) {
+      const uint4 w = philox4x32_10(
+          make_uint4((uint32_t)(lane * (P / 4) + h), (uint32_t)b, (uint32_t)step, (uint32_t)(step >> 32)), key);
+      draw[h * 4 + 0] = exp_draw(w.x);
+      draw[h * 4 + 1] = exp_draw(w.y);
+      draw[h * 4 + 2] = exp_draw(w.z);
+      draw[h * 4 + 3] = exp_draw(w.w);
+    }
+  }
+  float best = -1.f;
+  int best_j = 0x7fffffff;
+#pragma unroll
+  for (int e = 0; e < P; ++e) {
+    const int j = lane * P + e;
+    if (j < KK) {
+      const float s = round_to<T>(__fdiv_rn(pr[e], round_to<T>(draw[e])));
+      if (s > best) {
+        best = s;
+        best_j = j;
+      }
+      if (p.draws_out) p.draws_out[(int64_t)b * KK + j] = draw[e];
+      if (p.probs_out) static_cast<T*>(p.probs_out)[(int64_t)b * KK + j] = Elem<T>::from_f(pr[e]);
+      if (p.cand_out) p.cand_out[(int64_t)b * KK + j] = s_idx[j];
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oj = __shfl_xor_sync(0xffffffffu, best_j, o);
+    if (ob > best || (ob == best && oj < best_j)) {
+      best = ob;
+      best_j = oj;
+    }
+  }
+  if (lane == 0) {
+    const int idx = s_idx[best_j < KK ? best_j : 0];
+    p.tokens[(int64_t)b * p.tokens_stride] = p.index_map ? p.index_map[idx] : (int64_t)idx;
+    if (p.update_seen && p.seen) atomicOr(p.seen + (int64_t)b * p.seen_words + (idx >> 5), 1u << (idx & 31));
+  }
+}
+
+template <typename T>
+int launch_sample(SampleParams prm, int64_t batch, cudaStream_t s) {
+  constexpr int E = VecN<T>::value;
+  int ipt = (prm.vocab + kSampleThreads - 1) / kSampleThreads;
+  ipt = (ipt + E - 1) / E * E;
+  const size_t smem = (size_t)ipt * kSampleThreads * sizeof(T);
+  if (smem > (size_t)kSampleMaxDynSmem) return KANI_ERR_UNSUPPORTED;
+  prm.ipt = ipt;
+  cudaError_t e = cudaFuncSetAttribute(sample_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return (int)e;
+  sample_kernel<T><<<(unsigned)batch, kSampleThreads, smem, s>>>(prm);
+  return launch_status();
+}
+
+}  // namespace
+}  // namespace kani
+
+extern "C" int kani_sample_tokens(int32_t dtype, const void* logits, int64_t logits_row_stride, int64_t batch,
+                                  int32_t vocab, const void* logit_bias, uint32_t* seen_bitmap,
+                                  int64_t seen_row_words, int32_t update_seen, float repetition_penalty,
+                                  float temperature, float top_p, int32_t top_k, const int64_t* index_map,
+                                  uint64_t seed, const int64_t* step_counter, const float* exp_draws,
+                                  float* draws_out, void* probs_out, int32_t* cand_out, int64_t* tokens_out,
+                                  int64_t tokens_out_stride, void* stream) {
+  if (batch < 0) return KANI_ERR_INVALID_ARG;
+  if (batch == 0) return KANI_OK;
+  if (batch > 0x7fffffff || vocab < 1 || top_k < 1 || top_k > kani::kMaxTopK || top_k > vocab)
+    return KANI_ERR_INVALID_ARG;
+  if (!logits || !tokens_out) return KANI_ERR_INVALID_ARG;
+  if (!(temperature > 0.f) || !isfinite(temperature) || !(repetition_penalty > 0.f) ||
+      !isfinite(repetition_penalty) || isnan(top_p))
+    return KANI_ERR_INVALID_ARG;
+  if (batch > 1 && (logits_row_stride < vocab || tokens_out_stride < 1)) return KANI_ERR_INVALID_ARG;
+  if (seen_bitmap && seen_row_words < (vocab + 31) / 32) return KANI_ERR_INVALID_ARG;
+  kani::SampleParams prm{};
+  prm.logits = logits;
+  prm.row_stride = logits_row_stride;
+  prm.bias = logit_bias;
+  prm.seen = seen_bitmap;
+  prm.seen_words = seen_row_words;
+  prm.update_seen = update_seen;
+  prm.penalty = repetition_penalty;
+  prm.temperature = temperature;
+  prm.top_p = top_p;
+  prm.vocab = vocab;
+  prm.top_k = top_k;
+  prm.index_map = index_map;
+  prm.seed = seed;
+  prm.step = step_counter;
+  prm.draws = exp_draws;
+  prm.draws_out = draws_out;
+  prm.probs_out = probs_out;
+  prm.cand_out = cand_out;
+  prm.tokens = tokens_out;
+  prm.tokens_stride = tokens_out_stride;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return kani::dispatch_dtype(dtype, [&]<typename T>() { return kani::launch_sample<T>(prm, batch, s); });
+}

@@ -25,7 +25,11 @@ The GEMVs are cuBLAS calls; prefill attention is PyTorch SDPA.
 stream, causal SDPA, causal depthwise conv) and a CUDA-graph decode loop
 whose per-step bookkeeping (position schedule of inference_engine.py:615-619,
 KV slot, mask slot, next token) also runs inside the graph, so generation
-needs no host synchronisation per token.  Sampling is greedy.
+needs no host synchronisation per token.  The next token is the greedy
+argmax, or, given ``SamplingParams``, the reference's penalty / top-k /
+temperature / top-p / multinomial sampler (inference_engine.py:349-430) as one
+``sample_tokens`` launch per step, with the repetition history kept as a
+device bitmap and the Philox step counter advanced inside the graph.
 """
 from __future__ import annotations
 
@@ -34,9 +38,10 @@ import torch.nn.functional as F
 
 from . import _lib
 from .fused_kernels import (decode_attention, fused_add_rms_norm, fused_rms_norm, fused_rope_kv_write,
-                            fused_silu_mul, short_conv_step)
+                            fused_silu_mul, sample_tokens, short_conv_step)
 from .model import LFM2Config
 from .positions import learnable_inv_freq
+from .sampling import SamplingParams, seen_bitmap
 
 
 class FusedDecoder:
@@ -86,6 +91,8 @@ class FusedDecoder:
         self.reduced_to_full = torch.cat([
             torch.tensor([cfg.eos_token_id], device=dev, dtype=torch.long),
             torch.arange(cfg.audio_tokens_start, cfg.vocab_size, device=dev, dtype=torch.long)])
+        self.full_to_reduced = torch.full((cfg.vocab_size,), -1, device=dev, dtype=torch.long)
+        self.full_to_reduced[self.reduced_to_full] = torch.arange(self.reduced_to_full.numel(), device=dev)
         sp = state_dict.get("model.speaker_emb_projection.weight")
         self.speaker_proj = sp.to(dev, self.dtype) if sp is not None else None
 
@@ -203,12 +210,17 @@ class FusedDecoder:
 
 
 class DecodeEngine:
-    """Prefill + CUDA-graph greedy decode for `batch` independent streams."""
+    """Prefill + CUDA-graph decode (greedy, or sampled with ``sampling``) for
+    `batch` independent streams."""
 
-    def __init__(self, decoder: FusedDecoder, keep_mask: bool = False):
+    def __init__(self, decoder: FusedDecoder, keep_mask: bool = False, sampling: SamplingParams | None = None):
         self.dec = decoder
         self.keep_mask = keep_mask   # maintain the additive mask (for steps that use one)
+        self.sampling = sampling
         dev, b, s = decoder.device, decoder.batch, decoder.max_len
+        self.rng_step = torch.zeros(1, dtype=torch.long, device=dev)
+        self.next_tok = torch.zeros(b, dtype=torch.long, device=dev)
+        self.seen = None
         self.input_ids = torch.zeros(b, 1, dtype=torch.long, device=dev)
         self.positions = torch.zeros(b, dtype=torch.long, device=dev)
         self.slots = torch.zeros(b, dtype=torch.long, device=dev)
@@ -235,7 +247,11 @@ class DecodeEngine:
             pos = frame_level_positions(input_ids, cfg.audio_tokens_start, cfg.tokens_per_frame,
                                         cfg.audio_step).long()
         logits = dec.prefill(input_ids, pos, speaker_emb)
-        first = dec.reduced_to_full[logits[:, -1].argmax(-1)]
+        self.rng_step.zero_()
+        if self.sampling is not None:
+            # the prompt is the initial repetition history (inference_engine.py:553-556)
+            self.seen = seen_bitmap(input_ids, dec.head.shape[0], dec.full_to_reduced, device=dec.device)
+        first = self._next_token(logits[:, -1])
         self.input_ids.copy_(first.view(b, 1))
         self.mask.fill_(float("-inf"))
         self.mask[..., :t_eff] = 0.0
@@ -254,16 +270,29 @@ class DecodeEngine:
         if self.keep_mask:
             self.mask.scatter_(3, self.slots.view(-1, 1, 1, 1), 0.0)
         self.logits = self.dec.step(self.input_ids, self.positions, self.slots, self.kv_len, self.mask)
-        nxt = self.dec.reduced_to_full[self.logits[:, 0].argmax(-1)]
+        nxt = self._next_token(self.logits[:, 0])
         self.generated.index_copy_(1, k, nxt.view(-1, 1))
         self.input_ids.copy_(nxt.view(-1, 1))
         self.step_idx.add_(1)
+
+    def _next_token(self, logits: torch.Tensor) -> torch.Tensor:
+        """[B] full token ids from reduced logits [B, V_red]: greedy, or one
+        sampler launch that also extends the repetition bitmap and the step counter."""
+        if self.sampling is None:
+            return self.dec.reduced_to_full[logits.argmax(-1)]
+        sp = self.sampling
+        sample_tokens(logits, self.seen, temperature=sp.temperature, top_p=sp.top_p,
+                      repetition_penalty=sp.repetition_penalty, top_k=sp.top_k,
+                      index_map=self.dec.reduced_to_full, seed=sp.seed, step=self.rng_step, out=self.next_tok)
+        self.rng_step.add_(1)
+        return self.next_tok
 
     def capture(self) -> None:
         """Warm up once outside capture, then capture one decode step."""
         dec = self.dec
         saved = ({i: c.clone() for i, c in dec.conv_state.items()}, self.input_ids.clone(), self.mask.clone(),
-                 self.step_idx.clone())
+                 self.step_idx.clone(), self.rng_step.clone(),
+                 self.seen.clone() if self.seen is not None else None)
         s = torch.cuda.Stream(device=dec.device)
         s.wait_stream(torch.cuda.current_stream(dec.device))
         with torch.cuda.stream(s):
@@ -278,6 +307,9 @@ class DecodeEngine:
         self.input_ids.copy_(saved[1])
         self.mask.copy_(saved[2])
         self.step_idx.copy_(saved[3])
+        self.rng_step.copy_(saved[4])
+        if saved[5] is not None:
+            self.seen.copy_(saved[5])
 
     def run(self, n_steps: int) -> None:
         for _ in range(n_steps):

@@ -41,6 +41,7 @@ __all__ = [
     "fused_rope_kv_write",
     "decode_attention",
     "short_conv_step",
+    "sample_tokens",
 ]
 
 
@@ -422,6 +423,87 @@ def short_conv_step(bcx: torch.Tensor, state: torch.Tensor, conv_w: torch.Tensor
     check(lib.kani_short_conv_step(code, ptr(bv), bs, ptr(state), state.stride(0), ptr(conv_w.contiguous()),
                                    ptr(out), h, b, h, lc, stream_ptr(bcx.device)), "kani_short_conv_step")
     return out
+
+
+def sample_tokens(logits: torch.Tensor, seen: torch.Tensor | None = None, *, temperature: float = 1.0,
+                  top_p: float = 1.0, repetition_penalty: float = 1.0, top_k: int = 256,
+                  index_map: torch.Tensor | None = None, logit_bias: torch.Tensor | None = None,
+                  seed: int = 0, step: torch.Tensor | None = None, draws: torch.Tensor | None = None,
+                  update_seen: bool = True, out: torch.Tensor | None = None,
+                  return_details: bool = False):
+    """Sample one token per row of ``logits`` on the device (the reference's
+    ``_sample_next_token``, inference_engine.py:349-430, for B streams at once).
+
+    Args:
+        logits: [B, V] (or [B, 1, V]) bf16 / fp16 / fp32 CUDA tensor, unchanged.
+        seen: [B, ceil(V / 32)] int32 bitmap of penalised indices
+            (``sampling.seen_bitmap``), extended with the sampled index when
+            ``update_seen``; None = no repetition penalty.
+        temperature, top_p, repetition_penalty: as in the reference; k =
+            min(top_k, V).
+        index_map: [V] int64 index -> token id (the reduced-to-full map).
+        logit_bias: [V] additive bias of the logits dtype (the audio mask of
+            the full-vocab mode).
+        seed, step: Philox key and a device int64 step counter (may live in a
+            CUDA graph); ignored when ``draws`` [B, k] fp32 Exp(1) variates are given.
+        out: [B] (or any [B, ...] view with a batch stride) int64 for the token ids.
+    Returns:
+        token ids [B] int64, or (tokens, details) with ``draws``, ``probs`` and
+        ``cand`` [B, k] when ``return_details``.
+    """
+    require_cuda(logits, "logits")
+    lib = load_library()
+    code = dtype_code(logits, "logits")
+    v = logits.shape[-1]
+    lv, rows, rs = _rows_view(logits, v)
+    b = rows
+    if b == 0:
+        raise ValueError("empty logits")
+    k = min(int(top_k), v)
+    if not 1 <= k <= 256:
+        raise ValueError(f"top_k must be in [1, 256], got {top_k}")
+    dev = logits.device
+    words = (v + 31) // 32
+    if seen is not None:
+        require_cuda(seen, "seen")
+        if seen.dtype != torch.int32 or tuple(seen.shape) != (b, words) or not seen.is_contiguous():
+            raise ValueError(f"seen must be a contiguous int32 [{b}, {words}] bitmap")
+    if index_map is not None:
+        require_cuda(index_map, "index_map")
+        if index_map.dtype != torch.int64 or index_map.numel() != v or not index_map.is_contiguous():
+            raise ValueError(f"index_map must be a contiguous int64 [{v}] tensor")
+    if logit_bias is not None:
+        require_cuda(logit_bias, "logit_bias")
+        if logit_bias.dtype != logits.dtype or logit_bias.numel() != v or not logit_bias.is_contiguous():
+            raise ValueError(f"logit_bias must be a contiguous [{v}] tensor of the logits dtype")
+    if step is not None:
+        require_cuda(step, "step")
+        if step.dtype != torch.int64 or step.numel() < 1:
+            raise ValueError("step must be an int64 device tensor")
+    if draws is not None:
+        require_cuda(draws, "draws")
+        if draws.dtype != torch.float32 or tuple(draws.shape) != (b, k) or not draws.is_contiguous():
+            raise ValueError(f"draws must be a contiguous fp32 [{b}, {k}] tensor")
+    if out is None:
+        out = torch.empty(b, dtype=torch.int64, device=dev)
+    require_cuda(out, "out")
+    if out.dtype != torch.int64 or out.numel() != b:
+        raise ValueError(f"out must hold {b} int64 token ids")
+    out_stride = out.stride(0) if out.dim() >= 1 and b > 1 else 1
+    det = None
+    if return_details:
+        det = {"draws": torch.empty(b, k, dtype=torch.float32, device=dev),
+               "probs": torch.empty(b, k, dtype=logits.dtype, device=dev),
+               "cand": torch.empty(b, k, dtype=torch.int32, device=dev)}
+    check(lib.kani_sample_tokens(
+        code, ptr(lv), rs, b, v, ptr(logit_bias) if logit_bias is not None else None,
+        ptr(seen) if seen is not None else None, words, 1 if update_seen else 0,
+        float(repetition_penalty), float(temperature), float(top_p), k,
+        ptr(index_map) if index_map is not None else None, int(seed) & ((1 << 64) - 1),
+        ptr(step) if step is not None else None, ptr(draws) if draws is not None else None,
+        ptr(det["draws"]) if det else None, ptr(det["probs"]) if det else None,
+        ptr(det["cand"]) if det else None, ptr(out), out_stride, stream_ptr(dev)), "kani_sample_tokens")
+    return (out, det) if return_details else out
 
 
 def launch_count() -> int:

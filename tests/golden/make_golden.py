@@ -201,7 +201,109 @@ def main() -> None:
     save("frame_positions", cases)
 
     save("decode_step", decode_step_cases(sc, md, hf))
+    save("sampling", sampling_cases())
     print("golden vectors written to", OUT)
+
+
+def _tie_free_logits(v: int, n_top: int, lo: float, hi: float, seed: int) -> torch.Tensor:
+    """bf16 logits [1, v] whose n_top largest values are distinct bf16 numbers
+    drawn from [lo, hi) at random positions; the rest lie below lo."""
+    g = _gen(seed)
+    grid = torch.arange(0, 65536, dtype=torch.int32).to(torch.int16).view(torch.bfloat16)
+    grid = grid[torch.isfinite(grid) & (grid >= lo) & (grid < hi)]
+    pick = grid[torch.randperm(grid.numel(), generator=g)[:n_top]]
+    out = (torch.randn(1, v, generator=g) * 1.5 + (lo - 6.0)).clamp(max=lo - 0.5).to(torch.bfloat16)
+    pos = torch.randperm(v, generator=g)[:n_top]
+    out[0, pos] = pick
+    return out
+
+
+def sampling_cases():
+    """KaniInferenceEngine._sample_next_token (kani_tts/inference_engine.py:349-430)
+    run on the CPU with a stand-in engine object holding the attributes it reads.
+    torch.topk and torch.multinomial are wrapped: the topk wrapper records the
+    reference's candidates; the multinomial wrapper records the final
+    distribution and draws the sample by the exponential race torch.multinomial
+    performs for one sample (argmax(probs / q), q ~ Exp(1) in the probs dtype),
+    with q taken from stored fp32 draws so the selected token is reproducible."""
+    import types as _t
+    ie = importlib.import_module("kani_tts.inference_engine")
+    sample = ie.KaniInferenceEngine._sample_next_token
+    vocab, audio_start, eos = 80000, 64410, 7
+    n_red = 1 + vocab - audio_start
+    reduced_to_full = torch.cat([torch.tensor([eos]), torch.arange(audio_start, vocab)])
+    full_to_reduced = torch.full((vocab,), -1, dtype=torch.long)
+    full_to_reduced[eos] = 0
+    full_to_reduced[audio_start:] = torch.arange(1, n_red)
+    audio_mask = torch.full((1, vocab), float("-inf"), dtype=torch.bfloat16)
+    audio_mask[0, audio_start:] = 0.0
+    audio_mask[0, eos] = 0.0
+
+    specs = {
+        # name: (reduced?, penalty, temperature, top_p, (n_top, lo, hi), seed)
+        "config_defaults": (True, 1.2, 0.5, 0.85, (300, 1.0, 16.0), 10),
+        "engine_defaults": (True, 1.0, 0.7, 0.95, (300, 1.0, 16.0), 11),
+        "no_top_p": (True, 1.1, 1.0, 1.0, (300, 1.0, 16.0), 12),
+        "deep_nucleus": (True, 1.2, 1.0, 0.95, (300, 0.5, 4.0), 13),
+        "full_vocab_mask": (False, 1.2, 0.5, 0.85, (300, 1.0, 16.0), 14),
+    }
+    cases = {}
+    real_topk, real_multinomial = torch.topk, torch.multinomial
+    for name, (reduced, rp, temp, top_p, (n_top, lo, hi), seed) in specs.items():
+        v = n_red if reduced else vocab
+        g = _gen(100 + seed)
+        for attempt in range(50):
+            logits = _tie_free_logits(n_red, n_top, lo, hi, 1000 * seed + attempt)
+            if not reduced:   # full vocab: the same values on the EOS + audio ids, text ids anywhere
+                full = (torch.randn(1, vocab, generator=g) * 3.0).to(torch.bfloat16)
+                full[0, reduced_to_full] = logits[0]
+                logits = full
+            prompt = torch.randint(0, 64400, (1, 120), generator=g)
+            gen_red = torch.randint(0, n_red, (1, 80), generator=g)
+            history = torch.cat([prompt, reduced_to_full[gen_red]], dim=1)
+            # the penalised row must be tie-free inside the top k + 1
+            pen = logits.clone()
+            ids = history[0].unique()
+            ridx = full_to_reduced[ids] if reduced else ids
+            ridx = ridx[ridx >= 0]
+            pl = pen[0, ridx]
+            pen[0, ridx] = torch.where(pl > 0, pl / rp, pl * rp) if rp != 1.0 else pl
+            if not reduced:
+                pen = pen + audio_mask
+            top = torch.sort(pen.float(), descending=True).values[0, :257]
+            if bool((top[1:] < top[:-1]).all()):
+                break
+        else:
+            raise RuntimeError(f"no tie-free draw for {name}")
+        draws = -torch.log(torch.rand(1, 256, generator=g).clamp_min(2.0 ** -24))
+        rec = {}
+
+        def topk(x, k, dim=-1, **kw):
+            vals, idx = real_topk(x, k, dim=dim, **kw)
+            rec["topk_values"], rec["topk_indices"] = vals.clone(), idx.clone()
+            return vals, idx
+
+        def multinomial(probs, num_samples, **kw):
+            rec["probs"] = probs.clone()
+            q = draws[:, :probs.shape[-1]].to(probs.dtype)
+            return torch.argmax(probs / q, dim=-1, keepdim=True)
+
+        stand_in = _t.SimpleNamespace(
+            optimized_decoder=_t.SimpleNamespace(full_to_reduced=full_to_reduced,
+                                                 reduced_to_full=reduced_to_full),
+            vocab_size=vocab, repetition_penalty=rp, temperature=temp, top_p=top_p,
+            _audio_logit_mask=None if reduced else audio_mask)
+        torch.topk, torch.multinomial = topk, multinomial
+        try:
+            tok = sample(stand_in, logits.clone(), history)
+        finally:
+            torch.topk, torch.multinomial = real_topk, real_multinomial
+        cases[name] = dict(logits=logits, history=history, reduced=np.bool_(reduced),
+                           repetition_penalty=np.float64(rp), temperature=np.float64(temp),
+                           top_p=np.float64(top_p), draws=draws.float(), token=tok.view(-1),
+                           topk_values=rec["topk_values"], topk_indices=rec["topk_indices"],
+                           probs=rec["probs"])
+    return cases
 
 
 def decode_step_cases(sc, md, hf):
@@ -299,4 +401,8 @@ def decode_step_cases(sc, md, hf):
 
 
 if __name__ == "__main__":
-    main()
+    if len(sys.argv) > 1 and sys.argv[1] == "--only-sampling":
+        _import_reference()
+        save("sampling", sampling_cases())
+    else:
+        main()

@@ -144,3 +144,39 @@ def test_engine_graph_replay_matches_eager_steps():
     assert torch.equal(graph_tokens, ref.generated)
     assert int(eng.step_idx.item()) == n
     assert int(eng.dec.err_flag.item()) == 0
+
+
+def test_engine_with_device_sampling_graph_matches_eager():
+    """The sampler inside the captured step (Philox counter and repetition bitmap
+    advanced on the device) gives the same token sequence as eager steps, every
+    token is EOS or an audio token, and the bitmap holds each sampled token."""
+    from kani_tts_b200.sampling import SamplingParams
+    cfg = tiny_config()
+    sd = synthetic_state_dict(cfg, seed=17)
+    b, t, n, max_len = 3, 5, 10, 32
+    g = torch.Generator().manual_seed(19)
+    ids = torch.randint(0, cfg.audio_tokens_start, (b, t), generator=g).to(DEV)
+    sp = SamplingParams(temperature=0.9, top_p=0.95, repetition_penalty=1.3, top_k=64, seed=3)
+    eng = DecodeEngine(FusedDecoder(cfg, sd, DEV, batch=b, max_len=max_len), sampling=sp)
+    eng.start(ids, None, n)
+    first = eng.input_ids.clone()
+    eng.capture()
+    eng.run(n)
+    torch.cuda.synchronize()
+    graph_tokens = eng.generated.clone()
+
+    ref = DecodeEngine(FusedDecoder(cfg, sd, DEV, batch=b, max_len=max_len), sampling=sp)
+    ref.start(ids, None, n)
+    assert torch.equal(ref.input_ids, first)
+    for _ in range(n):
+        ref._step_body()
+    torch.cuda.synchronize()
+    assert torch.equal(graph_tokens, ref.generated)
+    assert torch.equal(eng.seen, ref.seen)
+    red = eng.dec.full_to_reduced[graph_tokens]
+    assert bool((red >= 0).all())
+    words = eng.seen.cpu().long() & 0xFFFFFFFF
+    for s in range(b):
+        for r in red[s].cpu().tolist():
+            assert (int(words[s, r // 32]) >> (r % 32)) & 1
+    assert int(eng.rng_step.item()) == n + 1

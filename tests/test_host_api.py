@@ -78,6 +78,26 @@ def test_abi_rejects_bad_arguments_without_launching():
     assert lib.kani_rope_kv_write(*args) == -1
     assert lib.kani_kv_cache_write(1, fake, fake, 1, 8, 64, fake, fake, 16, _null(), 0, _null(),
                                    _null()) == -1
+    # sampler: top_k outside [1, min(256, vocab)], non-positive temperature, NaN top_p,
+    # a bitmap row shorter than the vocabulary, missing output
+    n = _null()
+
+    def sample(**kw):
+        a = dict(dtype=1, logits=fake, rs=15591, b=2, v=15591, bias=n, seen=n, words=488, upd=1, rp=1.2,
+                 t=0.5, top_p=0.85, k=256, imap=n, seed=0, step=n, draws=n, dout=n, pout=n, cout=n,
+                 tok=fake, ts=1, stream=n)
+        a.update(kw)
+        return lib.kani_sample_tokens(*a.values())
+    assert sample(k=257) == -1
+    assert sample(k=0) == -1
+    assert sample(v=100, rs=100, k=101) == -1
+    assert sample(t=0.0) == -1
+    assert sample(rp=0.0) == -1
+    assert sample(top_p=float("nan")) == -1
+    assert sample(seen=fake, words=487) == -1
+    assert sample(tok=n) == -1
+    assert sample(rs=100) == -1
+    assert sample(dtype=5) == -2
     assert lib.kani_launch_count() == before
 
 
@@ -92,6 +112,8 @@ def test_abi_zero_sized_calls_are_noops():
     assert lib.kani_kv_cache_write(1, n, n, 0, 8, 64, n, n, 16, n, 0, n, n) == 0
     assert lib.kani_rope_kv_write(1, 0, 1, 16, 8, 64, n, 0, n, 0, n, 0, n, n, n, n, 1e-5, n, 0, n, 4,
                                   n, 0, 0, n, n, 0, 0, 0, 16, n, n, n) == 0
+    assert lib.kani_sample_tokens(1, n, 0, 0, 15591, n, n, 0, 1, 1.2, 0.5, 0.85, 256, n, 0, n, n, n, n, n,
+                                  n, 1, n) == 0
     assert lib.kani_launch_count() == before
 
 
@@ -100,6 +122,7 @@ def test_abi_zero_sized_calls_are_noops():
     lambda: K.fused_add_rms_norm(torch.zeros(2, 8), torch.zeros(2, 8), torch.ones(8)),
     lambda: K.fused_silu_mul(torch.zeros(2, 16)),
     lambda: K.fused_rope(torch.zeros(1, 2, 1, 8), torch.zeros(1, 1, 1, 8), torch.zeros(8), torch.zeros(8)),
+    lambda: K.sample_tokens(torch.zeros(2, 300)),
 ])
 def test_cpu_tensors_are_refused(call):
     with pytest.raises(ValueError, match="CUDA"):

@@ -390,7 +390,8 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
     }
   }
   if (lane == 0) {
-    const int idx = s_idx[best_j < KK ? best_j : 0];
+    int idx = s_idx[best_j < KK ? best_j : 0];
+    if (idx < 0 || idx >= V) idx = 0;  // unreachable: every sorted slot holds a row index
     p.tokens[(int64_t)b * p.tokens_stride] = p.index_map ? p.index_map[idx] : (int64_t)idx;
     if (p.update_seen && p.seen) atomicOr(p.seen + (int64_t)b * p.seen_words + (idx >> 5), 1u << (idx & 31));
   }

@@ -665,8 +665,28 @@ def run_op(name: str, size: int, steps: int, warmup: int) -> dict:
     e1.record()
     torch.cuda.synchronize(dev)
     us = e0.elapsed_time(e1) * 1e3 / steps
-    return {"op": name, "size": size, "us_per_call_eager": round(us, 3), "bytes": nbytes,
-            "GB_s": round(nbytes / us / 1e3, 1)}
+    # the same calls replayed from a CUDA graph: device time without the Python launch path
+    per_graph = 50
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        fn()
+    torch.cuda.current_stream(dev).wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(per_graph):
+            fn()
+    graph.replay()
+    torch.cuda.synchronize(dev)
+    reps = max(1, steps // per_graph)
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    us_g = e0.elapsed_time(e1) * 1e3 / (reps * per_graph)
+    return {"op": name, "size": size, "us_per_call_eager": round(us, 3), "us_per_call_graph": round(us_g, 3),
+            "bytes": nbytes, "GB_s": round(nbytes / us / 1e3, 1), "GB_s_graph": round(nbytes / us_g / 1e3, 1)}
 
 
 def main():

@@ -31,12 +31,14 @@
 // orders candidates by value, then by lower index (a stable descending sort).
 //
 // Layout: one 1024-thread CTA per stream.  The penalised row is staged in
-// shared memory (coalesced loads); the k-th largest value is found by an
-// 8-bit-digit radix select over order-preserving keys (2 passes for 16-bit
-// types, 4 for f32), with equal values at the boundary taken in index order
-// through one block-wide scan; the k candidates are sorted by counting ranks;
-// one warp then runs temperature, both softmaxes, the cumulative sum and the
-// race.  No global scratch; no waits.
+// shared memory (coalesced loads) and each thread takes a contiguous block of
+// it as order-preserving keys (in registers for rows up to 16384).  The k-th
+// largest key is found by bisection on the key value: each step counts the
+// keys above a threshold with a warp reduction and one barrier (16 steps for
+// 16-bit types, 32 for f32).  Equal keys at the boundary are taken in index
+// order through one block-wide scan; the k candidates are sorted by counting
+// ranks; one warp then runs temperature, both softmaxes, the cumulative sum
+// and the race.  No global scratch; no waits.
 #include "common.cuh"
 
 #include <math.h>
@@ -47,6 +49,7 @@ namespace {
 constexpr int kSampleThreads = 1024;
 constexpr int kMaxTopK = 256;
 constexpr int kSampleMaxDynSmem = 200 * 1024;
+constexpr int kRegItems = 16;  // items per thread held in registers (rows up to 16384)
 
 struct SampleParams {
   const void* logits;
@@ -112,20 +115,19 @@ __device__ __forceinline__ float exp_draw(uint32_t w) {
   return -logf(u);
 }
 
-template <typename T>
+template <typename T, bool REG>
 __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams p) {
   using K = KeyOf<T>;
   using Raw = typename K::Raw;
   constexpr int E = VecN<T>::value;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  __shared__ uint32_t hist[256];
+  __shared__ int warp_sum[2][32];
   __shared__ int warp_tot[32];
   __shared__ unsigned long long cand_key[kMaxTopK];
   __shared__ float cand_val[kMaxTopK];
   __shared__ int cand_idx[kMaxTopK];
   __shared__ float s_val[kMaxTopK];
   __shared__ int s_idx[kMaxTopK];
-  __shared__ uint32_t sh_digit, sh_need, sh_eq;
   __shared__ int sh_ncand;
 
   T* row = reinterpret_cast<T*>(smem_raw);
@@ -149,7 +151,8 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
   __syncthreads();
 
   // this thread's block of the row: [base, base + ipt), ipt a multiple of E,
-  // read from shared memory as 16-byte vectors
+  // read from shared memory as 16-byte vectors; with REG the keys stay in
+  // registers (ipt <= kRegItems), otherwise every pass re-reads shared memory
   const int base = tid * ipt;
   auto keys_at = [&](int i, uint32_t* key) {
     const uint4 raw = *reinterpret_cast<const uint4*>(row + i);
@@ -158,111 +161,105 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
 #pragma unroll
     for (int e = 0; e < E; ++e) key[e] = K::key(v[e]);
   };
-
-  // 2. radix select of the k-th largest key
-  uint32_t pre = 0, mask_hi = 0, need = (uint32_t)KK, eq = 0;
-  for (int shift = K::kBits - 8; shift >= 0; shift -= 8) {
-    if (tid < 256) hist[tid] = 0;
-    __syncthreads();
-    for (int r = 0; r < ipt; r += E) {
-      uint32_t key[E];
-      keys_at(base + r, key);
+  uint32_t rk[REG ? kRegItems : 1];
+  if constexpr (REG) {
 #pragma unroll
-      for (int e = 0; e < E; ++e) {
-        const bool m = base + r + e < V && (key[e] & mask_hi) == pre;
-        const uint32_t d = m ? (key[e] >> shift) & 255u : 256u + (uint32_t)lane;
-        const uint32_t peers = __match_any_sync(0xffffffffu, d);
-        if (m && lane == __ffs(peers) - 1) atomicAdd(&hist[d], (uint32_t)__popc(peers));
-      }
+    for (int r = 0; r < kRegItems; r += E) {
+      if (r < ipt) keys_at(base + r, rk + r);
+#pragma unroll
+      for (int e = 0; e < E; ++e)
+        if (r >= ipt || base + r + e >= V) rk[r + e] = 0;  // never counted: thresholds are >= 1
     }
-    __syncthreads();
-    if (warp == 0) {
-      uint32_t c[8], tot = 0;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        c[j] = hist[lane * 8 + j];
-        tot += c[j];
-      }
-      uint32_t suf = tot;  // inclusive suffix over lanes lane..31
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t v = __shfl_down_sync(0xffffffffu, suf, o);
-        if (lane + o < 32) suf += v;
-      }
-      const uint32_t above = suf - tot;
-      if (above < need && need <= suf) {
-        uint32_t acc = above;
-        for (int j = 7; j >= 0; --j) {
-          if (acc + c[j] >= need) {
-            sh_digit = (uint32_t)(lane * 8 + j);
-            sh_need = need - acc;
-            sh_eq = c[j];
-            break;
-          }
-          acc += c[j];
-        }
-      }
-    }
-    __syncthreads();
-    pre |= sh_digit << shift;
-    mask_hi |= 255u << shift;
-    need = sh_need;
-    eq = sh_eq;
-    if (eq == need) break;  // the whole group is taken: no lower digits needed
   }
-
-  // 3. equal keys at the boundary are taken in index order
-  int eq_rank = 0;
-  if (eq > need) {
-    int c = 0;
-    for (int r = 0; r < ipt && base + r < V; r += E) {
-      uint32_t key[E];
-      keys_at(base + r, key);
+  // f(i, key) over this thread's items in index order
+  auto for_items = [&](auto&& f) {
+    if constexpr (REG) {
 #pragma unroll
-      for (int e = 0; e < E; ++e) c += (base + r + e < V && (key[e] & mask_hi) == pre) ? 1 : 0;
+      for (int r = 0; r < kRegItems; ++r)
+        if (r < ipt && base + r < V) f(base + r, rk[r]);
+    } else {
+      for (int r = 0; r < ipt && base + r < V; r += E) {
+        uint32_t key[E];
+        keys_at(base + r, key);
+#pragma unroll
+        for (int e = 0; e < E; ++e)
+          if (base + r + e < V) f(base + r + e, key[e]);
+      }
     }
-    int inc = c;
+  };
+  // block-wide count of keys >= t (t >= 1); every thread gets the total.
+  // Partial sums alternate between two buffers so one barrier per call suffices.
+  int parity = 0;
+  auto count_ge = [&](uint32_t t) -> int {
+    int c = 0;
+    if constexpr (REG) {
+#pragma unroll
+      for (int r = 0; r < kRegItems; ++r) c += rk[r] >= t ? 1 : 0;
+    } else {
+      for_items([&](int, uint32_t k) { c += k >= t ? 1 : 0; });
+    }
+    c = __reduce_add_sync(0xffffffffu, c);
+    if (lane == 0) warp_sum[parity][warp] = c;
+    __syncthreads();
+    const int tot = __reduce_add_sync(0xffffffffu, warp_sum[parity][lane]);
+    parity ^= 1;
+    return tot;
+  };
+
+  // 2. the k-th largest key v: the largest t with count(key >= t) >= k,
+  //    by bisection over the key range (16 steps for 16-bit types, 32 for f32)
+  uint64_t lo = 0, hi = 1ull << K::kBits;   // count(>= lo) >= k > count(>= hi)
+  int c_hi = 0;
+  while (hi - lo > 1) {
+    const uint64_t mid = (lo + hi) >> 1;
+    const int c = count_ge((uint32_t)mid);
+    if (c >= KK) {
+      lo = mid;
+    } else {
+      hi = mid;
+      c_hi = c;
+    }
+  }
+  const uint32_t vk = (uint32_t)lo;
+  const int need = KK - c_hi;              // keys equal to vk to take, lowest indices first
+
+  // 3. rank of this thread's first equal key among all equal keys (index order)
+  int c_eq = 0;
+  for_items([&](int, uint32_t k) { c_eq += k == vk ? 1 : 0; });
+  int inc = c_eq;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += v;
+  }
+  if (lane == 31) warp_tot[warp] = inc;
+  __syncthreads();
+  if (warp == 0) {
+    const int t = warp_tot[lane];
+    int ti = t;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const int v = __shfl_up_sync(0xffffffffu, inc, o);
-      if (lane >= o) inc += v;
+      const int v = __shfl_up_sync(0xffffffffu, ti, o);
+      if (lane >= o) ti += v;
     }
-    if (lane == 31) warp_tot[warp] = inc;
-    __syncthreads();
-    if (warp == 0) {
-      const int t = warp_tot[lane];
-      int ti = t;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int v = __shfl_up_sync(0xffffffffu, ti, o);
-        if (lane >= o) ti += v;
-      }
-      warp_tot[lane] = ti - t;
-    }
-    __syncthreads();
-    eq_rank = warp_tot[warp] + inc - c;
+    warp_tot[lane] = ti - t;
   }
+  __syncthreads();
+  int eq_rank = warp_tot[warp] + inc - c_eq;
 
   // 4. gather the k candidates (unordered)
-  for (int r = 0; r < ipt && base + r < V; r += E) {
-    uint32_t key[E];
-    keys_at(base + r, key);
-#pragma unroll
-    for (int e = 0; e < E; ++e) {
-      const int i = base + r + e;
-      const uint32_t hk = key[e] & mask_hi;
-      bool take = i < V && hk > pre;
-      if (i < V && hk == pre) take = (uint32_t)(eq_rank++) < need;
-      if (take) {
-        const int slot = atomicAdd(&sh_ncand, 1);
-        if (slot < kMaxTopK) {  // exactly top_k items qualify; the guard only bounds the store
-          cand_key[slot] = ((unsigned long long)key[e] << 32) | (unsigned long long)(0xffffffffu - (uint32_t)i);
-          cand_val[slot] = Elem<T>::to_f(row[i]);
-          cand_idx[slot] = i;
-        }
+  for_items([&](int i, uint32_t k) {
+    bool take = k > vk;
+    if (k == vk) take = eq_rank++ < need;
+    if (take) {
+      const int slot = atomicAdd(&sh_ncand, 1);
+      if (slot < kMaxTopK) {  // exactly top_k items qualify; the guard only bounds the store
+        cand_key[slot] = ((unsigned long long)k << 32) | (unsigned long long)(0xffffffffu - (uint32_t)i);
+        cand_val[slot] = Elem<T>::to_f(row[i]);
+        cand_idx[slot] = i;
       }
     }
-  }
+  });
   __syncthreads();
 
   // 5. sort descending by (value, -index): rank = number of larger keys
@@ -405,9 +402,10 @@ int launch_sample(SampleParams prm, int64_t batch, cudaStream_t s) {
   const size_t smem = (size_t)ipt * kSampleThreads * sizeof(T);
   if (smem > (size_t)kSampleMaxDynSmem) return KANI_ERR_UNSUPPORTED;
   prm.ipt = ipt;
-  cudaError_t e = cudaFuncSetAttribute(sample_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  auto kern = ipt <= kRegItems ? sample_kernel<T, true> : sample_kernel<T, false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return (int)e;
-  sample_kernel<T><<<(unsigned)batch, kSampleThreads, smem, s>>>(prm);
+  kern<<<(unsigned)batch, kSampleThreads, smem, s>>>(prm);
   return launch_status();
 }
 

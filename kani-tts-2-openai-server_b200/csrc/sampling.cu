@@ -33,12 +33,14 @@
 // Layout: one 1024-thread CTA per stream.  The penalised row is staged in
 // shared memory (coalesced loads) and each thread takes a contiguous block of
 // it as order-preserving keys (in registers for rows up to 16384).  The k-th
-// largest key is found by bisection on the key value: each step counts the
-// keys above a threshold with a warp reduction and one barrier (16 steps for
-// 16-bit types, 32 for f32).  Equal keys at the boundary are taken in index
-// order through one block-wide scan; the k candidates are sorted by counting
-// ranks; one warp then runs temperature, both softmaxes, the cumulative sum
-// and the race.  No global scratch; no waits.
+// largest key is found by bisection on the key value inside a bracket below
+// the row's largest key: each step counts the keys above a threshold with a
+// warp reduction and one barrier (about 11 steps for 16-bit types).  One
+// block scan gives every key above the threshold a slot and places the equal
+// keys taken at the boundary (lowest indices first) directly at their sorted
+// positions; the keys above are sorted by counting ranks.  One warp then runs
+// temperature, both softmaxes, the cumulative sum (one lane's in-order add
+// chain) and the race.  No global scratch; no waits.
 #include "common.cuh"
 
 #include <math.h>
@@ -50,6 +52,7 @@ constexpr int kSampleThreads = 1024;
 constexpr int kMaxTopK = 256;
 constexpr int kSampleMaxDynSmem = 200 * 1024;
 constexpr int kRegItems = 16;  // items per thread held in registers (rows up to 16384)
+constexpr int kStageBatch = 16;  // row loads in flight per thread while staging
 
 struct SampleParams {
   const void* logits;
@@ -120,34 +123,62 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
   using K = KeyOf<T>;
   using Raw = typename K::Raw;
   constexpr int E = VecN<T>::value;
+  constexpr int P = kMaxTopK / 32;  // sorted positions per lane of the final warp
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  __shared__ int warp_sum[2][32];
+  __shared__ int warp_sum[2][3][32];
+  __shared__ uint32_t warp_max[32];
   __shared__ int warp_tot[32];
   __shared__ unsigned long long cand_key[kMaxTopK];
   __shared__ float cand_val[kMaxTopK];
   __shared__ int cand_idx[kMaxTopK];
   __shared__ float s_val[kMaxTopK];
   __shared__ int s_idx[kMaxTopK];
-  __shared__ int sh_ncand;
+  __shared__ __align__(16) float s_prob[kMaxTopK];
+  __shared__ long long s_tok[kMaxTopK];
 
   T* row = reinterpret_cast<T*>(smem_raw);
   const int b = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int V = p.vocab, KK = p.top_k, ipt = p.ipt;
-  const T* src = static_cast<const T*>(p.logits) + (int64_t)b * p.row_stride;
-  const T* bias = static_cast<const T*>(p.bias);
+  const Raw* src = reinterpret_cast<const Raw*>(static_cast<const T*>(p.logits) + (int64_t)b * p.row_stride);
+  const Raw* bias = static_cast<const Raw*>(p.bias);
   const uint32_t* seen = p.seen ? p.seen + (int64_t)b * p.seen_words : nullptr;
   const bool pen = seen != nullptr && p.penalty != 1.0f;
+  auto as_f = [](Raw r) {
+    T t;
+    memcpy(&t, &r, sizeof(Raw));
+    return Elem<T>::to_f(t);
+  };
 
-  // 1. stage the (penalised, biased) row in shared memory, coalesced
-  for (int i = tid; i < V; i += kSampleThreads) {
-    float v = Elem<T>::to_f(src[i]);
-    if (pen && ((__ldg(seen + (i >> 5)) >> (i & 31)) & 1u))
-      v = round_to<T>(v > 0.f ? __fdiv_rn(v, p.penalty) : __fmul_rn(v, p.penalty));
-    if (bias) v = round_to<T>(__fadd_rn(v, Elem<T>::to_f(bias[i])));
-    row[i] = Elem<T>::from_f(v);
+  // 1. stage the row in shared memory: penalty, then bias, per element (the
+  //    reference's order); loads of a batch are all in flight before any use
+  for (int i0 = 0; i0 < V; i0 += kStageBatch * kSampleThreads) {
+    Raw raw[kStageBatch], braw[kStageBatch];
+    uint32_t word[kStageBatch];
+#pragma unroll
+    for (int r = 0; r < kStageBatch; ++r) {
+      const int i = i0 + r * kSampleThreads + tid;
+      raw[r] = 0;
+      braw[r] = 0;
+      word[r] = 0;
+      if (i < V) {
+        raw[r] = __ldg(src + i);
+        if (pen) word[r] = __ldg(seen + (i >> 5));
+        if (bias) braw[r] = __ldg(bias + i);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < kStageBatch; ++r) {
+      const int i = i0 + r * kSampleThreads + tid;
+      if (i < V) {
+        float v = as_f(raw[r]);
+        if ((word[r] >> (i & 31)) & 1u)
+          v = round_to<T>(v > 0.f ? __fdiv_rn(v, p.penalty) : __fmul_rn(v, p.penalty));
+        if (bias) v = round_to<T>(__fadd_rn(v, as_f(braw[r])));
+        row[i] = Elem<T>::from_f(v);
+      }
+    }
   }
-  if (tid == 0) sh_ncand = 0;
   __syncthreads();
 
   // this thread's block of the row: [base, base + ipt), ipt a multiple of E,
@@ -187,32 +218,74 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
       }
     }
   };
-  // block-wide count of keys >= t (t >= 1); every thread gets the total.
-  // Partial sums alternate between two buffers so one barrier per call suffices.
+  // block-wide counts of keys >= t[0..N) (each t >= 1); every thread gets the
+  // totals.  Partial sums alternate between two buffers: one barrier per call.
   int parity = 0;
-  auto count_ge = [&](uint32_t t) -> int {
-    int c = 0;
+  auto count_ge = [&]<int N>(const uint32_t* t, int* tot) {
+    int c[N];
+#pragma unroll
+    for (int n = 0; n < N; ++n) c[n] = 0;
     if constexpr (REG) {
 #pragma unroll
-      for (int r = 0; r < kRegItems; ++r) c += rk[r] >= t ? 1 : 0;
+      for (int r = 0; r < kRegItems; ++r)
+#pragma unroll
+        for (int n = 0; n < N; ++n) c[n] += rk[r] >= t[n] ? 1 : 0;
     } else {
-      for_items([&](int, uint32_t k) { c += k >= t ? 1 : 0; });
+      for_items([&](int, uint32_t k) {
+#pragma unroll
+        for (int n = 0; n < N; ++n) c[n] += k >= t[n] ? 1 : 0;
+      });
     }
-    c = __reduce_add_sync(0xffffffffu, c);
-    if (lane == 0) warp_sum[parity][warp] = c;
+#pragma unroll
+    for (int n = 0; n < N; ++n) {
+      c[n] = __reduce_add_sync(0xffffffffu, c[n]);
+      if (lane == 0) warp_sum[parity][n][warp] = c[n];
+    }
     __syncthreads();
-    const int tot = __reduce_add_sync(0xffffffffu, warp_sum[parity][lane]);
+#pragma unroll
+    for (int n = 0; n < N; ++n) tot[n] = __reduce_add_sync(0xffffffffu, warp_sum[parity][n][lane]);
     parity ^= 1;
-    return tot;
   };
 
-  // 2. the k-th largest key v: the largest t with count(key >= t) >= k,
-  //    by bisection over the key range (16 steps for 16-bit types, 32 for f32)
-  uint64_t lo = 0, hi = 1ull << K::kBits;   // count(>= lo) >= k > count(>= hi)
+  // 2. the k-th largest key vk: the largest t with count(key >= t) >= k.
+  //    Bracket it below the row's largest key (spans 2^(B-9), 2^(B-7), 2^(B-5)
+  //    for B-bit keys, one barrier), then bisect inside the bracket.
+  uint32_t mk = 0;
+  for_items([&](int, uint32_t k) { mk = k > mk ? k : mk; });
+  mk = __reduce_max_sync(0xffffffffu, mk);
+  if (lane == 0) warp_max[warp] = mk;
+  __syncthreads();
+  const uint32_t maxk = __reduce_max_sync(0xffffffffu, warp_max[lane]);
+  uint64_t hi = (uint64_t)maxk + 1, lo = 0;  // invariant: count(>= lo) >= k > count(>= hi) = c_hi
   int c_hi = 0;
+  {
+    uint32_t t[3];
+    int c[3];
+#pragma unroll
+    for (int n = 0; n < 3; ++n) {
+      const uint64_t w = 1ull << (K::kBits - 9 + 2 * n);
+      t[n] = hi > w ? (uint32_t)(hi - w) : 1u;
+    }
+    count_ge.template operator()<3>(t, c);
+    if (c[0] >= KK) {
+      lo = t[0];
+    } else if (c[1] >= KK) {
+      lo = t[1];
+      hi = t[0];
+      c_hi = c[0];
+    } else if (c[2] >= KK) {
+      lo = t[2];
+      hi = t[1];
+      c_hi = c[1];
+    } else {
+      hi = t[2];
+      c_hi = c[2];
+    }
+  }
   while (hi - lo > 1) {
-    const uint64_t mid = (lo + hi) >> 1;
-    const int c = count_ge((uint32_t)mid);
+    const uint32_t mid = (uint32_t)((lo + hi) >> 1);
+    int c;
+    count_ge.template operator()<1>(&mid, &c);
     if (c >= KK) {
       lo = mid;
     } else {
@@ -221,12 +294,13 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
     }
   }
   const uint32_t vk = (uint32_t)lo;
-  const int need = KK - c_hi;              // keys equal to vk to take, lowest indices first
+  const int need = KK - c_hi;  // keys equal to vk to take, lowest indices first
 
-  // 3. rank of this thread's first equal key among all equal keys (index order)
-  int c_eq = 0;
-  for_items([&](int, uint32_t k) { c_eq += k == vk ? 1 : 0; });
-  int inc = c_eq;
+  // 3. one block scan of (greater, equal) counts packed as eq << 9 | gt
+  //    (the greater total is < k <= 256)
+  int c_pack = 0;
+  for_items([&](int, uint32_t k) { c_pack += k > vk ? 1 : (k == vk ? 512 : 0); });
+  int inc = c_pack;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const int v = __shfl_up_sync(0xffffffffu, inc, o);
@@ -245,31 +319,41 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
     warp_tot[lane] = ti - t;
   }
   __syncthreads();
-  int eq_rank = warp_tot[warp] + inc - c_eq;
+  const int excl = warp_tot[warp] + inc - c_pack;
+  int gt_slot = excl & 511, eq_rank = excl >> 9;
 
-  // 4. gather the k candidates (unordered)
+  // 4. greater keys to candidate slots [0, c_hi) (sorted next); the taken equal
+  //    keys are already in order: sorted positions [c_hi, k)
   for_items([&](int i, uint32_t k) {
-    bool take = k > vk;
-    if (k == vk) take = eq_rank++ < need;
-    if (take) {
-      const int slot = atomicAdd(&sh_ncand, 1);
-      if (slot < kMaxTopK) {  // exactly top_k items qualify; the guard only bounds the store
+    if (k > vk) {
+      const int slot = gt_slot++;
+      if (slot < kMaxTopK) {
         cand_key[slot] = ((unsigned long long)k << 32) | (unsigned long long)(0xffffffffu - (uint32_t)i);
         cand_val[slot] = Elem<T>::to_f(row[i]);
         cand_idx[slot] = i;
       }
+    } else if (k == vk) {
+      if (eq_rank < need) {
+        const int pos = c_hi + eq_rank;
+        s_val[pos] = Elem<T>::to_f(row[i]);
+        s_idx[pos] = i;
+      }
+      ++eq_rank;
     }
   });
   __syncthreads();
 
-  // 5. sort descending by (value, -index): rank = number of larger keys
+  // 5. sort the greater keys descending (all distinct): rank = number larger
   {
     const int j = tid >> 2, q = tid & 3;
-    const bool act = j < KK;
+    const bool act = j < c_hi;
     const unsigned long long kj = act ? cand_key[j] : 0ull;
     int rank = 0;
-    if (act)
-      for (int i = q; i < KK; i += 4) rank += cand_key[i] > kj ? 1 : 0;
+    if (act) {
+      const int i1 = min(c_hi, (q + 1) * (kMaxTopK / 4));
+#pragma unroll 8
+      for (int i = q * (kMaxTopK / 4); i < i1; ++i) rank += cand_key[i] > kj ? 1 : 0;
+    }
     rank += __shfl_xor_sync(0xffffffffu, rank, 1);
     rank += __shfl_xor_sync(0xffffffffu, rank, 2);
     if (act && q == 0) {
@@ -280,12 +364,35 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
   __syncthreads();
   if (warp != 0) return;
 
-  // 6. one warp: lane owns sorted positions lane*8 .. lane*8+7
-  constexpr int P = kMaxTopK / 32;
+  // 6. one warp: lane owns sorted positions lane*P .. lane*P+P-1.  The draws
+  //    and the token ids of the candidates are fetched first (independent of
+  //    the probabilities).
+  float draw[P];
+  if (p.draws) {
+#pragma unroll
+    for (int e = 0; e < P; ++e) {
+      const int j = lane * P + e;
+      draw[e] = j < KK ? __ldg(p.draws + (int64_t)b * KK + j) : 1.f;
+    }
+  } else {
+    const uint64_t step = p.step ? (uint64_t)*p.step : 0ull;
+    const uint2 key = make_uint2((uint32_t)p.seed, (uint32_t)(p.seed >> 32));
+#pragma unroll
+    for (int h = 0; h < P / 4; ++h) {
+      const uint4 w = philox4x32_10(
+          make_uint4((uint32_t)(lane * (P / 4) + h), (uint32_t)b, (uint32_t)step, (uint32_t)(step >> 32)), key);
+      draw[h * 4 + 0] = exp_draw(w.x);
+      draw[h * 4 + 1] = exp_draw(w.y);
+      draw[h * 4 + 2] = exp_draw(w.z);
+      draw[h * 4 + 3] = exp_draw(w.w);
+    }
+  }
   float x[P];
 #pragma unroll
   for (int e = 0; e < P; ++e) {
     const int j = lane * P + e;
+    const int idx = j < KK ? s_idx[j] : 0;
+    if (j < KK) s_tok[j] = p.index_map ? __ldg(p.index_map + idx) : (long long)idx;
     float v = j < KK ? s_val[j] : -INFINITY;
     if (j < KK && p.temperature != 1.0f) v = round_to<T>(__fdiv_rn(v, p.temperature));
     x[e] = v;
@@ -312,55 +419,39 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
   if (p.top_p < 1.0f) {
     softmax(KK, pr);
     // first dropped position: smallest j >= 1 with round(c[j-1]) >= round(top_p),
-    // c accumulated in order; each lane scans its 8 with the carry of the lanes before
-    using Acc = typename CumAcc<T>::type;
-    const float thr = round_to<T>(p.top_p);
-    int cut = KK;
-    Acc carry = 0;
-    for (int l = 0; l < 32 && cut == KK && l * P < KK; ++l) {
-      int lcut = KK;
-      Acc c = carry;
-      if (lane == l) {
+    // c the in-order running sum; one lane runs the add chain 8 positions at a time
+    float4* sp4 = reinterpret_cast<float4*>(s_prob);
+    sp4[lane * 2] = make_float4(pr[0], pr[1], pr[2], pr[3]);
+    sp4[lane * 2 + 1] = make_float4(pr[4], pr[5], pr[6], pr[7]);
+    __syncwarp();
+    if (lane == 0) {
+      using Acc = typename CumAcc<T>::type;
+      const float thr = round_to<T>(p.top_p);
+      Acc c = 0;
+      for (int j0 = 0; j0 < KK - 1; j0 += 8) {
+        const float4 a = sp4[j0 / 4], bq = sp4[j0 / 4 + 1];
+        const float pv[8] = {a.x, a.y, a.z, a.w, bq.x, bq.y, bq.z, bq.w};
+        Acc cs[8];
 #pragma unroll
-        for (int e = 0; e < P; ++e) {
-          const int j = l * P + e;
-          if (j + 1 >= KK) break;
-          c += (Acc)pr[e];
-          if (round_to<T>((float)c) >= thr) {
-            lcut = j + 1;
-            break;
-          }
+        for (int e = 0; e < 8; ++e) {
+          c += (Acc)pv[e];
+          cs[e] = c;
+        }
+        int hit = 8;
+#pragma unroll
+        for (int e = 7; e >= 0; --e)
+          if (j0 + e + 1 < KK && round_to<T>((float)cs[e]) >= thr) hit = e;
+        if (hit < 8) {
+          keep = j0 + hit + 1;
+          break;
         }
       }
-      lcut = __shfl_sync(0xffffffffu, lcut, l);
-      if (lcut < KK) cut = lcut;
-      carry = __shfl_sync(0xffffffffu, c, l);
     }
-    keep = cut;
+    keep = __shfl_sync(0xffffffffu, keep, 0);
   }
   softmax(keep, pr);
 
-  // 7. exponential race over the kept candidates
-  float draw[P];
-  if (p.draws) {
-#pragma unroll
-    for (int e = 0; e < P; ++e) {
-      const int j = lane * P + e;
-      draw[e] = j < KK ? p.draws[(int64_t)b * KK + j] : 1.f;
-    }
-  } else {
-    const uint64_t step = p.step ? (uint64_t)*p.step : 0ull;
-    const uint2 key = make_uint2((uint32_t)p.seed, (uint32_t)(p.seed >> 32));
-#pragma unroll
-    for (int h = 0; h < P / 4; ++h) {
-      const uint4 w = philox4x32_10(
-          make_uint4((uint32_t)(lane * (P / 4) + h), (uint32_t)b, (uint32_t)step, (uint32_t)(step >> 32)), key);
-      draw[h * 4 + 0] = exp_draw(w.x);
-      draw[h * 4 + 1] = exp_draw(w.y);
-      draw[h * 4 + 2] = exp_draw(w.z);
-      draw[h * 4 + 3] = exp_draw(w.w);
-    }
-  }
+  // 7. exponential race over the kept candidates: first maximum of round(p / round(E))
   float best = -1.f;
   int best_j = 0x7fffffff;
 #pragma unroll
@@ -386,10 +477,12 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
       best_j = oj;
     }
   }
+  if (best_j >= KK) best_j = 0;  // unreachable: position 0 always has a positive score
+  __syncwarp();
   if (lane == 0) {
-    int idx = s_idx[best_j < KK ? best_j : 0];
+    int idx = s_idx[best_j];
     if (idx < 0 || idx >= V) idx = 0;  // unreachable: every sorted slot holds a row index
-    p.tokens[(int64_t)b * p.tokens_stride] = p.index_map ? p.index_map[idx] : (int64_t)idx;
+    p.tokens[(int64_t)b * p.tokens_stride] = s_tok[best_j];
     if (p.update_seen && p.seen) atomicOr(p.seen + (int64_t)b * p.seen_words + (idx >> 5), 1u << (idx & 31));
   }
 }

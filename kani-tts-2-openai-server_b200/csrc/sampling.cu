@@ -95,6 +95,11 @@ template <> struct KeyOf<float> {
   }
 };
 
+// Smallest value of a 16-bit type that is a multiple of 2^-24 together with
+// every larger value: bf16 from 2^-17 (8 significant bits); every fp16 value is.
+template <typename T> constexpr float kExactMin = 0.f;
+template <> constexpr float kExactMin<__nv_bfloat16> = 7.62939453125e-06f;  // 2^-17
+
 // Cumulative-sum accumulator type of torch's CPU kernel for the dtype.
 template <typename T> struct CumAcc { using type = float; };
 template <> struct CumAcc<float> { using type = double; };
@@ -128,13 +133,13 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
   __shared__ int warp_sum[2][3][32];
   __shared__ uint32_t warp_max[32];
   __shared__ int warp_tot[32];
-  __shared__ unsigned long long cand_key[kMaxTopK];
+  __shared__ __align__(16) unsigned long long cand_key[kMaxTopK];
+  __shared__ int rank_part[kSampleThreads / kMaxTopK][kMaxTopK];
   __shared__ float cand_val[kMaxTopK];
   __shared__ int cand_idx[kMaxTopK];
   __shared__ float s_val[kMaxTopK];
   __shared__ int s_idx[kMaxTopK];
   __shared__ __align__(16) float s_prob[kMaxTopK];
-  __shared__ long long s_tok[kMaxTopK];
 
   T* row = reinterpret_cast<T*>(smem_raw);
   const int b = blockIdx.x;
@@ -154,25 +159,30 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
   //    reference's order); loads of a batch are all in flight before any use
   for (int i0 = 0; i0 < V; i0 += kStageBatch * kSampleThreads) {
     Raw raw[kStageBatch], braw[kStageBatch];
-    uint32_t word[kStageBatch];
+    // the 32 elements of a warp in round r share bitmap word (i0 + r * 1024) / 32 + warp;
+    // lane r fetches the word of round r
+    uint32_t myword = 0;
+    {
+      const int w = (i0 >> 5) + lane * (kSampleThreads / 32) + warp;
+      if (pen && lane < kStageBatch && w < (V + 31) / 32) myword = __ldg(seen + w);
+    }
 #pragma unroll
     for (int r = 0; r < kStageBatch; ++r) {
       const int i = i0 + r * kSampleThreads + tid;
       raw[r] = 0;
       braw[r] = 0;
-      word[r] = 0;
       if (i < V) {
         raw[r] = __ldg(src + i);
-        if (pen) word[r] = __ldg(seen + (i >> 5));
         if (bias) braw[r] = __ldg(bias + i);
       }
     }
 #pragma unroll
     for (int r = 0; r < kStageBatch; ++r) {
       const int i = i0 + r * kSampleThreads + tid;
+      const uint32_t word = __shfl_sync(0xffffffffu, myword, r);
       if (i < V) {
         float v = as_f(raw[r]);
-        if ((word[r] >> (i & 31)) & 1u)
+        if ((word >> (i & 31)) & 1u)
           v = round_to<T>(v > 0.f ? __fdiv_rn(v, p.penalty) : __fmul_rn(v, p.penalty));
         if (bias) v = round_to<T>(__fadd_rn(v, as_f(braw[r])));
         row[i] = Elem<T>::from_f(v);
@@ -343,23 +353,35 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
   });
   __syncthreads();
 
-  // 5. sort the greater keys descending (all distinct): rank = number larger
+  // 5. sort the greater keys descending (all distinct): rank = number larger.
+  //    Thread (q, j) counts over quarter q of the keys; a warp reads one key
+  //    pair per step at a single address (a broadcast).
   {
-    const int j = tid >> 2, q = tid & 3;
-    const bool act = j < c_hi;
-    const unsigned long long kj = act ? cand_key[j] : 0ull;
-    int rank = 0;
-    if (act) {
-      const int i1 = min(c_hi, (q + 1) * (kMaxTopK / 4));
+    const int j = tid & (kMaxTopK - 1), q = tid / kMaxTopK;
+    constexpr int QN = kMaxTopK / (kSampleThreads / kMaxTopK);
+    int part = 0;
+    if (q * QN < c_hi) {
+      const unsigned long long kj = j < c_hi ? cand_key[j] : ~0ull;
+      const ulonglong2* ck2 = reinterpret_cast<const ulonglong2*>(cand_key + q * QN);
+      const int n = min(QN, c_hi - q * QN);
 #pragma unroll 8
-      for (int i = q * (kMaxTopK / 4); i < i1; ++i) rank += cand_key[i] > kj ? 1 : 0;
+      for (int m = 0; m < QN / 2; ++m) {
+        if (2 * m < n) {
+          const ulonglong2 kk = ck2[m];
+          part += kk.x > kj ? 1 : 0;
+          part += (2 * m + 1 < n && kk.y > kj) ? 1 : 0;
+        }
+      }
     }
-    rank += __shfl_xor_sync(0xffffffffu, rank, 1);
-    rank += __shfl_xor_sync(0xffffffffu, rank, 2);
-    if (act && q == 0) {
-      s_val[rank] = cand_val[j];
-      s_idx[rank] = cand_idx[j];
-    }
+    rank_part[q][j] = part;
+  }
+  __syncthreads();
+  if (tid < c_hi) {
+    int rank = 0;
+#pragma unroll
+    for (int q = 0; q < kSampleThreads / kMaxTopK; ++q) rank += rank_part[q][tid];
+    s_val[rank] = cand_val[tid];
+    s_idx[rank] = cand_idx[tid];
   }
   __syncthreads();
   if (warp != 0) return;
@@ -392,7 +414,7 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
   for (int e = 0; e < P; ++e) {
     const int j = lane * P + e;
     const int idx = j < KK ? s_idx[j] : 0;
-    if (j < KK) s_tok[j] = p.index_map ? __ldg(p.index_map + idx) : (long long)idx;
+    if (j < KK && p.index_map) asm volatile("prefetch.L1 [%0];" ::"l"(p.index_map + idx));
     float v = j < KK ? s_val[j] : -INFINITY;
     if (j < KK && p.temperature != 1.0f) v = round_to<T>(__fdiv_rn(v, p.temperature));
     x[e] = v;
@@ -419,35 +441,85 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
   if (p.top_p < 1.0f) {
     softmax(KK, pr);
     // first dropped position: smallest j >= 1 with round(c[j-1]) >= round(top_p),
-    // c the in-order running sum; one lane runs the add chain 8 positions at a time
-    float4* sp4 = reinterpret_cast<float4*>(s_prob);
-    sp4[lane * 2] = make_float4(pr[0], pr[1], pr[2], pr[3]);
-    sp4[lane * 2 + 1] = make_float4(pr[4], pr[5], pr[6], pr[7]);
-    __syncwarp();
-    if (lane == 0) {
-      using Acc = typename CumAcc<T>::type;
-      const float thr = round_to<T>(p.top_p);
-      Acc c = 0;
-      for (int j0 = 0; j0 < KK - 1; j0 += 8) {
-        const float4 a = sp4[j0 / 4], bq = sp4[j0 / 4 + 1];
-        const float pv[8] = {a.x, a.y, a.z, a.w, bq.x, bq.y, bq.z, bq.w};
-        Acc cs[8];
+    // c the in-order running sum (fp32; double for f32).  Every value of a
+    // 16-bit type at or above kExactMin<T> is a multiple of 2^-24, so while the
+    // sum stays below 1 every partial sum is exact whatever the order: a warp
+    // scan then gives the in-order sums bit for bit.  Otherwise one lane runs
+    // the in-order add chain.
+    const float thr = round_to<T>(p.top_p);
+    bool done = false;
+    if constexpr (sizeof(T) == 2) {
+      float loc[P], run = 0.f;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          c += (Acc)pv[e];
-          cs[e] = c;
-        }
-        int hit = 8;
+      for (int e = 0; e < P; ++e) {
+        run = __fadd_rn(run, pr[e]);
+        loc[e] = run;
+      }
+      float incl = run;  // inclusive scan of lane totals
 #pragma unroll
-        for (int e = 7; e >= 0; --e)
-          if (j0 + e + 1 < KK && round_to<T>((float)cs[e]) >= thr) hit = e;
-        if (hit < 8) {
-          keep = j0 + hit + 1;
-          break;
-        }
+      for (int o = 1; o < 32; o <<= 1) {
+        const float v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl = __fadd_rn(incl, v);
+      }
+      float ex = __shfl_up_sync(0xffffffffu, incl, 1);
+      if (lane == 0) ex = 0.f;
+      int first = P;  // first position of this lane whose sum reaches the threshold
+#pragma unroll
+      for (int e = P - 1; e >= 0; --e) {
+        const int j = lane * P + e;
+        if (j + 1 < KK && round_to<T>(__fadd_rn(ex, loc[e])) >= thr) first = e;
+      }
+      const uint32_t any = __ballot_sync(0xffffffffu, first < P);
+      const int hl = any ? __ffs(any) - 1 : 31;  // lane holding the decisive position
+      const int he = __shfl_sync(0xffffffffu, first, hl);
+      const int jd = any ? hl * P + he : KK - 2;  // last position whose sum is used
+      // exact up to jd when every value there is >= kExactMin<T> and the sum at
+      // jd (the largest: the values are non-negative) is below 1; a computed sum
+      // below 1 implies every partial sum below 1 (rounding is monotone)
+      uint32_t pmin = 0xffffffffu;  // non-negative floats order like their bits
+      float sd = 0.f;
+#pragma unroll
+      for (int e = 0; e < P; ++e) {
+        const int j = lane * P + e;
+        if (j <= jd) pmin = min(pmin, __float_as_uint(pr[e]));
+        if (j == jd) sd = __fadd_rn(ex, loc[e]);
+      }
+      pmin = __reduce_min_sync(0xffffffffu, pmin);
+      sd = __shfl_sync(0xffffffffu, sd, jd < 0 ? 0 : jd / P);
+      if (jd < 0 || (__uint_as_float(pmin) >= kExactMin<T> && sd < 1.0f)) {
+        keep = any ? jd + 1 : KK;
+        done = true;
       }
     }
-    keep = __shfl_sync(0xffffffffu, keep, 0);
+    if (!done) {
+      float4* sp4 = reinterpret_cast<float4*>(s_prob);
+      sp4[lane * 2] = make_float4(pr[0], pr[1], pr[2], pr[3]);
+      sp4[lane * 2 + 1] = make_float4(pr[4], pr[5], pr[6], pr[7]);
+      __syncwarp();
+      if (lane == 0) {
+        using Acc = typename CumAcc<T>::type;
+        Acc c = 0;
+        for (int j0 = 0; j0 < KK - 1; j0 += 8) {
+          const float4 a = sp4[j0 / 4], bq = sp4[j0 / 4 + 1];
+          const float pv[8] = {a.x, a.y, a.z, a.w, bq.x, bq.y, bq.z, bq.w};
+          Acc cs[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            c += (Acc)pv[e];
+            cs[e] = c;
+          }
+          int hit = 8;
+#pragma unroll
+          for (int e = 7; e >= 0; --e)
+            if (j0 + e + 1 < KK && round_to<T>((float)cs[e]) >= thr) hit = e;
+          if (hit < 8) {
+            keep = j0 + hit + 1;
+            break;
+          }
+        }
+      }
+      keep = __shfl_sync(0xffffffffu, keep, 0);
+    }
   }
   softmax(keep, pr);
 
@@ -478,11 +550,10 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
     }
   }
   if (best_j >= KK) best_j = 0;  // unreachable: position 0 always has a positive score
-  __syncwarp();
   if (lane == 0) {
     int idx = s_idx[best_j];
     if (idx < 0 || idx >= V) idx = 0;  // unreachable: every sorted slot holds a row index
-    p.tokens[(int64_t)b * p.tokens_stride] = s_tok[best_j];
+    p.tokens[(int64_t)b * p.tokens_stride] = p.index_map ? __ldg(p.index_map + idx) : (int64_t)idx;
     if (p.update_seen && p.seen) atomicOr(p.seen + (int64_t)b * p.seen_words + (idx >> 5), 1u << (idx & 31));
   }
 }

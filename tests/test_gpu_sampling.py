@@ -121,7 +121,8 @@ def test_sampler_batch_with_ties_vs_oracle(dtype, rp, temp, top_p):
 
 
 @pytest.mark.parametrize("case", ["small_vocab", "all_equal", "masked_half", "top_k_1", "top_p_0",
-                                  "vocab_1", "full_vocab_bf16", "large_vocab_f32"])
+                                  "vocab_1", "full_vocab_bf16", "large_vocab_f32", "top_p_near_one",
+                                  "peaked_fp16"])
 def test_sampler_edge_cases(case):
     g = torch.Generator().manual_seed(31)
     dtype, top_k, top_p, temp, bias = torch.bfloat16, 256, 0.85, 0.5, None
@@ -143,6 +144,16 @@ def test_sampler_edge_cases(case):
         logits = torch.randn(3, 1, generator=g).to(dtype)
     elif case == "full_vocab_bf16":
         logits = (torch.randn(2, VOCAB, generator=g) * 2).to(dtype)
+    elif case == "top_p_near_one":
+        # one dominant candidate: the running sum reaches bf16(0.9999) = 1 only
+        # through values below 2^-17 (the kernel's in-order fallback chain)
+        logits = (torch.randn(3, N_RED, generator=g) * 0.5).to(dtype)
+        logits[:, 5] = 14.0
+        top_p, temp = 0.9999, 1.0
+    elif case == "peaked_fp16":
+        dtype = torch.float16
+        logits = (torch.randn(3, N_RED, generator=g) * 3).to(dtype)
+        top_p, temp = 0.99, 0.3
     else:
         dtype = torch.float32
         logits = torch.randn(2, 40000, generator=g) * 2

@@ -538,6 +538,136 @@ def run_decode(dev, world, rank, batch: int, steps: int, prompt: int = 128, eage
     return out
 
 
+def _reference_host_sample(logits, history, f2r, r2f, rp: float, temp: float, top_p: float):
+    """One token as the reference samples it on the host side of its decode loop
+    (KaniInferenceEngine._sample_next_token, inference_engine.py:349-430, reduced
+    vocabulary): eager ops on the device tensors, `unique()` and the implicit sync
+    of `valid.any()`, then `torch.multinomial`."""
+    if rp != 1.0:
+        unique_tokens = history[0].unique()
+        reduced_idx = f2r[unique_tokens]
+        valid = reduced_idx >= 0
+        if valid.any():
+            vr = reduced_idx[valid]
+            pl = logits[0, vr]
+            logits[0, vr] = torch.where(pl > 0, pl / rp, pl * rp)
+    k = min(256, logits.shape[-1])
+    tl, ti = torch.topk(logits, k=k, dim=-1)
+    if temp != 1.0:
+        tl = tl / temp
+    if top_p < 1.0:
+        probs = torch.softmax(tl, dim=-1)
+        cum = torch.cumsum(probs, dim=-1)
+        mask = torch.zeros_like(cum, dtype=torch.bool)
+        mask[..., 1:] = cum[..., :-1] >= top_p
+        tl.masked_fill_(mask, float("-inf"))
+    probs = torch.softmax(tl, dim=-1)
+    idx = torch.multinomial(probs, num_samples=1)
+    return r2f[ti.gather(-1, idx)]
+
+
+def run_decode_sampled(dev, world, rank, batch: int, steps: int, prompt: int = 128,
+                       reference_loop: bool = False) -> dict:
+    """Decode with the reference's sampling settings (temperature 0.5, top_p 0.85,
+    repetition penalty 1.2, top-k 256; config.py:28-31).
+
+    * fused_sampled: this library's engine, the sampler launched inside the
+      captured step (no host work per token).
+    * reference_loop_host_sampling (bs = 1): the reference decode loop
+      (inference_engine.py:633-667): per token the host writes the token,
+      position, cache slot and mask entry, replays a graph of the eager
+      reference-structure step, samples with eager ops and reads the token
+      back with `.item()`."""
+    from kani_tts_b200 import _lib
+    from kani_tts_b200.decode import DecodeEngine, FusedDecoder
+    from kani_tts_b200.model import LFM2Config, synthetic_state_dict
+    from kani_tts_b200.sampling import SamplingParams
+    cfg = LFM2Config()
+    sp = SamplingParams(seed=7 + rank)
+    sd = synthetic_state_dict(cfg, seed=0, device=dev)
+    g = torch.Generator(device="cpu").manual_seed(1 + rank)
+    ids = torch.randint(0, cfg.audio_tokens_start, (batch, prompt), generator=g).to(dev)
+    spk = torch.randn(batch, cfg.speaker_emb_dim, generator=g).to(dev)
+    out = {}
+    eng = DecodeEngine(FusedDecoder(cfg, sd, dev, batch=batch, max_len=2048), sampling=sp)
+    eng.start(ids, spk, steps + 8)
+    eng.capture()
+    eng.run(3)
+    torch.cuda.synchronize(dev)
+    _barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    eng.run(steps)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    _barrier(world)
+    sec = _max_over_ranks(e0.elapsed_time(e1) / 1e3, world, dev)
+    audio = eng.dec.full_to_reduced[eng.generated[:, :steps]] >= 0
+    out["fused_sampled"] = {"us_per_step": round(sec / steps * 1e6, 2),
+                            "tokens_per_s": round(world * batch * steps / sec, 1),
+                            "kernel_flags": int(eng.dec.err_flag.item()),
+                            "tokens_in_reduced_vocab": bool(audio.all())}
+    del eng
+    torch.cuda.empty_cache()
+    if reference_loop and batch == 1:
+        dec = _make_eager_decoder_cls()(cfg, sd, dev, batch=1, max_len=2048)
+        logits = dec.prefill(ids, torch.arange(prompt + 1, device=dev).view(1, -1), spk)
+        t_eff = prompt + 1
+        hist = torch.zeros(1, t_eff + steps + 8, dtype=torch.long, device=dev)
+        hist[0, :prompt] = ids[0]
+        gen_len = prompt
+        static_ids = torch.zeros(1, 1, dtype=torch.long, device=dev)
+        static_pos = torch.zeros(1, dtype=torch.long, device=dev)
+        static_slot = torch.zeros(1, dtype=torch.long, device=dev)
+        static_len = torch.zeros(1, dtype=torch.long, device=dev)
+        mask = torch.full((1, 1, 1, 2048), float("-inf"), dtype=torch.bfloat16, device=dev)
+        mask[..., :t_eff] = 0
+        schedule = (t_eff + (torch.arange(steps + 8, device=dev) + 1) // cfg.tokens_per_frame).long()
+        nxt = _reference_host_sample(logits[:, -1].clone(), hist[:, :gen_len], dec.full_to_reduced,
+                                     dec.reduced_to_full, sp.repetition_penalty, sp.temperature, sp.top_p)
+        hist[0, gen_len] = nxt.item()
+        gen_len += 1
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            dec.step(static_ids, static_pos, static_slot, static_len, mask)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            static_logits = dec.step(static_ids, static_pos, static_slot, static_len, mask)
+
+        def one(i):
+            nonlocal nxt, gen_len
+            static_ids.copy_(nxt.view(1, 1))
+            static_pos[0] = schedule[i]
+            off = t_eff + i
+            static_slot[0] = off
+            static_len[0] = off + 1
+            mask[..., off] = 0.0
+            graph.replay()
+            nxt = _reference_host_sample(static_logits[:, -1], hist[:, :gen_len], dec.full_to_reduced,
+                                         dec.reduced_to_full, sp.repetition_penalty, sp.temperature, sp.top_p)
+            hist[0, gen_len] = nxt[0, 0].item()
+            gen_len += 1
+        for i in range(3):
+            one(i)
+        torch.cuda.synchronize(dev)
+        e0.record()
+        for i in range(3, 3 + steps):
+            one(i)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        sec_r = e0.elapsed_time(e1) / 1e3
+        out["reference_loop_host_sampling"] = {"us_per_step": round(sec_r / steps * 1e6, 2),
+                                               "tokens_per_s": round(steps / sec_r, 1)}
+        out["speedup_vs_reference_loop"] = round(sec_r / sec, 3)
+        del graph, dec
+        torch.cuda.empty_cache()
+    out["config"] = (f"bs={batch} x {world} GPU(s), prompt {prompt}+speaker, {steps} decode steps, S=2048, "
+                     f"sampling T={sp.temperature} top_p={sp.top_p} rp={sp.repetition_penalty} top_k={sp.top_k}")
+    return out
+
+
 def run_gpu(args, world, rank, local):
     from kani_tts_b200 import _lib
     from kani_tts_b200 import fused_kernels as K
@@ -580,7 +710,10 @@ def run_gpu(args, world, rank, local):
     if not args.no_decode:
         # decode steps: bs=1 (with the eager reference-structure arm) and 64 streams per GPU
         extras["decode"] = {"bs1": run_decode(dev, world, rank, 1, args.decode_steps, eager=True),
-                            "bs64": run_decode(dev, world, rank, 64, args.decode_steps)}
+                            "bs64": run_decode(dev, world, rank, 64, args.decode_steps),
+                            "bs1_sampled": run_decode_sampled(dev, world, rank, 1, args.decode_steps,
+                                                              reference_loop=(world == 1)),
+                            "bs64_sampled": run_decode_sampled(dev, world, rank, 64, args.decode_steps)}
     if rank == 0:
         if not args.no_sweep:
             extras["sweep"] = run_sweep(K, dev, peak)
@@ -717,8 +850,10 @@ def main():
         dev = torch.device("cuda", local)
         torch.cuda.set_device(dev)
         res = run_decode(dev, world, rank, args.decode_batch, args.decode_steps, eager=args.decode_batch == 1)
+        res_s = run_decode_sampled(dev, world, rank, args.decode_batch, args.decode_steps,
+                                   reference_loop=(world == 1 and args.decode_batch == 1))
         if rank == 0:
-            print(json.dumps({"decode": res}), flush=True)
+            print(json.dumps({"decode": res, "decode_sampled": res_s}), flush=True)
         return
     if args.impl == "reference":
         # CPU arm: rank 0 alone measures; other ranks exit without work or a process group

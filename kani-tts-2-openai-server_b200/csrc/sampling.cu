@@ -53,6 +53,7 @@ constexpr int kMaxTopK = 256;
 constexpr int kSampleMaxDynSmem = 200 * 1024;
 constexpr int kRegItems = 16;  // items per thread held in registers (rows up to 16384)
 constexpr int kStageBatch = 16;  // row loads in flight per thread while staging
+constexpr int kLiveMax = 2048;   // keys inside the threshold bracket that one warp searches
 
 struct SampleParams {
   const void* logits;
@@ -140,6 +141,9 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
   __shared__ float s_val[kMaxTopK];
   __shared__ int s_idx[kMaxTopK];
   __shared__ __align__(16) float s_prob[kMaxTopK];
+  __shared__ uint32_t live_key[kLiveMax];
+  __shared__ int live_idx[kLiveMax];
+  __shared__ int sh_count;
 
   T* row = reinterpret_cast<T*>(smem_raw);
   const int b = blockIdx.x;
@@ -259,15 +263,15 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
 
   // 2. the k-th largest key vk: the largest t with count(key >= t) >= k.
   //    Bracket it below the row's largest key (spans 2^(B-9), 2^(B-7), 2^(B-5)
-  //    for B-bit keys, one barrier), then bisect inside the bracket.
+  //    for B-bit keys, one barrier): count(>= lo) = c_lo >= k > count(>= hi) = c_hi.
   uint32_t mk = 0;
   for_items([&](int, uint32_t k) { mk = k > mk ? k : mk; });
   mk = __reduce_max_sync(0xffffffffu, mk);
   if (lane == 0) warp_max[warp] = mk;
   __syncthreads();
   const uint32_t maxk = __reduce_max_sync(0xffffffffu, warp_max[lane]);
-  uint64_t hi = (uint64_t)maxk + 1, lo = 0;  // invariant: count(>= lo) >= k > count(>= hi) = c_hi
-  int c_hi = 0;
+  uint64_t hi = (uint64_t)maxk + 1, lo = 0;
+  int c_hi = 0, c_lo = V;
   {
     uint32_t t[3];
     int c[3];
@@ -279,12 +283,15 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
     count_ge.template operator()<3>(t, c);
     if (c[0] >= KK) {
       lo = t[0];
+      c_lo = c[0];
     } else if (c[1] >= KK) {
       lo = t[1];
+      c_lo = c[1];
       hi = t[0];
       c_hi = c[0];
     } else if (c[2] >= KK) {
       lo = t[2];
+      c_lo = c[2];
       hi = t[1];
       c_hi = c[1];
     } else {
@@ -292,66 +299,140 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
       c_hi = c[2];
     }
   }
-  while (hi - lo > 1) {
-    const uint32_t mid = (uint32_t)((lo + hi) >> 1);
-    int c;
-    count_ge.template operator()<1>(&mid, &c);
-    if (c >= KK) {
-      lo = mid;
-    } else {
-      hi = mid;
-      c_hi = c;
-    }
-  }
-  const uint32_t vk = (uint32_t)lo;
-  const int need = KK - c_hi;  // keys equal to vk to take, lowest indices first
 
-  // 3. one block scan of (greater, equal) counts packed as eq << 9 | gt
-  //    (the greater total is < k <= 256)
-  int c_pack = 0;
-  for_items([&](int, uint32_t k) { c_pack += k > vk ? 1 : (k == vk ? 512 : 0); });
-  int inc = c_pack;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int v = __shfl_up_sync(0xffffffffu, inc, o);
-    if (lane >= o) inc += v;
-  }
-  if (lane == 31) warp_tot[warp] = inc;
-  __syncthreads();
-  if (warp == 0) {
-    const int t = warp_tot[lane];
-    int ti = t;
+  // exclusive block scan of one int per thread (two barriers)
+  auto block_excl_scan = [&](int v) -> int {
+    int inc = v;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const int v = __shfl_up_sync(0xffffffffu, ti, o);
-      if (lane >= o) ti += v;
+      const int u = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += u;
     }
-    warp_tot[lane] = ti - t;
-  }
-  __syncthreads();
-  const int excl = warp_tot[warp] + inc - c_pack;
-  int gt_slot = excl & 511, eq_rank = excl >> 9;
+    if (lane == 31) warp_tot[warp] = inc;
+    __syncthreads();
+    if (warp == 0) {
+      const int t = warp_tot[lane];
+      int ti = t;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, ti, o);
+        if (lane >= o) ti += u;
+      }
+      warp_tot[lane] = ti - t;
+    }
+    __syncthreads();
+    return warp_tot[warp] + inc - v;
+  };
+  auto put_greater = [&](int slot, uint32_t k, int i) {
+    if (slot < kMaxTopK) {
+      cand_key[slot] = ((unsigned long long)k << 32) | (unsigned long long)(0xffffffffu - (uint32_t)i);
+      cand_val[slot] = Elem<T>::to_f(row[i]);
+      cand_idx[slot] = i;
+    }
+  };
 
-  // 4. greater keys to candidate slots [0, c_hi) (sorted next); the taken equal
-  //    keys are already in order: sorted positions [c_hi, k)
-  for_items([&](int i, uint32_t k) {
-    if (k > vk) {
-      const int slot = gt_slot++;
-      if (slot < kMaxTopK) {
-        cand_key[slot] = ((unsigned long long)k << 32) | (unsigned long long)(0xffffffffu - (uint32_t)i);
-        cand_val[slot] = Elem<T>::to_f(row[i]);
-        cand_idx[slot] = i;
+  // c_gt keys above vk go to candidate slots [0, c_gt) (sorted in step 5); the
+  // `need` equal keys taken at the boundary (lowest indices first) go straight
+  // to their sorted positions [c_gt, k)
+  int c_gt, need;
+  if (c_lo - c_hi <= kLiveMax) {
+    // 3a. few keys inside the bracket: keys >= hi are taken; the keys in
+    //     [lo, hi) are compacted in index order and one warp finishes the search
+    const int n_live = c_lo - c_hi;
+    const int pos = block_excl_scan(
+        [&] {
+          int v = 0;
+          for_items([&](int, uint32_t k) { v += k >= hi ? 1 : (k >= lo ? 512 : 0); });
+          return v;
+        }());
+    int sure = pos & 511, live = pos >> 9;
+    for_items([&](int i, uint32_t k) {
+      if (k >= hi) {
+        put_greater(sure++, k, i);
+      } else if (k >= lo) {
+        live_key[live] = k;
+        live_idx[live] = i;
+        ++live;
       }
-    } else if (k == vk) {
-      if (eq_rank < need) {
-        const int pos = c_hi + eq_rank;
-        s_val[pos] = Elem<T>::to_f(row[i]);
-        s_idx[pos] = i;
+    });
+    __syncthreads();
+    if (warp == 0) {
+      uint64_t l2 = lo, h2 = hi;
+      int ch = c_hi;
+      while (h2 - l2 > 1) {
+        const uint32_t mid = (uint32_t)((l2 + h2) >> 1);
+        int c = 0;
+        for (int m = lane; m < n_live; m += 32) c += live_key[m] >= mid ? 1 : 0;
+        c = __reduce_add_sync(0xffffffffu, c) + c_hi;
+        if (c >= KK) {
+          l2 = mid;
+        } else {
+          h2 = mid;
+          ch = c;
+        }
       }
-      ++eq_rank;
+      const uint32_t vk = (uint32_t)l2;
+      const int nd = KK - ch;
+      int gbase = c_hi, ebase = 0;
+      const uint32_t below = (1u << lane) - 1u;
+      for (int m0 = 0; m0 < n_live; m0 += 32) {
+        const int m = m0 + lane;
+        const uint32_t k = m < n_live ? live_key[m] : 0u;
+        const bool gt = m < n_live && k > vk, eq = m < n_live && k == vk;
+        const uint32_t bg = __ballot_sync(0xffffffffu, gt), be = __ballot_sync(0xffffffffu, eq);
+        if (gt) put_greater(gbase + __popc(bg & below), k, live_idx[m]);
+        if (eq) {
+          const int r = ebase + __popc(be & below);
+          if (r < nd) {
+            s_val[ch + r] = Elem<T>::to_f(row[live_idx[m]]);
+            s_idx[ch + r] = live_idx[m];
+          }
+        }
+        gbase += __popc(bg);
+        ebase += __popc(be);
+      }
+      if (lane == 0) sh_count = ch;
     }
-  });
-  __syncthreads();
+    __syncthreads();
+    c_gt = sh_count;
+    need = KK - c_gt;
+  } else {
+    // 3b. bisection inside the bracket over all keys, then one block scan of
+    //     packed (greater, equal) counts (the greater total is < k <= 256)
+    while (hi - lo > 1) {
+      const uint32_t mid = (uint32_t)((lo + hi) >> 1);
+      int c;
+      count_ge.template operator()<1>(&mid, &c);
+      if (c >= KK) {
+        lo = mid;
+      } else {
+        hi = mid;
+        c_hi = c;
+      }
+    }
+    const uint32_t vk = (uint32_t)lo;
+    c_gt = c_hi;
+    need = KK - c_gt;
+    const int excl = block_excl_scan(
+        [&] {
+          int v = 0;
+          for_items([&](int, uint32_t k) { v += k > vk ? 1 : (k == vk ? 512 : 0); });
+          return v;
+        }());
+    int gt_slot = excl & 511, eq_rank = excl >> 9;
+    for_items([&](int i, uint32_t k) {
+      if (k > vk) {
+        put_greater(gt_slot++, k, i);
+      } else if (k == vk) {
+        if (eq_rank < need) {
+          s_val[c_gt + eq_rank] = Elem<T>::to_f(row[i]);
+          s_idx[c_gt + eq_rank] = i;
+        }
+        ++eq_rank;
+      }
+    });
+    __syncthreads();
+  }
 
   // 5. sort the greater keys descending (all distinct): rank = number larger.
   //    Thread (q, j) counts over quarter q of the keys; a warp reads one key
@@ -360,10 +441,10 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
     const int j = tid & (kMaxTopK - 1), q = tid / kMaxTopK;
     constexpr int QN = kMaxTopK / (kSampleThreads / kMaxTopK);
     int part = 0;
-    if (q * QN < c_hi) {
-      const unsigned long long kj = j < c_hi ? cand_key[j] : ~0ull;
+    if (q * QN < c_gt) {
+      const unsigned long long kj = j < c_gt ? cand_key[j] : ~0ull;
       const ulonglong2* ck2 = reinterpret_cast<const ulonglong2*>(cand_key + q * QN);
-      const int n = min(QN, c_hi - q * QN);
+      const int n = min(QN, c_gt - q * QN);
 #pragma unroll 8
       for (int m = 0; m < QN / 2; ++m) {
         if (2 * m < n) {
@@ -376,7 +457,7 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
     rank_part[q][j] = part;
   }
   __syncthreads();
-  if (tid < c_hi) {
+  if (tid < c_gt) {
     int rank = 0;
 #pragma unroll
     for (int q = 0; q < kSampleThreads / kMaxTopK; ++q) rank += rank_part[q][tid];

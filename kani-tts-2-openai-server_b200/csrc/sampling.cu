@@ -52,8 +52,9 @@ constexpr int kSampleThreads = 1024;
 constexpr int kMaxTopK = 256;
 constexpr int kSampleMaxDynSmem = 200 * 1024;
 constexpr int kRegItems = 16;  // items per thread held in registers (rows up to 16384)
-constexpr int kStageBatch = 16;  // row loads in flight per thread while staging
+constexpr int kStageChunks = 4;  // 16-byte row chunks in flight per thread while staging
 constexpr int kLiveMax = 2048;   // keys inside the threshold bracket that one warp searches
+constexpr int kLiveReg = 16;     // of those, per lane in registers (lists up to 512)
 
 struct SampleParams {
   const void* logits;
@@ -145,7 +146,6 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
   __shared__ int live_idx[kLiveMax];
   __shared__ int sh_count;
 
-  T* row = reinterpret_cast<T*>(smem_raw);
   const int b = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int V = p.vocab, KK = p.top_k, ipt = p.ipt;
@@ -159,48 +159,71 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
     return Elem<T>::to_f(t);
   };
 
-  // 1. stage the row in shared memory: penalty, then bias, per element (the
-  //    reference's order); loads of a batch are all in flight before any use
-  for (int i0 = 0; i0 < V; i0 += kStageBatch * kSampleThreads) {
-    Raw raw[kStageBatch], braw[kStageBatch];
-    // the 32 elements of a warp in round r share bitmap word (i0 + r * 1024) / 32 + warp;
-    // lane r fetches the word of round r
-    uint32_t myword = 0;
-    {
-      const int w = (i0 >> 5) + lane * (kSampleThreads / 32) + warp;
-      if (pen && lane < kStageBatch && w < (V + 31) / 32) myword = __ldg(seen + w);
-    }
+  // 1. stage the row in shared memory.  The row starts o elements into a
+  //    16-byte chunk; it is stored shifted by o (row = row_s + o) so that whole
+  //    chunks move with 16-byte loads and stores and every thread's block below
+  //    stays 16-byte aligned.  Then the penalty (a sparse pass over the set bits
+  //    of the history bitmap) and the bias, in the reference's order.
+  T* row_s = reinterpret_cast<T*>(smem_raw);
+  const int o = (int)((reinterpret_cast<uintptr_t>(src) & 15u) / sizeof(T));
+  T* row = row_s + o;
+  {
+    const int C = (V + o + E - 1) / E;  // chunks touched by the row
+    const uint4* A = reinterpret_cast<const uint4*>(reinterpret_cast<uintptr_t>(src) - (uintptr_t)o * sizeof(T));
+    for (int c0 = 0; c0 < C; c0 += kStageChunks * kSampleThreads) {
+      uint4 v[kStageChunks];
 #pragma unroll
-    for (int r = 0; r < kStageBatch; ++r) {
-      const int i = i0 + r * kSampleThreads + tid;
-      raw[r] = 0;
-      braw[r] = 0;
-      if (i < V) {
-        raw[r] = __ldg(src + i);
-        if (bias) braw[r] = __ldg(bias + i);
+      for (int r = 0; r < kStageChunks; ++r) {
+        const int c = c0 + r * kSampleThreads + tid;
+        const int i0 = c * E - o;
+        if (c < C && i0 >= 0 && i0 + E <= V) v[r] = __ldg(A + c);
       }
-    }
 #pragma unroll
-    for (int r = 0; r < kStageBatch; ++r) {
-      const int i = i0 + r * kSampleThreads + tid;
-      const uint32_t word = __shfl_sync(0xffffffffu, myword, r);
-      if (i < V) {
-        float v = as_f(raw[r]);
-        if ((word >> (i & 31)) & 1u)
-          v = round_to<T>(v > 0.f ? __fdiv_rn(v, p.penalty) : __fmul_rn(v, p.penalty));
-        if (bias) v = round_to<T>(__fadd_rn(v, as_f(braw[r])));
-        row[i] = Elem<T>::from_f(v);
+      for (int r = 0; r < kStageChunks; ++r) {
+        const int c = c0 + r * kSampleThreads + tid;
+        const int i0 = c * E - o;
+        if (c >= C) continue;
+        if (i0 >= 0 && i0 + E <= V) {
+          reinterpret_cast<uint4*>(row_s)[c] = v[r];
+        } else {  // the partial first / last chunk: element loads inside the row only
+          for (int e = 0; e < E; ++e) {
+            const int i = i0 + e;
+            if (i >= 0 && i < V) {
+              const Raw x = __ldg(src + i);
+              memcpy(row + i, &x, sizeof(Raw));
+            }
+          }
+        }
       }
     }
   }
   __syncthreads();
+  if (pen) {
+    for (int w = tid; w < (V + 31) / 32; w += kSampleThreads) {
+      uint32_t m = __ldg(seen + w);
+      while (m) {
+        const int i = 32 * w + __ffs(m) - 1;
+        m &= m - 1u;
+        if (i < V) {
+          const float v = Elem<T>::to_f(row[i]);
+          row[i] = Elem<T>::from_f(v > 0.f ? __fdiv_rn(v, p.penalty) : __fmul_rn(v, p.penalty));
+        }
+      }
+    }
+    __syncthreads();
+  }
+  if (bias) {
+    for (int i = tid; i < V; i += kSampleThreads)
+      row[i] = Elem<T>::from_f(__fadd_rn(Elem<T>::to_f(row[i]), as_f(__ldg(bias + i))));
+    __syncthreads();
+  }
 
   // this thread's block of the row: [base, base + ipt), ipt a multiple of E,
   // read from shared memory as 16-byte vectors; with REG the keys stay in
   // registers (ipt <= kRegItems), otherwise every pass re-reads shared memory
-  const int base = tid * ipt;
-  auto keys_at = [&](int i, uint32_t* key) {
-    const uint4 raw = *reinterpret_cast<const uint4*>(row + i);
+  const int base = tid * ipt;  // in row_s positions; row index = position - o
+  auto keys_at = [&](int sp, uint32_t* key) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(row_s + sp);
     Raw v[E];
     memcpy(v, &raw, 16);
 #pragma unroll
@@ -212,23 +235,29 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
     for (int r = 0; r < kRegItems; r += E) {
       if (r < ipt) keys_at(base + r, rk + r);
 #pragma unroll
-      for (int e = 0; e < E; ++e)
-        if (r >= ipt || base + r + e >= V) rk[r + e] = 0;  // never counted: thresholds are >= 1
+      for (int e = 0; e < E; ++e) {
+        const int i = base + r + e - o;
+        if (r >= ipt || i < 0 || i >= V) rk[r + e] = 0;  // never counted: thresholds are >= 1
+      }
     }
   }
   // f(i, key) over this thread's items in index order
   auto for_items = [&](auto&& f) {
     if constexpr (REG) {
 #pragma unroll
-      for (int r = 0; r < kRegItems; ++r)
-        if (r < ipt && base + r < V) f(base + r, rk[r]);
+      for (int r = 0; r < kRegItems; ++r) {
+        const int i = base + r - o;
+        if (r < ipt && i >= 0 && i < V) f(i, rk[r]);
+      }
     } else {
-      for (int r = 0; r < ipt && base + r < V; r += E) {
+      for (int r = 0; r < ipt && base + r - o < V; r += E) {
         uint32_t key[E];
         keys_at(base + r, key);
 #pragma unroll
-        for (int e = 0; e < E; ++e)
-          if (base + r + e < V) f(base + r + e, key[e]);
+        for (int e = 0; e < E; ++e) {
+          const int i = base + r + e - o;
+          if (i >= 0 && i < V) f(i, key[e]);
+        }
       }
     }
   };
@@ -323,9 +352,15 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
     __syncthreads();
     return warp_tot[warp] + inc - v;
   };
+  // sort keys: value key, then lower index first; 32 bits when a 16-bit key and
+  // a row index below 2^16 fit (16-bit types, rows held in registers)
+  constexpr bool K32 = sizeof(T) == 2 && REG;
   auto put_greater = [&](int slot, uint32_t k, int i) {
     if (slot < kMaxTopK) {
-      cand_key[slot] = ((unsigned long long)k << 32) | (unsigned long long)(0xffffffffu - (uint32_t)i);
+      if constexpr (K32)
+        reinterpret_cast<uint32_t*>(cand_key)[slot] = (k << 16) | (0xffffu - (uint32_t)i);
+      else
+        cand_key[slot] = ((unsigned long long)k << 32) | (unsigned long long)(0xffffffffu - (uint32_t)i);
       cand_val[slot] = Elem<T>::to_f(row[i]);
       cand_idx[slot] = i;
     }
@@ -359,10 +394,24 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
     if (warp == 0) {
       uint64_t l2 = lo, h2 = hi;
       int ch = c_hi;
+      // up to kLiveReg keys per lane stay in registers; a longer list is re-read
+      uint32_t lk[kLiveReg];
+      const bool in_reg = n_live <= 32 * kLiveReg;
+#pragma unroll
+      for (int j = 0; j < kLiveReg; ++j) {
+        const int m = lane + 32 * j;
+        lk[j] = (in_reg && m < n_live) ? live_key[m] : 0u;  // key 0 is never counted (mid >= 1)
+      }
       while (h2 - l2 > 1) {
         const uint32_t mid = (uint32_t)((l2 + h2) >> 1);
         int c = 0;
-        for (int m = lane; m < n_live; m += 32) c += live_key[m] >= mid ? 1 : 0;
+        if (in_reg) {
+#pragma unroll
+          for (int j = 0; j < kLiveReg; ++j) c += lk[j] >= mid ? 1 : 0;
+        } else {
+#pragma unroll 4
+          for (int m = lane; m < n_live; m += 32) c += live_key[m] >= mid ? 1 : 0;
+        }
         c = __reduce_add_sync(0xffffffffu, c) + c_hi;
         if (c >= KK) {
           l2 = mid;
@@ -442,15 +491,31 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
     constexpr int QN = kMaxTopK / (kSampleThreads / kMaxTopK);
     int part = 0;
     if (q * QN < c_gt) {
-      const unsigned long long kj = j < c_gt ? cand_key[j] : ~0ull;
-      const ulonglong2* ck2 = reinterpret_cast<const ulonglong2*>(cand_key + q * QN);
       const int n = min(QN, c_gt - q * QN);
+      if constexpr (K32) {
+        const uint32_t* ck = reinterpret_cast<const uint32_t*>(cand_key);
+        const uint32_t kj = j < c_gt ? ck[j] : 0xffffffffu;
+        const uint4* ck4 = reinterpret_cast<const uint4*>(ck + q * QN);
+#pragma unroll 4
+        for (int m = 0; m < QN / 4; ++m) {
+          if (4 * m < n) {
+            const uint4 kk = ck4[m];
+            part += kk.x > kj ? 1 : 0;
+            part += (4 * m + 1 < n && kk.y > kj) ? 1 : 0;
+            part += (4 * m + 2 < n && kk.z > kj) ? 1 : 0;
+            part += (4 * m + 3 < n && kk.w > kj) ? 1 : 0;
+          }
+        }
+      } else {
+        const unsigned long long kj = j < c_gt ? cand_key[j] : ~0ull;
+        const ulonglong2* ck2 = reinterpret_cast<const ulonglong2*>(cand_key + q * QN);
 #pragma unroll 8
-      for (int m = 0; m < QN / 2; ++m) {
-        if (2 * m < n) {
-          const ulonglong2 kk = ck2[m];
-          part += kk.x > kj ? 1 : 0;
-          part += (2 * m + 1 < n && kk.y > kj) ? 1 : 0;
+        for (int m = 0; m < QN / 2; ++m) {
+          if (2 * m < n) {
+            const ulonglong2 kk = ck2[m];
+            part += kk.x > kj ? 1 : 0;
+            part += (2 * m + 1 < n && kk.y > kj) ? 1 : 0;
+          }
         }
       }
     }
@@ -642,7 +707,7 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
 template <typename T>
 int launch_sample(SampleParams prm, int64_t batch, cudaStream_t s) {
   constexpr int E = VecN<T>::value;
-  int ipt = (prm.vocab + kSampleThreads - 1) / kSampleThreads;
+  int ipt = (prm.vocab + E - 1 + kSampleThreads - 1) / kSampleThreads;  // room for a shift of up to E-1
   ipt = (ipt + E - 1) / E * E;
   const size_t smem = (size_t)ipt * kSampleThreads * sizeof(T);
   if (smem > (size_t)kSampleMaxDynSmem) return KANI_ERR_UNSUPPORTED;

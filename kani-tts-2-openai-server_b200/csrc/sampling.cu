@@ -145,6 +145,8 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
   __shared__ uint32_t live_key[kLiveMax];
   __shared__ int live_idx[kLiveMax];
   __shared__ int sh_count;
+  __shared__ long long s_tok[kMaxTopK];
+  __shared__ float s_draw[kMaxTopK];
 
   const int b = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -530,37 +532,39 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
     s_idx[rank] = cand_idx[tid];
   }
   __syncthreads();
-  if (warp != 0) return;
-
-  // 6. one warp: lane owns sorted positions lane*P .. lane*P+P-1.  The draws
-  //    and the token ids of the candidates are fetched first (independent of
-  //    the probabilities).
-  float draw[P];
-  if (p.draws) {
-#pragma unroll
-    for (int e = 0; e < P; ++e) {
-      const int j = lane * P + e;
-      draw[e] = j < KK ? __ldg(p.draws + (int64_t)b * KK + j) : 1.f;
+  // 6. warps 1..8 fetch every candidate's token id and Exp(1) draw into shared
+  //    memory and arrive on named barrier 1; warp 0 runs temperature, softmax
+  //    and top-p meanwhile and meets the barrier only before the race.
+  if (warp != 0) {
+    const int j = tid - 32;
+    if (j < kMaxTopK) {
+      if (j < KK) {
+        const int idx = s_idx[j];
+        s_tok[j] = p.index_map ? __ldg(p.index_map + idx) : (long long)idx;
+        float d;
+        if (p.draws) {
+          d = __ldg(p.draws + (int64_t)b * KK + j);
+        } else {
+          const uint64_t step = p.step ? (uint64_t)*p.step : 0ull;
+          const uint4 w = philox4x32_10(make_uint4((uint32_t)(j >> 2), (uint32_t)b, (uint32_t)step,
+                                                   (uint32_t)(step >> 32)),
+                                        make_uint2((uint32_t)p.seed, (uint32_t)(p.seed >> 32)));
+          const int q = j & 3;
+          d = exp_draw(q == 0 ? w.x : q == 1 ? w.y : q == 2 ? w.z : w.w);
+        }
+        s_draw[j] = d;
+      }
+      __syncwarp();
+      asm volatile("bar.arrive 1, %0;" ::"n"(32 + kMaxTopK) : "memory");
     }
-  } else {
-    const uint64_t step = p.step ? (uint64_t)*p.step : 0ull;
-    const uint2 key = make_uint2((uint32_t)p.seed, (uint32_t)(p.seed >> 32));
-#pragma unroll
-    for (int h = 0; h < P / 4; ++h) {
-      const uint4 w = philox4x32_10(
-          make_uint4((uint32_t)(lane * (P / 4) + h), (uint32_t)b, (uint32_t)step, (uint32_t)(step >> 32)), key);
-      draw[h * 4 + 0] = exp_draw(w.x);
-      draw[h * 4 + 1] = exp_draw(w.y);
-      draw[h * 4 + 2] = exp_draw(w.z);
-      draw[h * 4 + 3] = exp_draw(w.w);
-    }
+    return;
   }
+
+  // 7. warp 0: lane owns sorted positions lane*P .. lane*P+P-1
   float x[P];
 #pragma unroll
   for (int e = 0; e < P; ++e) {
     const int j = lane * P + e;
-    const int idx = j < KK ? s_idx[j] : 0;
-    if (j < KK && p.index_map) asm volatile("prefetch.L1 [%0];" ::"l"(p.index_map + idx));
     float v = j < KK ? s_val[j] : -INFINITY;
     if (j < KK && p.temperature != 1.0f) v = round_to<T>(__fdiv_rn(v, p.temperature));
     x[e] = v;
@@ -669,7 +673,11 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
   }
   softmax(keep, pr);
 
-  // 7. exponential race over the kept candidates: first maximum of round(p / round(E))
+  // 8. exponential race over the kept candidates: first maximum of round(p / round(E))
+  asm volatile("bar.sync 1, %0;" ::"n"(32 + kMaxTopK) : "memory");
+  float draw[P];
+#pragma unroll
+  for (int e = 0; e < P; ++e) draw[e] = lane * P + e < KK ? s_draw[lane * P + e] : 1.f;
   float best = -1.f;
   int best_j = 0x7fffffff;
 #pragma unroll
@@ -699,7 +707,7 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
   if (lane == 0) {
     int idx = s_idx[best_j];
     if (idx < 0 || idx >= V) idx = 0;  // unreachable: every sorted slot holds a row index
-    p.tokens[(int64_t)b * p.tokens_stride] = p.index_map ? __ldg(p.index_map + idx) : (int64_t)idx;
+    p.tokens[(int64_t)b * p.tokens_stride] = s_tok[best_j];
     if (p.update_seen && p.seen) atomicOr(p.seen + (int64_t)b * p.seen_words + (idx >> 5), 1u << (idx & 31));
   }
 }

@@ -88,6 +88,18 @@ template <> struct KeyOf<__nv_bfloat16> {
   }
 };
 template <> struct KeyOf<__half> : KeyOf<__nv_bfloat16> {};
+
+// The stored value of a key (the inverse map; -0 comes back as +0).
+template <typename T>
+__device__ __forceinline__ float value_of_key(uint32_t k) {
+  using Raw = typename KeyOf<T>::Raw;
+  const uint32_t top = 1u << (KeyOf<T>::kBits - 1);
+  const uint32_t all = KeyOf<T>::kBits == 32 ? 0xffffffffu : (1u << KeyOf<T>::kBits) - 1u;
+  const Raw r = (Raw)(k ^ ((k & top) ? top : all));
+  T t;
+  memcpy(&t, &r, sizeof(Raw));
+  return Elem<T>::to_f(t);
+}
 template <> struct KeyOf<float> {
   using Raw = uint32_t;
   static constexpr int kBits = 32;
@@ -363,7 +375,7 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
         reinterpret_cast<uint32_t*>(cand_key)[slot] = (k << 16) | (0xffffu - (uint32_t)i);
       else
         cand_key[slot] = ((unsigned long long)k << 32) | (unsigned long long)(0xffffffffu - (uint32_t)i);
-      cand_val[slot] = Elem<T>::to_f(row[i]);
+      cand_val[slot] = value_of_key<T>(k);
       cand_idx[slot] = i;
     }
   };
@@ -426,21 +438,30 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
       const int nd = KK - ch;
       int gbase = c_hi, ebase = 0;
       const uint32_t below = (1u << lane) - 1u;
-      for (int m0 = 0; m0 < n_live; m0 += 32) {
-        const int m = m0 + lane;
-        const uint32_t k = m < n_live ? live_key[m] : 0u;
+      // list order is index order: equal keys are ranked by ballots round by round
+      auto place = [&](int m, uint32_t k) {
         const bool gt = m < n_live && k > vk, eq = m < n_live && k == vk;
         const uint32_t bg = __ballot_sync(0xffffffffu, gt), be = __ballot_sync(0xffffffffu, eq);
         if (gt) put_greater(gbase + __popc(bg & below), k, live_idx[m]);
         if (eq) {
           const int r = ebase + __popc(be & below);
           if (r < nd) {
-            s_val[ch + r] = Elem<T>::to_f(row[live_idx[m]]);
+            s_val[ch + r] = value_of_key<T>(k);
             s_idx[ch + r] = live_idx[m];
           }
         }
         gbase += __popc(bg);
         ebase += __popc(be);
+      };
+      if (in_reg) {
+#pragma unroll
+        for (int j = 0; j < kLiveReg; ++j)
+          if (32 * j < n_live) place(lane + 32 * j, lk[j]);
+      } else {
+        for (int m0 = 0; m0 < n_live; m0 += 32) {
+          const int m = m0 + lane;
+          place(m, m < n_live ? live_key[m] : 0u);
+        }
       }
       if (lane == 0) sh_count = ch;
     }
@@ -476,7 +497,7 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
         put_greater(gt_slot++, k, i);
       } else if (k == vk) {
         if (eq_rank < need) {
-          s_val[c_gt + eq_rank] = Elem<T>::to_f(row[i]);
+          s_val[c_gt + eq_rank] = value_of_key<T>(k);
           s_idx[c_gt + eq_rank] = i;
         }
         ++eq_rank;

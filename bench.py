@@ -454,6 +454,8 @@ def _make_eager_decoder_cls():
     from kani_tts_b200.decode import FusedDecoder
 
     class EagerReferenceDecoder(FusedDecoder):
+        fused_greedy_head = False   # the reference's F.linear head and argmax
+
         def step(self, input_ids, positions, slots, kv_len, mask):
             b, hq, hk, d = self.batch, self.hq, self.hk, self.d
             hidden = F.embedding(input_ids, self.embed)
@@ -786,6 +788,17 @@ def run_op(name: str, size: int, steps: int, warmup: int) -> dict:
         fn = (lambda: K.sample_tokens(lg, seen, temperature=0.5, top_p=0.85, repetition_penalty=1.2, seed=1,
                                       step=step, out=tok))
         nbytes = size * (v * 2 + seen.shape[1] * 4 + 8)
+    elif name in ("head_argmax", "head_cublas"):  # size = streams; reduced head 15591 x 1024
+        rows, h = 15591, 1024
+        hid, wt = rn(size, h), rn(rows, h) * 0.05
+        imap = torch.arange(rows, device=dev) + 64410
+        out = torch.empty(size, dtype=torch.long, device=dev)
+        if name == "head_argmax":
+            scratch = torch.zeros(size + 1, dtype=torch.long, device=dev)
+            fn = lambda: K.head_argmax(hid, wt, imap, scratch=scratch, out=out)  # noqa: E731
+        else:                                   # the reference's F.linear head + greedy argmax + map
+            fn = lambda: out.copy_(imap[torch.nn.functional.linear(hid, wt).argmax(-1)])  # noqa: E731
+        nbytes = rows * h * 2 + size * h * 2
     else:
         raise SystemExit(f"unknown op {name}")
     for _ in range(warmup):
@@ -835,7 +848,8 @@ def main():
     ap.add_argument("--decode-only", action="store_true", help="profiling aid: run only the decode arms")
     ap.add_argument("--decode-batch", type=int, default=1, help="streams for --decode-only")
     ap.add_argument("--op", default=None, help="profiling aid: run one fused op alone "
-                    "(silu_mul, add_rms_norm, rope_kv_write, decode_attention, short_conv, sample)")
+                    "(silu_mul, add_rms_norm, rope_kv_write, decode_attention, short_conv, sample, "
+                    "head_argmax, head_cublas)")
     ap.add_argument("--size", type=int, default=4096, help="rows / tokens / streams for --op")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()

@@ -247,6 +247,41 @@ KANI_API int kani_sample_tokens(int32_t dtype, const void* logits, int64_t logit
                        int32_t* cand_out, int64_t* tokens_out, int64_t tokens_out_stride,
                        void* stream);
 
+/*
+ * Reduced LM head + greedy choice for up to 8 streams, one launch:
+ *   logits[b, r] = round(sum_k hidden[b, k] * weight[r, k])  (fp32 accumulation)
+ *   tokens_out[b * stride] = index_map[first r with the largest logits[b, r]]
+ * Replaces F.linear(hidden, audio_lm_head_weight) (kani_tts/optimized_decode.py:287,
+ * head built at :134-156) and the greedy reduced_to_full[argmax(...)] (:144-148).
+ *   hidden: [batch, hidden_size] (row stride); weight: [rows, hidden_size] (row
+ *   stride); bf16 or fp16; hidden_size one of 512, 1024, 2048; rows and strides
+ *   16-byte aligned.  logits_out [batch, rows] (row stride) may be NULL.
+ *   scratch: batch + 1 uint64 of device memory, zero before the first call; every
+ *   call leaves it zero (one call at a time per scratch buffer).
+ *   index_map: [rows] int64, NULL = identity.  batch > 8: KANI_ERR_UNSUPPORTED.
+ */
+KANI_API int kani_head_argmax(int32_t dtype, const void* hidden, int64_t hidden_row_stride, int64_t batch,
+                     int32_t hidden_size, const void* weight, int64_t weight_row_stride, int32_t rows,
+                     const int64_t* index_map, void* logits_out, int64_t logits_row_stride,
+                     unsigned long long* scratch, int64_t* tokens_out, int64_t tokens_out_stride,
+                     void* stream);
+
+/*
+ * Generated tokens -> NeMo codec codes for `batch` streams (replaces
+ * NemoAudioPlayer.get_nano_codes, kani_tts/core.py:86-108):
+ *   a stream's audio segment is its tokens before the first `eos_token`
+ *   (end-of-speech); frames = segment length / 4 (an incomplete frame is dropped);
+ *   codes_out[b, c, f] = tokens[b, 4 f + c] - c * codebook_size - audio_tokens_start,
+ *   -1 past the stream's frames.  tokens: [batch, n_tokens] int64 (row stride);
+ *   codes_out: [batch, 4, max_frames] int64, max_frames >= n_tokens / 4;
+ *   frames_out: [batch] int64; status_out: [batch] int32, bit 0 = a negative code,
+ *   bit 1 = no complete frame, bit 2 = no end-of-speech token.
+ */
+KANI_API int kani_codec_codes(const int64_t* tokens, int64_t tokens_row_stride, int64_t batch,
+                     int64_t n_tokens, int64_t eos_token, int64_t audio_tokens_start,
+                     int64_t codebook_size, int64_t* codes_out, int64_t max_frames,
+                     int64_t* frames_out, int32_t* status_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,221 @@
+// Reduced LM head + greedy token choice for up to 8 streams, one launch
+// (sm_100a).
+//
+// Reference: the reduced head of OptimizedDecoder (kani_tts/optimized_decode.py:
+// 134-156 builds W = [lm_head[eos]; lm_head[audio_tokens_start:]], :287 runs
+// logits = F.linear(hidden, W)) followed by the greedy choice
+// reduced_to_full[argmax(logits)] (the reduced-to-full map of :144-148).
+// Here the GEMV, the argmax and the map are one kernel:
+//   * logits[b, r] = round(sum_k h[b, k] * W[r, k])  (fp32 accumulation, one
+//     rounding to the storage type, as F.linear's bf16 output);
+//   * token[b] = index_map[first r with the largest logits[b, r]].
+// The weight rows stream from HBM once (16-byte loads, 4 rows per warp in
+// flight); the hidden rows are staged in shared memory.  Each CTA folds its
+// maxima, packed as (order key << 32 | ~row), into a per-stream 64-bit
+// atomicMax in global scratch; the last CTA to finish (a counter after a
+// fence) writes the tokens and returns the scratch to zero, so the next launch
+// (e.g. the next replay of a CUDA graph) starts clean.
+#include "common.cuh"
+
+namespace kani {
+namespace {
+
+constexpr int kHeadThreads = 256;
+constexpr int kHeadWarps = kHeadThreads / 32;
+constexpr int kHeadRows = 4;   // rows per warp in flight
+constexpr int kHeadMaxB = 8;
+
+struct HeadParams {
+  const void* h;
+  int64_t h_stride;
+  const void* w;
+  int64_t w_stride;
+  int rows, hidden, batch;
+  const int64_t* index_map;
+  void* logits;
+  int64_t logits_stride;
+  unsigned long long* scratch;  // [batch] packed maxima, then one CTA counter
+  int64_t* tokens;
+  int64_t tokens_stride;
+};
+
+template <typename T>
+__device__ __forceinline__ uint32_t order_key16(T v) {
+  uint16_t b;
+  memcpy(&b, &v, 2);
+  if ((b & 0x7fffu) == 0) b = 0;  // -0 == +0
+  return (uint32_t)(b ^ ((b & 0x8000u) ? 0xffffu : 0x8000u));
+}
+
+// B streams (compile-time upper bound), CH = hidden / 256 chunks of 8 per lane
+template <typename T, int B, int CH>
+__global__ void __launch_bounds__(kHeadThreads) head_argmax_kernel(HeadParams p) {
+  constexpr int E = 8;  // elements per 16-byte vector
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ unsigned long long s_best[kHeadWarps][B];
+  __shared__ bool s_last;
+  T* hs = reinterpret_cast<T*>(smem_raw);  // [B][hidden]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int H = CH * 256;
+
+  for (int v = tid; v < B * H / E; v += kHeadThreads) {
+    const int b = v / (H / E), c = v % (H / E);
+    uint4 x = make_uint4(0u, 0u, 0u, 0u);
+    if (b < p.batch) x = ld16_ro(static_cast<const T*>(p.h) + (int64_t)b * p.h_stride + c * E);
+    reinterpret_cast<uint4*>(hs)[v] = x;
+  }
+  __syncthreads();
+
+  unsigned long long best[B];
+#pragma unroll
+  for (int b = 0; b < B; ++b) best[b] = 0ull;
+  const T* W = static_cast<const T*>(p.w);
+  const int gw = blockIdx.x * kHeadWarps + warp, nw = gridDim.x * kHeadWarps;
+  for (int r0 = gw * kHeadRows; r0 < p.rows; r0 += nw * kHeadRows) {
+    uint4 wv[kHeadRows][CH];
+#pragma unroll
+    for (int q = 0; q < kHeadRows; ++q) {
+      const int r = min(r0 + q, p.rows - 1);
+#pragma unroll
+      for (int c = 0; c < CH; ++c) wv[q][c] = ld16_stream(W + (int64_t)r * p.w_stride + c * 256 + lane * E);
+    }
+    float acc[kHeadRows][B];
+#pragma unroll
+    for (int q = 0; q < kHeadRows; ++q)
+#pragma unroll
+      for (int b = 0; b < B; ++b) acc[q][b] = 0.f;
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      float wf[kHeadRows][E];
+#pragma unroll
+      for (int q = 0; q < kHeadRows; ++q) unpack16<T>(wv[q][c], wf[q]);
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        float hf[E];
+        unpack16<T>(reinterpret_cast<const uint4*>(hs + b * H + c * 256)[lane], hf);
+#pragma unroll
+        for (int q = 0; q < kHeadRows; ++q)
+#pragma unroll
+          for (int e = 0; e < E; ++e) acc[q][b] = fmaf(wf[q][e], hf[e], acc[q][b]);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < kHeadRows; ++q)
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        float a = acc[q][b];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+        acc[q][b] = a;
+      }
+    if (lane == 0) {
+#pragma unroll
+      for (int q = 0; q < kHeadRows; ++q) {
+        const int r = r0 + q;
+        if (r >= p.rows) break;
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+          if (b >= p.batch) break;
+          const T lv = Elem<T>::from_f(acc[q][b]);
+          if (p.logits) static_cast<T*>(p.logits)[(int64_t)b * p.logits_stride + r] = lv;
+          const unsigned long long pk =
+              ((unsigned long long)order_key16(lv) << 32) | (unsigned long long)(0xffffffffu - (uint32_t)r);
+          best[b] = pk > best[b] ? pk : best[b];
+        }
+      }
+    }
+  }
+
+  // fold the CTA's maxima into the per-stream scratch; the last CTA finishes
+  if (lane == 0) {
+#pragma unroll
+    for (int b = 0; b < B; ++b) s_best[warp][b] = best[b];
+  }
+  __syncthreads();
+  if (tid < B && tid < p.batch) {
+    unsigned long long m = 0ull;
+#pragma unroll
+    for (int w = 0; w < kHeadWarps; ++w) m = s_best[w][tid] > m ? s_best[w][tid] : m;
+    atomicMax(p.scratch + tid, m);
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const unsigned long long done = atomicAdd(p.scratch + p.batch, 1ull);
+    s_last = done == (unsigned long long)(gridDim.x - 1);
+  }
+  __syncthreads();
+  if (s_last && tid < p.batch) {
+    __threadfence();
+    const unsigned long long m = atomicExch(p.scratch + tid, 0ull);
+    const int r = (int)(0xffffffffu - (uint32_t)(m & 0xffffffffu));
+    const int row = (r >= 0 && r < p.rows) ? r : 0;
+    p.tokens[(int64_t)tid * p.tokens_stride] = p.index_map ? p.index_map[row] : (int64_t)row;
+  }
+  if (s_last && tid == 0) atomicExch(p.scratch + p.batch, 0ull);
+}
+
+template <typename T, int B>
+int launch_head_b(const HeadParams& prm, cudaStream_t s) {
+  const int ch = prm.hidden / 256;
+  const size_t smem = (size_t)B * prm.hidden * sizeof(T);
+  static int sms[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return KANI_ERR_INVALID_ARG;
+  if (sms[dev] == 0) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+  const int per_cta = kHeadWarps * kHeadRows;
+  auto go = [&](auto kern) -> int {
+    if (smem > 48 * 1024) {
+      const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return (int)e;
+    }
+    // one full wave of resident CTAs; warps stride over the rows
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kHeadThreads, smem) != cudaSuccess || occ < 1)
+      occ = 1;
+    const int64_t want = (prm.rows + per_cta - 1) / per_cta, cap = (int64_t)sms[dev] * occ;
+    const int grid = (int)(want < cap ? want : cap);
+    kern<<<grid, kHeadThreads, smem, s>>>(prm);
+    return launch_status();
+  };
+  switch (ch) {
+    case 2: return go(head_argmax_kernel<T, B, 2>);
+    case 4: return go(head_argmax_kernel<T, B, 4>);
+    case 8: return go(head_argmax_kernel<T, B, 8>);
+    default: return KANI_ERR_UNSUPPORTED;
+  }
+}
+
+template <typename T>
+int launch_head(const HeadParams& prm, cudaStream_t s) {
+  if (prm.batch <= 1) return launch_head_b<T, 1>(prm, s);
+  if (prm.batch <= 2) return launch_head_b<T, 2>(prm, s);
+  if (prm.batch <= 4) return launch_head_b<T, 4>(prm, s);
+  return launch_head_b<T, 8>(prm, s);
+}
+
+}  // namespace
+}  // namespace kani
+
+extern "C" int kani_head_argmax(int32_t dtype, const void* hidden, int64_t hidden_row_stride, int64_t batch,
+                                int32_t hidden_size, const void* weight, int64_t weight_row_stride, int32_t rows,
+                                const int64_t* index_map, void* logits_out, int64_t logits_row_stride,
+                                unsigned long long* scratch, int64_t* tokens_out, int64_t tokens_out_stride,
+                                void* stream) {
+  if (batch < 0 || rows < 0 || hidden_size < 0) return KANI_ERR_INVALID_ARG;
+  if (batch == 0) return KANI_OK;
+  if (rows == 0 || !hidden || !weight || !scratch || !tokens_out) return KANI_ERR_INVALID_ARG;
+  if (batch > kani::kHeadMaxB) return KANI_ERR_UNSUPPORTED;
+  if (dtype != KANI_DTYPE_BF16 && dtype != KANI_DTYPE_F16) return dtype == KANI_DTYPE_F32 ? KANI_ERR_UNSUPPORTED
+                                                                                          : KANI_ERR_DTYPE;
+  if (hidden_size % 256 != 0 || weight_row_stride < hidden_size || (batch > 1 && hidden_row_stride < hidden_size))
+    return KANI_ERR_INVALID_ARG;
+  if (logits_out && batch > 1 && logits_row_stride < rows) return KANI_ERR_INVALID_ARG;
+  if (!kani::aligned16(hidden) || !kani::aligned16(weight) || hidden_row_stride % 8 != 0 || weight_row_stride % 8 != 0)
+    return KANI_ERR_UNSUPPORTED;
+  kani::HeadParams prm{hidden, hidden_row_stride, weight, weight_row_stride, rows, hidden_size, (int)batch,
+                       index_map, logits_out, logits_row_stride, scratch, tokens_out, tokens_out_stride};
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == KANI_DTYPE_BF16) return kani::launch_head<__nv_bfloat16>(prm, s);
+  return kani::launch_head<__half>(prm, s);
+}

@@ -66,6 +66,10 @@ _SIGNATURES = {
                             _c_f32, _c_f32, _c_f32, _c_i32,
                             _c_p, ctypes.c_uint64, _c_p,
                             _c_p, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_p], ctypes.c_int),
+    "kani_head_argmax": ([_c_i32, _c_p, _c_i64, _c_i64, _c_i32, _c_p, _c_i64, _c_i32,
+                          _c_p, _c_p, _c_i64, _c_p, _c_p, _c_i64, _c_p], ctypes.c_int),
+    "kani_codec_codes": ([_c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_p, _c_p,
+                          _c_p], ctypes.c_int),
 }
 
 EXPORTED_SYMBOLS = tuple(_SIGNATURES)

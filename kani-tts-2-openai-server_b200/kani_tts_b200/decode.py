@@ -17,7 +17,9 @@
   distributed shared memory) instead of SDPA over the whole -inf-masked
   buffer (optimized_decode.py:243-248);
 * the gated short-conv step between in_proj and out_proj is one
-  ``short_conv_step`` launch (optimized_decode.py:256-277).
+  ``short_conv_step`` launch (optimized_decode.py:256-277);
+* greedy steps of up to 8 streams end in one ``head_argmax`` launch (the
+  reduced head GEMV, the argmax and the reduced-to-full map).
 
 The GEMVs are cuBLAS calls; prefill attention is PyTorch SDPA.
 
@@ -38,7 +40,7 @@ import torch.nn.functional as F
 
 from . import _lib
 from .fused_kernels import (decode_attention, fused_add_rms_norm, fused_rms_norm, fused_rope_kv_write,
-                            fused_silu_mul, sample_tokens, short_conv_step)
+                            fused_silu_mul, head_argmax, sample_tokens, short_conv_step)
 from .model import LFM2Config
 from .positions import learnable_inv_freq
 from .sampling import SamplingParams, seen_bitmap
@@ -103,8 +105,12 @@ class FusedDecoder:
         self.conv_state = {i: torch.zeros(batch, h, cfg.conv_L_cache, dtype=self.dtype, device=dev)
                            for i, L in enumerate(self.layers) if not L["attn"]}
         self.err_flag = _lib.error_flag(dev)
+        # cross-CTA argmax scratch of the fused greedy head (zero between launches)
+        self.head_scratch = torch.zeros(batch + 1, dtype=torch.long, device=dev) if batch <= 8 else None
 
     # ------------------------------------------------------------ decode
+    fused_greedy_head = True   # greedy steps may use the fused head + argmax (batch <= 8)
+
     def step(self, input_ids: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor,
              kv_len: torch.Tensor, mask: torch.Tensor | None = None) -> torch.Tensor:
         """One decode token per stream.
@@ -115,6 +121,20 @@ class FusedDecoder:
         ignored: the valid region is the prefix [0, kv_len).  Returns
         reduced-head logits [B, 1, num_reduced].
         """
+        return F.linear(self._final_hidden(input_ids, positions, slots, kv_len), self.head)
+
+    def step_greedy(self, input_ids: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor,
+                    kv_len: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """One decode token per stream, greedy: the reduced head, the argmax and the
+        reduced-to-full map in one ``head_argmax`` launch (batch <= 8).  Returns
+        the full token ids [B]."""
+        if self.head_scratch is None:
+            raise ValueError("the fused greedy head serves at most 8 streams")
+        normed = self._final_hidden(input_ids, positions, slots, kv_len)
+        return head_argmax(normed, self.head, self.reduced_to_full, scratch=self.head_scratch, out=out)
+
+    def _final_hidden(self, input_ids, positions, slots, kv_len) -> torch.Tensor:
+        """The decode layers and the final norm: [B, 1, H]."""
         b, hq, hk, d = self.batch, self.hq, self.hk, self.d
         hidden = F.embedding(input_ids, self.embed)              # [B, 1, H] residual stream
         delta = None
@@ -139,7 +159,7 @@ class FusedDecoder:
             normed, hidden = fused_add_rms_norm(delta, hidden, L["ffn_norm"], self.eps)
             delta = F.linear(fused_silu_mul(F.linear(normed, L["gate_up"])), L["down"])
         normed, _ = fused_add_rms_norm(delta, hidden, self.final_norm, self.eps)
-        return F.linear(normed, self.head)
+        return normed
 
     def _conv_step(self, i, L, normed):
         """Gated short-conv decode step: in_proj, one fused kernel, out_proj."""
@@ -269,8 +289,12 @@ class DecodeEngine:
         self.kv_len.copy_(self.slots + 1)
         if self.keep_mask:
             self.mask.scatter_(3, self.slots.view(-1, 1, 1, 1), 0.0)
-        self.logits = self.dec.step(self.input_ids, self.positions, self.slots, self.kv_len, self.mask)
-        nxt = self._next_token(self.logits[:, 0])
+        if self.sampling is None and self.dec.fused_greedy_head and self.dec.head_scratch is not None:
+            self.logits = None
+            nxt = self.dec.step_greedy(self.input_ids, self.positions, self.slots, self.kv_len, out=self.next_tok)
+        else:
+            self.logits = self.dec.step(self.input_ids, self.positions, self.slots, self.kv_len, self.mask)
+            nxt = self._next_token(self.logits[:, 0])
         self.generated.index_copy_(1, k, nxt.view(-1, 1))
         self.input_ids.copy_(nxt.view(-1, 1))
         self.step_idx.add_(1)

@@ -42,6 +42,8 @@ __all__ = [
     "decode_attention",
     "short_conv_step",
     "sample_tokens",
+    "head_argmax",
+    "codec_codes",
 ]
 
 
@@ -504,6 +506,91 @@ def sample_tokens(logits: torch.Tensor, seen: torch.Tensor | None = None, *, tem
         ptr(det["draws"]) if det else None, ptr(det["probs"]) if det else None,
         ptr(det["cand"]) if det else None, ptr(out), out_stride, stream_ptr(dev)), "kani_sample_tokens")
     return (out, det) if return_details else out
+
+
+def head_argmax(hidden: torch.Tensor, weight: torch.Tensor, index_map: torch.Tensor | None = None, *,
+                scratch: torch.Tensor | None = None, logits_out: torch.Tensor | None = None,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """Greedy next token from the reduced LM head (optimized_decode.py:287 and the
+    reduced-to-full map of :144-148) for up to 8 streams in one launch.
+
+    Args:
+        hidden: [B, H] or [B, 1, H] final-normed hidden state (bf16 / fp16).
+        weight: [rows, H] reduced head (same dtype).
+        index_map: [rows] int64 row -> token id (``reduced_to_full``); None = row index.
+        scratch: [B + 1] int64 device tensor, zero before the first call and left
+            zero by every call; allocated (zeroed) per call when None.
+        logits_out: optional [B, rows] tensor that receives the logits.
+        out: optional [B] int64 tensor for the token ids.
+    Returns:
+        [B] int64 token ids.
+    """
+    require_cuda(hidden, "hidden")
+    require_cuda(weight, "weight")
+    lib = load_library()
+    code = dtype_code(hidden, "hidden")
+    h = weight.shape[-1]
+    if weight.dim() != 2 or hidden.shape[-1] != h:
+        raise ValueError(f"hidden [..., {h}] and weight [rows, {h}] expected")
+    if weight.dtype != hidden.dtype:
+        raise TypeError("hidden and weight must share one dtype")
+    hv, b, hs = _rows_view(hidden, h)
+    if weight.stride(1) != 1:
+        weight = weight.contiguous()
+    rows = weight.shape[0]
+    dev = hidden.device
+    if scratch is None:
+        scratch = torch.zeros(b + 1, dtype=torch.int64, device=dev)
+    require_cuda(scratch, "scratch")
+    if scratch.dtype != torch.int64 or scratch.numel() < b + 1 or not scratch.is_contiguous():
+        raise ValueError(f"scratch must be a contiguous int64 tensor of >= {b + 1} elements")
+    if index_map is not None:
+        require_cuda(index_map, "index_map")
+        if index_map.dtype != torch.int64 or index_map.numel() != rows or not index_map.is_contiguous():
+            raise ValueError(f"index_map must be a contiguous int64 [{rows}] tensor")
+    ls = 0
+    if logits_out is not None:
+        require_cuda(logits_out, "logits_out")
+        if logits_out.dtype != hidden.dtype or logits_out.shape[-1] != rows or logits_out.stride(-1) != 1:
+            raise ValueError(f"logits_out must be [{b}, {rows}] of the hidden dtype")
+        ls = logits_out.stride(0) if logits_out.dim() > 1 else rows
+    if out is None:
+        out = torch.empty(b, dtype=torch.int64, device=dev)
+    if out.dtype != torch.int64 or out.numel() != b:
+        raise ValueError(f"out must hold {b} int64 token ids")
+    check(lib.kani_head_argmax(code, ptr(hv), hs, b, h, ptr(weight), weight.stride(0), rows,
+                               ptr(index_map) if index_map is not None else None,
+                               ptr(logits_out) if logits_out is not None else None, ls, ptr(scratch),
+                               ptr(out), out.stride(0) if b > 1 else 1, stream_ptr(dev)), "kani_head_argmax")
+    return out
+
+
+def codec_codes(tokens: torch.Tensor, eos_token: int, audio_tokens_start: int, codebook_size: int = 4032):
+    """NeMo codec codes of generated audio tokens (core.py:86-108) for B streams.
+
+    Args:
+        tokens: [B, T] int64 generated token ids (device).
+    Returns:
+        (codes [B, 4, T // 4] int64 (-1 past a stream's frames), frames [B] int64,
+        status [B] int32: bit 0 a negative code, bit 1 no complete frame, bit 2 no
+        end-of-speech token).
+    """
+    require_cuda(tokens, "tokens")
+    lib = load_library()
+    if tokens.dtype != torch.int64 or tokens.dim() != 2:
+        raise ValueError("tokens must be an int64 [batch, n_tokens] tensor")
+    if tokens.stride(1) != 1:
+        tokens = tokens.contiguous()
+    b, t = tokens.shape
+    mf = t // 4
+    dev = tokens.device
+    codes = torch.empty(b, 4, mf, dtype=torch.int64, device=dev)
+    frames = torch.empty(b, dtype=torch.int64, device=dev)
+    status = torch.empty(b, dtype=torch.int32, device=dev)
+    check(lib.kani_codec_codes(ptr(tokens), tokens.stride(0), b, t, int(eos_token), int(audio_tokens_start),
+                               int(codebook_size), ptr(codes), mf, ptr(frames), ptr(status), stream_ptr(dev)),
+          "kani_codec_codes")
+    return codes, frames, status
 
 
 def launch_count() -> int:

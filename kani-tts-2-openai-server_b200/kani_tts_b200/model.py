@@ -49,7 +49,7 @@ class LFM2Config:
     norm_eps: float = 1e-5
     rope_theta: float = 1e6
     audio_tokens_start: int = 64410
-    eos_token_id: int = 7
+    eos_token_id: int = 64402          # end-of-speech: the engine's EOS (core.py:599, config.py:12)
     tokens_per_frame: int = 4
     audio_step: float = 1.0
     speaker_emb_dim: int = 128

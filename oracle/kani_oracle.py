@@ -316,3 +316,49 @@ def ulp_distance(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     oa = torch.where(ia < 0, -(ia & mag), ia)
     ob = torch.where(ib < 0, -(ib & mag), ib)
     return (oa - ob).abs()
+
+
+def head_argmax_ref(hidden: torch.Tensor, weight: torch.Tensor, index_map: torch.Tensor | None = None
+                    ) -> tuple[torch.Tensor, torch.Tensor]:
+    """Reduced LM head + greedy choice (kani_tts/optimized_decode.py:287, the head
+    built at :134-156, the reduced-to-full map of :144-148): logits rounded once to
+    the storage type from a float64 dot product; token = map[first argmax].
+    Returns (tokens [B], logits [B, rows])."""
+    h = hidden.reshape(-1, hidden.shape[-1]).double()
+    logits = (h @ weight.double().T).to(hidden.dtype)
+    idx = torch.argmax(logits.float(), dim=-1)   # first index of the maximum
+    tok = index_map[idx] if index_map is not None else idx
+    return tok, logits
+
+
+def codec_codes_ref(tokens: torch.Tensor, eos_token: int, audio_tokens_start: int, codebook_size: int = 4032
+                    ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """NemoAudioPlayer.get_nano_codes (kani_tts/core.py:86-108) for each stream's
+    generated tokens: the segment before the first end-of-speech token, cut to
+    whole frames of 4, code = token - c * codebook_size - audio_tokens_start.
+    The reference raises where this returns status bits: 1 = a negative code,
+    2 = no complete frame, 4 = no end-of-speech token.
+    Returns (codes [B, 4, T // 4] with -1 past the frames, frames [B], status [B])."""
+    tokens = tokens.cpu().long()
+    b_n, t = tokens.shape
+    mf = t // 4
+    codes = torch.full((b_n, 4, mf), -1, dtype=torch.long)
+    frames = torch.zeros(b_n, dtype=torch.long)
+    status = torch.zeros(b_n, dtype=torch.int32)
+    for b in range(b_n):
+        hit = (tokens[b] == eos_token).nonzero(as_tuple=True)[0]
+        end = int(hit[0]) if hit.numel() else t
+        seg = tokens[b, :end]
+        seg = seg[: len(seg) - len(seg) % 4]
+        nf = len(seg) // 4
+        st = 0 if hit.numel() else 4
+        if nf == 0:
+            st |= 2
+        else:
+            c = seg.reshape(-1, 4) - torch.tensor([codebook_size * i for i in range(4)]) - audio_tokens_start
+            if bool((c < 0).any()):
+                st |= 1
+            codes[b, :, :nf] = c.T
+        frames[b] = nf
+        status[b] = st
+    return codes, frames, status

@@ -202,7 +202,53 @@ def main() -> None:
 
     save("decode_step", decode_step_cases(sc, md, hf))
     save("sampling", sampling_cases())
+    save("codec_codes", codec_cases())
     print("golden vectors written to", OUT)
+
+
+def codec_cases():
+    """NemoAudioPlayer.get_nano_codes (kani_tts/core.py:86-108) on token sequences
+    built as the engine returns them: prompt ending with start-of-speech, the
+    generated audio tokens, end-of-speech.  NeMo itself is absent, so placeholder
+    ``nemo.collections.tts.models`` modules let ``kani_tts.core`` import; the
+    function reads only the four attributes of the stand-in object.  Where the
+    reference raises, the case records the message instead of codes."""
+    import types as _t
+    for name in ["nemo", "nemo.collections", "nemo.collections.tts", "nemo.collections.tts.models"]:
+        sys.modules.setdefault(name, _t.ModuleType(name))
+    if not hasattr(sys.modules["nemo.collections.tts.models"], "AudioCodecModel"):
+        class AudioCodecModel:  # placeholder (type use only)
+            pass
+        sys.modules["nemo.collections.tts.models"].AudioCodecModel = AudioCodecModel
+    core = importlib.import_module("kani_tts.core")
+    tl = 64400
+    player = _t.SimpleNamespace(start_of_speech=tl + 1, end_of_speech=tl + 2, codebook_size=4032,
+                                audio_tokens_start=tl + 10)
+    g = _gen(77)
+
+    def audio(n):
+        c = torch.arange(n) % 4
+        return tl + 10 + c * 4032 + torch.randint(0, 4032, (n,), generator=g)
+
+    prompt = torch.cat([torch.randint(0, tl, (20,), generator=g), torch.tensor([tl + 1])])
+    cases = {}
+    for name, gen in {
+        "whole_frames": audio(48),
+        "partial_frame": audio(51),
+        "one_frame": audio(5),
+        "negative_code": torch.cat([audio(8), torch.tensor([tl + 10 + 4032 * 2 - 1]), audio(3)]),
+        "no_frame": audio(3),
+    }.items():
+        gen_ids = torch.cat([gen, torch.tensor([tl + 2])])
+        out_ids = torch.cat([prompt, gen_ids])
+        d = dict(generated=gen_ids)
+        try:
+            codes, n = core.NemoAudioPlayer.get_nano_codes(player, out_ids)
+            d.update(codes=codes, frames=n)
+        except ValueError as e:
+            d.update(error=np.array(str(e)))
+        cases[name] = d
+    return cases
 
 
 def _tie_free_logits(v: int, n_top: int, lo: float, hi: float, seed: int) -> torch.Tensor:
@@ -401,8 +447,10 @@ def decode_step_cases(sc, md, hf):
 
 
 if __name__ == "__main__":
-    if len(sys.argv) > 1 and sys.argv[1] == "--only-sampling":
+    if len(sys.argv) > 2 and sys.argv[1] == "--only":
         _import_reference()
-        save("sampling", sampling_cases())
+        makers = {"sampling": sampling_cases, "codec_codes": codec_cases}
+        for name in sys.argv[2:]:
+            save(name, makers[name]())
     else:
         main()

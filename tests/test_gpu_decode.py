@@ -180,3 +180,30 @@ def test_engine_with_device_sampling_graph_matches_eager():
         for r in red[s].cpu().tolist():
             assert (int(words[s, r // 32]) >> (r % 32)) & 1
     assert int(eng.rng_step.item()) == n + 1
+
+
+@pytest.mark.parametrize("full", [False, True])
+def test_fused_greedy_head_matches_logits_argmax(full):
+    """step_greedy (layers + fused head/argmax/map) picks a token whose F.linear
+    logit is the maximum within one bf16 ULP (the two GEMVs sum in different
+    orders), and the same token when the maximum is unique by a margin."""
+    cfg = LFM2Config() if full else tiny_config()
+    b, max_len = 3, 32
+    sd = synthetic_state_dict(cfg, seed=21)
+    dec = FusedDecoder(cfg, sd, DEV, batch=b, max_len=max_len)
+    ids = torch.randint(cfg.audio_tokens_start, cfg.vocab_size, (b, 1), generator=torch.Generator().manual_seed(2))
+    pos, slots = torch.tensor([3, 5, 7]), torch.tensor([4, 6, 8])
+    args = (ids.to(DEV), pos.to(DEV), slots.to(DEV), (slots + 1).to(DEV))
+    snap = ({i: c.clone() for i, c in dec.conv_state.items()})
+    logits = dec.step(*args)[:, 0].float().cpu()
+    for i, c in snap.items():
+        dec.conv_state[i].copy_(c)
+    tok = dec.step_greedy(*args).cpu()
+    red = dec.full_to_reduced.cpu()[tok]
+    top = logits.max(-1).values
+    picked = logits.gather(1, red.view(-1, 1)).view(-1)
+    assert bool((picked >= top - top.abs() * 2 ** -7).all())
+    margin = logits.topk(2, -1).values
+    clear = (margin[:, 0] - margin[:, 1]) > margin[:, 0].abs() * 2 ** -6
+    assert torch.equal(red[clear], logits.argmax(-1)[clear])
+    assert int(dec.head_scratch.abs().sum()) == 0

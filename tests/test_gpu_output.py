@@ -1,0 +1,130 @@
+"""GPU parity of the output-side kernels: the reduced head with the greedy choice
+(``kani_head_argmax``) and the codec-code mapping (``kani_codec_codes``).
+
+Tolerances:
+  * head logits: within 1 ULP of the oracle's float64 dot product rounded once
+    (fp32 accumulation in another order), >= 99 % identical;
+  * head token: identical to the first maximum of the kernel's own logits,
+    and to the oracle's token whenever the two logit rows are identical;
+  * codec codes, frame counts and status words: identical.
+"""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from golden_io import load
+from oracle import kani_oracle as O
+
+from kani_tts_b200 import fused_kernels as K
+from kani_tts_b200._lib import KaniError
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+EOS, AUDIO_START = 64402, 64410
+
+
+def rnd(shape, seed, dtype=torch.bfloat16, std=1.0):
+    g = torch.Generator().manual_seed(seed)
+    return (std * torch.randn(shape, generator=g)).to(dtype)
+
+
+def check_head(hidden, weight, imap, tok, logits):
+    ref_tok, ref_logits = O.head_argmax_ref(hidden, weight, imap)
+    d = O.ulp_distance(logits.cpu(), ref_logits)
+    assert int(d.max()) <= 1, f"max ULP {int(d.max())}"
+    assert float((d == 0).float().mean()) >= 0.99
+    own = torch.argmax(logits.cpu().float(), dim=-1)
+    want = imap[own] if imap is not None else own
+    assert torch.equal(tok.cpu(), want)
+    same = (d == 0).all(dim=-1)
+    assert torch.equal(tok.cpu()[same], ref_tok[same])
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("b,h,rows", [(1, 1024, 15591), (3, 1024, 15591), (8, 1024, 4000), (2, 512, 37),
+                                      (5, 2048, 1000)])
+def test_head_argmax_vs_oracle(dtype, b, h, rows):
+    hidden = rnd((b, h), 1300 + b, dtype)
+    weight = rnd((rows, h), 1301 + rows, dtype, std=0.05)
+    imap = torch.arange(rows, dtype=torch.long) * 3 + 11
+    logits = torch.empty(b, rows, dtype=dtype, device=DEV)
+    tok = K.head_argmax(hidden.to(DEV), weight.to(DEV), imap.to(DEV), logits_out=logits)
+    check_head(hidden, weight, imap, tok, logits)
+
+
+def test_head_argmax_scratch_is_left_clean_and_reused():
+    """Two calls on one scratch buffer (the second sees what the first left) and a
+    graph replayed with new hidden states; the scratch is all zero afterwards."""
+    b, h, rows = 4, 1024, 15591
+    weight = rnd((rows, h), 1310, std=0.05).to(DEV)
+    scratch = torch.zeros(b + 1, dtype=torch.long, device=DEV)
+    for seed in (1311, 1312):
+        hidden = rnd((b, h), seed)
+        logits = torch.empty(b, rows, dtype=torch.bfloat16, device=DEV)
+        tok = K.head_argmax(hidden.to(DEV), weight, scratch=scratch, logits_out=logits)
+        check_head(hidden, weight.cpu(), None, tok, logits)
+        assert int(scratch.abs().sum()) == 0
+    hid = torch.zeros(b, h, dtype=torch.bfloat16, device=DEV)
+    out = torch.zeros(b, dtype=torch.long, device=DEV)
+    logits = torch.empty(b, rows, dtype=torch.bfloat16, device=DEV)
+    s = torch.cuda.Stream(device=DEV)
+    s.wait_stream(torch.cuda.current_stream(DEV))
+    with torch.cuda.stream(s):
+        K.head_argmax(hid, weight, scratch=scratch, logits_out=logits, out=out)
+    torch.cuda.current_stream(DEV).wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        K.head_argmax(hid, weight, scratch=scratch, logits_out=logits, out=out)
+    for seed in (1313, 1314, 1315):
+        hidden = rnd((b, h), seed)
+        hid.copy_(hidden)
+        graph.replay()
+        torch.cuda.synchronize()
+        check_head(hidden, weight.cpu(), None, out, logits)
+    assert int(scratch.abs().sum()) == 0
+
+
+def test_head_argmax_ties_and_limits():
+    h, rows = 512, 300
+    weight = torch.zeros(rows, h, dtype=torch.bfloat16, device=DEV)
+    hidden = rnd((2, h), 1320).to(DEV)
+    imap = torch.arange(rows, device=DEV) + 1000
+    assert K.head_argmax(hidden, weight, imap).tolist() == [1000, 1000]      # all equal: the first row
+    weight[7, 0] = 1.0
+    weight[9, 0] = 1.0
+    hidden[:, 0] = 2.0
+    assert K.head_argmax(hidden, weight, imap).tolist() == [1007, 1007]      # equal maxima: the lower row
+    with pytest.raises(KaniError):
+        K.head_argmax(rnd((9, h), 1321).to(DEV), weight)                     # more than 8 streams
+
+
+@pytest.mark.parametrize("name", ["whole_frames", "partial_frame", "one_frame", "negative_code", "no_frame"])
+def test_codec_codes_match_reference_golden(name):
+    c = load("codec_codes")[name]
+    codes, frames, status = K.codec_codes(c["generated"].view(1, -1).to(DEV), EOS, AUDIO_START)
+    if "error" in c:
+        want = {"Invalid audio tokens!": 1, "No complete audio frames generated!": 2}[c["error"]]
+        assert int(status[0]) & want
+    else:
+        nf = int(c["frames"][0])
+        assert int(frames[0]) == nf and int(status[0]) == 0
+        assert torch.equal(codes[0, :, :nf].cpu(), c["codes"][0])
+
+
+def test_codec_codes_batch_vs_oracle():
+    g = torch.Generator().manual_seed(1330)
+    b, t = 6, 1500
+    c = torch.arange(t) % 4
+    toks = AUDIO_START + c * 4032 + torch.randint(0, 4032, (b, t), generator=g)
+    toks[0, 1000] = EOS                       # ends mid-frame
+    toks[1, 3] = EOS                          # no complete frame
+    toks[2, 400] = EOS
+    toks[2, 17] = AUDIO_START - 5             # a negative code
+    toks[4, 0] = EOS                          # empty
+    # stream 3 and 5: no end-of-speech token
+    got = K.codec_codes(toks.to(DEV), EOS, AUDIO_START)
+    ref = O.codec_codes_ref(toks, EOS, AUDIO_START)
+    for x, y in zip(got, ref):
+        assert torch.equal(x.cpu(), y)
+    assert [int(s) for s in ref[2]] == [0, 2, 1, 4, 2, 4]

@@ -98,6 +98,14 @@ def test_abi_rejects_bad_arguments_without_launching():
     assert sample(tok=n) == -1
     assert sample(rs=100) == -1
     assert sample(dtype=5) == -2
+    # reduced head: batch above 8, fp32, hidden size not a multiple of 256, missing scratch
+    assert lib.kani_head_argmax(1, fake, 1024, 9, 1024, fake, 1024, 100, n, n, 0, fake, fake, 1, n) == -3
+    assert lib.kani_head_argmax(0, fake, 1024, 1, 1024, fake, 1024, 100, n, n, 0, fake, fake, 1, n) == -3
+    assert lib.kani_head_argmax(1, fake, 1000, 1, 1000, fake, 1000, 100, n, n, 0, fake, fake, 1, n) == -1
+    assert lib.kani_head_argmax(1, fake, 1024, 1, 1024, fake, 1024, 100, n, n, 0, n, fake, 1, n) == -1
+    # codec codes: too few frames for the tokens, missing outputs
+    assert lib.kani_codec_codes(fake, 100, 2, 100, 64402, 64410, 4032, fake, 24, fake, fake, n) == -1
+    assert lib.kani_codec_codes(fake, 100, 2, 100, 64402, 64410, 4032, n, 25, fake, fake, n) == -1
     assert lib.kani_launch_count() == before
 
 
@@ -114,6 +122,8 @@ def test_abi_zero_sized_calls_are_noops():
                                   n, 0, 0, n, n, 0, 0, 0, 16, n, n, n) == 0
     assert lib.kani_sample_tokens(1, n, 0, 0, 15591, n, n, 0, 1, 1.2, 0.5, 0.85, 256, n, 0, n, n, n, n, n,
                                   n, 1, n) == 0
+    assert lib.kani_head_argmax(1, n, 0, 0, 1024, n, 1024, 15591, n, n, 0, n, n, 1, n) == 0
+    assert lib.kani_codec_codes(n, 0, 0, 100, 64402, 64410, 4032, n, 25, n, n, n) == 0
     assert lib.kani_launch_count() == before
 
 
@@ -123,6 +133,8 @@ def test_abi_zero_sized_calls_are_noops():
     lambda: K.fused_silu_mul(torch.zeros(2, 16)),
     lambda: K.fused_rope(torch.zeros(1, 2, 1, 8), torch.zeros(1, 1, 1, 8), torch.zeros(8), torch.zeros(8)),
     lambda: K.sample_tokens(torch.zeros(2, 300)),
+    lambda: K.head_argmax(torch.zeros(1, 256), torch.zeros(10, 256)),
+    lambda: K.codec_codes(torch.zeros(1, 8, dtype=torch.long), 64402, 64410),
 ])
 def test_cpu_tensors_are_refused(call):
     with pytest.raises(ValueError, match="CUDA"):

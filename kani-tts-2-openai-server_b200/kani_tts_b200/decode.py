@@ -106,7 +106,8 @@ class FusedDecoder:
                            for i, L in enumerate(self.layers) if not L["attn"]}
         self.err_flag = _lib.error_flag(dev)
         # cross-CTA argmax scratch of the fused greedy head (zero between launches)
-        self.head_scratch = torch.zeros(batch + 1, dtype=torch.long, device=dev) if batch <= 8 else None
+        fits = batch <= 8 and h in (512, 1024, 2048)
+        self.head_scratch = torch.zeros(batch + 1, dtype=torch.long, device=dev) if fits else None
 
     # ------------------------------------------------------------ decode
     fused_greedy_head = True   # greedy steps may use the fused head + argmax (batch <= 8)
@@ -126,10 +127,10 @@ class FusedDecoder:
     def step_greedy(self, input_ids: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor,
                     kv_len: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         """One decode token per stream, greedy: the reduced head, the argmax and the
-        reduced-to-full map in one ``head_argmax`` launch (batch <= 8).  Returns
-        the full token ids [B]."""
+        reduced-to-full map in one ``head_argmax`` launch (batch <= 8, hidden size
+        512 / 1024 / 2048).  Returns the full token ids [B]."""
         if self.head_scratch is None:
-            raise ValueError("the fused greedy head serves at most 8 streams")
+            raise ValueError("the fused greedy head serves at most 8 streams of hidden size 512, 1024 or 2048")
         normed = self._final_hidden(input_ids, positions, slots, kv_len)
         return head_argmax(normed, self.head, self.reduced_to_full, scratch=self.head_scratch, out=out)
 

@@ -3,7 +3,8 @@
 
 Tolerances:
   * head logits: within 1 ULP of the oracle's float64 dot product rounded once
-    (fp32 accumulation in another order), >= 99 % identical;
+    (fp32 accumulation in another order), or within 2^-16 x sum |h w| where
+    the products cancel towards zero; >= 99 % identical;
   * head token: identical to the first maximum of the kernel's own logits,
     and to the oracle's token whenever the two logit rows are identical;
   * codec codes, frame counts and status words: identical.
@@ -32,7 +33,11 @@ def rnd(shape, seed, dtype=torch.bfloat16, std=1.0):
 def check_head(hidden, weight, imap, tok, logits):
     ref_tok, ref_logits = O.head_argmax_ref(hidden, weight, imap)
     d = O.ulp_distance(logits.cpu(), ref_logits)
-    assert int(d.max()) <= 1, f"max ULP {int(d.max())}"
+    # 1 ULP, or an fp32-accumulation bound where the products cancel towards zero
+    mag = hidden.reshape(-1, hidden.shape[-1]).double().abs() @ weight.double().abs().T
+    err = (logits.cpu().double() - ref_logits.double()).abs()
+    ok = (d <= 1) | (err <= mag * 2.0 ** -16)
+    assert bool(ok.all()), f"{int((~ok).sum())} logits outside tolerance, max ULP {int(d.max())}"
     assert float((d == 0).float().mean()) >= 0.99
     own = torch.argmax(logits.cpu().float(), dim=-1)
     want = imap[own] if imap is not None else own

@@ -267,6 +267,18 @@ KANI_API int kani_head_argmax(int32_t dtype, const void* hidden, int64_t hidden_
                      void* stream);
 
 /*
+ * kani_head_argmax without the scratch argument: the scratch is a file-scope
+ * device array (zero at load, left zero by every call), located per device with
+ * cudaGetSymbolAddress; nothing is allocated.  batch + 1 must not exceed 64
+ * (KANI_ERR_UNSUPPORTED); calls on one device must not overlap in time.
+ */
+KANI_API int kani_head_argmax_noalloc(int32_t dtype, const void* hidden, int64_t hidden_row_stride,
+                     int64_t batch, int32_t hidden_size, const void* weight,
+                     int64_t weight_row_stride, int32_t rows, const int64_t* index_map,
+                     void* logits_out, int64_t logits_row_stride, int64_t* tokens_out,
+                     int64_t tokens_out_stride, void* stream);
+
+/*
  * Generated tokens -> NeMo codec codes for `batch` streams (replaces
  * NemoAudioPlayer.get_nano_codes, kani_tts/core.py:86-108):
  *   a stream's audio segment is its tokens before the first `eos_token`

@@ -219,3 +219,45 @@ extern "C" int kani_head_argmax(int32_t dtype, const void* hidden, int64_t hidde
   if (dtype == KANI_DTYPE_BF16) return kani::launch_head<__nv_bfloat16>(prm, s);
   return kani::launch_head<__half>(prm, s);
 }
+
+// ------------------------------------------------ entry point without a scratch
+//
+// The same launch with the cross-CTA scratch taken from a file-scope device
+// array instead of caller memory: nothing to allocate or zero.  The array is
+// zero at module load and every launch leaves it zero; one array per device is
+// shared by all callers, so calls on one device must not overlap in time.
+namespace kani {
+namespace {
+constexpr int kStaticScratchWords = 64;  // streams + 1 counter
+static_assert(kStaticScratchWords >= kHeadMaxB + 1, "static scratch too small");
+}  // namespace
+}  // namespace kani
+
+static __device__ __align__(256) unsigned long long g_head_scratch[kani::kStaticScratchWords];
+
+static unsigned long long* head_static_scratch() {
+  constexpr int kMaxDevices = 64;
+  static unsigned long long* addr[kMaxDevices] = {};
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  if (!addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_head_scratch) != cudaSuccess) return nullptr;
+    addr[dev] = static_cast<unsigned long long*>(p);
+  }
+  return addr[dev];
+}
+
+extern "C" int kani_head_argmax_noalloc(int32_t dtype, const void* hidden, int64_t hidden_row_stride,
+                                        int64_t batch, int32_t hidden_size, const void* weight,
+                                        int64_t weight_row_stride, int32_t rows, const int64_t* index_map,
+                                        void* logits_out, int64_t logits_row_stride, int64_t* tokens_out,
+                                        int64_t tokens_out_stride, void* stream) {
+  if (batch < 0) return KANI_ERR_INVALID_ARG;
+  if (batch == 0) return KANI_OK;
+  if (batch + 1 > kani::kStaticScratchWords) return KANI_ERR_UNSUPPORTED;  // size check
+  unsigned long long* scratch = head_static_scratch();
+  if (!scratch) return KANI_ERR_INVALID_ARG;
+  return kani_head_argmax(dtype, hidden, hidden_row_stride, batch, hidden_size, weight, weight_row_stride, rows,
+                          index_map, logits_out, logits_row_stride, scratch, tokens_out, tokens_out_stride, stream);
+}

@@ -565,6 +565,35 @@ def head_argmax(hidden: torch.Tensor, weight: torch.Tensor, index_map: torch.Ten
     return out
 
 
+def head_argmax_noalloc(hidden: torch.Tensor, weight: torch.Tensor, index_map: torch.Tensor | None = None, *,
+                        logits_out: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``head_argmax`` through ``kani_head_argmax_noalloc``: the cross-CTA scratch
+    is the library's own device array, so nothing is allocated per call (calls on
+    one device must not overlap in time)."""
+    require_cuda(hidden, "hidden")
+    require_cuda(weight, "weight")
+    lib = load_library()
+    code = dtype_code(hidden, "hidden")
+    h = weight.shape[-1]
+    if weight.dim() != 2 or hidden.shape[-1] != h or weight.dtype != hidden.dtype:
+        raise ValueError(f"hidden [..., {h}] and weight [rows, {h}] of one dtype expected")
+    hv, b, hs = _rows_view(hidden, h)
+    if weight.stride(1) != 1:
+        weight = weight.contiguous()
+    rows = weight.shape[0]
+    if index_map is not None and (index_map.dtype != torch.int64 or index_map.numel() != rows):
+        raise ValueError(f"index_map must be an int64 [{rows}] tensor")
+    ls = logits_out.stride(0) if logits_out is not None and logits_out.dim() > 1 else rows
+    if out is None:
+        out = torch.empty(b, dtype=torch.int64, device=hidden.device)
+    check(lib.kani_head_argmax_noalloc(code, ptr(hv), hs, b, h, ptr(weight), weight.stride(0), rows,
+                                       ptr(index_map) if index_map is not None else None,
+                                       ptr(logits_out) if logits_out is not None else None, ls, ptr(out),
+                                       out.stride(0) if b > 1 else 1, stream_ptr(hidden.device)),
+          "kani_head_argmax_noalloc")
+    return out
+
+
 def codec_codes(tokens: torch.Tensor, eos_token: int, audio_tokens_start: int, codebook_size: int = 4032):
     """NeMo codec codes of generated audio tokens (core.py:86-108) for B streams.
 

@@ -279,6 +279,27 @@ KANI_API int kani_head_argmax_noalloc(int32_t dtype, const void* hidden, int64_t
                      int64_t tokens_out_stride, void* stream);
 
 /*
+ * Decode GEMV for up to 8 streams with its neighbours fused:
+ *   y[b, r] = round(sum_k a[b, k] * weight[r, k])   (fp32 accumulation)
+ * a = x, or with norm_weight the RMSNorm of the residual stream:
+ *   h = round(x + residual) (residual may be NULL: h = x; residual_out, when given,
+ *   receives h), a = round((h * rr) * norm_weight), rr = 1 / sqrt(mean(h^2) + eps).
+ * silu_pairs != 0: weight holds 2 * n_out rows (gate, then up) and
+ *   y[b, r] = round(silu(round(gate_r)) * round(up_r)).
+ * Replaces the F.linear calls of the decode step (kani_tts/optimized_decode.py:
+ * 215, 255, 276, 281-282) with the residual add + RMSNorm before them (:206, :252,
+ * :277, :280, :283) and the SiLU·mul between the MLP GEMVs (triton_kernels.py:67-105).
+ *   x, residual, residual_out: [batch, k] (row strides, 16-byte aligned rows);
+ *   weight: [n_out or 2 n_out, k] (row stride); y: [batch, n_out] (row stride);
+ *   bf16 / fp16; k = 1024 or 4608; batch <= 8; residual_out must not be x or residual.
+ */
+KANI_API int kani_gemv(int32_t dtype, const void* x, int64_t x_row_stride, const void* residual,
+                     int64_t residual_row_stride, void* residual_out, int64_t residual_out_row_stride,
+                     const void* norm_weight, float eps, const void* weight, int64_t weight_row_stride,
+                     int32_t n_out, int32_t k, int64_t batch, int32_t silu_pairs, void* y,
+                     int64_t y_row_stride, void* stream);
+
+/*
  * Generated tokens -> NeMo codec codes for `batch` streams (replaces
  * NemoAudioPlayer.get_nano_codes, kani_tts/core.py:86-108):
  *   a stream's audio segment is its tokens before the first `eos_token`

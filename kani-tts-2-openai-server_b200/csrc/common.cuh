@@ -161,6 +161,19 @@ __device__ __forceinline__ void load_weights(const W* w, int64_t off, float* out
   }
 }
 
+// (g * sigmoid(g)) * u in fp32, the activation of the SwiGLU MLP (shared by the
+// SiLU kernel and the GEMV epilogue so both round identically).  sigmoid from
+// t = e^-|g| in (0, 1]: g / (1 + e^-g) is 1/(1+t) for g >= 0 and t/(1+t) for
+// g < 0, so the divisor stays in [1, 2], where the fast divide is accurate.
+// Below |g| ~ 87 the fast exponential flushes to zero while e^g is still
+// representable, so that (rare) case takes the full-range expf.
+__device__ __forceinline__ float silu_mul_f(float g, float u) {
+  const float t = __expf(-fabsf(g));
+  float sig = __fdividef(g >= 0.f ? 1.0f : t, 1.0f + t);
+  if (t == 0.f && g < 0.f) sig = expf(g);
+  return __fmul_rn(__fmul_rn(g, sig), u);
+}
+
 // ---------------------------------------------------------------- misc
 
 __host__ __device__ __forceinline__ bool aligned16(const void* p) {

@@ -1,0 +1,236 @@
+// Small-batch decode GEMV with its neighbours fused (sm_100a), for up to 8
+// streams.
+//
+//   y[b, r] = round(sum_k a[b, k] * W[r, k])            (fp32 accumulation)
+//
+// The input a[b] is either x[b] itself, or (NORM) the RMSNorm of the residual
+// stream, folded in front of the GEMV that consumes it:
+//   h = round(x + residual)  (when a residual is given; h is written to
+//                             residual_out by CTA 0 for the next layer)
+//   a = round((h * rr) * w), rr = 1 / sqrt(sum h^2 / K + eps)
+// — the arithmetic of kani_add_rms_norm / kani_rms_norm.  With SILU the
+// weight holds 2N rows (gate rows, then up rows) and the epilogue is
+//   y[b, r] = round(silu(round(g)) * round(u)),  g = acc row r, u = acc row N + r
+// — F.linear(gate_up) followed by the fused SiLU·mul kernel, rounding for
+// rounding.  Reference: the decode step of kani_tts/optimized_decode.py:175-289
+// (residual adds :252/:277/:283, norms :206/:280/:286, the QKV / in_proj /
+// gate_up / down / o_proj / out_proj F.linear calls, the SiLU·mul of
+// kani_tts/triton_kernels.py:67-105).  Merging norm + GEMV and GEMV + SiLU
+// removes a launch each per use; at one token per stream every launch costs
+// a few microseconds of latency, more than the bytes it moves.
+//
+// Layout: 256-thread CTAs; one warp per output row (SILU: per gate/up pair)
+// streams the row with 16-byte evict-first loads (K / 256 loads in flight per
+// lane); the B input rows sit in shared memory.  Every CTA recomputes the
+// norm (a few KB from L2).
+#include "common.cuh"
+
+namespace kani {
+namespace {
+
+constexpr int kGemvThreads = 256;
+constexpr int kGemvWarps = kGemvThreads / 32;
+constexpr int kGemvMaxB = 8;
+
+struct GemvParams {
+  const void* x;
+  int64_t x_stride;
+  const void* res;
+  int64_t res_stride;
+  void* res_out;
+  int64_t res_out_stride;
+  const void* norm_w;
+  float eps;
+  const void* w;
+  int64_t w_stride;
+  int n, k, batch;
+  void* y;
+  int64_t y_stride;
+};
+
+template <typename T, int B, int CH, bool NORM, bool SILU>
+__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvParams p) {
+  constexpr int E = 8;
+  constexpr int K = CH * 256;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ float s_part[kGemvWarps][B];
+  T* as = reinterpret_cast<T*>(smem_raw);  // [B][K] GEMV input
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+  // ---- input rows (NORM: residual add + RMSNorm) into shared memory
+  if constexpr (!NORM) {
+    for (int v = tid; v < B * K / E; v += kGemvThreads) {
+      const int b = v / (K / E), c = v % (K / E);
+      uint4 x = make_uint4(0u, 0u, 0u, 0u);
+      if (b < p.batch) x = ld16(static_cast<const T*>(p.x) + (int64_t)b * p.x_stride + c * E);
+      reinterpret_cast<uint4*>(as)[v] = x;
+    }
+  } else {
+    float ss[B];
+#pragma unroll
+    for (int b = 0; b < B; ++b) ss[b] = 0.f;
+    for (int v = tid; v < B * K / E; v += kGemvThreads) {
+      const int b = v / (K / E), c = v % (K / E);
+      float h[E];
+#pragma unroll
+      for (int e = 0; e < E; ++e) h[e] = 0.f;
+      if (b < p.batch) {
+        unpack16<T>(ld16(static_cast<const T*>(p.x) + (int64_t)b * p.x_stride + c * E), h);
+        if (p.res) {
+          float r[E];
+          unpack16<T>(ld16(static_cast<const T*>(p.res) + (int64_t)b * p.res_stride + c * E), r);
+#pragma unroll
+          for (int e = 0; e < E; ++e) h[e] = round_to<T>(__fadd_rn(h[e], r[e]));
+          if (p.res_out && blockIdx.x == 0)
+            st16(static_cast<T*>(p.res_out) + (int64_t)b * p.res_out_stride + c * E, pack16<T>(h));
+        }
+      }
+      float s = 0.f;
+#pragma unroll
+      for (int e = 0; e < E; ++e) s = fmaf(h[e], h[e], s);
+      // b is uniform over runs of K/E consecutive v, so accumulate per b
+#pragma unroll
+      for (int bb = 0; bb < B; ++bb)
+        if (bb == b) ss[bb] += s;
+      reinterpret_cast<uint4*>(as)[v] = pack16<T>(h);  // h (rounded), normalised below
+    }
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      float s = ss[b];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      if (lane == 0) s_part[warp][b] = s;
+    }
+    __syncthreads();
+    for (int v = tid; v < B * K / E; v += kGemvThreads) {
+      const int b = v / (K / E), c = v % (K / E);
+      float tot = 0.f;
+#pragma unroll
+      for (int w = 0; w < kGemvWarps; ++w) tot += s_part[w][b];
+      const float rr = 1.0f / sqrtf(tot / (float)K + p.eps);
+      float h[E], wf[E];
+      unpack16<T>(reinterpret_cast<const uint4*>(as)[v], h);
+      unpack16<T>(ld16_ro(static_cast<const T*>(p.norm_w) + c * E), wf);
+#pragma unroll
+      for (int e = 0; e < E; ++e) h[e] = __fmul_rn(__fmul_rn(h[e], rr), wf[e]);
+      reinterpret_cast<uint4*>(as)[v] = pack16<T>(h);
+    }
+  }
+  __syncthreads();
+
+  // ---- one warp per output row (SILU: per gate/up pair)
+  const T* W = static_cast<const T*>(p.w);
+  constexpr int NR = SILU ? 2 : 1;
+  for (int r = blockIdx.x * kGemvWarps + warp; r < p.n; r += gridDim.x * kGemvWarps) {
+    uint4 wv[NR][CH];
+#pragma unroll
+    for (int q = 0; q < NR; ++q)
+#pragma unroll
+      for (int c = 0; c < CH; ++c)
+        wv[q][c] = ld16_stream(W + (int64_t)(r + q * p.n) * p.w_stride + c * 256 + lane * E);
+    float acc[NR][B];
+#pragma unroll
+    for (int q = 0; q < NR; ++q)
+#pragma unroll
+      for (int b = 0; b < B; ++b) acc[q][b] = 0.f;
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      float wf[NR][E];
+#pragma unroll
+      for (int q = 0; q < NR; ++q) unpack16<T>(wv[q][c], wf[q]);
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        float af[E];
+        unpack16<T>(reinterpret_cast<const uint4*>(as + b * K + c * 256)[lane], af);
+#pragma unroll
+        for (int q = 0; q < NR; ++q)
+#pragma unroll
+          for (int e = 0; e < E; ++e) acc[q][b] = fmaf(wf[q][e], af[e], acc[q][b]);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < NR; ++q)
+#pragma unroll
+      for (int b = 0; b < B; ++b)
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc[q][b] += __shfl_xor_sync(0xffffffffu, acc[q][b], o);
+    // lane b stores stream b
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      if (lane == b && b < p.batch) {
+        float v;
+        if constexpr (SILU)
+          v = silu_mul_f(round_to<T>(acc[0][b]), round_to<T>(acc[1][b]));
+        else
+          v = acc[0][b];
+        static_cast<T*>(p.y)[(int64_t)b * p.y_stride + r] = Elem<T>::from_f(v);
+      }
+    }
+  }
+}
+
+template <typename T, int B, int CH>
+int launch_gemv_bk(const GemvParams& prm, bool norm, bool silu, cudaStream_t s) {
+  const size_t smem = (size_t)B * CH * 256 * sizeof(T);
+  const int want = (prm.n + kGemvWarps - 1) / kGemvWarps;
+  const int grid = want < 4096 ? want : 4096;
+  auto go = [&](auto kern) -> int {
+    if (smem > 48 * 1024) {
+      const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return (int)e;
+    }
+    kern<<<grid, kGemvThreads, smem, s>>>(prm);
+    return launch_status();
+  };
+  if (norm) return silu ? go(gemv_kernel<T, B, CH, true, true>) : go(gemv_kernel<T, B, CH, true, false>);
+  return silu ? go(gemv_kernel<T, B, CH, false, true>) : go(gemv_kernel<T, B, CH, false, false>);
+}
+
+template <typename T, int B>
+int launch_gemv_b(const GemvParams& prm, bool norm, bool silu, cudaStream_t s) {
+  switch (prm.k) {
+    case 1024: return launch_gemv_bk<T, B, 4>(prm, norm, silu, s);
+    case 4608: return launch_gemv_bk<T, B, 18>(prm, norm, silu, s);
+    default: return KANI_ERR_UNSUPPORTED;
+  }
+}
+
+template <typename T>
+int launch_gemv(const GemvParams& prm, bool norm, bool silu, cudaStream_t s) {
+  if (prm.batch <= 1) return launch_gemv_b<T, 1>(prm, norm, silu, s);
+  if (prm.batch <= 2) return launch_gemv_b<T, 2>(prm, norm, silu, s);
+  if (prm.batch <= 4) return launch_gemv_b<T, 4>(prm, norm, silu, s);
+  return launch_gemv_b<T, 8>(prm, norm, silu, s);
+}
+
+}  // namespace
+}  // namespace kani
+
+extern "C" int kani_gemv(int32_t dtype, const void* x, int64_t x_row_stride, const void* residual,
+                         int64_t residual_row_stride, void* residual_out, int64_t residual_out_row_stride,
+                         const void* norm_weight, float eps, const void* weight, int64_t weight_row_stride,
+                         int32_t n_out, int32_t k, int64_t batch, int32_t silu_pairs, void* y, int64_t y_row_stride,
+                         void* stream) {
+  if (batch < 0 || n_out < 0 || k < 0) return KANI_ERR_INVALID_ARG;
+  if (batch == 0 || n_out == 0) return KANI_OK;
+  if (!x || !weight || !y) return KANI_ERR_INVALID_ARG;
+  if ((residual || residual_out) && !norm_weight) return KANI_ERR_INVALID_ARG;  // the add belongs to the norm
+  if (residual_out && (residual_out == residual || residual_out == x)) return KANI_ERR_INVALID_ARG;
+  if (batch > kani::kGemvMaxB) return KANI_ERR_UNSUPPORTED;
+  if (dtype != KANI_DTYPE_BF16 && dtype != KANI_DTYPE_F16)
+    return dtype == KANI_DTYPE_F32 ? KANI_ERR_UNSUPPORTED : KANI_ERR_DTYPE;
+  if (weight_row_stride < k || (batch > 1 && (x_row_stride < k || y_row_stride < n_out)) ||
+      (residual && batch > 1 && residual_row_stride < k) || (residual_out && batch > 1 && residual_out_row_stride < k))
+    return KANI_ERR_INVALID_ARG;
+  if (!kani::aligned16(x) || !kani::aligned16(weight) || x_row_stride % 8 != 0 || weight_row_stride % 8 != 0 ||
+      (residual && (!kani::aligned16(residual) || residual_row_stride % 8 != 0)) ||
+      (residual_out && (!kani::aligned16(residual_out) || residual_out_row_stride % 8 != 0)) ||
+      (norm_weight && !kani::aligned16(norm_weight)))
+    return KANI_ERR_UNSUPPORTED;
+  kani::GemvParams prm{x, x_row_stride, residual, residual_row_stride, residual_out, residual_out_row_stride,
+                       norm_weight, eps, weight, weight_row_stride, n_out, k, (int)batch, y, y_row_stride};
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool norm = norm_weight != nullptr, silu = silu_pairs != 0;
+  if (dtype == KANI_DTYPE_BF16) return kani::launch_gemv<__nv_bfloat16>(prm, norm, silu, s);
+  return kani::launch_gemv<__half>(prm, norm, silu, s);
+}

@@ -17,18 +17,6 @@
 namespace kani {
 namespace {
 
-__device__ __forceinline__ float silu_mul_f(float g, float u) {
-  // (g * sigmoid(g)) * u.  sigmoid from t = e^-|g| in (0, 1]: g / (1 + e^-g)
-  // is 1/(1+t) for g >= 0 and t/(1+t) for g < 0, so the divisor stays in
-  // [1, 2], where the fast divide is accurate.  Below |g| ~ 87 the fast
-  // exponential flushes to zero while e^g is still representable, so that
-  // (rare) case takes the full-range expf.
-  const float t = __expf(-fabsf(g));
-  float sig = __fdividef(g >= 0.f ? 1.0f : t, 1.0f + t);
-  if (t == 0.f && g < 0.f) sig = expf(g);
-  return __fmul_rn(__fmul_rn(g, sig), u);
-}
-
 template <typename T, int RY>
 __global__ void __launch_bounds__(256)
 silu_mul_vec_kernel(const T* __restrict__ gu, int64_t in_stride, T* __restrict__ y,

@@ -19,9 +19,11 @@
 * the gated short-conv step between in_proj and out_proj is one
   ``short_conv_step`` launch (optimized_decode.py:256-277);
 * greedy steps of up to 8 streams end in one ``head_argmax`` launch (the
-  reduced head GEMV, the argmax and the reduced-to-full map).
+  reduced head GEMV, the argmax and the reduced-to-full map);
+* up to 8 streams, every projection is a ``gemv`` launch that folds in the
+  residual add + RMSNorm before it and the SiLU·mul after the gate/up GEMV.
 
-The GEMVs are cuBLAS calls; prefill attention is PyTorch SDPA.
+Beyond 8 streams the GEMMs are cuBLAS calls; prefill attention is PyTorch SDPA.
 
 ``DecodeEngine`` adds batched prefill (the same kernels at T tokens per
 stream, causal SDPA, causal depthwise conv) and a CUDA-graph decode loop
@@ -40,7 +42,7 @@ import torch.nn.functional as F
 
 from . import _lib
 from .fused_kernels import (decode_attention, fused_add_rms_norm, fused_rms_norm, fused_rope_kv_write,
-                            fused_silu_mul, head_argmax, sample_tokens, short_conv_step)
+                            fused_silu_mul, gemv, head_argmax, sample_tokens, short_conv_step)
 from .model import LFM2Config
 from .positions import learnable_inv_freq
 from .sampling import SamplingParams, seen_bitmap
@@ -108,6 +110,10 @@ class FusedDecoder:
         # cross-CTA argmax scratch of the fused greedy head (zero between launches)
         fits = batch <= 8 and h in (512, 1024, 2048)
         self.head_scratch = torch.zeros(batch + 1, dtype=torch.long, device=dev) if fits else None
+        # small batches take the fused-GEMV layer path (K of every GEMV: H or the FFN size)
+        self.small_batch = (batch <= 8 and h == 1024 and cfg.intermediate_size in (1024, 4608)
+                            and self.q_dim == h)
+        self.res_buf = [torch.empty(batch, 1, h, dtype=self.dtype, device=dev) for _ in range(2)]
 
     # ------------------------------------------------------------ decode
     fused_greedy_head = True   # greedy steps may use the fused head + argmax (batch <= 8)
@@ -136,6 +142,56 @@ class FusedDecoder:
 
     def _final_hidden(self, input_ids, positions, slots, kv_len) -> torch.Tensor:
         """The decode layers and the final norm: [B, 1, H]."""
+        if self.small_batch:
+            return self._final_hidden_small(input_ids, positions, slots, kv_len)
+        return self._final_hidden_large(input_ids, positions, slots, kv_len)
+
+    def _final_hidden_small(self, input_ids, positions, slots, kv_len) -> torch.Tensor:
+        """Up to 8 streams: every F.linear is a ``gemv`` launch that also applies the
+        residual add + RMSNorm before it and, for gate/up, the SiLU·mul after it,
+        so a layer is 5 launches (conv) or 6 (attention) instead of 8-9.  The
+        residual stream alternates between two static buffers (a launch reads one
+        and writes the other)."""
+        b, hq, hk, d = self.batch, self.hq, self.hk, self.d
+        hidden = F.embedding(input_ids, self.embed)              # [B, 1, H] residual stream
+        delta = None
+        flip = 0
+
+        def normed_gemv(weight, norm_w, silu=False):
+            # GEMV of RMSNorm(hidden + delta); the sum becomes the new residual stream
+            nonlocal hidden, flip
+            if delta is None:
+                return gemv(hidden, weight, norm_weight=norm_w, eps=self.eps, silu_pairs=silu)
+            out_res = self.res_buf[flip]
+            flip ^= 1
+            y = gemv(delta, weight, norm_weight=norm_w, residual=hidden, residual_out=out_res, eps=self.eps,
+                     silu_pairs=silu)
+            hidden = out_res
+            return y
+
+        for i, L in enumerate(self.layers):
+            if L["attn"]:
+                qkv = normed_gemv(L["qkv"], L["op_norm"])       # [B, 1, (Hq+2Hk)D]
+                q, k, v = qkv.split([self.q_dim, self.kv_dim, self.kv_dim], dim=-1)
+                q_rot = fused_rope_kv_write(
+                    q.view(b, 1, hq, d), k.view(b, 1, hk, d), v.view(b, 1, hk, d), L["inv_freq"], positions,
+                    self.k_cache[i], self.v_cache[i], slots, frame_table=self.frame_table,
+                    tokens_per_frame=self.cfg.tokens_per_frame, q_norm_w=L["q_norm"], k_norm_w=L["k_norm"],
+                    eps=self.eps, err_flag=self.err_flag)
+                attn = decode_attention(q_rot, self.k_cache[i], self.v_cache[i], kv_len, self.scale,
+                                        err_flag=self.err_flag)
+                delta = gemv(attn.view(b, 1, self.q_dim), L["o"])
+            else:
+                bcx = normed_gemv(L["in_proj"], L["op_norm"])
+                y = short_conv_step(bcx, self.conv_state[i], L["conv_w"])
+                delta = gemv(y, L["out_proj"])
+            act = normed_gemv(L["gate_up"], L["ffn_norm"], silu=True)
+            delta = gemv(act, L["down"])
+        normed, _ = fused_add_rms_norm(delta, hidden, self.final_norm, self.eps)
+        return normed
+
+    def _final_hidden_large(self, input_ids, positions, slots, kv_len) -> torch.Tensor:
+        """Many streams: cuBLAS GEMMs with the fused norm / activation launches between them."""
         b, hq, hk, d = self.batch, self.hq, self.hk, self.d
         hidden = F.embedding(input_ids, self.embed)              # [B, 1, H] residual stream
         delta = None

@@ -362,3 +362,23 @@ def codec_codes_ref(tokens: torch.Tensor, eos_token: int, audio_tokens_start: in
         frames[b] = nf
         status[b] = st
     return codes, frames, status
+
+
+def gemv_ref(x: torch.Tensor, weight: torch.Tensor, norm_weight: torch.Tensor | None = None,
+             residual: torch.Tensor | None = None, eps: float = 1e-5, silu_pairs: bool = False):
+    """The decode step's F.linear with its neighbours (optimized_decode.py:175-289):
+    optional residual add + RMSNorm before it (``add_rms_norm_ref`` /
+    ``rms_norm_ref``), the product as a float64 dot rounded once (F.linear's
+    output), optional SiLU·mul of the gate / up halves after it
+    (``silu_mul_ref``).  Returns (y, h) with h the residual-stream sum (or None)."""
+    h = None
+    a = x
+    if norm_weight is not None:
+        if residual is not None:
+            a, h = add_rms_norm_ref(x, residual, norm_weight, eps)
+        else:
+            a = rms_norm_ref(x, norm_weight, eps)
+    y = (a.double() @ weight.double().T).to(x.dtype)
+    if silu_pairs:
+        y = silu_mul_ref(y)
+    return y, h

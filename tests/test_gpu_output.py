@@ -133,3 +133,37 @@ def test_codec_codes_batch_vs_oracle():
     for x, y in zip(got, ref):
         assert torch.equal(x.cpu(), y)
     assert [int(s) for s in ref[2]] == [0, 2, 1, 4, 2, 4]
+
+
+@pytest.mark.parametrize("b", [1, 3, 8])
+@pytest.mark.parametrize("mode", ["plain_1024", "plain_4608", "norm", "add_norm", "add_norm_silu"])
+def test_gemv_vs_oracle(b, mode):
+    """Fused decode GEMV: the input row (or its residual add + RMSNorm) into smem,
+    fp32 dot products, optional SiLU·mul.  Outputs within 1 ULP of the oracle or
+    the cancellation bound; the residual sum bit-exact."""
+    k = 4608 if mode == "plain_4608" else 1024
+    n = {"plain_1024": 2048, "plain_4608": 1024, "norm": 3072, "add_norm": 1024, "add_norm_silu": 4608}[mode]
+    silu = mode == "add_norm_silu"
+    x = rnd((b, 1, k), 1500 + b)
+    w = rnd((2 * n if silu else n, k), 1501, std=0.03)
+    nw = (1.0 + 0.1 * rnd((k,), 1502, torch.float32)).to(torch.bfloat16) if mode != "plain_1024" and \
+        mode != "plain_4608" else None
+    res = rnd((b, 1, k), 1503) if mode.startswith("add") else None
+    h_out = torch.empty(b, 1, k, dtype=torch.bfloat16, device=DEV) if res is not None else None
+    y = K.gemv(x.to(DEV), w.to(DEV), norm_weight=nw.to(DEV) if nw is not None else None,
+               residual=res.to(DEV) if res is not None else None, residual_out=h_out, silu_pairs=silu)
+    ref, h_ref = O.gemv_ref(x, w, nw, res, 1e-5, silu)
+    assert y.shape == (b, 1, n)
+    d = O.ulp_distance(y.cpu(), ref)
+    a_ref = x if nw is None else (O.add_rms_norm_ref(x, res, nw, 1e-5)[0] if res is not None
+                                 else O.rms_norm_ref(x, nw, 1e-5))
+    mag = (a_ref.double().abs().reshape(b, k) @ w.double().abs().T)
+    if silu:   # the activation multiplies two rounded products: allow 2 ULP there
+        ok = d <= 2
+    else:
+        err = (y.cpu().double() - ref.double()).abs().reshape(b, n)
+        ok = (d.reshape(b, n) <= 1) | (err <= mag * 2.0 ** -16)
+    assert bool(ok.all()), f"max ULP {int(d.max())}"
+    assert float((d == 0).float().mean()) >= 0.97
+    if h_out is not None:
+        assert torch.equal(h_out.cpu(), h_ref)

@@ -103,6 +103,12 @@ def test_abi_rejects_bad_arguments_without_launching():
     assert lib.kani_head_argmax(0, fake, 1024, 1, 1024, fake, 1024, 100, n, n, 0, fake, fake, 1, n) == -3
     assert lib.kani_head_argmax(1, fake, 1000, 1, 1000, fake, 1000, 100, n, n, 0, fake, fake, 1, n) == -1
     assert lib.kani_head_argmax(1, fake, 1024, 1, 1024, fake, 1024, 100, n, n, 0, n, fake, 1, n) == -1
+    # fused GEMV: a residual without a norm, residual_out aliasing the residual, batch above 8, K unsupported
+    assert lib.kani_gemv(1, fake, 1024, fake, 1024, n, 0, n, 1e-5, fake, 1024, 64, 1024, 1, 0, fake, 64, n) == -1
+    assert lib.kani_gemv(1, fake, 1024, fake, 1024, fake, 1024, fake, 1e-5, fake, 1024, 64, 1024, 1, 0, fake, 64,
+                         n) == -1
+    assert lib.kani_gemv(1, fake, 1024, n, 0, n, 0, n, 1e-5, fake, 1024, 64, 1024, 9, 0, fake, 64, n) == -3
+    assert lib.kani_gemv(1, fake, 2048, n, 0, n, 0, n, 1e-5, fake, 2048, 64, 2048, 1, 0, fake, 64, n) == -3
     # codec codes: too few frames for the tokens, missing outputs
     assert lib.kani_codec_codes(fake, 100, 2, 100, 64402, 64410, 4032, fake, 24, fake, fake, n) == -1
     assert lib.kani_codec_codes(fake, 100, 2, 100, 64402, 64410, 4032, n, 25, fake, fake, n) == -1

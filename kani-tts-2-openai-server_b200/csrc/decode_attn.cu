@@ -65,6 +65,7 @@ __device__ __forceinline__ float merge_weight(float m, float mnew) {
 template <typename T, int G, int D>
 __global__ void __cluster_dims__(kClusterCTAs, 1, 1) __launch_bounds__(kAttnThreads)
 decode_attn_reg_kernel(AttnParams p) {
+  griddep_launch_dependents();  // a dependent GEMV may start streaming its weights
   constexpr int DL = D / 4;           // dims per lane
   constexpr int VE = VecN<T>::value;  // elements per 16-byte vector
   constexpr int NV = DL / VE;         // 16-byte vectors per lane per row
@@ -269,6 +270,7 @@ __device__ __forceinline__ bool attn_wait_bounded(uint32_t bar, uint32_t parity)
 template <typename T, int G, int D>
 __global__ void __launch_bounds__(kAttnThreads)
 decode_attn_kernel(AttnParams p) {
+  griddep_launch_dependents();  // a dependent GEMV may start streaming its weights
   constexpr int DL = D / 4;
   constexpr int VE = VecN<T>::value;
   constexpr int NV = DL / VE;

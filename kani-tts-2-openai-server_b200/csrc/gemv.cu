@@ -22,7 +22,10 @@
 // Layout: 256-thread CTAs; one warp per output row (SILU: per gate/up pair)
 // streams the row with 16-byte evict-first loads (K / 256 loads in flight per
 // lane); the B input rows sit in shared memory.  Every CTA recomputes the
-// norm (a few KB from L2).
+// norm (a few KB from L2).  Launches use programmatic dependent launch: a
+// warp issues its first row's weight loads before griddepcontrol.wait, so the
+// weight stream of one launch overlaps the tail of the launch before it; all
+// reads of activations and all writes come after the wait.
 #include "common.cuh"
 
 namespace kani {
@@ -57,6 +60,24 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvParams p) {
   T* as = reinterpret_cast<T*>(smem_raw);  // [B][K] GEMV input
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
+  // ---- the weights do not depend on earlier launches: start this warp's
+  //      first row streaming before waiting for them (programmatic dependent
+  //      launch), then let the next launch start its own weight stream
+  const T* W = static_cast<const T*>(p.w);
+  constexpr int NR = SILU ? 2 : 1;
+  int r = blockIdx.x * kGemvWarps + warp;
+  uint4 wv[NR][CH];
+  auto load_row = [&](int row) {
+#pragma unroll
+    for (int q = 0; q < NR; ++q)
+#pragma unroll
+      for (int c = 0; c < CH; ++c)
+        wv[q][c] = ld16_stream(W + (int64_t)(row + q * p.n) * p.w_stride + c * 256 + lane * E);
+  };
+  if (r < p.n) load_row(r);
+  griddep_launch_dependents();
+  griddep_wait();
+
   // ---- input rows (NORM: residual add + RMSNorm) into shared memory
   if constexpr (!NORM) {
     for (int v = tid; v < B * K / E; v += kGemvThreads) {
@@ -77,10 +98,10 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvParams p) {
       if (b < p.batch) {
         unpack16<T>(ld16(static_cast<const T*>(p.x) + (int64_t)b * p.x_stride + c * E), h);
         if (p.res) {
-          float r[E];
-          unpack16<T>(ld16(static_cast<const T*>(p.res) + (int64_t)b * p.res_stride + c * E), r);
+          float rv[E];
+          unpack16<T>(ld16(static_cast<const T*>(p.res) + (int64_t)b * p.res_stride + c * E), rv);
 #pragma unroll
-          for (int e = 0; e < E; ++e) h[e] = round_to<T>(__fadd_rn(h[e], r[e]));
+          for (int e = 0; e < E; ++e) h[e] = round_to<T>(__fadd_rn(h[e], rv[e]));
           if (p.res_out && blockIdx.x == 0)
             st16(static_cast<T*>(p.res_out) + (int64_t)b * p.res_out_stride + c * E, pack16<T>(h));
         }
@@ -118,16 +139,10 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvParams p) {
   }
   __syncthreads();
 
-  // ---- one warp per output row (SILU: per gate/up pair)
-  const T* W = static_cast<const T*>(p.w);
-  constexpr int NR = SILU ? 2 : 1;
-  for (int r = blockIdx.x * kGemvWarps + warp; r < p.n; r += gridDim.x * kGemvWarps) {
-    uint4 wv[NR][CH];
-#pragma unroll
-    for (int q = 0; q < NR; ++q)
-#pragma unroll
-      for (int c = 0; c < CH; ++c)
-        wv[q][c] = ld16_stream(W + (int64_t)(r + q * p.n) * p.w_stride + c * 256 + lane * E);
+  // ---- one warp per output row (SILU: per gate/up pair); row r's weights
+  //      are already in flight
+  for (; r < p.n; r += gridDim.x * kGemvWarps) {
+    if (r != blockIdx.x * kGemvWarps + warp) load_row(r);
     float acc[NR][B];
 #pragma unroll
     for (int q = 0; q < NR; ++q)
@@ -179,8 +194,9 @@ int launch_gemv_bk(const GemvParams& prm, bool norm, bool silu, cudaStream_t s) 
       const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e != cudaSuccess) return (int)e;
     }
-    kern<<<grid, kGemvThreads, smem, s>>>(prm);
-    return launch_status();
+    const cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kGemvThreads), smem, s, prm);
+    note_launch();
+    return e == cudaSuccess ? KANI_OK : (int)e;
   };
   if (norm) return silu ? go(gemv_kernel<T, B, CH, true, true>) : go(gemv_kernel<T, B, CH, true, false>);
   return silu ? go(gemv_kernel<T, B, CH, false, true>) : go(gemv_kernel<T, B, CH, false, false>);

@@ -27,6 +27,7 @@ short_conv_kernel(const T* __restrict__ bcx, int64_t bcx_stride, T* __restrict__
                   int64_t state_stride, const T* __restrict__ w, T* __restrict__ y, int64_t y_stride,
                   int64_t batch, int hidden) {
   constexpr int E = VecN<T>::value;
+  griddep_launch_dependents();  // a dependent GEMV may start streaming its weights
   const int groups = hidden / E;
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= batch * groups) return;

@@ -300,6 +300,37 @@ KANI_API int kani_gemv(int32_t dtype, const void* x, int64_t x_row_stride, const
                      int64_t y_row_stride, void* stream);
 
 /*
+ * kani_gemv with the LFM2 gated short-conv decode step as its epilogue: the
+ * in_proj GEMV (weight [3 * hidden, k]: B rows, C rows, x rows; optional
+ * residual add + RMSNorm prologue as in kani_gemv) followed, per channel c, by
+ * the step of kani_short_conv_step on conv_state[b, c, :] (updated in place) and
+ * conv_weight[c, :], writing y[b, c].  Replaces optimized_decode.py:255-277
+ * (in_proj through the conv) in one launch.  kernel_len must be 3; k = 1024.
+ */
+KANI_API int kani_gemv_short_conv(int32_t dtype, const void* x, int64_t x_row_stride, const void* residual,
+                     int64_t residual_row_stride, void* residual_out, int64_t residual_out_row_stride,
+                     const void* norm_weight, float eps, const void* in_proj_weight,
+                     int64_t weight_row_stride, int32_t hidden, int32_t k, int64_t batch,
+                     void* conv_state, int64_t conv_state_batch_stride, const void* conv_weight,
+                     int32_t kernel_len, void* y, int64_t y_row_stride, void* stream);
+
+/*
+ * Per-token decode-loop bookkeeping, one launch (replaces the host writes of
+ * kani_tts/inference_engine.py:615-619, 638-643, 669).  With k = *step, for each
+ * stream b: generated[b, k] = input_ids[b] = next_token[b] (generated written
+ * only for k < gen_cols); positions[b] = base_pos[b] +
+ * floor((k + 1) / tokens_per_frame) * audio_step; slots[b] = base_slot[b] + k + 1;
+ * kv_len[b] = slots[b] + 1.  Then *step = k + 1 and, if rng_step is not NULL,
+ * *rng_step += 1.  All pointers are device int64 arrays ([batch], generated
+ * [batch, gen_cols] with a row stride; step and rng_step single values).
+ */
+KANI_API int kani_decode_advance(const int64_t* next_token, int64_t* input_ids, int64_t* generated,
+                     int64_t gen_row_stride, int64_t gen_cols, int64_t* step, int64_t* rng_step,
+                     const int64_t* base_pos, const int64_t* base_slot, int32_t tokens_per_frame,
+                     float audio_step, int64_t* positions, int64_t* slots, int64_t* kv_len,
+                     int64_t batch, void* stream);
+
+/*
  * Generated tokens -> NeMo codec codes for `batch` streams (replaces
  * NemoAudioPlayer.get_nano_codes, kani_tts/core.py:86-108):
  *   a stream's audio segment is its tokens before the first `eos_token`

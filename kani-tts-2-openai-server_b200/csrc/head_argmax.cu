@@ -10,7 +10,8 @@
 //     rounding to the storage type, as F.linear's bf16 output);
 //   * token[b] = index_map[first r with the largest logits[b, r]].
 // The weight rows stream from HBM once (16-byte loads, 4 rows per warp in
-// flight); the hidden rows are staged in shared memory.  Each CTA folds its
+// flight; the first ones are issued before the programmatic-launch wait, so
+// they overlap the kernel before); the hidden rows are staged in shared memory.  Each CTA folds its
 // maxima, packed as (order key << 32 | ~row), into a per-stream 64-bit
 // atomicMax in global scratch; the last CTA to finish (a counter after a
 // fence) writes the tokens and returns the scratch to zero, so the next launch
@@ -57,6 +58,22 @@ __global__ void __launch_bounds__(kHeadThreads) head_argmax_kernel(HeadParams p)
   T* hs = reinterpret_cast<T*>(smem_raw);  // [B][hidden]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int H = CH * 256;
+  const T* W = static_cast<const T*>(p.w);
+  const int gw = blockIdx.x * kHeadWarps + warp, nw = gridDim.x * kHeadWarps;
+
+  // the weights do not depend on earlier launches: the first rows stream in
+  // before the programmatic-launch wait, the hidden rows are read after it
+  uint4 wv[kHeadRows][CH];
+  auto load_rows = [&](int r0) {
+#pragma unroll
+    for (int q = 0; q < kHeadRows; ++q) {
+      const int r = min(r0 + q, p.rows - 1);
+#pragma unroll
+      for (int c = 0; c < CH; ++c) wv[q][c] = ld16_stream(W + (int64_t)r * p.w_stride + c * 256 + lane * E);
+    }
+  };
+  if (gw * kHeadRows < p.rows) load_rows(gw * kHeadRows);
+  griddep_wait();
 
   for (int v = tid; v < B * H / E; v += kHeadThreads) {
     const int b = v / (H / E), c = v % (H / E);
@@ -69,16 +86,8 @@ __global__ void __launch_bounds__(kHeadThreads) head_argmax_kernel(HeadParams p)
   unsigned long long best[B];
 #pragma unroll
   for (int b = 0; b < B; ++b) best[b] = 0ull;
-  const T* W = static_cast<const T*>(p.w);
-  const int gw = blockIdx.x * kHeadWarps + warp, nw = gridDim.x * kHeadWarps;
   for (int r0 = gw * kHeadRows; r0 < p.rows; r0 += nw * kHeadRows) {
-    uint4 wv[kHeadRows][CH];
-#pragma unroll
-    for (int q = 0; q < kHeadRows; ++q) {
-      const int r = min(r0 + q, p.rows - 1);
-#pragma unroll
-      for (int c = 0; c < CH; ++c) wv[q][c] = ld16_stream(W + (int64_t)r * p.w_stride + c * 256 + lane * E);
-    }
+    if (r0 != gw * kHeadRows) load_rows(r0);
     float acc[kHeadRows][B];
 #pragma unroll
     for (int q = 0; q < kHeadRows; ++q)
@@ -175,8 +184,9 @@ int launch_head_b(const HeadParams& prm, cudaStream_t s) {
       occ = 1;
     const int64_t want = (prm.rows + per_cta - 1) / per_cta, cap = (int64_t)sms[dev] * occ;
     const int grid = (int)(want < cap ? want : cap);
-    kern<<<grid, kHeadThreads, smem, s>>>(prm);
-    return launch_status();
+    const cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kHeadThreads), smem, s, prm);
+    note_launch();
+    return e == cudaSuccess ? KANI_OK : (int)e;
   };
   switch (ch) {
     case 2: return go(head_argmax_kernel<T, B, 2>);

@@ -47,6 +47,7 @@ __device__ __forceinline__ float rrms_of(float ss, int n, float eps) {
 template <typename T, typename W, int V, bool RES>
 __global__ void __launch_bounds__(128)
 norm_group_kernel(NormParams p, int log2g) {
+  griddep_launch_dependents();  // a dependent GEMV may start streaming its weights
   constexpr int E = VecN<T>::value;
   const int G = 1 << log2g;
   const int64_t gtid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -129,6 +130,7 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 template <typename T, typename W, int V, bool RES, int BT>
 __global__ void __launch_bounds__(BT)
 norm_block_kernel(NormParams p) {
+  griddep_launch_dependents();  // a dependent GEMV may start streaming its weights
   constexpr int E = VecN<T>::value;
   __shared__ float red[33];
   const int nvec = p.n / E;
@@ -184,6 +186,7 @@ norm_block_kernel(NormParams p) {
 template <typename T, typename W, bool RES>
 __global__ void __launch_bounds__(256)
 norm_generic_kernel(NormParams p) {
+  griddep_launch_dependents();  // a dependent GEMV may start streaming its weights
   __shared__ float red[33];
   for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
     const T* xr = static_cast<const T*>(p.x) + row * p.xs;

@@ -21,7 +21,8 @@ LIB_DIR = PKG_DIR / "_lib"
 LIB_PATH = LIB_DIR / "libkani_b200.so"
 
 SOURCES = ["capi.cu", "rms_norm.cu", "silu_mul.cu", "rope_kv.cu", "decode_attn.cu", "short_conv.cu",
-           "sampling.cu", "head_argmax.cu", "codec_codes.cu", "gemv.cu"]
+           "sampling.cu", "head_argmax.cu", "codec_codes.cu", "gemv.cu",
+           "decode_advance.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

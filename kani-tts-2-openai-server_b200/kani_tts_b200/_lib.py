@@ -72,6 +72,10 @@ _SIGNATURES = {
                                   _c_p, _c_p, _c_i64, _c_p, _c_i64, _c_p], ctypes.c_int),
     "kani_gemv": ([_c_i32, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_f32, _c_p, _c_i64,
                    _c_i32, _c_i32, _c_i64, _c_i32, _c_p, _c_i64, _c_p], ctypes.c_int),
+    "kani_gemv_short_conv": ([_c_i32, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_f32, _c_p, _c_i64,
+                              _c_i32, _c_i32, _c_i64, _c_p, _c_i64, _c_p, _c_i32, _c_p, _c_i64, _c_p], ctypes.c_int),
+    "kani_decode_advance": ([_c_p, _c_p, _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_i32, _c_f32,
+                             _c_p, _c_p, _c_p, _c_i64, _c_p], ctypes.c_int),
     "kani_codec_codes": ([_c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_p, _c_p,
                           _c_p], ctypes.c_int),
 }

@@ -41,8 +41,9 @@ import torch
 import torch.nn.functional as F
 
 from . import _lib
-from .fused_kernels import (decode_attention, fused_add_rms_norm, fused_rms_norm, fused_rope_kv_write,
-                            fused_silu_mul, gemv, head_argmax, sample_tokens, short_conv_step)
+from .fused_kernels import (decode_advance, decode_attention, fused_add_rms_norm, fused_rms_norm,
+                            fused_rope_kv_write, fused_silu_mul, gemv, gemv_short_conv, head_argmax,
+                            sample_tokens, short_conv_step)
 from .model import LFM2Config
 from .positions import learnable_inv_freq
 from .sampling import SamplingParams, seen_bitmap
@@ -112,7 +113,7 @@ class FusedDecoder:
         self.head_scratch = torch.zeros(batch + 1, dtype=torch.long, device=dev) if fits else None
         # small batches take the fused-GEMV layer path (K of every GEMV: H or the FFN size)
         self.small_batch = (batch <= 8 and h == 1024 and cfg.intermediate_size in (1024, 4608)
-                            and self.q_dim == h)
+                            and self.q_dim == h and cfg.conv_L_cache == 3)
         self.res_buf = [torch.empty(batch, 1, h, dtype=self.dtype, device=dev) for _ in range(2)]
 
     # ------------------------------------------------------------ decode
@@ -149,7 +150,8 @@ class FusedDecoder:
     def _final_hidden_small(self, input_ids, positions, slots, kv_len) -> torch.Tensor:
         """Up to 8 streams: every F.linear is a ``gemv`` launch that also applies the
         residual add + RMSNorm before it and, for gate/up, the SiLU·mul after it,
-        so a layer is 5 launches (conv) or 6 (attention) instead of 8-9.  The
+        and the in_proj GEMV also runs the short-conv step, so a layer is 4
+        launches (conv) or 6 (attention) instead of 8-9.  The
         residual stream alternates between two static buffers (a launch reads one
         and writes the other)."""
         b, hq, hk, d = self.batch, self.hq, self.hk, self.d
@@ -157,21 +159,20 @@ class FusedDecoder:
         delta = None
         flip = 0
 
-        def normed_gemv(weight, norm_w, silu=False):
-            # GEMV of RMSNorm(hidden + delta); the sum becomes the new residual stream
+        def normed(fn, *args, **kw):
+            # fn (a GEMV launch) on RMSNorm(hidden + delta); the sum becomes the new residual stream
             nonlocal hidden, flip
             if delta is None:
-                return gemv(hidden, weight, norm_weight=norm_w, eps=self.eps, silu_pairs=silu)
+                return fn(hidden, *args, eps=self.eps, **kw)
             out_res = self.res_buf[flip]
             flip ^= 1
-            y = gemv(delta, weight, norm_weight=norm_w, residual=hidden, residual_out=out_res, eps=self.eps,
-                     silu_pairs=silu)
+            y = fn(delta, *args, residual=hidden, residual_out=out_res, eps=self.eps, **kw)
             hidden = out_res
             return y
 
         for i, L in enumerate(self.layers):
             if L["attn"]:
-                qkv = normed_gemv(L["qkv"], L["op_norm"])       # [B, 1, (Hq+2Hk)D]
+                qkv = normed(gemv, L["qkv"], norm_weight=L["op_norm"])   # [B, 1, (Hq+2Hk)D]
                 q, k, v = qkv.split([self.q_dim, self.kv_dim, self.kv_dim], dim=-1)
                 q_rot = fused_rope_kv_write(
                     q.view(b, 1, hq, d), k.view(b, 1, hk, d), v.view(b, 1, hk, d), L["inv_freq"], positions,
@@ -182,10 +183,9 @@ class FusedDecoder:
                                         err_flag=self.err_flag)
                 delta = gemv(attn.view(b, 1, self.q_dim), L["o"])
             else:
-                bcx = normed_gemv(L["in_proj"], L["op_norm"])
-                y = short_conv_step(bcx, self.conv_state[i], L["conv_w"])
+                y = normed(gemv_short_conv, L["in_proj"], self.conv_state[i], L["conv_w"], norm_weight=L["op_norm"])
                 delta = gemv(y, L["out_proj"])
-            act = normed_gemv(L["gate_up"], L["ffn_norm"], silu=True)
+            act = normed(gemv, L["gate_up"], norm_weight=L["ffn_norm"], silu_pairs=True)
             delta = gemv(act, L["down"])
         normed, _ = fused_add_rms_norm(delta, hidden, self.final_norm, self.eps)
         return normed
@@ -329,21 +329,20 @@ class DecodeEngine:
             # the prompt is the initial repetition history (inference_engine.py:553-556)
             self.seen = seen_bitmap(input_ids, dec.head.shape[0], dec.full_to_reduced, device=dec.device)
         first = self._next_token(logits[:, -1])
+        self.rng_step.add_(1)
         self.input_ids.copy_(first.view(b, 1))
         self.mask.fill_(float("-inf"))
         self.mask[..., :t_eff] = 0.0
         self.base_pos.fill_(t_eff)        # decode step k: t_eff + (k // tpf) * audio_step
         self.base_slot.fill_(t_eff)       # decode step k writes slot t_eff + k
         self.step_idx.zero_()
+        self.positions.copy_(self.base_pos)      # step 0; decode_advance computes the later ones
+        self.slots.copy_(self.base_slot)
+        self.kv_len.copy_(self.base_slot + 1)
         self.generated = torch.zeros(b, max_new_tokens, dtype=torch.long, device=dec.device)
 
     def _step_body(self):
         cfg = self.dec.cfg
-        k = self.step_idx
-        self.positions.copy_(self.base_pos + (torch.div(k, cfg.tokens_per_frame, rounding_mode="floor")
-                                              * cfg.audio_step).long())
-        self.slots.copy_(self.base_slot + k)
-        self.kv_len.copy_(self.slots + 1)
         if self.keep_mask:
             self.mask.scatter_(3, self.slots.view(-1, 1, 1, 1), 0.0)
         if self.sampling is None and self.dec.fused_greedy_head and self.dec.head_scratch is not None:
@@ -352,9 +351,10 @@ class DecodeEngine:
         else:
             self.logits = self.dec.step(self.input_ids, self.positions, self.slots, self.kv_len, self.mask)
             nxt = self._next_token(self.logits[:, 0])
-        self.generated.index_copy_(1, k, nxt.view(-1, 1))
-        self.input_ids.copy_(nxt.view(-1, 1))
-        self.step_idx.add_(1)
+        # record and feed back the token, next step's position / slot / length, counters
+        decode_advance(nxt.view(-1), self.input_ids, self.generated, self.step_idx, self.base_pos, self.base_slot,
+                       self.positions, self.slots, self.kv_len, cfg.tokens_per_frame, cfg.audio_step,
+                       rng_step=self.rng_step if self.sampling is not None else None)
 
     def _next_token(self, logits: torch.Tensor) -> torch.Tensor:
         """[B] full token ids from reduced logits [B, V_red]: greedy, or one
@@ -365,7 +365,6 @@ class DecodeEngine:
         sample_tokens(logits, self.seen, temperature=sp.temperature, top_p=sp.top_p,
                       repetition_penalty=sp.repetition_penalty, top_k=sp.top_k,
                       index_map=self.dec.reduced_to_full, seed=sp.seed, step=self.rng_step, out=self.next_tok)
-        self.rng_step.add_(1)
         return self.next_tok
 
     def capture(self) -> None:
@@ -373,7 +372,8 @@ class DecodeEngine:
         dec = self.dec
         saved = ({i: c.clone() for i, c in dec.conv_state.items()}, self.input_ids.clone(), self.mask.clone(),
                  self.step_idx.clone(), self.rng_step.clone(),
-                 self.seen.clone() if self.seen is not None else None)
+                 self.seen.clone() if self.seen is not None else None,
+                 self.positions.clone(), self.slots.clone(), self.kv_len.clone())
         s = torch.cuda.Stream(device=dec.device)
         s.wait_stream(torch.cuda.current_stream(dec.device))
         with torch.cuda.stream(s):
@@ -391,6 +391,9 @@ class DecodeEngine:
         self.rng_step.copy_(saved[4])
         if saved[5] is not None:
             self.seen.copy_(saved[5])
+        self.positions.copy_(saved[6])
+        self.slots.copy_(saved[7])
+        self.kv_len.copy_(saved[8])
 
     def run(self, n_steps: int) -> None:
         for _ in range(n_steps):

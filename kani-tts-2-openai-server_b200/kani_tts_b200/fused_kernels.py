@@ -45,6 +45,8 @@ __all__ = [
     "head_argmax",
     "codec_codes",
     "gemv",
+    "gemv_short_conv",
+    "decode_advance",
 ]
 
 
@@ -566,6 +568,54 @@ def gemv(x: torch.Tensor, weight: torch.Tensor, *, norm_weight: torch.Tensor | N
     return out
 
 
+def gemv_short_conv(x: torch.Tensor, in_proj_weight: torch.Tensor, conv_state: torch.Tensor,
+                    conv_weight: torch.Tensor, *, norm_weight: torch.Tensor | None = None,
+                    residual: torch.Tensor | None = None, residual_out: torch.Tensor | None = None,
+                    eps: float = 1e-5, out: torch.Tensor | None = None) -> torch.Tensor:
+    """in_proj GEMV + the gated short-conv decode step in one launch
+    (optimized_decode.py:255-277), with the optional residual add + RMSNorm
+    prologue of ``gemv``.  in_proj_weight [3H, K]; conv_state [B, H, 3] (updated in
+    place); conv_weight [H, 3].  Returns y [B, H] (or [B, 1, H])."""
+    for t, w in ((x, "x"), (in_proj_weight, "in_proj_weight"), (conv_state, "conv_state"),
+                 (conv_weight, "conv_weight")):
+        require_cuda(t, w)
+    lib = load_library()
+    code = dtype_code(x, "x")
+    k = x.shape[-1]
+    if conv_state.dim() != 3 or conv_weight.dim() != 2:
+        raise ValueError("conv_state must be [batch, hidden, L] and conv_weight [hidden, L]")
+    bsz, h, lc = conv_state.shape
+    if in_proj_weight.shape != (3 * h, k) or tuple(conv_weight.shape) != (h, lc):
+        raise ValueError(f"in_proj_weight [{3 * h}, {k}] and conv_weight [{h}, {lc}] expected")
+    if not (in_proj_weight.dtype == conv_state.dtype == conv_weight.dtype == x.dtype):
+        raise TypeError("all tensors must share the input dtype")
+    if conv_state.stride(2) != 1 or conv_state.stride(1) != lc:
+        raise ValueError("conv_state must be contiguous per stream")
+    xv, b, xs = _rows_view(x, k)
+    if b != bsz:
+        raise ValueError("conv_state must have one row per stream")
+    rv, rs, ov, os_ = None, 0, None, 0
+    if residual is not None:
+        require_cuda(residual, "residual")
+        rv, _, rs = _rows_view(residual, k)
+    if residual_out is not None:
+        require_cuda(residual_out, "residual_out")
+        ov, _, os_ = _rows_view(residual_out, k)
+    if norm_weight is not None:
+        require_cuda(norm_weight, "norm_weight")
+        norm_weight = norm_weight.contiguous()
+    if out is None:
+        out = torch.empty(*x.shape[:-1], h, dtype=x.dtype, device=x.device)
+    ov2, _, ys = _rows_view(out, h)
+    check(lib.kani_gemv_short_conv(code, ptr(xv), xs, ptr(rv) if rv is not None else None, rs,
+                                   ptr(ov) if ov is not None else None, os_,
+                                   ptr(norm_weight) if norm_weight is not None else None, float(eps),
+                                   ptr(in_proj_weight.contiguous()), k, h, k, b, ptr(conv_state), conv_state.stride(0),
+                                   ptr(conv_weight.contiguous()), lc, ptr(out), ys, stream_ptr(x.device)),
+          "kani_gemv_short_conv")
+    return out
+
+
 def head_argmax(hidden: torch.Tensor, weight: torch.Tensor, index_map: torch.Tensor | None = None, *,
                 scratch: torch.Tensor | None = None, logits_out: torch.Tensor | None = None,
                 out: torch.Tensor | None = None) -> torch.Tensor:
@@ -650,6 +700,34 @@ def head_argmax_noalloc(hidden: torch.Tensor, weight: torch.Tensor, index_map: t
                                        out.stride(0) if b > 1 else 1, stream_ptr(hidden.device)),
           "kani_head_argmax_noalloc")
     return out
+
+
+def decode_advance(next_token: torch.Tensor, input_ids: torch.Tensor, generated: torch.Tensor,
+                   step: torch.Tensor, base_pos: torch.Tensor, base_slot: torch.Tensor, positions: torch.Tensor,
+                   slots: torch.Tensor, kv_len: torch.Tensor, tokens_per_frame: int = 4, audio_step: float = 1.0,
+                   rng_step: torch.Tensor | None = None) -> None:
+    """End-of-step bookkeeping of the decode loop in one launch
+    (inference_engine.py:615-619, 638-643, 669): record the token, feed it back,
+    compute the next step's position / slot / valid length, advance the step
+    counter (and the sampler's, if given).  All device int64 tensors; [B] except
+    ``generated`` [B, max_new] and the single-value counters."""
+    ts = [next_token, input_ids, generated, step, base_pos, base_slot, positions, slots, kv_len]
+    for t in ts + ([rng_step] if rng_step is not None else []):
+        require_cuda(t, "bookkeeping tensor")
+        if t.dtype != torch.int64:
+            raise ValueError("bookkeeping tensors must be int64")
+    b = next_token.numel()
+    for t in (input_ids, base_pos, base_slot, positions, slots, kv_len):
+        if t.numel() != b or not t.is_contiguous():
+            raise ValueError(f"per-stream tensors must be contiguous with {b} elements")
+    if generated.dim() != 2 or generated.shape[0] != b or generated.stride(1) != 1:
+        raise ValueError("generated must be [B, max_new] with unit column stride")
+    lib = load_library()
+    check(lib.kani_decode_advance(ptr(next_token.contiguous()), ptr(input_ids), ptr(generated), generated.stride(0),
+                                  generated.shape[1], ptr(step), ptr(rng_step) if rng_step is not None else None,
+                                  ptr(base_pos), ptr(base_slot), int(tokens_per_frame), float(audio_step),
+                                  ptr(positions), ptr(slots), ptr(kv_len), b, stream_ptr(next_token.device)),
+          "kani_decode_advance")
 
 
 def codec_codes(tokens: torch.Tensor, eos_token: int, audio_tokens_start: int, codebook_size: int = 4032):

@@ -167,3 +167,47 @@ def test_gemv_vs_oracle(b, mode):
     assert float((d == 0).float().mean()) >= 0.97
     if h_out is not None:
         assert torch.equal(h_out.cpu(), h_ref)
+
+
+@pytest.mark.parametrize("b", [1, 4])
+def test_gemv_short_conv_equals_gemv_then_conv(b):
+    """The conv epilogue computes each channel's B, C, x rows in one warp with the
+    accumulation order of the plain GEMV, so it is bit-identical to
+    gemv(in_proj) followed by short_conv_step, state update included."""
+    h = 1024
+    x = rnd((b, 1, h), 1600 + b).to(DEV)
+    res = rnd((b, 1, h), 1601).to(DEV)
+    nw = (1.0 + 0.1 * rnd((h,), 1602, torch.float32)).to(torch.bfloat16).to(DEV)
+    w = rnd((3 * h, h), 1603, std=0.03).to(DEV)
+    cw = rnd((h, 3), 1604, std=0.3).to(DEV)
+    st0 = rnd((b, h, 3), 1605).to(DEV)
+    ha, hb = torch.empty_like(x), torch.empty_like(x)
+    st_a, st_b = st0.clone(), st0.clone()
+    bcx = K.gemv(x, w, norm_weight=nw, residual=res, residual_out=ha)
+    ya = K.short_conv_step(bcx, st_a, cw)
+    yb = K.gemv_short_conv(x, w, st_b, cw, norm_weight=nw, residual=res, residual_out=hb)
+    torch.cuda.synchronize()
+    assert torch.equal(ya, yb)
+    assert torch.equal(st_a, st_b)
+    assert torch.equal(ha, hb)
+
+
+def test_decode_advance_matches_the_reference_schedule():
+    """Per-step bookkeeping against the reference loop's arithmetic
+    (inference_engine.py:615-619, 638-643, 669) over 9 steps, 3 streams."""
+    b, n, tpf = 3, 9, 4
+    base = torch.tensor([130, 7, 40], device=DEV)
+    gen = torch.zeros(b, n, dtype=torch.long, device=DEV)
+    ids = torch.zeros(b, 1, dtype=torch.long, device=DEV)
+    step = torch.zeros(1, dtype=torch.long, device=DEV)
+    rng = torch.full((1,), 5, dtype=torch.long, device=DEV)
+    pos, slots, kvl = base.clone(), base.clone(), base + 1
+    for k in range(n):
+        tok = torch.tensor([1000 + k, 2000 + k, 3000 + k], device=DEV)
+        K.decode_advance(tok, ids, gen, step, base, base, pos, slots, kvl, tpf, 1.0, rng_step=rng)
+        torch.cuda.synchronize()
+        assert torch.equal(ids.view(-1).cpu(), tok.cpu())
+        assert torch.equal(pos.cpu(), (base + (k + 1) // tpf).cpu())
+        assert torch.equal(slots.cpu(), (base + k + 1).cpu()) and torch.equal(kvl.cpu(), (base + k + 2).cpu())
+    assert int(step.item()) == n and int(rng.item()) == 5 + n
+    assert torch.equal(gen.cpu(), (torch.arange(n) + torch.tensor([[1000], [2000], [3000]])))

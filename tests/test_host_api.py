@@ -109,6 +109,10 @@ def test_abi_rejects_bad_arguments_without_launching():
                          n) == -1
     assert lib.kani_gemv(1, fake, 1024, n, 0, n, 0, n, 1e-5, fake, 1024, 64, 1024, 9, 0, fake, 64, n) == -3
     assert lib.kani_gemv(1, fake, 2048, n, 0, n, 0, n, 1e-5, fake, 2048, 64, 2048, 1, 0, fake, 64, n) == -3
+    # decode bookkeeping: tokens per frame below 1, missing step counter
+    assert lib.kani_decode_advance(fake, fake, fake, 10, 10, fake, n, fake, fake, 0, 1.0, fake, fake, fake, 2,
+                                   n) == -1
+    assert lib.kani_decode_advance(fake, fake, fake, 10, 10, n, n, fake, fake, 4, 1.0, fake, fake, fake, 2, n) == -1
     # codec codes: too few frames for the tokens, missing outputs
     assert lib.kani_codec_codes(fake, 100, 2, 100, 64402, 64410, 4032, fake, 24, fake, fake, n) == -1
     assert lib.kani_codec_codes(fake, 100, 2, 100, 64402, 64410, 4032, n, 25, fake, fake, n) == -1

@@ -194,7 +194,8 @@ def make_inputs(seed: int, t: int = T_TOK, device="cpu"):
     q = torch.randn(t, HQ, D, generator=g).to(torch.bfloat16)
     k = torch.randn(t, HK, D, generator=g).to(torch.bfloat16)
     v = torch.randn(t, HK, D, generator=g).to(torch.bfloat16)
-    table = (0.02 * torch.randn(TABLE_ROWS, D, generator=g)).to(torch.bfloat16)
+    rows = max(TABLE_ROWS, (t + TPF - 1) // TPF)   # every position has a frame row (T > 4096 too)
+    table = (0.02 * torch.randn(rows, D, generator=g)).to(torch.bfloat16)
     inv = P.learnable_inv_freq(D, 1e6, 0.0)
     pos = torch.arange(t, dtype=torch.long)
     s_len = max(2048, t)
@@ -409,8 +410,9 @@ def run_sweep(K, dev, peak: float) -> dict:
             y = torch.empty(t, 4608, dtype=torch.bfloat16, device=dev)
             return lambda: K.fused_silu_mul(x, out=y)
         measure(f"silu_mul_bf16_T{t}", rot_sets(mk, nbytes), nbytes, launches=100 if t >= 32768 else 400)
-    # RoPE + frame table + KV write (config 2 sweep), and the decode step with q/k norm
-    for t in (1, 64, 512, 4096):
+    # RoPE + frame table + KV write (config 2 sweep, plus large-T points beyond it),
+    # and the decode step with q/k norm
+    for t in (1, 64, 512, 4096, 16384, 32768):
         nbytes = t * BYTES_PER_TOKEN
         def mk(i, t=t):
             s = make_inputs(100 + i, t, dev)
@@ -420,7 +422,7 @@ def run_sweep(K, dev, peak: float) -> dict:
                 s["pos"].fill_(p)
                 s["slots"].fill_(p)
             return lambda: launch(K, s, qo)
-        measure(f"rope_kv_write_bf16_T{t}", rot_sets(mk, nbytes), nbytes)
+        measure(f"rope_kv_write_bf16_T{t}", rot_sets(mk, nbytes), nbytes, launches=100 if t >= 16384 else 400)
     nbytes = BYTES_PER_TOKEN - 128 + 256
     def mk_norm(i):
         s = make_inputs(200 + i, 1, dev)

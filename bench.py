@@ -816,6 +816,13 @@ def run_op(name: str, size: int, steps: int, warmup: int) -> dict:
         fn = (lambda: K.sample_tokens(lg, seen, temperature=0.5, top_p=0.85, repetition_penalty=1.2, seed=1,
                                       step=step, out=tok))
         nbytes = size * (v * 2 + seen.shape[1] * 4 + 8)
+    elif name == "gemv_gate_up":               # size = streams; add + RMSNorm + gate/up GEMV + SiLU·mul
+        from kani_tts_b200.fused_kernels import gemv
+        x, r = rn(size, 1, 1024), rn(size, 1, 1024)
+        nw, wt = rn(1024), rn(9216, 1024) * 0.03
+        h, y = torch.empty_like(x), torch.empty(size, 1, 4608, dtype=bf, device=dev)
+        fn = lambda: gemv(x, wt, norm_weight=nw, residual=r, residual_out=h, silu_pairs=True, out=y)  # noqa: E731
+        nbytes = 9216 * 1024 * 2 + size * 1024 * 2 * 3 + size * 4608 * 2
     elif name in ("head_argmax", "head_cublas"):  # size = streams; reduced head 15591 x 1024
         rows, h = 15591, 1024
         hid, wt = rn(size, h), rn(rows, h) * 0.05
@@ -877,7 +884,7 @@ def main():
     ap.add_argument("--decode-batch", type=int, default=1, help="streams for --decode-only")
     ap.add_argument("--op", default=None, help="profiling aid: run one fused op alone "
                     "(silu_mul, add_rms_norm, rope_kv_write, decode_attention, short_conv, sample, "
-                    "head_argmax, head_cublas)")
+                    "head_argmax, head_cublas, gemv_gate_up)")
     ap.add_argument("--size", type=int, default=4096, help="rows / tokens / streams for --op")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()

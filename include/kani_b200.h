@@ -331,6 +331,29 @@ KANI_API int kani_decode_advance(const int64_t* next_token, int64_t* input_ids, 
                      int64_t batch, void* stream);
 
 /*
+ * The QKV GEMV of a decode step (input residual add + RMSNorm prologue as in
+ * kani_gemv; weight [(Hq + 2 Hk) * 64, k], Q rows then K then V) fused with
+ * kani_rope_kv_write's per-head work, one CTA per head: q/k RMSNorm (q_norm_w /
+ * k_norm_w, both or neither), rotary angles inv_freq * positions[b], rotate-half,
+ * the frame-table term (frame_table may be NULL), Q into q_out [batch, Hq, 64]
+ * (batch / head strides), K and V into cache[b, h, slots[b], :].  Replaces
+ * optimized_decode.py:215-240 (QKV F.linear through the cache update) in one
+ * launch.  batch <= 4, k = 1024, head_dim = 64, norm_weight required.
+ */
+KANI_API int kani_gemv_rope_kv(int32_t dtype, const void* x, int64_t x_row_stride, const void* residual,
+                     int64_t residual_row_stride, void* residual_out, int64_t residual_out_row_stride,
+                     const void* norm_weight, float eps, const void* qkv_weight,
+                     int64_t weight_row_stride, int32_t k, int64_t batch, int32_t num_q_heads,
+                     int32_t num_kv_heads, int32_t head_dim, const float* inv_freq,
+                     const int64_t* positions, const void* q_norm_w, const void* k_norm_w,
+                     float head_eps, const void* frame_table, int64_t frame_rows,
+                     const int64_t* frame_pos, int32_t tokens_per_frame, void* q_out,
+                     int64_t q_out_batch_stride, int64_t q_out_head_stride, void* k_cache,
+                     void* v_cache, int64_t cache_batch_stride, int64_t cache_head_stride,
+                     int64_t cache_slot_stride, int64_t cache_len, const int64_t* slots,
+                     int32_t* err_flag, void* stream);
+
+/*
  * Generated tokens -> NeMo codec codes for `batch` streams (replaces
  * NemoAudioPlayer.get_nano_codes, kani_tts/core.py:86-108):
  *   a stream's audio segment is its tokens before the first `eos_token`

@@ -29,6 +29,7 @@
 // weight stream of one launch overlaps the tail of the launch before it; all
 // reads of activations and all writes come after the wait.
 #include "common.cuh"
+#include "rope_core.cuh"
 
 namespace kani {
 namespace {
@@ -58,36 +59,13 @@ struct GemvParams {
 
 constexpr int kConvL = 3;  // the LFM2 short-conv kernel length the fused epilogue serves
 
-// EPI: 0 = store, 1 = SiLU·mul of the gate / up rows r and n + r,
-//      2 = gated short-conv step of channel r over rows r (B), n + r (C), 2n + r (x)
-template <typename T, int B, int CH, bool NORM, int EPI>
-__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvParams p) {
+// The B GEMV input rows into shared memory (as, [B][K]); with NORM the
+// residual add (h written to res_out by CTA 0) and the RMSNorm.  Ends with a
+// barrier.
+template <typename T, int B, int K, bool NORM>
+__device__ __forceinline__ void stage_input(const GemvParams& p, T* as, float (*s_part)[B], int tid, int lane,
+                                            int warp) {
   constexpr int E = 8;
-  constexpr int K = CH * 256;
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  __shared__ float s_part[kGemvWarps][B];
-  T* as = reinterpret_cast<T*>(smem_raw);  // [B][K] GEMV input
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-
-  // ---- the weights do not depend on earlier launches: start this warp's
-  //      first row streaming before waiting for them (programmatic dependent
-  //      launch), then let the next launch start its own weight stream
-  const T* W = static_cast<const T*>(p.w);
-  constexpr int NR = EPI == 0 ? 1 : (EPI == 1 ? 2 : 3);
-  int r = blockIdx.x * kGemvWarps + warp;
-  uint4 wv[NR][CH];
-  auto load_row = [&](int row) {
-#pragma unroll
-    for (int q = 0; q < NR; ++q)
-#pragma unroll
-      for (int c = 0; c < CH; ++c)
-        wv[q][c] = ld16_stream(W + (int64_t)(row + q * p.n) * p.w_stride + c * 256 + lane * E);
-  };
-  if (r < p.n) load_row(r);
-  griddep_launch_dependents();
-  griddep_wait();
-
-  // ---- input rows (NORM: residual add + RMSNorm) into shared memory
   if constexpr (!NORM) {
     for (int v = tid; v < B * K / E; v += kGemvThreads) {
       const int b = v / (K / E), c = v % (K / E);
@@ -147,6 +125,39 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvParams p) {
     }
   }
   __syncthreads();
+
+}
+
+// EPI: 0 = store, 1 = SiLU·mul of the gate / up rows r and n + r,
+//      2 = gated short-conv step of channel r over rows r (B), n + r (C), 2n + r (x)
+template <typename T, int B, int CH, bool NORM, int EPI>
+__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvParams p) {
+  constexpr int E = 8;
+  constexpr int K = CH * 256;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ float s_part[kGemvWarps][B];
+  T* as = reinterpret_cast<T*>(smem_raw);  // [B][K] GEMV input
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+  // ---- the weights do not depend on earlier launches: start this warp's
+  //      first row streaming before waiting for them (programmatic dependent
+  //      launch), then let the next launch start its own weight stream
+  const T* W = static_cast<const T*>(p.w);
+  constexpr int NR = EPI == 0 ? 1 : (EPI == 1 ? 2 : 3);
+  int r = blockIdx.x * kGemvWarps + warp;
+  uint4 wv[NR][CH];
+  auto load_row = [&](int row) {
+#pragma unroll
+    for (int q = 0; q < NR; ++q)
+#pragma unroll
+      for (int c = 0; c < CH; ++c)
+        wv[q][c] = ld16_stream(W + (int64_t)(row + q * p.n) * p.w_stride + c * 256 + lane * E);
+  };
+  if (r < p.n) load_row(r);
+  griddep_launch_dependents();
+  griddep_wait();
+
+  stage_input<T, B, K, NORM>(p, as, s_part, tid, lane, warp);
 
   // ---- one warp per output row (SILU: per gate/up pair); row r's weights
   //      are already in flight
@@ -208,6 +219,156 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvParams p) {
         static_cast<T*>(p.y)[(int64_t)b * p.y_stride + r] = Elem<T>::from_f(v);
       }
     }
+  }
+}
+
+// ------------------------------------------------- QKV GEMV + RoPE + KV write
+// One CTA per head of the packed QKV projection ([Q heads | K heads | V heads],
+// D = 64 rows each): the 8 warps compute the head's 64 outputs for every
+// stream (rows in the accumulation order of gemv_kernel), round them as
+// F.linear stores them, and warp 0 finishes the head for each stream with the
+// code of the RoPE + KV-write kernels: q/k RMSNorm, the rotary angles of the
+// stream's position, rotate-half, the frame-table term, the store to q_out or
+// to the cache slot (V heads: the copy).  Replaces the QKV F.linear and
+// kani_rope_kv_write of the decode step (optimized_decode.py:215-240).
+struct RopeKvParams {
+  int hq, hk;
+  const float* inv_freq;
+  const int64_t* positions;  // [batch]
+  const void* qw;
+  const void* kw;
+  float eps;
+  const void* table;
+  int64_t table_rows;
+  const int64_t* frame_pos;  // [batch] or NULL (= positions)
+  int tpf, tpf_shift;
+  void* q_out;
+  int64_t qobs, qohs;
+  void* k_cache;
+  void* v_cache;
+  int64_t cbs, chs, css, clen;
+  const int64_t* slots;  // [batch]
+  int32_t* err;
+};
+
+constexpr int kRopeD = 64;  // head_dim the fused epilogue serves
+constexpr int kRopeRowsPerWarp = kRopeD / kGemvWarps;
+
+// NORM: the input RMSNorm prologue; QKN: the per-head q / k RMSNorm; TABLE: the frame term
+template <typename T, int B, int CH, bool NORM, bool QKN, bool TABLE>
+__global__ void __launch_bounds__(kGemvThreads) gemv_rope_kv_kernel(GemvParams p, RopeKvParams r) {
+  constexpr int E = 8;
+  constexpr int K = CH * 256;
+  constexpr int RB = 4;  // rows per batch of loads
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ float s_part[kGemvWarps][B];
+  __shared__ __align__(16) T s_head[B][kRopeD];
+  T* as = reinterpret_cast<T*>(smem_raw);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int head = blockIdx.x;
+  const T* W = static_cast<const T*>(p.w);
+  const int row0 = head * kRopeD + warp * kRopeRowsPerWarp;
+
+  uint4 wv[RB][CH];
+  auto load_rows = [&](int rb) {
+#pragma unroll
+    for (int q = 0; q < RB; ++q)
+#pragma unroll
+      for (int c = 0; c < CH; ++c)
+        wv[q][c] = ld16_stream(W + (int64_t)(row0 + rb + q) * p.w_stride + c * 256 + lane * E);
+  };
+  load_rows(0);
+  griddep_launch_dependents();
+  griddep_wait();
+  stage_input<T, B, K, NORM>(p, as, s_part, tid, lane, warp);
+
+#pragma unroll
+  for (int rb = 0; rb < kRopeRowsPerWarp; rb += RB) {
+    if (rb) load_rows(rb);
+    float acc[RB][B];
+#pragma unroll
+    for (int q = 0; q < RB; ++q)
+#pragma unroll
+      for (int b = 0; b < B; ++b) acc[q][b] = 0.f;
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      float wf[RB][E];
+#pragma unroll
+      for (int q = 0; q < RB; ++q) unpack16<T>(wv[q][c], wf[q]);
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        float af[E];
+        unpack16<T>(reinterpret_cast<const uint4*>(as + b * K + c * 256)[lane], af);
+#pragma unroll
+        for (int q = 0; q < RB; ++q)
+#pragma unroll
+          for (int e = 0; e < E; ++e) acc[q][b] = fmaf(wf[q][e], af[e], acc[q][b]);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < RB; ++q)
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc[q][b] += __shfl_xor_sync(0xffffffffu, acc[q][b], o);
+        if (lane == 0) s_head[b][warp * kRopeRowsPerWarp + rb + q] = Elem<T>::from_f(acc[q][b]);
+      }
+  }
+  __syncthreads();
+  if (warp != 0) return;
+
+  // warp 0: lanes 0..3 carry the head's chunk pairs (lo, hi), the other lanes
+  // help with the sin/cos; one stream after another
+  constexpr int LOG2L = 2;  // (D/2)/E = 4 lanes per head
+  const int jj = lane & 3;
+  const bool mine = lane < 4;
+  const int lo = jj * E, hi = kRopeD / 2 + jj * E;
+  const bool is_q = head < r.hq, is_k = !is_q && head < r.hq + r.hk;
+  const int kv = is_q ? 0 : (is_k ? head - r.hq : head - r.hq - r.hk);
+  const LaneFreqs<T, LOG2L> lf = lane_freqs<T, LOG2L>(r.inv_freq, LOG2L, lane);
+  for (int b = 0; b < p.batch && b < B; ++b) {
+    const int64_t pos = r.positions[b];
+    const int64_t slot = r.slots[b];
+    const bool slot_ok = slot >= 0 && slot < r.clen;
+    int64_t frame = 0;
+    bool frame_ok = true;
+    if constexpr (TABLE) {
+      const int64_t fp = r.frame_pos ? r.frame_pos[b] : pos;
+      frame = fp < 0 ? -1 : (r.tpf_shift >= 0 ? (fp >> r.tpf_shift) : fp / r.tpf);
+      frame_ok = frame >= 0 && frame < r.table_rows;
+    }
+    if (lane == 0 && r.err && (head == r.hq || (head == 0 && TABLE))) {
+      int bits = 0;
+      if (head == r.hq && !slot_ok) bits |= KANI_FLAG_SLOT_OOB;
+      if (TABLE && head == 0 && !frame_ok) bits |= KANI_FLAG_FRAME_OOB;
+      if (bits) atomicOr(r.err, bits);
+    }
+    const uint4 xlo = *reinterpret_cast<const uint4*>(&s_head[b][lo]);
+    const uint4 xhi = *reinterpret_cast<const uint4*>(&s_head[b][hi]);
+    if (!is_q && !is_k) {  // V head: copy into the cache slot
+      if (mine && slot_ok) {
+        T* dst = static_cast<T*>(r.v_cache) + b * r.cbs + kv * r.chs + slot * r.css;
+        st16(dst + lo, xlo);
+        st16(dst + hi, xhi);
+      }
+      continue;
+    }
+    float cs[E], sn[E], nsn[E], pl[E], ph[E];
+    warp_cos_sin<T, LOG2L>(lf, (float)pos, LOG2L, lane, cs, sn);
+#pragma unroll
+    for (int e = 0; e < E; ++e) nsn[e] = -sn[e];
+    if constexpr (TABLE) {
+      if (frame_ok && mine) {
+        const T* pr = static_cast<const T*>(r.table) + frame * kRopeD;
+        unpack16<T>(ld16_ro(pr + lo), pl);
+        unpack16<T>(ld16_ro(pr + hi), ph);
+      }
+    }
+    T* dst = is_q ? static_cast<T*>(r.q_out) + b * r.qobs + head * r.qohs
+                  : static_cast<T*>(r.k_cache) + b * r.cbs + kv * r.chs + slot * r.css;
+    const bool live = mine && (is_q || slot_ok);
+    rope_chunk_store<T, QKN, TABLE>(xlo, xhi, live, cs, nsn, sn, pl, ph, frame_ok,
+                                     static_cast<const T*>(is_q ? r.qw : r.kw), lo, hi, LOG2L, kRopeD, r.eps, dst);
   }
 }
 
@@ -318,4 +479,82 @@ extern "C" int kani_gemv_short_conv(int32_t dtype, const void* x, int64_t x_row_
   const bool norm = norm_weight != nullptr;
   if (dtype == KANI_DTYPE_BF16) return kani::launch_gemv<__nv_bfloat16>(prm, norm, 2, s);
   return kani::launch_gemv<__half>(prm, norm, 2, s);
+}
+
+namespace kani {
+namespace {
+
+template <typename T, int B, bool NORM, bool QKN, bool TABLE>
+int launch_rope_kv_b(const GemvParams& prm, const RopeKvParams& r, cudaStream_t s) {
+  constexpr int CH = 4;  // K = 1024
+  const size_t smem = (size_t)B * CH * 256 * sizeof(T);
+  auto kern = gemv_rope_kv_kernel<T, B, CH, NORM, QKN, TABLE>;
+  const int grid = r.hq + 2 * r.hk;
+  const cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kGemvThreads), smem, s, prm, r);
+  note_launch();
+  return e == cudaSuccess ? KANI_OK : (int)e;
+}
+
+template <typename T, bool NORM, bool QKN, bool TABLE>
+int launch_rope_kv_t(const GemvParams& prm, const RopeKvParams& r, cudaStream_t s) {
+  if (prm.batch <= 1) return launch_rope_kv_b<T, 1, NORM, QKN, TABLE>(prm, r, s);
+  if (prm.batch <= 2) return launch_rope_kv_b<T, 2, NORM, QKN, TABLE>(prm, r, s);
+  return launch_rope_kv_b<T, 4, NORM, QKN, TABLE>(prm, r, s);
+}
+
+template <typename T>
+int launch_rope_kv(const GemvParams& prm, const RopeKvParams& r, bool norm, bool qkn, bool table, cudaStream_t s) {
+  // the decode step always normalises the input; the head norm and the table vary
+  if (!norm) return KANI_ERR_UNSUPPORTED;
+  if (qkn) return table ? launch_rope_kv_t<T, true, true, true>(prm, r, s) : launch_rope_kv_t<T, true, true, false>(prm, r, s);
+  return table ? launch_rope_kv_t<T, true, false, true>(prm, r, s) : launch_rope_kv_t<T, true, false, false>(prm, r, s);
+}
+
+}  // namespace
+}  // namespace kani
+
+extern "C" int kani_gemv_rope_kv(int32_t dtype, const void* x, int64_t x_row_stride, const void* residual,
+                                 int64_t residual_row_stride, void* residual_out, int64_t residual_out_row_stride,
+                                 const void* norm_weight, float eps, const void* qkv_weight,
+                                 int64_t weight_row_stride, int32_t k, int64_t batch, int32_t num_q_heads,
+                                 int32_t num_kv_heads, int32_t head_dim, const float* inv_freq,
+                                 const int64_t* positions, const void* q_norm_w, const void* k_norm_w,
+                                 float head_eps, const void* frame_table, int64_t frame_rows,
+                                 const int64_t* frame_pos, int32_t tokens_per_frame, void* q_out,
+                                 int64_t q_out_batch_stride, int64_t q_out_head_stride, void* k_cache,
+                                 void* v_cache, int64_t cache_batch_stride, int64_t cache_head_stride,
+                                 int64_t cache_slot_stride, int64_t cache_len, const int64_t* slots,
+                                 int32_t* err_flag, void* stream) {
+  if (batch < 0 || k < 0 || num_q_heads < 0 || num_kv_heads < 0) return KANI_ERR_INVALID_ARG;
+  if (batch == 0) return KANI_OK;
+  if (batch > 4 || k != 1024 || head_dim != kani::kRopeD || num_q_heads < 1 || num_kv_heads < 1)
+    return KANI_ERR_UNSUPPORTED;
+  if (!inv_freq || !positions || !q_out || !k_cache || !v_cache || !slots) return KANI_ERR_INVALID_ARG;
+  if ((q_norm_w == nullptr) != (k_norm_w == nullptr)) return KANI_ERR_INVALID_ARG;
+  if (frame_table && (frame_rows < 0 || tokens_per_frame < 1)) return KANI_ERR_INVALID_ARG;
+  const int32_t n_rows = (num_q_heads + 2 * num_kv_heads) * head_dim;
+  const int rc = kani::check_gemv(dtype, x, x_row_stride, residual, residual_row_stride, residual_out,
+                                  residual_out_row_stride, norm_weight, qkv_weight, weight_row_stride, n_rows, k,
+                                  batch, q_out, n_rows);
+  if (rc != KANI_OK) return rc;
+  if (!kani::aligned16(q_out) || !kani::aligned16(k_cache) || !kani::aligned16(v_cache) || q_out_head_stride % 8 ||
+      q_out_batch_stride % 8 || cache_batch_stride % 8 || cache_head_stride % 8 || cache_slot_stride % 8 ||
+      (q_norm_w && (!kani::aligned16(q_norm_w) || !kani::aligned16(k_norm_w))) ||
+      (frame_table && !kani::aligned16(frame_table)))
+    return KANI_ERR_UNSUPPORTED;
+  kani::GemvParams prm{x, x_row_stride, residual, residual_row_stride, residual_out, residual_out_row_stride,
+                       norm_weight, eps, qkv_weight, weight_row_stride, n_rows, k, (int)batch, q_out, 0,
+                       nullptr, 0, nullptr};
+  int shift = -1;
+  if (tokens_per_frame > 0 && (tokens_per_frame & (tokens_per_frame - 1)) == 0)
+    for (shift = 0; (1 << shift) < tokens_per_frame; ++shift) {
+    }
+  kani::RopeKvParams r{num_q_heads, num_kv_heads, inv_freq, positions, q_norm_w, k_norm_w, head_eps, frame_table,
+                       frame_rows, frame_pos, tokens_per_frame, shift, q_out, q_out_batch_stride, q_out_head_stride,
+                       k_cache, v_cache, cache_batch_stride, cache_head_stride, cache_slot_stride, cache_len, slots,
+                       err_flag};
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool norm = norm_weight != nullptr, qkn = q_norm_w != nullptr, table = frame_table != nullptr;
+  if (dtype == KANI_DTYPE_BF16) return kani::launch_rope_kv<__nv_bfloat16>(prm, r, norm, qkn, table, s);
+  return kani::launch_rope_kv<__half>(prm, r, norm, qkn, table, s);
 }

@@ -76,6 +76,10 @@ _SIGNATURES = {
                               _c_i32, _c_i32, _c_i64, _c_p, _c_i64, _c_p, _c_i32, _c_p, _c_i64, _c_p], ctypes.c_int),
     "kani_decode_advance": ([_c_p, _c_p, _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_i32, _c_f32,
                              _c_p, _c_p, _c_p, _c_i64, _c_p], ctypes.c_int),
+    "kani_gemv_rope_kv": ([_c_i32, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_f32, _c_p, _c_i64,
+                           _c_i32, _c_i64, _c_i32, _c_i32, _c_i32, _c_p, _c_p, _c_p, _c_p, _c_f32, _c_p, _c_i64,
+                           _c_p, _c_i32, _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_p,
+                           _c_p, _c_p], ctypes.c_int),
     "kani_codec_codes": ([_c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_p, _c_p,
                           _c_p], ctypes.c_int),
 }

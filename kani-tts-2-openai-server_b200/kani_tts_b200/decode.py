@@ -42,8 +42,8 @@ import torch.nn.functional as F
 
 from . import _lib
 from .fused_kernels import (decode_advance, decode_attention, fused_add_rms_norm, fused_rms_norm,
-                            fused_rope_kv_write, fused_silu_mul, gemv, gemv_short_conv, head_argmax,
-                            sample_tokens, short_conv_step)
+                            fused_rope_kv_write, fused_silu_mul, gemv, gemv_rope_kv_write, gemv_short_conv,
+                            head_argmax, sample_tokens, short_conv_step)
 from .model import LFM2Config
 from .positions import learnable_inv_freq
 from .sampling import SamplingParams, seen_bitmap
@@ -153,8 +153,9 @@ class FusedDecoder:
     def _final_hidden_small(self, input_ids, positions, slots, kv_len) -> torch.Tensor:
         """Up to 8 streams: every F.linear is a ``gemv`` launch that also applies the
         residual add + RMSNorm before it and, for gate/up, the SiLU·mul after it,
-        and the in_proj GEMV also runs the short-conv step, so a layer is 4
-        launches (conv) or 6 (attention) instead of 8-9.  The
+        the in_proj GEMV also runs the short-conv step and the QKV GEMV the
+        q/k norm + RoPE + KV write, so a layer is 4 launches (conv) or 5
+        (attention) instead of 8-9.  The
         residual stream alternates between two static buffers (a launch reads one
         and writes the other)."""
         b, hq, hk, d = self.batch, self.hq, self.hk, self.d
@@ -175,13 +176,12 @@ class FusedDecoder:
 
         for i, L in enumerate(self.layers):
             if L["attn"]:
-                qkv = normed(gemv, L["qkv"], norm_weight=L["op_norm"])   # [B, 1, (Hq+2Hk)D]
-                q, k, v = qkv.split([self.q_dim, self.kv_dim, self.kv_dim], dim=-1)
-                q_rot = fused_rope_kv_write(
-                    q.view(b, 1, hq, d), k.view(b, 1, hk, d), v.view(b, 1, hk, d), L["inv_freq"], positions,
-                    self.k_cache[i], self.v_cache[i], slots, frame_table=self.frame_table,
-                    tokens_per_frame=self.cfg.tokens_per_frame, q_norm_w=L["q_norm"], k_norm_w=L["k_norm"],
-                    eps=self.eps, err_flag=self.err_flag)
+                # QKV GEMV + q/k norm + RoPE + frame term + KV write, one launch
+                q_rot = normed(gemv_rope_kv_write, L["qkv"], L["op_norm"], L["inv_freq"], positions,
+                               self.k_cache[i], self.v_cache[i], slots, num_q_heads=hq, num_kv_heads=hk,
+                               q_norm_w=L["q_norm"], k_norm_w=L["k_norm"], head_eps=self.eps,
+                               frame_table=self.frame_table, tokens_per_frame=self.cfg.tokens_per_frame,
+                               err_flag=self.err_flag)
                 attn = decode_attention(q_rot, self.k_cache[i], self.v_cache[i], kv_len, self.scale,
                                         err_flag=self.err_flag)
                 delta = gemv(attn.view(b, 1, self.q_dim), L["o"])

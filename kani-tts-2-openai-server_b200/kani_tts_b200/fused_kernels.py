@@ -47,6 +47,7 @@ __all__ = [
     "gemv",
     "gemv_short_conv",
     "decode_advance",
+    "gemv_rope_kv_write",
 ]
 
 
@@ -614,6 +615,52 @@ def gemv_short_conv(x: torch.Tensor, in_proj_weight: torch.Tensor, conv_state: t
                                    ptr(conv_weight.contiguous()), lc, ptr(out), ys, stream_ptr(x.device)),
           "kani_gemv_short_conv")
     return out
+
+
+def gemv_rope_kv_write(x: torch.Tensor, qkv_weight: torch.Tensor, norm_weight: torch.Tensor,
+                       inv_freq: torch.Tensor, position: torch.Tensor, k_cache: torch.Tensor,
+                       v_cache: torch.Tensor, write_pos: torch.Tensor, *, num_q_heads: int, num_kv_heads: int,
+                       residual: torch.Tensor | None = None, residual_out: torch.Tensor | None = None,
+                       eps: float = 1e-5, q_norm_w: torch.Tensor | None = None,
+                       k_norm_w: torch.Tensor | None = None, head_eps: float = 1e-5,
+                       frame_table: torch.Tensor | None = None, tokens_per_frame: int = 4,
+                       frame_pos: torch.Tensor | None = None, q_out: torch.Tensor | None = None,
+                       err_flag: torch.Tensor | None = None) -> torch.Tensor:
+    """The attention block's QKV projection (with the input residual add +
+    RMSNorm) fused with q/k norm, RoPE, the frame term and the KV write, one
+    launch for up to 4 streams (optimized_decode.py:215-240).  x: [B, 1, K]
+    (the residual-stream update, or the normed input's source when no
+    residual); caches [B, Hk, S, 64]; position / write_pos: [B] int64.
+    Returns q_out [B, Hq, 64]."""
+    require_cuda(x, "x")
+    lib = load_library()
+    code = dtype_code(x, "x")
+    k = x.shape[-1]
+    d = k_cache.shape[-1]
+    xv, b, xs = _rows_view(x, k)
+    rv, rs, ov, os_ = None, 0, None, 0
+    if residual is not None:
+        rv, _, rs = _rows_view(residual, k)
+    if residual_out is not None:
+        ov, _, os_ = _rows_view(residual_out, k)
+    if q_out is None:
+        q_out = torch.empty(b, num_q_heads, d, dtype=x.dtype, device=x.device)
+    if err_flag is None:
+        err_flag = error_flag(x.device)
+    pos = position.reshape(-1).contiguous()
+    slots = write_pos.reshape(-1).contiguous()
+    fpos = frame_pos.reshape(-1).contiguous() if frame_pos is not None else None
+    check(lib.kani_gemv_rope_kv(
+        code, ptr(xv), xs, ptr(rv) if rv is not None else None, rs, ptr(ov) if ov is not None else None, os_,
+        ptr(norm_weight.contiguous()), float(eps), ptr(qkv_weight), qkv_weight.stride(0), k, b, num_q_heads,
+        num_kv_heads, d, ptr(inv_freq.float().contiguous()), ptr(pos),
+        ptr(q_norm_w) if q_norm_w is not None else None, ptr(k_norm_w) if k_norm_w is not None else None,
+        float(head_eps), ptr(frame_table) if frame_table is not None else None,
+        frame_table.shape[0] if frame_table is not None else 0, ptr(fpos) if fpos is not None else None,
+        int(tokens_per_frame), ptr(q_out), q_out.stride(0), q_out.stride(1), ptr(k_cache), ptr(v_cache),
+        k_cache.stride(0), k_cache.stride(1), k_cache.stride(2), k_cache.shape[2], ptr(slots), ptr(err_flag),
+        stream_ptr(x.device)), "kani_gemv_rope_kv")
+    return q_out
 
 
 def head_argmax(hidden: torch.Tensor, weight: torch.Tensor, index_map: torch.Tensor | None = None, *,

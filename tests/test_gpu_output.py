@@ -211,3 +211,44 @@ def test_decode_advance_matches_the_reference_schedule():
         assert torch.equal(slots.cpu(), (base + k + 1).cpu()) and torch.equal(kvl.cpu(), (base + k + 2).cpu())
     assert int(step.item()) == n and int(rng.item()) == 5 + n
     assert torch.equal(gen.cpu(), (torch.arange(n) + torch.tensor([[1000], [2000], [3000]])))
+
+
+@pytest.mark.parametrize("b,table", [(1, True), (3, True), (4, False)])
+def test_gemv_rope_kv_equals_gemv_then_rope(b, table):
+    """QKV GEMV with the q/k norm + RoPE + frame term + KV write in its epilogue:
+    bit-identical to gemv(QKV) followed by fused_rope_kv_write (same row
+    accumulation order, the same RoPE code), caches included; an out-of-range
+    slot is skipped and flagged."""
+    from kani_tts_b200 import _lib
+    from kani_tts_b200.positions import learnable_inv_freq
+    hq, hk, d, h, s_len = 16, 8, 64, 1024, 64
+    x = rnd((b, 1, h), 1700 + b).to(DEV)
+    res = rnd((b, 1, h), 1701).to(DEV)
+    nw = (1.0 + 0.1 * rnd((h,), 1702, torch.float32)).to(torch.bfloat16).to(DEV)
+    w = rnd(((hq + 2 * hk) * d, h), 1703, std=0.03).to(DEV)
+    qn = (1.0 + 0.1 * rnd((d,), 1704, torch.float32)).to(torch.bfloat16).to(DEV)
+    kn = (1.0 + 0.1 * rnd((d,), 1705, torch.float32)).to(torch.bfloat16).to(DEV)
+    inv = learnable_inv_freq(d, 1e6, torch.tensor(0.05)).to(DEV)
+    tab = rnd((32, d), 1706, std=0.02).to(DEV) if table else None
+    pos = torch.tensor([5, 77, 40, 13][:b], device=DEV)
+    slots = torch.tensor([3, 9, 63, 20][:b], device=DEV)
+    if b == 3:
+        slots[2] = 64                                    # out of range: skipped and flagged
+    kc0, vc0 = rnd((b, hk, s_len, d), 1707).to(DEV), rnd((b, hk, s_len, d), 1708).to(DEV)
+    kca, vca, kcb, vcb = kc0.clone(), vc0.clone(), kc0.clone(), vc0.clone()
+    ha, hb = torch.empty_like(x), torch.empty_like(x)
+    _lib.read_and_clear_errors(DEV)
+    qkv = K.gemv(x, w, norm_weight=nw, residual=res, residual_out=ha)
+    q, k, v = qkv.split([hq * d, hk * d, hk * d], dim=-1)
+    qa = K.fused_rope_kv_write(q.view(b, 1, hq, d), k.view(b, 1, hk, d), v.view(b, 1, hk, d), inv, pos, kca, vca,
+                               slots, frame_table=tab, tokens_per_frame=4, q_norm_w=qn, k_norm_w=kn, eps=1e-5)
+    fa = _lib.read_and_clear_errors(DEV)
+    qb = K.gemv_rope_kv_write(x, w, nw, inv, pos, kcb, vcb, slots, num_q_heads=hq, num_kv_heads=hk, residual=res,
+                              residual_out=hb, q_norm_w=qn, k_norm_w=kn, head_eps=1e-5, frame_table=tab,
+                              tokens_per_frame=4)
+    fb = _lib.read_and_clear_errors(DEV)
+    torch.cuda.synchronize()
+    assert torch.equal(qa.reshape(b, hq, d).cpu(), qb.cpu())
+    assert torch.equal(kca.cpu(), kcb.cpu()) and torch.equal(vca.cpu(), vcb.cpu())
+    assert torch.equal(ha.cpu(), hb.cpu())
+    assert fa == fb == (_lib.KANI_FLAG_SLOT_OOB if b == 3 else 0)

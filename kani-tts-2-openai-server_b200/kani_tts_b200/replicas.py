@@ -49,3 +49,55 @@ def aggregate_throughput(units: float, seconds: float, device="cpu") -> tuple[fl
 def barrier() -> None:
     if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
         dist.barrier()
+
+
+# ----------------------------------------------------------- failed replicas
+#
+# The collectives above assume every replica finishes.  For serving, a replica
+# that dies (its process killed, an exception) must not stall the others: each
+# rank posts its outcome to the process group's key-value store, and rank 0
+# collects with a deadline instead of a collective, so a silent rank is
+# reported as failed and the finished replicas' work still counts.
+
+def report_outcome(store, rank: int, units: float = 0.0, seconds: float = 0.0, error: str | None = None,
+                   prefix: str = "replica") -> None:
+    """Post this rank's result (or its error) under ``prefix/rank`` in a
+    ``torch.distributed`` Store (TCPStore / FileStore / HashStore)."""
+    msg = f"error:{error}" if error is not None else f"ok:{float(units)!r}:{float(seconds)!r}"
+    store.set(f"{prefix}/{rank}", msg)
+
+
+def collect_outcomes(store, world: int, timeout_s: float = 30.0, poll_s: float = 0.05,
+                     prefix: str = "replica") -> dict:
+    """Wait (at most ``timeout_s``) for every rank's report and summarise:
+    ``{"ok": [ranks], "failed": {rank: reason}, "units": sum over ok ranks,
+    "seconds": slowest ok rank, "rate": units / seconds}``.  A rank that never
+    reports within the deadline is listed as failed; the call never blocks on a
+    collective, so it returns even when a replica process has died."""
+    import time
+    keys = {r: f"{prefix}/{r}" for r in range(world)}
+    pending = set(keys)
+    results: dict[int, str] = {}
+    deadline = time.monotonic() + timeout_s
+    while pending:
+        for r in sorted(pending):
+            if store.check([keys[r]]):
+                results[r] = store.get(keys[r]).decode()
+                pending.discard(r)
+        if not pending or time.monotonic() > deadline:
+            break
+        time.sleep(poll_s)
+    ok, failed, units, seconds = [], {}, 0.0, 0.0
+    for r in range(world):
+        msg = results.get(r)
+        if msg is None:
+            failed[r] = f"no report within {timeout_s:g} s"
+        elif msg.startswith("error:"):
+            failed[r] = msg[len("error:"):]
+        else:
+            _, u, s = msg.split(":")
+            ok.append(r)
+            units += float(u)
+            seconds = max(seconds, float(s))
+    return {"ok": ok, "failed": failed, "units": units, "seconds": seconds,
+            "rate": units / seconds if seconds > 0 else 0.0}

@@ -66,3 +66,53 @@ def test_two_gloo_ranks_aggregate_like_the_bench():
         assert total == 2 * 64 * 1500
         assert slowest == 2.0                            # max over ranks
         assert rate == total / 2.0
+
+
+def _replica_worker(rank, world, port, mode, q):
+    """rank 0 hosts the store and collects; the others report, raise or die."""
+    import os
+    import torch.distributed as dist
+    from kani_tts_b200 import replicas as R
+    store = dist.TCPStore("127.0.0.1", port, world, rank == 0, timeout=__import__("datetime").timedelta(seconds=20))
+    if rank == 1 and mode == "killed":
+        os._exit(3)                                   # the process dies without a word
+    if rank == 1 and mode == "raised":
+        try:
+            raise RuntimeError("replica 1: CUDA error 700")
+        except RuntimeError as e:
+            R.report_outcome(store, rank, error=str(e))
+    else:
+        R.report_outcome(store, rank, units=1000.0 * (rank + 1), seconds=0.5 + 0.1 * rank)
+    if rank == 0:
+        q.put(R.collect_outcomes(store, world, timeout_s=3.0))
+        # keep the store alive until the others are done with it
+        import time
+        time.sleep(0.5)
+
+
+@pytest.mark.parametrize("mode", ["killed", "raised"])
+def test_failed_replica_is_reported_and_the_others_count(mode):
+    """Three replica processes; replica 1 dies (or reports an exception).  The
+    collector returns within its deadline, names replica 1 as failed and adds up
+    the work of replicas 0 and 2 (slowest ok time 0.7 s)."""
+    import multiprocessing as mp
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_replica_worker, args=(r, 3, port, mode, q)) for r in range(3)]
+    for p in procs:
+        p.start()
+    summary = q.get(timeout=60)
+    for p in procs:
+        p.join(timeout=30)
+    assert summary["ok"] == [0, 2]
+    assert list(summary["failed"]) == [1]
+    if mode == "raised":
+        assert "CUDA error 700" in summary["failed"][1]
+    else:
+        assert "no report" in summary["failed"][1]
+    assert summary["units"] == 4000.0 and abs(summary["seconds"] - 0.7) < 1e-9
+    assert procs[1].exitcode == (3 if mode == "killed" else 0)

@@ -118,6 +118,8 @@ class FusedDecoder:
         self.small_batch = (batch <= 4 and h == 1024 and cfg.intermediate_size in (1024, 4608)
                             and self.q_dim == h and cfg.conv_L_cache == 3)
         self.res_buf = [torch.empty(batch, 1, h, dtype=self.dtype, device=dev) for _ in range(2)]
+        self.logits_buf = torch.empty(batch, 1, self.head.shape[0], dtype=self.dtype, device=dev)
+        self.argmax_buf = torch.empty(batch, dtype=torch.long, device=dev)
 
     # ------------------------------------------------------------ decode
     fused_greedy_head = True   # greedy steps may use the fused head + argmax (batch <= 8)
@@ -133,6 +135,18 @@ class FusedDecoder:
         reduced-head logits [B, 1, num_reduced].
         """
         return F.linear(self._final_hidden(input_ids, positions, slots, kv_len), self.head)
+
+    def step_logits(self, input_ids: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor,
+                    kv_len: torch.Tensor) -> torch.Tensor:
+        """``step`` for up to 8 streams with the reduced head on ``head_argmax``, which
+        writes the logits while it streams the head (its greedy token is not used).
+        Returns reduced-head logits [B, 1, num_reduced] in a static buffer."""
+        if self.head_scratch is None:
+            return self.step(input_ids, positions, slots, kv_len)
+        normed = self._final_hidden(input_ids, positions, slots, kv_len)
+        head_argmax(normed, self.head, scratch=self.head_scratch, logits_out=self.logits_buf.view(self.batch, -1),
+                    out=self.argmax_buf)
+        return self.logits_buf
 
     def step_greedy(self, input_ids: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor,
                     kv_len: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
@@ -351,6 +365,9 @@ class DecodeEngine:
         if self.sampling is None and self.dec.fused_greedy_head and self.dec.head_scratch is not None:
             self.logits = None
             nxt = self.dec.step_greedy(self.input_ids, self.positions, self.slots, self.kv_len, out=self.next_tok)
+        elif self.dec.fused_greedy_head and self.dec.head_scratch is not None:
+            self.logits = self.dec.step_logits(self.input_ids, self.positions, self.slots, self.kv_len)
+            nxt = self._next_token(self.logits[:, 0])
         else:
             self.logits = self.dec.step(self.input_ids, self.positions, self.slots, self.kv_len, self.mask)
             nxt = self._next_token(self.logits[:, 0])

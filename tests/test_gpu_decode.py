@@ -209,3 +209,21 @@ def test_fused_greedy_head_matches_logits_argmax():
     clear = (margin[:, 0] - margin[:, 1]) > margin[:, 0].abs() * 2 ** -6
     assert torch.equal(red[clear], logits.argmax(-1)[clear])
     assert int(dec.head_scratch.abs().sum()) == 0
+
+
+def test_step_logits_from_fused_head_match_linear_head():
+    """The sampled small-batch path takes its logits from the fused head kernel;
+    they agree with F.linear's within the GEMV-order tolerance (2 % of the largest)."""
+    cfg = LFM2Config()
+    b = 2
+    dec = FusedDecoder(cfg, synthetic_state_dict(cfg, seed=23), DEV, batch=b, max_len=32)
+    ids = torch.randint(cfg.audio_tokens_start, cfg.vocab_size, (b, 1), generator=torch.Generator().manual_seed(4))
+    args = (ids.to(DEV), torch.tensor([3, 6], device=DEV), torch.tensor([4, 7], device=DEV),
+            torch.tensor([5, 8], device=DEV))
+    snap = {i: c.clone() for i, c in dec.conv_state.items()}
+    ref = dec.step(*args).clone()
+    for i, c in snap.items():
+        dec.conv_state[i].copy_(c)
+    got = dec.step_logits(*args)
+    close(got, ref, 0.02)
+    assert int(dec.head_scratch.abs().sum()) == 0

@@ -493,6 +493,7 @@ def _make_eager_decoder_cls():
                 n = gu.shape[-1] // 2
                 mlp = (gu[..., :n].float() * torch.sigmoid(gu[..., :n].float()) * gu[..., n:].float()).to(self.dtype)
                 hidden = hidden + F.linear(mlp, L["down"])
+            # the reference's F.linear on the unpadded reduced head (optimized_decode.py:287)
             return F.linear(_eager_rms(hidden, self.final_norm, self.eps), self.head)
 
     return EagerReferenceDecoder

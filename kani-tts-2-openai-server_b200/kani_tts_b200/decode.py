@@ -92,7 +92,15 @@ class FusedDecoder:
             self.layers.append(L)
         self.final_norm = t("model.embedding_norm.weight")
         head = t("lm_head.weight")
-        self.head = torch.cat([head[cfg.eos_token_id:cfg.eos_token_id + 1], head[cfg.audio_tokens_start:]], 0)
+        red = torch.cat([head[cfg.eos_token_id:cfg.eos_token_id + 1], head[cfg.audio_tokens_start:]], 0)
+        # F.linear's output row is padded to a multiple of 8 (16 bytes): an odd row of
+        # 15591 logits sends cuBLAS to an unaligned GEMM several times slower at
+        # 64 streams.  The extra zero rows are sliced off the logits; `head` is the
+        # view of the real rows (the fused head kernels and the samplers see only those).
+        pad = (-red.shape[0]) % 8
+        self.head_padded = torch.cat([red, red.new_zeros(pad, red.shape[1])], 0) if pad else red
+        self.head = self.head_padded[:red.shape[0]]
+        self.num_reduced = red.shape[0]
         self.reduced_to_full = torch.cat([
             torch.tensor([cfg.eos_token_id], device=dev, dtype=torch.long),
             torch.arange(cfg.audio_tokens_start, cfg.vocab_size, device=dev, dtype=torch.long)])
@@ -134,7 +142,11 @@ class FusedDecoder:
         ignored: the valid region is the prefix [0, kv_len).  Returns
         reduced-head logits [B, 1, num_reduced].
         """
-        return F.linear(self._final_hidden(input_ids, positions, slots, kv_len), self.head)
+        return self._linear_head(self._final_hidden(input_ids, positions, slots, kv_len))
+
+    def _linear_head(self, normed: torch.Tensor) -> torch.Tensor:
+        """Reduced-head logits by F.linear on the padded head: [..., num_reduced] view."""
+        return F.linear(normed, self.head_padded)[..., :self.num_reduced]
 
     def step_logits(self, input_ids: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor,
                     kv_len: torch.Tensor) -> torch.Tensor:
@@ -300,7 +312,7 @@ class FusedDecoder:
             normed, hidden = fused_add_rms_norm(delta, hidden, L["ffn_norm"], self.eps)
             delta = F.linear(fused_silu_mul(F.linear(normed, L["gate_up"])), L["down"])
         normed, _ = fused_add_rms_norm(delta[:, -1:], hidden[:, -1:], self.final_norm, self.eps)
-        return F.linear(normed, self.head)
+        return self._linear_head(normed)
 
 
 class DecodeEngine:

@@ -824,14 +824,21 @@ def run_op(name: str, size: int, steps: int, warmup: int) -> dict:
         h, y = torch.empty_like(x), torch.empty(size, 1, 4608, dtype=bf, device=dev)
         fn = lambda: gemv(x, wt, norm_weight=nw, residual=r, residual_out=h, silu_pairs=True, out=y)  # noqa: E731
         nbytes = 9216 * 1024 * 2 + size * 1024 * 2 * 3 + size * 4608 * 2
-    elif name in ("head_argmax", "head_cublas"):  # size = streams; reduced head 15591 x 1024
-        rows, h = 15591, 1024
+    elif name in ("head_argmax", "head_tc", "head_cublas", "head_cublas_pad8"):
+        rows, h = 15591, 1024                   # size = streams; reduced head 15591 x 1024
         hid, wt = rn(size, h), rn(rows, h) * 0.05
         imap = torch.arange(rows, device=dev) + 64410
         out = torch.empty(size, dtype=torch.long, device=dev)
         if name == "head_argmax":
             scratch = torch.zeros(size + 1, dtype=torch.long, device=dev)
             fn = lambda: K.head_argmax(hid, wt, imap, scratch=scratch, out=out)  # noqa: E731
+        elif name == "head_tc":
+            scratch = torch.zeros(size + 1, dtype=torch.int32, device=dev)
+            fn = lambda: K.head_argmax_tc(hid, wt, imap, scratch=scratch, out=out)  # noqa: E731
+        elif name == "head_cublas_pad8":        # head rows padded to a multiple of 8, logits sliced back
+            wp = torch.zeros((rows + 7) // 8 * 8, h, dtype=bf, device=dev)
+            wp[:rows].copy_(wt)
+            fn = lambda: out.copy_(imap[torch.nn.functional.linear(hid, wp)[:, :rows].argmax(-1)])  # noqa: E731
         else:                                   # the reference's F.linear head + greedy argmax + map
             fn = lambda: out.copy_(imap[torch.nn.functional.linear(hid, wt).argmax(-1)])  # noqa: E731
         nbytes = rows * h * 2 + size * h * 2
@@ -885,7 +892,7 @@ def main():
     ap.add_argument("--decode-batch", type=int, default=1, help="streams for --decode-only")
     ap.add_argument("--op", default=None, help="profiling aid: run one fused op alone "
                     "(silu_mul, add_rms_norm, rope_kv_write, decode_attention, short_conv, sample, "
-                    "head_argmax, head_cublas, gemv_gate_up)")
+                    "head_argmax, head_tc, head_cublas, head_cublas_pad8, gemv_gate_up)")
     ap.add_argument("--size", type=int, default=4096, help="rows / tokens / streams for --op")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()

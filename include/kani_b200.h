@@ -279,6 +279,28 @@ KANI_API int kani_head_argmax_noalloc(int32_t dtype, const void* hidden, int64_t
                      int64_t tokens_out_stride, void* stream);
 
 /*
+ * Reduced LM head + greedy choice for 2..64 streams on the tensor cores
+ * (tcgen05.mma, fp32 accumulators in tensor memory), one launch:
+ *   logits[b, r] = round(sum_k hidden[b, k] * weight[r, k])  (fp32 accumulation)
+ *   tokens_out[b * stride] = index_map[first r with the largest logits[b, r]]
+ * Replaces, for a batch of streams, F.linear(hidden, audio_lm_head_weight)
+ * (kani_tts/optimized_decode.py:287, head built at :134-156) and the greedy
+ * reduced_to_full[argmax(...)] (:144-148).
+ *   hidden: [batch, hidden_size]; weight: [rows, hidden_size]; bf16 or fp16;
+ *   hidden_size a multiple of 64, at most 1024; rows <= 65535; pointers and row
+ *   strides 16-byte aligned.  logits_out [batch, rows] (row stride) may be NULL.
+ *   scratch: batch + 1 uint32 of device memory, zero before the first call; every
+ *   call leaves it zero (one call at a time per scratch buffer).
+ *   err_flag (may be NULL): KANI_FLAG_TIMEOUT when an on-chip wait gave up.
+ *   batch > 64 or another shape: KANI_ERR_UNSUPPORTED.
+ */
+KANI_API int kani_head_argmax_tc(int32_t dtype, const void* hidden, int64_t hidden_row_stride, int64_t batch,
+                     int32_t hidden_size, const void* weight, int64_t weight_row_stride, int32_t rows,
+                     const int64_t* index_map, void* logits_out, int64_t logits_row_stride,
+                     uint32_t* scratch, int64_t* tokens_out, int64_t tokens_out_stride,
+                     int32_t* err_flag, void* stream);
+
+/*
  * Decode GEMV for up to 8 streams with its neighbours fused:
  *   y[b, r] = round(sum_k a[b, k] * weight[r, k])   (fp32 accumulation)
  * a = x, or with norm_weight the RMSNorm of the residual stream:

@@ -18,8 +18,10 @@
   buffer (optimized_decode.py:243-248);
 * the gated short-conv step between in_proj and out_proj is one
   ``short_conv_step`` launch (optimized_decode.py:256-277);
-* greedy steps of up to 8 streams end in one ``head_argmax`` launch (the
-  reduced head GEMV, the argmax and the reduced-to-full map);
+* greedy steps end in one fused head launch (the reduced head, the argmax
+  and the reduced-to-full map): ``head_argmax`` (CUDA-core GEMV) up to 8
+  streams, ``head_argmax_tc`` (tcgen05 tensor-core GEMM) from 9 to 64; sampled
+  steps take their logits from the same launch;
 * up to 8 streams, every projection is a ``gemv`` launch that folds in the
   residual add + RMSNorm before it and the SiLU·mul after the gate/up GEMV.
 
@@ -43,7 +45,7 @@ import torch.nn.functional as F
 from . import _lib
 from .fused_kernels import (decode_advance, decode_attention, fused_add_rms_norm, fused_rms_norm,
                             fused_rope_kv_write, fused_silu_mul, gemv, gemv_rope_kv_write, gemv_short_conv,
-                            head_argmax, sample_tokens, short_conv_step)
+                            head_argmax, head_argmax_tc, sample_tokens, short_conv_step)
 from .model import LFM2Config
 from .positions import learnable_inv_freq
 from .sampling import SamplingParams, seen_bitmap
@@ -116,9 +118,18 @@ class FusedDecoder:
         self.conv_state = {i: torch.zeros(batch, h, cfg.conv_L_cache, dtype=self.dtype, device=dev)
                            for i, L in enumerate(self.layers) if not L["attn"]}
         self.err_flag = _lib.error_flag(dev)
-        # cross-CTA argmax scratch of the fused greedy head (zero between launches)
-        fits = batch <= 8 and h in (512, 1024, 2048)
-        self.head_scratch = torch.zeros(batch + 1, dtype=torch.long, device=dev) if fits else None
+        # fused head + argmax: the CUDA-core GEMV kernel up to 8 streams (hidden 512 /
+        # 1024 / 2048), the tensor-core kernel up to 64 (hidden a multiple of 64, at
+        # most 1024); each keeps a cross-CTA argmax scratch that is zero between launches
+        if batch <= 8 and h in (512, 1024, 2048):
+            self.fused_head = "gemv"
+            self.head_scratch = torch.zeros(batch + 1, dtype=torch.long, device=dev)
+        elif batch <= 64 and h % 64 == 0 and h <= 1024 and red.shape[0] <= 0xffff:
+            self.fused_head = "tc"
+            self.head_scratch = torch.zeros(batch + 1, dtype=torch.int32, device=dev)
+        else:
+            self.fused_head = None
+            self.head_scratch = None
         # small batches take the fused-GEMV layer path (K of every GEMV: H or the FFN size).
         # Its CUDA-core dot products scale with the batch: measured per step on B200,
         # 1 / 2 / 4 / 8 streams take 285 / 351 / 560 / 892 us against ~750-790 us for
@@ -130,7 +141,7 @@ class FusedDecoder:
         self.argmax_buf = torch.empty(batch, dtype=torch.long, device=dev)
 
     # ------------------------------------------------------------ decode
-    fused_greedy_head = True   # greedy steps may use the fused head + argmax (batch <= 8)
+    fused_greedy_head = True   # greedy / sampled steps may use the fused head kernels
 
     def step(self, input_ids: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor,
              kv_len: torch.Tensor, mask: torch.Tensor | None = None) -> torch.Tensor:
@@ -148,27 +159,33 @@ class FusedDecoder:
         """Reduced-head logits by F.linear on the padded head: [..., num_reduced] view."""
         return F.linear(normed, self.head_padded)[..., :self.num_reduced]
 
+    def _fused_head(self, normed, index_map=None, logits_out=None, out=None) -> torch.Tensor:
+        fn = head_argmax if self.fused_head == "gemv" else head_argmax_tc
+        kw = {"err_flag": self.err_flag} if self.fused_head == "tc" else {}
+        return fn(normed, self.head, index_map, scratch=self.head_scratch, logits_out=logits_out, out=out, **kw)
+
     def step_logits(self, input_ids: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor,
                     kv_len: torch.Tensor) -> torch.Tensor:
-        """``step`` for up to 8 streams with the reduced head on ``head_argmax``, which
-        writes the logits while it streams the head (its greedy token is not used).
-        Returns reduced-head logits [B, 1, num_reduced] in a static buffer."""
-        if self.head_scratch is None:
+        """``step`` with the reduced head on the fused head kernel, which writes the
+        logits while it computes them (its greedy token is not used).  Returns
+        reduced-head logits [B, 1, num_reduced] in a static buffer."""
+        if self.fused_head is None:
             return self.step(input_ids, positions, slots, kv_len)
         normed = self._final_hidden(input_ids, positions, slots, kv_len)
-        head_argmax(normed, self.head, scratch=self.head_scratch, logits_out=self.logits_buf.view(self.batch, -1),
-                    out=self.argmax_buf)
+        self._fused_head(normed, logits_out=self.logits_buf.view(self.batch, -1), out=self.argmax_buf)
         return self.logits_buf
 
     def step_greedy(self, input_ids: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor,
                     kv_len: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         """One decode token per stream, greedy: the reduced head, the argmax and the
-        reduced-to-full map in one ``head_argmax`` launch (batch <= 8, hidden size
-        512 / 1024 / 2048).  Returns the full token ids [B]."""
-        if self.head_scratch is None:
-            raise ValueError("the fused greedy head serves at most 8 streams of hidden size 512, 1024 or 2048")
+        reduced-to-full map in one launch (``head_argmax`` up to 8 streams of hidden
+        size 512 / 1024 / 2048, ``head_argmax_tc`` up to 64 streams of hidden size a
+        multiple of 64 up to 1024).  Returns the full token ids [B]."""
+        if self.fused_head is None:
+            raise ValueError("the fused greedy head serves at most 64 streams (hidden size at most 1024, "
+                             "or 2048 up to 8 streams)")
         normed = self._final_hidden(input_ids, positions, slots, kv_len)
-        return head_argmax(normed, self.head, self.reduced_to_full, scratch=self.head_scratch, out=out)
+        return self._fused_head(normed, self.reduced_to_full, out=out)
 
     def _final_hidden(self, input_ids, positions, slots, kv_len) -> torch.Tensor:
         """The decode layers and the final norm: [B, 1, H]."""
@@ -374,10 +391,10 @@ class DecodeEngine:
         cfg = self.dec.cfg
         if self.keep_mask:
             self.mask.scatter_(3, self.slots.view(-1, 1, 1, 1), 0.0)
-        if self.sampling is None and self.dec.fused_greedy_head and self.dec.head_scratch is not None:
+        if self.sampling is None and self.dec.fused_greedy_head and self.dec.fused_head is not None:
             self.logits = None
             nxt = self.dec.step_greedy(self.input_ids, self.positions, self.slots, self.kv_len, out=self.next_tok)
-        elif self.dec.fused_greedy_head and self.dec.head_scratch is not None:
+        elif self.dec.fused_greedy_head and self.dec.fused_head is not None:
             self.logits = self.dec.step_logits(self.input_ids, self.positions, self.slots, self.kv_len)
             nxt = self._next_token(self.logits[:, 0])
         else:

@@ -43,6 +43,7 @@ __all__ = [
     "short_conv_step",
     "sample_tokens",
     "head_argmax",
+    "head_argmax_tc",
     "codec_codes",
     "gemv",
     "gemv_short_conv",
@@ -717,6 +718,73 @@ def head_argmax(hidden: torch.Tensor, weight: torch.Tensor, index_map: torch.Ten
                                ptr(index_map) if index_map is not None else None,
                                ptr(logits_out) if logits_out is not None else None, ls, ptr(scratch),
                                ptr(out), out.stride(0) if b > 1 else 1, stream_ptr(dev)), "kani_head_argmax")
+    return out
+
+
+def head_argmax_tc(hidden: torch.Tensor, weight: torch.Tensor, index_map: torch.Tensor | None = None, *,
+                   scratch: torch.Tensor | None = None, logits_out: torch.Tensor | None = None,
+                   out: torch.Tensor | None = None, err_flag: torch.Tensor | None = None) -> torch.Tensor:
+    """Greedy next tokens from the reduced LM head for a batch of up to 64
+    streams on the tensor cores (``kani_head_argmax_tc``): the batched form of
+    optimized_decode.py:287 with the reduced-to-full map of :144-148.
+
+    Args:
+        hidden: [B, H] or [B, 1, H] final-normed hidden states (bf16 / fp16),
+            H a multiple of 64 and at most 1024.
+        weight: [rows, H] reduced head (same dtype), rows <= 65535.
+        index_map: [rows] int64 row -> token id; None = row index.
+        scratch: [>= B + 1] int32 device tensor, zero before the first call and
+            left zero by every call; allocated (zeroed) per call when None.
+        logits_out: optional [B, rows] tensor that receives the logits.
+        out: optional [B] int64 tensor for the token ids.
+        err_flag: optional int32 device word; bit KANI_FLAG_TIMEOUT when an
+            on-chip wait gave up.
+    Returns:
+        [B] int64 token ids.
+    """
+    require_cuda(hidden, "hidden")
+    require_cuda(weight, "weight")
+    lib = load_library()
+    code = dtype_code(hidden, "hidden")
+    h = weight.shape[-1]
+    if weight.dim() != 2 or hidden.shape[-1] != h:
+        raise ValueError(f"hidden [..., {h}] and weight [rows, {h}] expected")
+    if weight.dtype != hidden.dtype:
+        raise TypeError("hidden and weight must share one dtype")
+    hv, b, hs = _rows_view(hidden, h)
+    if weight.stride(1) != 1:
+        weight = weight.contiguous()
+    rows = weight.shape[0]
+    dev = hidden.device
+    if scratch is None:
+        scratch = torch.zeros(b + 1, dtype=torch.int32, device=dev)
+    require_cuda(scratch, "scratch")
+    if scratch.dtype != torch.int32 or scratch.numel() < b + 1 or not scratch.is_contiguous():
+        raise ValueError(f"scratch must be a contiguous int32 tensor of >= {b + 1} elements")
+    if index_map is not None:
+        require_cuda(index_map, "index_map")
+        if index_map.dtype != torch.int64 or index_map.numel() != rows or not index_map.is_contiguous():
+            raise ValueError(f"index_map must be a contiguous int64 [{rows}] tensor")
+    ls = 0
+    if logits_out is not None:
+        require_cuda(logits_out, "logits_out")
+        if logits_out.dtype != hidden.dtype or logits_out.shape[-1] != rows or logits_out.stride(-1) != 1:
+            raise ValueError(f"logits_out must be [{b}, {rows}] of the hidden dtype")
+        ls = logits_out.stride(0) if logits_out.dim() > 1 else rows
+    if out is None:
+        out = torch.empty(b, dtype=torch.int64, device=dev)
+    if out.dtype != torch.int64 or out.numel() != b:
+        raise ValueError(f"out must hold {b} int64 token ids")
+    if err_flag is not None:
+        require_cuda(err_flag, "err_flag")
+        if err_flag.dtype != torch.int32:
+            raise ValueError("err_flag must be an int32 device tensor")
+    check(lib.kani_head_argmax_tc(code, ptr(hv), hs, b, h, ptr(weight), weight.stride(0), rows,
+                                  ptr(index_map) if index_map is not None else None,
+                                  ptr(logits_out) if logits_out is not None else None, ls, ptr(scratch),
+                                  ptr(out), out.stride(0) if b > 1 else 1,
+                                  ptr(err_flag) if err_flag is not None else None, stream_ptr(dev)),
+          "kani_head_argmax_tc")
     return out
 
 

@@ -186,15 +186,27 @@ def test_fused_greedy_head_matches_logits_argmax():
     """step_greedy (layers + fused head/argmax/map) picks a token whose F.linear
     logit is the maximum within one bf16 ULP (the two GEMVs sum in different
     orders), and the same token when the maximum is unique by a margin.  (The
-    tiny model's hidden size 128 takes the F.linear + argmax path instead.)"""
+    tiny model's hidden size 128 takes the tensor-core head at any batch.)"""
     assert FusedDecoder(tiny_config(), synthetic_state_dict(tiny_config(), seed=21), DEV, batch=3,
-                        max_len=32).head_scratch is None
+                        max_len=32).fused_head == "tc"
+    _check_greedy_head(3, "gemv")
+
+
+@pytest.mark.parametrize("b", [16, 64])
+def test_fused_tensor_core_head_matches_logits_argmax(b):
+    """9..64 streams: cuBLAS layers, then the tcgen05 head + argmax + map."""
+    _check_greedy_head(b, "tc")
+
+
+def _check_greedy_head(b, kind):
     cfg = LFM2Config()
-    b, max_len = 3, 32
+    max_len = 32
     sd = synthetic_state_dict(cfg, seed=21)
     dec = FusedDecoder(cfg, sd, DEV, batch=b, max_len=max_len)
+    assert dec.fused_head == kind
     ids = torch.randint(cfg.audio_tokens_start, cfg.vocab_size, (b, 1), generator=torch.Generator().manual_seed(2))
-    pos, slots = torch.tensor([3, 5, 7]), torch.tensor([4, 6, 8])
+    pos = torch.arange(b) % 7 * 2 + 3
+    slots = pos + 1
     args = (ids.to(DEV), pos.to(DEV), slots.to(DEV), (slots + 1).to(DEV))
     snap = ({i: c.clone() for i, c in dec.conv_state.items()})
     logits = dec.step(*args)[:, 0].float().cpu()

@@ -103,6 +103,11 @@ def test_abi_rejects_bad_arguments_without_launching():
     assert lib.kani_head_argmax(0, fake, 1024, 1, 1024, fake, 1024, 100, n, n, 0, fake, fake, 1, n) == -3
     assert lib.kani_head_argmax(1, fake, 1000, 1, 1000, fake, 1000, 100, n, n, 0, fake, fake, 1, n) == -1
     assert lib.kani_head_argmax(1, fake, 1024, 1, 1024, fake, 1024, 100, n, n, 0, n, fake, 1, n) == -1
+    # tensor-core head: batch above 64, fp32, hidden size not a multiple of 64, missing scratch
+    assert lib.kani_head_argmax_tc(1, fake, 1024, 65, 1024, fake, 1024, 100, n, n, 0, fake, fake, 1, n, n) == -3
+    assert lib.kani_head_argmax_tc(0, fake, 1024, 9, 1024, fake, 1024, 100, n, n, 0, fake, fake, 1, n, n) == -3
+    assert lib.kani_head_argmax_tc(1, fake, 1000, 9, 1000, fake, 1000, 100, n, n, 0, fake, fake, 1, n, n) == -3
+    assert lib.kani_head_argmax_tc(1, fake, 1024, 9, 1024, fake, 1024, 100, n, n, 0, n, fake, 1, n, n) == -1
     # fused GEMV: a residual without a norm, residual_out aliasing the residual, batch above 8, K unsupported
     assert lib.kani_gemv(1, fake, 1024, fake, 1024, n, 0, n, 1e-5, fake, 1024, 64, 1024, 1, 0, fake, 64, n) == -1
     assert lib.kani_gemv(1, fake, 1024, fake, 1024, fake, 1024, fake, 1e-5, fake, 1024, 64, 1024, 1, 0, fake, 64,
@@ -133,6 +138,7 @@ def test_abi_zero_sized_calls_are_noops():
     assert lib.kani_sample_tokens(1, n, 0, 0, 15591, n, n, 0, 1, 1.2, 0.5, 0.85, 256, n, 0, n, n, n, n, n,
                                   n, 1, n) == 0
     assert lib.kani_head_argmax(1, n, 0, 0, 1024, n, 1024, 15591, n, n, 0, n, n, 1, n) == 0
+    assert lib.kani_head_argmax_tc(1, n, 0, 0, 1024, n, 1024, 15591, n, n, 0, n, n, 1, n, n) == 0
     assert lib.kani_codec_codes(n, 0, 0, 100, 64402, 64410, 4032, n, 25, n, n, n) == 0
     assert lib.kani_launch_count() == before
 

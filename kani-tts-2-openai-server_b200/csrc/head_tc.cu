@@ -28,8 +28,9 @@
 //   * one thread issues the TMA loads and the MMAs: MMA batch kb is committed
 //     to the stage's "empty" barrier, and the stage of batch kb - 1 is refilled
 //     once that barrier completes; all waits are bounded (KANI_FLAG_TIMEOUT);
-//   * epilogue: each warp loads its 32 rows of D from tensor memory
-//     (tcgen05.ld 32x32b), rounds to the storage type (F.linear's output),
+//   * epilogue: each warp loads 32 rows x 16 columns of D from tensor memory
+//     (tcgen05.ld 32x32b; 16 warps cover 128 rows x 64 columns in one pass),
+//     rounds to the storage type (F.linear's output),
 //     optionally stores the logits, and reduces per stream the packed
 //     (order key << 16 | 0xffff - row) with a warp max; one 32-bit atomicMax
 //     per stream and CTA into the scratch; the last CTA (a counter after a
@@ -44,7 +45,9 @@
 namespace kani {
 namespace {
 
-constexpr int kTcThreads = 128;  // 4 warps: each owns 32 rows (TMEM lanes) in the epilogue
+// 16 warps: in the epilogue warp w reads TMEM lane quarter w % 4 (its 32 rows)
+// and column group w / 4 (16 streams), so 64 streams take one pass
+constexpr int kTcThreads = 512;
 constexpr int kTcM = 128;        // head rows per CTA (MMA M)
 constexpr int kTcN = 64;         // most streams (MMA N)
 constexpr int kTcKB = 64;        // hidden elements per tile: one 128-byte swizzle row
@@ -128,12 +131,32 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// Total-order key of a 16-bit float's bits (ascending with the value; -0 == +0).
+__device__ __forceinline__ uint32_t order_key16(uint32_t b) {
+  if ((b & 0x7fffu) == 0) b = 0;
+  return b ^ ((b & 0x8000u) ? 0xffffu : 0x8000u);
+}
+
+// Two fp32 values (as bits) rounded to nearest-even 16-bit floats: a in the
+// low half, b in the high half.  bf16 rounds in integer arithmetic — the same
+// bits as the hardware conversion (NaN -> the canonical 0x7fff), which costs
+// about 80 cycles per element in this epilogue where it cannot be hidden.
+__device__ __forceinline__ uint32_t bf16_rne_bits(uint32_t f) {
+  if ((f & 0x7fffffffu) > 0x7f800000u) return 0x7fffu;
+  return (f + 0x7fffu + ((f >> 16) & 1u)) >> 16;
+}
 template <typename T>
-__device__ __forceinline__ uint32_t order_key16(T v) {
-  uint16_t b;
-  memcpy(&b, &v, 2);
-  if ((b & 0x7fffu) == 0) b = 0;  // -0 == +0
-  return (uint32_t)(b ^ ((b & 0x8000u) ? 0xffffu : 0x8000u));
+__device__ __forceinline__ uint32_t round_pair(uint32_t a, uint32_t b);
+template <>
+__device__ __forceinline__ uint32_t round_pair<__nv_bfloat16>(uint32_t a, uint32_t b) {
+  return bf16_rne_bits(a) | (bf16_rne_bits(b) << 16);
+}
+template <>
+__device__ __forceinline__ uint32_t round_pair<__half>(uint32_t a, uint32_t b) {
+  const __half2 h = __floats2half2_rn(__uint_as_float(a), __uint_as_float(b));
+  uint32_t u;
+  memcpy(&u, &h, 4);
+  return u;
 }
 
 template <typename T>
@@ -263,13 +286,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) head_tc_kernel(const __grid_con
   if (!ok && lane == 0) atomicOr(&s_failed, 1);
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 
-  // ---- epilogue: warp w holds rows r0 + 32 w + lane, n_mma stream columns
-  const int row = r0 + warp * 32 + lane;
+  // ---- epilogue: warp w holds rows r0 + 32 (w % 4) + lane and the stream
+  // columns of groups w / 4, w / 4 + 4, ... (16 columns each, up to n_mma)
+  const int quarter = warp & 3;
+  const int row = r0 + quarter * 32 + lane;
   const bool row_ok = ok && row < p.rows;
-  const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
-#pragma unroll
-  for (int q = 0; q < kTcN / 16; ++q) {
-    if (q * 16 >= n_mma) break;  // uniform: columns past the MMA width were never written
+  const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16);
+#pragma unroll 1
+  for (int q = warp >> 2; q < n_mma / 16; q += kTcThreads / 128) {  // columns past the MMA width were never written
     uint32_t v[16];
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
@@ -279,25 +303,43 @@ __global__ void __launch_bounds__(kTcThreads, 1) head_tc_kernel(const __grid_con
           "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
         : "r"(taddr + (uint32_t)(q * 16))
         : "memory");
-    uint32_t pk[16];
+    // Round, then build the packed keys with selects only: a data-dependent
+    // branch per element (e.g. around the logits store) costs a divergence
+    // round trip each, several times the arithmetic.
+    const int n_valid = min(16, p.batch - q * 16);  // uniform
+    uint32_t bits[16], pk[16];
 #pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      const int b = q * 16 + e;
-      const T lv = Elem<T>::from_f(__uint_as_float(v[e]));
-      pk[e] = 0u;
-      if (row_ok && b < p.batch) {
-        if (p.logits) static_cast<T*>(p.logits)[(int64_t)b * p.logits_stride + row] = lv;
-        pk[e] = (order_key16(lv) << 16) | (0xffffu - (uint32_t)row);
+    for (int e = 0; e < 16; e += 2) {
+      const uint32_t pair = round_pair<T>(v[e], v[e + 1]);
+      bits[e] = pair & 0xffffu;
+      bits[e + 1] = pair >> 16;
+    }
+#pragma unroll
+    for (int e = 0; e < 16; ++e)
+      pk[e] = (row_ok && e < n_valid) ? ((order_key16(bits[e]) << 16) | (0xffffu - (uint32_t)row)) : 0u;
+    if (p.logits != nullptr && row_ok) {
+      uint16_t* dst = static_cast<uint16_t*>(p.logits) + (int64_t)(q * 16) * p.logits_stride + row;
+#pragma unroll
+      for (int e = 0; e < 16; ++e)
+        if (e < n_valid) dst[(int64_t)e * p.logits_stride] = (uint16_t)bits[e];
+    }
+    // Transpose-reduce over the warp: at each step a lane keeps the half of its
+    // columns selected by one lane bit and takes the max with the partner's copy
+    // of that half; after 4 steps lane l holds column (l >> 1) & 15 reduced over
+    // 16 lanes, and one more exchange covers all 32.
+#pragma unroll
+    for (int m = 16, n = 8; m >= 2; m >>= 1, n >>= 1) {
+      const bool upper = (lane & m) != 0;
+#pragma unroll
+      for (int i = 0; i < n; ++i) {
+        const uint32_t send = upper ? pk[i] : pk[i + n];
+        const uint32_t keep = upper ? pk[i + n] : pk[i];
+        pk[i] = max(keep, __shfl_xor_sync(0xffffffffu, send, m));
       }
     }
-#pragma unroll
-    for (int e = 0; e < 16; ++e) pk[e] = __reduce_max_sync(0xffffffffu, pk[e]);
-    if (lane < 16 && q * 16 + lane < p.batch) {
-      uint32_t mine = pk[0];
-#pragma unroll
-      for (int e = 1; e < 16; ++e) mine = lane == e ? pk[e] : mine;
-      atomicMax(&s_best[q * 16 + lane], mine);
-    }
+    const uint32_t col_max = max(pk[0], __shfl_xor_sync(0xffffffffu, pk[0], 1));
+    const int col = q * 16 + ((lane >> 1) & 15);
+    if ((lane & 1) == 0 && col < p.batch) atomicMax(&s_best[col], col_max);
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();

@@ -301,6 +301,30 @@ KANI_API int kani_head_argmax_tc(int32_t dtype, const void* hidden, int64_t hidd
                      int32_t* err_flag, void* stream);
 
 /*
+ * kani_gemv's operation for 2..64 streams on the tensor cores (tcgen05.mma, fp32
+ * accumulators in tensor memory; 128 weight rows per CTA, or 64 gate + 64 up rows
+ * with silu_pairs):
+ *   y[b, r] = round(sum_k a[b, k] * weight[r, k])   (fp32 accumulation)
+ * a = x, or with norm_weight round((round(x + residual) * rr) * norm_weight)
+ * (residual may be NULL; residual_out, when given, receives round(x + residual));
+ * silu_pairs != 0: weight holds 2 * n_out rows (gate, then up) and
+ *   y[b, r] = round(silu(round(gate_r)) * round(up_r)).
+ * Replaces, for a batch of streams, the F.linear calls of the decode step
+ * (kani_tts/optimized_decode.py:215, 255, 276, 281-282) with the residual add +
+ * RMSNorm before them (:206, :252, :277, :280, :283) and the SiLU·mul after the
+ * gate/up projection (triton_kernels.py:67-105).
+ *   bf16 / fp16; k a multiple of 64 (at most 1024 with norm_weight); batch <= 64;
+ *   n_out a multiple of 8 with silu_pairs; x, weight, residual, residual_out and
+ *   norm_weight 16-byte aligned with row strides a multiple of 8 elements.
+ *   err_flag (may be NULL): KANI_FLAG_TIMEOUT when an on-chip wait gave up.
+ */
+KANI_API int kani_gemm_tc(int32_t dtype, const void* x, int64_t x_row_stride, const void* residual,
+                     int64_t residual_row_stride, void* residual_out, int64_t residual_out_row_stride,
+                     const void* norm_weight, float eps, const void* weight, int64_t weight_row_stride,
+                     int32_t n_out, int32_t k, int64_t batch, int32_t silu_pairs, void* y,
+                     int64_t y_row_stride, int32_t* err_flag, void* stream);
+
+/*
  * Decode GEMV for up to 8 streams with its neighbours fused:
  *   y[b, r] = round(sum_k a[b, k] * weight[r, k])   (fp32 accumulation)
  * a = x, or with norm_weight the RMSNorm of the residual stream:

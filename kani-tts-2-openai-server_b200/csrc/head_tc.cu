@@ -35,12 +35,9 @@
 //     (order key << 16 | 0xffff - row) with a warp max; one 32-bit atomicMax
 //     per stream and CTA into the scratch; the last CTA (a counter after a
 //     fence) writes the mapped tokens and returns the scratch to zero.
-#include <cuda.h>  // CUtensorMap and its encoder's types (the encoder is fetched at run time)
-
 #include <algorithm>
-#include <mutex>
 
-#include "common.cuh"
+#include "tc_common.cuh"
 
 namespace kani {
 namespace {
@@ -48,15 +45,14 @@ namespace {
 // 16 warps: in the epilogue warp w reads TMEM lane quarter w % 4 (its 32 rows)
 // and column group w / 4 (16 streams), so 64 streams take one pass
 constexpr int kTcThreads = 512;
-constexpr int kTcM = 128;        // head rows per CTA (MMA M)
+constexpr int kTcM = tc::kM;     // head rows per CTA (MMA M)
 constexpr int kTcN = 64;         // most streams (MMA N)
-constexpr int kTcKB = 64;        // hidden elements per tile: one 128-byte swizzle row
+constexpr int kTcKB = tc::kKB;   // hidden elements per tile: one 128-byte swizzle row
 constexpr int kTcMaxStages = 16;
 constexpr int kTcMaxHidden = 1024;
 constexpr uint32_t kTmemCols = 64;  // fp32 accumulators: one column per stream slot
-constexpr uint32_t kABytes = kTcM * kTcKB * 2;  // head rows of one stage
+constexpr uint32_t kABytes = tc::kATileBytes;  // one K tile of the head rows
 constexpr size_t kTcSmemBudget = 230400;          // dynamic shared memory (227 KB less the static part)
-constexpr long long kTcWaitCycles = 2000000000LL;  // ~1 s
 
 struct HeadTcParams {
   CUtensorMap tmap_w;  // head rows: {64, rows, tiles}, box {64, 128, PZ}, 128-byte swizzle
@@ -71,92 +67,10 @@ struct HeadTcParams {
   int32_t* err;
 };
 
-__device__ __forceinline__ uint32_t smem_addr(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-// UMMA shared-memory descriptor for a K-major 128-byte-swizzle operand: start
-// address >> 4, leading offset 1 (unused by this layout), stride offset
-// 1024 bytes >> 4 (the next 8-row atom), version 1, layout type 2.
-__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t addr) {
-  return (uint64_t)((addr >> 4) & 0x3fffu) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) |
-         (2ull << 61);
-}
-
-// kind::f16 instruction descriptor: D fp32, A / B bf16 (1) or fp16 (0), both
-// K-major, N >> 3 at bit 17, M >> 4 at bit 24.
-template <typename T>
-__device__ __forceinline__ uint32_t umma_idesc(int n) {
-  constexpr uint32_t ab = std::is_same_v<T, __nv_bfloat16> ? 1u : 0u;
-  return (1u << 4) | (ab << 7) | (ab << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kTcM >> 4) << 24);
-}
-
-__device__ __forceinline__ void tc_mbar_init(uint32_t bar) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar) : "memory");
-}
-
-__device__ __forceinline__ void tc_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ bool tc_try_wait(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity), "r"(1000000u)
-      : "memory");
-  return ok != 0;
-}
-
-__device__ __forceinline__ bool tc_wait(uint32_t bar, uint32_t parity) {
-  if (tc_try_wait(bar, parity)) return true;
-  const long long start = clock64();
-  while (!tc_try_wait(bar, parity)) {
-    if (clock64() - start > kTcWaitCycles) return false;
-  }
-  return true;
-}
-
-// 3-D TMA tile load {elements, row, tile} into shared memory, completing on
-// an mbarrier; the innermost coordinate is 0 (16-byte aligned); rows past the
-// tensor read as zero.
-__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int row, int tile, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
-      "[%5];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(row), "r"(tile), "r"(bar)
-      : "memory");
-}
-
 // Total-order key of a 16-bit float's bits (ascending with the value; -0 == +0).
 __device__ __forceinline__ uint32_t order_key16(uint32_t b) {
   if ((b & 0x7fffu) == 0) b = 0;
   return b ^ ((b & 0x8000u) ? 0xffffu : 0x8000u);
-}
-
-// Two fp32 values (as bits) rounded to nearest-even 16-bit floats: a in the
-// low half, b in the high half.  bf16 rounds in integer arithmetic — the same
-// bits as the hardware conversion (NaN -> the canonical 0x7fff), which costs
-// about 80 cycles per element in this epilogue where it cannot be hidden.
-__device__ __forceinline__ uint32_t bf16_rne_bits(uint32_t f) {
-  if ((f & 0x7fffffffu) > 0x7f800000u) return 0x7fffu;
-  return (f + 0x7fffu + ((f >> 16) & 1u)) >> 16;
-}
-template <typename T>
-__device__ __forceinline__ uint32_t round_pair(uint32_t a, uint32_t b);
-template <>
-__device__ __forceinline__ uint32_t round_pair<__nv_bfloat16>(uint32_t a, uint32_t b) {
-  return bf16_rne_bits(a) | (bf16_rne_bits(b) << 16);
-}
-template <>
-__device__ __forceinline__ uint32_t round_pair<__half>(uint32_t a, uint32_t b) {
-  const __half2 h = __floats2half2_rn(__uint_as_float(a), __uint_as_float(b));
-  uint32_t u;
-  memcpy(&u, &h, 4);
-  return u;
 }
 
 template <typename T>
@@ -178,20 +92,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) head_tc_kernel(const __grid_con
   const int r0 = blockIdx.x * kTcM;
   // 1024-byte aligned stages (the 128-byte swizzle repeats every 8 rows):
   // stage s = [head rows: PZ tiles of 128 x 128 B][stream rows: PZ tiles of n_mma x 128 B]
-  const uint32_t raw = smem_addr(smem_raw);
+  const uint32_t raw = tc::smem_addr(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   const uint32_t b_bytes = (uint32_t)n_mma * 128u;
   const uint32_t stage_bytes = (uint32_t)PZ * (kABytes + b_bytes);
   auto a_tile = [&](int st) { return base + (uint32_t)st * stage_bytes; };
   auto b_tile = [&](int st) { return a_tile(st) + (uint32_t)PZ * kABytes; };
-  auto load_a = [&](int kb, int st) { tma_load_3d(a_tile(st), &p.tmap_w, r0, kb * PZ, smem_addr(&s_full[st])); };
-  auto load_b = [&](int kb, int st) { tma_load_3d(b_tile(st), &p.tmap_h, 0, kb * PZ, smem_addr(&s_full[st])); };
+  auto load_a = [&](int kb, int st) { tc::tma_load_3d(a_tile(st), &p.tmap_w, r0, kb * PZ, tc::smem_addr(&s_full[st])); };
+  auto load_b = [&](int kb, int st) { tc::tma_load_3d(b_tile(st), &p.tmap_h, 0, kb * PZ, tc::smem_addr(&s_full[st])); };
 
   if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&s_tmem)),
-                 "r"(kTmemCols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    tc::tmem_alloc(&s_tmem, kTmemCols);
   }
   if (tid < kTcN) s_best[tid] = 0u;
   bool failed = false;
@@ -199,17 +110,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) head_tc_kernel(const __grid_con
   if (tid == 0) {
     s_failed = 0;
     for (int st = 0; st < S; ++st) {
-      tc_mbar_init(smem_addr(&s_full[st]));
-      tc_mbar_init(smem_addr(&s_empty[st]));
+      tc::mbar_init(tc::smem_addr(&s_full[st]));
+      tc::mbar_init(tc::smem_addr(&s_empty[st]));
     }
-    tc_mbar_init(smem_addr(&s_done));
+    tc::mbar_init(tc::smem_addr(&s_done));
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.tmap_w)) : "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.tmap_h)) : "memory");
+    tc::prefetch_map(&p.tmap_w);
+    tc::prefetch_map(&p.tmap_h);
     // the head rows of the first stages stream in before the programmatic-launch
     // wait; each stage's barrier expects both of its loads
     for (int st = 0; st < first; ++st) {
-      tc_expect_tx(smem_addr(&s_full[st]), stage_bytes);
+      tc::expect_tx(tc::smem_addr(&s_full[st]), stage_bytes);
       load_a(st, st);
     }
   }
@@ -217,74 +128,65 @@ __global__ void __launch_bounds__(kTcThreads, 1) head_tc_kernel(const __grid_con
   griddep_wait();
   if (tid == 0)
     for (int st = 0; st < first; ++st) load_b(st, st);  // the streams' rows, written by the launch before
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  tc::fence_before_sync();
   __syncthreads();
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  tc::fence_after_sync();
   const uint32_t tmem = s_tmem;
 
   if (tid == 0) {
-    const uint32_t idesc = umma_idesc<T>(n_mma);
+    const uint32_t idesc = tc::idesc_f16<T>(kTcM, n_mma);
     int issued = first;  // tiles whose loads were issued
     int landed = 0;      // ... and whose full barrier was seen
     for (int kb = 0; kb < nkb; ++kb) {
       const int st = kb % S;
-      if (!tc_wait(smem_addr(&s_full[st]), (uint32_t)((kb / S) & 1))) {
+      if (!tc::wait(tc::smem_addr(&s_full[st]), (uint32_t)((kb / S) & 1))) {
         failed = true;
         break;
       }
       landed = kb + 1;
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      tc::fence_after_sync();
       for (int q = 0; q < PZ; ++q) {
         const uint32_t at = a_tile(st) + (uint32_t)q * kABytes, bt = b_tile(st) + (uint32_t)q * b_bytes;
 #pragma unroll
         for (int j = 0; j < kTcKB / 16; ++j) {
-          const uint64_t ad = umma_desc_sw128(at + (uint32_t)j * 32u);
-          const uint64_t bd = umma_desc_sw128(bt + (uint32_t)j * 32u);
+          const uint64_t ad = tc::desc_sw128(at + (uint32_t)j * 32u);
+          const uint64_t bd = tc::desc_sw128(bt + (uint32_t)j * 32u);
           const uint32_t acc = (kb > 0 || q > 0 || j > 0) ? 1u : 0u;
-          asm volatile(
-              "{\n\t.reg .pred p;\n\t"
-              "setp.ne.b32 p, %4, 0;\n\t"
-              "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
-              "l"(ad), "l"(bd), "r"(idesc), "r"(acc)
-              : "memory");
+          tc::mma_f16(tmem, ad, bd, idesc, acc != 0u);
         }
       }
-      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                       smem_addr(&s_empty[st]))
-                   : "memory");
+      tc::commit(tc::smem_addr(&s_empty[st]));
       // refill the stage of tile kb - 1 with tile kb - 1 + S once its MMAs completed
       const int prev = kb - 1;
       if (prev >= 0 && prev + S < nkb) {
         const int ps = prev % S;
-        if (!tc_wait(smem_addr(&s_empty[ps]), (uint32_t)((prev / S) & 1))) {
+        if (!tc::wait(tc::smem_addr(&s_empty[ps]), (uint32_t)((prev / S) & 1))) {
           failed = true;
           break;
         }
-        tc_expect_tx(smem_addr(&s_full[ps]), stage_bytes);
+        tc::expect_tx(tc::smem_addr(&s_full[ps]), stage_bytes);
         load_a(prev + S, ps);
         load_b(prev + S, ps);
         issued = prev + S + 1;
       }
     }
     if (!failed) {
-      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                       smem_addr(&s_done))
-                   : "memory");
+      tc::commit(tc::smem_addr(&s_done));
       // the stage commits no refill waited for (one per stage), so that no
       // arrive is pending on this CTA's shared memory when it exits
       for (int kb = max(0, nkb - S); kb < nkb; ++kb)
-        if (!tc_wait(smem_addr(&s_empty[kb % S]), (uint32_t)((kb / S) & 1))) failed = true;
+        if (!tc::wait(tc::smem_addr(&s_empty[kb % S]), (uint32_t)((kb / S) & 1))) failed = true;
     } else {
       // give copies still in flight a bounded time to land before the CTA exits
       for (int t = landed; t < issued; ++t)
-        if (!tc_wait(smem_addr(&s_full[t % S]), (uint32_t)((t / S) & 1))) break;
+        if (!tc::wait(tc::smem_addr(&s_full[t % S]), (uint32_t)((t / S) & 1))) break;
     }
     if (failed) s_failed = 1;
   }
   __syncthreads();  // thread 0's loop is over: s_failed is final, every MMA is issued
-  const bool ok = !s_failed && tc_wait(smem_addr(&s_done), 0u);
+  const bool ok = !s_failed && tc::wait(tc::smem_addr(&s_done), 0u);
   if (!ok && lane == 0) atomicOr(&s_failed, 1);
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  tc::fence_after_sync();
 
   // ---- epilogue: warp w holds rows r0 + 32 (w % 4) + lane and the stream
   // columns of groups w / 4, w / 4 + 4, ... (16 columns each, up to n_mma)
@@ -295,14 +197,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) head_tc_kernel(const __grid_con
 #pragma unroll 1
   for (int q = warp >> 2; q < n_mma / 16; q += kTcThreads / 128) {  // columns past the MMA width were never written
     uint32_t v[16];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-        "%15}, [%16];\n\t"
-        "tcgen05.wait::ld.sync.aligned;"
-        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-        : "r"(taddr + (uint32_t)(q * 16))
-        : "memory");
+    tc::tmem_ld16(taddr + (uint32_t)(q * 16), v);
     // Round, then build the packed keys with selects only: a data-dependent
     // branch per element (e.g. around the logits store) costs a divergence
     // round trip each, several times the arithmetic.
@@ -310,7 +205,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) head_tc_kernel(const __grid_con
     uint32_t bits[16], pk[16];
 #pragma unroll
     for (int e = 0; e < 16; e += 2) {
-      const uint32_t pair = round_pair<T>(v[e], v[e + 1]);
+      const uint32_t pair = tc::round_pair<T>(v[e], v[e + 1]);
       bits[e] = pair & 0xffffu;
       bits[e + 1] = pair >> 16;
     }
@@ -341,10 +236,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) head_tc_kernel(const __grid_con
     const int col = q * 16 + ((lane >> 1) & 15);
     if ((lane & 1) == 0 && col < p.batch) atomicMax(&s_best[col], col_max);
   }
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  tc::fence_before_sync();
   __syncthreads();
-  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols)
-                              : "memory");
+  if (warp == 0) tc::tmem_free(tmem, kTmemCols);
   if (tid == 0 && s_failed && p.err) atomicOr(p.err, KANI_FLAG_TIMEOUT);
 
   // ---- fold into the per-stream scratch; the last CTA writes the tokens
@@ -366,41 +260,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) head_tc_kernel(const __grid_con
     p.tokens[(int64_t)tid * p.tokens_stride] = p.index_map ? p.index_map[r] : (int64_t)r;
   }
   if (s_last && tid == 0) atomicExch(p.scratch + p.batch, 0u);
-}
-
-// cuTensorMapEncodeTiled, fetched once from the driver through the runtime
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_tiled_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* f = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(f);
-  });
-  return fn;
-}
-
-// Row-major [outer x inner] matrix of 16-bit elements viewed as the 3-D tensor
-// {64 elements, outer rows, inner / 64 tiles} (row stride, tile stride 128 B);
-// box {64, box_rows, pz}, 128-byte swizzle, zero fill past the edges.
-bool encode_rows(CUtensorMap* map, bool bf16, const void* base, int64_t inner, int64_t outer, int64_t row_stride,
-                 int box_rows, int pz) {
-  EncodeTiledFn fn = encode_tiled_fn();
-  if (!fn) return false;
-  const cuuint64_t dims[3] = {(cuuint64_t)kTcKB, (cuuint64_t)outer, (cuuint64_t)(inner / kTcKB)};
-  const cuuint64_t strides[2] = {(cuuint64_t)row_stride * 2u, (cuuint64_t)kTcKB * 2u};
-  const cuuint32_t box[3] = {(cuuint32_t)kTcKB, (cuuint32_t)box_rows, (cuuint32_t)pz};
-  const cuuint32_t estr[3] = {1u, 1u, 1u};
-  return fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
-            const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 size_t head_tc_stage_bytes(int n_mma, int pz) { return (size_t)pz * (kABytes + (size_t)n_mma * 128); }
@@ -453,8 +312,8 @@ extern "C" int kani_head_argmax_tc(int32_t dtype, const void* hidden, int64_t hi
   prm.n_mma = ((int)batch + 15) / 16 * 16;
   prm.pz = (hidden_size / kani::kTcKB) % 2 == 0 ? 2 : 1;
   prm.stages = kani::head_tc_stages(hidden_size, prm.n_mma, prm.pz);
-  if (!kani::encode_rows(&prm.tmap_w, bf16, weight, hidden_size, rows, weight_row_stride, kani::kTcM, prm.pz) ||
-      !kani::encode_rows(&prm.tmap_h, bf16, hidden, hidden_size, batch, hidden_row_stride, prm.n_mma, prm.pz))
+  if (!kani::tc::encode_rows(&prm.tmap_w, bf16, weight, hidden_size, rows, weight_row_stride, kani::kTcM, prm.pz) ||
+      !kani::tc::encode_rows(&prm.tmap_h, bf16, hidden, hidden_size, batch, hidden_row_stride, prm.n_mma, prm.pz))
     return KANI_ERR_UNSUPPORTED;
   prm.index_map = index_map;
   prm.logits = logits_out;

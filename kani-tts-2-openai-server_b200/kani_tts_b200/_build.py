@@ -22,7 +22,7 @@ LIB_PATH = LIB_DIR / "libkani_b200.so"
 
 SOURCES = ["capi.cu", "rms_norm.cu", "silu_mul.cu", "rope_kv.cu", "decode_attn.cu", "short_conv.cu",
            "sampling.cu", "head_argmax.cu", "codec_codes.cu", "gemv.cu",
-           "decode_advance.cu", "head_tc.cu"]
+           "decode_advance.cu", "head_tc.cu", "gemm_tc.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -72,6 +72,8 @@ _SIGNATURES = {
                                   _c_p, _c_p, _c_i64, _c_p, _c_i64, _c_p], ctypes.c_int),
     "kani_head_argmax_tc": ([_c_i32, _c_p, _c_i64, _c_i64, _c_i32, _c_p, _c_i64, _c_i32,
                              _c_p, _c_p, _c_i64, _c_p, _c_p, _c_i64, _c_p, _c_p], ctypes.c_int),
+    "kani_gemm_tc": ([_c_i32, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_f32, _c_p, _c_i64,
+                      _c_i32, _c_i32, _c_i64, _c_i32, _c_p, _c_i64, _c_p, _c_p], ctypes.c_int),
     "kani_gemv": ([_c_i32, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_f32, _c_p, _c_i64,
                    _c_i32, _c_i32, _c_i64, _c_i32, _c_p, _c_i64, _c_p], ctypes.c_int),
     "kani_gemv_short_conv": ([_c_i32, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_f32, _c_p, _c_i64,

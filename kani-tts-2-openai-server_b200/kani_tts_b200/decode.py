@@ -22,10 +22,15 @@
   and the reduced-to-full map): ``head_argmax`` (CUDA-core GEMV) up to 8
   streams, ``head_argmax_tc`` (tcgen05 tensor-core GEMM) from 9 to 64; sampled
   steps take their logits from the same launch;
-* up to 8 streams, every projection is a ``gemv`` launch that folds in the
-  residual add + RMSNorm before it and the SiLU·mul after the gate/up GEMV.
+* up to 4 streams, every projection is a ``gemv`` launch that folds in the
+  residual add + RMSNorm before it and the SiLU·mul after the gate/up GEMV;
+* otherwise up to 32 streams, every projection is a ``gemm_tc`` launch
+  (tcgen05 tensor cores): the gate/up one with the SiLU·mul as its epilogue,
+  the 1024-row output projections with K split over a thread-block cluster,
+  and up to 8 streams the residual add + RMSNorm as the input projections'
+  prologue.
 
-Beyond 8 streams the GEMMs are cuBLAS calls; prefill attention is PyTorch SDPA.
+Beyond 32 streams every GEMM is a cuBLAS call; prefill attention is PyTorch SDPA.
 
 ``DecodeEngine`` adds batched prefill (the same kernels at T tokens per
 stream, causal SDPA, causal depthwise conv) and a CUDA-graph decode loop
@@ -44,7 +49,7 @@ import torch.nn.functional as F
 
 from . import _lib
 from .fused_kernels import (decode_advance, decode_attention, fused_add_rms_norm, fused_rms_norm,
-                            fused_rope_kv_write, fused_silu_mul, gemv, gemv_rope_kv_write, gemv_short_conv,
+                            fused_rope_kv_write, fused_silu_mul, gemm_tc, gemv, gemv_rope_kv_write, gemv_short_conv,
                             head_argmax, head_argmax_tc, sample_tokens, short_conv_step)
 from .model import LFM2Config
 from .positions import learnable_inv_freq
@@ -136,12 +141,25 @@ class FusedDecoder:
         # cuBLAS, so it serves up to 4 streams.
         self.small_batch = (batch <= 4 and h == 1024 and cfg.intermediate_size in (1024, 4608)
                             and self.q_dim == h and cfg.conv_L_cache == 3)
+        # up to 32 streams not on the fused-GEMV path: every projection runs on the
+        # tensor-core GEMM (the gate/up one with the SiLU·mul as its epilogue, the
+        # 1024-row ones with K split over a cluster).  Measured per step on B200
+        # against cuBLAS + separate launches: 696 vs 767 us at 8 streams, 726 vs 781
+        # at 16, 743 vs 741 at 32, 816 vs 731 at 64 (there every CTA also streams
+        # the 128 KB activation operand from L2, half again its weight bytes).
+        self.tc_batch = (not self.small_batch and batch <= 32 and h % 64 == 0 and h <= 1024
+                         and cfg.intermediate_size % 8 == 0)
         self.res_buf = [torch.empty(batch, 1, h, dtype=self.dtype, device=dev) for _ in range(2)]
         self.logits_buf = torch.empty(batch, 1, self.head.shape[0], dtype=self.dtype, device=dev)
         self.argmax_buf = torch.empty(batch, dtype=torch.long, device=dev)
 
     # ------------------------------------------------------------ decode
     fused_greedy_head = True   # greedy / sampled steps may use the fused head kernels
+    tc_output_projections = True  # tensor-core path: o / out / down projections on gemm_tc (split K) too
+    # The norm prologue re-reads every stream's row in every CTA (from L2); beyond
+    # this many streams a separate add + RMSNorm launch is cheaper (measured: equal
+    # at 8 streams, 58 us per step slower at 16).
+    tc_norm_prologue_max_batch = 8
 
     def step(self, input_ids: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor,
              kv_len: torch.Tensor, mask: torch.Tensor | None = None) -> torch.Tensor:
@@ -191,6 +209,8 @@ class FusedDecoder:
         """The decode layers and the final norm: [B, 1, H]."""
         if self.small_batch:
             return self._final_hidden_small(input_ids, positions, slots, kv_len)
+        if self.tc_batch:
+            return self._final_hidden_tc(input_ids, positions, slots, kv_len)
         return self._final_hidden_large(input_ids, positions, slots, kv_len)
 
     def _final_hidden_small(self, input_ids, positions, slots, kv_len) -> torch.Tensor:
@@ -261,6 +281,59 @@ class FusedDecoder:
                 delta = self._conv_step(i, L, normed)
             normed, hidden = fused_add_rms_norm(delta, hidden, L["ffn_norm"], self.eps)
             delta = F.linear(fused_silu_mul(F.linear(normed, L["gate_up"])), L["down"])
+        normed, _ = fused_add_rms_norm(delta, hidden, self.final_norm, self.eps)
+        return normed
+
+    def _final_hidden_tc(self, input_ids, positions, slots, kv_len) -> torch.Tensor:
+        """Up to 64 streams: tensor-core input and gate/up projections with the residual
+        add + RMSNorm (and the SiLU·mul) fused in; output projections on the
+        tensor-core GEMM with K split over a cluster (or cuBLAS).  The residual
+        stream alternates between the two static buffers."""
+        b, hq, hk, d = self.batch, self.hq, self.hk, self.d
+        hidden = F.embedding(input_ids, self.embed)              # [B, 1, H] residual stream
+        delta, ri = None, 0
+        common = dict(eps=self.eps, err_flag=self.err_flag)
+        if self.tc_output_projections:
+            def proj(a, w):
+                return gemm_tc(a, w, err_flag=self.err_flag)
+        else:
+            proj = F.linear
+        fused_norm = b <= self.tc_norm_prologue_max_batch
+
+        def normed_input(delta, hidden, w, ri):
+            """(GEMM input, norm keyword arguments, residual stream after the step, ri)."""
+            if fused_norm:
+                if delta is None:
+                    return hidden, dict(norm_weight=w), hidden, ri
+                return delta, dict(norm_weight=w, residual=hidden, residual_out=self.res_buf[ri]), \
+                    self.res_buf[ri], ri ^ 1
+            if delta is None:
+                return fused_rms_norm(hidden, w, self.eps), {}, hidden, ri
+            normed, new_hidden = fused_add_rms_norm(delta, hidden, w, self.eps, residual_out=self.res_buf[ri])
+            return normed, {}, new_hidden, ri ^ 1
+
+        for i, L in enumerate(self.layers):
+            x_in, norm_kw, hidden_next, ri = normed_input(delta, hidden, L["op_norm"], ri)
+            if L["attn"]:
+                qkv = gemm_tc(x_in, L["qkv"], **norm_kw, **common)
+                hidden = hidden_next
+                q, k, v = qkv.split([self.q_dim, self.kv_dim, self.kv_dim], dim=-1)
+                q_rot = fused_rope_kv_write(
+                    q.view(b, 1, hq, d), k.view(b, 1, hk, d), v.view(b, 1, hk, d), L["inv_freq"], positions,
+                    self.k_cache[i], self.v_cache[i], slots, frame_table=self.frame_table,
+                    tokens_per_frame=self.cfg.tokens_per_frame, q_norm_w=L["q_norm"], k_norm_w=L["k_norm"],
+                    eps=self.eps, err_flag=self.err_flag)
+                attn = decode_attention(q_rot, self.k_cache[i], self.v_cache[i], kv_len, self.scale,
+                                        err_flag=self.err_flag)
+                delta = proj(attn.view(b, 1, self.q_dim), L["o"])
+            else:
+                bcx = gemm_tc(x_in, L["in_proj"], **norm_kw, **common)
+                hidden = hidden_next
+                delta = proj(short_conv_step(bcx, self.conv_state[i], L["conv_w"]), L["out_proj"])
+            x_in, norm_kw, hidden_next, ri = normed_input(delta, hidden, L["ffn_norm"], ri)
+            act = gemm_tc(x_in, L["gate_up"], silu_pairs=True, **norm_kw, **common)
+            hidden = hidden_next
+            delta = proj(act, L["down"])
         normed, _ = fused_add_rms_norm(delta, hidden, self.final_norm, self.eps)
         return normed
 

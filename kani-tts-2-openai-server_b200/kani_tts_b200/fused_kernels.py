@@ -44,6 +44,7 @@ __all__ = [
     "sample_tokens",
     "head_argmax",
     "head_argmax_tc",
+    "gemm_tc",
     "codec_codes",
     "gemv",
     "gemv_short_conv",
@@ -567,6 +568,71 @@ def gemv(x: torch.Tensor, weight: torch.Tensor, *, norm_weight: torch.Tensor | N
                         ptr(norm_weight) if norm_weight is not None else None, float(eps), ptr(weight),
                         weight.stride(0), n, k, b, 1 if silu_pairs else 0, ptr(out), ys, stream_ptr(x.device)),
           "kani_gemv")
+    return out
+
+
+def gemm_tc(x: torch.Tensor, weight: torch.Tensor, *, norm_weight: torch.Tensor | None = None,
+            residual: torch.Tensor | None = None, residual_out: torch.Tensor | None = None, eps: float = 1e-5,
+            silu_pairs: bool = False, out: torch.Tensor | None = None,
+            err_flag: torch.Tensor | None = None) -> torch.Tensor:
+    """``gemv``'s operation for up to 64 streams on the tensor cores
+    (``kani_gemm_tc``): the decode step's F.linear (optimized_decode.py:215, 255,
+    276, 281-282) with the residual add + RMSNorm before it and (``silu_pairs``)
+    the SiLU·mul after it, in one launch.
+
+    Args:
+        x: [B, K] or [B, 1, K] input (with ``norm_weight``, the residual-stream
+            update that is added to ``residual`` and normalised); K a multiple of
+            64, at most 1024 with ``norm_weight``.
+        weight: [N, K] ([2N, K], gate rows then up rows, with ``silu_pairs``).
+        residual_out: receives round(x + residual) (must not alias x or residual).
+        err_flag: optional int32 device word for KANI_FLAG_TIMEOUT.
+    Returns:
+        [B, N] (or [B, 1, N] for a [B, 1, K] input).
+    """
+    require_cuda(x, "x")
+    require_cuda(weight, "weight")
+    lib = load_library()
+    code = dtype_code(x, "x")
+    k = x.shape[-1]
+    if weight.dim() != 2 or weight.shape[1] != k or weight.dtype != x.dtype:
+        raise ValueError(f"weight must be [N, {k}] of the input dtype")
+    if weight.stride(1) != 1:
+        weight = weight.contiguous()
+    n = weight.shape[0] // 2 if silu_pairs else weight.shape[0]
+    if silu_pairs and weight.shape[0] % 2:
+        raise ValueError("silu_pairs needs an even number of weight rows")
+    xv, b, xs = _rows_view(x, k)
+    rv, rs, ov, os_ = None, 0, None, 0
+    if residual is not None:
+        require_cuda(residual, "residual")
+        rv, rb, rs = _rows_view(residual, k)
+        if rb != b:
+            raise ValueError("residual must have the input's rows")
+    if residual_out is not None:
+        require_cuda(residual_out, "residual_out")
+        if residual_out.shape[-1] != k or residual_out.stride(-1) != 1 or residual_out.numel() != b * k:
+            raise ValueError(f"residual_out must be [{b}, {k}] with unit stride")
+        ov, _, os_ = _rows_view(residual_out, k)
+    if norm_weight is not None:
+        require_cuda(norm_weight, "norm_weight")
+        if norm_weight.numel() != k or norm_weight.dtype != x.dtype:
+            raise ValueError(f"norm_weight must be [{k}] of the input dtype")
+        norm_weight = norm_weight.contiguous()
+    if out is None:
+        out = torch.empty(*x.shape[:-1], n, dtype=x.dtype, device=x.device)
+    ov2, ob, ys = _rows_view(out, n)
+    if ob != b or ov2.data_ptr() != out.data_ptr():
+        raise ValueError(f"out must be [{b}, {n}] rows with a uniform stride")
+    if err_flag is not None:
+        require_cuda(err_flag, "err_flag")
+        if err_flag.dtype != torch.int32:
+            raise ValueError("err_flag must be an int32 device tensor")
+    check(lib.kani_gemm_tc(code, ptr(xv), xs, ptr(rv) if rv is not None else None, rs,
+                           ptr(ov) if ov is not None else None, os_,
+                           ptr(norm_weight) if norm_weight is not None else None, float(eps), ptr(weight),
+                           weight.stride(0), n, k, b, 1 if silu_pairs else 0, ptr(out), ys,
+                           ptr(err_flag) if err_flag is not None else None, stream_ptr(x.device)), "kani_gemm_tc")
     return out
 
 

@@ -32,6 +32,16 @@ def same_argmax(got, ref):
     assert torch.equal(got.float().cpu().argmax(-1), ref.float().cpu().argmax(-1))
 
 
+def same_argmax_where_clear(got, ref, rel=2.0 ** -5):
+    """Equal argmax for every row whose reference top-2 margin exceeds rel x |top|
+    (a near-tie may flip under a different accumulation order)."""
+    g, r = got.float().cpu().flatten(0, -2), ref.float().cpu().flatten(0, -2)
+    top2 = r.topk(2, dim=-1).values
+    clear = (top2[:, 0] - top2[:, 1]) > rel * top2[:, 0].abs()
+    assert bool(clear.any())
+    assert torch.equal(g.argmax(-1)[clear], r.argmax(-1)[clear])
+
+
 def test_fused_decoder_matches_reference_decoder_golden():
     c = load("decode_step")["tiny"]
     cfg = tiny_config()
@@ -57,10 +67,12 @@ def test_fused_decoder_matches_reference_decoder_golden():
     assert int(dec.err_flag.item()) == 0
 
 
-@pytest.mark.parametrize("full", [False, True])
-def test_batched_fused_step_matches_oracle(full):
+@pytest.mark.parametrize("full,b", [(False, 3), (True, 2), (True, 16)])
+def test_batched_fused_step_matches_oracle(full, b):
+    """One decode step against the oracle decoder: 2 streams take the fused-GEMV
+    path, 3 (tiny model) and 16 streams the tensor-core GEMM path."""
     cfg = LFM2Config() if full else tiny_config()
-    b, max_len = (2, 64) if full else (3, 32)
+    max_len = 64 if full else 32
     sd = synthetic_state_dict(cfg, seed=7)
     dec = FusedDecoder(cfg, sd, DEV, batch=b, max_len=max_len)
     ora = OracleDecoder(cfg, sd, batch=b, max_len=max_len)
@@ -77,8 +89,8 @@ def test_batched_fused_step_matches_oracle(full):
         dec.conv_state[i].copy_(cs)
         ora.conv_state[i].copy_(cs)
     ids = torch.randint(cfg.audio_tokens_start, cfg.vocab_size, (b, 1), generator=g)
-    pos = torch.tensor([10, 17, 3][:b])
-    slots = torch.tensor([20, 25, 9][:b])
+    pos = torch.tensor([10, 17, 3] + [(7 * s) % 40 for s in range(3, b)])[:b]
+    slots = torch.tensor([20, 25, 9] + [(11 * s) % 50 + 1 for s in range(3, b)])[:b]
     mask = torch.full((b, 1, 1, max_len), float("-inf"), dtype=torch.bfloat16)
     for s in range(b):
         mask[s, ..., : int(slots[s]) + 1] = 0
@@ -88,13 +100,51 @@ def test_batched_fused_step_matches_oracle(full):
     close(got, ref, 0.05 if full else 0.02)
     cos = torch.nn.functional.cosine_similarity(got.float().cpu().flatten(1), ref.float().flatten(1))
     assert float(cos.min()) > 0.999
-    same_argmax(got, ref)
+    if b <= 3:
+        same_argmax(got, ref)
+    else:   # 16 streams x 15591 logits: compare where the maximum is not a near-tie
+        same_argmax_where_clear(got, ref)
     tol = 0.05 if full else 0.02
     for i in cfg.attn_layers:
         for s in range(b):
             sl = int(slots[s])
             close(dec.k_cache[i][s, :, sl], ora.k_cache[i][s, :, sl], tol)
             close(dec.v_cache[i][s, :, sl], ora.v_cache[i][s, :, sl], tol)
+
+
+@pytest.mark.parametrize("b", [8, 16])
+def test_tensor_core_layers_match_cublas_layers(b):
+    """The step through the tensor-core GEMMs (SiLU·mul fused, split-K output
+    projections; at 8 streams also the norm prologue) and through cuBLAS +
+    separate norm / SiLU launches: same logits within the GEMM rounding
+    tolerance, same conv states."""
+    cfg = LFM2Config()
+    max_len = 48
+    sd = synthetic_state_dict(cfg, seed=8)
+    a = FusedDecoder(cfg, sd, DEV, batch=b, max_len=max_len)
+    c = FusedDecoder(cfg, sd, DEV, batch=b, max_len=max_len)
+    assert a.tc_batch
+    c.tc_batch = False
+    g = torch.Generator().manual_seed(9)
+    for i in cfg.attn_layers:
+        kp = torch.randn(b, cfg.num_key_value_heads, max_len, cfg.head_dim, generator=g).bfloat16().to(DEV)
+        a.k_cache[i].copy_(kp)
+        c.k_cache[i].copy_(kp)
+    for i in a.conv_state:
+        cs = torch.randn(b, cfg.hidden_size, cfg.conv_L_cache, generator=g).bfloat16().to(DEV)
+        a.conv_state[i].copy_(cs)
+        c.conv_state[i].copy_(cs)
+    ids = torch.randint(cfg.audio_tokens_start, cfg.vocab_size, (b, 1), generator=g).to(DEV)
+    pos = torch.arange(b, device=DEV) * 2 + 3
+    slots = pos + 1
+    la = a.step(ids, pos, slots, slots + 1)
+    lc = c.step(ids, pos, slots, slots + 1)
+    close(la, lc, 0.05)
+    cos = torch.nn.functional.cosine_similarity(la.float().flatten(1), lc.float().flatten(1))
+    assert float(cos.min()) > 0.999
+    for i in a.conv_state:
+        close(a.conv_state[i], c.conv_state[i], 0.05)
+    assert int(a.err_flag.item()) == 0
 
 
 def test_prefill_matches_token_by_token_decode():

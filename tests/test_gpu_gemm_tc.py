@@ -1,0 +1,145 @@
+"""GPU parity of the tensor-core decode projection (``kani_gemm_tc``, 2..64
+streams) against the oracle composition ``gemv_ref`` (optional residual add +
+RMSNorm, the float64 dot rounded once, optional SiLU·mul).
+
+Tolerances (as for the CUDA-core GEMV):
+  * plain / norm outputs within 1 ULP of the oracle, or within 2^-16 x sum |a w|
+    where the products cancel towards zero; >= 97 % identical;
+  * SiLU·mul outputs: bit-identical to the library's SiLU·mul kernel applied to
+    the plain tensor-core GEMM's gate|up output (same accumulation order); against
+    the oracle, the gate and up products each carry the plain tolerance
+    (delta = max(1 ULP, 2^-16 x sum |a w|)), which the product propagates:
+    |y - ref| <= 1.1 |u| delta_g + |g| delta_u + 2 ULP(ref) (|silu'| <= 1.1,
+    |silu(g)| <= |g|); >= 97 % identical;
+  * the residual sum round(x + residual) bit-exact.
+"""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from oracle import kani_oracle as O
+
+from kani_tts_b200 import fused_kernels as K
+from kani_tts_b200._lib import KaniError
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+
+
+def rnd(shape, seed, dtype=torch.bfloat16, std=1.0):
+    g = torch.Generator().manual_seed(seed)
+    return (std * torch.randn(shape, generator=g)).to(dtype)
+
+
+def run_case(b, k, n, mode, dtype=torch.bfloat16, seed=0):
+    silu = mode.endswith("silu")
+    norm = mode != "plain"
+    x = rnd((b, 1, k), 1700 + b + seed, dtype)
+    w = rnd((2 * n if silu else n, k), 1701 + seed, dtype, std=0.03)
+    nw = (1.0 + 0.1 * rnd((k,), 1702, torch.float32)).to(dtype) if norm else None
+    res = rnd((b, 1, k), 1703 + seed, dtype) if mode.startswith("add") else None
+    h_out = torch.empty(b, 1, k, dtype=dtype, device=DEV) if res is not None else None
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    y = K.gemm_tc(x.to(DEV), w.to(DEV), norm_weight=nw.to(DEV) if nw is not None else None,
+                  residual=res.to(DEV) if res is not None else None, residual_out=h_out, silu_pairs=silu,
+                  err_flag=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    ref, h_ref = O.gemv_ref(x, w, nw, res, 1e-5, silu)
+    assert y.shape == (b, 1, n)
+    d = O.ulp_distance(y.cpu(), ref)
+    a_ref = x if nw is None else (O.add_rms_norm_ref(x, res, nw, 1e-5)[0] if res is not None
+                                 else O.rms_norm_ref(x, nw, 1e-5))
+    mag = (a_ref.double().abs().reshape(b, k) @ w.double().abs().T)
+    if silu:
+        pre, _ = O.gemv_ref(x, w, nw, res, 1e-5, False)            # oracle gate | up, rounded
+        g, u = pre.double().reshape(b, 2 * n)[:, :n], pre.double().reshape(b, 2 * n)[:, n:]
+        mg, mu = mag[:, :n], mag[:, n:]
+        ulp = lambda t: (t.abs() * 2.0 ** -7).clamp_min(2.0 ** -133)  # noqa: E731  (bf16: 8 significant bits)
+        dg = torch.maximum(ulp(g), mg * 2.0 ** -16)
+        du = torch.maximum(ulp(u), mu * 2.0 ** -16)
+        refd = ref.double().reshape(b, n)
+        bound = 1.1 * u.abs() * dg + g.abs() * du + 2 * ulp(refd)
+        ok = (d.reshape(b, n) <= 2) | ((y.cpu().double().reshape(b, n) - refd).abs() <= bound)
+        # the epilogue itself: bit-identical to the SiLU kernel on the plain GEMM's output
+        both = K.gemm_tc(x.to(DEV), w.to(DEV), norm_weight=nw.to(DEV) if nw is not None else None,
+                         residual=res.to(DEV) if res is not None else None)
+        assert torch.equal(y, K.fused_silu_mul(both))
+    else:
+        err_abs = (y.cpu().double() - ref.double()).abs().reshape(b, n)
+        ok = (d.reshape(b, n) <= 1) | (err_abs <= mag * 2.0 ** -16)
+    assert bool(ok.all()), f"max ULP {int(d.max())}, {int((~ok).sum())} outside"
+    assert float((d == 0).float().mean()) >= 0.97
+    if h_out is not None:
+        assert torch.equal(h_out.cpu(), h_ref)
+
+
+@pytest.mark.parametrize("b", [2, 9, 16, 33, 64])
+@pytest.mark.parametrize("mode,k,n", [("plain", 1024, 2048), ("plain", 4608, 1024), ("norm", 1024, 3072),
+                                      ("add_norm", 1024, 2048), ("add_norm_silu", 1024, 4608)])
+def test_gemm_tc_vs_oracle(b, mode, k, n):
+    run_case(b, k, n, mode)
+
+
+@pytest.mark.parametrize("mode,k,n", [("plain", 640, 200), ("add_norm", 576, 136), ("add_norm_silu", 128, 72),
+                                      ("norm_silu", 1024, 8)])
+def test_gemm_tc_ragged_shapes(mode, k, n):
+    """Partial row tiles, an odd tile count (K = 576, 9 tiles), tiny K, one gate/up group."""
+    run_case(5, k, n, mode, seed=3)
+    run_case(64, k, n, mode, seed=4)
+
+
+def test_gemm_tc_fp16():
+    run_case(24, 1024, 1024, "add_norm", dtype=torch.float16)
+    run_case(24, 1024, 512, "add_norm_silu", dtype=torch.float16)
+
+
+def test_gemm_tc_graph_replay_and_limits():
+    """Captured in a CUDA graph and replayed on new inputs; unsupported shapes refused."""
+    b, k, n = 40, 1024, 4608
+    w = rnd((2 * n, k), 1710, std=0.03).to(DEV)
+    nw = (1.0 + 0.1 * rnd((k,), 1711, torch.float32)).to(torch.bfloat16).to(DEV)
+    x = torch.zeros(b, 1, k, dtype=torch.bfloat16, device=DEV)
+    r = torch.zeros_like(x)
+    h = torch.empty_like(x)
+    y = torch.empty(b, 1, n, dtype=torch.bfloat16, device=DEV)
+    s = torch.cuda.Stream(device=DEV)
+    s.wait_stream(torch.cuda.current_stream(DEV))
+    with torch.cuda.stream(s):
+        K.gemm_tc(x, w, norm_weight=nw, residual=r, residual_out=h, silu_pairs=True, out=y)
+    torch.cuda.current_stream(DEV).wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        K.gemm_tc(x, w, norm_weight=nw, residual=r, residual_out=h, silu_pairs=True, out=y)
+    for seed in (1712, 1713):
+        xv, rv = rnd((b, 1, k), seed), rnd((b, 1, k), seed + 10)
+        x.copy_(xv)
+        r.copy_(rv)
+        g.replay()
+        torch.cuda.synchronize()
+        ref, h_ref = O.gemv_ref(xv, w.cpu(), nw.cpu(), rv, 1e-5, True)
+        assert torch.equal(y, K.fused_silu_mul(K.gemm_tc(xv.to(DEV), w, norm_weight=nw, residual=rv.to(DEV))))
+        assert float((O.ulp_distance(y.cpu(), ref) == 0).float().mean()) >= 0.97
+        assert torch.equal(h.cpu(), h_ref)
+    with pytest.raises(KaniError):
+        K.gemm_tc(rnd((65, k), 1714).to(DEV), w[:n])                        # more than 64 streams
+    with pytest.raises(KaniError):
+        K.gemm_tc(rnd((4, 2048), 1715).to(DEV), rnd((64, 2048), 1716).to(DEV), norm_weight=torch.ones(
+            2048, dtype=torch.bfloat16, device=DEV))                       # norm prologue above K = 1024
+
+
+def test_gemm_tc_matches_gemv_closely():
+    """Same operation as the CUDA-core GEMV: identical outputs but for the last
+    bit where the two accumulation orders round differently."""
+    b, k, n = 8, 1024, 4608
+    x = rnd((b, 1, k), 1720).to(DEV)
+    r = rnd((b, 1, k), 1721).to(DEV)
+    nw = (1.0 + 0.1 * rnd((k,), 1722, torch.float32)).to(torch.bfloat16).to(DEV)
+    w = rnd((2 * n, k), 1723, std=0.03).to(DEV)
+    ha, hb = torch.empty_like(x), torch.empty_like(x)
+    ya = K.gemv(x, w, norm_weight=nw, residual=r, residual_out=ha, silu_pairs=True)
+    yb = K.gemm_tc(x, w, norm_weight=nw, residual=r, residual_out=hb, silu_pairs=True)
+    torch.cuda.synchronize()
+    assert torch.equal(ha, hb)
+    assert float((ya == yb).float().mean()) >= 0.95

@@ -108,6 +108,14 @@ def test_abi_rejects_bad_arguments_without_launching():
     assert lib.kani_head_argmax_tc(0, fake, 1024, 9, 1024, fake, 1024, 100, n, n, 0, fake, fake, 1, n, n) == -3
     assert lib.kani_head_argmax_tc(1, fake, 1000, 9, 1000, fake, 1000, 100, n, n, 0, fake, fake, 1, n, n) == -3
     assert lib.kani_head_argmax_tc(1, fake, 1024, 9, 1024, fake, 1024, 100, n, n, 0, n, fake, 1, n, n) == -1
+    # tensor-core GEMM: batch above 64, norm prologue above K = 1024, residual without a norm, silu n % 8
+    assert lib.kani_gemm_tc(1, fake, 1024, n, 0, n, 0, n, 1e-5, fake, 1024, 64, 1024, 65, 0, fake, 64, n, n) == -3
+    assert lib.kani_gemm_tc(1, fake, 2048, n, 0, n, 0, fake, 1e-5, fake, 2048, 64, 2048, 4, 0, fake, 64, n,
+                            n) == -3
+    assert lib.kani_gemm_tc(1, fake, 1024, fake, 1024, n, 0, n, 1e-5, fake, 1024, 64, 1024, 4, 0, fake, 64, n,
+                            n) == -1
+    assert lib.kani_gemm_tc(1, fake, 1024, n, 0, n, 0, fake, 1e-5, fake, 1024, 60, 1024, 4, 1, fake, 64, n,
+                            n) == -3
     # fused GEMV: a residual without a norm, residual_out aliasing the residual, batch above 8, K unsupported
     assert lib.kani_gemv(1, fake, 1024, fake, 1024, n, 0, n, 1e-5, fake, 1024, 64, 1024, 1, 0, fake, 64, n) == -1
     assert lib.kani_gemv(1, fake, 1024, fake, 1024, fake, 1024, fake, 1e-5, fake, 1024, 64, 1024, 1, 0, fake, 64,
@@ -139,6 +147,7 @@ def test_abi_zero_sized_calls_are_noops():
                                   n, 1, n) == 0
     assert lib.kani_head_argmax(1, n, 0, 0, 1024, n, 1024, 15591, n, n, 0, n, n, 1, n) == 0
     assert lib.kani_head_argmax_tc(1, n, 0, 0, 1024, n, 1024, 15591, n, n, 0, n, n, 1, n, n) == 0
+    assert lib.kani_gemm_tc(1, n, 0, n, 0, n, 0, n, 1e-5, n, 1024, 64, 1024, 0, 0, n, 64, n, n) == 0
     assert lib.kani_codec_codes(n, 0, 0, 100, 64402, 64410, 4032, n, 25, n, n, n) == 0
     assert lib.kani_launch_count() == before
 

@@ -11,6 +11,7 @@ import os
 import shutil
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 PKG_DIR = Path(__file__).resolve().parent
@@ -56,16 +57,22 @@ def build_library(force: bool = False, verbose: bool = False, ptxas_report: bool
     obj_dir = PKG_DIR.parent / "_build"
     obj_dir.mkdir(exist_ok=True)
     LIB_DIR.mkdir(exist_ok=True)
-    objs = []
-    for src in SOURCES:
+    def compile_one(src: str):
         obj = obj_dir / (Path(src).stem + ".o")
         cmd = [nvcc, *NVCC_FLAGS, "-I", str(INCLUDE_DIR), "-I", str(CSRC_DIR), "-c",
                str(CSRC_DIR / src), "-o", str(obj)]
         if ptxas_report:
             cmd[1:1] = ["-Xptxas", "-v"]
+        return src, obj, cmd, subprocess.run(cmd, capture_output=True, text=True)
+
+    # one nvcc per source, as many at once as there are cores
+    workers = max(1, min(len(SOURCES), os.cpu_count() or 1))
+    with ThreadPoolExecutor(max_workers=workers) as pool:
+        results = list(pool.map(compile_one, SOURCES))
+    objs = []
+    for src, obj, cmd, res in results:
         if verbose:
             print(" ".join(cmd), flush=True)
-        res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:
             raise RuntimeError(f"nvcc failed on {src}:\n{res.stdout}\n{res.stderr}")
         if ptxas_report or verbose:

@@ -34,7 +34,7 @@ def rnd(shape, seed, dtype=torch.bfloat16, std=1.0):
 
 def run_case(b, k, n, mode, dtype=torch.bfloat16, seed=0):
     silu = mode.endswith("silu")
-    norm = mode != "plain"
+    norm = mode not in ("plain", "silu")
     x = rnd((b, 1, k), 1700 + b + seed, dtype)
     w = rnd((2 * n if silu else n, k), 1701 + seed, dtype, std=0.03)
     nw = (1.0 + 0.1 * rnd((k,), 1702, torch.float32)).to(dtype) if norm else None
@@ -62,10 +62,17 @@ def run_case(b, k, n, mode, dtype=torch.bfloat16, seed=0):
         refd = ref.double().reshape(b, n)
         bound = 1.1 * u.abs() * dg + g.abs() * du + 2 * ulp(refd)
         ok = (d.reshape(b, n) <= 2) | ((y.cpu().double().reshape(b, n) - refd).abs() <= bound)
-        # the epilogue itself: bit-identical to the SiLU kernel on the plain GEMM's output
-        both = K.gemm_tc(x.to(DEV), w.to(DEV), norm_weight=nw.to(DEV) if nw is not None else None,
-                         residual=res.to(DEV) if res is not None else None)
-        assert torch.equal(y, K.fused_silu_mul(both))
+        if norm:
+            # the epilogue itself: bit-identical to the SiLU kernel on the plain GEMM's output
+            # (with a norm prologue neither call splits K, so both sum in the same order)
+            both = K.gemm_tc(x.to(DEV), w.to(DEV), norm_weight=nw.to(DEV) if nw is not None else None,
+                             residual=res.to(DEV) if res is not None else None)
+            assert torch.equal(y, K.fused_silu_mul(both))
+        else:
+            # streamed activations: the plain GEMM of gate | up may split K where the SiLU·mul
+            # one does not, so the check here is the oracle bound above and a repeat call
+            again = K.gemm_tc(x.to(DEV), w.to(DEV), silu_pairs=True)
+            assert torch.equal(y, again)
     else:
         err_abs = (y.cpu().double() - ref.double()).abs().reshape(b, n)
         ok = (d.reshape(b, n) <= 1) | (err_abs <= mag * 2.0 ** -16)
@@ -82,8 +89,18 @@ def test_gemm_tc_vs_oracle(b, mode, k, n):
     run_case(b, k, n, mode)
 
 
+@pytest.mark.parametrize("b", [9, 33, 64])
+@pytest.mark.parametrize("mode,k,n", [("silu", 1024, 4608), ("silu", 4608, 1024), ("plain", 1024, 3072),
+                                      ("plain", 1024, 1024), ("plain", 192, 1024), ("plain", 1152, 512)])
+def test_gemm_tc_split_k(b, mode, k, n):
+    """Streamed activations (no norm prologue): plain projections with few row
+    tiles split K over a 2-8 CTA cluster (K tiles 16, 18 and 72; 3 K tiles do
+    not split), and the SiLU·mul epilogue fed by streamed activations."""
+    run_case(b, k, n, mode, seed=7)
+
+
 @pytest.mark.parametrize("mode,k,n", [("plain", 640, 200), ("add_norm", 576, 136), ("add_norm_silu", 128, 72),
-                                      ("norm_silu", 1024, 8)])
+                                      ("norm_silu", 1024, 8), ("silu", 576, 136), ("silu", 128, 8)])
 def test_gemm_tc_ragged_shapes(mode, k, n):
     """Partial row tiles, an odd tile count (K = 576, 9 tiles), tiny K, one gate/up group."""
     run_case(5, k, n, mode, seed=3)

@@ -60,11 +60,12 @@ struct GemvParams {
 constexpr int kConvL = 3;  // the LFM2 short-conv kernel length the fused epilogue serves
 
 // The B GEMV input rows into shared memory (as, [B][K]); with NORM the
-// residual add (h written to res_out by CTA 0) and the RMSNorm.  Ends with a
-// barrier.
+// residual add (h written to res_out by CTA 0) and the RMSNorm.  nw0 is the
+// norm-weight chunk of this thread's first row chunk (v = tid), fetched by the
+// caller before the programmatic-launch wait.  Ends with a barrier.
 template <typename T, int B, int K, bool NORM>
 __device__ __forceinline__ void stage_input(const GemvParams& p, T* as, float (*s_part)[B], int tid, int lane,
-                                            int warp) {
+                                            int warp, uint4 nw0) {
   constexpr int E = 8;
   if constexpr (!NORM) {
     for (int v = tid; v < B * K / E; v += kGemvThreads) {
@@ -118,7 +119,7 @@ __device__ __forceinline__ void stage_input(const GemvParams& p, T* as, float (*
       const float rr = 1.0f / sqrtf(tot / (float)K + p.eps);
       float h[E], wf[E];
       unpack16<T>(reinterpret_cast<const uint4*>(as)[v], h);
-      unpack16<T>(ld16_ro(static_cast<const T*>(p.norm_w) + c * E), wf);
+      unpack16<T>(v == tid ? nw0 : ld16_ro(static_cast<const T*>(p.norm_w) + c * E), wf);
 #pragma unroll
       for (int e = 0; e < E; ++e) h[e] = __fmul_rn(__fmul_rn(h[e], rr), wf[e]);
       reinterpret_cast<uint4*>(as)[v] = pack16<T>(h);
@@ -126,6 +127,14 @@ __device__ __forceinline__ void stage_input(const GemvParams& p, T* as, float (*
   }
   __syncthreads();
 
+}
+
+// The norm-weight chunk stage_input's thread `tid` applies first (a weight:
+// fetched before the programmatic-launch wait, like the matrix rows).
+template <typename T, int B, int K, bool NORM>
+__device__ __forceinline__ uint4 first_norm_chunk(const GemvParams& p, int tid) {
+  if (!NORM || tid >= B * K / 8) return make_uint4(0u, 0u, 0u, 0u);
+  return ld16_ro(static_cast<const T*>(p.norm_w) + (tid % (K / 8)) * 8);
 }
 
 // EPI: 0 = store, 1 = SiLU·mul of the gate / up rows r and n + r,
@@ -154,10 +163,11 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvParams p) {
         wv[q][c] = ld16_stream(W + (int64_t)(row + q * p.n) * p.w_stride + c * 256 + lane * E);
   };
   if (r < p.n) load_row(r);
+  const uint4 nw0 = first_norm_chunk<T, B, K, NORM>(p, tid);
   griddep_launch_dependents();
   griddep_wait();
 
-  stage_input<T, B, K, NORM>(p, as, s_part, tid, lane, warp);
+  stage_input<T, B, K, NORM>(p, as, s_part, tid, lane, warp, nw0);
 
   // ---- one warp per output row (SILU: per gate/up pair); row r's weights
   //      are already in flight
@@ -278,9 +288,10 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_rope_kv_kernel(GemvParams p
         wv[q][c] = ld16_stream(W + (int64_t)(row0 + rb + q) * p.w_stride + c * 256 + lane * E);
   };
   load_rows(0);
+  const uint4 nw0 = first_norm_chunk<T, B, K, NORM>(p, tid);
   griddep_launch_dependents();
   griddep_wait();
-  stage_input<T, B, K, NORM>(p, as, s_part, tid, lane, warp);
+  stage_input<T, B, K, NORM>(p, as, s_part, tid, lane, warp, nw0);
 
 #pragma unroll
   for (int rb = 0; rb < kRopeRowsPerWarp; rb += RB) {

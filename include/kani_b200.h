@@ -22,6 +22,12 @@
  *   - Data-dependent errors found on the device (a KV slot or a frame index out
  *     of range) do not trap: the offending access is skipped and a KANI_FLAG_*
  *     bit is OR-ed into the caller's device int32 `err_flag` (may be NULL).
+ *   - The projection entry points (kani_gemv*, kani_gemm_tc, kani_head_argmax*)
+ *     launch as programmatic dependents and start reading their weight
+ *     matrices and norm weights before the launch ahead of them on the stream
+ *     has finished.  Weights must therefore not be written by the immediately
+ *     preceding launch; activations, residuals and every other input are read
+ *     only after it completes.
  */
 #ifndef KANI_B200_H
 #define KANI_B200_H

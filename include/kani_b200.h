@@ -203,6 +203,26 @@ KANI_API int kani_decode_attention(int32_t dtype, int64_t batch, int32_t num_q_h
                           int32_t* err_flag, void* stream);
 
 /*
+ * kani_decode_attention for one decode step, launched as a programmatic
+ * dependent of the launch before it on the stream: the cache rows
+ * [0, kv_len[b] - 1) start streaming, and kv_len is read, before that launch has
+ * completed; q and the newest row, kv_len[b] - 1, are read after it.  So the
+ * launch just before may write q and the newest row (the step's RoPE + KV
+ * write, kani_tts/optimized_decode.py:220-240 then :243-248), but kv_len and the
+ * older rows must already be final.  Same arguments and bit-identical results as
+ * kani_decode_attention.
+ */
+KANI_API int kani_decode_attention_step(int32_t dtype, int64_t batch, int32_t num_q_heads,
+                          int32_t num_kv_heads, int32_t head_dim,
+                          const void* q, int64_t q_batch_stride, int64_t q_head_stride,
+                          const void* k_cache, const void* v_cache,
+                          int64_t cache_batch_stride, int64_t cache_head_stride,
+                          int64_t cache_slot_stride, int64_t cache_len,
+                          const int64_t* kv_len, float scale,
+                          void* out, int64_t out_batch_stride, int64_t out_head_stride,
+                          int32_t* err_flag, void* stream);
+
+/*
  * LFM2 gated short-convolution decode step for `batch` streams:
  *   [Bg | C | x] = bcx[b] (3*hidden, the in_proj output);  Bx = Bg * x;
  *   state[b] = roll(state[b], -1 along the kernel axis) with Bx in the last column;

@@ -320,12 +320,21 @@ decode_attn_kernel(AttnParams p) {
                      dst + TILE_BYTES),
                  "l"(vb + (int64_t)t * TILE_BYTES), "r"(bytes), "r"(bar) : "memory");
   };
+  // The tile holding the newest row, len - 1, is the only one a decode step's
+  // previous launch (its RoPE + KV write) may still be writing.  Launched as a
+  // programmatic dependent (kani_decode_attention_step), the other first tiles
+  // stream in before griddepcontrol.wait and that tile after it; launched
+  // plainly, the wait returns at once and the order does not matter.
+  const int t_new = (len - 1 >= k0 && len - 1 < k1) ? (int)((len - 1 - k0) / kAttnTile) : -1;
   if (tid == 0) {
     for (int st = 0; st < kAttnStages; ++st)
       asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(attn_smem_u32(&bars[st])), "r"(1) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    for (int t = 0; t < ntiles && t < kAttnStages; ++t) issue(t);
+    for (int t = 0; t < ntiles && t < kAttnStages; ++t)
+      if (t != t_new) issue(t);
   }
+  griddep_wait();  // q and the newest row may come from the launch before
+  if (tid == 0 && t_new >= 0 && t_new < kAttnStages) issue(t_new);
 
   // query heads (global) while the first tiles stream in
   float q[G][DL];
@@ -507,7 +516,7 @@ decode_attn_kernel(AttnParams p) {
 }
 
 template <typename T, int G, int D>
-int launch_attn(const AttnParams& p, int64_t batch, int hk, cudaStream_t s) {
+int launch_attn(const AttnParams& p, int64_t batch, int hk, cudaStream_t s, bool dependent) {
   if (p.cs == D) {  // contiguous cache rows: TMA-staged kernel, cluster size sized to fill the GPU
     static int sms[64] = {0};
     static int smem_set[64] = {0};
@@ -533,13 +542,15 @@ int launch_attn(const AttnParams& p, int64_t batch, int hk, cudaStream_t s) {
     cfg.blockDim = dim3(kAttnThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = (unsigned)cl;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = dependent ? 2 : 1;
     cudaLaunchKernelEx(&cfg, decode_attn_kernel<T, G, D>, p);
   } else {
     const dim3 grid(kClusterCTAs, (unsigned)hk, (unsigned)batch);
@@ -551,13 +562,13 @@ int launch_attn(const AttnParams& p, int64_t batch, int hk, cudaStream_t s) {
 }  // namespace
 }  // namespace kani
 
-extern "C" int kani_decode_attention(int32_t dtype, int64_t batch, int32_t num_q_heads, int32_t num_kv_heads,
-                                     int32_t head_dim, const void* q, int64_t q_batch_stride,
-                                     int64_t q_head_stride, const void* k_cache, const void* v_cache,
-                                     int64_t cache_batch_stride, int64_t cache_head_stride,
-                                     int64_t cache_slot_stride, int64_t cache_len, const int64_t* kv_len,
-                                     float scale, void* out, int64_t out_batch_stride,
-                                     int64_t out_head_stride, int32_t* err_flag, void* stream) {
+namespace {
+int decode_attention_impl(int32_t dtype, int64_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                          int32_t head_dim, const void* q, int64_t q_batch_stride, int64_t q_head_stride,
+                          const void* k_cache, const void* v_cache, int64_t cache_batch_stride,
+                          int64_t cache_head_stride, int64_t cache_slot_stride, int64_t cache_len,
+                          const int64_t* kv_len, float scale, void* out, int64_t out_batch_stride,
+                          int64_t out_head_stride, int32_t* err_flag, void* stream, bool dependent) {
   if (batch < 0 || num_q_heads < 0 || num_kv_heads < 0 || head_dim < 0 || cache_len < 0)
     return KANI_ERR_INVALID_ARG;
   if (batch == 0 || num_q_heads == 0) return KANI_OK;
@@ -576,13 +587,38 @@ extern "C" int kani_decode_attention(int32_t dtype, int64_t batch, int32_t num_q
                      cache_head_stride % E == 0 && cache_slot_stride % E == 0;
     if (!vec) return KANI_ERR_UNSUPPORTED;
     if (head_dim == 64) {
-      if (g == 1) return kani::launch_attn<T, 1, 64>(p, batch, num_kv_heads, s);
-      if (g == 2) return kani::launch_attn<T, 2, 64>(p, batch, num_kv_heads, s);
-      if (g == 4) return kani::launch_attn<T, 4, 64>(p, batch, num_kv_heads, s);
+      if (g == 1) return kani::launch_attn<T, 1, 64>(p, batch, num_kv_heads, s, dependent);
+      if (g == 2) return kani::launch_attn<T, 2, 64>(p, batch, num_kv_heads, s, dependent);
+      if (g == 4) return kani::launch_attn<T, 4, 64>(p, batch, num_kv_heads, s, dependent);
     } else if (head_dim == 128) {
-      if (g == 1) return kani::launch_attn<T, 1, 128>(p, batch, num_kv_heads, s);
-      if (g == 2) return kani::launch_attn<T, 2, 128>(p, batch, num_kv_heads, s);
+      if (g == 1) return kani::launch_attn<T, 1, 128>(p, batch, num_kv_heads, s, dependent);
+      if (g == 2) return kani::launch_attn<T, 2, 128>(p, batch, num_kv_heads, s, dependent);
     }
     return KANI_ERR_UNSUPPORTED;
   });
+}
+}  // namespace
+
+extern "C" int kani_decode_attention(int32_t dtype, int64_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                                     int32_t head_dim, const void* q, int64_t q_batch_stride,
+                                     int64_t q_head_stride, const void* k_cache, const void* v_cache,
+                                     int64_t cache_batch_stride, int64_t cache_head_stride,
+                                     int64_t cache_slot_stride, int64_t cache_len, const int64_t* kv_len,
+                                     float scale, void* out, int64_t out_batch_stride,
+                                     int64_t out_head_stride, int32_t* err_flag, void* stream) {
+  return decode_attention_impl(dtype, batch, num_q_heads, num_kv_heads, head_dim, q, q_batch_stride, q_head_stride,
+                               k_cache, v_cache, cache_batch_stride, cache_head_stride, cache_slot_stride, cache_len,
+                               kv_len, scale, out, out_batch_stride, out_head_stride, err_flag, stream, false);
+}
+
+extern "C" int kani_decode_attention_step(int32_t dtype, int64_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                                          int32_t head_dim, const void* q, int64_t q_batch_stride,
+                                          int64_t q_head_stride, const void* k_cache, const void* v_cache,
+                                          int64_t cache_batch_stride, int64_t cache_head_stride,
+                                          int64_t cache_slot_stride, int64_t cache_len, const int64_t* kv_len,
+                                          float scale, void* out, int64_t out_batch_stride,
+                                          int64_t out_head_stride, int32_t* err_flag, void* stream) {
+  return decode_attention_impl(dtype, batch, num_q_heads, num_kv_heads, head_dim, q, q_batch_stride, q_head_stride,
+                               k_cache, v_cache, cache_batch_stride, cache_head_stride, cache_slot_stride, cache_len,
+                               kv_len, scale, out, out_batch_stride, out_head_stride, err_flag, stream, true);
 }

@@ -75,10 +75,15 @@ __global__ void __launch_bounds__(kHeadThreads) head_argmax_kernel(HeadParams p)
   if (gw * kHeadRows < p.rows) load_rows(gw * kHeadRows);
   griddep_wait();
 
+  // The hidden rows are written by the launch before, which may still be
+  // running while this grid is resident, so they are read with coherent loads
+  // after the wait: the read-only (.nc) path is only valid for data that stays
+  // unwritten for the whole life of the kernel, and a stale line from an
+  // earlier read of the same address (a graph replay reuses it) could be served.
   for (int v = tid; v < B * H / E; v += kHeadThreads) {
     const int b = v / (H / E), c = v % (H / E);
     uint4 x = make_uint4(0u, 0u, 0u, 0u);
-    if (b < p.batch) x = ld16_ro(static_cast<const T*>(p.h) + (int64_t)b * p.h_stride + c * E);
+    if (b < p.batch) x = ld16(static_cast<const T*>(p.h) + (int64_t)b * p.h_stride + c * E);
     reinterpret_cast<uint4*>(hs)[v] = x;
   }
   __syncthreads();

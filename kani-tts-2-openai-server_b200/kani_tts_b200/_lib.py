@@ -59,6 +59,9 @@ _SIGNATURES = {
     "kani_decode_attention": ([_c_i32, _c_i64, _c_i32, _c_i32, _c_i32,
                                _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_i64, _c_i64, _c_i64, _c_i64,
                                _c_p, _c_f32, _c_p, _c_i64, _c_i64, _c_p, _c_p], ctypes.c_int),
+    "kani_decode_attention_step": ([_c_i32, _c_i64, _c_i32, _c_i32, _c_i32,
+                                    _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_i64, _c_i64, _c_i64, _c_i64,
+                                    _c_p, _c_f32, _c_p, _c_i64, _c_i64, _c_p, _c_p], ctypes.c_int),
     "kani_short_conv_step": ([_c_i32, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_p, _c_i64, _c_i64, _c_i32, _c_i32,
                               _c_p], ctypes.c_int),
     "kani_sample_tokens": ([_c_i32, _c_p, _c_i64, _c_i64, _c_i32, _c_p,

@@ -156,6 +156,14 @@ class FusedDecoder:
     # ------------------------------------------------------------ decode
     fused_greedy_head = True   # greedy / sampled steps may use the fused head kernels
     tc_output_projections = True  # tensor-core path: o / out / down projections on gemm_tc (split K) too
+    # One stream: decode attention launches as a programmatic dependent of the
+    # RoPE + KV write and streams the older cache rows while that launch runs
+    # (kani_decode_attention_step).  Measured per step on B200: 270 vs 272-275 us
+    # at 1 stream; at 4 streams its early-resident CTAs cost 589 vs 562 us.
+    @property
+    def dependent_attention(self) -> bool:
+        return self.batch == 1
+
     # The norm prologue re-reads every stream's row in every CTA (from L2); beyond
     # this many streams a separate add + RMSNorm launch is cheaper (measured: equal
     # at 8 streams, 58 us per step slower at 16).
@@ -246,7 +254,7 @@ class FusedDecoder:
                                frame_table=self.frame_table, tokens_per_frame=self.cfg.tokens_per_frame,
                                err_flag=self.err_flag)
                 attn = decode_attention(q_rot, self.k_cache[i], self.v_cache[i], kv_len, self.scale,
-                                        err_flag=self.err_flag)
+                                        err_flag=self.err_flag, prefix_final=self.dependent_attention)
                 delta = gemv(attn.view(b, 1, self.q_dim), L["o"])
             else:
                 y = normed(gemv_short_conv, L["in_proj"], self.conv_state[i], L["conv_w"], norm_weight=L["op_norm"])
@@ -275,7 +283,7 @@ class FusedDecoder:
                     tokens_per_frame=self.cfg.tokens_per_frame, q_norm_w=L["q_norm"], k_norm_w=L["k_norm"],
                     eps=self.eps, err_flag=self.err_flag)
                 attn = decode_attention(q_rot, self.k_cache[i], self.v_cache[i], kv_len, self.scale,
-                                        err_flag=self.err_flag)   # [B, Hq, D]
+                                        err_flag=self.err_flag, prefix_final=self.dependent_attention)   # [B, Hq, D]
                 delta = F.linear(attn.view(b, 1, self.q_dim), L["o"])
             else:
                 delta = self._conv_step(i, L, normed)
@@ -324,7 +332,7 @@ class FusedDecoder:
                     tokens_per_frame=self.cfg.tokens_per_frame, q_norm_w=L["q_norm"], k_norm_w=L["k_norm"],
                     eps=self.eps, err_flag=self.err_flag)
                 attn = decode_attention(q_rot, self.k_cache[i], self.v_cache[i], kv_len, self.scale,
-                                        err_flag=self.err_flag)
+                                        err_flag=self.err_flag, prefix_final=self.dependent_attention)
                 delta = proj(attn.view(b, 1, self.q_dim), L["o"])
             else:
                 bcx = gemm_tc(x_in, L["in_proj"], **norm_kw, **common)

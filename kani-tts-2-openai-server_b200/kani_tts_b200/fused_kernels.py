@@ -367,12 +367,17 @@ def fused_rope_kv_write(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, inv_f
 
 def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, kv_len: torch.Tensor,
                      scale: float | None = None, out: torch.Tensor | None = None,
-                     err_flag: torch.Tensor | None = None) -> torch.Tensor:
+                     err_flag: torch.Tensor | None = None, prefix_final: bool = False) -> torch.Tensor:
     """GQA decode attention of one query token per stream over cache slots [0, kv_len[b]).
 
     Replaces SDPA over the whole -inf-masked static buffer (optimized_decode.py:243-248).
         q: [B, Hq, D] or [B, 1, Hq, D] (heads at stride D); k_cache / v_cache: [B, Hk, S, D];
         kv_len: device int64 [B].  Returns out [B, Hq, D] (or writes ``out``).
+        prefix_final: a decode step whose launch just before (its RoPE + KV write)
+            writes at most q and the newest row, kv_len - 1, of each stream, while
+            kv_len and the older rows are already final.  Then
+            ``kani_decode_attention_step`` streams those rows before that launch
+            completes (same results).
     """
     for t, w in ((q, "q"), (k_cache, "k_cache"), (v_cache, "v_cache"), (kv_len, "kv_len")):
         require_cuda(t, w)
@@ -398,11 +403,13 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     ov = out.view(b, hq, d)
     flag = err_flag if err_flag is not None else error_flag(q.device)
     cs = k_cache.stride()
-    check(lib.kani_decode_attention(
+    fn, name = ((lib.kani_decode_attention_step, "kani_decode_attention_step") if prefix_final
+                else (lib.kani_decode_attention, "kani_decode_attention"))
+    check(fn(
         code, b, hq, hk, d, ptr(qv), qv.stride(0), qv.stride(1), ptr(k_cache), ptr(v_cache),
         cs[0], cs[1], cs[2], s_len, ptr(kv_len.contiguous()),
         float(d ** -0.5 if scale is None else scale), ptr(ov), ov.stride(0), ov.stride(1), ptr(flag),
-        stream_ptr(q.device)), "kani_decode_attention")
+        stream_ptr(q.device)), name)
     return out
 
 

@@ -196,6 +196,41 @@ def test_engine_graph_replay_matches_eager_steps():
     assert int(eng.dec.err_flag.item()) == 0
 
 
+@pytest.mark.parametrize("b", [1, 2])
+def test_full_size_graph_replays_are_deterministic(b):
+    """Full-size model on the fused small-batch path (fused GEMVs, dependent
+    decode attention at one stream, the fused greedy head): two captured
+    engines and the eager steps produce the same 40 tokens per stream.  Graph
+    replays reuse every buffer address, so a kernel that read an activation
+    written by the launch before it through the read-only cache path could pick
+    up a line left from the previous replay; this caught such a read in the
+    fused head at two streams."""
+    cfg = LFM2Config()
+    sd = synthetic_state_dict(cfg, seed=0, device=DEV)
+    n = 40
+    g = torch.Generator().manual_seed(1)
+    ids = torch.randint(0, cfg.audio_tokens_start, (b, 128), generator=g).to(DEV)
+    spk = torch.randn(b, cfg.speaker_emb_dim, generator=g).to(DEV)
+    runs = []
+    for _ in range(2):
+        eng = DecodeEngine(FusedDecoder(cfg, sd, DEV, batch=b, max_len=256))
+        assert eng.dec.small_batch and eng.dec.fused_head == "gemv"
+        eng.start(ids, spk, n)
+        eng.capture()
+        eng.run(n)
+        torch.cuda.synchronize()
+        runs.append(eng.generated.clone())
+        assert int(eng.dec.err_flag.item()) == 0
+        del eng
+    ref = DecodeEngine(FusedDecoder(cfg, sd, DEV, batch=b, max_len=256))
+    ref.start(ids, spk, n)
+    for _ in range(n):
+        ref._step_body()
+    torch.cuda.synchronize()
+    assert torch.equal(runs[0], runs[1])
+    assert torch.equal(runs[0], ref.generated)
+
+
 def test_engine_with_device_sampling_graph_matches_eager():
     """The sampler inside the captured step (Philox counter and repetition bitmap
     advanced on the device) gives the same token sequence as eager steps, every

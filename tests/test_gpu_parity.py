@@ -595,6 +595,61 @@ def test_decode_attention_ignores_slots_past_the_prefix_and_flags_overflow():
     assert _lib.read_and_clear_errors(DEV) == _lib.KANI_FLAG_SLOT_OOB
 
 
+@pytest.mark.parametrize("b,lens", [(1, [100]), (1, [1629]), (3, [5, 640, 1200]), (4, [2048, 1, 64, 65])])
+def test_decode_attention_step_after_the_kv_write(b, lens):
+    """kani_decode_attention_step launched right behind the fused QKV GEMV +
+    RoPE + KV write, which releases its dependents early and writes q and each
+    stream's newest row (kv_len - 1): bit-identical to kani_decode_attention,
+    eagerly and replayed from a CUDA graph, and close to the oracle.  The newest
+    row falls in a first-stage tile (100 slots over 8 CTAs) and in a later one
+    (1629 slots)."""
+    hq, hk, d, h, s_len = 16, 8, 64, 1024, 2048
+    kv_len = torch.tensor(lens, dtype=torch.long)
+    slots = kv_len - 1
+    x = gpu(rnd((b, 1, h), 1130))
+    res = gpu(rnd((b, 1, h), 1131))
+    nw = gpu((1.0 + 0.1 * rnd((h,), 1132, torch.float32)).to(torch.bfloat16))
+    w = gpu(rnd(((hq + 2 * hk) * d, h), 1133, std=0.03))
+    inv = gpu(P.learnable_inv_freq(d, 1e6, 0.0))
+    kc0, vc0 = rnd((b, hk, s_len, d), 1134), rnd((b, hk, s_len, d), 1135)
+    pos, sl, kl = gpu(slots), gpu(slots), gpu(kv_len)
+
+    def chain(prefix_final, kc, vc, hbuf, out):
+        q_rot = K.gemv_rope_kv_write(x, w, nw, inv, pos, kc, vc, sl, num_q_heads=hq, num_kv_heads=hk,
+                                     residual=res, residual_out=hbuf)
+        return K.decode_attention(q_rot, kc, vc, kl, out=out, prefix_final=prefix_final)
+
+    runs = {}
+    for mode in (False, True):
+        kc, vc = gpu(kc0), gpu(vc0)
+        hbuf = torch.empty_like(x)
+        out = torch.empty(b, hq, d, dtype=torch.bfloat16, device=DEV)
+        chain(mode, kc, vc, hbuf, out)
+        torch.cuda.synchronize()
+        runs[mode] = (out.clone(), kc.clone(), vc.clone())
+        # the same chain captured and replayed (the rows it writes are rewritten identically)
+        s = torch.cuda.Stream(device=DEV)
+        s.wait_stream(torch.cuda.current_stream(DEV))
+        with torch.cuda.stream(s):
+            chain(mode, kc, vc, hbuf, out)
+        torch.cuda.current_stream(DEV).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            chain(mode, kc, vc, hbuf, out)
+        out.zero_()
+        g.replay()
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, runs[mode][0])
+    assert torch.equal(runs[True][0], runs[False][0])
+    q_rot = K.gemv_rope_kv_write(x, w, nw, inv, pos, gpu(kc0), gpu(vc0), sl, num_q_heads=hq, num_kv_heads=hk,
+                                 residual=res, residual_out=torch.empty_like(x))
+    ref = O.decode_attention_ref(q_rot.reshape(b, hq, d).cpu(), runs[True][1].cpu(), runs[True][2].cpu(), kv_len,
+                                 d ** -0.5)
+    assert_attention_close(runs[True][0], ref)
+    assert _lib.read_and_clear_errors(DEV) == 0
+
+
 @pytest.mark.parametrize("b,h", [(1, 1024), (64, 1024), (3, 256)])
 def test_short_conv_step_bit_exact_vs_eager(b, h):
     bcx = rnd((b, 3 * h), 1200)

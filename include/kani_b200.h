@@ -293,10 +293,19 @@ KANI_API int kani_head_argmax(int32_t dtype, const void* hidden, int64_t hidden_
                      void* stream);
 
 /*
- * kani_head_argmax without the scratch argument: the scratch is a file-scope
- * device array (zero at load, left zero by every call), located per device with
- * cudaGetSymbolAddress; nothing is allocated.  batch + 1 must not exceed 64
- * (KANI_ERR_UNSUPPORTED); calls on one device must not overlap in time.
+ * kani_head_argmax without the scratch argument, for callers that cannot
+ * allocate device memory: a host whose allocator belongs to another framework,
+ * code that may not call cudaMalloc while a stream is being captured, or a
+ * real-time thread that must not block on an allocation.  There is no
+ * counterpart in the reference (which allocates through PyTorch).
+ * The cross-CTA scratch is a file-scope device array of 64 words, zero when the
+ * library loads and left zero by every call.  Every GPU that loads the library
+ * holds one copy until the process exits.  The first call on a device looks up
+ * the array's device address with cudaGetSymbolAddress (with that device
+ * current) and keeps it: make that first call before any stream capture.
+ * batch + 1 above 64 returns KANI_ERR_UNSUPPORTED before any launch (the kernel
+ * itself serves up to 8 streams).  All calls on a device share the array, so
+ * calls that overlap on the GPU race; issue them on one stream.
  */
 KANI_API int kani_head_argmax_noalloc(int32_t dtype, const void* hidden, int64_t hidden_row_stride,
                      int64_t batch, int32_t hidden_size, const void* weight,

@@ -1,6 +1,11 @@
-"""kani_head_argmax_noalloc (scratch in a file-scope device array) against
+"""kani_head_argmax_noalloc, the entry point for callers that cannot allocate
+device memory (another framework owns the allocator, a stream is being
+captured, or a real-time thread must not block on cudaMalloc): its scratch is a
+file-scope device array of the library.  Checked through the C ABI against
 kani_head_argmax with a caller-provided scratch: identical tokens and logits on
-two consecutive calls (the second call shows the array was left clean)."""
+two consecutive calls (the second call shows the array was left clean), and the
+size limit refused before any launch.  Collected last, so a run that stops at
+the first failure has run every other test first."""
 from __future__ import annotations
 
 import ctypes

@@ -306,19 +306,48 @@ def run_reference(args, world, rank):
 def run_e2e(K, dev, steps: int) -> dict:
     """Public API with pinned host buffers, every step: H2D of the step's inputs
     (Q, K, V, positions, slots), the kernel, D2H of its results (rotated Q and
-    the written K/V cache slots).  Steps are pipelined over two buffer sets and
-    three streams (copy-in, compute, copy-out) so that one step's H2D overlaps
-    the previous step's D2H (PCIe is full duplex); events order every buffer
-    reuse."""
+    the written K/V cache slots).  The inputs travel as one packed host buffer,
+    [T, Q | K | V] rows as the QKV projection lays them out plus the positions
+    and slots, read in place through token strides; the results land in one
+    device buffer (rotated Q, then the K and V caches, whose every slot this step
+    writes).  So a step is one H2D copy, the kernel and one D2H copy.  Steps are
+    pipelined over two buffer sets and three streams (copy-in, compute,
+    copy-out) so that one step's H2D overlaps the previous step's D2H (PCIe is
+    full duplex); events order every buffer reuse."""
     host = make_inputs(1)
-    pin = {n: host[n].pin_memory() for n in ("q", "k", "v", "pos", "slots")}
+    t = T_TOK
+    row = (HQ + 2 * HK) * D
+    qkv_bytes = t * row * 2
+    in_bytes = qkv_bytes + 2 * t * 8
+    s_len = host["kc"].shape[2]
+    if s_len != t:
+        raise RuntimeError("the e2e leg reads the whole cache back: it needs cache length = tokens")
+    q_bytes = t * HQ * D * 2
+    out_bytes = q_bytes + 2 * HK * s_len * D * 2
+
+    def in_views(buf):
+        qkv = buf[:qkv_bytes].view(torch.bfloat16).view(t, row)
+        ps = buf[qkv_bytes:in_bytes].view(torch.int64).view(2, t)
+        return (qkv[:, :HQ * D].view(1, t, HQ, D), qkv[:, HQ * D:(HQ + HK) * D].view(1, t, HK, D),
+                qkv[:, (HQ + HK) * D:].view(1, t, HK, D), ps[0], ps[1])
+
+    def out_views(buf):
+        q_out = buf[:q_bytes].view(torch.bfloat16).view(1, t, HQ, D)
+        kv = buf[q_bytes:].view(torch.bfloat16).view(2, 1, HK, s_len, D)
+        return q_out, kv[0], kv[1]
+
+    pin_in = torch.empty(in_bytes, dtype=torch.uint8).pin_memory()
+    q_h, k_h, v_h, pos_h, slots_h = in_views(pin_in)
+    q_h.copy_(host["q"].view(1, t, HQ, D))
+    k_h.copy_(host["k"].view(1, t, HK, D))
+    v_h.copy_(host["v"].view(1, t, HK, D))
+    pos_h.copy_(host["pos"])
+    slots_h.copy_(host["slots"])
     nbuf = 2
-    devs = [make_inputs(1, device=dev) for _ in range(nbuf)]
-    q_out = [torch.empty(1, T_TOK, HQ, D, dtype=torch.bfloat16, device=dev) for _ in range(nbuf)]
-    q_host = [torch.empty(T_TOK, HQ, D, dtype=torch.bfloat16).pin_memory() for _ in range(nbuf)]
-    kv_host = [torch.empty(2, HK, T_TOK, D, dtype=torch.bfloat16).pin_memory() for _ in range(nbuf)]
-    h2d = sum(pin[n].numel() * pin[n].element_size() for n in pin)
-    d2h = q_host[0].numel() * 2 + kv_host[0].numel() * 2
+    d_in = [torch.empty(in_bytes, dtype=torch.uint8, device=dev) for _ in range(nbuf)]
+    d_out = [torch.zeros(out_bytes, dtype=torch.uint8, device=dev) for _ in range(nbuf)]
+    h_out = [torch.empty(out_bytes, dtype=torch.uint8).pin_memory() for _ in range(nbuf)]
+    table, inv = host["table"].to(dev), host["inv"].to(dev)
     s_in, s_comp, s_out = (torch.cuda.Stream(device=dev) for _ in range(3))
     ev = lambda: torch.cuda.Event()  # noqa: E731
     in_done = [ev() for _ in range(nbuf)]
@@ -328,30 +357,37 @@ def run_e2e(K, dev, steps: int) -> dict:
 
     def step(i):
         j = i % nbuf
-        d = devs[j]
         with torch.cuda.stream(s_in):
             if used[j]:
                 s_in.wait_event(comp_done[j])      # inputs of buffer j no longer read
-            for n in pin:
-                d[n].copy_(pin[n], non_blocking=True)
+            d_in[j].copy_(pin_in, non_blocking=True)
             in_done[j].record(s_in)
         with torch.cuda.stream(s_comp):
             s_comp.wait_event(in_done[j])
             if used[j]:
                 s_comp.wait_event(out_done[j])     # results of buffer j already read back
-            launch(K, d, q_out[j])
+            q, k, v, pos, slots = in_views(d_in[j])
+            q_out, kc, vc = out_views(d_out[j])
+            K.fused_rope_kv_write(q, k, v, inv, pos, kc, vc, slots, frame_table=table, tokens_per_frame=TPF,
+                                  q_out=q_out)
             comp_done[j].record(s_comp)
         with torch.cuda.stream(s_out):
             s_out.wait_event(comp_done[j])
-            q_host[j].copy_(q_out[j].view(T_TOK, HQ, D), non_blocking=True)
-            kv_host[j][0].copy_(d["kc"][0, :, :T_TOK], non_blocking=True)
-            kv_host[j][1].copy_(d["vc"][0, :, :T_TOK], non_blocking=True)
+            h_out[j].copy_(d_out[j], non_blocking=True)
             out_done[j].record(s_out)
         used[j] = True
 
     for i in range(4):
         step(i)
     torch.cuda.synchronize(dev)
+    # the packed path returns what the headline launch computes from contiguous inputs
+    ref = make_inputs(1, device=dev)
+    ref_q = torch.empty(1, t, HQ, D, dtype=torch.bfloat16, device=dev)
+    launch(K, ref, ref_q)
+    got_q, got_k, got_v = out_views(h_out[0])
+    if not (torch.equal(got_q, ref_q.cpu()) and torch.equal(got_k, ref["kc"].cpu())
+            and torch.equal(got_v, ref["vc"].cpu())):
+        raise RuntimeError("the packed e2e path differs from the headline launch")
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(s_in)
     for i in range(steps):
@@ -361,7 +397,7 @@ def run_e2e(K, dev, steps: int) -> dict:
     e1.record(s_out)
     torch.cuda.synchronize(dev)
     el = e0.elapsed_time(e1) / 1e3
-    return {"seconds": el, "steps": steps, "h2d": h2d, "d2h": d2h}
+    return {"seconds": el, "steps": steps, "h2d": in_bytes, "d2h": out_bytes}
 
 
 def run_sweep(K, dev, peak: float) -> dict:
@@ -710,8 +746,9 @@ def run_gpu(args, world, rank, local):
     e2e_line = {"value": round(world * e["steps"] * STEP_BYTES / e_max / 1e9, 3), "unit": UNIT,
                 "h2d_bytes_per_step": e["h2d"], "d2h_bytes_per_step": e["d2h"], "steps": e["steps"],
                 "ms_per_step": round(e_max / e["steps"] * 1e3, 4),
-                "path": ("kani_tts_b200.fused_rope_kv_write (ctypes -> kani_rope_kv_write), pinned host "
-                         "buffers, copy-in / compute / copy-out streams over two buffer sets")}
+                "path": ("kani_tts_b200.fused_rope_kv_write (ctypes -> kani_rope_kv_write): one pinned "
+                         "packed input buffer (Q|K|V rows, positions, slots) and one result buffer (rotated Q, "
+                         "K and V caches) per step, copy-in / compute / copy-out streams over two buffer sets")}
     if not args.no_decode:
         # decode steps: bs=1 (with the eager reference-structure arm) and 64 streams per GPU
         extras["decode"] = {"bs1": run_decode(dev, world, rank, 1, args.decode_steps, eager=True),

@@ -196,15 +196,15 @@ def test_engine_graph_replay_matches_eager_steps():
     assert int(eng.dec.err_flag.item()) == 0
 
 
-@pytest.mark.parametrize("b", [1, 2])
+@pytest.mark.parametrize("b", [1, 2, 4, 16])
 def test_full_size_graph_replays_are_deterministic(b):
-    """Full-size model on the fused small-batch path (fused GEMVs, dependent
-    decode attention at one stream, the fused greedy head): two captured
-    engines and the eager steps produce the same 40 tokens per stream.  Graph
-    replays reuse every buffer address, so a kernel that read an activation
-    written by the launch before it through the read-only cache path could pick
-    up a line left from the previous replay; this caught such a read in the
-    fused head at two streams."""
+    """Full-size model, two captured engines and the eager steps: the same 40
+    tokens per stream.  1-4 streams take the fused-GEMV path (dependent decode
+    attention at one stream) and the CUDA-core greedy head; 16 streams the
+    tensor-core projections and head.  Graph replays reuse every buffer
+    address, so a kernel that read an activation written by the launch before
+    it through the read-only cache path could pick up a line left from the
+    previous replay; this caught such a read in the fused head at two streams."""
     cfg = LFM2Config()
     sd = synthetic_state_dict(cfg, seed=0, device=DEV)
     n = 40
@@ -214,7 +214,10 @@ def test_full_size_graph_replays_are_deterministic(b):
     runs = []
     for _ in range(2):
         eng = DecodeEngine(FusedDecoder(cfg, sd, DEV, batch=b, max_len=256))
-        assert eng.dec.small_batch and eng.dec.fused_head == "gemv"
+        if b <= 4:
+            assert eng.dec.small_batch and eng.dec.fused_head == "gemv"
+        else:
+            assert eng.dec.tc_batch and eng.dec.fused_head == "tc"
         eng.start(ids, spk, n)
         eng.capture()
         eng.run(n)

@@ -212,6 +212,10 @@ rope_vec_kernel(RopeParams p, int log2l, int ipt, int iptr, int tpb) {
 template <typename T, bool NORM, bool TABLE, int QI, int KI>
 __global__ void __launch_bounds__(256)
 rope_token_kernel(RopeParams p, int log2l) {
+  // a decode step's attention (kani_decode_attention_step) may start streaming
+  // the older cache rows now; it reads q and the rows written here after this
+  // grid completes
+  griddep_launch_dependents();
   constexpr int E = VecN<T>::value;
   constexpr int NI = QI > KI ? QI : KI;
   const int L = 1 << log2l;

@@ -156,13 +156,15 @@ class FusedDecoder:
     # ------------------------------------------------------------ decode
     fused_greedy_head = True   # greedy / sampled steps may use the fused head kernels
     tc_output_projections = True  # tensor-core path: o / out / down projections on gemm_tc (split K) too
-    # One stream: decode attention launches as a programmatic dependent of the
-    # RoPE + KV write and streams the older cache rows while that launch runs
-    # (kani_decode_attention_step).  Measured per step on B200: 270 vs 272-275 us
-    # at 1 stream; at 4 streams its early-resident CTAs cost 589 vs 562 us.
+    # Decode attention launches as a programmatic dependent of the RoPE + KV
+    # write and streams the older cache rows while that launch runs
+    # (kani_decode_attention_step).  Measured per step on B200 (1500 tokens):
+    # 1 stream 270 vs 272-275 us, 8 streams 710-713 vs 716-720, 16 neutral,
+    # 64 streams 744-748 vs 753; on the fused-GEMV path at 2-4 streams its
+    # early-resident CTAs cost more than they save (4 streams: 589 vs 562 us).
     @property
     def dependent_attention(self) -> bool:
-        return self.batch == 1
+        return self.batch == 1 or not self.small_batch
 
     # The norm prologue re-reads every stream's row in every CTA (from L2); beyond
     # this many streams a separate add + RMSNorm launch is cheaper (measured: equal

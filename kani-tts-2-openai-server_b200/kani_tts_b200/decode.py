@@ -160,8 +160,9 @@ class FusedDecoder:
     # write and streams the older cache rows while that launch runs
     # (kani_decode_attention_step).  Measured per step on B200 (1500 tokens):
     # 1 stream 270 vs 272-275 us, 8 streams 710-713 vs 716-720, 16 neutral,
-    # 64 streams 744-748 vs 753; on the fused-GEMV path at 2-4 streams its
-    # early-resident CTAs cost more than they save (4 streams: 589 vs 562 us).
+    # 64 streams about 1 % (bench: 795 vs 799-801 us); on the fused-GEMV path at
+    # 2-4 streams its early-resident CTAs cost more than they save (4 streams:
+    # 589 vs 562 us).
     @property
     def dependent_attention(self) -> bool:
         return self.batch == 1 or not self.small_batch

@@ -16,8 +16,10 @@ Headline workload (one "step" = one launch of the fused kernel):
   1024 + V slot 1024).
 
 Timing: W warm-up launches, then exactly K launches replayed from CUDA
-graphs, bracketed by a barrier + synchronize and CUDA events on the
-launching stream; the max over ranks is taken.  N > 1 runs N independent
+graphs, bracketed by a barrier + synchronize; the CUDA events that time them
+are recorded inside the graphs on the launching stream, after 8 untimed
+lead-in launches, so the host's graph submission is outside the timed
+region.  The max over ranks is taken.  N > 1 runs N independent
 replicas (the work shards by independent streams; there is no collective on
 the data path), so scaling is weak.
 
@@ -25,18 +27,25 @@ Also reported:
   e2e         — the same metric through the public Python API with pinned host
                 buffers: per step H2D of Q/K/V/positions/slots, the kernel, and
                 D2H of the rotated Q and the written K/V slots;
-  roofline    — achieved vs the measured HBM copy peak (MEASURED_PEAKS.json);
+  roofline    — achieved vs the measured HBM copy peak (MEASURED_PEAKS.json),
+                with the steady-state DRAM traffic per launch from the committed
+                ncu summary;
   cpu_baseline— the CPU oracle (PyTorch eager restatement of the reference
                 path) on the host cores, rank 0 at N = 1;
-  sweep       — every fused op at its configuration sizes (µs per call and GB/s);
-  decode      — the synthetic LFM2 decode step on the fused kernels: bs=1 latency next
-                to the reference's decode structure with eager ops, and 64 streams
-                per GPU (tokens/s aggregated over the N GPUs);
+  sweep       — every fused op at its configuration sizes (µs per call and GB/s),
+                next to the reference's own Triton kernels on the same GPU and
+                inputs when the reference is installed in baseline/_ref;
+  decode      — the synthetic LFM2 decode step on the fused kernels: bs=1 and 64
+                streams per GPU (tokens/s aggregated over the N GPUs), greedy and
+                sampled, and at bs=1 the reference's own Triton + CUDA-graph
+                engine (OptimizedDecoder captured by KaniInferenceEngine) on the
+                same GPU, with its greedy tokens compared to this library's;
   clocks      — nvidia-smi samples taken during the timed region.
 
-``--impl reference`` times the reference's CPU path (the oracle port; the
-reference's Triton source cannot be shipped to the GPU host) on the same
-workload and prints the same line with "impl": "reference".
+``--impl reference`` times the reference's CPU path (the oracle port: the
+reference's decode path has no CPU implementation besides the eager ops the
+oracle restates) on the same workload and prints the same line with
+"impl": "reference".  Rank 0 alone runs it.
 """
 from __future__ import annotations
 
@@ -77,18 +86,25 @@ def _peaks() -> tuple[float, str]:
     return 6650.0, "fallback"
 
 
-def _traffic_per_launch() -> float | None:
-    """DRAM bytes per headline launch from the committed ncu summary, if any."""
-    p = ROOT / "profiles" / "rope_kv_write_t4096.md"
+def _traffic_per_launch() -> tuple[float | None, str | None]:
+    """Steady-state DRAM bytes (read + write) per headline launch, from the
+    committed summary of one ncu capture of back-to-back launches with the
+    cache left warm between them (profiles/rope_kv_write_t4096_traffic.json)."""
+    p = ROOT / "profiles" / "rope_kv_write_t4096_traffic.json"
     if not p.exists():
-        return None
-    for line in p.read_text().splitlines():
-        if line.startswith("traffic_bytes_per_launch:"):
-            try:
-                return float(line.split(":", 1)[1].strip())
-            except ValueError:
-                return None
-    return None
+        return None, None
+    try:
+        d = json.loads(p.read_text())
+        return float(d["steady_state_bytes_per_launch"]), "profiles/rope_kv_write_t4096_traffic.json"
+    except (ValueError, KeyError):
+        return None, None
+
+
+def _ref_unavailable(args) -> str:
+    if args.no_reference_gpu:
+        return "skipped (--no-reference-gpu)"
+    from baseline import reference as R
+    return R.why_unavailable()
 
 
 # ------------------------------------------------------------ distributed
@@ -110,6 +126,13 @@ def _barrier(world):
     if world > 1:
         from kani_tts_b200.replicas import barrier
         barrier()
+
+
+def _gather_over_ranks(x: float, world: int, dev) -> list[float]:
+    if world == 1:
+        return [x]
+    from kani_tts_b200.replicas import gather_over_ranks
+    return gather_over_ranks(x, dev)
 
 
 def _max_over_ranks(x: float, world: int, dev) -> float:
@@ -220,29 +243,57 @@ def graph_of(fn_list):
     return g
 
 
-def time_graph_steps(step_fns, steps: int, dev, world: int, chunk: int = 1000):
-    """Replay exactly `steps` launches (cycling step_fns) from CUDA graphs;
-    return (elapsed seconds on this rank, launches captured per full graph)."""
+def time_graph_steps(step_fns, steps: int, dev, world: int, chunk: int = 1000, lead: int = 8):
+    """Replay exactly `steps` launches (cycling step_fns) from CUDA graphs and
+    return the device time of those launches on this rank, in seconds.
+
+    The start and end events are recorded inside the captured graphs (event
+    record nodes): the first graph runs `lead` untimed launches, then records
+    the start event, then its share of the timed launches; the last graph
+    ends with the end event.  The host's graph submission and the graph's own
+    launch latency therefore stay outside the timed region, however few
+    launches it holds."""
+    n = len(step_fns)
     chunk = max(1, min(chunk, steps))
-    full = steps // chunk
-    rest = steps - full * chunk
-    g_full = graph_of([step_fns[i % len(step_fns)] for i in range(chunk)])
-    g_rest = graph_of([step_fns[i % len(step_fns)] for i in range(rest)]) if rest else None
-    # one untimed replay of each graph (first replay uploads the graph)
-    g_full.replay()
-    if g_rest is not None:
-        g_rest.replay()
+    e0 = torch.cuda.Event(enable_timing=True, external=True)
+    e1 = torch.cuda.Event(enable_timing=True, external=True)
+
+    def body(first, count):
+        for i in range(first, first + count):
+            step_fns[i % n]()
+
+    def capture(fn):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        return g
+
+    first = min(chunk, steps)
+    full_rest = steps - first
+    mids, rest = divmod(full_rest, chunk)
+
+    def g_first_body():
+        body(0, lead)
+        e0.record()
+        body(lead, first)
+        if full_rest == 0:
+            e1.record()
+    graphs = [capture(g_first_body)]
+    g_mid = capture(lambda: body(lead + first, chunk)) if mids else None
+    g_last = None
+    if full_rest:
+        def g_last_body():
+            body(lead + first + mids * chunk, rest)
+            e1.record()
+        g_last = capture(g_last_body)
+    seq = graphs + [g_mid] * mids + ([g_last] if g_last is not None else [])
+    for g in {id(g): g for g in seq}.values():   # the first replay uploads each graph
+        g.replay()
     torch.cuda.synchronize(dev)
     _barrier(world)
     torch.cuda.synchronize(dev)
-    st = torch.cuda.current_stream(dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(st)
-    for _ in range(full):
-        g_full.replay()
-    if g_rest is not None:
-        g_rest.replay()
-    e1.record(st)
+    for g in seq:
+        g.replay()
     torch.cuda.synchronize(dev)
     _barrier(world)
     return e0.elapsed_time(e1) / 1e3
@@ -400,34 +451,96 @@ def run_e2e(K, dev, steps: int) -> dict:
     return {"seconds": el, "steps": steps, "h2d": in_bytes, "d2h": out_bytes}
 
 
-def run_sweep(K, dev, peak: float) -> dict:
-    """Every fused op at its configuration sizes, graph-replayed, inputs rotated."""
-    from kani_tts_b200 import positions as P
+def _ref_cache(ref, dev, s_len: int = 2048):
+    """The reference's StaticLfm2HybridConvCache for one attention layer of the
+    decode shapes (16 Q heads, 8 KV heads, head_dim 64)."""
+    import types as _t
+    cfg = _t.SimpleNamespace(num_key_value_heads=HK, head_dim=D, num_hidden_layers=1, hidden_size=HQ * D,
+                             num_attention_heads=HQ, layer_types=["full_attention"], conv_L_cache=3)
+    return ref.static_cache.StaticLfm2HybridConvCache(cfg, max_total_len=s_len, batch_size=1,
+                                                      dtype=torch.bfloat16, device=dev)
+
+
+def _ref_rope_kv_step(ref, q, k, v, inv, pos, cache, qw=None, kw=None):
+    """The reference's RoPE + KV write of one decode token (optimized_decode.py:
+    220-240): optional q/k norm (Triton), cos/sin from inv_freq * position with
+    eager ops, the two Triton RoPE launches, and the cache's scatter_ update."""
+    tk = ref.triton_kernels
+    if qw is not None:
+        q = tk.fused_rms_norm(q, qw, 1e-5)
+        k = tk.fused_rms_norm(k, kw, 1e-5)
+    q = q.reshape(1, HQ, 1, D)
+    k = k.reshape(1, HK, 1, D)
+    freqs = inv * pos[0].float()
+    emb = torch.cat([freqs, freqs])
+    cos, sin = emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16)
+    q, k = tk.fused_rope(q, k, cos, sin)
+    return q, cache.update(k, v.reshape(1, HK, 1, D), 0)
+
+
+def _triton_rms(ref, x, w, y, eps):
+    """The reference's ``_rms_norm_kernel`` launched as ``fused_rms_norm`` launches it
+    (triton_kernels.py:49-59), into a given output."""
+    import triton
+    n = x.shape[-1]
+    ref.triton_kernels._rms_norm_kernel[(x.numel() // n,)](x, w, y, N=n, eps=eps, BLOCK_N=triton.next_power_of_2(n))
+
+
+def _triton_silu(ref, x, y):
+    """The reference's ``_silu_mul_kernel`` launched as ``fused_silu_mul`` launches it
+    (triton_kernels.py:94-103), into a given output."""
+    import triton
+    n = x.shape[-1] // 2
+    ref.triton_kernels._silu_mul_kernel[(x.numel() // (2 * n),)](x, y, N=n, BLOCK_N=triton.next_power_of_2(n))
+
+
+def run_sweep(K, dev, peak: float, ref=None) -> dict:
+    """Every fused op at its configuration sizes, graph-replayed, inputs rotated.
+    With the reference installed (``ref``), its own Triton kernels run on the same
+    inputs as a second column: ``triton_us`` / ``triton_GB_s`` (the same
+    algorithmic bytes).  They are launched as the reference's wrappers launch
+    them (grid, block size) but write into the same rotated output buffers as
+    this library's kernels: the wrappers' fresh ``torch.empty`` output would,
+    inside a CUDA graph, reuse one pooled address every launch and stay in L2,
+    which the rotated outputs here do not."""
     out = {}
     g = torch.Generator().manual_seed(5)
+    tk = ref.triton_kernels if ref is not None else None
 
     def rot_sets(make, nbytes):
         n = int(min(64, max(1, -(-256e6 // max(nbytes, 1)))))
         return [make(i) for i in range(n)]
 
-    def measure(name, fns, nbytes, launches=400):
+    def time_us(fns, launches):
         torch.cuda.synchronize(dev)
         g_ = graph_of([fns[i % len(fns)] for i in range(launches)])
         g_.replay()
         torch.cuda.synchronize(dev)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g_.replay()                     # lead-in: the timed replay is queued while it runs
         e0.record()
         g_.replay()
         e1.record()
         torch.cuda.synchronize(dev)
-        us = e0.elapsed_time(e1) * 1e3 / launches
-        gbs = nbytes / (us * 1e-6) / 1e9
-        out[name] = {"us": round(us, 3), "GB_s": round(gbs, 1), "frac": round(gbs / peak, 4),
-                     "bytes": int(nbytes), "rotated_sets": len(fns)}
         del g_
+        return e0.elapsed_time(e1) * 1e3 / launches
 
-    # add + RMSNorm (config 1 and row sweep)
-    for dtype, rows in [(torch.float32, 8), (torch.bfloat16, 1), (torch.bfloat16, 16384),
+    def measure(name, sets, nbytes, launches=400):
+        us = time_us([s[0] for s in sets], launches)
+        gbs = nbytes / (us * 1e-6) / 1e9
+        row = {"us": round(us, 3), "GB_s": round(gbs, 1), "frac": round(gbs / peak, 4),
+               "bytes": int(nbytes), "rotated_sets": len(sets)}
+        if sets[0][1] is not None:
+            tus = time_us([s[1] for s in sets], launches)
+            row["triton_us"] = round(tus, 3)
+            row["triton_GB_s"] = round(nbytes / (tus * 1e-6) / 1e9, 1)
+            row["speedup_vs_triton"] = round(tus / us, 3)
+        out[name] = row
+
+    # add + RMSNorm (config 1, the 64-stream decode shape, and a row sweep); the
+    # reference's composition is the eager add then the Triton norm
+    # (optimized_decode.py:252 + :280); its fp32 output holds bf16-rounded values
+    for dtype, rows in [(torch.float32, 8), (torch.bfloat16, 1), (torch.bfloat16, 64), (torch.bfloat16, 16384),
                         (torch.bfloat16, 65536), (torch.float32, 16384)]:
         es = torch.tensor([], dtype=dtype).element_size()
         nbytes = rows * 1024 * es * 4 + 1024 * es
@@ -436,7 +549,11 @@ def run_sweep(K, dev, peak: float) -> dict:
             r = torch.randn(rows, 1024, generator=g).to(dtype).to(dev)
             w = (1 + 0.02 * torch.randn(1024, generator=g)).to(dtype).to(dev)
             y, h = torch.empty_like(x), torch.empty_like(x)
-            return lambda: K.fused_add_rms_norm(x, r, w, 1e-5, out=y, residual_out=h)
+            ours = lambda: K.fused_add_rms_norm(x, r, w, 1e-5, out=y, residual_out=h)  # noqa: E731
+            def theirs():   # the eager add (optimized_decode.py:252), then the Triton norm
+                torch.add(x, r, out=h)
+                _triton_rms(ref, h, w, y, 1e-5)
+            return ours, (theirs if tk else None)
         measure(f"add_rms_norm_{str(dtype)[6:]}_{rows}x1024", rot_sets(mk, nbytes), nbytes)
     # SiLU*mul (config 3)
     for t in (1, 64, 512, 4096, 32768):
@@ -444,20 +561,26 @@ def run_sweep(K, dev, peak: float) -> dict:
         def mk(i, t=t):
             x = torch.randn(t, 9216, generator=g).to(torch.bfloat16).to(dev)
             y = torch.empty(t, 4608, dtype=torch.bfloat16, device=dev)
-            return lambda: K.fused_silu_mul(x, out=y)
+            return (lambda: K.fused_silu_mul(x, out=y)), ((lambda: _triton_silu(ref, x, y)) if tk else None)
         measure(f"silu_mul_bf16_T{t}", rot_sets(mk, nbytes), nbytes, launches=100 if t >= 32768 else 400)
-    # RoPE + frame table + KV write (config 2 sweep, plus large-T points beyond it),
-    # and the decode step with q/k norm
+    # RoPE + frame table + KV write (config 2 sweep, plus large-T points beyond it).
+    # The reference has a one-token path only (triton_kernels.py:152-155), so its
+    # column is at T = 1 (without a frame table, which it does not have).
     for t in (1, 64, 512, 4096, 16384, 32768):
         nbytes = t * BYTES_PER_TOKEN
         def mk(i, t=t):
             s = make_inputs(100 + i, t, dev)
             qo = torch.empty(1, t, HQ, D, dtype=torch.bfloat16, device=dev)
+            theirs = None
             if t == 1:
                 p = int(torch.randint(0, 2048, (1,), generator=g))
                 s["pos"].fill_(p)
                 s["slots"].fill_(p)
-            return lambda: launch(K, s, qo)
+                if tk is not None:
+                    rc = _ref_cache(ref, dev)
+                    rc.set_write_position(p)
+                    theirs = lambda: _ref_rope_kv_step(ref, s["q"], s["k"], s["v"], s["inv"], s["pos"], rc)  # noqa: E731
+            return (lambda: launch(K, s, qo)), theirs
         measure(f"rope_kv_write_bf16_T{t}", rot_sets(mk, nbytes), nbytes, launches=100 if t >= 16384 else 400)
     nbytes = BYTES_PER_TOKEN - 128 + 256
     def mk_norm(i):
@@ -465,171 +588,70 @@ def run_sweep(K, dev, peak: float) -> dict:
         qw = (1 + 0.02 * torch.randn(D, generator=g)).to(torch.bfloat16).to(dev)
         kw = (1 + 0.02 * torch.randn(D, generator=g)).to(torch.bfloat16).to(dev)
         qo = torch.empty(1, 1, HQ, D, dtype=torch.bfloat16, device=dev)
-        return lambda: K.fused_rope_kv_write(s["q"].view(1, 1, HQ, D), s["k"].view(1, 1, HK, D),
-                                             s["v"].view(1, 1, HK, D), s["inv"], s["pos"], s["kc"], s["vc"],
-                                             s["slots"], q_norm_w=qw, k_norm_w=kw, q_out=qo)
+        theirs = None
+        if tk is not None:
+            rc = _ref_cache(ref, dev)
+            rc.set_write_position(int(s["slots"][0]))
+            theirs = lambda: _ref_rope_kv_step(ref, s["q"], s["k"], s["v"], s["inv"], s["pos"], rc, qw, kw)  # noqa: E731
+        return (lambda: K.fused_rope_kv_write(s["q"].view(1, 1, HQ, D), s["k"].view(1, 1, HK, D),
+                                              s["v"].view(1, 1, HK, D), s["inv"], s["pos"], s["kc"], s["vc"],
+                                              s["slots"], q_norm_w=qw, k_norm_w=kw, q_out=qo)), theirs
     measure("rope_kv_write_qknorm_decode_bf16", rot_sets(mk_norm, nbytes), nbytes)
-    del P
     return out
 
 
 # ------------------------------------------------------------ decode step
 
-def _eager_rms(x, w, eps):
-    """The reference RMSNorm math (triton_kernels.py:28-35) as eager ops."""
-    xf = x.float()
-    return ((xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)) * w.float()).to(x.dtype)
-
-
-def _make_eager_decoder_cls():
-    """The reference decode step (optimized_decode.py:175-289) with eager PyTorch
-    ops in place of its three Triton kernels and scatter_ for the KV write: the
-    comparison arm for the decode-step latency (the reference's Triton source
-    cannot be shipped to the GPU host).  Attention is the reference's SDPA call
-    over the whole masked static buffer and the short-conv step its eager
-    composition."""
-    import torch.nn.functional as F
-    from kani_tts_b200.decode import FusedDecoder
-
-    class EagerReferenceDecoder(FusedDecoder):
-        fused_greedy_head = False   # the reference's F.linear head and argmax
-
-        def step(self, input_ids, positions, slots, kv_len, mask):
-            b, hq, hk, d = self.batch, self.hq, self.hk, self.d
-            hidden = F.embedding(input_ids, self.embed)
-            for i, L in enumerate(self.layers):
-                normed = _eager_rms(hidden, L["op_norm"], self.eps)
-                if L["attn"]:
-                    qkv = F.linear(normed, L["qkv"])
-                    q, k, v = qkv.split([self.q_dim, self.kv_dim, self.kv_dim], dim=-1)
-                    q = _eager_rms(q.reshape(b, 1, hq, d), L["q_norm"], self.eps).reshape(b, hq, 1, d)
-                    k = _eager_rms(k.reshape(b, 1, hk, d), L["k_norm"], self.eps).reshape(b, hk, 1, d)
-                    v = v.reshape(b, hk, 1, d)
-                    freqs = L["inv_freq"] * positions.float().view(b, 1)           # :229-231
-                    emb = torch.cat([freqs, freqs], dim=-1)
-                    cos = emb.cos().to(self.dtype).view(b, 1, 1, d)
-                    sin = emb.sin().to(self.dtype).view(b, 1, 1, d)
-
-                    def rope(x):                                                  # Triton RoPE math
-                        xf = x.float()
-                        rot = torch.cat([-xf[..., d // 2:], xf[..., : d // 2]], dim=-1)
-                        return (xf * cos.float() + rot * sin.float()).to(self.dtype)
-                    q, k = rope(q), rope(k)
-                    idx = slots.view(b, 1, 1, 1).expand(b, hk, 1, d)               # static_cache.py:135-140
-                    self.k_cache[i].scatter_(2, idx, k)
-                    self.v_cache[i].scatter_(2, idx, v)
-                    # the reference's SDPA over the whole masked buffer (GQA as the reference calls it)
-                    attn = F.scaled_dot_product_attention(q, self.k_cache[i], self.v_cache[i], attn_mask=mask,
-                                                          scale=self.scale, enable_gqa=True)
-                    hidden = hidden + F.linear(attn.reshape(b, 1, self.q_dim), L["o"])
-                else:
-                    hidden = hidden + self._conv_step_eager(i, L, normed)
-                normed = _eager_rms(hidden, L["ffn_norm"], self.eps)
-                gu = F.linear(normed, L["gate_up"])
-                n = gu.shape[-1] // 2
-                mlp = (gu[..., :n].float() * torch.sigmoid(gu[..., :n].float()) * gu[..., n:].float()).to(self.dtype)
-                hidden = hidden + F.linear(mlp, L["down"])
-            # the reference's F.linear on the unpadded reduced head (optimized_decode.py:287)
-            return F.linear(_eager_rms(hidden, self.final_norm, self.eps), self.head)
-
-    return EagerReferenceDecoder
-
-
-def run_decode(dev, world, rank, batch: int, steps: int, prompt: int = 128, eager: bool = False) -> dict:
-    """Synthetic LFM2 (16 layers: 10 short-conv + 6 GQA 16/8/64, H 1024, FF 4608,
-    vocab 80000, random bf16 weights std 0.02): `prompt`-token prefill (plus a
-    128-d speaker embedding inserted at position 1), then `steps` greedy decode
-    tokens per stream from a captured CUDA graph, static cache 2048 slots."""
-    from kani_tts_b200 import _lib
-    from kani_tts_b200.decode import DecodeEngine, FusedDecoder
+def _synthetic(dev, rank: int, batch: int, prompt: int):
+    """The synthetic LFM2 (16 layers: 10 short-conv + 6 GQA 16/8/64, H 1024,
+    FF 4608, vocab 80000, random bf16 weights std 0.02), `prompt` random ids and
+    a 128-d speaker embedding per stream."""
     from kani_tts_b200.model import LFM2Config, synthetic_state_dict
     cfg = LFM2Config()
     sd = synthetic_state_dict(cfg, seed=0, device=dev)
     g = torch.Generator(device="cpu").manual_seed(1 + rank)
     ids = torch.randint(0, cfg.audio_tokens_start, (batch, prompt), generator=g).to(dev)
     spk = torch.randn(batch, cfg.speaker_emb_dim, generator=g).to(dev)
-    out = {}
-    arms = [("fused", FusedDecoder)] + ([("eager_reference", _make_eager_decoder_cls())] if eager else [])
-    for name, cls in arms:
-        eng = DecodeEngine(cls(cfg, sd, dev, batch=batch, max_len=2048), keep_mask=(name != "fused"))
-        eng.start(ids, spk, steps + 8)
-        eng.capture()
-        eng.run(3)                                     # warm-up replays
-        torch.cuda.synchronize(dev)
-        launches0 = _lib.launch_count()
-        _barrier(world)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        eng.run(steps)
-        e1.record()
-        torch.cuda.synchronize(dev)
-        _barrier(world)
-        sec = _max_over_ranks(e0.elapsed_time(e1) / 1e3, world, dev)
-        flags = int(eng.dec.err_flag.item())
-        out[name] = {"us_per_step": round(sec / steps * 1e6, 2),
+    return cfg, sd, ids, spk
+
+
+def run_decode(dev, world, rank, batch: int, steps: int, prompt: int = 128) -> dict:
+    """`prompt`-token prefill (plus the speaker embedding inserted at position 1),
+    then `steps` greedy decode tokens per stream from a captured CUDA graph,
+    static cache 2048 slots."""
+    from kani_tts_b200.decode import DecodeEngine, FusedDecoder
+    cfg, sd, ids, spk = _synthetic(dev, rank, batch, prompt)
+    eng = DecodeEngine(FusedDecoder(cfg, sd, dev, batch=batch, max_len=2048))
+    eng.start(ids, spk, steps + 8)
+    eng.capture()
+    eng.run(3)                                     # warm-up replays
+    torch.cuda.synchronize(dev)
+    _barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    eng.run(steps)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    _barrier(world)
+    sec = _max_over_ranks(e0.elapsed_time(e1) / 1e3, world, dev)
+    out = {"fused": {"us_per_step": round(sec / steps * 1e6, 2),
                      "tokens_per_s": round(world * batch * steps / sec, 1),
-                     "kernel_flags": flags}
-        del eng
-        torch.cuda.empty_cache()
-    if eager:
-        out["speedup_vs_eager_reference"] = round(out["eager_reference"]["us_per_step"] /
-                                                  out["fused"]["us_per_step"], 3)
+                     "kernel_flags": int(eng.dec.err_flag.item())}}
+    del eng
+    torch.cuda.empty_cache()
     out["config"] = (f"bs={batch} x {world} GPU(s), prompt {prompt}+speaker, {steps} decode steps, "
                      "S=2048, CUDA graph, greedy")
     return out
 
 
-def _reference_host_sample(logits, history, f2r, r2f, rp: float, temp: float, top_p: float):
-    """One token as the reference samples it on the host side of its decode loop
-    (KaniInferenceEngine._sample_next_token, inference_engine.py:349-430, reduced
-    vocabulary): eager ops on the device tensors, `unique()` and the implicit sync
-    of `valid.any()`, then `torch.multinomial`."""
-    if rp != 1.0:
-        unique_tokens = history[0].unique()
-        reduced_idx = f2r[unique_tokens]
-        valid = reduced_idx >= 0
-        if valid.any():
-            vr = reduced_idx[valid]
-            pl = logits[0, vr]
-            logits[0, vr] = torch.where(pl > 0, pl / rp, pl * rp)
-    k = min(256, logits.shape[-1])
-    tl, ti = torch.topk(logits, k=k, dim=-1)
-    if temp != 1.0:
-        tl = tl / temp
-    if top_p < 1.0:
-        probs = torch.softmax(tl, dim=-1)
-        cum = torch.cumsum(probs, dim=-1)
-        mask = torch.zeros_like(cum, dtype=torch.bool)
-        mask[..., 1:] = cum[..., :-1] >= top_p
-        tl.masked_fill_(mask, float("-inf"))
-    probs = torch.softmax(tl, dim=-1)
-    idx = torch.multinomial(probs, num_samples=1)
-    return r2f[ti.gather(-1, idx)]
-
-
-def run_decode_sampled(dev, world, rank, batch: int, steps: int, prompt: int = 128,
-                       reference_loop: bool = False) -> dict:
+def run_decode_sampled(dev, world, rank, batch: int, steps: int, prompt: int = 128) -> dict:
     """Decode with the reference's sampling settings (temperature 0.5, top_p 0.85,
-    repetition penalty 1.2, top-k 256; config.py:28-31).
-
-    * fused_sampled: this library's engine, the sampler launched inside the
-      captured step (no host work per token).
-    * reference_loop_host_sampling (bs = 1): the reference decode loop
-      (inference_engine.py:633-667): per token the host writes the token,
-      position, cache slot and mask entry, replays a graph of the eager
-      reference-structure step, samples with eager ops and reads the token
-      back with `.item()`."""
-    from kani_tts_b200 import _lib
+    repetition penalty 1.2, top-k 256; config.py:28-31), the sampler launched
+    inside the captured step (no host work per token)."""
     from kani_tts_b200.decode import DecodeEngine, FusedDecoder
-    from kani_tts_b200.model import LFM2Config, synthetic_state_dict
     from kani_tts_b200.sampling import SamplingParams
-    cfg = LFM2Config()
+    cfg, sd, ids, spk = _synthetic(dev, rank, batch, prompt)
     sp = SamplingParams(seed=7 + rank)
-    sd = synthetic_state_dict(cfg, seed=0, device=dev)
-    g = torch.Generator(device="cpu").manual_seed(1 + rank)
-    ids = torch.randint(0, cfg.audio_tokens_start, (batch, prompt), generator=g).to(dev)
-    spk = torch.randn(batch, cfg.speaker_emb_dim, generator=g).to(dev)
-    out = {}
     eng = DecodeEngine(FusedDecoder(cfg, sd, dev, batch=batch, max_len=2048), sampling=sp)
     eng.start(ids, spk, steps + 8)
     eng.capture()
@@ -644,68 +666,180 @@ def run_decode_sampled(dev, world, rank, batch: int, steps: int, prompt: int = 1
     _barrier(world)
     sec = _max_over_ranks(e0.elapsed_time(e1) / 1e3, world, dev)
     audio = eng.dec.full_to_reduced[eng.generated[:, :steps]] >= 0
-    out["fused_sampled"] = {"us_per_step": round(sec / steps * 1e6, 2),
-                            "tokens_per_s": round(world * batch * steps / sec, 1),
-                            "kernel_flags": int(eng.dec.err_flag.item()),
-                            "tokens_in_reduced_vocab": bool(audio.all())}
+    out = {"fused_sampled": {"us_per_step": round(sec / steps * 1e6, 2),
+                             "tokens_per_s": round(world * batch * steps / sec, 1),
+                             "kernel_flags": int(eng.dec.err_flag.item()),
+                             "tokens_in_reduced_vocab": bool(audio.all())}}
     del eng
     torch.cuda.empty_cache()
-    if reference_loop and batch == 1:
-        dec = _make_eager_decoder_cls()(cfg, sd, dev, batch=1, max_len=2048)
-        logits = dec.prefill(ids, torch.arange(prompt + 1, device=dev).view(1, -1), spk)
-        t_eff = prompt + 1
-        hist = torch.zeros(1, t_eff + steps + 8, dtype=torch.long, device=dev)
-        hist[0, :prompt] = ids[0]
-        gen_len = prompt
-        static_ids = torch.zeros(1, 1, dtype=torch.long, device=dev)
-        static_pos = torch.zeros(1, dtype=torch.long, device=dev)
-        static_slot = torch.zeros(1, dtype=torch.long, device=dev)
-        static_len = torch.zeros(1, dtype=torch.long, device=dev)
-        mask = torch.full((1, 1, 1, 2048), float("-inf"), dtype=torch.bfloat16, device=dev)
-        mask[..., :t_eff] = 0
-        schedule = (t_eff + (torch.arange(steps + 8, device=dev) + 1) // cfg.tokens_per_frame).long()
-        nxt = _reference_host_sample(logits[:, -1].clone(), hist[:, :gen_len], dec.full_to_reduced,
-                                     dec.reduced_to_full, sp.repetition_penalty, sp.temperature, sp.top_p)
-        hist[0, gen_len] = nxt.item()
-        gen_len += 1
-        s = torch.cuda.Stream(device=dev)
-        s.wait_stream(torch.cuda.current_stream(dev))
-        with torch.cuda.stream(s):
-            dec.step(static_ids, static_pos, static_slot, static_len, mask)
-        torch.cuda.current_stream(dev).wait_stream(s)
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            static_logits = dec.step(static_ids, static_pos, static_slot, static_len, mask)
-
-        def one(i):
-            nonlocal nxt, gen_len
-            static_ids.copy_(nxt.view(1, 1))
-            static_pos[0] = schedule[i]
-            off = t_eff + i
-            static_slot[0] = off
-            static_len[0] = off + 1
-            mask[..., off] = 0.0
-            graph.replay()
-            nxt = _reference_host_sample(static_logits[:, -1], hist[:, :gen_len], dec.full_to_reduced,
-                                         dec.reduced_to_full, sp.repetition_penalty, sp.temperature, sp.top_p)
-            hist[0, gen_len] = nxt[0, 0].item()
-            gen_len += 1
-        for i in range(3):
-            one(i)
-        torch.cuda.synchronize(dev)
-        e0.record()
-        for i in range(3, 3 + steps):
-            one(i)
-        e1.record()
-        torch.cuda.synchronize(dev)
-        sec_r = e0.elapsed_time(e1) / 1e3
-        out["reference_loop_host_sampling"] = {"us_per_step": round(sec_r / steps * 1e6, 2),
-                                               "tokens_per_s": round(steps / sec_r, 1)}
-        out["speedup_vs_reference_loop"] = round(sec_r / sec, 3)
-        del graph, dec
-        torch.cuda.empty_cache()
     out["config"] = (f"bs={batch} x {world} GPU(s), prompt {prompt}+speaker, {steps} decode steps, S=2048, "
                      f"sampling T={sp.temperature} top_p={sp.top_p} rp={sp.repetition_penalty} top_k={sp.top_k}")
+    return out
+
+
+def run_reference_decode(dev, ref, steps: int, prompt: int = 128, n_compare: int = 64) -> dict:
+    """The reference's own decode engine at bs = 1 on the same synthetic model and
+    GPU: ``OptimizedDecoder`` with its Triton kernels, captured into a CUDA graph
+    by ``KaniInferenceEngine._initialize_cuda_graphs`` (inference_engine.py:
+    230-331), then the loop body of ``generate`` (inference_engine.py:638-667)
+    for `steps` tokens.
+
+    The reference's HF prefill needs its full HF model class, so the prompt pass
+    is this library's (``DecodeEngine.start``); its KV cache and conv states
+    enter the reference engine through ``_initialize_cuda_graphs`` as the
+    dynamic cache, as the reference's prefill results would.  Two loops:
+
+    * ``reference_triton_graph`` (greedy): per token the loop's host writes
+      (token, position, cache slot, mask slot), the graph replay, then
+      ``reduced_to_full[argmax]`` on the device fed back as the next token
+      — no host synchronisation, the step itself as the reference runs it.
+      Before it, an untimed pass records the reference's first `n_compare`
+      greedy tokens and logits; this library's decode step is then fed the
+      same tokens from the same prefill state and its logits compared
+      (``parity``).
+    * ``reference_engine_sampled``: the same loop with the reference's
+      ``_sample_next_token`` and its per-token ``.item()`` (sampling settings
+      of config.py:28-31), the reference's serving loop.  It runs all `steps`
+      tokens (an EOS does not stop the timing loop; ``eos_sampled`` counts
+      them).
+
+    Audio-count convention: the reference's graph loop starts after one HF
+    decode step, so its index i is audio token i + 1 (position schedule
+    inference_engine.py:615-619).  Here the first decode step is a graph step,
+    so step k is audio token k: position = prefill length + (k // 4) * step."""
+    import types as _t
+    from baseline import reference as R
+    from kani_tts_b200.decode import DecodeEngine, FusedDecoder
+    cfg, sd, ids, spk = _synthetic(dev, 0, 1, prompt)
+    mine = DecodeEngine(FusedDecoder(cfg, sd, dev, batch=1, max_len=2048))
+    mine.start(ids, spk, steps + 8)
+    t_eff = prompt + 1
+    dyn = _t.SimpleNamespace(
+        key_cache=[mine.dec.k_cache[i][:, :, :t_eff].clone() if i in mine.dec.k_cache else torch.empty(0)
+                   for i in range(cfg.num_hidden_layers)],
+        value_cache=[mine.dec.v_cache[i][:, :, :t_eff].clone() if i in mine.dec.v_cache else torch.empty(0)
+                     for i in range(cfg.num_hidden_layers)],
+        conv_cache=[mine.dec.conv_state[i].clone() if i in mine.dec.conv_state else
+                    torch.zeros(1, cfg.hidden_size, cfg.conv_L_cache, dtype=torch.bfloat16, device=dev)
+                    for i in range(cfg.num_hidden_layers)])
+    first = mine.input_ids.clone()
+    mine.capture()
+    mine.run(n_compare)
+    torch.cuda.synchronize(dev)
+    mine_tokens = mine.generated[0, :n_compare].clone()
+    dec = mine.dec
+    mine.graph = None
+
+    math_sdp = torch.backends.cuda.math_sdp_enabled()   # the engine turns the math SDPA off
+    model = R.stand_in_model(ref, cfg, sd, dev)
+    eng = R.engine(ref, model, cfg, max_new_tokens=2048 - 512, temperature=0.5, top_p=0.85,
+                   repetition_penalty=1.2)
+    R.capture(eng, dyn, t_eff)
+    od = eng.optimized_decoder
+    sched = (t_eff + torch.arange(steps + 8, device=dev) // cfg.tokens_per_frame * cfg.audio_step).long()
+    out = {}
+
+    def body(i, next_token):
+        # inference_engine.py:641-651 (the graph branch of the decode loop)
+        eng.static_input_ids.copy_(next_token.view(1, 1))
+        eng.static_position_ids[0, 0] = sched[i]
+        step_offset = t_eff + i
+        eng.static_cache_position[0] = step_offset
+        eng.static_cache.set_write_position(step_offset)
+        eng.static_mask[:, :, :, step_offset] = 0.0
+        eng.cuda_graph.replay()
+        eng.static_cache.advance_position()
+        return eng.static_logits[:, -1, :]
+
+    # parity pass (untimed): the reference's greedy tokens and logits; then this
+    # library's decode step fed the same tokens from the same prefill state
+    ref_logits, ref_inputs = [], [first.view(1, 1)]
+    nt = first.view(1, 1)
+    for i in range(n_compare):
+        lg = body(i, nt)
+        ref_logits.append(lg.clone())
+        nt = od.reduced_to_full[lg.argmax(-1)].view(1, 1)
+        ref_inputs.append(nt.clone())
+    ref_tokens = torch.cat([t.view(-1) for t in ref_inputs[1:]])
+    for i in dec.k_cache:
+        dec.k_cache[i][:, :, :t_eff].copy_(dyn.key_cache[i])
+        dec.v_cache[i][:, :, :t_eff].copy_(dyn.value_cache[i])
+    for i in dec.conv_state:
+        dec.conv_state[i].copy_(dyn.conv_cache[i])
+    errs, coss, agree, clear, agree_clear = [], [], 0, 0, 0
+    for i in range(n_compare):
+        pos = sched[i:i + 1]
+        slot = torch.tensor([t_eff + i], device=dev)
+        mine_lg = dec.step_logits(ref_inputs[i], pos, slot, slot + 1)[:, -1, :].float()
+        rl = ref_logits[i].float()
+        errs.append(float((mine_lg - rl).abs().max() / rl.abs().max()))
+        coss.append(float(torch.nn.functional.cosine_similarity(mine_lg.flatten(), rl.flatten(), dim=0)))
+        same = int(mine_lg.argmax()) == int(rl.argmax())
+        agree += same
+        top2 = rl.flatten().topk(2).values
+        if float(top2[0] - top2[1]) > 2.0 ** -5 * abs(float(top2[0])):
+            clear += 1
+            agree_clear += same
+    same = (ref_tokens == mine_tokens).tolist()
+    parity = {"steps": n_compare, "max_logit_err_frac": round(max(errs), 5), "min_cosine": round(min(coss), 6),
+              "argmax_agree": f"{agree}/{n_compare}", "argmax_agree_where_clear": f"{agree_clear}/{clear}",
+              "free_running_identical_prefix": same.index(False) if False in same else len(same),
+              "how": "teacher-forced: this library's decode step fed the reference's greedy tokens from the "
+                     "same prefill state; clear = top-2 margin above 2^-5 of the top logit"}
+    eng._refresh_static_cache(dyn, t_eff)
+
+    # greedy loop (timed)
+    toks = torch.zeros(steps + 8, dtype=torch.long, device=dev)
+    nt = first.view(1, 1)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for i in range(steps + 3):
+        if i == 3:
+            e0.record()
+        nt = od.reduced_to_full[body(i, nt).argmax(-1)]
+        toks[i] = nt.view(-1)[0]
+    e1.record()
+    torch.cuda.synchronize(dev)
+    sec = e0.elapsed_time(e1) / 1e3
+    out["reference_triton_graph"] = {
+        "us_per_step": round(sec / steps * 1e6, 2), "tokens_per_s": round(steps / sec, 1),
+        "path": "kani_tts OptimizedDecoder (Triton) captured by KaniInferenceEngine._initialize_cuda_graphs; "
+                "generate() loop body with a device-side greedy choice"}
+    out["parity"] = parity
+
+    # the reference's serving loop: its sampler and .item() per token
+    eng._refresh_static_cache(dyn, t_eff)
+    gen = torch.zeros(1, prompt + steps + 16, dtype=torch.long, device=dev)
+    gen[0, :prompt] = ids[0]
+    gen_len = prompt
+    gen[0, gen_len] = int(first.view(-1)[0])
+    gen_len += 1
+    nt = first.view(1, 1)
+    eos = torch.tensor([cfg.eos_token_id], device=dev, dtype=torch.long)
+    prev_is_eos, n_eos = None, 0
+    for i in range(steps + 3):
+        if i == 3:
+            torch.cuda.synchronize(dev)
+            e0.record()
+        logits = body(i, nt)
+        nt = eng._sample_next_token(logits, gen[:, :gen_len])          # :654
+        tid = nt[0, 0].item()                                           # :655
+        gen[0, gen_len] = tid
+        gen_len += 1
+        if prev_is_eos is not None and prev_is_eos.item():             # :661-667 (pipelined EOS check)
+            n_eos += 1
+        prev_is_eos = (nt.view(-1) == eos)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    sec_s = e0.elapsed_time(e1) / 1e3
+    out["reference_engine_sampled"] = {
+        "us_per_step": round(sec_s / steps * 1e6, 2), "tokens_per_s": round(steps / sec_s, 1),
+        "eos_sampled": n_eos,
+        "path": "generate() loop body: graph replay, _sample_next_token, .item() per token"}
+    del eng, model, od, mine, dec
+    torch.backends.cuda.enable_math_sdp(math_sdp)
+    torch.cuda.empty_cache()
+    out["config"] = (f"bs=1, prompt {prompt}+speaker (prefill by this library), {steps} decode steps, "
+                     "static cache 2048 (max(prefill, 512) + 1536), reference sampling T=0.5 top_p=0.85 rp=1.2")
     return out
 
 
@@ -730,6 +864,7 @@ def run_gpu(args, world, rank, local):
         elapsed = time_graph_steps(fns, args.steps, dev, world)
     captured = _lib.launch_count() - c0        # launches recorded into the graphs
     elapsed_max = _max_over_ranks(elapsed, world, dev)
+    per_rank_us = [round(s / args.steps * 1e6, 3) for s in _gather_over_ranks(elapsed, world, dev)]
     flags = _lib.read_and_clear_errors(dev)
     if flags:
         raise RuntimeError(f"kernel error flags set during the bench: {flags}")
@@ -749,23 +884,39 @@ def run_gpu(args, world, rank, local):
                 "path": ("kani_tts_b200.fused_rope_kv_write (ctypes -> kani_rope_kv_write): one pinned "
                          "packed input buffer (Q|K|V rows, positions, slots) and one result buffer (rotated Q, "
                          "K and V caches) per step, copy-in / compute / copy-out streams over two buffer sets")}
+    ref = None
+    if not args.no_reference_gpu:
+        from baseline import reference as R
+        ref = R.import_reference() if R.available() else None
     if not args.no_decode:
-        # decode steps: bs=1 (with the eager reference-structure arm) and 64 streams per GPU
-        extras["decode"] = {"bs1": run_decode(dev, world, rank, 1, args.decode_steps, eager=True),
+        # decode steps: bs=1 and 64 streams per GPU, greedy and sampled
+        extras["decode"] = {"bs1": run_decode(dev, world, rank, 1, args.decode_steps),
                             "bs64": run_decode(dev, world, rank, 64, args.decode_steps),
-                            "bs1_sampled": run_decode_sampled(dev, world, rank, 1, args.decode_steps,
-                                                              reference_loop=(world == 1)),
+                            "bs1_sampled": run_decode_sampled(dev, world, rank, 1, args.decode_steps),
                             "bs64_sampled": run_decode_sampled(dev, world, rank, 64, args.decode_steps)}
+        if rank == 0:
+            # the reference's Triton + CUDA-graph engine on the same GPU (bs = 1)
+            if ref is None:
+                extras["decode"]["bs1_reference"] = {"unavailable": _ref_unavailable(args)}
+            else:
+                r = run_reference_decode(dev, ref, args.decode_steps)
+                mine_g = extras["decode"]["bs1"]["fused"]["us_per_step"]
+                mine_s = extras["decode"]["bs1_sampled"]["fused_sampled"]["us_per_step"]
+                r["speedup_greedy"] = round(r["reference_triton_graph"]["us_per_step"] / mine_g, 3)
+                r["speedup_sampled"] = round(r["reference_engine_sampled"]["us_per_step"] / mine_s, 3)
+                extras["decode"]["bs1_reference"] = r
     copy_ref = None
     if rank == 0:
         copy_ref = same_traffic_copy(dev, STEP_BYTES // 2)
         if not args.no_sweep:
-            extras["sweep"] = run_sweep(K, dev, peak)
+            extras["sweep"] = run_sweep(K, dev, peak, ref)
+            if ref is None:
+                extras["sweep"]["triton"] = {"unavailable": _ref_unavailable(args)}
         if world == 1 and not args.no_cpu:
             cpu = cpu_oracle_rate(args.cpu_seconds)
     if rank != 0:
         return
-    traffic = _traffic_per_launch()
+    traffic, traffic_src = _traffic_per_launch()
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": max(3, args.warmup), "ms_per_step": round(elapsed_max / args.steps * 1e3, 6),
@@ -777,6 +928,7 @@ def run_gpu(args, world, rank, local):
                    "parallelism": f"replicas x{world} (independent streams, no collectives)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": traffic,
+                     "traffic_source": traffic_src,
                      "algorithmic_bytes": STEP_BYTES,
                      "kernel": "rope_bulk_kernel<bf16, NORM=0, TABLE=1, QI=2, KI=1, LOG2L=2>",
                      "same_traffic_copy": (None if copy_ref is None else
@@ -784,6 +936,7 @@ def run_gpu(args, world, rank, local):
         "e2e": e2e_line,
         "gpu_launches": args.steps,
         "graph_launches_captured": captured,
+        "us_per_launch_by_rank": per_rank_us,
         "clocks": clocks.summary(),
     }
     if cpu is not None:
@@ -805,6 +958,7 @@ def same_traffic_copy(dev, nbytes: int, sets: int = 8, launches: int = 1000) -> 
     g.replay()
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g.replay()                           # lead-in, untimed
     e0.record()
     g.replay()
     e1.record()
@@ -924,6 +1078,8 @@ def main():
     ap.add_argument("--no-sweep", action="store_true", help="skip the per-op sweep")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode-step measurements")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="skip the reference's Triton kernels and Triton + CUDA-graph engine on the GPU")
     ap.add_argument("--decode-steps", type=int, default=1500)
     ap.add_argument("--decode-only", action="store_true", help="profiling aid: run only the decode arms")
     ap.add_argument("--decode-batch", type=int, default=1, help="streams for --decode-only")
@@ -943,9 +1099,12 @@ def main():
         world, rank, local = _dist_init()
         dev = torch.device("cuda", local)
         torch.cuda.set_device(dev)
-        res = run_decode(dev, world, rank, args.decode_batch, args.decode_steps, eager=args.decode_batch == 1)
-        res_s = run_decode_sampled(dev, world, rank, args.decode_batch, args.decode_steps,
-                                   reference_loop=(world == 1 and args.decode_batch == 1))
+        res = run_decode(dev, world, rank, args.decode_batch, args.decode_steps)
+        res_s = run_decode_sampled(dev, world, rank, args.decode_batch, args.decode_steps)
+        if rank == 0 and args.decode_batch == 1 and not args.no_reference_gpu:
+            from baseline import reference as R
+            if R.available():
+                res["reference"] = run_reference_decode(dev, R.import_reference(), args.decode_steps)
         if rank == 0:
             print(json.dumps({"decode": res, "decode_sampled": res_s}), flush=True)
         return

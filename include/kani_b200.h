@@ -67,6 +67,19 @@ KANI_API const char* kani_status_string(int status);
 KANI_API uint64_t kani_launch_count(void);
 
 /*
+ * Bound of the on-chip waits of later launches (the TMA mbarrier waits of the
+ * bulk RoPE + KV-write kernel and of decode attention), in clock64 cycles;
+ * 0 restores the default (about 1 s, with a 1 ms suspend hint per try).  A
+ * nonzero limit also turns the suspend hint off, so a wait can run out while
+ * its copies are still in flight: the kernel then ORs KANI_FLAG_TIMEOUT into
+ * its error flag, lets its own copies land (with the default bound) and
+ * returns; its outputs for that launch are not valid.  A diagnostic for tests
+ * of that path, process-wide.  No counterpart in the reference, whose Triton
+ * kernels have no on-chip waits.  Returns KANI_ERR_INVALID_ARG for cycles < 0.
+ */
+KANI_API int kani_set_wait_limit(int64_t cycles);
+
+/*
  * RMSNorm over the last dimension:  y = round(x * rsqrt(mean(x^2) + eps) * w).
  * Replaces `_rms_norm_kernel` and its launch in `fused_rms_norm`
  * (kani_tts/triton_kernels.py:17-35, :38-60).  Unlike the reference, an fp32
@@ -305,7 +318,9 @@ KANI_API int kani_head_argmax(int32_t dtype, const void* hidden, int64_t hidden_
  * current) and keeps it: make that first call before any stream capture.
  * batch + 1 above 64 returns KANI_ERR_UNSUPPORTED before any launch (the kernel
  * itself serves up to 8 streams).  All calls on a device share the array, so
- * calls that overlap on the GPU race; issue them on one stream.
+ * calls that overlap on the GPU race; issue them on one stream.  The cached
+ * address belongs to the device's primary context: after cudaDeviceReset do
+ * not call this entry point again in the same process.
  */
 KANI_API int kani_head_argmax_noalloc(int32_t dtype, const void* hidden, int64_t hidden_row_stride,
                      int64_t batch, int32_t hidden_size, const void* weight,

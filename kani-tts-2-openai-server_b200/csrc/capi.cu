@@ -8,13 +8,37 @@
 namespace kani {
 namespace {
 std::atomic<uint64_t> g_launches{0};
+std::atomic<long long> g_wait_limit{0};  // 0: the default bound of each kernel
 }  // namespace
 
+WaitBound wait_bound(long long default_cycles) {
+  const long long c = g_wait_limit.load(std::memory_order_relaxed);
+  if (c <= 0) return WaitBound{default_cycles, kWaitSuspendNs};
+  return WaitBound{c, 0u};
+}
+
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+int sm_count() {
+  static std::atomic<int> cached[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  int n = cached[dev].load(std::memory_order_relaxed);
+  if (n > 0) return n;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+  cached[dev].store(n, std::memory_order_relaxed);
+  return n;
+}
 
 }  // namespace kani
 
 extern "C" int kani_version(void) { return 100; }
+
+extern "C" int kani_set_wait_limit(int64_t cycles) {
+  if (cycles < 0) return KANI_ERR_INVALID_ARG;
+  kani::g_wait_limit.store((long long)cycles, std::memory_order_relaxed);
+  return KANI_OK;
+}
 
 extern "C" uint64_t kani_launch_count(void) {
   return kani::g_launches.load(std::memory_order_relaxed);

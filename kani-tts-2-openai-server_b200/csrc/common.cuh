@@ -183,6 +183,23 @@ __host__ __device__ __forceinline__ bool aligned16(const void* p) {
 // Host-side launch accounting (number of kernels this library launched).
 void note_launch();
 
+// Streaming multiprocessors of the current device (queried once per device).
+int sm_count();
+
+// Bound of a kernel's on-chip waits (TMA mbarrier phases): clock64 cycles
+// before the wait gives up and sets KANI_FLAG_TIMEOUT, and the suspend-time
+// hint (ns) of each mbarrier.try_wait.  By default about 1 s with a 1 ms
+// hint; kani_set_wait_limit(c) makes later launches give up after c cycles
+// with no suspension, so a test can make a real wait run out while its copies
+// still land.  Only a kernel's first wait on a stage takes the limit; the
+// drain of copies still in flight keeps the default bound.
+struct WaitBound {
+  long long cycles;
+  unsigned suspend_ns;
+};
+constexpr unsigned kWaitSuspendNs = 1000000u;
+WaitBound wait_bound(long long default_cycles);
+
 // Dispatch a runtime dtype code to a C++ type and invoke f.template
 // operator()<T>().  Returns KANI_ERR_DTYPE for unknown codes.
 template <typename F>

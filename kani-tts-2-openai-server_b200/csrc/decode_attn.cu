@@ -48,6 +48,8 @@ struct AttnParams {
   int64_t ob, oh;  // strides of out [B, Hq, D]
   float qscale;    // scale * log2(e)
   int32_t* err;
+  long long wait_cycles = 0;  // bound of each tile's first mbarrier wait (WaitBound)
+  unsigned wait_suspend_ns = 0;
 };
 
 // 2^x with the hardware approximation (ex2.approx: relative error ~2^-22,
@@ -246,23 +248,39 @@ __device__ __forceinline__ uint32_t attn_smem_u32(const void* ptr) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(ptr));
 }
 
-__device__ __forceinline__ bool attn_try_wait(uint32_t bar, uint32_t parity) {
+// One wait attempt.  With a suspend hint the thread may sleep (up to the hint,
+// in ns) until the phase completes, so a waiting warp leaves the issue slots
+// free; with none (a test's short limit) it only tests the phase, since a
+// try_wait without a hint may still block for a system-defined time.
+__device__ __forceinline__ bool attn_try_wait(uint32_t bar, uint32_t parity, uint32_t suspend_ns) {
   uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity), "r"(1000000u)
-      : "memory");
+  if (suspend_ns == 0) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(suspend_ns)
+        : "memory");
+  }
   return ok != 0;
 }
 
-__device__ __forceinline__ bool attn_wait_bounded(uint32_t bar, uint32_t parity) {
-  if (attn_try_wait(bar, parity)) return true;
+__device__ __forceinline__ bool attn_wait_bounded(uint32_t bar, uint32_t parity,
+                                                  long long limit = kAttnWaitCycles,
+                                                  uint32_t suspend_ns = kWaitSuspendNs) {
+  if (attn_try_wait(bar, parity, suspend_ns)) return true;
   const long long start = clock64();
-  while (!attn_try_wait(bar, parity)) {
-    if (clock64() - start > kAttnWaitCycles) return false;
+  while (!attn_try_wait(bar, parity, suspend_ns)) {
+    if (clock64() - start > limit) return false;
   }
   return true;
 }
@@ -363,7 +381,8 @@ decode_attn_kernel(AttnParams p) {
   int t_fail = ntiles;
   for (int t = 0; t < ntiles; ++t) {
     const int st = t % kAttnStages;
-    if (!failed && !attn_wait_bounded(attn_smem_u32(&bars[st]), (uint32_t)((t / kAttnStages) & 1))) {
+    if (!failed && !attn_wait_bounded(attn_smem_u32(&bars[st]), (uint32_t)((t / kAttnStages) & 1),
+                                      p.wait_cycles, p.wait_suspend_ns)) {
       failed = true;
       t_fail = t;
       if (lane == 0 && p.err != nullptr) atomicOr(p.err, KANI_FLAG_TIMEOUT);
@@ -579,6 +598,9 @@ int decode_attention_impl(int32_t dtype, int64_t batch, int32_t num_q_heads, int
   kani::AttnParams p{q, q_batch_stride, q_head_stride, k_cache, v_cache, cache_batch_stride,
                      cache_head_stride, cache_slot_stride, cache_len, kv_len, out, out_batch_stride,
                      out_head_stride, scale * 1.4426950408889634f, err_flag};
+  const kani::WaitBound wb = kani::wait_bound(kani::kAttnWaitCycles);
+  p.wait_cycles = wb.cycles;
+  p.wait_suspend_ns = wb.suspend_ns;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return kani::dispatch_dtype(dtype, [&]<typename T>() -> int {
     constexpr int E = kani::VecN<T>::value;

@@ -16,6 +16,8 @@
 // atomicMax in global scratch; the last CTA to finish (a counter after a
 // fence) writes the tokens and returns the scratch to zero, so the next launch
 // (e.g. the next replay of a CUDA graph) starts clean.
+#include <atomic>
+
 #include "common.cuh"
 
 namespace kani {
@@ -250,17 +252,24 @@ static_assert(kStaticScratchWords >= kHeadMaxB + 1, "static scratch too small");
 
 static __device__ __align__(256) unsigned long long g_head_scratch[kani::kStaticScratchWords];
 
+// The array's device address, looked up once per device (with that device
+// current) and cached.  The slots are atomic, so first calls from several host
+// threads at once store the same address without a data race.  The cache
+// outlives the device's primary context: after cudaDeviceReset the entry point
+// must not be called again in this process (it would pass the old address).
 static unsigned long long* head_static_scratch() {
   constexpr int kMaxDevices = 64;
-  static unsigned long long* addr[kMaxDevices] = {};
+  static std::atomic<unsigned long long*> addr[kMaxDevices] = {};
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
-  if (!addr[dev]) {
+  unsigned long long* a = addr[dev].load(std::memory_order_acquire);
+  if (!a) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_head_scratch) != cudaSuccess) return nullptr;
-    addr[dev] = static_cast<unsigned long long*>(p);
+    a = static_cast<unsigned long long*>(p);
+    addr[dev].store(a, std::memory_order_release);
   }
-  return addr[dev];
+  return a;
 }
 
 extern "C" int kani_head_argmax_noalloc(int32_t dtype, const void* hidden, int64_t hidden_row_stride,

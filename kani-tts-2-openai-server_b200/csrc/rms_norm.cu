@@ -228,13 +228,18 @@ int launch_norm(const NormParams& p, cudaStream_t s) {
     while ((1 << log2g) < nvec && log2g < 5) ++log2g;
     const int G = 1 << log2g;
     const int per = (nvec + G - 1) / G;
-    const int rows_per_block = 128 / G;
+    // 128-thread blocks, narrowed (down to one warp) while the grid would leave
+    // SMs idle: 64 decode rows of 1024 take 64 one-warp CTAs instead of 16
+    int bt = 128;
+    const int64_t want = 2LL * sm_count();
+    while (bt > 32 && (p.rows * G + bt - 1) / bt < want) bt >>= 1;
+    const int rows_per_block = bt / G;
     const int64_t grid = (p.rows + rows_per_block - 1) / rows_per_block;
     if (grid > 0x7fffffff) return KANI_ERR_UNSUPPORTED;
-    if (per <= 1)      norm_group_kernel<T, W, 1, RES><<<(unsigned)grid, 128, 0, s>>>(p, log2g);
-    else if (per <= 2) norm_group_kernel<T, W, 2, RES><<<(unsigned)grid, 128, 0, s>>>(p, log2g);
-    else if (per <= 4) norm_group_kernel<T, W, 4, RES><<<(unsigned)grid, 128, 0, s>>>(p, log2g);
-    else               norm_group_kernel<T, W, 8, RES><<<(unsigned)grid, 128, 0, s>>>(p, log2g);
+    if (per <= 1)      norm_group_kernel<T, W, 1, RES><<<(unsigned)grid, bt, 0, s>>>(p, log2g);
+    else if (per <= 2) norm_group_kernel<T, W, 2, RES><<<(unsigned)grid, bt, 0, s>>>(p, log2g);
+    else if (per <= 4) norm_group_kernel<T, W, 4, RES><<<(unsigned)grid, bt, 0, s>>>(p, log2g);
+    else               norm_group_kernel<T, W, 8, RES><<<(unsigned)grid, bt, 0, s>>>(p, log2g);
     return launch_status();
   }
   const unsigned grid = (unsigned)(p.rows < kMaxGrid ? p.rows : kMaxGrid);

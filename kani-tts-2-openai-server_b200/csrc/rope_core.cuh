@@ -39,6 +39,8 @@ struct RopeParams {
   int64_t cbs, chs, css, clen;
   const int64_t* slots;
   int32_t* err;
+  long long wait_cycles;  // bound of the bulk kernel's first mbarrier wait (WaitBound)
+  unsigned wait_suspend_ns;
 };
 
 struct TokenMeta {

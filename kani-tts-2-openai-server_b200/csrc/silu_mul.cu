@@ -3,15 +3,17 @@
 // Reference: kani_tts/triton_kernels.py:67-105 — fp32 math
 // (gate * sigmoid(gate)) * up, one rounding to the storage type.
 //
-// Launch shape: the output row is split into 16-byte column vectors; a 2-D
-// grid gives each thread one column vector of RY consecutive rows, so every
-// thread has 2*RY independent 16-byte loads in flight before it computes.
-// grid.x covers the columns with a block width that divides the vector count
-// when it can (n = 4608 bf16 -> 576 vectors = 3 x 192 threads); grid.y
-// strides over row groups.  At one row (the decode step) the op spreads over
-// grid.x CTAs instead of the reference's single program.  Inputs are read
-// once, so they use evict-first loads; the output stays L2-resident for the
-// down-projection GEMV that consumes it.
+// Launch shapes (measured on B200 against the reference's one-program-per-row
+// Triton kernel, bf16 [T, 2 x 4608]):
+//   * T >= 2048: one 192-thread CTA per row; each thread loads all of its
+//     16-byte gate and up vectors of that row (3 + 3 at n = 4608) before it
+//     computes (T = 4096: 18.6 us, T = 32768: 128.5 us).
+//   * shorter calls: a 2-D grid of 16-byte column vectors x rows, one row per
+//     thread; the block narrows to 64 threads while the grid would leave SMs
+//     idle (T = 512: 4.1 us; T = 64: 9 x 64 CTAs, 2.0 us; T = 1: 9 CTAs, 1.3
+//     us, against the reference's single program).
+// Inputs are read once; the output stays L2-resident for the down-projection
+// GEMV that consumes it.
 #include "common.cuh"
 
 namespace kani {
@@ -49,6 +51,41 @@ silu_mul_vec_kernel(const T* __restrict__ gu, int64_t in_stride, T* __restrict__
   }
 }
 
+// Long calls: one CTA per row (grid-stride), like one program per row, so a
+// CTA reads one contiguous gate row and one up row; each thread issues all
+// of its CV gate and CV up vectors before it computes.  Plain loads: here the
+// evict-first hint measured slower (T = 4096: 18.6 against 19.3 us).
+template <typename T, int CV>
+__global__ void __launch_bounds__(192)
+silu_mul_row_kernel(const T* __restrict__ gu, int64_t in_stride, T* __restrict__ y, int64_t out_stride,
+                    int64_t rows, int vpr, int64_t n) {
+  constexpr int E = VecN<T>::value;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const T* base = gu + r * in_stride;
+    uint4 g[CV], u[CV];
+#pragma unroll
+    for (int j = 0; j < CV; ++j) {
+      const int c = j * 192 + threadIdx.x;
+      if (c < vpr) {
+        g[j] = ld16(base + (int64_t)c * E);
+        u[j] = ld16(base + n + (int64_t)c * E);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < CV; ++j) {
+      const int c = j * 192 + threadIdx.x;
+      if (c < vpr) {
+        float gf[E], uf[E], o[E];
+        unpack16<T>(g[j], gf);
+        unpack16<T>(u[j], uf);
+#pragma unroll
+        for (int e = 0; e < E; ++e) o[e] = silu_mul_f(gf[e], uf[e]);
+        st16(y + r * out_stride + (int64_t)c * E, pack16<T>(o));
+      }
+    }
+  }
+}
+
 // Any n / alignment: one thread per output element of a row chunk.
 template <typename T>
 __global__ void __launch_bounds__(256)
@@ -63,6 +100,8 @@ silu_mul_generic_kernel(const T* __restrict__ gu, int64_t in_stride, T* __restri
     y[r * out_stride + c] = Elem<T>::from_f(silu_mul_f(g, u));
   }
 }
+
+constexpr int64_t kRowKernelMinRows = 2048;
 
 int pick_block_width(int vpr) {
   const int cand[] = {256, 192, 128, 96, 64};
@@ -80,19 +119,32 @@ int launch_silu(const void* gu, int64_t in_stride, void* y, int64_t out_stride, 
                    (out_stride % E) == 0 && n / E <= 0x7fffffff;
   if (vec) {
     const int vpr = (int)(n / E);
-    const int bx = pick_block_width(vpr);
-    const unsigned gx = (unsigned)((vpr + bx - 1) / bx);
-    constexpr int RY = 4;
-    const int64_t groups = (rows + RY - 1) / RY;
-    const unsigned gy = (unsigned)(groups < 65535 ? groups : 65535);
-    if (rows >= RY) {
-      silu_mul_vec_kernel<T, RY><<<dim3(gx, gy), bx, 0, s>>>(
-          static_cast<const T*>(gu), in_stride, static_cast<T*>(y), out_stride, rows, vpr, n);
-    } else {
-      const unsigned gy1 = (unsigned)rows;
-      silu_mul_vec_kernel<T, 1><<<dim3(gx, gy1), bx, 0, s>>>(
-          static_cast<const T*>(gu), in_stride, static_cast<T*>(y), out_stride, rows, vpr, n);
+    const int cv = (vpr + 191) / 192;
+    if (rows >= kRowKernelMinRows && cv <= 8) {
+      const unsigned grid = (unsigned)(rows < 0x7fffffff ? rows : 0x7fffffff);
+      auto go = [&](auto kern) {
+        kern<<<grid, 192, 0, s>>>(static_cast<const T*>(gu), in_stride, static_cast<T*>(y), out_stride, rows,
+                                  vpr, n);
+      };
+      if (cv <= 2)      go(silu_mul_row_kernel<T, 2>);
+      else if (cv <= 3) go(silu_mul_row_kernel<T, 3>);
+      else if (cv <= 4) go(silu_mul_row_kernel<T, 4>);
+      else if (cv <= 6) go(silu_mul_row_kernel<T, 6>);
+      else              go(silu_mul_row_kernel<T, 8>);
+      return launch_status();
     }
+    // shorter calls: one row per thread, and narrower blocks while the grid
+    // would leave SMs idle (T = 64: 9 x 64 CTAs of 64 threads)
+    int bx = pick_block_width(vpr);
+    unsigned gx = (unsigned)((vpr + bx - 1) / bx);
+    const int64_t want = 2LL * sm_count();
+    if ((int64_t)gx * rows < want && bx > 64) {
+      bx = 64;
+      gx = (unsigned)((vpr + bx - 1) / bx);
+    }
+    const unsigned gy = (unsigned)(rows < 65535 ? rows : 65535);
+    silu_mul_vec_kernel<T, 1><<<dim3(gx, gy), bx, 0, s>>>(static_cast<const T*>(gu), in_stride,
+                                                          static_cast<T*>(y), out_stride, rows, vpr, n);
     return launch_status();
   }
   const int64_t gx64 = (n + 255) / 256;

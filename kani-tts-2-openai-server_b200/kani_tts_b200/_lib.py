@@ -39,6 +39,7 @@ _SIGNATURES = {
     "kani_version": ([], ctypes.c_int),
     "kani_status_string": ([ctypes.c_int], ctypes.c_char_p),
     "kani_launch_count": ([], ctypes.c_uint64),
+    "kani_set_wait_limit": ([_c_i64], ctypes.c_int),
     "kani_rms_norm": ([_c_i32, _c_i32, _c_p, _c_i64, _c_p, _c_p, _c_i64, _c_i64, _c_i64, _c_f32, _c_p],
                       ctypes.c_int),
     "kani_add_rms_norm": ([_c_i32, _c_i32, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_p, _c_i64, _c_p, _c_i64,
@@ -128,6 +129,12 @@ def status_string(code: int) -> str:
 
 def launch_count() -> int:
     return int(load_library().kani_launch_count())
+
+
+def set_wait_limit(cycles: int) -> None:
+    """Bound the kernels' on-chip TMA waits to `cycles` (0: the default ~1 s);
+    a test of the timeout path (KANI_FLAG_TIMEOUT).  Process-wide."""
+    check(load_library().kani_set_wait_limit(int(cycles)), "kani_set_wait_limit")
 
 
 def check(code: int, op: str) -> None:

@@ -181,6 +181,12 @@ class FusedDecoder:
         ``mask`` is accepted for interface parity with the reference step and
         ignored: the valid region is the prefix [0, kv_len).  Returns
         reduced-head logits [B, 1, num_reduced].
+
+        Every stream must write its newest valid row: ``slots[b] == kv_len[b] - 1``
+        (as ``DecodeEngine`` keeps them).  Where ``dependent_attention`` holds
+        (one stream, or more than 4), the attention launch streams the rows
+        below ``kv_len - 1`` while the RoPE + KV write before it still runs, so
+        a step that wrote any other row would be read before the write lands.
         """
         return self._linear_head(self._final_hidden(input_ids, positions, slots, kv_len))
 

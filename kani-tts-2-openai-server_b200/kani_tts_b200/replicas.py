@@ -39,6 +39,16 @@ def sum_over_ranks(x: float, device="cpu") -> float:
     return _reduce(x, dist.ReduceOp.SUM if dist.is_available() else None, device)
 
 
+def gather_over_ranks(x: float, device="cpu") -> list[float]:
+    """Every rank's value of a per-rank scalar, in rank order (one all-gather)."""
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return [float(x)]
+    t = torch.tensor([float(x)], dtype=torch.float64, device=device)
+    out = [torch.empty_like(t) for _ in range(dist.get_world_size())]
+    dist.all_gather(out, t)
+    return [float(v.item()) for v in out]
+
+
 def aggregate_throughput(units: float, seconds: float, device="cpu") -> tuple[float, float, float]:
     """(total units, slowest rank's seconds, units per second for the whole job)."""
     total = sum_over_ranks(units, device)

@@ -650,6 +650,77 @@ def test_decode_attention_step_after_the_kv_write(b, lens):
     assert _lib.read_and_clear_errors(DEV) == 0
 
 
+def _lens(b: int, seed: int) -> list[int]:
+    """Valid lengths for b streams: the newest row in a first-stage tile (100
+    slots), in a later tile (1629), at both ends (1, 2048), and seeded others."""
+    fixed = [100, 1629, 1, 2048, 65]
+    g = torch.Generator().manual_seed(seed)
+    extra = torch.randint(1, 2049, (max(0, b - len(fixed)),), generator=g).tolist()
+    return (fixed + extra)[:b]
+
+
+@pytest.mark.parametrize("b", [5, 8, 64])
+def test_decode_attention_step_after_the_token_rope_kv_write(b):
+    """kani_decode_attention_step behind the token-kernel RoPE + KV write
+    (fused_rope_kv_write with q/k norm on packed QKV views, the producer of the
+    5-64-stream decode paths), which releases its dependents at entry and
+    writes q and each stream's newest row: bit-identical to
+    kani_decode_attention, eagerly and replayed from a CUDA graph, and close to
+    the oracle.  Each stream's newest row first holds other values, so a read
+    of the stale row would change the output."""
+    hq, hk, d, s_len = 16, 8, 64, 2048
+    kv_len = torch.tensor(_lens(b, 1140 + b), dtype=torch.long)
+    slots = kv_len - 1
+    qkv = gpu(rnd((b, 1, (hq + 2 * hk) * d), 1141))
+    qv = qkv[..., :hq * d].view(b, 1, hq, d)
+    kv = qkv[..., hq * d:(hq + hk) * d].view(b, 1, hk, d)
+    vv = qkv[..., (hq + hk) * d:].view(b, 1, hk, d)
+    qw = gpu((1.0 + 0.1 * rnd((d,), 1142, torch.float32)).to(torch.bfloat16))
+    kw = gpu((1.0 + 0.1 * rnd((d,), 1143, torch.float32)).to(torch.bfloat16))
+    inv = gpu(P.learnable_inv_freq(d, 1e6, 0.0))
+    kc0, vc0 = rnd((b, hk, s_len, d), 1144), rnd((b, hk, s_len, d), 1145)
+    pos, sl, kl = gpu(slots // 4 + 3), gpu(slots), gpu(kv_len)
+
+    def chain(prefix_final, kc, vc, out):
+        q_rot = K.fused_rope_kv_write(qv, kv, vv, inv, pos, kc, vc, sl, q_norm_w=qw, k_norm_w=kw, eps=1e-5)
+        return K.decode_attention(q_rot, kc, vc, kl, out=out, prefix_final=prefix_final)
+
+    runs = {}
+    for mode in (False, True):
+        kc, vc = gpu(kc0), gpu(vc0)
+        out = torch.empty(b, hq, d, dtype=torch.bfloat16, device=DEV)
+        chain(mode, kc, vc, out)
+        torch.cuda.synchronize()
+        runs[mode] = (out.clone(), kc.clone(), vc.clone())
+        # captured and replayed from a fresh cache copy: the stale rows are back in place
+        kc.copy_(gpu(kc0))
+        vc.copy_(gpu(vc0))
+        s = torch.cuda.Stream(device=DEV)
+        s.wait_stream(torch.cuda.current_stream(DEV))
+        with torch.cuda.stream(s):
+            chain(mode, kc, vc, out)
+        torch.cuda.current_stream(DEV).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            chain(mode, kc, vc, out)
+        for _ in range(3):
+            kc.copy_(gpu(kc0))
+            vc.copy_(gpu(vc0))
+            out.zero_()
+            g.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(out, runs[mode][0])
+            assert torch.equal(kc, runs[mode][1]) and torch.equal(vc, runs[mode][2])
+    assert torch.equal(runs[True][0], runs[False][0])
+    for i in range(b):   # the newest rows were rewritten
+        assert not torch.equal(runs[True][1][i, :, int(slots[i])].cpu(), kc0[i, :, int(slots[i])])
+    q_rot = K.fused_rope_kv_write(qv, kv, vv, inv, pos, gpu(kc0), gpu(vc0), sl, q_norm_w=qw, k_norm_w=kw, eps=1e-5)
+    ref = O.decode_attention_ref(q_rot.reshape(b, hq, d).cpu(), runs[True][1].cpu(), runs[True][2].cpu(), kv_len,
+                                 d ** -0.5)
+    assert_attention_close(runs[True][0], ref)
+    assert _lib.read_and_clear_errors(DEV) == 0
+
+
 @pytest.mark.parametrize("b,h", [(1, 1024), (64, 1024), (3, 256)])
 def test_short_conv_step_bit_exact_vs_eager(b, h):
     bcx = rnd((b, 3 * h), 1200)

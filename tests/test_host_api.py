@@ -46,6 +46,15 @@ def _null():
     return ctypes.c_void_p(0)
 
 
+def test_wait_limit_setter():
+    lib = _lib.load_library()
+    assert lib.kani_set_wait_limit(-1) == -1
+    assert lib.kani_set_wait_limit(100) == 0
+    assert lib.kani_set_wait_limit(0) == 0        # back to the default bound
+    with pytest.raises(_lib.KaniError):
+        _lib.set_wait_limit(-5)
+
+
 def test_abi_rejects_bad_arguments_without_launching():
     lib = _lib.load_library()
     before = lib.kani_launch_count()

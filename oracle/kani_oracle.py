@@ -118,6 +118,20 @@ def rope_ref(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, rounding: st
     return _store(_rope_f32(_f32(x), _f32(cos).reshape(d), _f32(sin).reshape(d)), x.dtype, rounding)
 
 
+def rope_compose_ref(xn: torch.Tensor, cos_rows: torch.Tensor, sin_rows: torch.Tensor,
+                     table_rows: torch.Tensor | None = None) -> torch.Tensor:
+    """The rotation half of ``rope_kv_write_ref`` on given inputs: heads xn
+    [N, H, D] (already normed and rounded), one cos and one sin row [N, D] per
+    token (already rounded), optional frame rows [N, D]; rotate-half in fp32
+    (triton_kernels.py:121-130), the frame row added in fp32, one rounding to
+    xn's dtype.  Used to check a kernel's rotation given its own cos/sin and
+    norm outputs."""
+    out = _rope_f32(_f32(xn), _f32(cos_rows).unsqueeze(1), _f32(sin_rows).unsqueeze(1))
+    if table_rows is not None:
+        out = out + _f32(table_rows).unsqueeze(1)
+    return out.to(xn.dtype)
+
+
 def rope_cos_sin_ref(inv_freq: torch.Tensor, pos, dtype=torch.bfloat16):
     """cos/sin rows of one decode step (optimized_decode.py:229-234):
     freqs = inv_freq * float(pos) (fp32); emb = cat(freqs, freqs); cos/sin

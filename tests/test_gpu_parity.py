@@ -12,7 +12,11 @@ Tolerances (written per test):
     the sum-of-squares order differ between CPU and GPU) can become several
     ULPs of a small, cancelled output.  An element passes when it is within
     1 ULP or within 2^-8 x the largest magnitude of its head vector (the size
-    of such a one-ULP input change); >= 99 % of elements are bit-identical;
+    of such a one-ULP input change); at most 0.1 % of elements lie beyond
+    2 ULP; >= 99 % of elements are bit-identical.  Given the kernel's own
+    cos/sin and normed inputs the oracle reproduces its outputs bit for bit,
+    and every element beyond 2 ULP is shown to sit on a differing input
+    (test_rope_deviation_traces_to_cos_sin_and_norm_inputs);
   * KV-cache slots and V copies: bit-exact, and no other slot changes.
 """
 from __future__ import annotations
@@ -50,13 +54,20 @@ def assert_close_ulp(got, ref, max_ulp=1, min_exact=0.999):
         assert float((d == 0).float().mean()) >= min_exact, f"exact fraction {float((d == 0).float().mean())}"
 
 
-def assert_rope_close(got, ref, min_exact=0.99):
+def assert_rope_close(got, ref, min_exact=0.99, max_far_frac=1e-3):
+    """RoPE outputs with in-kernel cos/sin against the oracle: every element within
+    1 ULP, or within 2^-8 of its head's largest magnitude; at most `max_far_frac`
+    of the elements beyond 2 ULP (each of those traces to a 1-ULP cos/sin or
+    norm input: test_rope_deviation_traces_to_cos_sin_and_norm_inputs); at
+    least `min_exact` bit-identical."""
     got, ref = got.cpu(), ref.cpu()
     d = ulp(got, ref)
     scale = ref.float().abs().amax(dim=-1, keepdim=True) * 2.0 ** -8
     ok = (d <= 1) | ((got.float() - ref.float()).abs() <= scale)
+    far = int((d > 2).sum())
     assert bool(ok.all()), f"{int((~ok).sum())} elements outside tolerance, max ULP {int(d.max())}"
     if d.numel():
+        assert far <= max_far_frac * d.numel(), f"{far} of {d.numel()} elements beyond 2 ULP"
         assert float((d == 0).float().mean()) >= min_exact, f"exact fraction {float((d == 0).float().mean())}"
 
 
@@ -536,6 +547,91 @@ def test_rope_kv_write_bulk_partial_group_and_unaligned_metadata():
                                k_norm_w=gpu(c["kw"]))
     assert torch.equal(q2.cpu().reshape(q.shape), q.cpu())
     assert torch.equal(kc2.cpu(), kc.cpu()) and torch.equal(vc2.cpu(), vc.cpu())
+
+
+def _kernel_cos_sin(inv, pos, d=64):
+    """The kernel's own rounded cos/sin rows [N, D] at positions `pos` [N], read back
+    through RoPE of the unit vector [1 ... 1 | 0 ... 0] (y = [cos | sin])."""
+    n = pos.numel()
+    x = torch.zeros(1, n, 1, d, dtype=torch.bfloat16, device=DEV)
+    x[..., : d // 2] = 1.0
+    kc = torch.zeros(1, 1, n, d, dtype=torch.bfloat16, device=DEV)
+    y = K.fused_rope_kv_write(x, x.clone(), x.clone(), gpu(inv), gpu(pos), kc, torch.zeros_like(kc),
+                              torch.arange(n, device=DEV)).reshape(n, d).cpu()
+    c, s = y[:, : d // 2], y[:, d // 2:]
+    return torch.cat([c, c], -1), torch.cat([s, s], -1)
+
+
+def _kernel_norms(c, t, b):
+    """The kernel's own q/k RMSNorm outputs: the same call at angle 0 (cos 1, sin 0:
+    the rotation is the identity) without the frame table."""
+    hq, d = c["q"].shape[1:]
+    hk = c["k"].shape[1]
+    n = b * t
+    kc = torch.zeros(b, hk, t, d, dtype=torch.bfloat16, device=DEV)
+    qn = K.fused_rope_kv_write(
+        gpu(c["q"]).view(b, t, hq, d), gpu(c["k"]).view(b, t, hk, d), gpu(c["v"]).view(b, t, hk, d),
+        gpu(c["inv"]), torch.zeros(n, dtype=torch.long, device=DEV), kc, torch.zeros_like(kc),
+        torch.arange(t, device=DEV).repeat(b), q_norm_w=gpu(c["qw"]), k_norm_w=gpu(c["kw"]), eps=1e-5)
+    return qn.reshape(n, hq, d).cpu(), kc.transpose(1, 2).reshape(n, hk, d).cpu()
+
+
+@pytest.mark.parametrize("t,norm", [(1, False), (1, True), (64, False), (512, True), (4096, False),
+                                    (4096, True)])
+def test_rope_deviation_traces_to_cos_sin_and_norm_inputs(t, norm):
+    """Accounting for every RoPE output element beyond 2 bf16 ULP of the oracle.
+
+    1. Given the kernel's own rounded cos/sin rows and (with q/k norm) its own
+       normed heads, the oracle's rotate-half + frame term + one rounding
+       reproduces the kernel's Q output and K cache rows bit for bit: the
+       rotation arithmetic is the reference's exactly.
+    2. Those inputs are within 1 ULP of the oracle's (torch's cos/sin of the
+       same fp32 angles; the oracle's norm).
+    3. Every output element more than 2 ULP from the plain oracle sits on a
+       lane whose own cos/sin value or one of whose two normed inputs (x_i,
+       x_paired) differs from the oracle's: rotate-half subtracts two
+       products, so a 1-ULP input change can move a cancelled output by many
+       of its own ULPs.
+    Config 2 shapes (Q 16 heads, K/V 8, D 64, theta 1e6, frame table [1024, 64]),
+    decode (T = 1, p ~ U[0, 2047]) and the prefill sweep (consecutive p)."""
+    b = 1
+    p0 = None if t == 1 else (17 if t < 4096 else 0)      # frames p // 4 stay inside the 1024-row table
+    c = _config2_case(2000 + t + (7 if norm else 0), t=t, s_len=max(2048, t + 17), p0=p0, norm=norm)
+    q, kc, vc, eq, ekc, evc, flags = _run_both(c, t, b)
+    assert flags == 0 and _lib.read_and_clear_errors(DEV) == 0
+    n, d = b * t, 64
+    slots = c["slots"]
+    k_rows = kc.cpu()[0, :, slots].transpose(0, 1)          # [N, Hk, D]
+    ek_rows = ekc[0, :, slots].transpose(0, 1)
+    kcos, ksin = _kernel_cos_sin(c["inv"], c["pos"])
+    ocos, osin = O.rope_cos_sin_ref(c["inv"], c["pos"])
+    assert int(ulp(kcos, ocos).max()) <= 1 and int(ulp(ksin, osin).max()) <= 1
+    if norm:
+        qn, kn = _kernel_norms(c, t, b)
+        oqn, okn = O.rms_norm_ref(c["q"], c["qw"], 1e-5), O.rms_norm_ref(c["k"], c["kw"], 1e-5)
+        assert int(ulp(qn, oqn).max()) <= 1 and int(ulp(kn, okn).max()) <= 1
+    else:
+        qn, kn, oqn, okn = c["q"], c["k"], c["q"], c["k"]
+    rows = c["tab"][torch.div(c["pos"], 4, rounding_mode="floor")]
+    # 1. bit-exact given the kernel's own inputs
+    assert torch.equal(q.cpu(), O.rope_compose_ref(qn, kcos, ksin, rows))
+    assert torch.equal(k_rows, O.rope_compose_ref(kn, kcos, ksin, rows))
+    assert torch.equal(vc.cpu(), evc)
+    # 3. every element beyond 2 ULP of the oracle traces to a differing input
+    half = d // 2
+    stats = {}
+    for name, got, want, xk, xo in (("q", q.cpu(), eq, qn, oqn), ("k", k_rows, ek_rows, kn, okn)):
+        dist = ulp(got, want)
+        far = dist > 2
+        cs_diff = ((kcos != ocos) | (ksin != osin)).unsqueeze(1)                  # [N, 1, D]
+        x_diff = xk != xo
+        pair_diff = torch.cat([x_diff[..., half:], x_diff[..., :half]], -1)
+        explained = cs_diff | x_diff | pair_diff
+        assert bool((~far | explained).all()), f"{name}: {int((far & ~explained).sum())} unexplained elements"
+        stats[name] = (int(far.sum()), far.numel(), int(dist.max()))
+    print(f"rope T={t} norm={norm}: elements > 2 ULP of the oracle (all traced to a 1-ULP cos/sin or norm "
+          f"input): Q {stats['q'][0]}/{stats['q'][1]} (max {stats['q'][2]} ULP), "
+          f"K {stats['k'][0]}/{stats['k'][1]} (max {stats['k'][2]} ULP)")
 
 
 @pytest.mark.parametrize("t", [64, 65536])

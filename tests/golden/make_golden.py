@@ -1,9 +1,9 @@
 """Generate the golden vectors in tests/golden/*.npz from the reference itself.
 
-Run in a container that has the reference checkout (default
-/root/reference, override with KANI_REFERENCE_DIR):
+Run where the reference checkout is available, naming it in
+KANI_REFERENCE_DIR:
 
-    python tests/golden/make_golden.py
+    KANI_REFERENCE_DIR=<checkout> python tests/golden/make_golden.py
 
 What runs, all on the CPU:
   * the reference's three Triton kernels (kani_tts/triton_kernels.py) under
@@ -36,11 +36,13 @@ import numpy as np
 os.environ["TRITON_INTERPRET"] = "1"
 import torch  # noqa: E402
 
-REF = Path(os.environ.get("KANI_REFERENCE_DIR", "/root/reference"))
+REF = Path(os.environ["KANI_REFERENCE_DIR"]) if os.environ.get("KANI_REFERENCE_DIR") else None
 OUT = Path(__file__).resolve().parent
 
 
 def _import_reference():
+    if REF is None:
+        raise SystemExit("set KANI_REFERENCE_DIR to the reference checkout")
     import transformers.models.lfm2.modeling_lfm2 as hf
     if not hasattr(hf, "Lfm2HybridConvCache"):
         class Lfm2HybridConvCache:  # placeholder for the removed HF class (type use only)

@@ -451,6 +451,49 @@ def run_e2e(K, dev, steps: int) -> dict:
     return {"seconds": el, "steps": steps, "h2d": in_bytes, "d2h": out_bytes}
 
 
+def host_link_copies(dev, in_bytes: int, out_bytes: int, steps: int) -> float:
+    """The host link's share of the e2e leg: the same per-step copies (one pinned
+    H2D of `in_bytes`, one D2H of `out_bytes`), pipelined the same way over two
+    buffer sets and copy-in / copy-out streams, with no kernel between them.
+    Seconds for `steps` steps: the time the e2e leg would take if the kernel
+    cost nothing (each rank measures its own, so at N > 1 it shows what the
+    GPUs sharing one host get)."""
+    nbuf = 2
+    h_in = torch.empty(in_bytes, dtype=torch.uint8).pin_memory()
+    h_out = [torch.empty(out_bytes, dtype=torch.uint8).pin_memory() for _ in range(nbuf)]
+    d_in = [torch.empty(in_bytes, dtype=torch.uint8, device=dev) for _ in range(nbuf)]
+    d_out = [torch.zeros(out_bytes, dtype=torch.uint8, device=dev) for _ in range(nbuf)]
+    s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    in_done = [torch.cuda.Event() for _ in range(nbuf)]
+    out_done = [torch.cuda.Event() for _ in range(nbuf)]
+    used = [False] * nbuf
+
+    def step(i):
+        j = i % nbuf
+        with torch.cuda.stream(s_in):
+            if used[j]:
+                s_in.wait_event(out_done[j])
+            d_in[j].copy_(h_in, non_blocking=True)
+            in_done[j].record(s_in)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(in_done[j])
+            h_out[j].copy_(d_out[j], non_blocking=True)
+            out_done[j].record(s_out)
+        used[j] = True
+
+    for i in range(4):
+        step(i)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s_in)
+    for i in range(steps):
+        step(i)
+    s_out.wait_stream(s_in)
+    e1.record(s_out)
+    torch.cuda.synchronize(dev)
+    return e0.elapsed_time(e1) / 1e3
+
+
 def _ref_cache(ref, dev, s_len: int = 2048):
     """The reference's StaticLfm2HybridConvCache for one attention layer of the
     decode shapes (16 Q heads, 8 KV heads, head_dim 64)."""
@@ -878,9 +921,13 @@ def run_gpu(args, world, rank, local):
     _barrier(world)
     e = run_e2e(K, dev, min(args.steps, 200))
     e_max = _max_over_ranks(e["seconds"], world, dev)
+    link = _max_over_ranks(host_link_copies(dev, e["h2d"], e["d2h"], e["steps"]), world, dev)
     e2e_line = {"value": round(world * e["steps"] * STEP_BYTES / e_max / 1e9, 3), "unit": UNIT,
                 "h2d_bytes_per_step": e["h2d"], "d2h_bytes_per_step": e["d2h"], "steps": e["steps"],
                 "ms_per_step": round(e_max / e["steps"] * 1e3, 4),
+                "host_link_ceiling": {"value": round(world * e["steps"] * STEP_BYTES / link / 1e9, 3), "unit": UNIT,
+                                      "ms_per_step": round(link / e["steps"] * 1e3, 4),
+                                      "what": "the same copies per step with no kernel (slowest rank)"},
                 "path": ("kani_tts_b200.fused_rope_kv_write (ctypes -> kani_rope_kv_write): one pinned "
                          "packed input buffer (Q|K|V rows, positions, slots) and one result buffer (rotated Q, "
                          "K and V caches) per step, copy-in / compute / copy-out streams over two buffer sets")}

@@ -327,3 +327,52 @@ def test_step_logits_from_fused_head_match_linear_head():
     got = dec.step_logits(*args)
     close(got, ref, 0.02)
     assert int(dec.head_scratch.abs().sum()) == 0
+
+
+def test_full_size_teacher_forced_steps_match_the_oracle_decoder():
+    """Full-size model, one stream, 12 consecutive decode steps fed the same tokens:
+    this library's step (fused-GEMV path, fused head writing the logits) against the
+    oracle decode step on the CPU, from the same random cache prefix and conv
+    states, with the engine's position schedule (4 tokens per frame).  Every step:
+    logits within 5 % of the largest logit, cosine > 0.999, and the same argmax
+    wherever the oracle's top-2 margin is clear; the caches stay close too."""
+    cfg = LFM2Config()
+    sd = synthetic_state_dict(cfg, seed=21)
+    b, max_len, prefix, n = 1, 64, 30, 12
+    dec = FusedDecoder(cfg, sd, DEV, batch=b, max_len=max_len)
+    ora = OracleDecoder(cfg, sd, batch=b, max_len=max_len)
+    g = torch.Generator().manual_seed(22)
+    for i in cfg.attn_layers:
+        kp = torch.randn(b, cfg.num_key_value_heads, max_len, cfg.head_dim, generator=g).bfloat16()
+        vp = torch.randn(b, cfg.num_key_value_heads, max_len, cfg.head_dim, generator=g).bfloat16()
+        kp[:, :, prefix:] = 0
+        vp[:, :, prefix:] = 0
+        for c in (dec, ora):
+            c.k_cache[i].copy_(kp)
+            c.v_cache[i].copy_(vp)
+    for i in dec.conv_state:
+        cs = torch.randn(b, cfg.hidden_size, cfg.conv_L_cache, generator=g).bfloat16()
+        dec.conv_state[i].copy_(cs)
+        ora.conv_state[i].copy_(cs)
+    tokens = torch.randint(cfg.audio_tokens_start, cfg.vocab_size, (n,), generator=g)
+    mask = torch.full((b, 1, 1, max_len), float("-inf"), dtype=torch.bfloat16)
+    mask[..., :prefix] = 0
+    n_clear = 0
+    for k in range(n):
+        pos = torch.tensor([prefix + k // cfg.tokens_per_frame])
+        slot = torch.tensor([prefix + k])
+        mask[..., prefix + k] = 0
+        got = dec.step_logits(tokens[k].view(1, 1).to(DEV), pos.to(DEV), slot.to(DEV), (slot + 1).to(DEV))
+        want = ora.step(tokens[k].view(1, 1), pos, slot, mask)
+        close(got, want, 0.05)
+        cos = torch.nn.functional.cosine_similarity(got.float().cpu().flatten(), want.float().flatten(), dim=0)
+        assert float(cos) > 0.999
+        top2 = want.float().flatten().topk(2).values
+        if float(top2[0] - top2[1]) > 2.0 ** -5 * abs(float(top2[0])):
+            n_clear += 1
+            assert int(got.float().cpu().argmax()) == int(want.float().argmax())
+    assert n_clear >= n // 3
+    for i in cfg.attn_layers:
+        close(dec.k_cache[i][:, :, prefix:prefix + n], ora.k_cache[i][:, :, prefix:prefix + n], 0.05)
+        close(dec.v_cache[i][:, :, prefix:prefix + n], ora.v_cache[i][:, :, prefix:prefix + n], 0.05)
+    assert int(dec.err_flag.item()) == 0

@@ -192,3 +192,58 @@ def test_reference_engine_captures_and_replays_the_kernels_full_size(ref):
         assert float(cos) > 0.999
         n_clear += same_argmax_where_clear(got, want)
     assert n_clear >= 4
+
+
+def test_decoder_teacher_forced_against_the_reference_triton_engine(ref):
+    """This library's decode step against the reference's own Triton + CUDA-graph
+    engine, full-size model, 32 steps from the same cache state, both fed the
+    reference's greedy tokens: logits within 5 % of the largest logit, cosine >
+    0.999, and the same argmax on every step whose top-2 margin is clear."""
+    from kani_tts_b200.decode import FusedDecoder
+    cfg = LFM2Config()
+    sd = synthetic_state_dict(cfg, seed=23, device=DEV)
+    g = torch.Generator().manual_seed(24)
+    prefill_len, n = 40, 32
+    dyn = types.SimpleNamespace(
+        key_cache=[torch.randn(1, cfg.num_key_value_heads, prefill_len, cfg.head_dim, generator=g).bfloat16().to(DEV)
+                   if t == "full_attention" else torch.empty(0) for t in cfg.layer_types],
+        value_cache=[torch.randn(1, cfg.num_key_value_heads, prefill_len, cfg.head_dim, generator=g).bfloat16()
+                     .to(DEV) if t == "full_attention" else torch.empty(0) for t in cfg.layer_types],
+        conv_cache=[torch.randn(1, cfg.hidden_size, cfg.conv_L_cache, generator=g).bfloat16().to(DEV)
+                    for _ in cfg.layer_types])
+    model = R.stand_in_model(ref, cfg, sd, DEV)
+    eng = R.engine(ref, model, cfg, max_new_tokens=256)
+    R.capture(eng, dyn, prefill_len)
+    od = eng.optimized_decoder
+    positions = (prefill_len + torch.arange(n) // cfg.tokens_per_frame).to(DEV)
+    tok = torch.tensor([[cfg.audio_tokens_start + 5]], device=DEV)
+    inputs, ref_logits = [], []
+    for i in range(n):                                   # inference_engine.py:641-651, greedy choice
+        inputs.append(tok.clone())
+        eng.static_input_ids.copy_(tok)
+        eng.static_position_ids[0, 0] = positions[i]
+        eng.static_cache_position[0] = prefill_len + i
+        eng.static_cache.set_write_position(prefill_len + i)
+        eng.static_mask[:, :, :, prefill_len + i] = 0.0
+        eng.cuda_graph.replay()
+        eng.static_cache.advance_position()
+        lg = eng.static_logits[:, -1, :].clone()
+        ref_logits.append(lg)
+        tok = od.reduced_to_full[lg.argmax(-1)].view(1, 1)
+    del eng
+    dec = FusedDecoder(cfg, sd, DEV, batch=1, max_len=512)
+    for i in cfg.attn_layers:
+        dec.k_cache[i][:, :, :prefill_len].copy_(dyn.key_cache[i])
+        dec.v_cache[i][:, :, :prefill_len].copy_(dyn.value_cache[i])
+    for i in dec.conv_state:
+        dec.conv_state[i].copy_(dyn.conv_cache[i])
+    n_clear = 0
+    for i in range(n):
+        slot = torch.tensor([prefill_len + i], device=DEV)
+        got = dec.step_logits(inputs[i], positions[i:i + 1], slot, slot + 1)[:, -1, :]
+        close(got, ref_logits[i], 0.05)
+        cos = torch.nn.functional.cosine_similarity(got.float().flatten(), ref_logits[i].float().flatten(), dim=0)
+        assert float(cos) > 0.999
+        n_clear += same_argmax_where_clear(got, ref_logits[i])
+    assert n_clear >= n // 3
+    assert int(dec.err_flag.item()) == 0

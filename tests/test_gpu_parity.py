@@ -663,6 +663,8 @@ def test_in_kernel_cos_sin_match_cuda_math(t):
 @pytest.mark.parametrize("b,hq,hk,s_len,lens", [(1, 16, 8, 2048, [1629]), (3, 16, 8, 512, [1, 7, 512]),
                                                 (2, 8, 8, 64, [33, 64]), (2, 16, 4, 300, [250, 9]),
                                                 # enough streams that the split drops to 2 and 1 CTAs
+                                                # (the largest split whose grid is one wave)
+                                                (24, 16, 8, 256, [(37 * i) % 256 + 1 for i in range(24)]),
                                                 (40, 16, 8, 256, [(37 * i) % 256 + 1 for i in range(40)]),
                                                 (80, 16, 8, 256, [(53 * i) % 256 + 1 for i in range(80)])])
 def test_decode_attention_vs_oracle(b, hq, hk, s_len, lens):

@@ -215,6 +215,31 @@ def test_silu_mul_other_dtypes(dtype):
         assert_close_ulp(y, ref)
 
 
+@pytest.mark.parametrize("dtype,n", [(torch.bfloat16, 4608), (torch.float16, 4608), (torch.float32, 4608),
+                                     (torch.bfloat16, 1000), (torch.bfloat16, 8192), (torch.float32, 6144)])
+def test_silu_mul_row_per_cta_path(dtype, n):
+    """Long calls (>= 2048 rows) take one CTA per row: every dtype, a width whose
+    vectors do not fill the last 192-thread pass (n = 1000 bf16: 125 vectors),
+    the widest row it takes (fp32 6144: 8 passes), a strided row view, and the
+    extreme gate values of the short path."""
+    rows = 2304
+    gu = rnd((rows, 2 * n), 13, dtype)
+    gu[0, :8] = torch.tensor([-100.0, -20.0, -1e-3, 0.0, 1e-3, 20.0, 88.0, -88.0], dtype=dtype)
+    y = K.fused_silu_mul(gpu(gu))
+    ref = O.silu_mul_ref(gu)
+    if dtype == torch.float32:
+        assert torch.allclose(y.cpu(), ref, rtol=1e-5, atol=1e-6)
+    else:
+        assert_close_ulp(y, ref)
+    big = rnd((rows, 2 * n + 64), 14, dtype)
+    ys = K.fused_silu_mul(gpu(big)[:, : 2 * n])
+    refs = O.silu_mul_ref(big[:, : 2 * n])
+    if dtype == torch.float32:
+        assert torch.allclose(ys.cpu(), refs, rtol=1e-5, atol=1e-6)
+    else:
+        assert_close_ulp(ys, refs)
+
+
 def test_silu_mul_strided_and_odd():
     big = rnd((9, 2 * 4608 + 64), 11)
     y = K.fused_silu_mul(gpu(big)[:, : 2 * 4608])          # row stride 9280, vector path

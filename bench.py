@@ -248,9 +248,11 @@ def time_graph_steps(step_fns, steps: int, dev, world: int, chunk: int = 1000, l
     return the device time of those launches on this rank, in seconds.
 
     The start and end events are recorded inside the captured graphs (event
-    record nodes): the first graph runs `lead` untimed launches, then records
-    the start event, then its share of the timed launches; the last graph
-    ends with the end event.  The host's graph submission and the graph's own
+    record nodes): the first graph runs `lead` untimed launches, records the
+    start event on a branch forked after them (so the timed launches stay
+    chained to the lead-in launch by launch, programmatic edges included),
+    then its share of the timed launches; the last graph ends with the end
+    event.  The host's graph submission and the graph's own
     launch latency therefore stay outside the timed region, however few
     launches it holds."""
     n = len(step_fns)
@@ -271,11 +273,19 @@ def time_graph_steps(step_fns, steps: int, dev, world: int, chunk: int = 1000, l
     first = min(chunk, steps)
     full_rest = steps - first
     mids, rest = divmod(full_rest, chunk)
+    side = torch.cuda.Stream(device=dev)
 
     def g_first_body():
         body(0, lead)
-        e0.record()
+        # the start event on a forked branch: it fires when the lead-in completes,
+        # and the first timed launch keeps its programmatic edge to the last
+        # lead-in launch (an event node between them would break that edge)
+        main = torch.cuda.current_stream(dev)
+        side.wait_stream(main)
+        with torch.cuda.stream(side):
+            e0.record(side)
         body(lead, first)
+        main.wait_stream(side)
         if full_rest == 0:
             e1.record()
     graphs = [capture(g_first_body)]

@@ -9,7 +9,7 @@ import socket
 import pytest
 import torch.multiprocessing as mp
 
-from kani_tts_b200.replicas import aggregate_throughput, max_over_ranks, stream_shard
+from kani_tts_b200.replicas import aggregate_throughput, gather_over_ranks, max_over_ranks, stream_shard
 
 
 def test_stream_shard_partitions_all_streams():
@@ -26,6 +26,7 @@ def test_stream_shard_partitions_all_streams():
 
 def test_single_process_aggregation_is_identity():
     assert max_over_ranks(3.5) == 3.5
+    assert gather_over_ranks(3.5) == [3.5]
     assert aggregate_throughput(64 * 1500, 2.0) == (96000.0, 2.0, 48000.0)
 
 
@@ -44,7 +45,8 @@ def _worker(rank, world, port, q):
         shard = stream_shard(64 * world, world, rank)
         # rank r "processes" its shard in (r + 1) seconds
         total, slowest, rate = aggregate_throughput(len(shard) * 1500, float(rank + 1))
-        q.put((rank, list(shard)[:1], len(shard), total, slowest, rate))
+        per_rank = gather_over_ranks(7.5 + rank)   # the bench's per-rank times, in rank order
+        q.put((rank, list(shard)[:1], len(shard), total, slowest, rate, per_rank))
     finally:
         dist.destroy_process_group()
 
@@ -61,11 +63,12 @@ def test_two_gloo_ranks_aggregate_like_the_bench():
         assert p.exitcode == 0
     res = sorted(q.get(timeout=10) for _ in range(world))
     assert [r[1] for r in res] == [[0], [64]]           # disjoint shards of 64 streams
-    for _, _, n, total, slowest, rate in res:
+    for _, _, n, total, slowest, rate, per_rank in res:
         assert n == 64
         assert total == 2 * 64 * 1500
         assert slowest == 2.0                            # max over ranks
         assert rate == total / 2.0
+        assert per_rank == [7.5, 8.5]                    # every rank's value, in rank order
 
 
 def _replica_worker(rank, world, port, mode, q):

@@ -110,6 +110,26 @@ KANI_API int kani_add_rms_norm(int32_t dtype, int32_t w_dtype,
                       int64_t rows, int64_t n, float eps, void* stream);
 
 /*
+ * The residual add + RMSNorm that follows a projection computed as S fp32 partial
+ * products over slices of K (a batched GEMM with an fp32 output, one product per
+ * slice): d = round(p[0] + ... + p[S-1]) summed in split order (F.linear's
+ * output), then h = round(d + residual), y = round(h * rsqrt(mean(h^2) + eps) * w),
+ * as kani_add_rms_norm.  Replaces `hidden = hidden + F.linear(...)` and the next
+ * `fused_rms_norm` (kani_tts/optimized_decode.py:252, 277, 283 with :206, :280,
+ * :286) for batched decode, where the K-split GEMM with an fp32 output is faster
+ * than the plain one.
+ *   partials: fp32, element (s, row, k) at s * split_stride + row * partial_row_stride + k;
+ *             the splits must not overlap; 16-byte aligned, strides multiples of 4
+ *   residual, y, residual_out: [rows, n] of dtype; y must differ from residual_out
+ *   n: a multiple of 4, at most 4096
+ */
+KANI_API int kani_reduce_add_rms_norm(int32_t dtype, int32_t w_dtype, const float* partials, int64_t split_stride,
+                                      int64_t partial_row_stride, int32_t splits, const void* residual,
+                                      int64_t r_row_stride, const void* weight, void* y, int64_t y_row_stride,
+                                      void* residual_out, int64_t h_row_stride, int64_t rows, int64_t n, float eps,
+                                      void* stream);
+
+/*
  * SiLU-gated activation: y[r, i] = round(silu(g[r, i]) * u[r, i]) where each
  * input row is [g (n) | u (n)].
  * Replaces `_silu_mul_kernel` and `fused_silu_mul`

@@ -254,6 +254,121 @@ int launch_norm(const NormParams& p, cudaStream_t s) {
   return launch_status();
 }
 
+// ------------------------------------------- K-split partials + add + RMSNorm
+// The projection before a residual add, computed as S fp32 partial products over
+// slices of K (a batched GEMM with an fp32 output), is finished here:
+//   d = round_T(p[0] + p[1] + ... + p[S-1])   (fp32, in split order: F.linear's
+//                                              output, one rounding)
+//   h = round_T(d + r), y = round_T((h * rr) * w)   (as kani_add_rms_norm)
+// One CTA of 256 threads per row; a thread owns 4-element chunks c = tid,
+// tid + 256, ... and issues every split's load of a chunk before it sums.
+struct RedParams {
+  const float* part;
+  int64_t ps;  // elements between splits
+  int64_t pr;  // elements between rows of one split
+  int splits;
+  const void* r;
+  int64_t rs;
+  const void* w;
+  void* y;
+  int64_t ys;
+  void* h;
+  int64_t hs;
+  int64_t rows;
+  int n;
+  float eps;
+};
+
+constexpr int kRedThreads = 256;
+
+template <typename T>
+__device__ __forceinline__ void ld4(const T* ptr, float* f) {
+  if constexpr (sizeof(T) == 2) {
+    const uint2 v = *reinterpret_cast<const uint2*>(ptr);
+    const T* e = reinterpret_cast<const T*>(&v);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) f[i] = Elem<T>::to_f(e[i]);
+  } else {
+    const float4 v = *reinterpret_cast<const float4*>(ptr);
+    f[0] = v.x; f[1] = v.y; f[2] = v.z; f[3] = v.w;
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void st4(T* ptr, const float* f) {
+  if constexpr (sizeof(T) == 2) {
+    uint2 v;
+    T* e = reinterpret_cast<T*>(&v);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) e[i] = Elem<T>::from_f(f[i]);
+    *reinterpret_cast<uint2*>(ptr) = v;
+  } else {
+    *reinterpret_cast<float4*>(ptr) = make_float4(f[0], f[1], f[2], f[3]);
+  }
+}
+
+template <typename T, typename W, int V>
+__global__ void __launch_bounds__(kRedThreads) reduce_add_norm_kernel(RedParams p) {
+  griddep_launch_dependents();  // a dependent GEMV may start streaming its weights
+  __shared__ float red[33];
+  const int tid = threadIdx.x;
+  for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
+    float h[V][4];
+    float ss = 0.f;
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      const int c = (v * kRedThreads + tid) * 4;
+      if (c < p.n) {
+        const float* src = p.part + row * p.pr + c;
+        float acc[4];
+        {
+          const float4 a = *reinterpret_cast<const float4*>(src);
+          acc[0] = a.x; acc[1] = a.y; acc[2] = a.z; acc[3] = a.w;
+        }
+#pragma unroll 4
+        for (int sp = 1; sp < p.splits; ++sp) {
+          const float4 a = *reinterpret_cast<const float4*>(src + sp * p.ps);
+          acc[0] = __fadd_rn(acc[0], a.x);
+          acc[1] = __fadd_rn(acc[1], a.y);
+          acc[2] = __fadd_rn(acc[2], a.z);
+          acc[3] = __fadd_rn(acc[3], a.w);
+        }
+        float rv[4];
+        ld4<T>(static_cast<const T*>(p.r) + row * p.rs + c, rv);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          h[v][e] = round_to<T>(__fadd_rn(round_to<T>(acc[e]), rv[e]));
+          ss = fmaf(h[v][e], h[v][e], ss);
+        }
+      }
+    }
+    ss = block_sum<kRedThreads>(ss, red);
+    const float rr = rrms_of(ss, p.n, p.eps);
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      const int c = (v * kRedThreads + tid) * 4;
+      if (c < p.n) {
+        float wf[4], o[4];
+        ld4<W>(static_cast<const W*>(p.w) + c, wf);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[e] = __fmul_rn(__fmul_rn(h[v][e], rr), wf[e]);
+        st4<T>(static_cast<T*>(p.h) + row * p.hs + c, h[v]);
+        st4<T>(static_cast<T*>(p.y) + row * p.ys + c, o);
+      }
+    }
+  }
+}
+
+template <typename T, typename W>
+int launch_reduce_norm(const RedParams& p, cudaStream_t s) {
+  const unsigned grid = (unsigned)(p.rows < kMaxGrid ? p.rows : kMaxGrid);
+  const int v = (p.n + 4 * kRedThreads - 1) / (4 * kRedThreads);
+  if (v <= 1)      reduce_add_norm_kernel<T, W, 1><<<grid, kRedThreads, 0, s>>>(p);
+  else if (v <= 2) reduce_add_norm_kernel<T, W, 2><<<grid, kRedThreads, 0, s>>>(p);
+  else             reduce_add_norm_kernel<T, W, 4><<<grid, kRedThreads, 0, s>>>(p);
+  return launch_status();
+}
+
 template <bool RES>
 int norm_entry(int32_t dtype, int32_t w_dtype, const NormParams& p, cudaStream_t s) {
   return dispatch_dtype(dtype, [&]<typename T>() {
@@ -299,4 +414,34 @@ extern "C" int kani_add_rms_norm(int32_t dtype, int32_t w_dtype, const void* x, 
   NormParams p{x, x_row_stride, residual, r_row_stride, weight, y, y_row_stride,
                residual_out, h_row_stride, rows, (int)n, eps};
   return kani::norm_entry<true>(dtype, w_dtype, p, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int kani_reduce_add_rms_norm(int32_t dtype, int32_t w_dtype, const float* partials, int64_t split_stride,
+                                        int64_t partial_row_stride, int32_t splits, const void* residual,
+                                        int64_t r_row_stride, const void* weight, void* y, int64_t y_row_stride,
+                                        void* residual_out, int64_t h_row_stride, int64_t rows, int64_t n, float eps,
+                                        void* stream) {
+  if (rows < 0 || n < 0 || splits < 1) return KANI_ERR_INVALID_ARG;
+  if (rows == 0 || n == 0) return KANI_OK;
+  if (!partials || !residual || !weight || !y || !residual_out) return KANI_ERR_INVALID_ARG;
+  if (y == residual_out) return KANI_ERR_INVALID_ARG;
+  if (rows > 1 && (partial_row_stride < n || r_row_stride < n || y_row_stride < n || h_row_stride < n))
+    return KANI_ERR_INVALID_ARG;
+  if (splits > 1) {  // the splits must not overlap: split-major or row-major blocks of partials
+    const bool split_major = split_stride >= (rows - 1) * partial_row_stride + n;
+    const bool row_major = split_stride >= n && partial_row_stride >= (splits - 1) * split_stride + n;
+    if (!split_major && !row_major) return KANI_ERR_INVALID_ARG;
+  }
+  if (n % 4 != 0 || n > 4 * 4 * kani::kRedThreads) return KANI_ERR_UNSUPPORTED;
+  if (!kani::aligned16(partials) || split_stride % 4 != 0 || partial_row_stride % 4 != 0 ||
+      (reinterpret_cast<uintptr_t>(residual) | reinterpret_cast<uintptr_t>(y) |
+       reinterpret_cast<uintptr_t>(residual_out) | reinterpret_cast<uintptr_t>(weight)) % 16 != 0 ||
+      r_row_stride % 4 != 0 || y_row_stride % 4 != 0 || h_row_stride % 4 != 0)
+    return KANI_ERR_UNSUPPORTED;
+  kani::RedParams p{partials, split_stride, partial_row_stride, splits, residual, r_row_stride, weight, y,
+                    y_row_stride, residual_out, h_row_stride, rows, (int)n, eps};
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return kani::dispatch_dtype(dtype, [&]<typename T>() {
+    return kani::dispatch_dtype(w_dtype, [&]<typename W>() { return kani::launch_reduce_norm<T, W>(p, s); });
+  });
 }

@@ -44,6 +44,8 @@ _SIGNATURES = {
                       ctypes.c_int),
     "kani_add_rms_norm": ([_c_i32, _c_i32, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_p, _c_i64, _c_p, _c_i64,
                            _c_i64, _c_i64, _c_f32, _c_p], ctypes.c_int),
+    "kani_reduce_add_rms_norm": ([_c_i32, _c_i32, _c_p, _c_i64, _c_i64, _c_i32, _c_p, _c_i64, _c_p, _c_p, _c_i64,
+                                  _c_p, _c_i64, _c_i64, _c_i64, _c_f32, _c_p], ctypes.c_int),
     "kani_silu_mul": ([_c_i32, _c_p, _c_i64, _c_p, _c_i64, _c_i64, _c_i64, _c_p], ctypes.c_int),
     "kani_rope_qk": ([_c_i32, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_p],
                      ctypes.c_int),

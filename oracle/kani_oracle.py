@@ -93,6 +93,17 @@ def add_rms_norm_ref(x: torch.Tensor, r: torch.Tensor, w: torch.Tensor, eps: flo
     return rms_norm_ref(h, w, eps, rounding), h
 
 
+def reduce_add_rms_norm_ref(partials: torch.Tensor, r: torch.Tensor, w: torch.Tensor, eps: float):
+    """A projection given as fp32 partial products over slices of K, finished by
+    the residual add and RMSNorm of the decode step: the partials summed in split
+    order and rounded as F.linear rounds its output, then ``add_rms_norm_ref``
+    (optimized_decode.py:252 + :280).  Returns (y, h)."""
+    acc = partials[0].float()
+    for s in range(1, partials.shape[0]):
+        acc = acc + partials[s].float()
+    return add_rms_norm_ref(acc.to(r.dtype).reshape(r.shape), r, w, eps)
+
+
 def silu_mul_ref(gate_up: torch.Tensor, rounding: str = "rne") -> torch.Tensor:
     """Triton SiLU x mul (triton_kernels.py:77-82): (g * sigmoid(g)) * u in fp32."""
     n = gate_up.shape[-1] // 2

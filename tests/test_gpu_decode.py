@@ -67,10 +67,11 @@ def test_fused_decoder_matches_reference_decoder_golden():
     assert int(dec.err_flag.item()) == 0
 
 
-@pytest.mark.parametrize("full,b", [(False, 3), (True, 2), (True, 16)])
+@pytest.mark.parametrize("full,b", [(False, 3), (True, 2), (True, 16), (True, 64)])
 def test_batched_fused_step_matches_oracle(full, b):
     """One decode step against the oracle decoder: 2 streams take the fused-GEMV
-    path, 3 (tiny model) and 16 streams the tensor-core GEMM path."""
+    path, 3 (tiny model) and 16 streams the tensor-core GEMM path, 64 streams the
+    cuBLAS path with K-split partials finished by the add + RMSNorm launch."""
     cfg = LFM2Config() if full else tiny_config()
     max_len = 64 if full else 32
     sd = synthetic_state_dict(cfg, seed=7)

@@ -187,6 +187,43 @@ def test_add_rms_norm_rows(dtype, rows):
 # ---------------------------------------------------------------- SiLU*mul
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("splits,rows,n", [(1, 1, 1024), (2, 64, 1024), (4, 64, 1024), (18, 5, 1024),
+                                           (4, 300, 2048), (3, 7, 4096)])
+def test_reduce_add_rms_norm_vs_oracle(dtype, splits, rows, n):
+    """K-split fp32 partials summed in split order, rounded, added to the residual,
+    RMSNorm: the residual sum bit-exact, the norm <= 1 ULP (fp32: 1e-5 relative)."""
+    part = torch.randn(splits, rows, n, generator=torch.Generator().manual_seed(splits * 7 + rows)) * 0.3
+    r = rnd((rows, n), 1310 + n, dtype)
+    w = rnd((n,), 1311, dtype, 1.0, 0.02)
+    y, h = K.reduce_add_rms_norm(gpu(part), gpu(r), gpu(w), 1e-5)
+    yo, ho = O.reduce_add_rms_norm_ref(part, r, w, 1e-5)
+    assert torch.equal(h.cpu(), ho)
+    if dtype == torch.float32:
+        assert_rel(y, yo, 1e-5)
+    else:
+        assert_close_ulp(y, yo)
+    # row-major partials ([rows, splits, n] viewed as [splits, rows, n]) and in-place residual
+    rm = gpu(part.transpose(0, 1).contiguous()).transpose(0, 1)
+    rg = gpu(r)
+    y2 = torch.empty_like(rg)
+    K.reduce_add_rms_norm(rm, rg, gpu(w), 1e-5, out=y2, residual_out=rg)
+    assert torch.equal(rg.cpu(), ho) and torch.equal(y2.cpu(), y.cpu())
+
+
+def test_linear_split_k_sums_to_the_product():
+    x = rnd((64, 4608), 1320)
+    w = rnd((1024, 4608), 1321, std=0.03)
+    p4 = K.linear_split_k(gpu(x), gpu(w), 4)
+    assert p4.shape == (4, 64, 1024) and p4.dtype == torch.float32
+    want = (x.double() @ w.double().t())
+    assert float((p4.sum(0).double().cpu() - want).abs().max()) <= 1e-3 * float(want.abs().max())
+    for s_ in range(4):                                   # each slice is the product over its K range
+        sl = slice(s_ * 1152, (s_ + 1) * 1152)
+        ws = x[:, sl].double() @ w[:, sl].double().t()
+        assert float((p4[s_].double().cpu() - ws).abs().max()) <= 1e-3 * float(ws.abs().max())
+
+
 @pytest.mark.parametrize("case", ["rows4_bf16", "decode_bf16", "odd_bf16"])
 def test_silu_mul_vs_reference_golden(case):
     c = load("triton_silu_mul")[case]

@@ -138,6 +138,16 @@ def test_abi_rejects_bad_arguments_without_launching():
     # codec codes: too few frames for the tokens, missing outputs
     assert lib.kani_codec_codes(fake, 100, 2, 100, 64402, 64410, 4032, fake, 24, fake, fake, n) == -1
     assert lib.kani_codec_codes(fake, 100, 2, 100, 64402, 64410, 4032, n, 25, fake, fake, n) == -1
+    # K-split reduce + add + RMSNorm: no splits, y aliasing residual_out, n not a multiple of 4,
+    # overlapping splits
+    assert lib.kani_reduce_add_rms_norm(1, 1, fake, 4096, 1024, 0, fake, 1024, fake, fake, 1024, fake, 1024, 4,
+                                        1024, 1e-5, n) == -1
+    assert lib.kani_reduce_add_rms_norm(1, 1, fake, 4096, 1024, 2, fake, 1024, fake, fake, 1024, fake, 1024, 4,
+                                        1024, 1e-5, n) == -1
+    assert lib.kani_reduce_add_rms_norm(1, 1, fake, 4096, 1024, 2, fake, 1022, fake, ctypes.c_void_p(0x2000), 1022,
+                                        fake, 1022, 4, 1022, 1e-5, n) == -3
+    assert lib.kani_reduce_add_rms_norm(1, 1, fake, 1024, 1024, 2, fake, 1024, fake, ctypes.c_void_p(0x2000), 1024,
+                                        fake, 1024, 4, 1024, 1e-5, n) == -1
     assert lib.kani_launch_count() == before
 
 

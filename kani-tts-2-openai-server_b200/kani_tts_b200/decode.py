@@ -282,8 +282,10 @@ class FusedDecoder:
     # the next RMSNorm.  Measured at 64 streams (µs per launch, graph replay):
     # down 4.6 (4 slices) against 7.9 for the bf16 GEMM, o_proj 3.2 (2 slices)
     # against 3.7, and the sum rides in the add + RMSNorm launch that follows
-    # anyway.  0 turns a projection back into F.linear.
-    split_k_down = 4
+    # anyway.  In the whole step (64 streams, 600 tokens) the split counts gave
+    # 608 µs (down 6, out 2), 612-618 (down 2-4, out 2-4), 642 (out unsplit) and
+    # 697 without any split.  0 turns a projection back into F.linear.
+    split_k_down = 6
     split_k_out = 2
 
     def _final_hidden_large(self, input_ids, positions, slots, kv_len) -> torch.Tensor:

@@ -80,6 +80,20 @@ KANI_API uint64_t kani_launch_count(void);
 KANI_API int kani_set_wait_limit(int64_t cycles);
 
 /*
+ * L2 prefetch hint for the next decode launch: the next call of kani_gemv,
+ * kani_gemv_short_conv, kani_gemv_rope_kv or kani_head_argmax made on the same
+ * host thread takes these (up to two) device ranges and clears them; every CTA
+ * of that launch issues its share as cp.async.bulk.prefetch.L2 as it starts,
+ * before the programmatic-launch wait.  The ranges must hold data no launch
+ * writes (the weights of later launches), so that reading them early is safe.
+ * A range with 0 bytes is unused.  Returns KANI_ERR_INVALID_ARG for negative
+ * sizes or a null pointer with a size, KANI_ERR_UNSUPPORTED for a size or
+ * address that is not a multiple of 16 bytes.  No counterpart in the reference,
+ * whose decode step launches each F.linear on its own.
+ */
+KANI_API int kani_set_l2_prefetch(const void* ptr0, int64_t bytes0, const void* ptr1, int64_t bytes1);
+
+/*
  * RMSNorm over the last dimension:  y = round(x * rsqrt(mean(x^2) + eps) * w).
  * Replaces `_rms_norm_kernel` and its launch in `fused_rms_norm`
  * (kani_tts/triton_kernels.py:17-35, :38-60).  Unlike the reference, an fp32

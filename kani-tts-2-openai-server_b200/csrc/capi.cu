@@ -17,6 +17,16 @@ WaitBound wait_bound(long long default_cycles) {
   return WaitBound{c, 0u};
 }
 
+namespace {
+thread_local L2Prefetch t_l2_prefetch = {{nullptr, nullptr}, {0, 0}};
+}  // namespace
+
+L2Prefetch take_l2_prefetch() {
+  const L2Prefetch pf = t_l2_prefetch;
+  t_l2_prefetch = L2Prefetch{{nullptr, nullptr}, {0, 0}};
+  return pf;
+}
+
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 int sm_count() {
@@ -37,6 +47,15 @@ extern "C" int kani_version(void) { return 100; }
 extern "C" int kani_set_wait_limit(int64_t cycles) {
   if (cycles < 0) return KANI_ERR_INVALID_ARG;
   kani::g_wait_limit.store((long long)cycles, std::memory_order_relaxed);
+  return KANI_OK;
+}
+
+extern "C" int kani_set_l2_prefetch(const void* ptr0, int64_t bytes0, const void* ptr1, int64_t bytes1) {
+  if (bytes0 < 0 || bytes1 < 0 || (bytes0 > 0 && !ptr0) || (bytes1 > 0 && !ptr1)) return KANI_ERR_INVALID_ARG;
+  if (bytes0 % 16 || bytes1 % 16 || (ptr0 && !kani::aligned16(ptr0)) || (ptr1 && !kani::aligned16(ptr1)))
+    return KANI_ERR_UNSUPPORTED;
+  kani::t_l2_prefetch = kani::L2Prefetch{{bytes0 ? ptr0 : nullptr, bytes1 ? ptr1 : nullptr},
+                                         {(long long)bytes0, (long long)bytes1}};
   return KANI_OK;
 }
 

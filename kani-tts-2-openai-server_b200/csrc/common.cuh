@@ -200,6 +200,37 @@ struct WaitBound {
 constexpr unsigned kWaitSuspendNs = 1000000u;
 WaitBound wait_bound(long long default_cycles);
 
+// Device ranges a decode launch prefetches into L2 as it starts: the weights
+// of later launches, which do not depend on any earlier launch.  Set from the
+// host with kani_set_l2_prefetch and taken (and cleared) by the next decode
+// GEMV / head entry point called on the same host thread.
+struct L2Prefetch {
+  const void* ptr[2];
+  long long bytes[2];
+};
+L2Prefetch take_l2_prefetch();
+
+// Thread 0 of each CTA issues its even share of the ranges (16-byte units,
+// pieces of at most 64 KB) as cp.async.bulk.prefetch.L2: no data comes back
+// to the SM, nothing waits on it, and it reads only memory that no launch
+// writes, so it may run before griddepcontrol.wait.
+__device__ __forceinline__ void l2_prefetch_share(const L2Prefetch& pf) {
+  if (threadIdx.x != 0) return;
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const long long units = pf.bytes[j] >> 4;
+    if (pf.ptr[j] == nullptr || units <= 0) continue;
+    const long long per = (units + gridDim.x - 1) / gridDim.x;
+    const long long u0 = per * blockIdx.x, u1 = u0 + per < units ? u0 + per : units;
+    for (long long u = u0; u < u1; u += 4096) {
+      const unsigned n = (unsigned)((u1 - u < 4096 ? u1 - u : 4096) * 16);
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(static_cast<const char*>(pf.ptr[j]) + u * 16),
+                   "r"(n)
+                   : "memory");
+    }
+  }
+}
+
 // Dispatch a runtime dtype code to a C++ type and invoke f.template
 // operator()<T>().  Returns KANI_ERR_DTYPE for unknown codes.
 template <typename F>

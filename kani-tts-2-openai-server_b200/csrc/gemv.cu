@@ -55,6 +55,7 @@ struct GemvParams {
   void* conv_state;  // EPI 2: [batch, n, kConvL] state, batch stride
   int64_t conv_state_stride;
   const void* conv_w;  // EPI 2: [n, kConvL]
+  L2Prefetch pf;       // later launches' weights, prefetched into L2 at entry
 };
 
 constexpr int kConvL = 3;  // the LFM2 short-conv kernel length the fused epilogue serves
@@ -164,6 +165,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvParams p) {
   };
   if (r < p.n) load_row(r);
   const uint4 nw0 = first_norm_chunk<T, B, K, NORM>(p, tid);
+  l2_prefetch_share(p.pf);
   griddep_launch_dependents();
   griddep_wait();
 
@@ -289,6 +291,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_rope_kv_kernel(GemvParams p
   };
   load_rows(0);
   const uint4 nw0 = first_norm_chunk<T, B, K, NORM>(p, tid);
+  l2_prefetch_share(p.pf);
   griddep_launch_dependents();
   griddep_wait();
   stage_input<T, B, K, NORM>(p, as, s_part, tid, lane, warp, nw0);
@@ -452,6 +455,7 @@ extern "C" int kani_gemv(int32_t dtype, const void* x, int64_t x_row_stride, con
                          const void* norm_weight, float eps, const void* weight, int64_t weight_row_stride,
                          int32_t n_out, int32_t k, int64_t batch, int32_t silu_pairs, void* y, int64_t y_row_stride,
                          void* stream) {
+  const kani::L2Prefetch pf = kani::take_l2_prefetch();
   if (batch < 0 || n_out < 0 || k < 0) return KANI_ERR_INVALID_ARG;
   if (batch == 0 || n_out == 0) return KANI_OK;
   const int rc = kani::check_gemv(dtype, x, x_row_stride, residual, residual_row_stride, residual_out,
@@ -460,7 +464,7 @@ extern "C" int kani_gemv(int32_t dtype, const void* x, int64_t x_row_stride, con
   if (rc != KANI_OK) return rc;
   kani::GemvParams prm{x, x_row_stride, residual, residual_row_stride, residual_out, residual_out_row_stride,
                        norm_weight, eps, weight, weight_row_stride, n_out, k, (int)batch, y, y_row_stride,
-                       nullptr, 0, nullptr};
+                       nullptr, 0, nullptr, pf};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool norm = norm_weight != nullptr;
   const int epi = silu_pairs != 0 ? 1 : 0;
@@ -474,6 +478,7 @@ extern "C" int kani_gemv_short_conv(int32_t dtype, const void* x, int64_t x_row_
                                     int64_t weight_row_stride, int32_t hidden, int32_t k, int64_t batch,
                                     void* conv_state, int64_t conv_state_batch_stride, const void* conv_weight,
                                     int32_t kernel_len, void* y, int64_t y_row_stride, void* stream) {
+  const kani::L2Prefetch pf = kani::take_l2_prefetch();
   if (batch < 0 || hidden < 0 || k < 0) return KANI_ERR_INVALID_ARG;
   if (batch == 0 || hidden == 0) return KANI_OK;
   if (!conv_state || !conv_weight) return KANI_ERR_INVALID_ARG;
@@ -485,7 +490,7 @@ extern "C" int kani_gemv_short_conv(int32_t dtype, const void* x, int64_t x_row_
   if (rc != KANI_OK) return rc;
   kani::GemvParams prm{x, x_row_stride, residual, residual_row_stride, residual_out, residual_out_row_stride,
                        norm_weight, eps, in_proj_weight, weight_row_stride, hidden, k, (int)batch, y, y_row_stride,
-                       conv_state, conv_state_batch_stride, conv_weight};
+                       conv_state, conv_state_batch_stride, conv_weight, pf};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool norm = norm_weight != nullptr;
   if (dtype == KANI_DTYPE_BF16) return kani::launch_gemv<__nv_bfloat16>(prm, norm, 2, s);
@@ -536,6 +541,7 @@ extern "C" int kani_gemv_rope_kv(int32_t dtype, const void* x, int64_t x_row_str
                                  void* v_cache, int64_t cache_batch_stride, int64_t cache_head_stride,
                                  int64_t cache_slot_stride, int64_t cache_len, const int64_t* slots,
                                  int32_t* err_flag, void* stream) {
+  const kani::L2Prefetch pf = kani::take_l2_prefetch();
   if (batch < 0 || k < 0 || num_q_heads < 0 || num_kv_heads < 0) return KANI_ERR_INVALID_ARG;
   if (batch == 0) return KANI_OK;
   if (batch > 4 || k != 1024 || head_dim != kani::kRopeD || num_q_heads < 1 || num_kv_heads < 1)
@@ -555,7 +561,7 @@ extern "C" int kani_gemv_rope_kv(int32_t dtype, const void* x, int64_t x_row_str
     return KANI_ERR_UNSUPPORTED;
   kani::GemvParams prm{x, x_row_stride, residual, residual_row_stride, residual_out, residual_out_row_stride,
                        norm_weight, eps, qkv_weight, weight_row_stride, n_rows, k, (int)batch, q_out, 0,
-                       nullptr, 0, nullptr};
+                       nullptr, 0, nullptr, pf};
   int shift = -1;
   if (tokens_per_frame > 0 && (tokens_per_frame & (tokens_per_frame - 1)) == 0)
     for (shift = 0; (1 << shift) < tokens_per_frame; ++shift) {

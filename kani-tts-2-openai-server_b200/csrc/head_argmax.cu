@@ -40,6 +40,7 @@ struct HeadParams {
   unsigned long long* scratch;  // [batch] packed maxima, then one CTA counter
   int64_t* tokens;
   int64_t tokens_stride;
+  L2Prefetch pf;  // later launches' weights, prefetched into L2 at entry
 };
 
 template <typename T>
@@ -75,6 +76,7 @@ __global__ void __launch_bounds__(kHeadThreads) head_argmax_kernel(HeadParams p)
     }
   };
   if (gw * kHeadRows < p.rows) load_rows(gw * kHeadRows);
+  l2_prefetch_share(p.pf);
   griddep_wait();
 
   // The hidden rows are written by the launch before, which may still be
@@ -219,6 +221,7 @@ extern "C" int kani_head_argmax(int32_t dtype, const void* hidden, int64_t hidde
                                 const int64_t* index_map, void* logits_out, int64_t logits_row_stride,
                                 unsigned long long* scratch, int64_t* tokens_out, int64_t tokens_out_stride,
                                 void* stream) {
+  const kani::L2Prefetch pf = kani::take_l2_prefetch();
   if (batch < 0 || rows < 0 || hidden_size < 0) return KANI_ERR_INVALID_ARG;
   if (batch == 0) return KANI_OK;
   if (rows == 0 || !hidden || !weight || !scratch || !tokens_out) return KANI_ERR_INVALID_ARG;
@@ -231,7 +234,7 @@ extern "C" int kani_head_argmax(int32_t dtype, const void* hidden, int64_t hidde
   if (!kani::aligned16(hidden) || !kani::aligned16(weight) || hidden_row_stride % 8 != 0 || weight_row_stride % 8 != 0)
     return KANI_ERR_UNSUPPORTED;
   kani::HeadParams prm{hidden, hidden_row_stride, weight, weight_row_stride, rows, hidden_size, (int)batch,
-                       index_map, logits_out, logits_row_stride, scratch, tokens_out, tokens_out_stride};
+                       index_map, logits_out, logits_row_stride, scratch, tokens_out, tokens_out_stride, pf};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == KANI_DTYPE_BF16) return kani::launch_head<__nv_bfloat16>(prm, s);
   return kani::launch_head<__half>(prm, s);

@@ -40,6 +40,7 @@ _SIGNATURES = {
     "kani_status_string": ([ctypes.c_int], ctypes.c_char_p),
     "kani_launch_count": ([], ctypes.c_uint64),
     "kani_set_wait_limit": ([_c_i64], ctypes.c_int),
+    "kani_set_l2_prefetch": ([_c_p, _c_i64, _c_p, _c_i64], ctypes.c_int),
     "kani_rms_norm": ([_c_i32, _c_i32, _c_p, _c_i64, _c_p, _c_p, _c_i64, _c_i64, _c_i64, _c_f32, _c_p],
                       ctypes.c_int),
     "kani_add_rms_norm": ([_c_i32, _c_i32, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_p, _c_i64, _c_p, _c_i64,
@@ -137,6 +138,18 @@ def set_wait_limit(cycles: int) -> None:
     """Bound the kernels' on-chip TMA waits to `cycles` (0: the default ~1 s);
     a test of the timeout path (KANI_FLAG_TIMEOUT).  Process-wide."""
     check(load_library().kani_set_wait_limit(int(cycles)), "kani_set_wait_limit")
+
+
+def set_l2_prefetch(ranges) -> None:
+    """Name up to two device ranges ((address, bytes) pairs, 16-byte aligned)
+    that the next decode GEMV / head launch from this thread prefetches into L2
+    as it starts; ``None`` or ``()`` clears the hint."""
+    r = list(ranges or ())
+    if len(r) > 2:
+        raise ValueError("at most two L2 prefetch ranges per launch")
+    r += [(None, 0)] * (2 - len(r))
+    check(load_library().kani_set_l2_prefetch(r[0][0], int(r[0][1]), r[1][0], int(r[1][1])),
+          "kani_set_l2_prefetch")
 
 
 def check(code: int, op: str) -> None:

@@ -118,6 +118,7 @@ class FusedDecoder:
         self.full_to_reduced[self.reduced_to_full] = torch.arange(self.reduced_to_full.numel(), device=dev)
         sp = state_dict.get("model.speaker_emb_projection.weight")
         self.speaker_proj = sp.to(dev, self.dtype) if sp is not None else None
+        self._pack_weights()
 
         # static state: caches, conv states, error flag
         self.k_cache = {i: torch.zeros(batch, self.hk, max_len, d, dtype=self.dtype, device=dev)
@@ -155,6 +156,68 @@ class FusedDecoder:
         self.res_buf = [torch.empty(batch, 1, h, dtype=self.dtype, device=dev) for _ in range(2)]
         self.logits_buf = torch.empty(batch, 1, self.head.shape[0], dtype=self.dtype, device=dev)
         self.argmax_buf = torch.empty(batch, dtype=torch.long, device=dev)
+
+    # ------------------------------------------------------------ weights in HBM
+    def _pack_weights(self) -> None:
+        """Moves the projection weights and the padded head into one buffer in the
+        order a decode step reads them (per layer: QKV or in_proj, o_proj or
+        out_proj, gate/up, down; then the head), so the weights of the launches
+        ahead of any launch are one contiguous range (two where the step wraps
+        around).  ``weight_spans`` holds each projection's [start, end) byte range."""
+        keys = []
+        for L in self.layers:
+            keys += [(L, k) for k in (("qkv", "o") if L["attn"] else ("in_proj", "out_proj")) + ("gate_up", "down")]
+        total = sum(L[k].numel() for L, k in keys) + self.head_padded.numel()
+        self.weight_arena = arena = torch.empty(total, dtype=self.dtype, device=self.device)
+        es = arena.element_size()
+        self.weight_spans = []
+        off = 0
+        for L, k in keys:
+            n = L[k].numel()
+            L[k] = arena[off:off + n].view_as(L[k]).copy_(L[k])
+            self.weight_spans.append((off * es, (off + n) * es))
+            off += n
+        n = self.head_padded.numel()
+        self.head_padded = arena[off:off + n].view_as(self.head_padded).copy_(self.head_padded)
+        self.head = self.head_padded[:self.num_reduced]
+        self.weight_spans.append((off * es, (off + n) * es))
+        self._l2_plan = None
+
+    # Each decode GEMV (and the fused head) prefetches into L2, as it starts, the
+    # weights of the launches after it, up to this many bytes past the end of
+    # its own: the weight stream keeps DRAM busy through the launch boundaries,
+    # the attention launch and each GEMV's tail.  0 turns the prefetch off.
+    l2_prefetch_ahead = 32 << 20
+
+    def _l2_prefetch_plan(self) -> list:
+        """Per weight-reading launch of the fused-GEMV step (in step order, the head
+        last): the (address, bytes) ranges it prefetches, [F(i-1), F(i)) with
+        F(i) = end of its weights + ``l2_prefetch_ahead``, taken modulo the
+        arena (the head's frontier wraps into the next step's first layers)."""
+        ahead = int(self.l2_prefetch_ahead) // 16 * 16
+        if ahead <= 0:
+            return [None] * len(self.weight_spans)
+        if self._l2_plan is not None and self._l2_plan[0] == ahead:
+            return self._l2_plan[1]
+        total = self.weight_arena.numel() * self.weight_arena.element_size()
+        ahead = min(ahead, total)
+        base = self.weight_arena.data_ptr()
+        plan = []
+        prev = ahead  # the frontier the previous step's head launch left, modulo the arena
+        for _, end in self.weight_spans:
+            front = end + ahead
+            lo, hi = prev, front
+            ranges = []
+            if hi > lo:
+                a, b = lo % total, (hi - 1) % total + 1
+                if lo // total == (hi - 1) // total:
+                    ranges.append((base + a, b - a))
+                else:
+                    ranges += [(base + a, total - a), (base, b)]
+            plan.append(ranges or None)
+            prev = max(prev, front)
+        self._l2_plan = (ahead, plan)
+        return plan
 
     # ------------------------------------------------------------ decode
     fused_greedy_head = True   # greedy / sampled steps may use the fused head kernels
@@ -199,7 +262,10 @@ class FusedDecoder:
 
     def _fused_head(self, normed, index_map=None, logits_out=None, out=None) -> torch.Tensor:
         fn = head_argmax if self.fused_head == "gemv" else head_argmax_tc
-        kw = {"err_flag": self.err_flag} if self.fused_head == "tc" else {}
+        if self.fused_head == "tc":
+            kw = {"err_flag": self.err_flag}
+        else:
+            kw = {"l2_prefetch": self._l2_prefetch_plan()[-1]} if self.small_batch else {}
         return fn(normed, self.head, index_map, scratch=self.head_scratch, logits_out=logits_out, out=out, **kw)
 
     def step_logits(self, input_ids: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor,
@@ -245,6 +311,7 @@ class FusedDecoder:
         hidden = F.embedding(input_ids, self.embed)              # [B, 1, H] residual stream
         delta = None
         flip = 0
+        pf = iter(self._l2_prefetch_plan())
 
         def normed(fn, *args, **kw):
             # fn (a GEMV launch) on RMSNorm(hidden + delta); the sum becomes the new residual stream
@@ -264,15 +331,16 @@ class FusedDecoder:
                                self.k_cache[i], self.v_cache[i], slots, num_q_heads=hq, num_kv_heads=hk,
                                q_norm_w=L["q_norm"], k_norm_w=L["k_norm"], head_eps=self.eps,
                                frame_table=self.frame_table, tokens_per_frame=self.cfg.tokens_per_frame,
-                               err_flag=self.err_flag)
+                               err_flag=self.err_flag, l2_prefetch=next(pf))
                 attn = decode_attention(q_rot, self.k_cache[i], self.v_cache[i], kv_len, self.scale,
                                         err_flag=self.err_flag, prefix_final=self.dependent_attention)
-                delta = gemv(attn.view(b, 1, self.q_dim), L["o"])
+                delta = gemv(attn.view(b, 1, self.q_dim), L["o"], l2_prefetch=next(pf))
             else:
-                y = normed(gemv_short_conv, L["in_proj"], self.conv_state[i], L["conv_w"], norm_weight=L["op_norm"])
-                delta = gemv(y, L["out_proj"])
-            act = normed(gemv, L["gate_up"], norm_weight=L["ffn_norm"], silu_pairs=True)
-            delta = gemv(act, L["down"])
+                y = normed(gemv_short_conv, L["in_proj"], self.conv_state[i], L["conv_w"], norm_weight=L["op_norm"],
+                           l2_prefetch=next(pf))
+                delta = gemv(y, L["out_proj"], l2_prefetch=next(pf))
+            act = normed(gemv, L["gate_up"], norm_weight=L["ffn_norm"], silu_pairs=True, l2_prefetch=next(pf))
+            delta = gemv(act, L["down"], l2_prefetch=next(pf))
         normed, _ = fused_add_rms_norm(delta, hidden, self.final_norm, self.eps)
         return normed
 

@@ -593,7 +593,7 @@ def sample_tokens(logits: torch.Tensor, seen: torch.Tensor | None = None, *, tem
 
 def gemv(x: torch.Tensor, weight: torch.Tensor, *, norm_weight: torch.Tensor | None = None,
          residual: torch.Tensor | None = None, residual_out: torch.Tensor | None = None, eps: float = 1e-5,
-         silu_pairs: bool = False, out: torch.Tensor | None = None) -> torch.Tensor:
+         silu_pairs: bool = False, out: torch.Tensor | None = None, l2_prefetch=None) -> torch.Tensor:
     """Decode GEMV for up to 8 streams with the residual add + RMSNorm before it and
     (``silu_pairs``) the SiLU·mul after it, in one launch (the F.linear calls of
     optimized_decode.py:175-289 with their neighbouring norm / activation).
@@ -603,6 +603,8 @@ def gemv(x: torch.Tensor, weight: torch.Tensor, *, norm_weight: torch.Tensor | N
             the residual-stream update that is added to ``residual`` and normalised).
         weight: [N, K] ([2N, K], gate rows then up rows, with ``silu_pairs``).
         residual_out: receives round(x + residual) (must not alias x or residual).
+        l2_prefetch: up to two (address, bytes) device ranges, the weights of
+            later launches, that this launch prefetches into L2 as it starts.
     Returns:
         [B, N] (or [B, 1, N] for a [B, 1, K] input).
     """
@@ -640,6 +642,8 @@ def gemv(x: torch.Tensor, weight: torch.Tensor, *, norm_weight: torch.Tensor | N
     ov2, ob, ys = _rows_view(out, n)
     if ob != b or ov2.data_ptr() != out.data_ptr():
         raise ValueError(f"out must be [{b}, {n}] rows with a uniform stride")
+    if l2_prefetch:
+        _lib.set_l2_prefetch(l2_prefetch)
     check(lib.kani_gemv(code, ptr(xv), xs, ptr(rv) if rv is not None else None, rs,
                         ptr(ov) if ov is not None else None, os_,
                         ptr(norm_weight) if norm_weight is not None else None, float(eps), ptr(weight),
@@ -716,11 +720,12 @@ def gemm_tc(x: torch.Tensor, weight: torch.Tensor, *, norm_weight: torch.Tensor 
 def gemv_short_conv(x: torch.Tensor, in_proj_weight: torch.Tensor, conv_state: torch.Tensor,
                     conv_weight: torch.Tensor, *, norm_weight: torch.Tensor | None = None,
                     residual: torch.Tensor | None = None, residual_out: torch.Tensor | None = None,
-                    eps: float = 1e-5, out: torch.Tensor | None = None) -> torch.Tensor:
+                    eps: float = 1e-5, out: torch.Tensor | None = None, l2_prefetch=None) -> torch.Tensor:
     """in_proj GEMV + the gated short-conv decode step in one launch
     (optimized_decode.py:255-277), with the optional residual add + RMSNorm
     prologue of ``gemv``.  in_proj_weight [3H, K]; conv_state [B, H, 3] (updated in
-    place); conv_weight [H, 3].  Returns y [B, H] (or [B, 1, H])."""
+    place); conv_weight [H, 3].  ``l2_prefetch`` as in ``gemv``.  Returns y [B, H]
+    (or [B, 1, H])."""
     for t, w in ((x, "x"), (in_proj_weight, "in_proj_weight"), (conv_state, "conv_state"),
                  (conv_weight, "conv_weight")):
         require_cuda(t, w)
@@ -752,6 +757,8 @@ def gemv_short_conv(x: torch.Tensor, in_proj_weight: torch.Tensor, conv_state: t
     if out is None:
         out = torch.empty(*x.shape[:-1], h, dtype=x.dtype, device=x.device)
     ov2, _, ys = _rows_view(out, h)
+    if l2_prefetch:
+        _lib.set_l2_prefetch(l2_prefetch)
     check(lib.kani_gemv_short_conv(code, ptr(xv), xs, ptr(rv) if rv is not None else None, rs,
                                    ptr(ov) if ov is not None else None, os_,
                                    ptr(norm_weight) if norm_weight is not None else None, float(eps),
@@ -769,13 +776,13 @@ def gemv_rope_kv_write(x: torch.Tensor, qkv_weight: torch.Tensor, norm_weight: t
                        k_norm_w: torch.Tensor | None = None, head_eps: float = 1e-5,
                        frame_table: torch.Tensor | None = None, tokens_per_frame: int = 4,
                        frame_pos: torch.Tensor | None = None, q_out: torch.Tensor | None = None,
-                       err_flag: torch.Tensor | None = None) -> torch.Tensor:
+                       err_flag: torch.Tensor | None = None, l2_prefetch=None) -> torch.Tensor:
     """The attention block's QKV projection (with the input residual add +
     RMSNorm) fused with q/k norm, RoPE, the frame term and the KV write, one
     launch for up to 4 streams (optimized_decode.py:215-240).  x: [B, 1, K]
     (the residual-stream update, or the normed input's source when no
     residual); caches [B, Hk, S, 64]; position / write_pos: [B] int64.
-    Returns q_out [B, Hq, 64]."""
+    ``l2_prefetch`` as in ``gemv``.  Returns q_out [B, Hq, 64]."""
     require_cuda(x, "x")
     lib = load_library()
     code = dtype_code(x, "x")
@@ -794,6 +801,8 @@ def gemv_rope_kv_write(x: torch.Tensor, qkv_weight: torch.Tensor, norm_weight: t
     pos = position.reshape(-1).contiguous()
     slots = write_pos.reshape(-1).contiguous()
     fpos = frame_pos.reshape(-1).contiguous() if frame_pos is not None else None
+    if l2_prefetch:
+        _lib.set_l2_prefetch(l2_prefetch)
     check(lib.kani_gemv_rope_kv(
         code, ptr(xv), xs, ptr(rv) if rv is not None else None, rs, ptr(ov) if ov is not None else None, os_,
         ptr(norm_weight.contiguous()), float(eps), ptr(qkv_weight), qkv_weight.stride(0), k, b, num_q_heads,
@@ -809,7 +818,7 @@ def gemv_rope_kv_write(x: torch.Tensor, qkv_weight: torch.Tensor, norm_weight: t
 
 def head_argmax(hidden: torch.Tensor, weight: torch.Tensor, index_map: torch.Tensor | None = None, *,
                 scratch: torch.Tensor | None = None, logits_out: torch.Tensor | None = None,
-                out: torch.Tensor | None = None) -> torch.Tensor:
+                out: torch.Tensor | None = None, l2_prefetch=None) -> torch.Tensor:
     """Greedy next token from the reduced LM head (optimized_decode.py:287 and the
     reduced-to-full map of :144-148) for up to 8 streams in one launch.
 
@@ -821,6 +830,7 @@ def head_argmax(hidden: torch.Tensor, weight: torch.Tensor, index_map: torch.Ten
             zero by every call; allocated (zeroed) per call when None.
         logits_out: optional [B, rows] tensor that receives the logits.
         out: optional [B] int64 tensor for the token ids.
+        l2_prefetch: as in ``gemv``.
     Returns:
         [B] int64 token ids.
     """
@@ -857,6 +867,8 @@ def head_argmax(hidden: torch.Tensor, weight: torch.Tensor, index_map: torch.Ten
         out = torch.empty(b, dtype=torch.int64, device=dev)
     if out.dtype != torch.int64 or out.numel() != b:
         raise ValueError(f"out must hold {b} int64 token ids")
+    if l2_prefetch:
+        _lib.set_l2_prefetch(l2_prefetch)
     check(lib.kani_head_argmax(code, ptr(hv), hs, b, h, ptr(weight), weight.stride(0), rows,
                                ptr(index_map) if index_map is not None else None,
                                ptr(logits_out) if logits_out is not None else None, ls, ptr(scratch),

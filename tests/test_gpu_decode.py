@@ -235,6 +235,40 @@ def test_full_size_graph_replays_are_deterministic(b):
     assert torch.equal(runs[0], ref.generated)
 
 
+@pytest.mark.parametrize("b", [1, 3])
+def test_l2_prefetch_changes_no_output(b):
+    """The L2 prefetch of later launches' weights (issued by each decode GEMV and
+    the head as they start) moves no data into any output: logits of two steps
+    and 40 captured greedy tokens are identical with the prefetch off, at its
+    default distance and at a distance past the whole weight buffer."""
+    cfg = LFM2Config()
+    sd = synthetic_state_dict(cfg, seed=0, device=DEV)
+    n = 40
+    g = torch.Generator().manual_seed(5)
+    ids = torch.randint(0, cfg.audio_tokens_start, (b, 128), generator=g).to(DEV)
+    spk = torch.randn(b, cfg.speaker_emb_dim, generator=g).to(DEV)
+    dec = FusedDecoder(cfg, sd, DEV, batch=b, max_len=256)
+    assert dec.small_batch and dec.l2_prefetch_ahead > 0
+    total = dec.weight_arena.numel() * dec.weight_arena.element_size()
+    assert dec.weight_spans[-1][1] == total
+    tokens, logits = [], []
+    for ahead in (0, FusedDecoder.l2_prefetch_ahead, 2 * total):
+        dec.l2_prefetch_ahead = ahead
+        eng = DecodeEngine(dec)
+        eng.start(ids, spk, n)
+        lg = [dec.step_logits(eng.input_ids, eng.positions, eng.slots, eng.kv_len).clone()]
+        eng.capture()
+        eng.run(n)
+        torch.cuda.synchronize()
+        tokens.append(eng.generated.clone())
+        logits.append(lg[0])
+        assert int(dec.err_flag.item()) == 0
+        eng.graph = None
+        del eng
+    assert torch.equal(tokens[0], tokens[1]) and torch.equal(tokens[0], tokens[2])
+    assert torch.equal(logits[0], logits[1]) and torch.equal(logits[0], logits[2])
+
+
 def test_engine_with_device_sampling_graph_matches_eager():
     """The sampler inside the captured step (Philox counter and repetition bitmap
     advanced on the device) gives the same token sequence as eager steps, every

@@ -55,6 +55,62 @@ def test_wait_limit_setter():
         _lib.set_wait_limit(-5)
 
 
+def test_l2_prefetch_hint_setter():
+    lib = _lib.load_library()
+    a = ctypes.c_void_p(0x10000)
+    assert lib.kani_set_l2_prefetch(a, -16, None, 0) == -1          # negative size
+    assert lib.kani_set_l2_prefetch(None, 16, None, 0) == -1        # size without a range
+    assert lib.kani_set_l2_prefetch(a, 24, None, 0) == -3           # not a multiple of 16 bytes
+    assert lib.kani_set_l2_prefetch(ctypes.c_void_p(0x10008), 16, None, 0) == -3
+    assert lib.kani_set_l2_prefetch(a, 4096, a, 1 << 20) == 0
+    # the next GEMV entry point takes the hint even when it rejects its own
+    # arguments (batch > 8 here), so a refused call leaves no stale hint behind
+    fake = ctypes.c_void_p(0x1000)
+    n = None
+    assert lib.kani_gemv(1, fake, 1024, n, 0, n, 0, n, 1e-5, fake, 1024, 64, 1024, 9, 0, fake, 64, n) == -3
+    assert lib.kani_set_l2_prefetch(None, 0, None, 0) == 0
+    with pytest.raises(ValueError):
+        _lib.set_l2_prefetch([(0x10000, 16)] * 3)
+    with pytest.raises(_lib.KaniError):
+        _lib.set_l2_prefetch([(0x10000, 17)])
+    _lib.set_l2_prefetch(None)
+
+
+def test_l2_prefetch_plan_covers_the_weights_once_per_step():
+    """The decode step's prefetch ranges, launch by launch: each launch's ranges
+    continue where the previous launch's ended, run `ahead` bytes past the end of
+    its own weights, and over one step cover the weight buffer exactly once
+    (the head's ranges wrap into the next step's first layers)."""
+    from types import SimpleNamespace
+
+    import torch
+    from kani_tts_b200.decode import FusedDecoder
+
+    arena = torch.empty(1 << 16, dtype=torch.bfloat16)       # 128 KB of "weights"
+    total = arena.numel() * 2
+    cuts = [0, 4096, 6144, 40960, 57344, 61440, 63488, 98304, 114688, total]
+    for ahead in (16384, 40000 // 16 * 16, total, 3 * total):
+        fake = SimpleNamespace(weight_arena=arena, weight_spans=list(zip(cuts[:-1], cuts[1:])),
+                               l2_prefetch_ahead=ahead, _l2_plan=None)
+        plan = FusedDecoder._l2_prefetch_plan(fake)
+        assert len(plan) == len(cuts) - 1
+        base = arena.data_ptr()
+        covered = []
+        for (_, end), ranges in zip(fake.weight_spans, plan):
+            for addr, nbytes in ranges or ():
+                assert nbytes > 0 and nbytes % 16 == 0 and (addr - base) % 16 == 0
+                assert base <= addr and addr + nbytes <= base + total
+                covered.append((addr - base, addr - base + nbytes))
+        covered.sort()
+        assert covered[0][0] == 0 and covered[-1][1] == total
+        assert all(a[1] == b[0] for a, b in zip(covered, covered[1:]))   # no gap, no overlap
+        first = plan[0][0]
+        assert first[0] - base == min(ahead, total) % total or ahead >= total
+    fake.l2_prefetch_ahead = 0
+    fake._l2_plan = None
+    assert FusedDecoder._l2_prefetch_plan(fake) == [None] * (len(cuts) - 1)
+
+
 def test_abi_rejects_bad_arguments_without_launching():
     lib = _lib.load_library()
     before = lib.kani_launch_count()

@@ -24,6 +24,8 @@
 // hardware barriers that every CTA of the cluster reaches.  With contiguous
 // cache rows the K/V range is staged by TMA (decode_attn_kernel below);
 // otherwise the register variant reads it directly.
+#include <atomic>
+
 #include <cooperative_groups.h>
 
 #include "common.cuh"
@@ -232,16 +234,28 @@ decode_attn_reg_kernel(AttnParams p) {
 
 // ------------------------------------------------------- TMA-staged variant
 // Same math and lane layout; the CTA's key range is brought into a ring of
-// kAttnStages shared-memory stages of kAttnTile keys (K tile + V tile) by TMA
-// bulk copies completing on one mbarrier per stage (plain bulk copies, each
+// STAGES shared-memory stages of TILE keys (K tile + V tile) by TMA bulk
+// copies completing on one mbarrier per stage (plain bulk copies, each
 // targeting this CTA only), so the bytes in flight are bounded by shared
 // memory instead of registers.  Needs contiguous cache rows (slot stride ==
 // head_dim).  Each lane takes two keys per tile pass and rescales its running
-// sums once per pair.  Waits are bounded (KANI_FLAG_TIMEOUT); a CTA that
-// times out contributes an empty partial and still reaches both cluster
-// barriers.
+// sums once per pair; NW warps take 16 * NW keys per pass.  Two shapes: 4
+// warps over 64-key tiles (3 stages) for many streams, and 8 warps over
+// 128-key tiles (2 stages) for up to 4 streams, where each CTA's share of the
+// prefix (at most 256 keys of a 2048-slot cache) is one or two passes.
+//
+// The CTAs of a cluster merge their partials by pushing them into rank 0's
+// shared memory (distributed shared-memory stores), then one split cluster
+// barrier (arrive.release / wait.acquire); rank 0 finishes alone from its own
+// shared memory.  A barrier phase armed at kernel entry and waited on before
+// the first remote store makes sure every CTA of the cluster has started.
+// Waits are bounded (KANI_FLAG_TIMEOUT); a CTA that times out contributes an
+// empty partial and still reaches both barrier phases.
 constexpr int kAttnTile = 64;
 constexpr int kAttnStages = 3;
+constexpr int kAttnWideTile = 128;
+constexpr int kAttnWideStages = 2;
+constexpr int kAttnWideWarps = 8;
 constexpr long long kAttnWaitCycles = 2000000000LL;  // ~1 s
 
 __device__ __forceinline__ uint32_t attn_smem_u32(const void* ptr) {
@@ -285,26 +299,38 @@ __device__ __forceinline__ bool attn_wait_bounded(uint32_t bar, uint32_t parity,
   return true;
 }
 
-template <typename T, int G, int D>
-__global__ void __launch_bounds__(kAttnThreads)
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+template <typename T, int G, int D, int NW, int TILE, int STAGES>
+__global__ void __launch_bounds__(NW * 32)
 decode_attn_kernel(AttnParams p) {
   griddep_launch_dependents();  // a dependent GEMV may start streaming its weights
+  constexpr int NT = NW * 32;
   constexpr int DL = D / 4;
   constexpr int VE = VecN<T>::value;
   constexpr int NV = DL / VE;
-  constexpr int NW = kAttnThreads / 32;
   constexpr uint32_t ROW = D * sizeof(T);
-  constexpr uint32_t TILE_BYTES = kAttnTile * ROW;
+  constexpr uint32_t TILE_BYTES = TILE * ROW;
+  static_assert(TILE % (16 * NW) == 0, "a tile is whole passes of 16 keys per warp");
   extern __shared__ __align__(128) unsigned char ring[];  // [stage][K tile | V tile]
-  __shared__ __align__(8) uint64_t bars[kAttnStages];
+  __shared__ __align__(8) uint64_t bars[STAGES];
   __shared__ float w_m[NW][G], w_l[NW][G];
   __shared__ float w_acc[NW][G][D];
-  __shared__ float c_m[G], c_l[G];
-  __shared__ float c_acc[G][D];
+  __shared__ float g_m[kClusterCTAs][G], g_l[kClusterCTAs][G];  // rank 0: the cluster's partials
+  __shared__ float g_acc[kClusterCTAs][G][D];
 
   cg::cluster_group cluster = cg::this_cluster();
   const int crank = (int)cluster.block_rank();
   const int ncl = (int)cluster.num_blocks();  // CTAs splitting this (b, h): 1, 2, 4 or 8
+  if (ncl > 1) cluster_arrive_relaxed();      // phase 1: this CTA has started
   const int h = blockIdx.y;
   const int b = blockIdx.z;
   const int tid = threadIdx.x;
@@ -321,13 +347,13 @@ decode_attn_kernel(AttnParams p) {
   const int64_t k0 = crank * chunk;
   const int64_t k1 = k0 + chunk < len ? k0 + chunk : len;
   const int n = k1 > k0 ? (int)(k1 - k0) : 0;
-  const int ntiles = (n + kAttnTile - 1) / kAttnTile;
+  const int ntiles = (n + TILE - 1) / TILE;
   const char* kb = reinterpret_cast<const char*>(static_cast<const T*>(p.k) + b * p.cb + (int64_t)h * p.ch + k0 * p.cs);
   const char* vb = reinterpret_cast<const char*>(static_cast<const T*>(p.v) + b * p.cb + (int64_t)h * p.ch + k0 * p.cs);
 
-  auto issue = [&](int t) {  // thread 0: tile t into stage t % kAttnStages
-    const int st = t % kAttnStages;
-    const int rows = n - t * kAttnTile < kAttnTile ? n - t * kAttnTile : kAttnTile;
+  auto issue = [&](int t) {  // thread 0: tile t into stage t % STAGES
+    const int st = t % STAGES;
+    const int rows = n - t * TILE < TILE ? n - t * TILE : TILE;
     const uint32_t bytes = (uint32_t)rows * ROW;
     const uint32_t bar = attn_smem_u32(&bars[st]);
     const uint32_t dst = attn_smem_u32(ring + (size_t)st * 2 * TILE_BYTES);
@@ -343,16 +369,16 @@ decode_attn_kernel(AttnParams p) {
   // programmatic dependent (kani_decode_attention_step), the other first tiles
   // stream in before griddepcontrol.wait and that tile after it; launched
   // plainly, the wait returns at once and the order does not matter.
-  const int t_new = (len - 1 >= k0 && len - 1 < k1) ? (int)((len - 1 - k0) / kAttnTile) : -1;
+  const int t_new = (len - 1 >= k0 && len - 1 < k1) ? (int)((len - 1 - k0) / TILE) : -1;
   if (tid == 0) {
-    for (int st = 0; st < kAttnStages; ++st)
+    for (int st = 0; st < STAGES; ++st)
       asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(attn_smem_u32(&bars[st])), "r"(1) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    for (int t = 0; t < ntiles && t < kAttnStages; ++t)
+    for (int t = 0; t < ntiles && t < STAGES; ++t)
       if (t != t_new) issue(t);
   }
   griddep_wait();  // q and the newest row may come from the launch before
-  if (tid == 0 && t_new >= 0 && t_new < kAttnStages) issue(t_new);
+  if (tid == 0 && t_new >= 0 && t_new < STAGES) issue(t_new);
 
   // query heads (global) while the first tiles stream in
   float q[G][DL];
@@ -380,19 +406,19 @@ decode_attn_kernel(AttnParams p) {
   bool failed = false;
   int t_fail = ntiles;
   for (int t = 0; t < ntiles; ++t) {
-    const int st = t % kAttnStages;
-    if (!failed && !attn_wait_bounded(attn_smem_u32(&bars[st]), (uint32_t)((t / kAttnStages) & 1),
+    const int st = t % STAGES;
+    if (!failed && !attn_wait_bounded(attn_smem_u32(&bars[st]), (uint32_t)((t / STAGES) & 1),
                                       p.wait_cycles, p.wait_suspend_ns)) {
       failed = true;
       t_fail = t;
       if (lane == 0 && p.err != nullptr) atomicOr(p.err, KANI_FLAG_TIMEOUT);
     }
-    const int rows = n - t * kAttnTile < kAttnTile ? n - t * kAttnTile : kAttnTile;
+    const int rows = n - t * TILE < TILE ? n - t * TILE : TILE;
     const T* ktile = reinterpret_cast<const T*>(ring + (size_t)st * 2 * TILE_BYTES);
     const T* vtile = reinterpret_cast<const T*>(ring + (size_t)st * 2 * TILE_BYTES + TILE_BYTES);
     // two keys per lane group per pass: r0 and r0 + 8*NW
 #pragma unroll 1
-    for (int base = warp * 8; base < kAttnTile; base += 16 * NW) {
+    for (int base = warp * 8; base < TILE; base += 16 * NW) {
       const int r0 = base + kg, r1 = base + kg + 8 * NW;
       const bool v0 = !failed && r0 < rows, v1 = !failed && r1 < rows;
       float k0f[DL], k1f[DL];
@@ -447,17 +473,19 @@ decode_attn_kernel(AttnParams p) {
         }
       }
     }
-    __syncthreads();  // stage st is free again
-    if (tid == 0 && !failed && t + kAttnStages < ntiles) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      issue(t + kAttnStages);
+    if (t + STAGES < ntiles) {
+      __syncthreads();  // stage st is free again
+      if (tid == 0 && !failed) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        issue(t + STAGES);
+      }
     }
   }
   if (failed && tid == 0) {
-    // tiles t_fail .. t_fail + kAttnStages - 1 were issued and never consumed:
+    // tiles t_fail .. t_fail + STAGES - 1 were issued and never consumed:
     // let those copies into this CTA's shared memory land before it exits
-    for (int t = t_fail; t < ntiles && t < t_fail + kAttnStages; ++t)
-      attn_wait_bounded(attn_smem_u32(&bars[t % kAttnStages]), (uint32_t)((t / kAttnStages) & 1));
+    for (int t = t_fail; t < ntiles && t < t_fail + STAGES; ++t)
+      attn_wait_bounded(attn_smem_u32(&bars[t % STAGES]), (uint32_t)((t / STAGES) & 1));
   }
 
   // merge key groups (shuffles), warps (shared memory), CTAs (DSMEM)
@@ -490,7 +518,13 @@ decode_attn_kernel(AttnParams p) {
     }
   }
   __syncthreads();
-  for (int t = tid; t < G * D; t += kAttnThreads) {
+  // this CTA's partial for (g, d): warps merged; written out at once by a
+  // lone CTA, pushed into rank 0's shared memory otherwise
+  if (ncl > 1) asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // phase 1: all CTAs started
+  float* rm = ncl > 1 ? cluster.map_shared_rank(&g_m[crank][0], 0) : nullptr;
+  float* rl = ncl > 1 ? cluster.map_shared_rank(&g_l[crank][0], 0) : nullptr;
+  float* ra = ncl > 1 ? cluster.map_shared_rank(&g_acc[crank][0][0], 0) : nullptr;
+  for (int t = tid; t < G * D; t += NT) {
     const int g = t / D, d = t - (t / D) * D;
     float mx = -INFINITY;
 #pragma unroll
@@ -502,77 +536,99 @@ decode_attn_kernel(AttnParams p) {
       ls += w_l[w][g] * wt;
       as += w_acc[w][g][d] * wt;
     }
-    c_acc[g][d] = as;
-    if (d == 0) {
-      c_m[g] = mx;
-      c_l[g] = ls;
-    }
-  }
-  cluster.sync();
-  if (crank == 0) {
-    for (int t = tid; t < G * D; t += kAttnThreads) {
-      const int g = t / D, d = t - (t / D) * D;
-      float mr[kClusterCTAs];
-      float mx = -INFINITY;
-#pragma unroll
-      for (int r = 0; r < kClusterCTAs; ++r) {
-        mr[r] = r < ncl ? *cluster.map_shared_rank(&c_m[g], r) : -INFINITY;
-        mx = fmaxf(mx, mr[r]);
-      }
-      float ls = 0.f, as = 0.f;
-#pragma unroll
-      for (int r = 0; r < kClusterCTAs; ++r) {
-        if (r >= ncl) break;
-        const float wt = merge_weight(mr[r], mx);
-        ls += *cluster.map_shared_rank(&c_l[g], r) * wt;
-        as += *cluster.map_shared_rank(&c_acc[g][d], r) * wt;
-      }
+    if (ncl == 1) {
       T* o = static_cast<T*>(p.out) + b * p.ob + (int64_t)(h * G + g) * p.oh + d;
       *o = Elem<T>::from_f(ls > 0.f ? as / ls : 0.f);
+    } else {
+      ra[t] = as;
+      if (d == 0) {
+        rm[g] = mx;
+        rl[g] = ls;
+      }
     }
   }
-  cluster.sync();
+  if (ncl == 1) return;
+  cluster_arrive_release();  // phase 2: this CTA's partial is in rank 0's shared memory
+  if (crank != 0) return;    // nothing reads the other CTAs' shared memory
+  cluster_wait_acquire();
+  for (int t = tid; t < G * D; t += NT) {
+    const int g = t / D, d = t - (t / D) * D;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < kClusterCTAs; ++r)
+      if (r < ncl) mx = fmaxf(mx, g_m[r][g]);
+    float ls = 0.f, as = 0.f;
+#pragma unroll
+    for (int r = 0; r < kClusterCTAs; ++r) {
+      if (r >= ncl) break;
+      const float wt = merge_weight(g_m[r][g], mx);
+      ls += g_l[r][g] * wt;
+      as += g_acc[r][g][d] * wt;
+    }
+    T* o = static_cast<T*>(p.out) + b * p.ob + (int64_t)(h * G + g) * p.oh + d;
+    *o = Elem<T>::from_f(ls > 0.f ? as / ls : 0.f);
+  }
+}
+
+// CTAs of one decode_attn_kernel shape resident at once on the current device
+// (occupancy API, once per device); 0 if its shared memory cannot be granted.
+template <typename T, int G, int D, int NW, int TILE, int STAGES>
+int attn_resident() {
+  static std::atomic<int> resident[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  int r = resident[dev].load(std::memory_order_relaxed);
+  if (r > 0) return r;
+  constexpr size_t smem = (size_t)STAGES * 2 * TILE * D * sizeof(T);
+  auto kern = decode_attn_kernel<T, G, D, NW, TILE, STAGES>;
+  // dynamic + static shared memory may pass the 48 KB default
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return 0;
+  int occ = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, NW * 32, smem) != cudaSuccess || occ < 1) return 0;
+  r = occ * sm_count();
+  resident[dev].store(r, std::memory_order_relaxed);
+  return r;
+}
+
+template <typename T, int G, int D, int NW, int TILE, int STAGES>
+void launch_attn_tma(const AttnParams& p, int64_t batch, int hk, int cl, cudaStream_t s, bool dependent) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)cl, (unsigned)hk, (unsigned)batch);
+  cfg.blockDim = dim3(NW * 32);
+  cfg.dynamicSmemBytes = (size_t)STAGES * 2 * TILE * D * sizeof(T);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)cl;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = dependent ? 2 : 1;
+  cudaLaunchKernelEx(&cfg, decode_attn_kernel<T, G, D, NW, TILE, STAGES>, p);
 }
 
 template <typename T, int G, int D>
 int launch_attn(const AttnParams& p, int64_t batch, int hk, cudaStream_t s, bool dependent) {
   if (p.cs == D) {  // contiguous cache rows: TMA-staged kernel, cluster size sized to fill the GPU
-    static int resident[64] = {0};  // CTAs of this kernel resident at once on the device
-    constexpr size_t smem = (size_t)kAttnStages * 2 * kAttnTile * D * sizeof(T);
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return KANI_ERR_UNSUPPORTED;
-    if (!resident[dev]) {  // dynamic + static shared memory may pass the 48 KB default
-      if (cudaFuncSetAttribute(decode_attn_kernel<T, G, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)smem) != cudaSuccess)
-        return launch_status();
-      int occ = 0;
-      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_attn_kernel<T, G, D>, kAttnThreads, smem) !=
-              cudaSuccess ||
-          occ < 1)
-        occ = 1;
-      resident[dev] = occ * sm_count();
-    }
-    // split each (stream, KV head) over the most CTAs (1, 2, 4 or 8) that still
+    // Few streams: 8-CTA clusters of the wide shape (8 warps, 128-key tiles),
+    // when all of them fit in one wave.  Otherwise the 4-warp shape, each
+    // (stream, KV head) split over the most CTAs (1, 2, 4 or 8) that still
     // fit in one wave: at 64 streams x 8 heads that is 1 (512 CTAs), at 16
-    // streams 4, at one stream 8.  A second, partial wave measured slower (64
-    // streams, 880 valid slots: 27.4 us with 1024 CTAs, 23.5 us with 512)
+    // streams 4.  A second, partial wave measured slower (64 streams, 880
+    // valid slots: 27.4 us with 1024 CTAs, 23.5 us with 512)
+    const int wide = attn_resident<T, G, D, kAttnWideWarps, kAttnWideTile, kAttnWideStages>();
+    if (wide > 0 && batch * hk * kClusterCTAs <= wide) {
+      launch_attn_tma<T, G, D, kAttnWideWarps, kAttnWideTile, kAttnWideStages>(p, batch, hk, kClusterCTAs, s,
+                                                                               dependent);
+      return launch_status();
+    }
+    const int resident = attn_resident<T, G, D, kAttnThreads / 32, kAttnTile, kAttnStages>();
+    if (resident <= 0) return launch_status();
     int cl = kClusterCTAs;
-    while (cl > 1 && batch * hk * cl > resident[dev]) cl >>= 1;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)cl, (unsigned)hk, (unsigned)batch);
-    cfg.blockDim = dim3(kAttnThreads);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = (unsigned)cl;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[1].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = dependent ? 2 : 1;
-    cudaLaunchKernelEx(&cfg, decode_attn_kernel<T, G, D>, p);
+    while (cl > 1 && batch * hk * cl > resident) cl >>= 1;
+    launch_attn_tma<T, G, D, kAttnThreads / 32, kAttnTile, kAttnStages>(p, batch, hk, cl, s, dependent);
   } else {
     const dim3 grid(kClusterCTAs, (unsigned)hk, (unsigned)batch);
     decode_attn_reg_kernel<T, G, D><<<grid, kAttnThreads, 0, s>>>(p);

@@ -79,11 +79,14 @@ def test_bulk_rope_wait_times_out_and_the_next_call_is_exact(short_waits):
         assert bool(ok.all())
 
 
-def test_decode_attention_wait_times_out_and_the_next_call_is_exact(short_waits):
-    b, hq, hk, dh, s_len = 8, 16, 8, 64, 2048
+# 8 streams run the 4-warp shape (64-key tiles, 3 stages), 2 streams the 8-warp
+# shape (128-key tiles, 2 stages) in 8-CTA clusters
+@pytest.mark.parametrize("lens", [[1629, 100, 2048, 1, 700, 1500, 65, 900], [1629, 2048]])
+def test_decode_attention_wait_times_out_and_the_next_call_is_exact(short_waits, lens):
+    b, hq, hk, dh, s_len = len(lens), 16, 8, 64, 2048
     q = rnd((b, hq, dh), 11)
     kc, vc = rnd((b, hk, s_len, dh), 12), rnd((b, hk, s_len, dh), 13)
-    kv_len = torch.tensor([1629, 100, 2048, 1, 700, 1500, 65, 900], dtype=torch.long)
+    kv_len = torch.tensor(lens, dtype=torch.long)
     flag = torch.zeros(1, dtype=torch.int32, device=DEV)
     qd, kd, vd, ld = q.to(DEV), kc.to(DEV), vc.to(DEV), kv_len.to(DEV)
     out = torch.empty(b, hq, dh, dtype=torch.bfloat16, device=DEV)

@@ -267,11 +267,18 @@ constexpr int kRopeD = 64;  // head_dim the fused epilogue serves
 constexpr int kRopeRowsPerWarp = kRopeD / kGemvWarps;
 
 // NORM: the input RMSNorm prologue; QKN: the per-head q / k RMSNorm; TABLE: the frame term
+//
+// Everything that no earlier launch writes is fetched before the
+// programmatic-launch wait: all 8 weight rows of each warp, and for warp 0
+// the lane's rotary frequencies and the head-norm weight chunks.  Right after
+// the wait warp 0 reads each stream's position, slot and frame-table row, so
+// their latency overlaps the input norm and the dot products.
 template <typename T, int B, int CH, bool NORM, bool QKN, bool TABLE>
 __global__ void __launch_bounds__(kGemvThreads) gemv_rope_kv_kernel(GemvParams p, RopeKvParams r) {
   constexpr int E = 8;
   constexpr int K = CH * 256;
-  constexpr int RB = 4;  // rows per batch of loads
+  constexpr int RW = kRopeRowsPerWarp;
+  constexpr int LOG2L = 2;  // (D/2)/E = 4 lanes per head
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ float s_part[kGemvWarps][B];
   __shared__ __align__(16) T s_head[B][kRopeD];
@@ -279,110 +286,128 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_rope_kv_kernel(GemvParams p
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int head = blockIdx.x;
   const T* W = static_cast<const T*>(p.w);
-  const int row0 = head * kRopeD + warp * kRopeRowsPerWarp;
+  const int row0 = head * kRopeD + warp * RW;
 
-  uint4 wv[RB][CH];
-  auto load_rows = [&](int rb) {
+  uint4 wv[RW][CH];
 #pragma unroll
-    for (int q = 0; q < RB; ++q)
+  for (int q = 0; q < RW; ++q)
 #pragma unroll
-      for (int c = 0; c < CH; ++c)
-        wv[q][c] = ld16_stream(W + (int64_t)(row0 + rb + q) * p.w_stride + c * 256 + lane * E);
-  };
-  load_rows(0);
+    for (int c = 0; c < CH; ++c) wv[q][c] = ld16_stream(W + (int64_t)(row0 + q) * p.w_stride + c * 256 + lane * E);
   const uint4 nw0 = first_norm_chunk<T, B, K, NORM>(p, tid);
-  l2_prefetch_share(p.pf);
-  griddep_launch_dependents();
-  griddep_wait();
-  stage_input<T, B, K, NORM>(p, as, s_part, tid, lane, warp, nw0);
-
-#pragma unroll
-  for (int rb = 0; rb < kRopeRowsPerWarp; rb += RB) {
-    if (rb) load_rows(rb);
-    float acc[RB][B];
-#pragma unroll
-    for (int q = 0; q < RB; ++q)
-#pragma unroll
-      for (int b = 0; b < B; ++b) acc[q][b] = 0.f;
-#pragma unroll
-    for (int c = 0; c < CH; ++c) {
-      float wf[RB][E];
-#pragma unroll
-      for (int q = 0; q < RB; ++q) unpack16<T>(wv[q][c], wf[q]);
-#pragma unroll
-      for (int b = 0; b < B; ++b) {
-        float af[E];
-        unpack16<T>(reinterpret_cast<const uint4*>(as + b * K + c * 256)[lane], af);
-#pragma unroll
-        for (int q = 0; q < RB; ++q)
-#pragma unroll
-          for (int e = 0; e < E; ++e) acc[q][b] = fmaf(wf[q][e], af[e], acc[q][b]);
-      }
-    }
-#pragma unroll
-    for (int q = 0; q < RB; ++q)
-#pragma unroll
-      for (int b = 0; b < B; ++b) {
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) acc[q][b] += __shfl_xor_sync(0xffffffffu, acc[q][b], o);
-        if (lane == 0) s_head[b][warp * kRopeRowsPerWarp + rb + q] = Elem<T>::from_f(acc[q][b]);
-      }
-  }
-  __syncthreads();
-  if (warp != 0) return;
-
   // warp 0: lanes 0..3 carry the head's chunk pairs (lo, hi), the other lanes
-  // help with the sin/cos; one stream after another
-  constexpr int LOG2L = 2;  // (D/2)/E = 4 lanes per head
+  // help with the sin/cos
   const int jj = lane & 3;
   const bool mine = lane < 4;
   const int lo = jj * E, hi = kRopeD / 2 + jj * E;
   const bool is_q = head < r.hq, is_k = !is_q && head < r.hq + r.hk;
   const int kv = is_q ? 0 : (is_k ? head - r.hq : head - r.hq - r.hk);
-  const LaneFreqs<T, LOG2L> lf = lane_freqs<T, LOG2L>(r.inv_freq, LOG2L, lane);
-  for (int b = 0; b < p.batch && b < B; ++b) {
-    const int64_t pos = r.positions[b];
-    const int64_t slot = r.slots[b];
-    const bool slot_ok = slot >= 0 && slot < r.clen;
-    int64_t frame = 0;
-    bool frame_ok = true;
-    if constexpr (TABLE) {
-      const int64_t fp = r.frame_pos ? r.frame_pos[b] : pos;
-      frame = fp < 0 ? -1 : (r.tpf_shift >= 0 ? (fp >> r.tpf_shift) : fp / r.tpf);
-      frame_ok = frame >= 0 && frame < r.table_rows;
+  LaneFreqs<T, LOG2L> lf{};
+  uint4 hwlo = make_uint4(0u, 0u, 0u, 0u), hwhi = hwlo;
+  if (warp == 0 && (is_q || is_k)) {
+    lf = lane_freqs<T, LOG2L>(r.inv_freq, LOG2L, lane);
+    if constexpr (QKN) {
+      const T* nw = static_cast<const T*>(is_q ? r.qw : r.kw);
+      hwlo = ld16_ro(nw + lo);
+      hwhi = ld16_ro(nw + hi);
     }
+  }
+  l2_prefetch_share(p.pf);
+  griddep_launch_dependents();
+  griddep_wait();
+
+  int64_t pos[B], slot[B];
+  uint4 plo[B], phi[B];
+  bool frame_ok[B];
+  if (warp == 0) {
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      pos[b] = 0;
+      slot[b] = -1;
+      frame_ok[b] = true;
+      plo[b] = phi[b] = make_uint4(0u, 0u, 0u, 0u);
+      if (b < p.batch) {
+        pos[b] = r.positions[b];
+        slot[b] = r.slots[b];
+        if constexpr (TABLE) {
+          const int64_t fp = r.frame_pos ? r.frame_pos[b] : pos[b];
+          const int64_t frame = fp < 0 ? -1 : (r.tpf_shift >= 0 ? (fp >> r.tpf_shift) : fp / r.tpf);
+          frame_ok[b] = frame >= 0 && frame < r.table_rows;
+          if (frame_ok[b] && mine && (is_q || is_k)) {
+            const T* pr = static_cast<const T*>(r.table) + frame * kRopeD;
+            plo[b] = ld16_ro(pr + lo);
+            phi[b] = ld16_ro(pr + hi);
+          }
+        }
+      }
+    }
+  }
+  stage_input<T, B, K, NORM>(p, as, s_part, tid, lane, warp, nw0);
+
+  float acc[RW][B];
+#pragma unroll
+  for (int q = 0; q < RW; ++q)
+#pragma unroll
+    for (int b = 0; b < B; ++b) acc[q][b] = 0.f;
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      float af[E];
+      unpack16<T>(reinterpret_cast<const uint4*>(as + b * K + c * 256)[lane], af);
+#pragma unroll
+      for (int q = 0; q < RW; ++q) {
+        float wf[E];
+        unpack16<T>(wv[q][c], wf);
+#pragma unroll
+        for (int e = 0; e < E; ++e) acc[q][b] = fmaf(wf[e], af[e], acc[q][b]);
+      }
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < RW; ++q)
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc[q][b] += __shfl_xor_sync(0xffffffffu, acc[q][b], o);
+      if (lane == 0) s_head[b][warp * RW + q] = Elem<T>::from_f(acc[q][b]);
+    }
+  __syncthreads();
+  if (warp != 0) return;
+
+  // warp 0 finishes the head, one stream after another
+#pragma unroll
+  for (int b = 0; b < B; ++b) {
+    if (b >= p.batch) break;
+    const bool slot_ok = slot[b] >= 0 && slot[b] < r.clen;
     if (lane == 0 && r.err && (head == r.hq || (head == 0 && TABLE))) {
       int bits = 0;
       if (head == r.hq && !slot_ok) bits |= KANI_FLAG_SLOT_OOB;
-      if (TABLE && head == 0 && !frame_ok) bits |= KANI_FLAG_FRAME_OOB;
+      if (TABLE && head == 0 && !frame_ok[b]) bits |= KANI_FLAG_FRAME_OOB;
       if (bits) atomicOr(r.err, bits);
     }
     const uint4 xlo = *reinterpret_cast<const uint4*>(&s_head[b][lo]);
     const uint4 xhi = *reinterpret_cast<const uint4*>(&s_head[b][hi]);
     if (!is_q && !is_k) {  // V head: copy into the cache slot
       if (mine && slot_ok) {
-        T* dst = static_cast<T*>(r.v_cache) + b * r.cbs + kv * r.chs + slot * r.css;
+        T* dst = static_cast<T*>(r.v_cache) + b * r.cbs + kv * r.chs + slot[b] * r.css;
         st16(dst + lo, xlo);
         st16(dst + hi, xhi);
       }
       continue;
     }
     float cs[E], sn[E], nsn[E], pl[E], ph[E];
-    warp_cos_sin<T, LOG2L>(lf, (float)pos, LOG2L, lane, cs, sn);
+    warp_cos_sin<T, LOG2L>(lf, (float)pos[b], LOG2L, lane, cs, sn);
 #pragma unroll
     for (int e = 0; e < E; ++e) nsn[e] = -sn[e];
     if constexpr (TABLE) {
-      if (frame_ok && mine) {
-        const T* pr = static_cast<const T*>(r.table) + frame * kRopeD;
-        unpack16<T>(ld16_ro(pr + lo), pl);
-        unpack16<T>(ld16_ro(pr + hi), ph);
-      }
+      unpack16<T>(plo[b], pl);
+      unpack16<T>(phi[b], ph);
     }
     T* dst = is_q ? static_cast<T*>(r.q_out) + b * r.qobs + head * r.qohs
-                  : static_cast<T*>(r.k_cache) + b * r.cbs + kv * r.chs + slot * r.css;
+                  : static_cast<T*>(r.k_cache) + b * r.cbs + kv * r.chs + slot[b] * r.css;
     const bool live = mine && (is_q || slot_ok);
-    rope_chunk_store<T, QKN, TABLE>(xlo, xhi, live, cs, nsn, sn, pl, ph, frame_ok,
-                                     static_cast<const T*>(is_q ? r.qw : r.kw), lo, hi, LOG2L, kRopeD, r.eps, dst);
+    rope_chunk_store_w<T, QKN, TABLE>(xlo, xhi, live, cs, nsn, sn, pl, ph, frame_ok[b], hwlo, hwhi, lo, hi, LOG2L,
+                                      kRopeD, r.eps, dst);
   }
 }
 

@@ -215,11 +215,14 @@ __device__ __forceinline__ void warp_cos_sin(const LaneFreqs<T, LOG2L_CT>& lf, f
 // sm_100's paired fp32 units (__fmul2_rn / __fadd2_rn: two independent
 // round-to-nearest operations per instruction, bit-identical to the scalar
 // form).  nsn holds -sin.
+// rope_chunk_store_w takes the two norm-weight chunks (elements [lo, lo+E)
+// and [hi, hi+E) of the head-norm weight) already loaded, so a caller can
+// fetch them ahead of time; rope_chunk_store loads them from nw.
 template <typename T, bool NORM, bool TABLE>
-__device__ __forceinline__ void rope_chunk_store(uint4 xlo, uint4 xhi, bool live, const float* cs,
-                                                 const float* nsn, const float* sn, const float* pl,
-                                                 const float* ph, bool frame_ok, const T* nw, int lo,
-                                                 int hi, int log2l, int d, float eps, T* dst) {
+__device__ __forceinline__ void rope_chunk_store_w(uint4 xlo, uint4 xhi, bool live, const float* cs,
+                                                   const float* nsn, const float* sn, const float* pl,
+                                                   const float* ph, bool frame_ok, uint4 nwlo, uint4 nwhi,
+                                                   int lo, int hi, int log2l, int d, float eps, T* dst) {
   constexpr int E = VecN<T>::value;
   float a[E], b[E];
   unpack16<T>(xlo, a);
@@ -236,8 +239,8 @@ __device__ __forceinline__ void rope_chunk_store(uint4 xlo, uint4 xhi, bool live
     for (int off = (1 << log2l) >> 1; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
     if (live) {
       float wl[E], wh[E];
-      unpack16<T>(ld16_ro(nw + lo), wl);
-      unpack16<T>(ld16_ro(nw + hi), wh);
+      unpack16<T>(nwlo, wl);
+      unpack16<T>(nwhi, wh);
       const float r = rrms_of(ss, d, eps);
       const float2 r2 = make_float2(r, r);
 #pragma unroll
@@ -275,6 +278,22 @@ __device__ __forceinline__ void rope_chunk_store(uint4 xlo, uint4 xhi, bool live
   }
   st16(dst + lo, pack16<T>(ylo));
   st16(dst + hi, pack16<T>(yhi));
+}
+
+template <typename T, bool NORM, bool TABLE>
+__device__ __forceinline__ void rope_chunk_store(uint4 xlo, uint4 xhi, bool live, const float* cs,
+                                                 const float* nsn, const float* sn, const float* pl,
+                                                 const float* ph, bool frame_ok, const T* nw, int lo,
+                                                 int hi, int log2l, int d, float eps, T* dst) {
+  uint4 wlo = make_uint4(0u, 0u, 0u, 0u), whi = wlo;
+  if constexpr (NORM) {
+    if (live) {
+      wlo = ld16_ro(nw + lo);
+      whi = ld16_ro(nw + hi);
+    }
+  }
+  rope_chunk_store_w<T, NORM, TABLE>(xlo, xhi, live, cs, nsn, sn, pl, ph, frame_ok, wlo, whi, lo, hi, log2l, d, eps,
+                                     dst);
 }
 
 }  // namespace

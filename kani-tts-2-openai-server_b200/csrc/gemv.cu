@@ -165,9 +165,28 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvParams p) {
   };
   if (r < p.n) load_row(r);
   const uint4 nw0 = first_norm_chunk<T, B, K, NORM>(p, tid);
+  // EPI 2: lane b's conv weights of the warp's first channel (before the wait)
+  // and stream b's conv state of it (after the wait), fetched ahead of the dot
+  // products instead of after them
+  const int r_first = r;
+  float cw0[kConvL] = {}, st0[kConvL] = {};
+  if constexpr (EPI == 2) {
+    if (r < p.n && lane < p.batch && lane < B) {
+      const T* cw = static_cast<const T*>(p.conv_w) + (int64_t)r * kConvL;
+#pragma unroll
+      for (int i = 0; i < kConvL; ++i) cw0[i] = Elem<T>::to_f(cw[i]);
+    }
+  }
   l2_prefetch_share(p.pf);
   griddep_launch_dependents();
   griddep_wait();
+  if constexpr (EPI == 2) {
+    if (r < p.n && lane < p.batch && lane < B) {
+      const T* st = static_cast<const T*>(p.conv_state) + (int64_t)lane * p.conv_state_stride + (int64_t)r * kConvL;
+#pragma unroll
+      for (int i = 0; i + 1 < kConvL; ++i) st0[i] = Elem<T>::to_f(st[i + 1]);
+    }
+  }
 
   stage_input<T, B, K, NORM>(p, as, s_part, tid, lane, warp, nw0);
 
@@ -214,15 +233,18 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvParams p) {
           const float bg = round_to<T>(acc[0][b]), cg = round_to<T>(acc[1][b]), xg = round_to<T>(acc[2][b]);
           T* st = static_cast<T*>(p.conv_state) + (int64_t)b * p.conv_state_stride + (int64_t)r * kConvL;
           const T* cw = static_cast<const T*>(p.conv_w) + (int64_t)r * kConvL;
-          float sv[kConvL];
+          const bool pre = r == r_first;  // the first channel's state and weights are in registers
+          float sv[kConvL], wc[kConvL];
 #pragma unroll
-          for (int i = 0; i + 1 < kConvL; ++i) sv[i] = Elem<T>::to_f(st[i + 1]);
+          for (int i = 0; i + 1 < kConvL; ++i) sv[i] = pre ? st0[i] : Elem<T>::to_f(st[i + 1]);
+#pragma unroll
+          for (int i = 0; i < kConvL; ++i) wc[i] = pre ? cw0[i] : Elem<T>::to_f(cw[i]);
           sv[kConvL - 1] = round_to<T>(__fmul_rn(bg, xg));
           float conv = 0.f;
 #pragma unroll
           for (int i = 0; i < kConvL; ++i) {
             st[i] = Elem<T>::from_f(sv[i]);
-            conv = __fadd_rn(conv, round_to<T>(__fmul_rn(sv[i], Elem<T>::to_f(cw[i]))));
+            conv = __fadd_rn(conv, round_to<T>(__fmul_rn(sv[i], wc[i])));
           }
           v = __fmul_rn(cg, round_to<T>(conv));
         } else {

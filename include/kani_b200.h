@@ -81,8 +81,9 @@ KANI_API int kani_set_wait_limit(int64_t cycles);
 
 /*
  * L2 prefetch hint for the next decode launch: the next call of kani_gemv,
- * kani_gemv_short_conv, kani_gemv_rope_kv or kani_head_argmax made on the same
- * host thread takes these (up to two) device ranges and clears them; every CTA
+ * kani_gemv_short_conv, kani_gemv_rope_kv, kani_head_argmax,
+ * kani_reduce_add_rms_norm or kani_silu_mul made on the same host thread
+ * takes these (up to two) device ranges and clears them; every CTA
  * of that launch issues its share as cp.async.bulk.prefetch.L2 as it starts,
  * before the programmatic-launch wait.  The ranges must hold data no launch
  * writes (the weights of later launches), so that reading them early is safe.

@@ -203,7 +203,8 @@ WaitBound wait_bound(long long default_cycles);
 // Device ranges a decode launch prefetches into L2 as it starts: the weights
 // of later launches, which do not depend on any earlier launch.  Set from the
 // host with kani_set_l2_prefetch and taken (and cleared) by the next decode
-// GEMV / head entry point called on the same host thread.
+// GEMV / head / reduce + add + RMSNorm / SiLU·mul entry point called on the
+// same host thread.
 struct L2Prefetch {
   const void* ptr[2];
   long long bytes[2];
@@ -215,13 +216,15 @@ L2Prefetch take_l2_prefetch();
 // to the SM, nothing waits on it, and it reads only memory that no launch
 // writes, so it may run before griddepcontrol.wait.
 __device__ __forceinline__ void l2_prefetch_share(const L2Prefetch& pf) {
-  if (threadIdx.x != 0) return;
+  if (threadIdx.x != 0 || threadIdx.y != 0 || threadIdx.z != 0) return;
+  const long long ncta = (long long)gridDim.x * gridDim.y * gridDim.z;
+  const long long cta = blockIdx.x + (long long)gridDim.x * (blockIdx.y + (long long)gridDim.y * blockIdx.z);
 #pragma unroll
   for (int j = 0; j < 2; ++j) {
     const long long units = pf.bytes[j] >> 4;
     if (pf.ptr[j] == nullptr || units <= 0) continue;
-    const long long per = (units + gridDim.x - 1) / gridDim.x;
-    const long long u0 = per * blockIdx.x, u1 = u0 + per < units ? u0 + per : units;
+    const long long per = (units + ncta - 1) / ncta;
+    const long long u0 = per * cta, u1 = u0 + per < units ? u0 + per : units;
     for (long long u = u0; u < u1; u += 4096) {
       const unsigned n = (unsigned)((u1 - u < 4096 ? u1 - u : 4096) * 16);
       asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(static_cast<const char*>(pf.ptr[j]) + u * 16),

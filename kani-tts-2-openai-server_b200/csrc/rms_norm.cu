@@ -277,6 +277,7 @@ struct RedParams {
   int64_t rows;
   int n;
   float eps;
+  L2Prefetch pf;  // later launches' weights, prefetched into L2 at entry
 };
 
 constexpr int kRedThreads = 256;
@@ -310,6 +311,7 @@ __device__ __forceinline__ void st4(T* ptr, const float* f) {
 template <typename T, typename W, int V>
 __global__ void __launch_bounds__(kRedThreads) reduce_add_norm_kernel(RedParams p) {
   griddep_launch_dependents();  // a dependent GEMV may start streaming its weights
+  l2_prefetch_share(p.pf);
   __shared__ float red[33];
   const int tid = threadIdx.x;
   for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
@@ -421,6 +423,7 @@ extern "C" int kani_reduce_add_rms_norm(int32_t dtype, int32_t w_dtype, const fl
                                         int64_t r_row_stride, const void* weight, void* y, int64_t y_row_stride,
                                         void* residual_out, int64_t h_row_stride, int64_t rows, int64_t n, float eps,
                                         void* stream) {
+  const kani::L2Prefetch pf = kani::take_l2_prefetch();
   if (rows < 0 || n < 0 || splits < 1) return KANI_ERR_INVALID_ARG;
   if (rows == 0 || n == 0) return KANI_OK;
   if (!partials || !residual || !weight || !y || !residual_out) return KANI_ERR_INVALID_ARG;
@@ -439,7 +442,7 @@ extern "C" int kani_reduce_add_rms_norm(int32_t dtype, int32_t w_dtype, const fl
       r_row_stride % 4 != 0 || y_row_stride % 4 != 0 || h_row_stride % 4 != 0)
     return KANI_ERR_UNSUPPORTED;
   kani::RedParams p{partials, split_stride, partial_row_stride, splits, residual, r_row_stride, weight, y,
-                    y_row_stride, residual_out, h_row_stride, rows, (int)n, eps};
+                    y_row_stride, residual_out, h_row_stride, rows, (int)n, eps, pf};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return kani::dispatch_dtype(dtype, [&]<typename T>() {
     return kani::dispatch_dtype(w_dtype, [&]<typename W>() { return kani::launch_reduce_norm<T, W>(p, s); });

@@ -22,8 +22,9 @@ namespace {
 template <typename T, int RY>
 __global__ void __launch_bounds__(256)
 silu_mul_vec_kernel(const T* __restrict__ gu, int64_t in_stride, T* __restrict__ y,
-                    int64_t out_stride, int64_t rows, int vpr, int64_t n) {
+                    int64_t out_stride, int64_t rows, int vpr, int64_t n, L2Prefetch pf) {
   constexpr int E = VecN<T>::value;
+  l2_prefetch_share(pf);
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= vpr) return;
   const int64_t col = (int64_t)c * E;
@@ -58,8 +59,9 @@ silu_mul_vec_kernel(const T* __restrict__ gu, int64_t in_stride, T* __restrict__
 template <typename T, int CV>
 __global__ void __launch_bounds__(192)
 silu_mul_row_kernel(const T* __restrict__ gu, int64_t in_stride, T* __restrict__ y, int64_t out_stride,
-                    int64_t rows, int vpr, int64_t n) {
+                    int64_t rows, int vpr, int64_t n, L2Prefetch pf) {
   constexpr int E = VecN<T>::value;
+  l2_prefetch_share(pf);
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const T* base = gu + r * in_stride;
     uint4 g[CV], u[CV];
@@ -90,7 +92,8 @@ silu_mul_row_kernel(const T* __restrict__ gu, int64_t in_stride, T* __restrict__
 template <typename T>
 __global__ void __launch_bounds__(256)
 silu_mul_generic_kernel(const T* __restrict__ gu, int64_t in_stride, T* __restrict__ y,
-                        int64_t out_stride, int64_t rows, int64_t n) {
+                        int64_t out_stride, int64_t rows, int64_t n, L2Prefetch pf) {
+  l2_prefetch_share(pf);
   const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= n) return;
   for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {
@@ -113,7 +116,7 @@ int pick_block_width(int vpr) {
 
 template <typename T>
 int launch_silu(const void* gu, int64_t in_stride, void* y, int64_t out_stride, int64_t rows,
-                int64_t n, cudaStream_t s) {
+                int64_t n, const L2Prefetch& pf, cudaStream_t s) {
   constexpr int E = VecN<T>::value;
   const bool vec = (n % E) == 0 && aligned16(gu) && aligned16(y) && (in_stride % E) == 0 &&
                    (out_stride % E) == 0 && n / E <= 0x7fffffff;
@@ -124,7 +127,7 @@ int launch_silu(const void* gu, int64_t in_stride, void* y, int64_t out_stride, 
       const unsigned grid = (unsigned)(rows < 0x7fffffff ? rows : 0x7fffffff);
       auto go = [&](auto kern) {
         kern<<<grid, 192, 0, s>>>(static_cast<const T*>(gu), in_stride, static_cast<T*>(y), out_stride, rows,
-                                  vpr, n);
+                                  vpr, n, pf);
       };
       if (cv <= 2)      go(silu_mul_row_kernel<T, 2>);
       else if (cv <= 3) go(silu_mul_row_kernel<T, 3>);
@@ -144,14 +147,14 @@ int launch_silu(const void* gu, int64_t in_stride, void* y, int64_t out_stride, 
     }
     const unsigned gy = (unsigned)(rows < 65535 ? rows : 65535);
     silu_mul_vec_kernel<T, 1><<<dim3(gx, gy), bx, 0, s>>>(static_cast<const T*>(gu), in_stride,
-                                                          static_cast<T*>(y), out_stride, rows, vpr, n);
+                                                          static_cast<T*>(y), out_stride, rows, vpr, n, pf);
     return launch_status();
   }
   const int64_t gx64 = (n + 255) / 256;
   if (gx64 > 0x7fffffff) return KANI_ERR_UNSUPPORTED;
   const unsigned gy = (unsigned)(rows < 65535 ? rows : 65535);
   silu_mul_generic_kernel<T><<<dim3((unsigned)gx64, gy), 256, 0, s>>>(
-      static_cast<const T*>(gu), in_stride, static_cast<T*>(y), out_stride, rows, n);
+      static_cast<const T*>(gu), in_stride, static_cast<T*>(y), out_stride, rows, n, pf);
   return launch_status();
 }
 
@@ -160,12 +163,13 @@ int launch_silu(const void* gu, int64_t in_stride, void* y, int64_t out_stride, 
 
 extern "C" int kani_silu_mul(int32_t dtype, const void* gate_up, int64_t in_row_stride, void* y,
                              int64_t out_row_stride, int64_t rows, int64_t n, void* stream) {
+  const kani::L2Prefetch pf = kani::take_l2_prefetch();
   if (rows < 0 || n < 0) return KANI_ERR_INVALID_ARG;
   if (rows == 0 || n == 0) return KANI_OK;
   if (gate_up == nullptr || y == nullptr) return KANI_ERR_INVALID_ARG;
   if (rows > 1 && (in_row_stride < 2 * n || out_row_stride < n)) return KANI_ERR_INVALID_ARG;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return kani::dispatch_dtype(dtype, [&]<typename T>() {
-    return kani::launch_silu<T>(gate_up, in_row_stride, y, out_row_stride, rows, n, s);
+    return kani::launch_silu<T>(gate_up, in_row_stride, y, out_row_stride, rows, n, pf, s);
   });
 }

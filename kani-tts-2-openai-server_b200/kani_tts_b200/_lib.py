@@ -142,8 +142,9 @@ def set_wait_limit(cycles: int) -> None:
 
 def set_l2_prefetch(ranges) -> None:
     """Name up to two device ranges ((address, bytes) pairs, 16-byte aligned)
-    that the next decode GEMV / head launch from this thread prefetches into L2
-    as it starts; ``None`` or ``()`` clears the hint."""
+    that the next decode GEMV / head / reduce + add + RMSNorm / SiLU·mul launch
+    from this thread prefetches into L2 as it starts; ``None`` or ``()`` clears
+    the hint."""
     r = list(ranges or ())
     if len(r) > 2:
         raise ValueError("at most two L2 prefetch ranges per launch")

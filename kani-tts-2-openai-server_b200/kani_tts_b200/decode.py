@@ -188,6 +188,12 @@ class FusedDecoder:
     # its own: the weight stream keeps DRAM busy through the launch boundaries,
     # the attention launch and each GEMV's tail.  0 turns the prefetch off.
     l2_prefetch_ahead = 32 << 20
+    # The same prefetch ahead of the cuBLAS GEMMs above 32 streams, from the add +
+    # RMSNorm and SiLU·mul launches before them.  Off: at 64 streams (600 greedy
+    # tokens) it measured 613-624 us per step at 0-24 MB ahead against 613-615
+    # without, and 633-659 at 32-64 MB, where the K/V stream of attention
+    # (about 115 MB per layer) evicts the lines before their GEMM reads them.
+    l2_prefetch_large = False
 
     def _l2_prefetch_plan(self) -> list:
         """Per weight-reading launch of the fused-GEMV step (in step order, the head
@@ -362,13 +368,17 @@ class FusedDecoder:
         that the add + RMSNorm launch sums (``reduce_add_rms_norm``)."""
         b, hq, hk, d = self.batch, self.hq, self.hk, self.d
         hidden = F.embedding(input_ids, self.embed)              # [B, 1, H] residual stream
+        # the launch before each GEMM prefetches the weights ahead of it into L2
+        # (the plan's entry of that GEMM); launches without the hint skip theirs
+        plan = self._l2_prefetch_plan() if self.l2_prefetch_large else [None] * len(self.weight_spans)
+        gi = 0
 
         def proj(x, w, splits):
             return linear_split_k(x, w, splits) if splits > 1 else F.linear(x, w)
 
-        def add_norm(delta, hidden, w):
+        def add_norm(delta, hidden, w, pf=None):
             if delta.dtype == torch.float32 and delta.dim() == 3 and self.dtype != torch.float32:
-                return reduce_add_rms_norm(delta, hidden, w, self.eps)      # K-split partials
+                return reduce_add_rms_norm(delta, hidden, w, self.eps, l2_prefetch=pf)   # K-split partials
             return fused_add_rms_norm(delta, hidden, w, self.eps)
 
         delta = None
@@ -376,7 +386,8 @@ class FusedDecoder:
             if delta is None:
                 normed = fused_rms_norm(hidden, L["op_norm"], self.eps)
             else:
-                normed, hidden = add_norm(delta, hidden, L["op_norm"])
+                normed, hidden = add_norm(delta, hidden, L["op_norm"], plan[gi])
+            gi += 1
             if L["attn"]:
                 qkv = F.linear(normed, L["qkv"])                  # [B, 1, (Hq+2Hk)D]
                 q, k, v = qkv.split([self.q_dim, self.kv_dim, self.kv_dim], dim=-1)
@@ -391,9 +402,12 @@ class FusedDecoder:
             else:
                 y = short_conv_step(F.linear(normed, L["in_proj"]), self.conv_state[i], L["conv_w"])
                 delta = proj(y, L["out_proj"], self.split_k_out)
-            normed, hidden = add_norm(delta, hidden, L["ffn_norm"])
-            delta = proj(fused_silu_mul(F.linear(normed, L["gate_up"])), L["down"], self.split_k_down)
-        normed, _ = add_norm(delta, hidden, self.final_norm)
+            gi += 1
+            normed, hidden = add_norm(delta, hidden, L["ffn_norm"], plan[gi])
+            act = fused_silu_mul(F.linear(normed, L["gate_up"]), l2_prefetch=plan[gi + 1])
+            delta = proj(act, L["down"], self.split_k_down)
+            gi += 2
+        normed, _ = add_norm(delta, hidden, self.final_norm, plan[gi])
         return normed
 
     def _final_hidden_tc(self, input_ids, positions, slots, kv_len) -> torch.Tensor:

@@ -169,8 +169,8 @@ def linear_split_k(x: torch.Tensor, weight: torch.Tensor, splits: int) -> torch.
 
 
 def reduce_add_rms_norm(partials: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6,
-                        out: torch.Tensor | None = None,
-                        residual_out: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+                        out: torch.Tensor | None = None, residual_out: torch.Tensor | None = None,
+                        l2_prefetch=None) -> tuple[torch.Tensor, torch.Tensor]:
     """``fused_add_rms_norm(round(partials.sum(0)), residual, weight)`` in one launch
     (``kani_reduce_add_rms_norm``): the fp32 partials of ``linear_split_k`` are summed
     in split order and rounded as F.linear rounds its output, then the residual add
@@ -180,7 +180,8 @@ def reduce_add_rms_norm(partials: torch.Tensor, residual: torch.Tensor, weight: 
         partials: fp32 [S, rows, N] (the splits and rows may carry strides).
         residual: [..., N] with rows rows (bf16 / fp16 / fp32).
     Returns ``(normed, h)`` shaped like ``residual``; ``out`` / ``residual_out`` as
-    in ``fused_add_rms_norm``.
+    in ``fused_add_rms_norm``; ``l2_prefetch`` as in ``gemv`` (the weights of the
+    GEMMs after this launch).
     """
     for t, w in ((partials, "partials"), (residual, "residual"), (weight, "weight")):
         require_cuda(t, w)
@@ -208,17 +209,20 @@ def reduce_add_rms_norm(partials: torch.Tensor, residual: torch.Tensor, weight: 
                                                                   device=residual.device)
     if y.data_ptr() == h.data_ptr() and y.numel() > 0:
         raise ValueError("out and residual_out must be different tensors")
+    if l2_prefetch:
+        _lib.set_l2_prefetch(l2_prefetch)
     check(lib.kani_reduce_add_rms_norm(code, wcode, ptr(partials), partials.stride(0), partials.stride(1), s_,
                                        ptr(rv), rs, ptr(weight), ptr(y), n, ptr(h), n, rows, n, float(eps),
                                        stream_ptr(residual.device)), "kani_reduce_add_rms_norm")
     return y, h
 
 
-def fused_silu_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+def fused_silu_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None, l2_prefetch=None) -> torch.Tensor:
     """SiLU(gate) * up from a concatenated [gate | up] tensor (triton_kernels.py:85-105).
 
     Args:
         gate_up: [..., 2 * intermediate_size].
+        l2_prefetch: as in ``gemv`` (the weights of the GEMMs after this launch).
     Returns:
         [..., intermediate_size] of gate_up's dtype.
     """
@@ -237,6 +241,8 @@ def fused_silu_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None) -> to
         require_cuda(out, "out")
         if tuple(out.shape) != shape or out.dtype != gate_up.dtype or not out.is_contiguous():
             raise ValueError(f"out must be a contiguous {gate_up.dtype} tensor of shape {shape}")
+    if l2_prefetch:
+        _lib.set_l2_prefetch(l2_prefetch)
     check(lib.kani_silu_mul(code, ptr(gv), gs, ptr(out), n, rows, n, stream_ptr(gate_up.device)),
           "kani_silu_mul")
     return out

@@ -211,6 +211,27 @@ def test_reduce_add_rms_norm_vs_oracle(dtype, splits, rows, n):
     assert torch.equal(rg.cpu(), ho) and torch.equal(y2.cpu(), y.cpu())
 
 
+def test_l2_prefetch_hint_on_norm_and_silu_changes_nothing():
+    """reduce_add_rms_norm and fused_silu_mul with an L2 prefetch hint (a 20 MB
+    weight buffer split over the launch's CTAs, in two ranges) give the same bytes
+    as without one, and the hint is consumed by the call it was given to."""
+    wbuf = torch.zeros(10 << 20, dtype=torch.bfloat16, device=DEV)
+    half = wbuf.numel() // 2
+    ranges = [(wbuf.data_ptr(), half * 2), (wbuf.data_ptr() + half * 2, half * 2)]
+    part = gpu(torch.randn(6, 64, 1024, generator=torch.Generator().manual_seed(5)) * 0.3)
+    r, w = gpu(rnd((64, 1024), 1330)), gpu(rnd((1024,), 1331, torch.bfloat16, 1.0, 0.02))
+    y0, h0 = K.reduce_add_rms_norm(part, r, w, 1e-5)
+    y1, h1 = K.reduce_add_rms_norm(part, r, w, 1e-5, l2_prefetch=ranges)
+    assert torch.equal(y0, y1) and torch.equal(h0, h1)
+    for t in (1, 64, 4096):
+        gu = gpu(rnd((t, 2 * 4608), 1332 + t))
+        a0 = K.fused_silu_mul(gu)
+        a1 = K.fused_silu_mul(gu, l2_prefetch=ranges)
+        assert torch.equal(a0, a1)
+    torch.cuda.synchronize()
+    assert _lib.read_and_clear_errors(DEV) == 0
+
+
 def test_linear_split_k_sums_to_the_product():
     x = rnd((64, 4608), 1320)
     w = rnd((1024, 4608), 1321, std=0.03)

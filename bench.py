@@ -765,7 +765,8 @@ def run_reference_decode(dev, ref, steps: int, prompt: int = 128, n_compare: int
     from kani_tts_b200.decode import DecodeEngine, FusedDecoder
     cfg, sd, ids, spk = _synthetic(dev, 0, 1, prompt)
     mine = DecodeEngine(FusedDecoder(cfg, sd, dev, batch=1, max_len=2048))
-    mine.start(ids, spk, steps + 8)
+    n_total = max(steps, n_compare) + 8   # the parity pass runs n_compare steps even for a short timing run
+    mine.start(ids, spk, n_total)
     t_eff = prompt + 1
     dyn = _t.SimpleNamespace(
         key_cache=[mine.dec.k_cache[i][:, :, :t_eff].clone() if i in mine.dec.k_cache else torch.empty(0)
@@ -789,7 +790,7 @@ def run_reference_decode(dev, ref, steps: int, prompt: int = 128, n_compare: int
                    repetition_penalty=1.2)
     R.capture(eng, dyn, t_eff)
     od = eng.optimized_decoder
-    sched = (t_eff + torch.arange(steps + 8, device=dev) // cfg.tokens_per_frame * cfg.audio_step).long()
+    sched = (t_eff + torch.arange(n_total, device=dev) // cfg.tokens_per_frame * cfg.audio_step).long()
     out = {}
 
     def body(i, next_token):

@@ -341,6 +341,24 @@ KANI_API int kani_head_argmax(int32_t dtype, const void* hidden, int64_t hidden_
                      void* stream);
 
 /*
+ * kani_head_argmax with the decode step's final residual add + RMSNorm
+ * (optimized_decode.py:283 + :286) folded in front of the head: each CTA forms
+ * h = round(x + residual) (residual may be NULL: h = x) and
+ * round((h * rsqrt(mean(h^2) + eps)) * norm_weight) in shared memory, with the
+ * arithmetic of the decode GEMVs' normed input (kani_gemv with norm_weight),
+ * then runs the head, the argmax and the map as kani_head_argmax does.  The
+ * logits are those of kani_gemv(x, residual, norm_weight, weight) bit for bit.
+ * The new residual stream is not written (the step ends here).
+ *   x, residual: [batch, hidden_size] rows; norm_weight: [hidden_size], non-NULL.
+ */
+KANI_API int kani_head_argmax_norm(int32_t dtype, const void* x, int64_t x_row_stride, const void* residual,
+                          int64_t residual_row_stride, const void* norm_weight, float eps, int64_t batch,
+                          int32_t hidden_size, const void* weight, int64_t weight_row_stride, int32_t rows,
+                          const int64_t* index_map, void* logits_out, int64_t logits_row_stride,
+                          unsigned long long* scratch, int64_t* tokens_out, int64_t tokens_out_stride,
+                          void* stream);
+
+/*
  * kani_head_argmax without the scratch argument, for callers that cannot
  * allocate device memory: a host whose allocator belongs to another framework,
  * code that may not call cudaMalloc while a stream is being captured, or a

@@ -29,6 +29,7 @@
 // weight stream of one launch overlaps the tail of the launch before it; all
 // reads of activations and all writes come after the wait.
 #include "common.cuh"
+#include "gemv_input.cuh"
 #include "rope_core.cuh"
 
 namespace kani {
@@ -60,84 +61,6 @@ struct GemvParams {
 
 constexpr int kConvL = 3;  // the LFM2 short-conv kernel length the fused epilogue serves
 
-// The B GEMV input rows into shared memory (as, [B][K]); with NORM the
-// residual add (h written to res_out by CTA 0) and the RMSNorm.  nw0 is the
-// norm-weight chunk of this thread's first row chunk (v = tid), fetched by the
-// caller before the programmatic-launch wait.  Ends with a barrier.
-template <typename T, int B, int K, bool NORM>
-__device__ __forceinline__ void stage_input(const GemvParams& p, T* as, float (*s_part)[B], int tid, int lane,
-                                            int warp, uint4 nw0) {
-  constexpr int E = 8;
-  if constexpr (!NORM) {
-    for (int v = tid; v < B * K / E; v += kGemvThreads) {
-      const int b = v / (K / E), c = v % (K / E);
-      uint4 x = make_uint4(0u, 0u, 0u, 0u);
-      if (b < p.batch) x = ld16(static_cast<const T*>(p.x) + (int64_t)b * p.x_stride + c * E);
-      reinterpret_cast<uint4*>(as)[v] = x;
-    }
-  } else {
-    float ss[B];
-#pragma unroll
-    for (int b = 0; b < B; ++b) ss[b] = 0.f;
-    for (int v = tid; v < B * K / E; v += kGemvThreads) {
-      const int b = v / (K / E), c = v % (K / E);
-      float h[E];
-#pragma unroll
-      for (int e = 0; e < E; ++e) h[e] = 0.f;
-      if (b < p.batch) {
-        unpack16<T>(ld16(static_cast<const T*>(p.x) + (int64_t)b * p.x_stride + c * E), h);
-        if (p.res) {
-          float rv[E];
-          unpack16<T>(ld16(static_cast<const T*>(p.res) + (int64_t)b * p.res_stride + c * E), rv);
-#pragma unroll
-          for (int e = 0; e < E; ++e) h[e] = round_to<T>(__fadd_rn(h[e], rv[e]));
-          if (p.res_out && blockIdx.x == 0)
-            st16(static_cast<T*>(p.res_out) + (int64_t)b * p.res_out_stride + c * E, pack16<T>(h));
-        }
-      }
-      float s = 0.f;
-#pragma unroll
-      for (int e = 0; e < E; ++e) s = fmaf(h[e], h[e], s);
-      // b is uniform over runs of K/E consecutive v, so accumulate per b
-#pragma unroll
-      for (int bb = 0; bb < B; ++bb)
-        if (bb == b) ss[bb] += s;
-      reinterpret_cast<uint4*>(as)[v] = pack16<T>(h);  // h (rounded), normalised below
-    }
-#pragma unroll
-    for (int b = 0; b < B; ++b) {
-      float s = ss[b];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-      if (lane == 0) s_part[warp][b] = s;
-    }
-    __syncthreads();
-    for (int v = tid; v < B * K / E; v += kGemvThreads) {
-      const int b = v / (K / E), c = v % (K / E);
-      float tot = 0.f;
-#pragma unroll
-      for (int w = 0; w < kGemvWarps; ++w) tot += s_part[w][b];
-      const float rr = 1.0f / sqrtf(tot / (float)K + p.eps);
-      float h[E], wf[E];
-      unpack16<T>(reinterpret_cast<const uint4*>(as)[v], h);
-      unpack16<T>(v == tid ? nw0 : ld16_ro(static_cast<const T*>(p.norm_w) + c * E), wf);
-#pragma unroll
-      for (int e = 0; e < E; ++e) h[e] = __fmul_rn(__fmul_rn(h[e], rr), wf[e]);
-      reinterpret_cast<uint4*>(as)[v] = pack16<T>(h);
-    }
-  }
-  __syncthreads();
-
-}
-
-// The norm-weight chunk stage_input's thread `tid` applies first (a weight:
-// fetched before the programmatic-launch wait, like the matrix rows).
-template <typename T, int B, int K, bool NORM>
-__device__ __forceinline__ uint4 first_norm_chunk(const GemvParams& p, int tid) {
-  if (!NORM || tid >= B * K / 8) return make_uint4(0u, 0u, 0u, 0u);
-  return ld16_ro(static_cast<const T*>(p.norm_w) + (tid % (K / 8)) * 8);
-}
-
 // EPI: 0 = store, 1 = SiLU·mul of the gate / up rows r and n + r,
 //      2 = gated short-conv step of channel r over rows r (B), n + r (C), 2n + r (x)
 template <typename T, int B, int CH, bool NORM, int EPI>
@@ -164,7 +87,8 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvParams p) {
         wv[q][c] = ld16_stream(W + (int64_t)(row + q * p.n) * p.w_stride + c * 256 + lane * E);
   };
   if (r < p.n) load_row(r);
-  const uint4 nw0 = first_norm_chunk<T, B, K, NORM>(p, tid);
+  const NormIn in{p.x, p.x_stride, p.res, p.res_stride, p.res_out, p.res_out_stride, p.norm_w, p.eps, p.batch};
+  const uint4 nw0 = first_norm_chunk<T, B, K, NORM>(in, tid);
   // EPI 2: lane b's conv weights of the warp's first channel (before the wait)
   // and stream b's conv state of it (after the wait), fetched ahead of the dot
   // products instead of after them
@@ -188,7 +112,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvParams p) {
     }
   }
 
-  stage_input<T, B, K, NORM>(p, as, s_part, tid, lane, warp, nw0);
+  stage_input<T, B, K, NORM, kGemvThreads>(in, as, s_part, tid, lane, warp, nw0);
 
   // ---- one warp per output row (SILU: per gate/up pair); row r's weights
   //      are already in flight
@@ -315,7 +239,8 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_rope_kv_kernel(GemvParams p
   for (int q = 0; q < RW; ++q)
 #pragma unroll
     for (int c = 0; c < CH; ++c) wv[q][c] = ld16_stream(W + (int64_t)(row0 + q) * p.w_stride + c * 256 + lane * E);
-  const uint4 nw0 = first_norm_chunk<T, B, K, NORM>(p, tid);
+  const NormIn in{p.x, p.x_stride, p.res, p.res_stride, p.res_out, p.res_out_stride, p.norm_w, p.eps, p.batch};
+  const uint4 nw0 = first_norm_chunk<T, B, K, NORM>(in, tid);
   // warp 0: lanes 0..3 carry the head's chunk pairs (lo, hi), the other lanes
   // help with the sin/cos
   const int jj = lane & 3;
@@ -363,7 +288,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_rope_kv_kernel(GemvParams p
       }
     }
   }
-  stage_input<T, B, K, NORM>(p, as, s_part, tid, lane, warp, nw0);
+  stage_input<T, B, K, NORM, kGemvThreads>(in, as, s_part, tid, lane, warp, nw0);
 
   float acc[RW][B];
 #pragma unroll

@@ -19,6 +19,7 @@
 #include <atomic>
 
 #include "common.cuh"
+#include "gemv_input.cuh"
 
 namespace kani {
 namespace {
@@ -41,6 +42,10 @@ struct HeadParams {
   int64_t* tokens;
   int64_t tokens_stride;
   L2Prefetch pf;  // later launches' weights, prefetched into L2 at entry
+  const void* res;     // NORM: h = round(h_in + res), normalised with norm_w (the final norm)
+  int64_t res_stride;
+  const void* norm_w;
+  float eps;
 };
 
 template <typename T>
@@ -51,12 +56,15 @@ __device__ __forceinline__ uint32_t order_key16(T v) {
   return (uint32_t)(b ^ ((b & 0x8000u) ? 0xffffu : 0x8000u));
 }
 
-// B streams (compile-time upper bound), CH = hidden / 256 chunks of 8 per lane
-template <typename T, int B, int CH>
+// B streams (compile-time upper bound), CH = hidden / 256 chunks of 8 per lane;
+// NORM: the hidden rows are the final residual add + RMSNorm of (h, res), with
+// the arithmetic of the decode GEMVs' input prologue
+template <typename T, int B, int CH, bool NORM>
 __global__ void __launch_bounds__(kHeadThreads) head_argmax_kernel(HeadParams p) {
   constexpr int E = 8;  // elements per 16-byte vector
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ unsigned long long s_best[kHeadWarps][B];
+  __shared__ float s_part[kHeadWarps][B];
   __shared__ bool s_last;
   T* hs = reinterpret_cast<T*>(smem_raw);  // [B][hidden]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -76,21 +84,18 @@ __global__ void __launch_bounds__(kHeadThreads) head_argmax_kernel(HeadParams p)
     }
   };
   if (gw * kHeadRows < p.rows) load_rows(gw * kHeadRows);
+  const NormIn in{p.h, p.h_stride, p.res, p.res_stride, nullptr, 0, p.norm_w, p.eps, p.batch};
+  const uint4 nw0 = first_norm_chunk<T, B, CH * 256, NORM>(in, tid);
   l2_prefetch_share(p.pf);
   griddep_wait();
 
-  // The hidden rows are written by the launch before, which may still be
-  // running while this grid is resident, so they are read with coherent loads
-  // after the wait: the read-only (.nc) path is only valid for data that stays
-  // unwritten for the whole life of the kernel, and a stale line from an
-  // earlier read of the same address (a graph replay reuses it) could be served.
-  for (int v = tid; v < B * H / E; v += kHeadThreads) {
-    const int b = v / (H / E), c = v % (H / E);
-    uint4 x = make_uint4(0u, 0u, 0u, 0u);
-    if (b < p.batch) x = ld16(static_cast<const T*>(p.h) + (int64_t)b * p.h_stride + c * E);
-    reinterpret_cast<uint4*>(hs)[v] = x;
-  }
-  __syncthreads();
+  // The hidden rows (or the update and residual of the final norm) are written
+  // by the launch before, which may still be running while this grid is
+  // resident, so they are read with coherent loads after the wait: the
+  // read-only (.nc) path is only valid for data that stays unwritten for the
+  // whole life of the kernel, and a stale line from an earlier read of the
+  // same address (a graph replay reuses it) could be served.
+  stage_input<T, B, CH * 256, NORM, kHeadThreads>(in, hs, s_part, tid, lane, warp, nw0);
 
   unsigned long long best[B];
 #pragma unroll
@@ -197,10 +202,11 @@ int launch_head_b(const HeadParams& prm, cudaStream_t s) {
     note_launch();
     return e == cudaSuccess ? KANI_OK : (int)e;
   };
+  const bool norm = prm.norm_w != nullptr;
   switch (ch) {
-    case 2: return go(head_argmax_kernel<T, B, 2>);
-    case 4: return go(head_argmax_kernel<T, B, 4>);
-    case 8: return go(head_argmax_kernel<T, B, 8>);
+    case 2: return norm ? go(head_argmax_kernel<T, B, 2, true>) : go(head_argmax_kernel<T, B, 2, false>);
+    case 4: return norm ? go(head_argmax_kernel<T, B, 4, true>) : go(head_argmax_kernel<T, B, 4, false>);
+    case 8: return norm ? go(head_argmax_kernel<T, B, 8, true>) : go(head_argmax_kernel<T, B, 8, false>);
     default: return KANI_ERR_UNSUPPORTED;
   }
 }
@@ -216,28 +222,60 @@ int launch_head(const HeadParams& prm, cudaStream_t s) {
 }  // namespace
 }  // namespace kani
 
+namespace {
+int head_argmax_impl(int32_t dtype, const void* hidden, int64_t hidden_row_stride, const void* residual,
+                     int64_t residual_row_stride, const void* norm_weight, float eps, int64_t batch,
+                     int32_t hidden_size, const void* weight, int64_t weight_row_stride, int32_t rows,
+                     const int64_t* index_map, void* logits_out, int64_t logits_row_stride,
+                     unsigned long long* scratch, int64_t* tokens_out, int64_t tokens_out_stride, void* stream) {
+  const kani::L2Prefetch pf = kani::take_l2_prefetch();
+  if (batch < 0 || rows < 0 || hidden_size < 0) return KANI_ERR_INVALID_ARG;
+  if (batch == 0) return KANI_OK;
+  if (rows == 0 || !hidden || !weight || !scratch || !tokens_out) return KANI_ERR_INVALID_ARG;
+  if (residual && !norm_weight) return KANI_ERR_INVALID_ARG;  // the add belongs to the norm
+  if (batch > kani::kHeadMaxB) return KANI_ERR_UNSUPPORTED;
+  if (dtype != KANI_DTYPE_BF16 && dtype != KANI_DTYPE_F16) return dtype == KANI_DTYPE_F32 ? KANI_ERR_UNSUPPORTED
+                                                                                          : KANI_ERR_DTYPE;
+  if (hidden_size % 256 != 0 || weight_row_stride < hidden_size || (batch > 1 && hidden_row_stride < hidden_size) ||
+      (residual && batch > 1 && residual_row_stride < hidden_size))
+    return KANI_ERR_INVALID_ARG;
+  if (logits_out && batch > 1 && logits_row_stride < rows) return KANI_ERR_INVALID_ARG;
+  if (!kani::aligned16(hidden) || !kani::aligned16(weight) || hidden_row_stride % 8 != 0 || weight_row_stride % 8 != 0 ||
+      (residual && (!kani::aligned16(residual) || residual_row_stride % 8 != 0)) ||
+      (norm_weight && !kani::aligned16(norm_weight)))
+    return KANI_ERR_UNSUPPORTED;
+  kani::HeadParams prm{hidden, hidden_row_stride, weight, weight_row_stride, rows, hidden_size, (int)batch,
+                       index_map, logits_out, logits_row_stride, scratch, tokens_out, tokens_out_stride, pf,
+                       residual, residual_row_stride, norm_weight, eps};
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == KANI_DTYPE_BF16) return kani::launch_head<__nv_bfloat16>(prm, s);
+  return kani::launch_head<__half>(prm, s);
+}
+}  // namespace
+
 extern "C" int kani_head_argmax(int32_t dtype, const void* hidden, int64_t hidden_row_stride, int64_t batch,
                                 int32_t hidden_size, const void* weight, int64_t weight_row_stride, int32_t rows,
                                 const int64_t* index_map, void* logits_out, int64_t logits_row_stride,
                                 unsigned long long* scratch, int64_t* tokens_out, int64_t tokens_out_stride,
                                 void* stream) {
-  const kani::L2Prefetch pf = kani::take_l2_prefetch();
-  if (batch < 0 || rows < 0 || hidden_size < 0) return KANI_ERR_INVALID_ARG;
-  if (batch == 0) return KANI_OK;
-  if (rows == 0 || !hidden || !weight || !scratch || !tokens_out) return KANI_ERR_INVALID_ARG;
-  if (batch > kani::kHeadMaxB) return KANI_ERR_UNSUPPORTED;
-  if (dtype != KANI_DTYPE_BF16 && dtype != KANI_DTYPE_F16) return dtype == KANI_DTYPE_F32 ? KANI_ERR_UNSUPPORTED
-                                                                                          : KANI_ERR_DTYPE;
-  if (hidden_size % 256 != 0 || weight_row_stride < hidden_size || (batch > 1 && hidden_row_stride < hidden_size))
+  return head_argmax_impl(dtype, hidden, hidden_row_stride, nullptr, 0, nullptr, 0.f, batch, hidden_size, weight,
+                          weight_row_stride, rows, index_map, logits_out, logits_row_stride, scratch, tokens_out,
+                          tokens_out_stride, stream);
+}
+
+extern "C" int kani_head_argmax_norm(int32_t dtype, const void* x, int64_t x_row_stride, const void* residual,
+                                     int64_t residual_row_stride, const void* norm_weight, float eps, int64_t batch,
+                                     int32_t hidden_size, const void* weight, int64_t weight_row_stride,
+                                     int32_t rows, const int64_t* index_map, void* logits_out,
+                                     int64_t logits_row_stride, unsigned long long* scratch, int64_t* tokens_out,
+                                     int64_t tokens_out_stride, void* stream) {
+  if (!norm_weight) {
+    kani::take_l2_prefetch();
     return KANI_ERR_INVALID_ARG;
-  if (logits_out && batch > 1 && logits_row_stride < rows) return KANI_ERR_INVALID_ARG;
-  if (!kani::aligned16(hidden) || !kani::aligned16(weight) || hidden_row_stride % 8 != 0 || weight_row_stride % 8 != 0)
-    return KANI_ERR_UNSUPPORTED;
-  kani::HeadParams prm{hidden, hidden_row_stride, weight, weight_row_stride, rows, hidden_size, (int)batch,
-                       index_map, logits_out, logits_row_stride, scratch, tokens_out, tokens_out_stride, pf};
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (dtype == KANI_DTYPE_BF16) return kani::launch_head<__nv_bfloat16>(prm, s);
-  return kani::launch_head<__half>(prm, s);
+  }
+  return head_argmax_impl(dtype, x, x_row_stride, residual, residual_row_stride, norm_weight, eps, batch,
+                          hidden_size, weight, weight_row_stride, rows, index_map, logits_out, logits_row_stride,
+                          scratch, tokens_out, tokens_out_stride, stream);
 }
 
 // ------------------------------------------------ entry point without a scratch

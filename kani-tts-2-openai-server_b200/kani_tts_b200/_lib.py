@@ -75,6 +75,8 @@ _SIGNATURES = {
                             _c_p, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_p], ctypes.c_int),
     "kani_head_argmax": ([_c_i32, _c_p, _c_i64, _c_i64, _c_i32, _c_p, _c_i64, _c_i32,
                           _c_p, _c_p, _c_i64, _c_p, _c_p, _c_i64, _c_p], ctypes.c_int),
+    "kani_head_argmax_norm": ([_c_i32, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_f32, _c_i64, _c_i32, _c_p, _c_i64,
+                               _c_i32, _c_p, _c_p, _c_i64, _c_p, _c_p, _c_i64, _c_p], ctypes.c_int),
     "kani_head_argmax_noalloc": ([_c_i32, _c_p, _c_i64, _c_i64, _c_i32, _c_p, _c_i64, _c_i32,
                                   _c_p, _c_p, _c_i64, _c_p, _c_i64, _c_p], ctypes.c_int),
     "kani_head_argmax_tc": ([_c_i32, _c_p, _c_i64, _c_i64, _c_i32, _c_p, _c_i64, _c_i32,

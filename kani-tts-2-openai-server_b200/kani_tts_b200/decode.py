@@ -183,11 +183,15 @@ class FusedDecoder:
         self.weight_spans.append((off * es, (off + n) * es))
         self._l2_plan = None
 
-    # Each decode GEMV (and the fused head) prefetches into L2, as it starts, the
-    # weights of the launches after it, up to this many bytes past the end of
-    # its own: the weight stream keeps DRAM busy through the launch boundaries,
-    # the attention launch and each GEMV's tail.  0 turns the prefetch off.
-    l2_prefetch_ahead = 32 << 20
+    # Each decode GEMV (and the fused head) can prefetch into L2, as it starts,
+    # the weights of the launches after it, up to this many bytes past the end
+    # of its own; 0 turns the prefetch off.  Off by default: it took the bs = 1
+    # step from 274-276 to 266 us when the GEMVs still fetched part of their
+    # weights after the launch wait, and measures within noise at one stream
+    # (236.8-237.7 us off, 236.0-237.9 at 16-64 MB ahead) and slower at two and
+    # four streams (301.4-301.9 against 306.1-308.2 us, 525.7-526.4 against
+    # 527.6-534.7) now that every weight a GEMV needs is requested before its wait.
+    l2_prefetch_ahead = 0
     # The same prefetch ahead of the cuBLAS GEMMs above 32 streams, from the add +
     # RMSNorm and SiLU·mul launches before them.  Off: at 64 streams (600 greedy
     # tokens) it measured 613-624 us per step at 0-24 MB ahead against 613-615
@@ -266,12 +270,27 @@ class FusedDecoder:
         """Reduced-head logits by F.linear on the padded head: [..., num_reduced] view."""
         return F.linear(normed, self.head_padded)[..., :self.num_reduced]
 
+    # Up to 4 streams the final residual add + RMSNorm runs inside the head
+    # launch (kani_head_argmax_norm) instead of a launch of its own: measured
+    # 6.5 us of the bs = 1 step for that launch.
+    fuse_final_norm = True
+
+    def _head_input(self, input_ids, positions, slots, kv_len):
+        """The decode layers, ending either in the final-normed hidden state or, where
+        the fused head takes the final norm, in (update, residual stream)."""
+        if self.small_batch and self.fused_head == "gemv" and self.fuse_final_norm:
+            return self._final_hidden_small(input_ids, positions, slots, kv_len, fuse_final=True)
+        return self._final_hidden(input_ids, positions, slots, kv_len)
+
     def _fused_head(self, normed, index_map=None, logits_out=None, out=None) -> torch.Tensor:
         fn = head_argmax if self.fused_head == "gemv" else head_argmax_tc
         if self.fused_head == "tc":
             kw = {"err_flag": self.err_flag}
         else:
             kw = {"l2_prefetch": self._l2_prefetch_plan()[-1]} if self.small_batch else {}
+            if isinstance(normed, tuple):        # (update, residual stream): the final norm in the head
+                normed, residual = normed
+                kw.update(norm_weight=self.final_norm, residual=residual, eps=self.eps)
         return fn(normed, self.head, index_map, scratch=self.head_scratch, logits_out=logits_out, out=out, **kw)
 
     def step_logits(self, input_ids: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor,
@@ -281,7 +300,7 @@ class FusedDecoder:
         reduced-head logits [B, 1, num_reduced] in a static buffer."""
         if self.fused_head is None:
             return self.step(input_ids, positions, slots, kv_len)
-        normed = self._final_hidden(input_ids, positions, slots, kv_len)
+        normed = self._head_input(input_ids, positions, slots, kv_len)
         self._fused_head(normed, logits_out=self.logits_buf.view(self.batch, -1), out=self.argmax_buf)
         return self.logits_buf
 
@@ -294,7 +313,7 @@ class FusedDecoder:
         if self.fused_head is None:
             raise ValueError("the fused greedy head serves at most 64 streams (hidden size at most 1024, "
                              "or 2048 up to 8 streams)")
-        normed = self._final_hidden(input_ids, positions, slots, kv_len)
+        normed = self._head_input(input_ids, positions, slots, kv_len)
         return self._fused_head(normed, self.reduced_to_full, out=out)
 
     def _final_hidden(self, input_ids, positions, slots, kv_len) -> torch.Tensor:
@@ -305,14 +324,16 @@ class FusedDecoder:
             return self._final_hidden_tc(input_ids, positions, slots, kv_len)
         return self._final_hidden_large(input_ids, positions, slots, kv_len)
 
-    def _final_hidden_small(self, input_ids, positions, slots, kv_len) -> torch.Tensor:
+    def _final_hidden_small(self, input_ids, positions, slots, kv_len, fuse_final: bool = False):
         """Up to 8 streams: every F.linear is a ``gemv`` launch that also applies the
         residual add + RMSNorm before it and, for gate/up, the SiLU·mul after it,
         the in_proj GEMV also runs the short-conv step and the QKV GEMV the
         q/k norm + RoPE + KV write, so a layer is 4 launches (conv) or 5
         (attention) instead of 8-9.  The
         residual stream alternates between two static buffers (a launch reads one
-        and writes the other)."""
+        and writes the other).  With ``fuse_final`` the last update and residual
+        stream are returned as they are, for the head launch that applies the
+        final add + RMSNorm itself."""
         b, hq, hk, d = self.batch, self.hq, self.hk, self.d
         hidden = F.embedding(input_ids, self.embed)              # [B, 1, H] residual stream
         delta = None
@@ -347,6 +368,8 @@ class FusedDecoder:
                 delta = gemv(y, L["out_proj"], l2_prefetch=next(pf))
             act = normed(gemv, L["gate_up"], norm_weight=L["ffn_norm"], silu_pairs=True, l2_prefetch=next(pf))
             delta = gemv(act, L["down"], l2_prefetch=next(pf))
+        if fuse_final:
+            return delta, hidden   # the fused head applies the final add + RMSNorm
         normed, _ = fused_add_rms_norm(delta, hidden, self.final_norm, self.eps)
         return normed
 

@@ -824,7 +824,8 @@ def gemv_rope_kv_write(x: torch.Tensor, qkv_weight: torch.Tensor, norm_weight: t
 
 def head_argmax(hidden: torch.Tensor, weight: torch.Tensor, index_map: torch.Tensor | None = None, *,
                 scratch: torch.Tensor | None = None, logits_out: torch.Tensor | None = None,
-                out: torch.Tensor | None = None, l2_prefetch=None) -> torch.Tensor:
+                out: torch.Tensor | None = None, l2_prefetch=None, norm_weight: torch.Tensor | None = None,
+                residual: torch.Tensor | None = None, eps: float = 1e-5) -> torch.Tensor:
     """Greedy next token from the reduced LM head (optimized_decode.py:287 and the
     reduced-to-full map of :144-148) for up to 8 streams in one launch.
 
@@ -837,6 +838,11 @@ def head_argmax(hidden: torch.Tensor, weight: torch.Tensor, index_map: torch.Ten
         logits_out: optional [B, rows] tensor that receives the logits.
         out: optional [B] int64 tensor for the token ids.
         l2_prefetch: as in ``gemv``.
+        norm_weight: with it, ``hidden`` is the residual-stream update and the
+            launch first forms the final residual add + RMSNorm
+            (``kani_head_argmax_norm``; optimized_decode.py:283, :286) with
+            ``residual`` (None: RMSNorm of ``hidden`` alone) and ``eps``, with the
+            arithmetic of ``gemv``'s normed input.
     Returns:
         [B] int64 token ids.
     """
@@ -873,12 +879,30 @@ def head_argmax(hidden: torch.Tensor, weight: torch.Tensor, index_map: torch.Ten
         out = torch.empty(b, dtype=torch.int64, device=dev)
     if out.dtype != torch.int64 or out.numel() != b:
         raise ValueError(f"out must hold {b} int64 token ids")
+    rv, rs = None, 0
+    if norm_weight is not None:
+        require_cuda(norm_weight, "norm_weight")
+        if norm_weight.numel() != h or norm_weight.dtype != hidden.dtype:
+            raise ValueError(f"norm_weight must be [{h}] of the hidden dtype")
+        norm_weight = norm_weight.contiguous()
+        if residual is not None:
+            require_cuda(residual, "residual")
+            rv, rb, rs = _rows_view(residual, h)
+            if rb != b or residual.dtype != hidden.dtype:
+                raise ValueError("residual must have the hidden rows and dtype")
+    elif residual is not None:
+        raise ValueError("residual needs norm_weight (the add belongs to the final norm)")
     if l2_prefetch:
         _lib.set_l2_prefetch(l2_prefetch)
-    check(lib.kani_head_argmax(code, ptr(hv), hs, b, h, ptr(weight), weight.stride(0), rows,
-                               ptr(index_map) if index_map is not None else None,
-                               ptr(logits_out) if logits_out is not None else None, ls, ptr(scratch),
-                               ptr(out), out.stride(0) if b > 1 else 1, stream_ptr(dev)), "kani_head_argmax")
+    tail = (rows, ptr(index_map) if index_map is not None else None,
+            ptr(logits_out) if logits_out is not None else None, ls, ptr(scratch),
+            ptr(out), out.stride(0) if b > 1 else 1, stream_ptr(dev))
+    if norm_weight is None:
+        check(lib.kani_head_argmax(code, ptr(hv), hs, b, h, ptr(weight), weight.stride(0), *tail), "kani_head_argmax")
+    else:
+        check(lib.kani_head_argmax_norm(code, ptr(hv), hs, ptr(rv) if rv is not None else None, rs, ptr(norm_weight),
+                                        float(eps), b, h, ptr(weight), weight.stride(0), *tail),
+              "kani_head_argmax_norm")
     return out
 
 

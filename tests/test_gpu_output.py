@@ -58,6 +58,32 @@ def test_head_argmax_vs_oracle(dtype, b, h, rows):
     check_head(hidden, weight, imap, tok, logits)
 
 
+@pytest.mark.parametrize("b,res", [(1, True), (3, True), (4, False), (8, True)])
+def test_head_argmax_norm_equals_the_normed_gemv(b, res):
+    """kani_head_argmax_norm (the final residual add + RMSNorm folded into the
+    head): its logits are kani_gemv's with the same norm weight and residual, bit
+    for bit (one input prologue, one accumulation order), its token the first
+    maximum of them, mapped; and the scratch is left zero."""
+    h, rows = 1024, 15591
+    x = rnd((b, 1, h), 1340 + b)
+    r = rnd((b, 1, h), 1341 + b) if res else None
+    nw = (1.0 + 0.1 * rnd((h,), 1342, torch.float32)).to(torch.bfloat16)
+    w = rnd((rows, h), 1343, std=0.05).to(DEV)
+    imap = (torch.arange(rows, dtype=torch.long) * 5 + 3).to(DEV)
+    logits = torch.empty(b, rows, dtype=torch.bfloat16, device=DEV)
+    scratch = torch.zeros(b + 1, dtype=torch.int64, device=DEV)
+    tok = K.head_argmax(x.to(DEV), w, imap, scratch=scratch, logits_out=logits, norm_weight=nw.to(DEV),
+                        residual=r.to(DEV) if r is not None else None, eps=1e-5)
+    want = K.gemv(x.to(DEV), w, norm_weight=nw.to(DEV), residual=r.to(DEV) if r is not None else None,
+                  residual_out=torch.empty(b, 1, h, dtype=torch.bfloat16, device=DEV) if r is not None else None,
+                  eps=1e-5).reshape(b, rows)
+    assert torch.equal(logits, want)
+    assert torch.equal(tok, imap[torch.argmax(want.float(), dim=-1)])
+    assert int(scratch.abs().sum()) == 0
+    with pytest.raises(ValueError):
+        K.head_argmax(x.to(DEV), w, residual=x.to(DEV))            # an add without the norm
+
+
 def test_head_argmax_scratch_is_left_clean_and_reused():
     """Two calls on one scratch buffer (the second sees what the first left) and a
     graph replayed with new hidden states; the scratch is all zero afterwards."""

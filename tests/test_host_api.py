@@ -163,6 +163,9 @@ def test_abi_rejects_bad_arguments_without_launching():
     assert sample(tok=n) == -1
     assert sample(rs=100) == -1
     assert sample(dtype=5) == -2
+    # the head with the final norm: no norm weight, or a residual the norm does not cover
+    assert lib.kani_head_argmax_norm(1, fake, 1024, fake, 1024, n, 1e-5, 1, 1024, fake, 1024, 100, n, n, 0, fake,
+                                     fake, 1, n) == -1
     # reduced head: batch above 8, fp32, hidden size not a multiple of 256, missing scratch
     assert lib.kani_head_argmax(1, fake, 1024, 9, 1024, fake, 1024, 100, n, n, 0, fake, fake, 1, n) == -3
     assert lib.kani_head_argmax(0, fake, 1024, 1, 1024, fake, 1024, 100, n, n, 0, fake, fake, 1, n) == -3

@@ -19,11 +19,12 @@
 // fp32 (base-2 exponentials, the query pre-scaled by scale * log2 e).  The
 // partials are merged across key groups by shuffles, across the CTA's warps
 // through shared memory, and across the cluster through distributed shared
-// memory by CTA rank 0, which writes the normalised output with one
-// rounding.  No global scratch is used; the two cluster barriers are
-// hardware barriers that every CTA of the cluster reaches.  With contiguous
-// cache rows the K/V range is staged by TMA (decode_attn_kernel below);
-// otherwise the register variant reads it directly.
+// memory in CTA rank 0, which writes the normalised output with one
+// rounding.  No global scratch is used; the cluster barriers are hardware
+// barriers that every CTA of the cluster reaches.  With contiguous cache rows
+// the K/V range is staged by TMA (decode_attn_kernel below: each CTA pushes
+// its partial into rank 0, one split barrier); otherwise the register
+// variant reads it directly (rank 0 pulls the partials between two barriers).
 #include <atomic>
 
 #include <cooperative_groups.h>

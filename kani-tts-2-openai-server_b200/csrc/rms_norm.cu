@@ -48,6 +48,7 @@ template <typename T, typename W, int V, bool RES>
 __global__ void __launch_bounds__(128)
 norm_group_kernel(NormParams p, int log2g) {
   griddep_launch_dependents();  // a dependent GEMV may start streaming its weights
+  griddep_wait();               // launched as a programmatic dependent: the inputs come from the launch before
   constexpr int E = VecN<T>::value;
   const int G = 1 << log2g;
   const int64_t gtid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -131,6 +132,7 @@ template <typename T, typename W, int V, bool RES, int BT>
 __global__ void __launch_bounds__(BT)
 norm_block_kernel(NormParams p) {
   griddep_launch_dependents();  // a dependent GEMV may start streaming its weights
+  griddep_wait();               // launched as a programmatic dependent: the inputs come from the launch before
   constexpr int E = VecN<T>::value;
   __shared__ float red[33];
   const int nvec = p.n / E;
@@ -187,6 +189,7 @@ template <typename T, typename W, bool RES>
 __global__ void __launch_bounds__(256)
 norm_generic_kernel(NormParams p) {
   griddep_launch_dependents();  // a dependent GEMV may start streaming its weights
+  griddep_wait();               // launched as a programmatic dependent: the inputs come from the launch before
   __shared__ float red[33];
   for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
     const T* xr = static_cast<const T*>(p.x) + row * p.xs;
@@ -236,21 +239,21 @@ int launch_norm(const NormParams& p, cudaStream_t s) {
     const int rows_per_block = bt / G;
     const int64_t grid = (p.rows + rows_per_block - 1) / rows_per_block;
     if (grid > 0x7fffffff) return KANI_ERR_UNSUPPORTED;
-    if (per <= 1)      norm_group_kernel<T, W, 1, RES><<<(unsigned)grid, bt, 0, s>>>(p, log2g);
-    else if (per <= 2) norm_group_kernel<T, W, 2, RES><<<(unsigned)grid, bt, 0, s>>>(p, log2g);
-    else if (per <= 4) norm_group_kernel<T, W, 4, RES><<<(unsigned)grid, bt, 0, s>>>(p, log2g);
-    else               norm_group_kernel<T, W, 8, RES><<<(unsigned)grid, bt, 0, s>>>(p, log2g);
+    if (per <= 1)      launch_pdl(norm_group_kernel<T, W, 1, RES>, dim3((unsigned)grid), dim3(bt), 0, s, p, log2g);
+    else if (per <= 2) launch_pdl(norm_group_kernel<T, W, 2, RES>, dim3((unsigned)grid), dim3(bt), 0, s, p, log2g);
+    else if (per <= 4) launch_pdl(norm_group_kernel<T, W, 4, RES>, dim3((unsigned)grid), dim3(bt), 0, s, p, log2g);
+    else               launch_pdl(norm_group_kernel<T, W, 8, RES>, dim3((unsigned)grid), dim3(bt), 0, s, p, log2g);
     return launch_status();
   }
   const unsigned grid = (unsigned)(p.rows < kMaxGrid ? p.rows : kMaxGrid);
   if (vec && nvec <= 256 * 8) {
     const int per = (nvec + 255) / 256;
-    if (per <= 2)      norm_block_kernel<T, W, 2, RES, 256><<<grid, 256, 0, s>>>(p);
-    else if (per <= 4) norm_block_kernel<T, W, 4, RES, 256><<<grid, 256, 0, s>>>(p);
-    else               norm_block_kernel<T, W, 8, RES, 256><<<grid, 256, 0, s>>>(p);
+    if (per <= 2)      launch_pdl(norm_block_kernel<T, W, 2, RES, 256>, dim3(grid), dim3(256), 0, s, p);
+    else if (per <= 4) launch_pdl(norm_block_kernel<T, W, 4, RES, 256>, dim3(grid), dim3(256), 0, s, p);
+    else               launch_pdl(norm_block_kernel<T, W, 8, RES, 256>, dim3(grid), dim3(256), 0, s, p);
     return launch_status();
   }
-  norm_generic_kernel<T, W, RES><<<grid, 256, 0, s>>>(p);
+  launch_pdl(norm_generic_kernel<T, W, RES>, dim3(grid), dim3(256), 0, s, p);
   return launch_status();
 }
 
@@ -311,6 +314,7 @@ __device__ __forceinline__ void st4(T* ptr, const float* f) {
 template <typename T, typename W, int V>
 __global__ void __launch_bounds__(kRedThreads) reduce_add_norm_kernel(RedParams p) {
   griddep_launch_dependents();  // a dependent GEMV may start streaming its weights
+  griddep_wait();               // launched as a programmatic dependent: the inputs come from the launch before
   l2_prefetch_share(p.pf);
   __shared__ float red[33];
   const int tid = threadIdx.x;
@@ -365,9 +369,9 @@ template <typename T, typename W>
 int launch_reduce_norm(const RedParams& p, cudaStream_t s) {
   const unsigned grid = (unsigned)(p.rows < kMaxGrid ? p.rows : kMaxGrid);
   const int v = (p.n + 4 * kRedThreads - 1) / (4 * kRedThreads);
-  if (v <= 1)      reduce_add_norm_kernel<T, W, 1><<<grid, kRedThreads, 0, s>>>(p);
-  else if (v <= 2) reduce_add_norm_kernel<T, W, 2><<<grid, kRedThreads, 0, s>>>(p);
-  else             reduce_add_norm_kernel<T, W, 4><<<grid, kRedThreads, 0, s>>>(p);
+  if (v <= 1)      launch_pdl(reduce_add_norm_kernel<T, W, 1>, dim3(grid), dim3(kRedThreads), 0, s, p);
+  else if (v <= 2) launch_pdl(reduce_add_norm_kernel<T, W, 2>, dim3(grid), dim3(kRedThreads), 0, s, p);
+  else             launch_pdl(reduce_add_norm_kernel<T, W, 4>, dim3(grid), dim3(kRedThreads), 0, s, p);
   return launch_status();
 }
 

@@ -216,6 +216,7 @@ rope_token_kernel(RopeParams p, int log2l) {
   // the older cache rows now; it reads q and the rows written here after this
   // grid completes
   griddep_launch_dependents();
+  griddep_wait();  // launched as a programmatic dependent: the inputs come from the launch before
   constexpr int E = VecN<T>::value;
   constexpr int NI = QI > KI ? QI : KI;
   const int L = 1 << log2l;
@@ -715,11 +716,11 @@ int launch_rope_t(const RopeParams& p, cudaStream_t s) {
       if (grid <= 0x7fffffff) {
         const dim3 blk((unsigned)(64 * tpb));
         if (p.hq <= 2 * G && p.hk <= G) {
-          rope_token_kernel<T, NORM, TABLE, 2, 1><<<(unsigned)grid, blk, 0, s>>>(p, log2l);
+          launch_pdl(rope_token_kernel<T, NORM, TABLE, 2, 1>, dim3((unsigned)grid), dim3(blk), 0, s, p, log2l);
           return launch_status();
         }
         if (p.hq <= 4 * G && p.hk <= 2 * G) {
-          rope_token_kernel<T, NORM, TABLE, 4, 2><<<(unsigned)grid, blk, 0, s>>>(p, log2l);
+          launch_pdl(rope_token_kernel<T, NORM, TABLE, 4, 2>, dim3((unsigned)grid), dim3(blk), 0, s, p, log2l);
           return launch_status();
         }
       }

@@ -28,6 +28,7 @@ short_conv_kernel(const T* __restrict__ bcx, int64_t bcx_stride, T* __restrict__
                   int64_t batch, int hidden) {
   constexpr int E = VecN<T>::value;
   griddep_launch_dependents();  // a dependent GEMV may start streaming its weights
+  griddep_wait();               // launched as a programmatic dependent: the inputs come from the launch before
   const int groups = hidden / E;
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= batch * groups) return;
@@ -102,9 +103,9 @@ int launch_conv(const void* bcx, int64_t bcx_stride, void* state, int64_t state_
   const T* wp = static_cast<const T*>(w);
   T* yp = static_cast<T*>(y);
   switch (L) {
-    case 2: short_conv_kernel<T, 2><<<(unsigned)grid, 128, 0, s>>>(bp, bcx_stride, sp, state_stride, wp, yp, y_stride, batch, hidden); break;
-    case 3: short_conv_kernel<T, 3><<<(unsigned)grid, 128, 0, s>>>(bp, bcx_stride, sp, state_stride, wp, yp, y_stride, batch, hidden); break;
-    case 4: short_conv_kernel<T, 4><<<(unsigned)grid, 128, 0, s>>>(bp, bcx_stride, sp, state_stride, wp, yp, y_stride, batch, hidden); break;
+    case 2: launch_pdl(short_conv_kernel<T, 2>, dim3((unsigned)grid), dim3(128), 0, s, bp, bcx_stride, sp, state_stride, wp, yp, y_stride, batch, hidden); break;
+    case 3: launch_pdl(short_conv_kernel<T, 3>, dim3((unsigned)grid), dim3(128), 0, s, bp, bcx_stride, sp, state_stride, wp, yp, y_stride, batch, hidden); break;
+    case 4: launch_pdl(short_conv_kernel<T, 4>, dim3((unsigned)grid), dim3(128), 0, s, bp, bcx_stride, sp, state_stride, wp, yp, y_stride, batch, hidden); break;
     default: return KANI_ERR_UNSUPPORTED;
   }
   return launch_status();

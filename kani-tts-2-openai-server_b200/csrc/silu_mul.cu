@@ -25,6 +25,7 @@ silu_mul_vec_kernel(const T* __restrict__ gu, int64_t in_stride, T* __restrict__
                     int64_t out_stride, int64_t rows, int vpr, int64_t n, L2Prefetch pf) {
   constexpr int E = VecN<T>::value;
   l2_prefetch_share(pf);
+  griddep_wait();  // launched as a programmatic dependent: the input comes from the launch before
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= vpr) return;
   const int64_t col = (int64_t)c * E;
@@ -62,6 +63,7 @@ silu_mul_row_kernel(const T* __restrict__ gu, int64_t in_stride, T* __restrict__
                     int64_t rows, int vpr, int64_t n, L2Prefetch pf) {
   constexpr int E = VecN<T>::value;
   l2_prefetch_share(pf);
+  griddep_wait();  // launched as a programmatic dependent: the input comes from the launch before
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const T* base = gu + r * in_stride;
     uint4 g[CV], u[CV];
@@ -94,6 +96,7 @@ __global__ void __launch_bounds__(256)
 silu_mul_generic_kernel(const T* __restrict__ gu, int64_t in_stride, T* __restrict__ y,
                         int64_t out_stride, int64_t rows, int64_t n, L2Prefetch pf) {
   l2_prefetch_share(pf);
+  griddep_wait();  // launched as a programmatic dependent: the input comes from the launch before
   const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= n) return;
   for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {
@@ -126,8 +129,8 @@ int launch_silu(const void* gu, int64_t in_stride, void* y, int64_t out_stride, 
     if (rows >= kRowKernelMinRows && cv <= 8) {
       const unsigned grid = (unsigned)(rows < 0x7fffffff ? rows : 0x7fffffff);
       auto go = [&](auto kern) {
-        kern<<<grid, 192, 0, s>>>(static_cast<const T*>(gu), in_stride, static_cast<T*>(y), out_stride, rows,
-                                  vpr, n, pf);
+        launch_pdl(kern, dim3(grid), dim3(192), 0, s, static_cast<const T*>(gu), in_stride, static_cast<T*>(y),
+                   out_stride, rows, vpr, n, pf);
       };
       if (cv <= 2)      go(silu_mul_row_kernel<T, 2>);
       else if (cv <= 3) go(silu_mul_row_kernel<T, 3>);
@@ -146,15 +149,15 @@ int launch_silu(const void* gu, int64_t in_stride, void* y, int64_t out_stride, 
       gx = (unsigned)((vpr + bx - 1) / bx);
     }
     const unsigned gy = (unsigned)(rows < 65535 ? rows : 65535);
-    silu_mul_vec_kernel<T, 1><<<dim3(gx, gy), bx, 0, s>>>(static_cast<const T*>(gu), in_stride,
-                                                          static_cast<T*>(y), out_stride, rows, vpr, n, pf);
+    launch_pdl(silu_mul_vec_kernel<T, 1>, dim3(gx, gy), dim3(bx), 0, s, static_cast<const T*>(gu), in_stride,
+               static_cast<T*>(y), out_stride, rows, vpr, n, pf);
     return launch_status();
   }
   const int64_t gx64 = (n + 255) / 256;
   if (gx64 > 0x7fffffff) return KANI_ERR_UNSUPPORTED;
   const unsigned gy = (unsigned)(rows < 65535 ? rows : 65535);
-  silu_mul_generic_kernel<T><<<dim3((unsigned)gx64, gy), 256, 0, s>>>(
-      static_cast<const T*>(gu), in_stride, static_cast<T*>(y), out_stride, rows, n, pf);
+  launch_pdl(silu_mul_generic_kernel<T>, dim3((unsigned)gx64, gy), dim3(256), 0, s, static_cast<const T*>(gu),
+             in_stride, static_cast<T*>(y), out_stride, rows, n, pf);
   return launch_status();
 }
 

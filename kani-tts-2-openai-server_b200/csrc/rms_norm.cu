@@ -239,21 +239,21 @@ int launch_norm(const NormParams& p, cudaStream_t s) {
     const int rows_per_block = bt / G;
     const int64_t grid = (p.rows + rows_per_block - 1) / rows_per_block;
     if (grid > 0x7fffffff) return KANI_ERR_UNSUPPORTED;
-    if (per <= 1)      launch_pdl(norm_group_kernel<T, W, 1, RES>, dim3((unsigned)grid), dim3(bt), 0, s, p, log2g);
-    else if (per <= 2) launch_pdl(norm_group_kernel<T, W, 2, RES>, dim3((unsigned)grid), dim3(bt), 0, s, p, log2g);
-    else if (per <= 4) launch_pdl(norm_group_kernel<T, W, 4, RES>, dim3((unsigned)grid), dim3(bt), 0, s, p, log2g);
-    else               launch_pdl(norm_group_kernel<T, W, 8, RES>, dim3((unsigned)grid), dim3(bt), 0, s, p, log2g);
+    if (per <= 1)      launch_maybe_pdl(p.rows <= kPdlMaxRows, norm_group_kernel<T, W, 1, RES>, dim3((unsigned)grid), dim3(bt), 0, s, p, log2g);
+    else if (per <= 2) launch_maybe_pdl(p.rows <= kPdlMaxRows, norm_group_kernel<T, W, 2, RES>, dim3((unsigned)grid), dim3(bt), 0, s, p, log2g);
+    else if (per <= 4) launch_maybe_pdl(p.rows <= kPdlMaxRows, norm_group_kernel<T, W, 4, RES>, dim3((unsigned)grid), dim3(bt), 0, s, p, log2g);
+    else               launch_maybe_pdl(p.rows <= kPdlMaxRows, norm_group_kernel<T, W, 8, RES>, dim3((unsigned)grid), dim3(bt), 0, s, p, log2g);
     return launch_status();
   }
   const unsigned grid = (unsigned)(p.rows < kMaxGrid ? p.rows : kMaxGrid);
   if (vec && nvec <= 256 * 8) {
     const int per = (nvec + 255) / 256;
-    if (per <= 2)      launch_pdl(norm_block_kernel<T, W, 2, RES, 256>, dim3(grid), dim3(256), 0, s, p);
-    else if (per <= 4) launch_pdl(norm_block_kernel<T, W, 4, RES, 256>, dim3(grid), dim3(256), 0, s, p);
-    else               launch_pdl(norm_block_kernel<T, W, 8, RES, 256>, dim3(grid), dim3(256), 0, s, p);
+    if (per <= 2)      launch_maybe_pdl(p.rows <= kPdlMaxRows, norm_block_kernel<T, W, 2, RES, 256>, dim3(grid), dim3(256), 0, s, p);
+    else if (per <= 4) launch_maybe_pdl(p.rows <= kPdlMaxRows, norm_block_kernel<T, W, 4, RES, 256>, dim3(grid), dim3(256), 0, s, p);
+    else               launch_maybe_pdl(p.rows <= kPdlMaxRows, norm_block_kernel<T, W, 8, RES, 256>, dim3(grid), dim3(256), 0, s, p);
     return launch_status();
   }
-  launch_pdl(norm_generic_kernel<T, W, RES>, dim3(grid), dim3(256), 0, s, p);
+  launch_maybe_pdl(p.rows <= kPdlMaxRows, norm_generic_kernel<T, W, RES>, dim3(grid), dim3(256), 0, s, p);
   return launch_status();
 }
 
@@ -369,9 +369,9 @@ template <typename T, typename W>
 int launch_reduce_norm(const RedParams& p, cudaStream_t s) {
   const unsigned grid = (unsigned)(p.rows < kMaxGrid ? p.rows : kMaxGrid);
   const int v = (p.n + 4 * kRedThreads - 1) / (4 * kRedThreads);
-  if (v <= 1)      launch_pdl(reduce_add_norm_kernel<T, W, 1>, dim3(grid), dim3(kRedThreads), 0, s, p);
-  else if (v <= 2) launch_pdl(reduce_add_norm_kernel<T, W, 2>, dim3(grid), dim3(kRedThreads), 0, s, p);
-  else             launch_pdl(reduce_add_norm_kernel<T, W, 4>, dim3(grid), dim3(kRedThreads), 0, s, p);
+  if (v <= 1)      launch_maybe_pdl(p.rows <= kPdlMaxRows, reduce_add_norm_kernel<T, W, 1>, dim3(grid), dim3(kRedThreads), 0, s, p);
+  else if (v <= 2) launch_maybe_pdl(p.rows <= kPdlMaxRows, reduce_add_norm_kernel<T, W, 2>, dim3(grid), dim3(kRedThreads), 0, s, p);
+  else             launch_maybe_pdl(p.rows <= kPdlMaxRows, reduce_add_norm_kernel<T, W, 4>, dim3(grid), dim3(kRedThreads), 0, s, p);
   return launch_status();
 }
 

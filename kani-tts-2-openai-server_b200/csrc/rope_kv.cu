@@ -716,11 +716,11 @@ int launch_rope_t(const RopeParams& p, cudaStream_t s) {
       if (grid <= 0x7fffffff) {
         const dim3 blk((unsigned)(64 * tpb));
         if (p.hq <= 2 * G && p.hk <= G) {
-          launch_pdl(rope_token_kernel<T, NORM, TABLE, 2, 1>, dim3((unsigned)grid), dim3(blk), 0, s, p, log2l);
+          launch_maybe_pdl(p.n_tokens <= kPdlMaxRows, rope_token_kernel<T, NORM, TABLE, 2, 1>, dim3((unsigned)grid), dim3(blk), 0, s, p, log2l);
           return launch_status();
         }
         if (p.hq <= 4 * G && p.hk <= 2 * G) {
-          launch_pdl(rope_token_kernel<T, NORM, TABLE, 4, 2>, dim3((unsigned)grid), dim3(blk), 0, s, p, log2l);
+          launch_maybe_pdl(p.n_tokens <= kPdlMaxRows, rope_token_kernel<T, NORM, TABLE, 4, 2>, dim3((unsigned)grid), dim3(blk), 0, s, p, log2l);
           return launch_status();
         }
       }

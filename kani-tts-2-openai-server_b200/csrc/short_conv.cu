@@ -103,9 +103,9 @@ int launch_conv(const void* bcx, int64_t bcx_stride, void* state, int64_t state_
   const T* wp = static_cast<const T*>(w);
   T* yp = static_cast<T*>(y);
   switch (L) {
-    case 2: launch_pdl(short_conv_kernel<T, 2>, dim3((unsigned)grid), dim3(128), 0, s, bp, bcx_stride, sp, state_stride, wp, yp, y_stride, batch, hidden); break;
-    case 3: launch_pdl(short_conv_kernel<T, 3>, dim3((unsigned)grid), dim3(128), 0, s, bp, bcx_stride, sp, state_stride, wp, yp, y_stride, batch, hidden); break;
-    case 4: launch_pdl(short_conv_kernel<T, 4>, dim3((unsigned)grid), dim3(128), 0, s, bp, bcx_stride, sp, state_stride, wp, yp, y_stride, batch, hidden); break;
+    case 2: launch_maybe_pdl(batch <= kPdlMaxRows, short_conv_kernel<T, 2>, dim3((unsigned)grid), dim3(128), 0, s, bp, bcx_stride, sp, state_stride, wp, yp, y_stride, batch, hidden); break;
+    case 3: launch_maybe_pdl(batch <= kPdlMaxRows, short_conv_kernel<T, 3>, dim3((unsigned)grid), dim3(128), 0, s, bp, bcx_stride, sp, state_stride, wp, yp, y_stride, batch, hidden); break;
+    case 4: launch_maybe_pdl(batch <= kPdlMaxRows, short_conv_kernel<T, 4>, dim3((unsigned)grid), dim3(128), 0, s, bp, bcx_stride, sp, state_stride, wp, yp, y_stride, batch, hidden); break;
     default: return KANI_ERR_UNSUPPORTED;
   }
   return launch_status();

@@ -129,7 +129,7 @@ int launch_silu(const void* gu, int64_t in_stride, void* y, int64_t out_stride, 
     if (rows >= kRowKernelMinRows && cv <= 8) {
       const unsigned grid = (unsigned)(rows < 0x7fffffff ? rows : 0x7fffffff);
       auto go = [&](auto kern) {
-        launch_pdl(kern, dim3(grid), dim3(192), 0, s, static_cast<const T*>(gu), in_stride, static_cast<T*>(y),
+        launch_maybe_pdl(rows <= kPdlMaxRows, kern, dim3(grid), dim3(192), 0, s, static_cast<const T*>(gu), in_stride, static_cast<T*>(y),
                    out_stride, rows, vpr, n, pf);
       };
       if (cv <= 2)      go(silu_mul_row_kernel<T, 2>);
@@ -149,14 +149,14 @@ int launch_silu(const void* gu, int64_t in_stride, void* y, int64_t out_stride, 
       gx = (unsigned)((vpr + bx - 1) / bx);
     }
     const unsigned gy = (unsigned)(rows < 65535 ? rows : 65535);
-    launch_pdl(silu_mul_vec_kernel<T, 1>, dim3(gx, gy), dim3(bx), 0, s, static_cast<const T*>(gu), in_stride,
+    launch_maybe_pdl(rows <= kPdlMaxRows, silu_mul_vec_kernel<T, 1>, dim3(gx, gy), dim3(bx), 0, s, static_cast<const T*>(gu), in_stride,
                static_cast<T*>(y), out_stride, rows, vpr, n, pf);
     return launch_status();
   }
   const int64_t gx64 = (n + 255) / 256;
   if (gx64 > 0x7fffffff) return KANI_ERR_UNSUPPORTED;
   const unsigned gy = (unsigned)(rows < 65535 ? rows : 65535);
-  launch_pdl(silu_mul_generic_kernel<T>, dim3((unsigned)gx64, gy), dim3(256), 0, s, static_cast<const T*>(gu),
+  launch_maybe_pdl(rows <= kPdlMaxRows, silu_mul_generic_kernel<T>, dim3((unsigned)gx64, gy), dim3(256), 0, s, static_cast<const T*>(gu),
              in_stride, static_cast<T*>(y), out_stride, rows, n, pf);
   return launch_status();
 }

@@ -24,6 +24,7 @@ decode_advance_kernel(const int64_t* __restrict__ next_token, int64_t* __restric
                       int64_t* rng_step, const int64_t* __restrict__ base_pos, const int64_t* __restrict__ base_slot,
                       int tokens_per_frame, float audio_step, int64_t* __restrict__ positions,
                       int64_t* __restrict__ slots, int64_t* __restrict__ kv_len, int64_t batch) {
+  griddep_wait();  // up to kPdlMaxRows streams a programmatic dependent: the token comes from the launch before
   const int64_t k = *step;
   for (int64_t b = threadIdx.x; b < batch; b += blockDim.x) {
     const int64_t t = next_token[b];
@@ -57,8 +58,9 @@ extern "C" int kani_decode_advance(const int64_t* next_token, int64_t* input_ids
     return KANI_ERR_INVALID_ARG;
   if (batch > 1 && gen_row_stride < gen_cols) return KANI_ERR_INVALID_ARG;
   const int threads = batch < 256 ? (int)((batch + 31) / 32 * 32) : 256;
-  kani::decode_advance_kernel<<<1, threads, 0, static_cast<cudaStream_t>(stream)>>>(
-      next_token, input_ids, generated, gen_row_stride, gen_cols, step, rng_step, base_pos, base_slot,
-      tokens_per_frame, audio_step, positions, slots, kv_len, batch);
+  kani::launch_maybe_pdl(batch <= kani::kPdlMaxRows, kani::decode_advance_kernel, dim3(1), dim3(threads), 0,
+                         static_cast<cudaStream_t>(stream), next_token, input_ids, generated, gen_row_stride, gen_cols,
+                         step, rng_step, base_pos, base_slot, tokens_per_frame, audio_step, positions, slots, kv_len,
+                         batch);
   return kani::launch_status();
 }

@@ -71,6 +71,7 @@ __global__ void __launch_bounds__(kHeadThreads) head_argmax_kernel(HeadParams p)
   const int H = CH * 256;
   const T* W = static_cast<const T*>(p.w);
   const int gw = blockIdx.x * kHeadWarps + warp, nw = gridDim.x * kHeadWarps;
+  griddep_launch_dependents();  // the sampler or the bookkeeping launch after this one may be scheduled
 
   // the weights do not depend on earlier launches: the first rows stream in
   // before the programmatic-launch wait, the hidden rows are read after it

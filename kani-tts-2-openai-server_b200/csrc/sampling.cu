@@ -159,6 +159,8 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(SampleParams 
   __shared__ int sh_count;
   __shared__ long long s_tok[kMaxTopK];
   __shared__ float s_draw[kMaxTopK];
+  griddep_launch_dependents();  // the bookkeeping launch after this one may be scheduled
+  griddep_wait();               // up to kPdlMaxRows streams a programmatic dependent: the logits come from the launch before
 
   const int b = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -744,7 +746,7 @@ int launch_sample(SampleParams prm, int64_t batch, cudaStream_t s) {
   auto kern = ipt <= kRegItems ? sample_kernel<T, true> : sample_kernel<T, false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return (int)e;
-  kern<<<(unsigned)batch, kSampleThreads, smem, s>>>(prm);
+  launch_maybe_pdl(batch <= kPdlMaxRows, kern, dim3((unsigned)batch), dim3(kSampleThreads), smem, s, prm);
   return launch_status();
 }
 

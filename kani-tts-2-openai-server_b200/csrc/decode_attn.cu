@@ -352,34 +352,41 @@ decode_attn_kernel(AttnParams p) {
   const char* kb = reinterpret_cast<const char*>(static_cast<const T*>(p.k) + b * p.cb + (int64_t)h * p.ch + k0 * p.cs);
   const char* vb = reinterpret_cast<const char*>(static_cast<const T*>(p.v) + b * p.cb + (int64_t)h * p.ch + k0 * p.cs);
 
-  auto issue = [&](int t) {  // thread 0: tile t into stage t % STAGES
+  // thread 0: tile t into stage t % STAGES.  part 0: the whole tile; part 1:
+  // the stage's expected bytes and every row but the tile's last; part 2: that
+  // last row alone (the stage's phase completes once both parts have landed)
+  auto issue = [&](int t, int part = 0) {
     const int st = t % STAGES;
     const int rows = n - t * TILE < TILE ? n - t * TILE : TILE;
     const uint32_t bytes = (uint32_t)rows * ROW;
     const uint32_t bar = attn_smem_u32(&bars[st]);
     const uint32_t dst = attn_smem_u32(ring + (size_t)st * 2 * TILE_BYTES);
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(2 * bytes) : "memory");
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-                 "l"(kb + (int64_t)t * TILE_BYTES), "r"(bytes), "r"(bar) : "memory");
+    if (part != 2)
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(2 * bytes) : "memory");
+    const uint32_t r0 = part == 2 ? (uint32_t)(rows - 1) * ROW : 0u;
+    const uint32_t nb = part == 0 ? bytes : (part == 1 ? bytes - ROW : ROW);
+    if (nb == 0) return;
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst + r0),
+                 "l"(kb + (int64_t)t * TILE_BYTES + r0), "r"(nb), "r"(bar) : "memory");
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     dst + TILE_BYTES),
-                 "l"(vb + (int64_t)t * TILE_BYTES), "r"(bytes), "r"(bar) : "memory");
+                     dst + TILE_BYTES + r0),
+                 "l"(vb + (int64_t)t * TILE_BYTES + r0), "r"(nb), "r"(bar) : "memory");
   };
-  // The tile holding the newest row, len - 1, is the only one a decode step's
-  // previous launch (its RoPE + KV write) may still be writing.  Launched as a
-  // programmatic dependent (kani_decode_attention_step), the other first tiles
-  // stream in before griddepcontrol.wait and that tile after it; launched
+  // The newest row, len - 1, is the only one a decode step's previous launch
+  // (its RoPE + KV write) may still be writing; it is the last row of this
+  // CTA's range, so the last row of its tile.  Launched as a programmatic
+  // dependent (kani_decode_attention_step), the first tiles stream in before
+  // griddepcontrol.wait, all but that row, which is fetched after it; launched
   // plainly, the wait returns at once and the order does not matter.
   const int t_new = (len - 1 >= k0 && len - 1 < k1) ? (int)((len - 1 - k0) / TILE) : -1;
   if (tid == 0) {
     for (int st = 0; st < STAGES; ++st)
       asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(attn_smem_u32(&bars[st])), "r"(1) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    for (int t = 0; t < ntiles && t < STAGES; ++t)
-      if (t != t_new) issue(t);
+    for (int t = 0; t < ntiles && t < STAGES; ++t) issue(t, t == t_new ? 1 : 0);
   }
   griddep_wait();  // q and the newest row may come from the launch before
-  if (tid == 0 && t_new >= 0 && t_new < STAGES) issue(t_new);
+  if (tid == 0 && t_new >= 0 && t_new < STAGES) issue(t_new, 2);
 
   // query heads (global) while the first tiles stream in
   float q[G][DL];

@@ -111,6 +111,45 @@ def test_l2_prefetch_plan_covers_the_weights_once_per_step():
     assert FusedDecoder._l2_prefetch_plan(fake) == [None] * (len(cuts) - 1)
 
 
+def test_weight_buffer_holds_the_projections_in_step_order():
+    """The decoder's projection weights and padded head move into one buffer, in
+    the order a decode step reads them; every tensor becomes a view of it with its
+    values unchanged, and the spans tile the buffer with no gap."""
+    from types import SimpleNamespace
+
+    import torch
+    from kani_tts_b200.decode import FusedDecoder
+
+    g = torch.Generator().manual_seed(9)
+
+    def w(r, c):
+        return torch.randn(r, c, generator=g).to(torch.bfloat16)
+
+    layers = [{"attn": False, "in_proj": w(12, 8), "out_proj": w(8, 8), "gate_up": w(16, 8), "down": w(8, 8)},
+              {"attn": True, "qkv": w(16, 8), "o": w(8, 8), "gate_up": w(16, 8), "down": w(8, 8)}]
+    want = [[v.clone() for k, v in L.items() if k != "attn"] for L in layers]
+    head = w(6, 8)
+    fake = SimpleNamespace(layers=layers, head_padded=head.clone(), num_reduced=5, dtype=torch.bfloat16,
+                           device=torch.device("cpu"))
+    FusedDecoder._pack_weights(fake)
+    arena = fake.weight_arena
+    order = [("in_proj", "out_proj", "gate_up", "down"), ("qkv", "o", "gate_up", "down")]
+    spans = iter(fake.weight_spans)
+    end = 0
+    for L, keys, vals in zip(layers, order, want):
+        for key in keys:
+            t = L[key]
+            a, b = next(spans)
+            assert a == end and t.untyped_storage().data_ptr() == arena.untyped_storage().data_ptr()
+            assert t.data_ptr() - arena.data_ptr() == a and b - a == t.numel() * 2
+            end = b
+        assert all(torch.equal(L[k], v) for k, v in zip([k for k in L if k != "attn"], vals))
+    a, b = next(spans)
+    assert a == end and b == arena.numel() * 2
+    assert torch.equal(fake.head_padded, head) and fake.head.shape == (5, 8)
+    assert fake.head.data_ptr() == fake.head_padded.data_ptr() == arena.data_ptr() + a
+
+
 def test_abi_rejects_bad_arguments_without_launching():
     lib = _lib.load_library()
     before = lib.kani_launch_count()
